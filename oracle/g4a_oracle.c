@@ -1,0 +1,600 @@
+/*
+ * CPU ORACLE — test infrastructure only (see g4a_oracle.h).
+ *
+ * Restates gemma4-rs's f32 attention arithmetic step for step, in the same
+ * operation order, so that its results are the reference's on the same libm.
+ * Compiled with -O2 -ffp-contract=off and no fast-math: Rust never fuses a
+ * multiply and an add, and neither may this file.
+ */
+#define _GNU_SOURCE
+#include "g4a_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdatomic.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+/* ------------------------------------------------------------------------ */
+/* Rust float helpers                                                         */
+/* ------------------------------------------------------------------------ */
+
+/* f32::total_cmp key (core::f32::total_cmp): flip the magnitude bits of
+ * negative values so that a signed integer compare gives IEEE totalOrder. */
+static int32_t total_key(float x) {
+    int32_t i;
+    memcpy(&i, &x, sizeof i);
+    i ^= (int32_t)(((uint32_t)(i >> 31)) >> 1);
+    return i;
+}
+
+float orc_round_f16(float x) { return (float)(_Float16)x; }
+
+float orc_round_bf16(float x) {
+    uint32_t u;
+    memcpy(&u, &x, sizeof u);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) { /* NaN stays NaN */
+        u |= 0x00400000u;
+    } else {
+        u += 0x7fffu + ((u >> 16) & 1u); /* round to nearest, ties to even */
+    }
+    u &= 0xffff0000u;
+    memcpy(&x, &u, sizeof x);
+    return x;
+}
+
+/* ------------------------------------------------------------------------ */
+/* ops.rs                                                                     */
+/* ------------------------------------------------------------------------ */
+
+/* ops.rs:45-56 rms_norm: mean of squares accumulated in f64 (each square is
+ * an f32 product widened to f64, summed left to right), mean cast to f32,
+ * scale = 1 / sqrt(mean + eps) in f32, y = x * scale [* weight]. */
+int orc_rms_norm(const float *x, size_t n, const float *weight, float eps, float *out) {
+    if (n == 0 || eps < 0.0f) return ORC_COMPUTE;
+    double sum = -0.0;
+    for (size_t i = 0; i < n; i++) {
+        float sq = x[i] * x[i];
+        sum += (double)sq;
+    }
+    float mean = (float)(sum / (double)n);
+    float scale = 1.0f / sqrtf(mean + eps);
+    if (weight) {
+        for (size_t i = 0; i < n; i++) out[i] = (x[i] * scale) * weight[i];
+    } else {
+        for (size_t i = 0; i < n; i++) out[i] = x[i] * scale;
+    }
+    return ORC_OK;
+}
+
+/* ops.rs:65-76 dot_f32: 16 strided accumulators (element i goes to lane
+ * i % 16 for the full chunks), lanes summed in order from -0.0 (Rust's f32
+ * Sum identity), then the tail (its own in-order sum) added last. */
+float orc_dot_f32(const float *a, const float *b, size_t n) {
+    enum { LANES = 16 };
+    float lanes[LANES] = {0};
+    size_t full = n - n % LANES;
+    float tail = -0.0f;
+    for (size_t i = full; i < n; i++) tail += a[i] * b[i];
+    for (size_t c = 0; c < full; c += LANES)
+        for (int l = 0; l < LANES; l++) lanes[l] += a[c + l] * b[c + l];
+    float s = -0.0f;
+    for (int l = 0; l < LANES; l++) s += lanes[l];
+    return s + tail;
+}
+
+/* ops.rs:105-127 softmax_f32: max by total_cmp, e = exp(x - max), in-order
+ * f32 sum, error if the sum is not finite or zero, p = e / sum. */
+int orc_softmax_f32(const float *x, size_t n, float *out) {
+    if (n == 0) return ORC_COMPUTE;
+    float mx = x[0];
+    int32_t mk = total_key(mx);
+    for (size_t i = 1; i < n; i++) { /* max_by keeps the last of equal maxima */
+        int32_t k = total_key(x[i]);
+        if (k >= mk) { mk = k; mx = x[i]; }
+    }
+    float sum = -0.0f;
+    for (size_t i = 0; i < n; i++) {
+        out[i] = expf(x[i] - mx);
+        sum += out[i];
+    }
+    if (!isfinite(sum) || sum == 0.0f) return ORC_NONFINITE;
+    for (size_t i = 0; i < n; i++) out[i] = out[i] / sum;
+    return ORC_OK;
+}
+
+/* ops.rs:134-162 rope_neox: pairs (x[i], x[i + n_rot/2]); the angle of pair
+ * i is theta_i / factor_i with theta_0 = position and theta_{i+1} =
+ * theta_i * base^(-2/n_rot), built by repeated f32 multiplication. */
+int orc_rope_neox(float *x, size_t len, size_t position, float base, size_t n_rot,
+                  const float *freq_factors, size_t n_factors) {
+    size_t half = n_rot / 2;
+    if (n_rot == 0 || n_rot % 2 != 0 || n_rot > len || base <= 0.0f ||
+        (freq_factors && n_factors < half))
+        return ORC_COMPUTE;
+    float theta_scale = powf(base, -2.0f / (float)n_rot);
+    float theta = (float)position;
+    for (size_t i = 0; i < half; i++) {
+        float factor = freq_factors ? freq_factors[i] : 1.0f;
+        float angle = theta / factor;
+        float s = sinf(angle), c = cosf(angle);
+        float a = x[i], b = x[i + half];
+        float ac = a * c, bs = b * s, as_ = a * s, bc = b * c;
+        x[i] = ac - bs;
+        x[i + half] = as_ + bc;
+        theta *= theta_scale;
+    }
+    return ORC_OK;
+}
+
+void orc_rope_sincos(size_t position, float base, size_t n_rot, const float *freq_factors,
+                     float *sin_out, float *cos_out) {
+    size_t half = n_rot / 2;
+    float theta_scale = powf(base, -2.0f / (float)n_rot);
+    float theta = (float)position;
+    for (size_t i = 0; i < half; i++) {
+        float factor = freq_factors ? freq_factors[i] : 1.0f;
+        float angle = theta / factor;
+        sin_out[i] = sinf(angle);
+        cos_out[i] = cosf(angle);
+        theta *= theta_scale;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* idea/mod.rs, eng/mod.rs                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* idea/mod.rs:48-68 Gemma4HyperParams::e2b (attention fields). */
+void orc_hparams_e2b(orc_hparams *hp) {
+    hp->n_layers = 35;
+    hp->n_heads = 8;
+    hp->n_kv_heads = 1;
+    hp->head_dim_local = 256;
+    hp->head_dim_global = 512;
+    hp->sliding_window = 512;
+    hp->shared_kv_layers = 20;
+    hp->local_rope_base = 10000.0f;
+    hp->global_rope_base = 1000000.0f;
+    hp->global_p = 0.25f;
+    hp->rms_norm_eps = 1e-6f;
+}
+
+/* idea/mod.rs:148-156 layer_attention_kind: global iff last layer or l%5==4. */
+int orc_layer_is_global(const orc_hparams *hp, int32_t layer) {
+    return (layer + 1 == hp->n_layers) || (layer % 5 == 4);
+}
+
+/* idea/mod.rs:140-145 head_dim. */
+int32_t orc_head_dim(const orc_hparams *hp, int32_t layer) {
+    return orc_layer_is_global(hp, layer) ? hp->head_dim_global : hp->head_dim_local;
+}
+
+/* eng/mod.rs:71-90 kv_source_layer. err_detail receives the KvShareError
+ * variant on failure: 1 LayerOutOfRange, 2 TooManySharedLayers,
+ * 3 NoEarlierLayerOfSameKind. */
+int orc_kv_source_layer(const orc_hparams *hp, int32_t layer, int32_t *source, int32_t *err_detail) {
+    int32_t n = hp->n_layers;
+    if (layer < 0 || layer >= n) { if (err_detail) *err_detail = 1; return ORC_BAD_LAYER; }
+    int32_t first_shared = n - hp->shared_kv_layers;
+    if (hp->shared_kv_layers > n || first_shared <= 0) { if (err_detail) *err_detail = 2; return ORC_BAD_LAYER; }
+    if (layer < first_shared) { *source = layer; return ORC_OK; }
+    int kind = orc_layer_is_global(hp, layer);
+    for (int32_t e = first_shared - 1; e >= 0; e--) {
+        if (orc_layer_is_global(hp, e) == kind) { *source = e; return ORC_OK; }
+    }
+    if (err_detail) *err_detail = 3;
+    return ORC_BAD_LAYER;
+}
+
+/* eng/mod.rs:10-12 windowed_len: seq_len.saturating_sub(window)..seq_len. */
+void orc_windowed_len(size_t seq_len, size_t window, size_t *lo, size_t *hi) {
+    *lo = seq_len > window ? seq_len - window : 0;
+    *hi = seq_len;
+}
+
+/* idea/mod.rs:162-165 proportional_rope_freq_factors. */
+void orc_proportional_rope_freq_factors(size_t head_dim, float p, float *out) {
+    size_t rotated = (size_t)((float)head_dim * p / 2.0f);
+    for (size_t pair = 0; pair < head_dim / 2; pair++) out[pair] = pair < rotated ? 1.0f : 1e30f;
+}
+
+/* ------------------------------------------------------------------------ */
+/* pool.rs: persistent workers, atomic chunk claims, spin then sleep          */
+/* ------------------------------------------------------------------------ */
+
+#define SPIN_FOR_NS 200000L   /* pool.rs:28 SPIN_FOR = 200 us */
+#define CHUNKS_PER_THREAD 4   /* pool.rs:36 */
+
+typedef struct orc_task {
+    size_t chunks;
+    atomic_size_t next;
+    atomic_size_t remaining;
+    atomic_int refs;
+    void (*run_chunk)(void *ctx, size_t chunk);
+    void *ctx;
+    pthread_mutex_t mu;
+    pthread_cond_t cv;
+    int finished;
+} orc_task;
+
+typedef struct qnode { orc_task *task; struct qnode *next; } qnode;
+
+typedef struct worker {
+    pthread_t th;
+    pthread_mutex_t mu;
+    pthread_cond_t cv;
+    qnode *head, *tail;
+    atomic_int pending;
+} worker;
+
+static struct {
+    pthread_mutex_t init_mu;
+    int inited;
+    int n_workers;
+    worker *workers;
+} g_pool = {PTHREAD_MUTEX_INITIALIZER, 0, 0, NULL};
+
+static long now_ns(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1000000000L + ts.tv_nsec;
+}
+
+static void task_release(orc_task *t) {
+    if (atomic_fetch_sub(&t->refs, 1) == 1) {
+        pthread_mutex_destroy(&t->mu);
+        pthread_cond_destroy(&t->cv);
+        free(t);
+    }
+}
+
+/* pool.rs:49-63 Task::work: claim chunks until none are left. */
+static void task_work(orc_task *t) {
+    for (;;) {
+        size_t chunk = atomic_fetch_add_explicit(&t->next, 1, memory_order_relaxed);
+        if (chunk >= t->chunks) return;
+        t->run_chunk(t->ctx, chunk);
+        if (atomic_fetch_sub_explicit(&t->remaining, 1, memory_order_acq_rel) == 1) {
+            pthread_mutex_lock(&t->mu);
+            t->finished = 1;
+            pthread_cond_broadcast(&t->cv);
+            pthread_mutex_unlock(&t->mu);
+        }
+    }
+}
+
+/* pool.rs:65-77 Task::wait: spin for SPIN_FOR, then sleep on the signal. */
+static void task_wait(orc_task *t) {
+    long deadline = now_ns() + SPIN_FOR_NS;
+    while (now_ns() < deadline) {
+        if (atomic_load_explicit(&t->remaining, memory_order_acquire) == 0) return;
+    }
+    pthread_mutex_lock(&t->mu);
+    while (!t->finished) pthread_cond_wait(&t->cv, &t->mu);
+    pthread_mutex_unlock(&t->mu);
+}
+
+/* pool.rs:114-124 next_task: spin for SPIN_FOR before sleeping. */
+static orc_task *next_task(worker *w) {
+    long deadline = now_ns() + SPIN_FOR_NS;
+    for (;;) {
+        if (atomic_load_explicit(&w->pending, memory_order_acquire) > 0 || now_ns() >= deadline) {
+            pthread_mutex_lock(&w->mu);
+            while (!w->head) pthread_cond_wait(&w->cv, &w->mu);
+            qnode *n = w->head;
+            w->head = n->next;
+            if (!w->head) w->tail = NULL;
+            atomic_fetch_sub(&w->pending, 1);
+            pthread_mutex_unlock(&w->mu);
+            orc_task *t = n->task;
+            free(n);
+            return t;
+        }
+    }
+}
+
+static void *worker_main(void *arg) {
+    worker *w = (worker *)arg;
+    for (;;) {
+        orc_task *t = next_task(w);
+        task_work(t);
+        task_release(t);
+    }
+    return NULL;
+}
+
+/* pool.rs:86-110 pool(): LLM_THREADS if set, else every core. `threads`
+ * > 0 overrides (used to time the baseline at a stated thread count); the
+ * pool can be sized once per process. */
+int orc_pool_init(int threads) {
+    pthread_mutex_lock(&g_pool.init_mu);
+    if (!g_pool.inited) {
+        if (threads <= 0) {
+            const char *env = getenv("LLM_THREADS");
+            threads = env ? atoi(env) : 0;
+            if (threads <= 0) threads = (int)sysconf(_SC_NPROCESSORS_ONLN);
+            if (threads <= 0) threads = 1;
+        }
+        g_pool.n_workers = threads - 1;
+        g_pool.workers = calloc((size_t)(g_pool.n_workers > 0 ? g_pool.n_workers : 1), sizeof(worker));
+        for (int i = 0; i < g_pool.n_workers; i++) {
+            worker *w = &g_pool.workers[i];
+            pthread_mutex_init(&w->mu, NULL);
+            pthread_cond_init(&w->cv, NULL);
+            atomic_init(&w->pending, 0);
+            pthread_create(&w->th, NULL, worker_main, w);
+            pthread_detach(w->th);
+        }
+        g_pool.inited = 1;
+    }
+    int n = g_pool.n_workers + 1;
+    pthread_mutex_unlock(&g_pool.init_mu);
+    return n;
+}
+
+/* pool.rs:82-84 threads(). */
+int orc_pool_threads(void) { return orc_pool_init(0); }
+
+/* pool.rs:160-197 run_chunks: inline below the work threshold, otherwise
+ * ceil(count / (threads * 4)) items per chunk, claimed by the caller and the
+ * workers. Each chunk writes its own output slots, so no concatenation step
+ * is needed here. */
+static void run_chunks(size_t count, size_t work_per_item, size_t parallel_min_work,
+                       void (*run_range)(void *ctx, size_t lo, size_t hi), void *ctx);
+
+typedef struct { void (*run_range)(void *, size_t, size_t); void *ctx; size_t chunk_len, count; } range_ctx;
+static void run_chunk_range(void *c, size_t chunk) {
+    range_ctx *rc = (range_ctx *)c;
+    size_t lo = chunk * rc->chunk_len;
+    size_t hi = lo + rc->chunk_len < rc->count ? lo + rc->chunk_len : rc->count;
+    rc->run_range(rc->ctx, lo, hi);
+}
+
+static void run_chunks(size_t count, size_t work_per_item, size_t parallel_min_work,
+                       void (*run_range)(void *ctx, size_t lo, size_t hi), void *ctx) {
+    int threads = orc_pool_init(0);
+    size_t work = count * work_per_item;
+    if (threads <= 1 || work < parallel_min_work) { run_range(ctx, 0, count); return; }
+    size_t per = (size_t)threads * CHUNKS_PER_THREAD;
+    size_t chunk_len = (count + per - 1) / per;
+    if (chunk_len == 0) chunk_len = 1;
+    size_t chunks = (count + chunk_len - 1) / chunk_len;
+    range_ctx rc = {run_range, ctx, chunk_len, count};
+    orc_task *t = calloc(1, sizeof *t);
+    t->chunks = chunks;
+    atomic_init(&t->next, 0);
+    atomic_init(&t->remaining, chunks);
+    atomic_init(&t->refs, g_pool.n_workers + 1);
+    t->run_chunk = run_chunk_range;
+    t->ctx = &rc;
+    pthread_mutex_init(&t->mu, NULL);
+    pthread_cond_init(&t->cv, NULL);
+    for (int i = 0; i < g_pool.n_workers; i++) { /* pool.rs:188-190 send to every worker */
+        worker *w = &g_pool.workers[i];
+        qnode *n = malloc(sizeof *n);
+        n->task = t;
+        n->next = NULL;
+        pthread_mutex_lock(&w->mu);
+        if (w->tail) w->tail->next = n; else w->head = n;
+        w->tail = n;
+        atomic_fetch_add(&w->pending, 1);
+        pthread_cond_signal(&w->cv);
+        pthread_mutex_unlock(&w->mu);
+    }
+    task_work(t);
+    task_wait(t);
+    /* Workers that arrive after the last chunk only see next >= chunks and
+     * never touch rc; the task itself lives until every worker let go. */
+    task_release(t);
+}
+
+/* ------------------------------------------------------------------------ */
+/* model.rs:307-366 attention                                                 */
+/* ------------------------------------------------------------------------ */
+
+#define ATTENTION_PARALLEL_MIN_WORK ((size_t)1 << 18) /* model.rs:308 */
+
+typedef struct {
+    const float *q, *keys, *values;
+    size_t len, kv_width, head_dim, n_heads, n_kv_heads;
+    float scale;
+    float *out;
+    int *head_failed;
+} attn_job;
+
+/* model.rs:326-343 attend_head: scores = dot_f32(q_h, k_j[kv]) * scale for
+ * every key in order, softmax, out = sum_j p_j * v_j[kv] accumulated in key
+ * order. A failed softmax marks the head (the reference returns an empty
+ * vector, which attend then reports as non-finite). */
+static void attend_head(const attn_job *job, size_t head) {
+    size_t hd = job->head_dim;
+    const float *qh = job->q + head * hd;
+    size_t kv_head = head * job->n_kv_heads / job->n_heads;
+    size_t off = kv_head * hd;
+    float *scores = malloc((job->len ? job->len : 1) * sizeof(float));
+    float *probs = malloc((job->len ? job->len : 1) * sizeof(float));
+    for (size_t j = 0; j < job->len; j++)
+        scores[j] = orc_dot_f32(qh, job->keys + j * job->kv_width + off, hd) * job->scale;
+    float *o = job->out + head * hd;
+    if (job->len == 0 || orc_softmax_f32(scores, job->len, probs) != ORC_OK) {
+        job->head_failed[head] = 1;
+    } else {
+        for (size_t i = 0; i < hd; i++) o[i] = 0.0f;
+        for (size_t j = 0; j < job->len; j++) {
+            const float *vj = job->values + j * job->kv_width + off;
+            float p = probs[j];
+            for (size_t i = 0; i < hd; i++) {
+                float pv = p * vj[i];
+                o[i] += pv;
+            }
+        }
+    }
+    free(scores);
+    free(probs);
+}
+
+static void attend_range(void *ctx, size_t lo, size_t hi) {
+    for (size_t h = lo; h < hi; h++) attend_head((const attn_job *)ctx, h);
+}
+
+/* model.rs:348-366 attend: keys/values are already one contiguous row per
+ * position (the reference's `concat`), heads run on the pool once
+ * n_heads * 2 * len * head_dim reaches ATTENTION_PARALLEL_MIN_WORK. */
+int orc_attend(const float *q, const float *keys, const float *values, size_t len,
+               size_t n_heads, size_t n_kv_heads, size_t head_dim, float scale, float *out) {
+    if (n_heads == 0 || n_kv_heads == 0 || head_dim == 0) return ORC_COMPUTE;
+    int failed[1024];
+    if (n_heads > 1024) return ORC_COMPUTE;
+    memset(failed, 0, n_heads * sizeof(int));
+    attn_job job = {q, keys, values, len, n_kv_heads * head_dim, head_dim, n_heads, n_kv_heads,
+                    scale, out, failed};
+    size_t work_per_head = 2 * len * head_dim;
+    run_chunks(n_heads, work_per_head, ATTENTION_PARALLEL_MIN_WORK, attend_range, &job);
+    for (size_t h = 0; h < n_heads; h++)
+        if (failed[h]) return ORC_NONFINITE; /* model.rs:362-364 */
+    return ORC_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* context_memory.rs                                                          */
+/* ------------------------------------------------------------------------ */
+
+typedef struct { float *keys, *values; size_t len, cap, width; } kv_layer;
+struct orc_kv { kv_layer *layers; size_t n_layers; };
+
+orc_kv *orc_kv_create(void) { return calloc(1, sizeof(orc_kv)); }
+
+void orc_kv_clear(orc_kv *kv) { /* context_memory.rs:83-85 */
+    for (size_t i = 0; i < kv->n_layers; i++) { free(kv->layers[i].keys); free(kv->layers[i].values); }
+    free(kv->layers);
+    kv->layers = NULL;
+    kv->n_layers = 0;
+}
+
+void orc_kv_destroy(orc_kv *kv) { if (kv) { orc_kv_clear(kv); free(kv); } }
+
+/* context_memory.rs:44-51 append: grow the layer list, push one row. */
+int orc_kv_append(orc_kv *kv, size_t layer, const float *k, const float *v, size_t width) {
+    if (kv->n_layers <= layer) {
+        kv->layers = realloc(kv->layers, (layer + 1) * sizeof(kv_layer));
+        memset(kv->layers + kv->n_layers, 0, (layer + 1 - kv->n_layers) * sizeof(kv_layer));
+        kv->n_layers = layer + 1;
+    }
+    kv_layer *L = &kv->layers[layer];
+    if (L->len > 0 && L->width != width) return ORC_COMPUTE;
+    L->width = width;
+    if (L->len == L->cap) {
+        L->cap = L->cap ? 2 * L->cap : 64;
+        L->keys = realloc(L->keys, L->cap * width * sizeof(float));
+        L->values = realloc(L->values, L->cap * width * sizeof(float));
+    }
+    memcpy(L->keys + L->len * width, k, width * sizeof(float));
+    memcpy(L->values + L->len * width, v, width * sizeof(float));
+    L->len++;
+    return ORC_OK;
+}
+
+/* context_memory.rs:53-69 view: a missing layer is fine only for len 0;
+ * asking for more rows than stored is ContextTooLong. A layer that exists
+ * only because a later one was appended (resize_with) has zero rows. */
+int orc_kv_view(const orc_kv *kv, size_t layer, size_t len, const float **keys,
+                const float **values, size_t *width, size_t *max_len) {
+    if (layer >= kv->n_layers) {
+        if (len == 0) { *keys = NULL; *values = NULL; *width = 0; return ORC_OK; }
+        return ORC_MISSING_LAYER;
+    }
+    const kv_layer *L = &kv->layers[layer];
+    if (max_len) *max_len = L->len;
+    if (len > L->len) return ORC_CONTEXT_TOO_LONG;
+    *keys = L->keys;
+    *values = L->values;
+    *width = L->width;
+    return ORC_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* model.rs:393-410: one layer's attention block without the projections      */
+/* ------------------------------------------------------------------------ */
+
+/* norm_heads (model.rs:283-290) over n_heads heads of width hd, in place. */
+static int norm_heads(float *x, size_t n_heads, size_t hd, const float *w, float eps) {
+    float *tmp = malloc(hd * sizeof(float));
+    for (size_t h = 0; h < n_heads; h++) {
+        int rc = orc_rms_norm(x + h * hd, hd, w, eps, tmp);
+        if (rc) { free(tmp); return rc; }
+        memcpy(x + h * hd, tmp, hd * sizeof(float));
+    }
+    free(tmp);
+    return ORC_OK;
+}
+
+/* rope_heads (model.rs:295-304): local layers use the local base and no
+ * factors; global layers use the global base and rope_freqs. */
+static int rope_heads(float *x, size_t n_heads, size_t hd, size_t pos, int global,
+                      const orc_hparams *hp, const float *rope_freqs) {
+    float base = global ? hp->global_rope_base : hp->local_rope_base;
+    const float *ff = global ? rope_freqs : NULL;
+    for (size_t h = 0; h < n_heads; h++) {
+        int rc = orc_rope_neox(x + h * hd, hd, pos, base, hd, ff, ff ? hd / 2 : 0);
+        if (rc) return rc;
+    }
+    return ORC_OK;
+}
+
+int orc_attention_block(orc_kv *kv, const orc_hparams *hp, int32_t layer, size_t position,
+                        const float *q_raw, const float *k_raw, const float *v_raw,
+                        const float *q_norm_w, const float *k_norm_w,
+                        const float *rope_freqs, int kv_store, float *out) {
+    size_t nh = (size_t)hp->n_heads, nkv = (size_t)hp->n_kv_heads;
+    size_t hd = (size_t)orc_head_dim(hp, layer);
+    int global = orc_layer_is_global(hp, layer);
+    float *q = malloc(nh * hd * sizeof(float));
+    memcpy(q, q_raw, nh * hd * sizeof(float));
+    int rc = norm_heads(q, nh, hd, q_norm_w, hp->rms_norm_eps);           /* :395 */
+    if (!rc) rc = rope_heads(q, nh, hd, position, global, hp, rope_freqs); /* :396 */
+    int32_t source = -1;
+    if (!rc) rc = orc_kv_source_layer(hp, layer, &source, NULL);            /* :398 */
+    if (!rc && source == layer) {                                           /* :399-406 */
+        size_t w = nkv * hd;
+        float *k = malloc(w * sizeof(float)), *v = malloc(w * sizeof(float));
+        memcpy(k, k_raw, w * sizeof(float));
+        memcpy(v, v_raw, w * sizeof(float));
+        rc = norm_heads(k, nkv, hd, k_norm_w, hp->rms_norm_eps);
+        if (!rc) rc = norm_heads(v, nkv, hd, NULL, hp->rms_norm_eps);
+        if (!rc) rc = rope_heads(k, nkv, hd, position, global, hp, rope_freqs);
+        if (!rc && kv_store == 1)
+            for (size_t i = 0; i < w; i++) { k[i] = orc_round_f16(k[i]); v[i] = orc_round_f16(v[i]); }
+        if (!rc) rc = orc_kv_append(kv, (size_t)layer, k, v, w);
+        free(k);
+        free(v);
+    }
+    const float *keys = NULL, *values = NULL;
+    size_t width = 0;
+    if (!rc) rc = orc_kv_view(kv, (size_t)source, position + 1, &keys, &values, &width, NULL); /* :407 */
+    if (!rc) {
+        size_t lo, hi;                                                       /* :408 */
+        if (global) { lo = 0; hi = position + 1; }
+        else orc_windowed_len(position + 1, (size_t)hp->sliding_window, &lo, &hi);
+        rc = orc_attend(q, keys + lo * width, values + lo * width, hi - lo, nh, nkv, hd, 1.0f, out); /* :410 */
+    }
+    free(q);
+    return rc;
+}
+
+/* Token-at-a-time prefill attention over T positions of one KV head:
+ * position t attends keys [max(0, t+1-window), t] (window 0 = global),
+ * each position one call of the reference's attend. */
+int orc_prefill_attend(const float *q, const float *k, const float *v, size_t T, size_t n_heads,
+                       size_t head_dim, size_t window, float *out) {
+    for (size_t t = 0; t < T; t++) {
+        size_t lo = 0, hi = t + 1;
+        if (window) orc_windowed_len(t + 1, window, &lo, &hi);
+        int rc = orc_attend(q + t * n_heads * head_dim, k + lo * head_dim, v + lo * head_dim,
+                            hi - lo, n_heads, 1, head_dim, 1.0f, out + t * n_heads * head_dim);
+        if (rc) return rc;
+    }
+    return ORC_OK;
+}
