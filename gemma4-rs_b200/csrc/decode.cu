@@ -1,0 +1,550 @@
+// Decode-side kernels of g4attn for sm_100a:
+//   * fused q/k RMSNorm + NEOX RoPE + KV append + split-KV attention with an
+//     in-kernel log-sum-exp combine (the last CTA of a task merges), replacing
+//     crates/llm-gemma4/src/impl_/model.rs:393-410 and :326-366;
+//   * the bulk append / view kernels behind ContextMemory
+//     (crates/llm-eng/src/context_memory.rs:44-69);
+//   * a generic attend kernel for shapes other than E2B's 8:1 heads;
+//   * the log-sum-exp merge of partial results.
+//
+// Arithmetic notes. RMSNorm follows ops.rs:45-56: squares in f32, summed in
+// f64, mean cast to f32, scale = 1/sqrt(mean + eps) with IEEE sqrt and
+// division, then (x * scale) * w. RoPE uses (sin, cos) tables built on the
+// host exactly as ops.rs:150-159 builds its angles, and applies them with
+// round-to-nearest multiplies and adds that are never fused, so q and the
+// stored k/v match the reference bit for bit. Attention sums in a different
+// order than the reference (within the 1e-4 decode tolerance).
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include "internal.h"
+
+namespace g4a {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float load_elem(const float *p) { return *p; }
+__device__ __forceinline__ float load_elem(const __half *p) { return __half2float(*p); }
+__device__ __forceinline__ void store_elem(float *p, float v) { *p = v; }
+__device__ __forceinline__ void store_elem(__half *p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ float round_to(float v, const float *) { return v; }
+__device__ __forceinline__ float round_to(float v, const __half *) { return __half2float(__float2half_rn(v)); }
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// Row r of a cache layer: paged (block table) or contiguous.
+template <typename KT>
+__device__ __forceinline__ const KT *row_ptr(const void *base, const int32_t *bt, int page_tokens, int hd, int r) {
+    size_t idx;
+    if (bt) {
+        int page = __ldg(bt + r / page_tokens);
+        idx = ((size_t)page * page_tokens + (r % page_tokens)) * hd;
+    } else {
+        idx = (size_t)r * hd;
+    }
+    return reinterpret_cast<const KT *>(base) + idx;
+}
+
+// RMSNorm (+ optional weight) and optional NEOX RoPE of one head held by a
+// warp: lane owns elements lane + 32*k. Returns the values in x.
+template <int HD>
+__device__ __forceinline__ void norm_rope_warp(float (&x)[HD / 32], const float *w, const float2 *rope_row,
+                                               float eps, int lane) {
+    constexpr int PL = HD / 32;
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < PL; k++) {
+        float sq = __fmul_rn(x[k], x[k]);
+        ss += (double)sq;
+    }
+    ss = warp_sum_f64(ss);
+    float mean = (float)(ss / (double)HD);
+    float scale = 1.0f / sqrtf(mean + eps);
+#pragma unroll
+    for (int k = 0; k < PL; k++) {
+        float y = __fmul_rn(x[k], scale);
+        if (w) y = __fmul_rn(y, __ldg(w + lane + 32 * k));
+        x[k] = y;
+    }
+    if (rope_row) {
+#pragma unroll
+        for (int k = 0; k < PL / 2; k++) {
+            float2 sc = __ldg(rope_row + lane + 32 * k);  // (sin, cos)
+            float a = x[k], b = x[k + PL / 2];
+            x[k] = __fsub_rn(__fmul_rn(a, sc.y), __fmul_rn(b, sc.x));
+            x[k + PL / 2] = __fadd_rn(__fmul_rn(a, sc.x), __fmul_rn(b, sc.y));
+        }
+    }
+}
+
+// Sum 8 per-lane partials across the warp. On return, lanes with
+// (lane & 3) == 0 hold the total of head ((lane>>4)&1)*4 + ((lane>>3)&1)*2 + ((lane>>2)&1).
+__device__ __forceinline__ float reduce8(float (&v)[kHeads], int lane) {
+    {
+        const bool up = lane & 16;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float send = up ? v[j] : v[j + 4];
+            float keep = up ? v[j + 4] : v[j];
+            v[j] = keep + __shfl_xor_sync(kFull, send, 16);
+        }
+    }
+    {
+        const bool up = lane & 8;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            float send = up ? v[j] : v[j + 2];
+            float keep = up ? v[j + 2] : v[j];
+            v[j] = keep + __shfl_xor_sync(kFull, send, 8);
+        }
+    }
+    {
+        const bool up = lane & 4;
+        float send = up ? v[0] : v[1];
+        float keep = up ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(kFull, send, 4);
+    }
+    float r = v[0];
+    r += __shfl_xor_sync(kFull, r, 2);
+    r += __shfl_xor_sync(kFull, r, 1);
+    return r;
+}
+
+__device__ __forceinline__ int reduce8_head(int lane) {
+    return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+}
+
+// Fused decode attention: one CTA per work item (a contiguous range of cache
+// rows of one task). 8 warps; rows are processed in blocks of BLK with an
+// online softmax; partials of split tasks are merged by the last CTA.
+template <int HD, typename KT>
+__global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) {
+    constexpr int BLK = 64;
+    constexpr int PL = HD / 32;        // elements per lane in a warp-owned row
+    constexpr int CPT = HD / kDecodeThreads;  // output columns per thread
+    __shared__ __align__(16) float q_s[kHeads][HD];
+    __shared__ float s_s[kHeads][BLK];
+    __shared__ __align__(16) float knew_s[HD];
+    __shared__ __align__(16) float vnew_s[HD];
+    __shared__ float alpha_s[kHeads], m_s[kHeads], l_s[kHeads];
+    __shared__ int last_s;
+
+    const DecodeItem it = p.items[blockIdx.x];
+    const DecodeTask &tk = p.tasks[it.task];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
+    const float2 *rope = tk.global ? p.rope_global : p.rope_local;
+
+    // ---- q: norm + RoPE (model.rs:395-396), one warp per head ----
+    {
+        float x[PL];
+        const float *src = tk.q_raw + (size_t)warp * HD;
+#pragma unroll
+        for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (!tk.q_ready) norm_rope_warp<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+#pragma unroll
+        for (int k = 0; k < PL; k++) q_s[warp][lane + 32 * k] = x[k];
+    }
+    // ---- the appended token (model.rs:400-405): only the CTA holding its row ----
+    // A row appended past the attended range (position < cache length, as
+    // the reference permits) is still stored, by the task's last item.
+    const bool has_new = tk.new_row >= 0 && ((tk.new_row >= it.row_lo && tk.new_row < it.row_hi) ||
+                                             (it.split == tk.n_splits - 1 && tk.new_row >= it.row_hi));
+    if (has_new && warp < 2) {
+        float x[PL];
+        const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
+#pragma unroll
+        for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (warp == 0)
+            norm_rope_warp<HD>(x, tk.k_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+        else
+            norm_rope_warp<HD>(x, nullptr, nullptr, p.eps, lane);
+        KT *dst = const_cast<KT *>(row_ptr<KT>(warp == 0 ? tk.k_base : tk.v_base, bt, p.page_tokens, HD, tk.new_row));
+        float *sm = warp == 0 ? knew_s : vnew_s;
+#pragma unroll
+        for (int k = 0; k < PL; k++) {
+            store_elem(dst + lane + 32 * k, x[k]);
+            sm[lane + 32 * k] = round_to(x[k], (const KT *)nullptr);
+        }
+    }
+    if (threadIdx.x < kHeads) {
+        m_s[threadIdx.x] = -CUDART_INF_F;
+        l_s[threadIdx.x] = 0.0f;
+    }
+    float acc[kHeads][CPT];
+#pragma unroll
+    for (int h = 0; h < kHeads; h++)
+#pragma unroll
+        for (int u = 0; u < CPT; u++) acc[h][u] = 0.0f;
+    bool bad = false;
+    __syncthreads();
+
+    for (int b0 = it.row_lo; b0 < it.row_hi; b0 += BLK) {
+        const int nb = min(BLK, it.row_hi - b0);
+        // ---- scores: warp w takes rows w, w+8, ... of the block ----
+        for (int r = warp; r < nb; r += kHeads) {
+            const int row = b0 + r;
+            float part[kHeads];
+#pragma unroll
+            for (int h = 0; h < kHeads; h++) part[h] = 0.0f;
+            if (row == tk.new_row) {
+#pragma unroll
+                for (int k = 0; k < PL; k++) {
+                    const int e = lane + 32 * k;
+                    const float kv = knew_s[e];
+#pragma unroll
+                    for (int h = 0; h < kHeads; h++) part[h] = fmaf(q_s[h][e], kv, part[h]);
+                }
+            } else {
+                const KT *krow = row_ptr<KT>(tk.k_base, bt, p.page_tokens, HD, row);
+#pragma unroll
+                for (int k = 0; k < PL; k++) {
+                    const int e = lane + 32 * k;
+                    const float kv = load_elem(krow + e);
+#pragma unroll
+                    for (int h = 0; h < kHeads; h++) part[h] = fmaf(q_s[h][e], kv, part[h]);
+                }
+            }
+            const float tot = reduce8(part, lane);
+            if ((lane & 3) == 0) s_s[reduce8_head(lane)][r] = tot * tk.scale;
+        }
+        __syncthreads();
+        // ---- online softmax update, warp h owns head h ----
+        {
+            const int h = warp;
+            float s0 = lane < nb ? s_s[h][lane] : -CUDART_INF_F;
+            float s1 = lane + 32 < nb ? s_s[h][lane + 32] : -CUDART_INF_F;
+            if (isnan(s0) || s0 == CUDART_INF_F || isnan(s1) || s1 == CUDART_INF_F) bad = true;
+            const float bmax = warp_max(fmaxf(s0, s1));
+            const float m_old = m_s[h];
+            const float m_new = fmaxf(m_old, bmax);
+            float p0 = 0.0f, p1 = 0.0f, alpha = 1.0f;
+            if (m_new != -CUDART_INF_F) {
+                p0 = expf(s0 - m_new);
+                p1 = expf(s1 - m_new);
+                alpha = expf(m_old - m_new);
+            }
+            const float bsum = warp_sum(p0 + p1);
+            if (lane < nb) s_s[h][lane] = p0;
+            if (lane + 32 < nb) s_s[h][lane + 32] = p1;
+            __syncwarp();
+            if (lane == 0) {
+                alpha_s[h] = alpha;
+                m_s[h] = m_new;
+                l_s[h] = l_s[h] * alpha + bsum;
+            }
+        }
+        __syncthreads();
+        // ---- O += P V: thread owns columns threadIdx.x + 256*u ----
+#pragma unroll
+        for (int h = 0; h < kHeads; h++) {
+            const float a = alpha_s[h];
+#pragma unroll
+            for (int u = 0; u < CPT; u++) acc[h][u] *= a;
+        }
+        for (int r = 0; r < nb; r++) {
+            const int row = b0 + r;
+            float v[CPT];
+            if (row == tk.new_row) {
+#pragma unroll
+                for (int u = 0; u < CPT; u++) v[u] = vnew_s[threadIdx.x + kDecodeThreads * u];
+            } else {
+                const KT *vrow = row_ptr<KT>(tk.v_base, bt, p.page_tokens, HD, row);
+#pragma unroll
+                for (int u = 0; u < CPT; u++) v[u] = load_elem(vrow + threadIdx.x + kDecodeThreads * u);
+            }
+#pragma unroll
+            for (int h = 0; h < kHeads; h++) {
+                const float pr = s_s[h][r];
+#pragma unroll
+                for (int u = 0; u < CPT; u++) acc[h][u] = fmaf(pr, v[u], acc[h][u]);
+            }
+        }
+        __syncthreads();
+    }
+    if (bad) atomicOr(p.err_flag, 1);
+
+    if (tk.n_splits == 1) {
+#pragma unroll
+        for (int h = 0; h < kHeads; h++) {
+            const float l = l_s[h];
+            if (threadIdx.x == 0 && !(l > 0.0f)) atomicOr(p.err_flag, 1);
+#pragma unroll
+            for (int u = 0; u < CPT; u++) tk.out[(size_t)h * HD + threadIdx.x + kDecodeThreads * u] = acc[h][u] / l;
+        }
+        return;
+    }
+    // ---- split task: publish the partial, the last arriving CTA merges ----
+    const int slot = tk.partial_base + it.split;
+    float *po = p.part_o + (size_t)slot * kHeads * HD;
+#pragma unroll
+    for (int h = 0; h < kHeads; h++)
+#pragma unroll
+        for (int u = 0; u < CPT; u++) po[(size_t)h * HD + threadIdx.x + kDecodeThreads * u] = acc[h][u];
+    if (threadIdx.x < kHeads) {
+        p.part_ml[(size_t)slot * 2 * kHeads + threadIdx.x] = m_s[threadIdx.x];
+        p.part_ml[(size_t)slot * 2 * kHeads + kHeads + threadIdx.x] = l_s[threadIdx.x];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(p.tickets + it.task, 1u);
+        last_s = prev == (unsigned)(tk.n_splits - 1);
+    }
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    const float *pml = p.part_ml + (size_t)tk.partial_base * 2 * kHeads;
+    const float *pall = p.part_o + (size_t)tk.partial_base * kHeads * HD;
+#pragma unroll 1
+    for (int h = 0; h < kHeads; h++) {
+        float M = -CUDART_INF_F;
+        for (int s = 0; s < tk.n_splits; s++) M = fmaxf(M, __ldcg(pml + (size_t)s * 2 * kHeads + h));
+        float L = 0.0f;
+        float o[CPT];
+#pragma unroll
+        for (int u = 0; u < CPT; u++) o[u] = 0.0f;
+        for (int s = 0; s < tk.n_splits; s++) {
+            const float ms = __ldcg(pml + (size_t)s * 2 * kHeads + h);
+            const float ls = __ldcg(pml + (size_t)s * 2 * kHeads + kHeads + h);
+            const float w = ms == -CUDART_INF_F ? 0.0f : expf(ms - M);
+            L = fmaf(ls, w, L);
+#pragma unroll
+            for (int u = 0; u < CPT; u++)
+                o[u] = fmaf(__ldcg(pall + ((size_t)s * kHeads + h) * HD + threadIdx.x + kDecodeThreads * u), w, o[u]);
+        }
+        if (threadIdx.x == 0 && !(L > 0.0f)) atomicOr(p.err_flag, 1);
+#pragma unroll
+        for (int u = 0; u < CPT; u++) tk.out[(size_t)h * HD + threadIdx.x + kDecodeThreads * u] = o[u] / L;
+    }
+    if (threadIdx.x == 0) p.tickets[it.task] = 0u;  // ready for the next call
+}
+
+// Generic attend for any (n_heads, n_kv, hd <= 1024): one CTA per query
+// head, online softmax over blocks of 256 rows. Used for shapes the fused
+// E2B kernels do not serve (e.g. the reference's small synthetic models).
+__global__ void __launch_bounds__(256) attend_generic_kernel(const float *q, const float *keys, const float *values,
+                                                             int64_t len, int n_heads, int n_kv, int hd,
+                                                             float scale, float *out, int *err_flag) {
+    constexpr int BLK = 256;
+    __shared__ float q_s[1024];
+    __shared__ float p_s[BLK];
+    __shared__ float red_s[32];
+    const int h = blockIdx.x;
+    const int kvh = h * n_kv / n_heads;
+    const int width = n_kv * hd;
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) q_s[e] = q[(size_t)h * hd + e];
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float m = -CUDART_INF_F, l = 0.0f;
+    bool bad = false;
+    __syncthreads();
+    for (int64_t b0 = 0; b0 < len; b0 += BLK) {
+        const int nb = (int)min((int64_t)BLK, len - b0);
+        float s = -CUDART_INF_F;
+        if ((int)threadIdx.x < nb) {
+            const float *k = keys + (size_t)(b0 + threadIdx.x) * width + (size_t)kvh * hd;
+            float d = 0.0f;
+            for (int e = 0; e < hd; e++) d = fmaf(q_s[e], k[e], d);
+            s = d * scale;
+            if (isnan(s) || s == CUDART_INF_F) bad = true;
+        }
+        // block max
+        float bm = warp_max(s);
+        if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = bm;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float v = threadIdx.x < blockDim.x / 32 ? red_s[threadIdx.x] : -CUDART_INF_F;
+            v = warp_max(v);
+            if (threadIdx.x == 0) red_s[0] = v;
+        }
+        __syncthreads();
+        const float m_new = fmaxf(m, red_s[0]);
+        __syncthreads();
+        float pr = 0.0f, alpha = 1.0f;
+        if (m_new != -CUDART_INF_F) {
+            pr = (int)threadIdx.x < nb ? expf(s - m_new) : 0.0f;
+            alpha = expf(m - m_new);
+        }
+        p_s[threadIdx.x] = pr;
+        float bs = warp_sum(pr);
+        if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = bs;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float v = threadIdx.x < blockDim.x / 32 ? red_s[threadIdx.x] : 0.0f;
+            v = warp_sum(v);
+            if (threadIdx.x == 0) red_s[0] = v;
+        }
+        __syncthreads();
+        l = l * alpha + red_s[0];
+        m = m_new;
+        for (int u = 0; u < 4; u++) {
+            const int c = threadIdx.x + 256 * u;
+            if (c >= hd) break;
+            float a = acc[u] * alpha;
+            for (int r = 0; r < nb; r++)
+                a = fmaf(p_s[r], values[(size_t)(b0 + r) * width + (size_t)kvh * hd + c], a);
+            acc[u] = a;
+        }
+        __syncthreads();
+    }
+    if (bad || !(l > 0.0f)) atomicOr(err_flag, 1);
+    for (int u = 0; u < 4; u++) {
+        const int c = threadIdx.x + 256 * u;
+        if (c < hd) out[(size_t)h * hd + c] = acc[u] / l;
+    }
+}
+
+// Bulk append: one warp per (row, K|V). Raw mode applies k-norm + RoPE to K
+// and the unweighted norm to V (model.rs:402-404); otherwise rows are stored
+// as given.
+template <int HD, typename KT>
+__global__ void __launch_bounds__(64) append_kernel(AppendParams p) {
+    constexpr int PL = HD / 32;
+    const int row = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *src = (warp == 0 ? p.k_src : p.v_src) + (size_t)row * HD;
+    float x[PL];
+#pragma unroll
+    for (int k = 0; k < PL; k++) x[k] = src[lane + 32 * k];
+    if (p.raw) {
+        if (warp == 0)
+            norm_rope_warp<HD>(x, p.k_w, p.rope + (size_t)(p.first_pos + row) * (HD / 2), p.eps, lane);
+        else
+            norm_rope_warp<HD>(x, nullptr, nullptr, p.eps, lane);
+    }
+    const int r = p.first_row + row;
+    const int page = p.block_table[r / p.page_tokens];
+    KT *dst = reinterpret_cast<KT *>(warp == 0 ? p.k_pool : p.v_pool) +
+              ((size_t)page * p.page_tokens + (r % p.page_tokens)) * HD;
+#pragma unroll
+    for (int k = 0; k < PL; k++) store_elem(dst + lane + 32 * k, x[k]);
+}
+
+template <typename KT>
+__global__ void append_any_kernel(AppendParams p) {
+    const int row = blockIdx.x;
+    const int r = p.first_row + row;
+    const int page = p.block_table[r / p.page_tokens];
+    const size_t off = ((size_t)page * p.page_tokens + (r % p.page_tokens)) * p.hd;
+    for (int e = threadIdx.x; e < p.hd; e += blockDim.x) {
+        store_elem(reinterpret_cast<KT *>(p.k_pool) + off + e, p.k_src[(size_t)row * p.hd + e]);
+        store_elem(reinterpret_cast<KT *>(p.v_pool) + off + e, p.v_src[(size_t)row * p.hd + e]);
+    }
+}
+
+template <typename KT>
+__global__ void view_kernel(ViewParams p) {
+    const int r = blockIdx.x;
+    const int page = p.block_table[r / p.page_tokens];
+    const size_t off = ((size_t)page * p.page_tokens + (r % p.page_tokens)) * p.hd;
+    for (int e = threadIdx.x; e < p.hd; e += blockDim.x) {
+        p.k_out[(size_t)r * p.hd + e] = load_elem(reinterpret_cast<const KT *>(p.k_pool) + off + e);
+        p.v_out[(size_t)r * p.hd + e] = load_elem(reinterpret_cast<const KT *>(p.v_pool) + off + e);
+    }
+}
+
+constexpr int kMaxMergeParts = 16;
+struct MergeArgs {
+    const float *o[kMaxMergeParts];
+    const float *lse[kMaxMergeParts];
+};
+
+// out = sum_i exp(lse_i - L) out_i, L = log(sum_i exp(lse_i)); one CTA per
+// (row, head).
+__global__ void lse_merge_kernel(MergeArgs a, int n_parts, int hd, float *out, float *lse) {
+    const size_t rh = blockIdx.x;  // row * n_heads + head
+    float M = -CUDART_INF_F;
+    for (int i = 0; i < n_parts; i++) M = fmaxf(M, a.lse[i][rh]);
+    float L = 0.0f;
+    float w[kMaxMergeParts];
+    for (int i = 0; i < n_parts; i++) {
+        w[i] = M == -CUDART_INF_F ? 0.0f : expf(a.lse[i][rh] - M);
+        L += w[i];
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+        float o = 0.0f;
+        for (int i = 0; i < n_parts; i++) o = fmaf(w[i], a.o[i][rh * hd + c], o);
+        out[rh * hd + c] = o * inv;
+    }
+    if (lse && threadIdx.x == 0) lse[rh] = L > 0.0f ? M + logf(L) : -CUDART_INF_F;
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool /*fast*/, cudaStream_t s) {
+    if (p.n_items == 0) return cudaSuccess;
+    dim3 grid(p.n_items), block(kDecodeThreads);
+    if (hd == 256) {
+        if (kv_f16) decode_kernel<256, __half><<<grid, block, 0, s>>>(p);
+        else decode_kernel<256, float><<<grid, block, 0, s>>>(p);
+    } else if (hd == 512) {
+        if (kv_f16) decode_kernel<512, __half><<<grid, block, 0, s>>>(p);
+        else decode_kernel<512, float><<<grid, block, 0, s>>>(p);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attend_generic(const float *q, const float *k, const float *v, int64_t len, int n_heads, int n_kv,
+                                  int hd, float scale, float *out, int *err_flag, cudaStream_t s) {
+    attend_generic_kernel<<<n_heads, 256, 0, s>>>(q, k, v, len, n_heads, n_kv, hd, scale, out, err_flag);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_append(const AppendParams &p, int kv_f16, cudaStream_t s) {
+    if (p.n_rows == 0) return cudaSuccess;
+    if (p.hd == 256 || p.hd == 512) {
+        if (p.hd == 256) {
+            if (kv_f16) append_kernel<256, __half><<<p.n_rows, 64, 0, s>>>(p);
+            else append_kernel<256, float><<<p.n_rows, 64, 0, s>>>(p);
+        } else {
+            if (kv_f16) append_kernel<512, __half><<<p.n_rows, 64, 0, s>>>(p);
+            else append_kernel<512, float><<<p.n_rows, 64, 0, s>>>(p);
+        }
+    } else {
+        if (p.raw) return cudaErrorInvalidValue;
+        if (kv_f16) append_any_kernel<__half><<<p.n_rows, 128, 0, s>>>(p);
+        else append_any_kernel<float><<<p.n_rows, 128, 0, s>>>(p);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_view(const ViewParams &p, int kv_f16, cudaStream_t s) {
+    if (p.n_rows == 0) return cudaSuccess;
+    if (kv_f16) view_kernel<__half><<<p.n_rows, 128, 0, s>>>(p);
+    else view_kernel<float><<<p.n_rows, 128, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lse_merge(int n_parts, const float *const *parts_o, const float *const *parts_lse, int64_t rows,
+                             int n_heads, int hd, float *out, float *lse, cudaStream_t s) {
+    if (n_parts < 1 || n_parts > kMaxMergeParts) return cudaErrorInvalidValue;
+    MergeArgs a{};
+    for (int i = 0; i < n_parts; i++) {
+        a.o[i] = parts_o[i];
+        a.lse[i] = parts_lse[i];
+    }
+    const int64_t n = rows * n_heads;
+    if (n == 0) return cudaSuccess;
+    lse_merge_kernel<<<(unsigned)n, 128, 0, s>>>(a, n_parts, hd, out, lse);
+    return cudaGetLastError();
+}
+
+}  // namespace g4a

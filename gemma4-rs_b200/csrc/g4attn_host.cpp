@@ -1,0 +1,756 @@
+// Host side of g4attn: the C ABI declared in include/g4attn.h.
+//
+// Mirrors the reference's attention boundary: hyperparameters and layer
+// policies (crates/llm-gemma4/src/idea/mod.rs, eng/mod.rs), the per-layer
+// K/V memory (crates/llm-eng/src/context_memory.rs) as a paged device cache,
+// and the attention block of TransformerSpec::layer
+// (crates/llm-gemma4/src/impl_/model.rs:393-410) as one fused device call.
+// Error statuses and messages follow crates/llm-eng/src/error.rs.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/g4attn.h"
+#include "internal.h"
+
+using namespace g4a;
+
+// --------------------------------------------------------------------------
+// hyperparameters and policies
+// --------------------------------------------------------------------------
+
+extern "C" void g4a_hparams_e2b(g4a_hparams *hp) {  // idea/mod.rs:48-68
+    hp->n_layers = 35;
+    hp->n_heads = 8;
+    hp->n_kv_heads = 1;
+    hp->head_dim_local = 256;
+    hp->head_dim_global = 512;
+    hp->sliding_window = 512;
+    hp->shared_kv_layers = 20;
+    hp->local_rope_base = 10000.0f;
+    hp->global_rope_base = 1000000.0f;
+    hp->global_p = 0.25f;
+    hp->rms_norm_eps = 1e-6f;
+}
+
+extern "C" int g4a_layer_is_global(const g4a_hparams *hp, int32_t layer) {  // idea/mod.rs:148-156
+    return (layer + 1 == hp->n_layers) || (layer % 5 == 4);
+}
+
+extern "C" int32_t g4a_head_dim(const g4a_hparams *hp, int32_t layer) {  // idea/mod.rs:140-145
+    return g4a_layer_is_global(hp, layer) ? hp->head_dim_global : hp->head_dim_local;
+}
+
+extern "C" int g4a_kv_source_layer(const g4a_hparams *hp, int32_t layer, int32_t *source, int32_t *detail) {
+    // eng/mod.rs:71-90
+    const int32_t n = hp->n_layers;
+    if (layer < 0 || layer >= n) {
+        if (detail) *detail = 1;
+        return G4A_BAD_LAYER;
+    }
+    const int32_t first_shared = n - hp->shared_kv_layers;
+    if (hp->shared_kv_layers > n || first_shared <= 0) {
+        if (detail) *detail = 2;
+        return G4A_BAD_LAYER;
+    }
+    if (layer < first_shared) {
+        *source = layer;
+        return G4A_OK;
+    }
+    const int kind = g4a_layer_is_global(hp, layer);
+    for (int32_t e = first_shared - 1; e >= 0; e--) {
+        if (g4a_layer_is_global(hp, e) == kind) {
+            *source = e;
+            return G4A_OK;
+        }
+    }
+    if (detail) *detail = 3;
+    return G4A_BAD_LAYER;
+}
+
+extern "C" void g4a_windowed_len(int64_t seq_len, int64_t window, int64_t *lo, int64_t *hi) {  // eng/mod.rs:10-12
+    *lo = seq_len > window ? seq_len - window : 0;
+    *hi = seq_len;
+}
+
+extern "C" void g4a_proportional_rope_freq_factors(int32_t head_dim, float p, float *out) {  // idea/mod.rs:162-165
+    const int32_t rotated = (int32_t)((float)head_dim * p / 2.0f);
+    for (int32_t pair = 0; pair < head_dim / 2; pair++) out[pair] = pair < rotated ? 1.0f : 1e30f;
+}
+
+// --------------------------------------------------------------------------
+// context
+// --------------------------------------------------------------------------
+
+struct g4a_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    g4a_hparams hp{};
+    std::vector<float> rope_freqs;  // head_dim_global / 2 divisors
+    int32_t max_positions = 0;
+    float2 *d_rope_local = nullptr;
+    float2 *d_rope_global = nullptr;
+    int *d_err = nullptr;
+    std::string last_error;
+    float *d_part_o = nullptr;
+    size_t part_o_cap = 0;  // floats
+    float *d_part_ml = nullptr;
+    size_t part_ml_cap = 0;
+    unsigned *d_tickets = nullptr;
+    size_t tickets_cap = 0;
+    uint8_t *d_meta = nullptr;
+    size_t meta_cap = 0;
+    std::vector<uint8_t> h_meta;
+    PrefillScratch *prefill = nullptr;
+};
+
+namespace {
+
+int fail(g4a_ctx *ctx, int code, const char *fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        ctx->last_error = buf;
+    }
+    return code;
+}
+
+int cuda_fail(g4a_ctx *ctx, cudaError_t e, const char *what) {
+    return fail(ctx, G4A_CUDA, "compute: %s: %s", what, cudaGetErrorString(e));
+}
+
+#define G4A_CUDA_TRY(ctx, call)                              \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+    } while (0)
+
+// Builds (sin, cos) of every pair at positions [0, n_pos) exactly as
+// ops.rs:150-159 does: theta_scale = base^(-2/n_rot) by powf, theta grows by
+// repeated f32 multiplication, angle = theta / factor.
+std::vector<float2> rope_table(int32_t n_pos, float base, int32_t n_rot, const float *factors) {
+    const int32_t half = n_rot / 2;
+    std::vector<float2> t((size_t)n_pos * half);
+    const float theta_scale = powf(base, -2.0f / (float)n_rot);
+    for (int32_t pos = 0; pos < n_pos; pos++) {
+        float theta = (float)pos;
+        float2 *row = t.data() + (size_t)pos * half;
+        for (int32_t i = 0; i < half; i++) {
+            const float factor = factors ? factors[i] : 1.0f;
+            const float angle = theta / factor;
+            row[i] = make_float2(sinf(angle), cosf(angle));
+            theta *= theta_scale;
+        }
+    }
+    return t;
+}
+
+int ensure_rope(g4a_ctx *ctx, int32_t n_pos) {
+    if (n_pos <= ctx->max_positions && ctx->d_rope_local) return G4A_OK;
+    cudaSetDevice(ctx->device);
+    if (ctx->d_rope_local) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->d_rope_local);
+        cudaFree(ctx->d_rope_global);
+        ctx->d_rope_local = ctx->d_rope_global = nullptr;
+    }
+    const g4a_hparams &hp = ctx->hp;
+    auto loc = rope_table(n_pos, hp.local_rope_base, hp.head_dim_local, nullptr);
+    auto glo = rope_table(n_pos, hp.global_rope_base, hp.head_dim_global, ctx->rope_freqs.data());
+    G4A_CUDA_TRY(ctx, cudaMalloc(&ctx->d_rope_local, loc.size() * sizeof(float2)));
+    G4A_CUDA_TRY(ctx, cudaMalloc(&ctx->d_rope_global, glo.size() * sizeof(float2)));
+    G4A_CUDA_TRY(ctx, cudaMemcpy(ctx->d_rope_local, loc.data(), loc.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    G4A_CUDA_TRY(ctx, cudaMemcpy(ctx->d_rope_global, glo.data(), glo.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    ctx->max_positions = n_pos;
+    return G4A_OK;
+}
+
+template <typename T>
+int grow(g4a_ctx *ctx, T **ptr, size_t *cap, size_t need, bool zero) {
+    if (need <= *cap) return G4A_OK;
+    size_t n = std::max(need, *cap * 2);
+    if (*ptr) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        *cap = 0;
+    }
+    G4A_CUDA_TRY(ctx, cudaMalloc(ptr, n * sizeof(T)));
+    if (zero) G4A_CUDA_TRY(ctx, cudaMemsetAsync(*ptr, 0, n * sizeof(T), ctx->stream));
+    *cap = n;
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_ctx_create(int device, const g4a_hparams *hp, const float *rope_freqs, int32_t max_positions,
+                              g4a_ctx **out) {
+    if (!hp || !out) return G4A_COMPUTE;
+    *out = nullptr;
+    if (hp->n_layers <= 0 || hp->n_heads <= 0 || hp->n_kv_heads <= 0 || hp->n_heads % hp->n_kv_heads != 0 ||
+        hp->head_dim_local <= 0 || hp->head_dim_global <= 0 || hp->head_dim_local % 2 || hp->head_dim_global % 2 ||
+        hp->rms_norm_eps < 0.0f || max_positions <= 0)
+        return G4A_COMPUTE;  // idea/mod.rs:125-137 validate
+    auto *ctx = new g4a_ctx();
+    ctx->device = device;
+    ctx->hp = *hp;
+    ctx->rope_freqs.resize(hp->head_dim_global / 2);
+    if (rope_freqs)
+        std::copy(rope_freqs, rope_freqs + hp->head_dim_global / 2, ctx->rope_freqs.begin());
+    else
+        g4a_proportional_rope_freq_factors(hp->head_dim_global, hp->global_p, ctx->rope_freqs.data());
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return G4A_CUDA;
+    }
+    ctx->prefill = prefill_scratch_new();
+    int rc = ensure_rope(ctx, max_positions);
+    if (rc == G4A_OK) {
+        e = cudaMalloc(&ctx->d_err, sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+        if (e != cudaSuccess) rc = G4A_CUDA;
+    }
+    if (rc != G4A_OK) {
+        g4a_ctx_destroy(ctx);
+        return rc;
+    }
+    *out = ctx;
+    return G4A_OK;
+}
+
+extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->d_rope_local);
+    cudaFree(ctx->d_rope_global);
+    cudaFree(ctx->d_err);
+    cudaFree(ctx->d_part_o);
+    cudaFree(ctx->d_part_ml);
+    cudaFree(ctx->d_tickets);
+    cudaFree(ctx->d_meta);
+    prefill_scratch_free(ctx->prefill);
+    delete ctx;
+}
+
+extern "C" const char *g4a_last_error(const g4a_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "no context"; }
+
+extern "C" int g4a_ctx_set_stream(g4a_ctx *ctx, void *stream) {
+    if (!ctx) return G4A_COMPUTE;
+    ctx->stream = (cudaStream_t)stream;
+    return G4A_OK;
+}
+
+extern "C" int g4a_sync(g4a_ctx *ctx) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    int flag = 0;
+    G4A_CUDA_TRY(ctx, cudaMemcpy(&flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+        return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
+    }
+    return G4A_OK;
+}
+
+// --------------------------------------------------------------------------
+// paged KV cache
+// --------------------------------------------------------------------------
+
+struct g4a_kv {
+    g4a_ctx *ctx = nullptr;
+    int32_t n_seqs = 0, max_tokens = 0, page_tokens = 0, n_pages = 0, dtype = 0, max_pages = 0;
+    size_t elem = 4;
+    struct Layer {
+        bool held = false;
+        int32_t hd = 0;
+        void *k = nullptr, *v = nullptr;
+    };
+    std::vector<Layer> layers;       // indexed by model layer
+    std::vector<int32_t> h_bt;       // [n_seqs][max_pages], -1 = unassigned
+    int32_t *d_bt = nullptr;
+    bool bt_dirty = true;
+    std::vector<int64_t> len;        // [n_seqs][n_layers] rows stored
+    std::vector<int32_t> seq_pages;  // logical pages assigned per sequence
+    std::vector<int32_t> free_pages;
+};
+
+namespace {
+
+int64_t &kv_len(g4a_kv *kv, int32_t seq, int32_t layer) { return kv->len[(size_t)seq * kv->layers.size() + layer]; }
+
+int ensure_rows(g4a_kv *kv, int32_t seq, int64_t rows) {
+    const int32_t need = (int32_t)((rows + kv->page_tokens - 1) / kv->page_tokens);
+    while (kv->seq_pages[seq] < need) {
+        if (kv->free_pages.empty())
+            return fail(kv->ctx, G4A_OUT_OF_PAGES, "compute: KV page pool exhausted (%d pages)", kv->n_pages);
+        const int32_t page = kv->free_pages.back();
+        kv->free_pages.pop_back();
+        kv->h_bt[(size_t)seq * kv->max_pages + kv->seq_pages[seq]] = page;
+        kv->seq_pages[seq]++;
+        kv->bt_dirty = true;
+    }
+    return G4A_OK;
+}
+
+int upload_bt(g4a_kv *kv) {
+    if (!kv->bt_dirty) return G4A_OK;
+    G4A_CUDA_TRY(kv->ctx, cudaMemcpyAsync(kv->d_bt, kv->h_bt.data(), kv->h_bt.size() * sizeof(int32_t),
+                                          cudaMemcpyHostToDevice, kv->ctx->stream));
+    kv->bt_dirty = false;
+    return G4A_OK;
+}
+
+// view (context_memory.rs:53-69) checks, for a layer this cache may hold.
+int check_view(g4a_kv *kv, int32_t seq, int32_t layer, int64_t want) {
+    g4a_ctx *ctx = kv->ctx;
+    if (seq < 0 || seq >= kv->n_seqs) return fail(ctx, G4A_COMPUTE, "compute: sequence %d out of range", seq);
+    if (layer < 0 || layer >= (int32_t)kv->layers.size() || !kv->layers[layer].held) {
+        if (want == 0) return G4A_OK;
+        return fail(ctx, G4A_MISSING_LAYER, "layer %d has no cached K/V", layer);
+    }
+    const int64_t have = kv_len(kv, seq, layer);
+    if (want > have)
+        return fail(ctx, G4A_CONTEXT_TOO_LONG, "context length %lld exceeds configured max %lld", (long long)want,
+                    (long long)have);
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_kv_create(g4a_ctx *ctx, int32_t n_seqs, int32_t max_tokens, int32_t page_tokens, int32_t n_pages,
+                             int32_t dtype, const int32_t *layers, int32_t n_layers, g4a_kv **out) {
+    if (!ctx || !out) return G4A_COMPUTE;
+    *out = nullptr;
+    if (n_seqs <= 0 || max_tokens <= 0 || page_tokens <= 0 || n_pages < 0 || (dtype != G4A_KV_F32 && dtype != G4A_KV_F16))
+        return fail(ctx, G4A_COMPUTE, "compute: invalid KV cache shape");
+    cudaSetDevice(ctx->device);
+    const g4a_hparams &hp = ctx->hp;
+    auto *kv = new g4a_kv();
+    kv->ctx = ctx;
+    kv->n_seqs = n_seqs;
+    kv->max_tokens = max_tokens;
+    kv->page_tokens = page_tokens;
+    kv->max_pages = (max_tokens + page_tokens - 1) / page_tokens;
+    kv->n_pages = n_pages ? n_pages : n_seqs * kv->max_pages;
+    kv->dtype = dtype;
+    kv->elem = dtype == G4A_KV_F16 ? 2 : 4;
+    kv->layers.resize(hp.n_layers);
+    std::vector<int32_t> want;
+    if (layers) {
+        want.assign(layers, layers + n_layers);
+    } else {
+        for (int32_t l = 0; l < hp.n_layers; l++) {
+            int32_t src = -1;
+            if (g4a_kv_source_layer(&hp, l, &src, nullptr) == G4A_OK && src == l) want.push_back(l);
+        }
+    }
+    for (int32_t l : want) {
+        int32_t src = -1;
+        if (g4a_kv_source_layer(&hp, l, &src, nullptr) != G4A_OK || src != l) {
+            delete kv;
+            return fail(ctx, G4A_BAD_LAYER, "layer %d does not own a K/V cache", l);
+        }
+        auto &L = kv->layers[l];
+        if (L.held) continue;
+        L.held = true;
+        L.hd = g4a_head_dim(&hp, l) * hp.n_kv_heads;
+        const size_t bytes = (size_t)kv->n_pages * page_tokens * L.hd * kv->elem;
+        if (cudaMalloc(&L.k, bytes) != cudaSuccess || cudaMalloc(&L.v, bytes) != cudaSuccess) {
+            g4a_kv_destroy(kv);
+            return fail(ctx, G4A_CUDA, "compute: out of device memory for the KV cache");
+        }
+    }
+    kv->h_bt.assign((size_t)n_seqs * kv->max_pages, -1);
+    kv->len.assign((size_t)n_seqs * hp.n_layers, 0);
+    kv->seq_pages.assign(n_seqs, 0);
+    kv->free_pages.resize(kv->n_pages);
+    for (int32_t i = 0; i < kv->n_pages; i++) kv->free_pages[i] = kv->n_pages - 1 - i;  // pop gives 0, 1, ...
+    if (cudaMalloc(&kv->d_bt, kv->h_bt.size() * sizeof(int32_t)) != cudaSuccess) {
+        g4a_kv_destroy(kv);
+        return fail(ctx, G4A_CUDA, "compute: out of device memory for the block table");
+    }
+    int rc = ensure_rope(ctx, std::max(ctx->max_positions, max_tokens));
+    if (rc != G4A_OK) {
+        g4a_kv_destroy(kv);
+        return rc;
+    }
+    *out = kv;
+    return G4A_OK;
+}
+
+extern "C" void g4a_kv_destroy(g4a_kv *kv) {
+    if (!kv) return;
+    cudaSetDevice(kv->ctx->device);
+    cudaStreamSynchronize(kv->ctx->stream);
+    for (auto &L : kv->layers) {
+        cudaFree(L.k);
+        cudaFree(L.v);
+    }
+    cudaFree(kv->d_bt);
+    delete kv;
+}
+
+extern "C" int g4a_kv_clear(g4a_kv *kv, int32_t seq) {
+    if (!kv) return G4A_COMPUTE;
+    const int32_t lo = seq < 0 ? 0 : seq, hi = seq < 0 ? kv->n_seqs : seq + 1;
+    if (seq >= kv->n_seqs) return fail(kv->ctx, G4A_COMPUTE, "compute: sequence %d out of range", seq);
+    for (int32_t s = lo; s < hi; s++) {
+        for (int32_t j = 0; j < kv->seq_pages[s]; j++) {
+            int32_t &e = kv->h_bt[(size_t)s * kv->max_pages + j];
+            kv->free_pages.push_back(e);
+            e = -1;
+        }
+        kv->seq_pages[s] = 0;
+        for (size_t l = 0; l < kv->layers.size(); l++) kv_len(kv, s, (int32_t)l) = 0;
+    }
+    kv->bt_dirty = true;
+    return G4A_OK;
+}
+
+extern "C" int g4a_kv_len(const g4a_kv *kv, int32_t seq, int32_t layer, int64_t *len) {
+    if (!kv || !len || seq < 0 || seq >= kv->n_seqs || layer < 0 || layer >= (int32_t)kv->layers.size())
+        return G4A_COMPUTE;
+    *len = kv->len[(size_t)seq * kv->layers.size() + layer];
+    return G4A_OK;
+}
+
+namespace {
+
+int append_impl(g4a_kv *kv, int32_t seq, int32_t layer, const float *k, const float *v, const float *k_w,
+                int64_t n, bool raw) {
+    g4a_ctx *ctx = kv->ctx;
+    cudaSetDevice(ctx->device);
+    if (seq < 0 || seq >= kv->n_seqs) return fail(ctx, G4A_COMPUTE, "compute: sequence %d out of range", seq);
+    if (layer < 0 || layer >= (int32_t)kv->layers.size() || !kv->layers[layer].held)
+        return fail(ctx, G4A_MISSING_LAYER, "layer %d has no cached K/V", layer);
+    if (n < 0 || (n > 0 && (!k || !v))) return fail(ctx, G4A_COMPUTE, "compute: invalid append rows");
+    if (raw && !k_w) return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `blk.%d.attn_k_norm.weight`", layer);
+    const auto &L = kv->layers[layer];
+    if (raw && L.hd != 256 && L.hd != 512)
+        return fail(ctx, G4A_COMPUTE, "compute: fused norm/RoPE append needs head width 256 or 512");
+    int64_t &len = kv_len(kv, seq, layer);
+    if (len + n > kv->max_tokens)
+        return fail(ctx, G4A_CONTEXT_TOO_LONG, "context length %lld exceeds configured max %d", (long long)(len + n),
+                    kv->max_tokens);
+    if (raw && len + n > ctx->max_positions)
+        return fail(ctx, G4A_CONTEXT_TOO_LONG, "context length %lld exceeds configured max %d", (long long)(len + n),
+                    ctx->max_positions);
+    int rc = ensure_rows(kv, seq, len + n);
+    if (rc) return rc;
+    if ((rc = upload_bt(kv))) return rc;
+    AppendParams p{};
+    p.k_pool = L.k;
+    p.v_pool = L.v;
+    p.block_table = kv->d_bt + (size_t)seq * kv->max_pages;
+    p.k_src = k;
+    p.v_src = v;
+    p.k_w = k_w;
+    const bool global = g4a_layer_is_global(&ctx->hp, layer);
+    p.rope = global ? ctx->d_rope_global : ctx->d_rope_local;
+    p.hd = L.hd;
+    p.page_tokens = kv->page_tokens;
+    p.first_row = (int32_t)len;
+    p.first_pos = (int32_t)len;
+    p.n_rows = (int32_t)n;
+    p.raw = raw;
+    p.eps = ctx->hp.rms_norm_eps;
+    G4A_CUDA_TRY(ctx, launch_append(p, kv->dtype == G4A_KV_F16, ctx->stream));
+    len += n;
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_kv_append(g4a_kv *kv, int32_t seq, int32_t layer, const float *k, const float *v, int64_t n) {
+    if (!kv) return G4A_COMPUTE;
+    return append_impl(kv, seq, layer, k, v, nullptr, n, false);
+}
+
+extern "C" int g4a_kv_append_tokens(g4a_kv *kv, int32_t seq, int32_t layer, const float *k_raw, const float *v_raw,
+                                    const float *k_w, int64_t n) {
+    if (!kv) return G4A_COMPUTE;
+    return append_impl(kv, seq, layer, k_raw, v_raw, k_w, n, true);
+}
+
+extern "C" int g4a_kv_view(const g4a_kv *kv_c, int32_t seq, int32_t layer, int64_t len, float *k_out, float *v_out) {
+    if (!kv_c) return G4A_COMPUTE;
+    auto *kv = const_cast<g4a_kv *>(kv_c);
+    g4a_ctx *ctx = kv->ctx;
+    cudaSetDevice(ctx->device);
+    int rc = check_view(kv, seq, layer, len);
+    if (rc || len == 0) return rc;
+    if (!k_out || !v_out) return fail(ctx, G4A_COMPUTE, "compute: null view output");
+    if ((rc = upload_bt(kv))) return rc;
+    ViewParams p{};
+    p.k_pool = kv->layers[layer].k;
+    p.v_pool = kv->layers[layer].v;
+    p.block_table = kv->d_bt + (size_t)seq * kv->max_pages;
+    p.k_out = k_out;
+    p.v_out = v_out;
+    p.hd = kv->layers[layer].hd;
+    p.page_tokens = kv->page_tokens;
+    p.n_rows = (int32_t)len;
+    G4A_CUDA_TRY(ctx, launch_view(p, kv->dtype == G4A_KV_F16, ctx->stream));
+    return G4A_OK;
+}
+
+// --------------------------------------------------------------------------
+// decode
+// --------------------------------------------------------------------------
+
+namespace {
+
+struct Plan {
+    std::vector<DecodeTask> tasks;
+    std::vector<DecodeItem> items[2];  // by head width: [0] 256, [1] 512
+    int32_t slots = 0;
+};
+
+// Rows per work item. Aims at about two items per SM over the whole call,
+// weighting rows by head width, with at least 16 rows per item.
+int32_t rows_per_item(int64_t weighted_total, int32_t weight) {
+    const int64_t target_items = 2 * 148;
+    int64_t w = (weighted_total + target_items - 1) / target_items;
+    int64_t rows = (w + weight - 1) / weight;
+    rows = std::max<int64_t>(16, (rows + 15) / 16 * 16);
+    return (int32_t)std::min<int64_t>(rows, 1 << 20);
+}
+
+void add_items(Plan &plan, DecodeTask &t, int32_t task_index, int32_t rows_per, int which) {
+    const int32_t n_rows = t.hi - t.lo;
+    const int32_t n = std::max<int32_t>(1, (n_rows + rows_per - 1) / rows_per);
+    t.n_splits = n;
+    t.partial_base = n > 1 ? plan.slots : 0;
+    if (n > 1) plan.slots += n;
+    for (int32_t s = 0; s < n; s++) {
+        DecodeItem it;
+        it.task = task_index;
+        it.split = s;
+        it.row_lo = t.lo + (int32_t)((int64_t)n_rows * s / n);
+        it.row_hi = t.lo + (int32_t)((int64_t)n_rows * (s + 1) / n);
+        plan.items[which].push_back(it);
+    }
+}
+
+int run_plan(g4a_ctx *ctx, Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens, int kv_f16) {
+    const size_t n_tasks = plan.tasks.size();
+    const size_t n_items = plan.items[0].size() + plan.items[1].size();
+    const size_t bytes_tasks = n_tasks * sizeof(DecodeTask);
+    const size_t bytes = bytes_tasks + n_items * sizeof(DecodeItem);
+    int rc;
+    if ((rc = grow(ctx, &ctx->d_meta, &ctx->meta_cap, bytes, false))) return rc;
+    if ((rc = grow(ctx, &ctx->d_part_o, &ctx->part_o_cap, (size_t)std::max(plan.slots, 1) * kHeads * 512, false)))
+        return rc;
+    if ((rc = grow(ctx, &ctx->d_part_ml, &ctx->part_ml_cap, (size_t)std::max(plan.slots, 1) * 2 * kHeads, false)))
+        return rc;
+    if ((rc = grow(ctx, &ctx->d_tickets, &ctx->tickets_cap, std::max<size_t>(n_tasks, 1), true))) return rc;
+    ctx->h_meta.resize(bytes);
+    std::memcpy(ctx->h_meta.data(), plan.tasks.data(), bytes_tasks);
+    std::memcpy(ctx->h_meta.data() + bytes_tasks, plan.items[0].data(), plan.items[0].size() * sizeof(DecodeItem));
+    std::memcpy(ctx->h_meta.data() + bytes_tasks + plan.items[0].size() * sizeof(DecodeItem), plan.items[1].data(),
+                plan.items[1].size() * sizeof(DecodeItem));
+    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->d_meta, ctx->h_meta.data(), bytes, cudaMemcpyHostToDevice, ctx->stream));
+    DecodeParams p{};
+    p.tasks = reinterpret_cast<const DecodeTask *>(ctx->d_meta);
+    p.block_table = d_bt;
+    p.max_pages = max_pages;
+    p.page_tokens = page_tokens;
+    p.rope_local = ctx->d_rope_local;
+    p.rope_global = ctx->d_rope_global;
+    p.eps = ctx->hp.rms_norm_eps;
+    p.part_o = ctx->d_part_o;
+    p.part_ml = ctx->d_part_ml;
+    p.tickets = ctx->d_tickets;
+    p.err_flag = ctx->d_err;
+    const DecodeItem *items = reinterpret_cast<const DecodeItem *>(ctx->d_meta + bytes_tasks);
+    for (int which = 0; which < 2; which++) {
+        p.items = items;
+        p.n_items = (int32_t)plan.items[which].size();
+        G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, kv_f16, true, ctx->stream));
+        items += plan.items[which].size();
+    }
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_attend(g4a_ctx *ctx, const float *q, const float *keys, const float *values, int64_t len,
+                          int32_t n_heads, int32_t n_kv, int32_t hd, float scale, float *out) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (n_heads <= 0 || n_kv <= 0 || hd <= 0 || n_heads % n_kv != 0 || len < 0 || !q || !out)
+        return fail(ctx, G4A_COMPUTE, "compute: invalid attention shape");
+    if (len == 0) return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");  // model.rs:337,362-364
+    if (!keys || !values) return fail(ctx, G4A_COMPUTE, "compute: null keys or values");
+    if (n_heads == kHeads && n_kv == 1 && (hd == 256 || hd == 512) && len < (1LL << 31)) {
+        Plan plan;
+        DecodeTask t{};
+        t.k_base = keys;
+        t.v_base = values;
+        t.q_raw = q;
+        t.out = out;
+        t.lo = 0;
+        t.hi = (int32_t)len;
+        t.new_row = -1;
+        t.q_ready = 1;
+        t.scale = scale;
+        const int which = hd == 512;
+        add_items(plan, t, 0, rows_per_item(len * (hd / 256), hd / 256), which);
+        plan.tasks.push_back(t);
+        return run_plan(ctx, plan, nullptr, 0, 1, 0);
+    }
+    if (hd > 1024) return fail(ctx, G4A_COMPUTE, "compute: head width %d above 1024", hd);
+    G4A_CUDA_TRY(ctx, launch_attend_generic(q, keys, values, len, n_heads, n_kv, hd, scale, out, ctx->d_err, ctx->stream));
+    return G4A_OK;
+}
+
+extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
+                          const int32_t *seq_ids, const int32_t *positions) {
+    if (!ctx || !kv || kv->ctx != ctx) return fail(ctx, G4A_COMPUTE, "compute: cache belongs to another context");
+    cudaSetDevice(ctx->device);
+    const g4a_hparams &hp = ctx->hp;
+    if (n_layers < 0 || n_seqs < 0 || (n_layers > 0 && !layers) || (n_seqs > 0 && (!seq_ids || !positions)))
+        return fail(ctx, G4A_COMPUTE, "compute: invalid decode arguments");
+    if (hp.n_heads != kHeads || hp.n_kv_heads != 1)
+        return fail(ctx, G4A_COMPUTE, "compute: fused decode serves %d query heads over 1 KV head", kHeads);
+    // ---- validate layers (model.rs:389-399) ----
+    std::vector<int32_t> src(n_layers), hd(n_layers);
+    std::vector<char> owner(n_layers), global(n_layers);
+    for (int32_t i = 0; i < n_layers; i++) {
+        const g4a_decode_layer &a = layers[i];
+        int32_t detail = 0;
+        if (g4a_kv_source_layer(&hp, a.layer, &src[i], &detail) != G4A_OK)
+            return fail(ctx, G4A_BAD_LAYER, "compute: layer %d has no KV source (kind %d)", a.layer, detail);
+        owner[i] = src[i] == a.layer;
+        global[i] = (char)g4a_layer_is_global(&hp, a.layer);
+        hd[i] = g4a_head_dim(&hp, a.layer);
+        if (hd[i] != 256 && hd[i] != 512) return fail(ctx, G4A_COMPUTE, "compute: head width %d unsupported", hd[i]);
+        if (!a.q_raw_dev || !a.out_dev) return fail(ctx, G4A_COMPUTE, "compute: null q or output");
+        if (!a.q_norm_w_dev) return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `blk.%d.attn_q_norm.weight`", a.layer);
+        if (owner[i] && (!a.k_raw_dev || !a.v_raw_dev))
+            return fail(ctx, G4A_COMPUTE, "compute: layer %d owns its cache and needs k and v", a.layer);
+        if (owner[i] && !a.k_norm_w_dev)
+            return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `blk.%d.attn_k_norm.weight`", a.layer);
+        if (src[i] >= (int32_t)kv->layers.size() || !kv->layers[src[i]].held)
+            return fail(ctx, G4A_MISSING_LAYER, "layer %d has no cached K/V", src[i]);
+        for (int32_t j = 0; j < n_layers; j++)
+            if (j != i && (layers[j].layer == a.layer || (!owner[i] && layers[j].layer == src[i])))
+                return fail(ctx, G4A_COMPUTE, "compute: layer %d listed with itself or its KV source", a.layer);
+    }
+    // ---- validate sequences and positions (context_memory.rs:53-69) ----
+    std::vector<char> seen(kv->n_seqs, 0);
+    for (int32_t j = 0; j < n_seqs; j++) {
+        const int32_t s = seq_ids[j];
+        if (s < 0 || s >= kv->n_seqs) return fail(ctx, G4A_COMPUTE, "compute: sequence %d out of range", s);
+        if (seen[s]) return fail(ctx, G4A_COMPUTE, "compute: sequence %d listed twice", s);
+        seen[s] = 1;
+        const int64_t pos = positions[j];
+        if (pos < 0) return fail(ctx, G4A_COMPUTE, "compute: negative position");
+        if (pos >= ctx->max_positions)
+            return fail(ctx, G4A_CONTEXT_TOO_LONG, "context length %lld exceeds configured max %d", (long long)pos + 1,
+                        ctx->max_positions);
+        for (int32_t i = 0; i < n_layers; i++) {
+            if (owner[i]) {
+                const int64_t new_row = kv_len(kv, s, layers[i].layer);
+                if (new_row + 1 > kv->max_tokens)
+                    return fail(ctx, G4A_CONTEXT_TOO_LONG, "context length %lld exceeds configured max %d",
+                                (long long)new_row + 1, kv->max_tokens);
+                if (pos + 1 > new_row + 1)
+                    return fail(ctx, G4A_CONTEXT_TOO_LONG, "context length %lld exceeds configured max %lld",
+                                (long long)pos + 1, (long long)new_row + 1);
+            } else {
+                int rc = check_view(kv, s, src[i], pos + 1);
+                if (rc) return rc;
+            }
+        }
+    }
+    // ---- allocate rows for the appends, then plan ----
+    for (int32_t j = 0; j < n_seqs; j++)
+        for (int32_t i = 0; i < n_layers; i++)
+            if (owner[i]) {
+                int rc = ensure_rows(kv, seq_ids[j], kv_len(kv, seq_ids[j], layers[i].layer) + 1);
+                if (rc) return rc;
+            }
+    int rc = upload_bt(kv);
+    if (rc) return rc;
+    Plan plan;
+    int64_t weighted = 0;
+    std::vector<int64_t> lo_hi;
+    for (int32_t i = 0; i < n_layers; i++)
+        for (int32_t j = 0; j < n_seqs; j++) {
+            int64_t lo, hi;
+            if (global[i]) lo = 0, hi = (int64_t)positions[j] + 1;
+            else g4a_windowed_len((int64_t)positions[j] + 1, hp.sliding_window, &lo, &hi);
+            weighted += (hi - lo) * (hd[i] / 256);
+        }
+    for (int32_t i = 0; i < n_layers; i++) {
+        const g4a_decode_layer &a = layers[i];
+        const auto &L = kv->layers[src[i]];
+        const int which = hd[i] == 512;
+        const int32_t rows_per = rows_per_item(weighted, hd[i] / 256);
+        for (int32_t j = 0; j < n_seqs; j++) {
+            const int32_t s = seq_ids[j];
+            DecodeTask t{};
+            t.k_base = L.k;
+            t.v_base = L.v;
+            const size_t qw = (size_t)kHeads * hd[i];
+            t.q_raw = a.q_raw_dev + (size_t)j * qw;
+            t.k_raw = owner[i] ? a.k_raw_dev + (size_t)j * hd[i] : nullptr;
+            t.v_raw = owner[i] ? a.v_raw_dev + (size_t)j * hd[i] : nullptr;
+            t.q_w = a.q_norm_w_dev;
+            t.k_w = a.k_norm_w_dev;
+            t.out = a.out_dev + (size_t)j * qw;
+            t.seq = s;
+            t.position = positions[j];
+            int64_t lo, hi;
+            if (global[i]) lo = 0, hi = (int64_t)positions[j] + 1;
+            else g4a_windowed_len((int64_t)positions[j] + 1, hp.sliding_window, &lo, &hi);
+            t.lo = (int32_t)lo;
+            t.hi = (int32_t)hi;
+            t.new_row = owner[i] ? (int32_t)kv_len(kv, s, a.layer) : -1;
+            t.global = global[i];
+            t.q_ready = 0;
+            t.scale = 1.0f;
+            add_items(plan, t, (int32_t)plan.tasks.size(), rows_per, which);
+            plan.tasks.push_back(t);
+        }
+    }
+    if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16))) return rc;
+    for (int32_t i = 0; i < n_layers; i++)
+        if (owner[i])
+            for (int32_t j = 0; j < n_seqs; j++) kv_len(kv, seq_ids[j], layers[i].layer) += 1;
+    return G4A_OK;
+}
+
+extern "C" int g4a_lse_merge(g4a_ctx *ctx, int32_t n_parts, const float *const *parts_out, const float *const *parts_lse,
+                             int64_t rows, int32_t n_heads, int32_t hd, float *out, float *lse) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (n_parts < 1 || n_parts > 16 || rows < 0 || n_heads <= 0 || hd <= 0 || !parts_out || !parts_lse || !out)
+        return fail(ctx, G4A_COMPUTE, "compute: invalid merge arguments");
+    G4A_CUDA_TRY(ctx, launch_lse_merge(n_parts, parts_out, parts_lse, rows, n_heads, hd, out, lse, ctx->stream));
+    return G4A_OK;
+}
+
+extern "C" int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *problems) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (ctx->hp.n_heads != kHeads || ctx->hp.n_kv_heads != 1)
+        return fail(ctx, G4A_COMPUTE, "compute: prefill serves %d query heads over 1 KV head", kHeads);
+    const char *msg = "";
+    const int rc = prefill_run(ctx->prefill, ctx->d_err, n, problems, ctx->stream, &msg);
+    if (rc != G4A_OK) return fail(ctx, rc, "compute: %s", msg);
+    return G4A_OK;
+}

@@ -1,0 +1,95 @@
+// Shared host/device definitions of the g4attn library (not part of the ABI).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace g4a {
+
+// Query heads per KV head served by the fused E2B kernels (idea/mod.rs:53-54:
+// 8 query heads, 1 KV head).
+constexpr int kHeads = 8;
+// Threads of a decode CTA: one warp per query head in the q-preparation phase.
+constexpr int kDecodeThreads = 256;
+
+// One (sequence, layer) attention task of a decode call.
+struct DecodeTask {
+    const void *k_base;   // paged: the layer's K page pool; contiguous: row 0
+    const void *v_base;
+    const float *q_raw;   // [kHeads][hd] raw q of this task (or ready q)
+    const float *k_raw;   // [hd] raw k of the appended token (owners only)
+    const float *v_raw;
+    const float *q_w;     // attn_q_norm weight [hd]
+    const float *k_w;     // attn_k_norm weight [hd]
+    float *out;           // [kHeads][hd]
+    int32_t seq;          // row of the block table
+    int32_t position;     // RoPE position of the query (and of the new key)
+    int32_t lo, hi;       // rows attended: [lo, hi)
+    int32_t new_row;      // cache row receiving the new token, -1 if none
+    int32_t n_splits;     // work items of this task
+    int32_t partial_base; // first partial slot of this task
+    int32_t global;       // 1 = global RoPE table
+    int32_t q_ready;      // 1 = q is already normalised and rotated
+    float scale;          // score scale (1.0 in the model, model.rs:409)
+    int32_t pad;
+};
+
+// One CTA's share of a task: cache rows [row_lo, row_hi).
+struct DecodeItem {
+    int32_t task, split, row_lo, row_hi;
+};
+
+struct DecodeParams {
+    const DecodeTask *tasks;
+    const DecodeItem *items;
+    const int32_t *block_table;  // [n_seqs][max_pages]; nullptr = contiguous rows
+    int32_t max_pages;
+    int32_t page_tokens;
+    const float2 *rope_local;    // [max_positions][hd_local/2] (sin, cos)
+    const float2 *rope_global;   // [max_positions][hd_global/2]
+    float eps;
+    float *part_o;               // [slots][kHeads][hd]
+    float *part_ml;              // [slots][2][kHeads] (max, sum)
+    unsigned *tickets;           // [tasks] arrival counters, zero between calls
+    int *err_flag;               // bit 0: non-finite softmax
+    int32_t n_items;
+};
+
+// Bulk append of already processed rows, or norm+RoPE of raw rows.
+struct AppendParams {
+    void *k_pool, *v_pool;       // the layer's pools
+    const int32_t *block_table;  // this sequence's row of the block table
+    const float *k_src, *v_src;  // [n][hd]
+    const float *k_w;            // k norm weight (raw mode)
+    const float2 *rope;          // table of this layer kind (raw mode)
+    int32_t hd, page_tokens, first_row, first_pos, n_rows, raw;
+    float eps;
+};
+
+struct ViewParams {
+    const void *k_pool, *v_pool;
+    const int32_t *block_table;
+    float *k_out, *v_out;
+    int32_t hd, page_tokens, n_rows;
+};
+
+// Launchers (decode.cu).
+cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, cudaStream_t s);
+cudaError_t launch_attend_generic(const float *q, const float *k, const float *v, int64_t len, int n_heads,
+                                  int n_kv, int hd, float scale, float *out, int *err_flag, cudaStream_t s);
+cudaError_t launch_append(const AppendParams &p, int kv_f16, cudaStream_t s);
+cudaError_t launch_view(const ViewParams &p, int kv_f16, cudaStream_t s);
+cudaError_t launch_lse_merge(int n_parts, const float *const *parts_o, const float *const *parts_lse,
+                             int64_t rows, int n_heads, int hd, float *out, float *lse, cudaStream_t s);
+
+// Prefill (prefill_sm100.cu): per-context scratch and the launcher behind
+// g4a_prefill. Returns a g4a_status and points *msg at a description.
+struct PrefillScratch;
+PrefillScratch *prefill_scratch_new();
+void prefill_scratch_free(PrefillScratch *s);
+int prefill_run(PrefillScratch *s, int *d_err, int32_t n, const struct g4a_prefill_problem *problems,
+                cudaStream_t st, const char **msg);
+
+}  // namespace g4a

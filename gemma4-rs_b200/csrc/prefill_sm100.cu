@@ -1,0 +1,612 @@
+// Causal / sliding-window prefill attention on sm_100a tensor cores.
+//
+// Replaces the reference's token-at-a-time prompt processing, in which query
+// position t runs crates/llm-gemma4/src/impl_/model.rs:326-366 (attend) over
+// keys [max(0, t+1-window), t] (crates/llm-gemma4/src/eng/mod.rs:10-36), with
+// one batched kernel over bf16 inputs and f32 accumulation.
+//
+// Tiling. A CTA owns 16 query tokens x 8 heads = 128 rows (the tcgen05 M
+// dimension), so each K/V tile it loads serves all 8 heads of the single KV
+// head (grouped-query reuse without any multicast), and one 256-wide half of
+// the head dimension of the output (head width 512 runs two CTAs per row tile
+// that each recompute S over the full width). Keys come in tiles of 128.
+//
+// Roles (192 threads):
+//   warp 0      TMA producer: Q once, then K and V boxes (64 columns x 128
+//               rows, 128-byte swizzle) through a ring of 16 KB slots.
+//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma:
+//               S = Q K^T (bf16, f32 in TMEM, double-buffered 2 x 128 cols),
+//               O += P V (P fp16 read from TMEM, V fp16 from shared memory,
+//               N = 256, f32 accumulator in TMEM cols 0-255).
+//   warps 2-5   softmax: one TMEM lane (row) per thread; mask, row max,
+//               exp2, P written back into the S columns as fp16; the running
+//               max is rescaled lazily (only when it grows by more than 2^8),
+//               then the epilogue divides by the row sum and stores f32.
+// Every mbarrier wait is bounded; on time-out the CTA records an error flag,
+// drains its own TMA loads and MMAs, frees TMEM and exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "../../include/g4attn.h"
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace g4a {
+namespace {
+
+constexpr int kRows = 128;          // tcgen05 M: 16 tokens x 8 heads
+constexpr int kTokensPerTile = 16;
+constexpr int kKeysPerTile = 128;   // tcgen05 N of S
+constexpr int kDV = 256;            // output columns per CTA
+constexpr int kBoxBytes = 128 * 128;  // 64 bf16 columns x 128 rows
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 0, kColS0 = 256, kColS1 = 384;
+constexpr uint32_t kWaitLimit = 1u << 22;  // polls; far above any legitimate wait
+
+struct alignas(64) ProblemDev {
+    CUtensorMap tq, tk, tv;  // Q [n_q*8, hd] bf16, K [n_kv, hd] bf16, V [n_kv, hd] fp16
+    int32_t hd, window, n_q, q_pos0, n_kv, kv_pos0;
+    float *out;
+    float *lse;
+};
+
+struct WorkItem {
+    int32_t problem, q_tile, dv_half, kv_tile_lo, n_kv_tiles, pad;
+};
+
+template <int HD>
+struct Cfg {
+    static constexpr int kQBoxes = HD / 64;
+    static constexpr int kRing = HD == 256 ? 8 : 4;  // slots; a multiple of 4 (V groups never wrap)
+    static constexpr int kSmemQ = kQBoxes * kBoxBytes;
+    static constexpr int kSmemRing = kRing * kBoxBytes;
+    static constexpr int kSmemBytes = kSmemQ + kSmemRing + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+};
+
+struct Barriers {
+    uint64_t q_full;
+    uint64_t s_full[2];
+    uint64_t p_full[2];
+    uint64_t o_done;
+    uint64_t mma_done;
+    uint64_t ring_full[8];
+    uint64_t ring_empty[8];
+    uint32_t tmem_base;
+    int abort;
+};
+
+// Bounded wait: false if another role aborted or the limit ran out (which
+// aborts the CTA and records bit 1 of the error flag).
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023) == 1023 && *abort) return false;
+    }
+    *abort = 1;
+    atomicOr(err, 2);
+    return false;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
+    using C = Cfg<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *q_smem = smem;
+    uint8_t *ring = smem + C::kSmemQ;
+    Barriers *bars = reinterpret_cast<Barriers *>(ring + C::kSmemRing);
+    volatile int *abort = &bars->abort;
+
+    const WorkItem it = items[blockIdx.x];
+    const ProblemDev &pb = problems[it.problem];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = it.n_kv_tiles;
+
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bars->q_full, 1);
+        for (int i = 0; i < 2; i++) {
+            ptx::mbar_init(&bars->s_full[i], 1);
+            ptx::mbar_init(&bars->p_full[i], 128);
+        }
+        ptx::mbar_init(&bars->o_done, 1);
+        ptx::mbar_init(&bars->mma_done, 1);
+        for (int i = 0; i < C::kRing; i++) {
+            ptx::mbar_init(&bars->ring_full[i], 1);
+            ptx::mbar_init(&bars->ring_empty[i], 1);
+        }
+        bars->abort = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(&bars->tmem_base, kTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0 && n_tiles > 0) {
+            ptx::prefetch_tmap(&pb.tq);
+            ptx::prefetch_tmap(&pb.tk);
+            ptx::prefetch_tmap(&pb.tv);
+            ptx::mbar_arrive_expect_tx(&bars->q_full, C::kSmemQ);
+            for (int c = 0; c < C::kQBoxes; c++)
+                ptx::tma_load_2d(q_smem + c * kBoxBytes, &pb.tq, &bars->q_full, 64 * c, it.q_tile * kRows);
+            int slot = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;  // bit s: slot s received at least one load
+            bool ok = true;
+            auto push = [&](const CUtensorMap *m, int x, int y) {
+                if (!ok) return;
+                if (!wait_bar(&bars->ring_empty[slot], phase ^ 1u, abort, err)) {
+                    ok = false;
+                    return;
+                }
+                ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], kBoxBytes);
+                ptx::tma_load_2d(ring + slot * kBoxBytes, m, &bars->ring_full[slot], x, y);
+                issued |= 1u << slot;
+                if (++slot == C::kRing) {
+                    slot = 0;
+                    phase ^= 1u;
+                }
+            };
+            auto push_k = [&](int j) {
+                for (int c = 0; c < C::kQBoxes; c++) push(&pb.tk, 64 * c, (it.kv_tile_lo + j) * kKeysPerTile);
+            };
+            auto push_v = [&](int j) {
+                for (int c = 0; c < kDV / 64; c++)
+                    push(&pb.tv, it.dv_half * kDV + 64 * c, (it.kv_tile_lo + j) * kKeysPerTile);
+            };
+            push_k(0);
+            for (int j = 0; j < n_tiles && ok; j++) {
+                if (j + 1 < n_tiles) push_k(j + 1);
+                push_v(j);
+            }
+            // Drain: no TMA write may land after the CTA exits. Normally the
+            // MMA thread already waited for every load; after an abort, wait
+            // here (bounded) for Q and for each slot's latest load.
+            for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->q_full, 0); i++) {
+            }
+            if (!ok || *abort) {
+                for (int s = 0; s < C::kRing; s++) {
+                    if (!(issued >> s & 1u)) continue;
+                    const uint32_t ph = s < slot ? phase : phase ^ 1u;
+                    for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->ring_full[s], ph); i++) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, kRows, kKeysPerTile);
+            constexpr uint32_t kIdescPV = ptx::idesc_f16(0, 0, 1, kRows, kDV);
+            const uint32_t q_base = ptx::smem_u32(q_smem);
+            const uint32_t ring_base = ptx::smem_u32(ring);
+            int slot = 0;
+            uint32_t phase = 0;
+            bool ok = n_tiles > 0 && wait_bar(&bars->q_full, 0, abort, err);
+            if (ok) ptx::tc_fence_after();
+            auto advance = [&](int n) {
+                slot += n;
+                if (slot >= C::kRing) {
+                    slot -= C::kRing;
+                    phase ^= 1u;
+                }
+            };
+            auto issue_s = [&](int j) {
+                const uint32_t d = tmem + ((j & 1) ? kColS1 : kColS0);
+                for (int c = 0; c < C::kQBoxes && ok; c++) {
+                    if (!wait_bar(&bars->ring_full[slot], phase, abort, err)) {
+                        ok = false;
+                        return;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t kb = ring_base + slot * kBoxBytes;
+                    const uint32_t qb = q_base + c * kBoxBytes;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        ptx::mma_ss(d, ptx::smem_desc(qb + 32 * kk, 16, 1024), ptx::smem_desc(kb + 32 * kk, 16, 1024),
+                                    kIdescS, (c | kk) != 0);
+                    }
+                    ptx::mma_commit(&bars->ring_empty[slot]);
+                    advance(1);
+                }
+                ptx::mma_commit(&bars->s_full[j & 1]);
+            };
+            auto issue_pv = [&](int j) {
+                if (!wait_bar(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, abort, err)) {
+                    ok = false;
+                    return;
+                }
+                for (int c = 0; c < 4; c++)
+                    if (!wait_bar(&bars->ring_full[slot + c], phase, abort, err)) {
+                        ok = false;
+                        return;
+                    }
+                ptx::tc_fence_after();
+                const uint32_t vb = ring_base + slot * kBoxBytes;
+                const uint32_t p_tmem = tmem + ((j & 1) ? kColS1 : kColS0);
+#pragma unroll
+                for (int ks = 0; ks < kKeysPerTile / 16; ks++) {
+                    ptx::mma_ts(tmem + kColO, p_tmem + 8 * ks, ptx::smem_desc(vb + 2048 * ks, kBoxBytes, 1024),
+                                kIdescPV, (j > 0 || ks > 0));
+                }
+                for (int c = 0; c < 4; c++) ptx::mma_commit(&bars->ring_empty[slot + c]);
+                ptx::mma_commit(&bars->o_done);
+                advance(4);
+            };
+            if (ok) {
+                issue_s(0);
+                for (int j = 0; j < n_tiles && ok; j++) {
+                    if (j + 1 < n_tiles) issue_s(j + 1);
+                    if (ok) issue_pv(j);
+                }
+            }
+            // Every issued MMA completes before TMEM is released.
+            ptx::mma_commit(&bars->mma_done);
+            for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->mma_done, 0); i++) {
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax + epilogue
+        const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
+        const int row = quad * 32 + lane;           // tile row = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const int tok = it.q_tile * kTokensPerTile + row / 8;
+        const int head = row % 8;
+        const bool row_valid = tok < pb.n_q;
+        const int qpos = pb.q_pos0 + tok;
+        const float kLog2e = 1.4426950408889634f;
+        float m_used = -CUDART_INF_F;  // running max in log2 units
+        float l = 0.0f;
+        bool ok = true;
+        // tcgen05.ld/st are warp-collective (.sync.aligned): every branch that
+        // contains one is decided by a warp vote, never per row.
+        for (int j = 0; j < n_tiles && ok; j++) {
+            if (!__all_sync(0xffffffffu, wait_bar(&bars->s_full[j & 1], (uint32_t)(j >> 1) & 1u, abort, err))) {
+                ok = false;
+                break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t s_addr = tmem + lane_addr + ((j & 1) ? kColS1 : kColS0);
+            float s[kKeysPerTile];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                uint32_t r[32];
+                ptx::tmem_ld32(s_addr + 32 * c, r);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++) s[32 * c + i] = __uint_as_float(r[i]);
+            }
+            const int k0 = (it.kv_tile_lo + j) * kKeysPerTile;
+            float mx = -CUDART_INF_F;
+#pragma unroll
+            for (int i = 0; i < kKeysPerTile; i++) {
+                const int kidx = k0 + i;
+                const int kpos = pb.kv_pos0 + kidx;
+                const bool valid =
+                    row_valid && kidx < pb.n_kv && kpos <= qpos && (pb.window == 0 || qpos - kpos < pb.window);
+                s[i] = valid ? s[i] * kLog2e : -CUDART_INF_F;
+                mx = fmaxf(mx, s[i]);
+            }
+            // Lazy rescale: move this row's reference max only when the tile
+            // max exceeds it by more than 8 (P then stays below 2^8).
+            const bool grow = mx > m_used + 8.0f;
+            const bool o_live = grow && m_used != -CUDART_INF_F;  // O holds weights of the old max
+            if (__any_sync(0xffffffffu, o_live)) {
+                const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
+                if (!__all_sync(0xffffffffu, wait_bar(&bars->o_done, (uint32_t)(j - 1) & 1u, abort, err))) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < kDV / 32; c++) {
+                    uint32_t r[32];
+                    ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
+                    ptx::tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+                    ptx::tmem_st32(tmem + lane_addr + kColO + 32 * c, r);
+                }
+                ptx::tmem_wait_st();
+                l *= f;
+            }
+            if (grow) m_used = mx;
+            uint32_t pk[kKeysPerTile / 2];
+            float rs = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kKeysPerTile / 2; i++) {
+                const float p0 = s[2 * i] == -CUDART_INF_F ? 0.0f : ptx::ex2(s[2 * i] - m_used);
+                const float p1 = s[2 * i + 1] == -CUDART_INF_F ? 0.0f : ptx::ex2(s[2 * i + 1] - m_used);
+                rs += p0 + p1;
+                pk[i] = ptx::pack_half2(p0, p1);
+            }
+            l += rs;
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                uint32_t r[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) r[i] = pk[32 * c + i];
+                ptx::tmem_st32(s_addr + 32 * c, r);
+            }
+            ptx::tmem_wait_st();
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&bars->p_full[j & 1]);
+        }
+        // ---- epilogue: O / l (TMEM loads by the whole warp, stores per row) ----
+        if (ok && n_tiles > 0 &&
+            !__all_sync(0xffffffffu, wait_bar(&bars->o_done, (uint32_t)(n_tiles - 1) & 1u, abort, err)))
+            ok = false;
+        ptx::tc_fence_after();
+        if (ok) {
+            float *dst = pb.out + ((size_t)tok * 8 + head) * HD + it.dv_half * kDV;
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll 1
+            for (int c = 0; c < kDV / 32; c++) {
+                uint32_t r[32];
+                if (n_tiles > 0) {
+                    ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
+                    ptx::tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) r[i] = 0u;
+                }
+                if (row_valid) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                               __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                        *reinterpret_cast<float4 *>(dst + 32 * c + i) = v;
+                    }
+                }
+            }
+            if (row_valid && pb.lse && it.dv_half == 0)
+                pb.lse[(size_t)tok * 8 + head] = l > 0.0f ? (m_used + log2f(l)) * 0.6931471805599453f : -CUDART_INF_F;
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+__global__ void bf16_to_f16_kernel(const __nv_bfloat16 *__restrict__ src, __half *__restrict__ dst, size_t n) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (; i < n; i += stride) dst[i] = __float2half_rn(__bfloat162float(src[i]));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver's tensor-map encoder, looked up at run time so that the library
+// loads (for symbol checks) on machines without a driver.
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+bool encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// Host-side state the prefill keeps in the context between calls.
+struct PrefillScratch {
+    __half *v16 = nullptr;
+    size_t v16_cap = 0;  // elements
+    ProblemDev *d_problems = nullptr;
+    size_t problems_cap = 0;
+    WorkItem *d_items = nullptr;
+    size_t items_cap = 0;
+    bool attr_set = false;
+};
+
+PrefillScratch *prefill_scratch_new() { return new PrefillScratch(); }
+void prefill_scratch_free(PrefillScratch *s) {
+    if (!s) return;
+    cudaFree(s->v16);
+    cudaFree(s->d_problems);
+    cudaFree(s->d_items);
+    delete s;
+}
+
+template <typename T>
+static cudaError_t grow_buf(T **p, size_t *cap, size_t need, cudaStream_t st) {
+    if (need <= *cap) return cudaSuccess;
+    if (*p) {
+        cudaStreamSynchronize(st);
+        cudaFree(*p);
+        *p = nullptr;
+        *cap = 0;
+    }
+    const size_t n = std::max(need, *cap * 2);
+    cudaError_t e = cudaMalloc(p, n * sizeof(T));
+    if (e == cudaSuccess) *cap = n;
+    return e;
+}
+
+// Validates, converts V to fp16, builds tensor maps and the work list, and
+// launches one kernel per head width. Returns a g4a_status; *msg names the
+// failure.
+int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_problem *pr, cudaStream_t st,
+                const char **msg) {
+    *msg = "";
+    if (n < 0 || (n > 0 && !pr)) {
+        *msg = "invalid prefill problem list";
+        return G4A_COMPUTE;
+    }
+    // distinct V arrays -> fp16 copies
+    std::vector<const void *> v_src;
+    std::vector<size_t> v_off;
+    size_t v_total = 0;
+    for (int32_t i = 0; i < n; i++) {
+        const g4a_prefill_problem &p = pr[i];
+        if (p.head_dim != 256 && p.head_dim != 512) {
+            *msg = "prefill head width must be 256 or 512";
+            return G4A_COMPUTE;
+        }
+        if (p.n_q < 0 || p.n_kv < 0 || p.window < 0 || p.q_pos0 < 0 || p.kv_pos0 < 0 ||
+            (int64_t)p.n_q * 8 > INT32_MAX) {
+            *msg = "invalid prefill shape";
+            return G4A_COMPUTE;
+        }
+        if (p.n_q > 0 && (!p.q_dev || !p.out_dev)) {
+            *msg = "null prefill query or output";
+            return G4A_COMPUTE;
+        }
+        if (p.n_kv > 0 && (!p.k_dev || !p.v_dev)) {
+            *msg = "null prefill keys or values";
+            return G4A_COMPUTE;
+        }
+        const uintptr_t al = (uintptr_t)p.q_dev | (uintptr_t)p.k_dev | (uintptr_t)p.v_dev | (uintptr_t)p.out_dev;
+        if (al & 15u) {
+            *msg = "prefill buffers must be 16-byte aligned";
+            return G4A_COMPUTE;
+        }
+        if (p.n_kv > 0 && std::find(v_src.begin(), v_src.end(), p.v_dev) == v_src.end()) {
+            v_src.push_back(p.v_dev);
+            v_off.push_back(v_total);
+            v_total += (size_t)p.n_kv * p.head_dim;
+        }
+    }
+    cudaError_t e = grow_buf(&S->v16, &S->v16_cap, std::max<size_t>(v_total, 1), st);
+    if (e != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return G4A_CUDA;
+    }
+    // one fp16 copy per distinct V (sizes from the first problem naming it)
+    std::vector<size_t> v_len(v_src.size(), 0);
+    for (int32_t i = 0; i < n; i++) {
+        if (pr[i].n_kv == 0) continue;
+        size_t k = std::find(v_src.begin(), v_src.end(), pr[i].v_dev) - v_src.begin();
+        v_len[k] = std::max(v_len[k], (size_t)pr[i].n_kv * pr[i].head_dim);
+    }
+    for (size_t k = 0; k < v_src.size(); k++) {
+        const size_t cnt = v_len[k];
+        const int blocks = (int)std::min<size_t>((cnt + 255) / 256, 148 * 16);
+        bf16_to_f16_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(v_src[k]), S->v16 + v_off[k],
+                                                   cnt);
+    }
+    std::vector<ProblemDev> hp(std::max(n, 1));
+    std::vector<WorkItem> work[2];
+    for (int32_t i = 0; i < n; i++) {
+        const g4a_prefill_problem &p = pr[i];
+        ProblemDev &d = hp[i];
+        std::memset(&d, 0, sizeof d);
+        d.hd = p.head_dim;
+        d.window = p.window;
+        d.n_q = p.n_q;
+        d.q_pos0 = p.q_pos0;
+        d.n_kv = p.n_kv;
+        d.kv_pos0 = p.kv_pos0;
+        d.out = p.out_dev;
+        d.lse = p.lse_dev;
+        if (p.n_q == 0) continue;
+        if (!encode_2d(&d.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8)) {
+            *msg = "cuTensorMapEncodeTiled failed for Q";
+            return G4A_CUDA;
+        }
+        if (p.n_kv > 0) {
+            size_t k = std::find(v_src.begin(), v_src.end(), p.v_dev) - v_src.begin();
+            if (!encode_2d(&d.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.k_dev, p.head_dim, p.n_kv) ||
+                !encode_2d(&d.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, S->v16 + v_off[k], p.head_dim, p.n_kv)) {
+                *msg = "cuTensorMapEncodeTiled failed for K/V";
+                return G4A_CUDA;
+            }
+        }
+        const int n_qt = (p.n_q + kTokensPerTile - 1) / kTokensPerTile;
+        for (int t = 0; t < n_qt; t++) {
+            const int64_t q_lo = (int64_t)p.q_pos0 + (int64_t)t * kTokensPerTile;
+            const int64_t q_hi = (int64_t)p.q_pos0 + std::min<int64_t>((int64_t)(t + 1) * kTokensPerTile, p.n_q) - 1;
+            int64_t k_lo = p.window > 0 ? q_lo - p.window + 1 : 0;  // first key position any row may see
+            int64_t klo = std::max<int64_t>(0, k_lo - p.kv_pos0);
+            int64_t khi = std::min<int64_t>((int64_t)p.n_kv - 1, q_hi - p.kv_pos0);
+            WorkItem w{};
+            w.problem = i;
+            w.q_tile = t;
+            if (khi < klo) {
+                w.kv_tile_lo = 0;
+                w.n_kv_tiles = 0;
+            } else {
+                w.kv_tile_lo = (int32_t)(klo / kKeysPerTile);
+                w.n_kv_tiles = (int32_t)(khi / kKeysPerTile) - w.kv_tile_lo + 1;
+            }
+            for (int h = 0; h < p.head_dim / kDV; h++) {
+                w.dv_half = h;
+                work[p.head_dim == 512].push_back(w);
+            }
+        }
+    }
+    // Largest work first: the block scheduler then fills SMs longest-first.
+    for (auto &w : work)
+        std::stable_sort(w.begin(), w.end(),
+                         [](const WorkItem &a, const WorkItem &b) { return a.n_kv_tiles > b.n_kv_tiles; });
+    const size_t n_items = work[0].size() + work[1].size();
+    if ((e = grow_buf(&S->d_problems, &S->problems_cap, hp.size(), st)) != cudaSuccess ||
+        (e = grow_buf(&S->d_items, &S->items_cap, std::max<size_t>(n_items, 1), st)) != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return G4A_CUDA;
+    }
+    std::vector<WorkItem> all(work[0]);
+    all.insert(all.end(), work[1].begin(), work[1].end());
+    if ((e = cudaMemcpyAsync(S->d_problems, hp.data(), hp.size() * sizeof(ProblemDev), cudaMemcpyHostToDevice, st)) !=
+            cudaSuccess ||
+        (n_items && (e = cudaMemcpyAsync(S->d_items, all.data(), n_items * sizeof(WorkItem), cudaMemcpyHostToDevice,
+                                         st)) != cudaSuccess)) {
+        *msg = cudaGetErrorString(e);
+        return G4A_CUDA;
+    }
+    if (!S->attr_set) {
+        cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
+        S->attr_set = true;
+    }
+    if (!work[0].empty())
+        prefill_kernel<256><<<(unsigned)work[0].size(), kThreads, Cfg<256>::kSmemBytes, st>>>(S->d_problems, S->d_items,
+                                                                                            d_err);
+    if (!work[1].empty())
+        prefill_kernel<512><<<(unsigned)work[1].size(), kThreads, Cfg<512>::kSmemBytes, st>>>(
+            S->d_problems, S->d_items + work[0].size(), d_err);
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return G4A_CUDA;
+    }
+    return G4A_OK;
+}
+
+}  // namespace g4a

@@ -1,0 +1,287 @@
+"""Python binding of libg4attn.so (the C ABI in include/g4attn.h).
+
+Names follow the reference's attention boundary so that tests read like the
+reference's own: `attend` (crates/llm-gemma4/src/impl_/model.rs:348),
+`KvCache.append / view / clear` (crates/llm-eng/src/context_memory.rs:11-18),
+`kv_source_layer`, `windowed_len`, `layer_is_global`, `head_dim`
+(crates/llm-gemma4/src/{eng,idea}/mod.rs). Errors raise `EngError` carrying
+the status code and the library's message.
+
+Device memory is passed as torch CUDA tensors (only their data pointers cross
+the boundary). There is no CPU fallback: every compute call goes to the CUDA
+library, and importing this module fails if the library was not built.
+"""
+from __future__ import annotations
+
+import atexit
+import ctypes
+import re
+import weakref
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libg4attn.so"
+HEADER = HERE.parent.parent / "include" / "g4attn.h"
+
+OK, CONTEXT_TOO_LONG, MISSING_LAYER, MISSING_WEIGHT, COMPUTE, NONFINITE, BAD_LAYER, CUDA, NCCL, TIMEOUT, \
+    OUT_OF_PAGES = range(11)
+KV_F32, KV_F16 = 0, 1
+
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+
+
+class HParams(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int32), ("n_heads", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
+        ("head_dim_local", ctypes.c_int32), ("head_dim_global", ctypes.c_int32),
+        ("sliding_window", ctypes.c_int32), ("shared_kv_layers", ctypes.c_int32),
+        ("local_rope_base", ctypes.c_float), ("global_rope_base", ctypes.c_float),
+        ("global_p", ctypes.c_float), ("rms_norm_eps", ctypes.c_float),
+    ]
+
+
+class DecodeLayer(ctypes.Structure):
+    _fields_ = [("layer", ctypes.c_int32), ("q_raw_dev", _vp), ("k_raw_dev", _vp), ("v_raw_dev", _vp),
+                ("q_norm_w_dev", _vp), ("k_norm_w_dev", _vp), ("out_dev", _vp)]
+
+
+class PrefillProblem(ctypes.Structure):
+    _fields_ = [("head_dim", ctypes.c_int32), ("window", ctypes.c_int32), ("n_q", ctypes.c_int32),
+                ("q_pos0", ctypes.c_int32), ("n_kv", ctypes.c_int32), ("kv_pos0", ctypes.c_int32),
+                ("q_dev", _vp), ("k_dev", _vp), ("v_dev", _vp), ("out_dev", _vp), ("lse_dev", _vp)]
+
+
+class EngError(RuntimeError):
+    """A non-zero g4a_status (EngError of crates/llm-eng/src/error.rs)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+        self.message = message
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: run `python gemma4-rs_b200/build.py` (no CPU fallback exists)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    hp = ctypes.POINTER(HParams)
+    L.g4a_hparams_e2b.argtypes = [hp]
+    L.g4a_hparams_e2b.restype = None
+    L.g4a_layer_is_global.argtypes = [hp, ctypes.c_int32]
+    L.g4a_head_dim.argtypes = [hp, ctypes.c_int32]
+    L.g4a_kv_source_layer.argtypes = [hp, ctypes.c_int32, _i32p, _i32p]
+    L.g4a_windowed_len.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64),
+                                   ctypes.POINTER(ctypes.c_int64)]
+    L.g4a_windowed_len.restype = None
+    L.g4a_proportional_rope_freq_factors.argtypes = [ctypes.c_int32, ctypes.c_float, _f32p]
+    L.g4a_proportional_rope_freq_factors.restype = None
+    L.g4a_ctx_create.argtypes = [ctypes.c_int, hp, _f32p, ctypes.c_int32, ctypes.POINTER(_vp)]
+    L.g4a_ctx_destroy.argtypes = [_vp]
+    L.g4a_ctx_destroy.restype = None
+    L.g4a_last_error.argtypes = [_vp]
+    L.g4a_last_error.restype = ctypes.c_char_p
+    L.g4a_ctx_set_stream.argtypes = [_vp, _vp]
+    L.g4a_sync.argtypes = [_vp]
+    L.g4a_attend.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                             ctypes.c_float, _vp]
+    L.g4a_kv_create.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                _i32p, ctypes.c_int32, ctypes.POINTER(_vp)]
+    L.g4a_kv_destroy.argtypes = [_vp]
+    L.g4a_kv_destroy.restype = None
+    L.g4a_kv_clear.argtypes = [_vp, ctypes.c_int32]
+    L.g4a_kv_len.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)]
+    L.g4a_kv_append.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, _vp, _vp, ctypes.c_int64]
+    L.g4a_kv_view.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, _vp, _vp]
+    L.g4a_kv_append_tokens.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp, ctypes.c_int64]
+    L.g4a_decode.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(DecodeLayer), ctypes.c_int32, _i32p, _i32p]
+    L.g4a_prefill.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(PrefillProblem)]
+    L.g4a_lse_merge.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int64,
+                                ctypes.c_int32, ctypes.c_int32, _vp, _vp]
+    return L
+
+
+lib = _load()
+
+# Handles still open when the interpreter exits are closed from an atexit hook,
+# while the CUDA runtime is still up (finalizers that run later must not call
+# into the library).
+_live: "weakref.WeakSet" = weakref.WeakSet()
+_exiting = False
+
+
+def _close_all():
+    global _exiting
+    for obj in sorted(list(_live), key=lambda o: isinstance(o, Context)):  # caches before contexts
+        try:
+            obj.close()
+        except Exception:
+            pass
+    _exiting = True
+
+
+atexit.register(_close_all)
+
+
+def declared_symbols() -> list[str]:
+    """Every function the public header declares."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(g4a_\w+)\s*\(", text, re.M)))
+
+
+# ---- hyperparameters and policies (host only) ----
+
+def hparams_e2b() -> HParams:
+    hp = HParams()
+    lib.g4a_hparams_e2b(ctypes.byref(hp))
+    return hp
+
+
+def layer_is_global(hp: HParams, layer: int) -> bool:
+    return bool(lib.g4a_layer_is_global(ctypes.byref(hp), layer))
+
+
+def head_dim(hp: HParams, layer: int) -> int:
+    return int(lib.g4a_head_dim(ctypes.byref(hp), layer))
+
+
+def kv_source_layer(hp: HParams, layer: int):
+    src, det = ctypes.c_int32(-1), ctypes.c_int32(0)
+    rc = lib.g4a_kv_source_layer(ctypes.byref(hp), layer, ctypes.byref(src), ctypes.byref(det))
+    return (src.value, None) if rc == OK else (None, det.value)
+
+
+def windowed_len(seq_len: int, window: int):
+    lo, hi = ctypes.c_int64(), ctypes.c_int64()
+    lib.g4a_windowed_len(seq_len, window, ctypes.byref(lo), ctypes.byref(hi))
+    return lo.value, hi.value
+
+
+def proportional_rope_freq_factors(hd: int, p: float):
+    out = (ctypes.c_float * (hd // 2))()
+    lib.g4a_proportional_rope_freq_factors(hd, p, out)
+    return list(out)
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    assert t.is_cuda and t.is_contiguous(), "device tensors must be contiguous CUDA tensors"
+    return t.data_ptr()
+
+
+class Context:
+    """g4a_ctx: one device, one stream, RoPE tables and decode scratch."""
+
+    def __init__(self, device: int = 0, hp: HParams | None = None, rope_freqs=None, max_positions: int = 4096):
+        self.hp = hp or hparams_e2b()
+        h = _vp()
+        ff = None
+        if rope_freqs is not None:
+            arr = (ctypes.c_float * len(rope_freqs))(*[float(x) for x in rope_freqs])
+            ff = ctypes.cast(arr, _f32p)
+        rc = lib.g4a_ctx_create(device, ctypes.byref(self.hp), ff, max_positions, ctypes.byref(h))
+        if rc != OK:
+            raise EngError(rc, "g4a_ctx_create failed")
+        self.h = h
+        self.device = device
+        _live.add(self)
+
+    def close(self):
+        if getattr(self, "h", None) and not _exiting:
+            for kv in [o for o in _live if isinstance(o, KvCache) and o.ctx is self]:
+                kv.close()
+            lib.g4a_ctx_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def check(self, rc: int):
+        if rc != OK:
+            raise EngError(rc, lib.g4a_last_error(self.h).decode())
+
+    def set_stream(self, stream_handle: int | None):
+        self.check(lib.g4a_ctx_set_stream(self.h, stream_handle))
+
+    def sync(self):
+        self.check(lib.g4a_sync(self.h))
+
+    # model.rs:348 attend
+    def attend(self, q, keys, values, n_heads: int, n_kv_heads: int, scale: float, out, length: int | None = None):
+        hd = q.numel() // n_heads
+        if length is None:
+            length = keys.numel() // (n_kv_heads * hd) if keys is not None else 0
+        self.check(lib.g4a_attend(self.h, _ptr(q), _ptr(keys) if length else None,
+                                  _ptr(values) if length else None, length, n_heads, n_kv_heads, hd, scale,
+                                  _ptr(out)))
+
+    def decode(self, kv: "KvCache", layers: list[dict], seq_ids: list[int], positions: list[int]):
+        arr = (DecodeLayer * max(1, len(layers)))()
+        for i, a in enumerate(layers):
+            arr[i] = DecodeLayer(a["layer"], _ptr(a["q_raw"]), _ptr(a.get("k_raw")), _ptr(a.get("v_raw")),
+                                 _ptr(a.get("q_norm_w")), _ptr(a.get("k_norm_w")), _ptr(a["out"]))
+        n = len(seq_ids)
+        s = (ctypes.c_int32 * max(1, n))(*seq_ids)
+        p = (ctypes.c_int32 * max(1, n))(*positions)
+        self.check(lib.g4a_decode(self.h, kv.h, len(layers), arr, n, s, p))
+
+    def prefill(self, problems: list[dict]):
+        arr = (PrefillProblem * max(1, len(problems)))()
+        for i, a in enumerate(problems):
+            arr[i] = PrefillProblem(a["head_dim"], a.get("window", 0), a["n_q"], a.get("q_pos0", 0), a["n_kv"],
+                                    a.get("kv_pos0", 0), _ptr(a["q"]), _ptr(a["k"]), _ptr(a["v"]), _ptr(a["out"]),
+                                    _ptr(a.get("lse")))
+        self.check(lib.g4a_prefill(self.h, len(problems), arr))
+
+    def lse_merge(self, outs, lses, rows: int, n_heads: int, hd: int, out, lse=None):
+        n = len(outs)
+        po = (_vp * n)(*[_ptr(t) for t in outs])
+        pl = (_vp * n)(*[_ptr(t) for t in lses])
+        self.check(lib.g4a_lse_merge(self.h, n, po, pl, rows, n_heads, hd, _ptr(out), _ptr(lse)))
+
+
+class KvCache:
+    """g4a_kv: the paged device cache behind ContextMemory."""
+
+    def __init__(self, ctx: Context, n_seqs: int, max_tokens: int, dtype: int = KV_F32, layers=None,
+                 page_tokens: int = 64, n_pages: int = 0):
+        self.ctx = ctx
+        h = _vp()
+        if layers is None:
+            lp, nl = None, 0
+        else:
+            lp = (ctypes.c_int32 * max(1, len(layers)))(*layers)
+            nl = len(layers)
+        ctx.check(lib.g4a_kv_create(ctx.h, n_seqs, max_tokens, page_tokens, n_pages, dtype, lp, nl, ctypes.byref(h)))
+        self.h = h
+        self.dtype = dtype
+        _live.add(self)
+
+    def close(self):
+        if getattr(self, "h", None) and not _exiting:
+            lib.g4a_kv_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def clear(self, seq: int = -1):
+        self.ctx.check(lib.g4a_kv_clear(self.h, seq))
+
+    def len(self, seq: int, layer: int) -> int:
+        n = ctypes.c_int64()
+        self.ctx.check(lib.g4a_kv_len(self.h, seq, layer, ctypes.byref(n)))
+        return n.value
+
+    def append(self, seq: int, layer: int, k, v):
+        rows = k.shape[0] if k.dim() > 1 else 1
+        self.ctx.check(lib.g4a_kv_append(self.h, seq, layer, _ptr(k), _ptr(v), rows))
+
+    def append_tokens(self, seq: int, layer: int, k_raw, v_raw, k_norm_w):
+        rows = k_raw.shape[0] if k_raw.dim() > 1 else 1
+        self.ctx.check(lib.g4a_kv_append_tokens(self.h, seq, layer, _ptr(k_raw), _ptr(v_raw), _ptr(k_norm_w), rows))
+
+    def view(self, seq: int, layer: int, length: int, keys_out, values_out):
+        self.ctx.check(lib.g4a_kv_view(self.h, seq, layer, length, _ptr(keys_out), _ptr(values_out)))

@@ -1,0 +1,210 @@
+/*
+ * g4attn — Gemma 4 E2B attention on B200 (sm_100a), C ABI.
+ *
+ * This is the drop-in boundary for gemma4-rs's attention path. Everything a
+ * Rust `llm-backend-cuda` crate would bind is declared here: plain C types,
+ * explicit lengths, an int status per call. No CUDA or torch type appears in
+ * a signature (streams are passed as `void *`).
+ *
+ * Reference interfaces replaced (paths relative to the gemma4-rs workspace):
+ *   crates/llm-gemma4/src/impl_/model.rs:348  attend(q, keys, values, n_heads, n_kv_heads, scale)
+ *   crates/llm-gemma4/src/impl_/model.rs:393-410  the attention block of TransformerSpec::layer
+ *   crates/llm-gemma4/src/impl_/model.rs:283-304  norm_heads / rope_heads (fused into decode)
+ *   crates/llm-eng/src/context_memory.rs:11-18  ContextMemory::{append, view, clear}
+ *   crates/llm-gemma4/src/eng/mod.rs:10-36,71-90  window policies, kv_source_layer
+ *   crates/llm-gemma4/src/idea/mod.rs:48-68,140-165  E2B hyperparameters, layer kinds, p-RoPE factors
+ *
+ * Memory: pointers named `*_dev` are device pointers owned by the caller;
+ * `*_host` pointers are host memory. The context owns the RoPE tables, the
+ * split-KV scratch and the KV pages.
+ *
+ * Threading: one context drives one CUDA stream; calls on a context (and on
+ * the caches made from it) are not thread-safe, as `&mut self` in the
+ * reference's `layer`. Device work is asynchronous: a call returns once its
+ * kernels are queued. Shape, position and capacity errors are returned
+ * immediately; a non-finite softmax is detected on the device and returned
+ * by the next g4a_sync (the reference returns it from `attend`).
+ */
+#ifndef G4ATTN_H
+#define G4ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes. 1-5 map 1:1 onto crates/llm-eng/src/error.rs:3-15 EngError. */
+typedef enum g4a_status {
+    G4A_OK = 0,
+    G4A_CONTEXT_TOO_LONG = 1, /* EngError::ContextTooLong { got, max } */
+    G4A_MISSING_LAYER = 2,    /* EngError::MissingLayer(layer) */
+    G4A_MISSING_WEIGHT = 3,   /* EngError::MissingWeight (a required norm weight is NULL) */
+    G4A_COMPUTE = 4,          /* EngError::Compute: invalid shapes or inputs */
+    G4A_NONFINITE = 5,        /* EngError::Compute("softmax input is not finite"), model.rs:363 */
+    G4A_BAD_LAYER = 6,        /* KvShareError, crates/llm-gemma4/src/eng/mod.rs:38-43 */
+    G4A_CUDA = 7,             /* a CUDA runtime call failed */
+    G4A_NCCL = 8,             /* a collective failed */
+    G4A_TIMEOUT = 9,          /* a bounded wait ran out */
+    G4A_OUT_OF_PAGES = 10     /* the paged KV cache has no free page */
+} g4a_status;
+
+/* Storage type of the paged KV cache. */
+typedef enum g4a_kv_dtype { G4A_KV_F32 = 0, G4A_KV_F16 = 1 } g4a_kv_dtype;
+
+/* Attention-relevant fields of Gemma4HyperParams (idea/mod.rs:16-34). */
+typedef struct g4a_hparams {
+    int32_t n_layers, n_heads, n_kv_heads, head_dim_local, head_dim_global;
+    int32_t sliding_window, shared_kv_layers;
+    float local_rope_base, global_rope_base, global_p, rms_norm_eps;
+} g4a_hparams;
+
+typedef struct g4a_ctx g4a_ctx;
+typedef struct g4a_kv g4a_kv;
+
+/* ---- hyperparameters and policies (host only, no device work) ---------- */
+
+/* idea/mod.rs:48-68 Gemma4HyperParams::e2b. */
+void g4a_hparams_e2b(g4a_hparams *out);
+/* idea/mod.rs:148-156 layer_attention_kind: 1 = global, 0 = sliding window. */
+int g4a_layer_is_global(const g4a_hparams *hp, int32_t layer);
+/* idea/mod.rs:140-145 head_dim. */
+int32_t g4a_head_dim(const g4a_hparams *hp, int32_t layer);
+/* eng/mod.rs:71-90 kv_source_layer. On G4A_BAD_LAYER, *detail (if non-NULL)
+ * is 1 LayerOutOfRange, 2 TooManySharedLayers, 3 NoEarlierLayerOfSameKind. */
+int g4a_kv_source_layer(const g4a_hparams *hp, int32_t layer, int32_t *source, int32_t *detail);
+/* eng/mod.rs:10-12 windowed_len: [seq_len - window saturating, seq_len). */
+void g4a_windowed_len(int64_t seq_len, int64_t window, int64_t *lo, int64_t *hi);
+/* idea/mod.rs:162-165 proportional_rope_freq_factors: head_dim/2 values. */
+void g4a_proportional_rope_freq_factors(int32_t head_dim, float p, float *out_host);
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Creates a context on `device`. rope_freqs_host holds head_dim_global/2
+ * per-pair divisors for global layers (the GGUF `rope_freqs.weight`,
+ * model.rs:298); NULL derives them from hp->global_p. max_positions bounds
+ * the positions decode and append accept (RoPE tables are built for
+ * [0, max_positions)). */
+int g4a_ctx_create(int device, const g4a_hparams *hp, const float *rope_freqs_host,
+                   int32_t max_positions, g4a_ctx **out);
+void g4a_ctx_destroy(g4a_ctx *ctx);
+/* The message of the last failed call on this context (EngError's Display). */
+const char *g4a_last_error(const g4a_ctx *ctx);
+/* Sets the cudaStream_t all later calls queue on (NULL = legacy default). */
+int g4a_ctx_set_stream(g4a_ctx *ctx, void *cuda_stream);
+/* Waits for queued work and returns G4A_NONFINITE if a softmax since the
+ * last g4a_sync saw a non-finite input (the flag is then cleared). */
+int g4a_sync(g4a_ctx *ctx);
+
+/* ---- attention primitive ---------------------------------------------- */
+
+/* model.rs:348-366 attend: grouped-query attention for one query position.
+ * q_dev [n_heads*head_dim] f32; keys_dev/values_dev [len][n_kv_heads*head_dim]
+ * f32 rows (the reference's concatenated rows); out_dev [n_heads*head_dim].
+ * len == 0 is reported as G4A_NONFINITE like the reference (empty softmax). */
+int g4a_attend(g4a_ctx *ctx, const float *q_dev, const float *keys_dev, const float *values_dev,
+               int64_t len, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, float scale,
+               float *out_dev);
+
+/* ---- paged KV cache: ContextMemory (context_memory.rs:11-18) ------------ */
+
+/* A paged cache for n_seqs sequences of up to max_tokens rows per layer.
+ * page_tokens rows per page (64 recommended); n_pages 0 = enough for every
+ * sequence at max_tokens. layers_host lists the owner layers to hold
+ * (kv_source_layer(l) == l); NULL holds every owner layer. Pages are shared
+ * by index across layers: a sequence's logical page j is one physical page in
+ * every held layer's pool. */
+int g4a_kv_create(g4a_ctx *ctx, int32_t n_seqs, int32_t max_tokens, int32_t page_tokens,
+                  int32_t n_pages, int32_t dtype, const int32_t *layers_host, int32_t n_layers,
+                  g4a_kv **out);
+void g4a_kv_destroy(g4a_kv *kv);
+/* ContextMemory::clear (context_memory.rs:83-85) for one sequence, or all
+ * when seq < 0; frees its pages. */
+int g4a_kv_clear(g4a_kv *kv, int32_t seq);
+/* Rows stored for (seq, layer). */
+int g4a_kv_len(const g4a_kv *kv, int32_t seq, int32_t layer, int64_t *len);
+/* ContextMemory::append (context_memory.rs:44-51) of n_rows already
+ * normalised and rotated rows: k_dev/v_dev [n_rows][n_kv_heads*head_dim] f32,
+ * stored in the cache's dtype. */
+int g4a_kv_append(g4a_kv *kv, int32_t seq, int32_t layer, const float *k_dev, const float *v_dev,
+                  int64_t n_rows);
+/* ContextMemory::view (context_memory.rs:53-69): copies rows [0, len) of
+ * (seq, layer) out as f32. MissingLayer / ContextTooLong as the reference. */
+int g4a_kv_view(const g4a_kv *kv, int32_t seq, int32_t layer, int64_t len, float *keys_dev,
+                float *values_dev);
+/* The K/V half of model.rs:400-405 for n_tokens consecutive tokens of one
+ * sequence: k = rope(rms_norm(k_raw, k_norm_w)), v = rms_norm(v_raw), appended
+ * at positions len .. len+n_tokens-1. k_raw_dev/v_raw_dev [n_tokens][hd] f32. */
+int g4a_kv_append_tokens(g4a_kv *kv, int32_t seq, int32_t layer, const float *k_raw_dev,
+                         const float *v_raw_dev, const float *k_norm_w_dev, int64_t n_tokens);
+
+/* ---- fused decode step: model.rs:393-410 without the projections ------- */
+
+/* One layer's inputs for a decode batch. q_raw_dev [n][n_heads*hd] f32 are
+ * the attn_q projections; k_raw_dev/v_raw_dev [n][hd] f32 the attn_k/attn_v
+ * projections (ignored, may be NULL, for KV-shared layers); q_norm_w_dev /
+ * k_norm_w_dev [hd] the attn_q_norm / attn_k_norm weights; out_dev
+ * [n][n_heads*hd] f32 receives the attention output (attn_output's input). */
+typedef struct g4a_decode_layer {
+    int32_t layer;
+    const float *q_raw_dev;
+    const float *k_raw_dev;
+    const float *v_raw_dev;
+    const float *q_norm_w_dev;
+    const float *k_norm_w_dev;
+    float *out_dev;
+} g4a_decode_layer;
+
+/* Decode step for n_seqs sequences over n_layers layers in one launch. For
+ * sequence i (cache row seq_ids_host[i]) at position positions_host[i] and
+ * each listed layer: q-norm + RoPE, and on KV-owning layers k-norm, v-norm,
+ * k RoPE and append; then attention over the window of the source layer's
+ * cache (local: the last `sliding_window` rows up to the position; global:
+ * all), scale 1. A call may not list a shared layer together with its
+ * source layer (the shared layer would race the append). */
+int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers_host,
+               int32_t n_seqs, const int32_t *seq_ids_host, const int32_t *positions_host);
+
+/* ---- prefill attention (tcgen05 tensor cores) -------------------------- */
+
+/* One causal attention problem over bf16 inputs that are already normalised
+ * and rotated: q [n_q][n_heads][hd], k/v [n_kv][hd] (1 KV head). Query row i
+ * has absolute position q_pos0 + i and sees key row j (position kv_pos0 + j)
+ * when key_pos <= q_pos and, for window > 0, q_pos - key_pos < window
+ * (eng/mod.rs:10-12 applied per position, as the reference's token-at-a-time
+ * prefill does). out [n_q][n_heads][hd] f32 is normalised; lse (optional,
+ * [n_q][n_heads] f32) receives the natural-log sum of exp(scores) for merging
+ * partial results; rows that see no key get out 0 and lse -inf. */
+typedef struct g4a_prefill_problem {
+    int32_t head_dim;  /* 256 or 512 */
+    int32_t window;    /* 0 = global (full causal) */
+    int32_t n_q, q_pos0, n_kv, kv_pos0;
+    const void *q_dev; /* bf16 */
+    const void *k_dev; /* bf16 */
+    const void *v_dev; /* bf16 */
+    float *out_dev;
+    float *lse_dev;
+} g4a_prefill_problem;
+
+/* Runs n problems (e.g. the 35 layers of a prompt) in one launch. */
+int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *problems_host);
+
+/* Merges partial attention results over disjoint key sets (log-sum-exp):
+ * out = sum_i exp(lse_i - L) * out_i with L = log sum_i exp(lse_i).
+ * parts_out_dev / parts_lse_dev hold n_parts arrays of rows*n_heads*hd and
+ * rows*n_heads; results go to out_dev / lse_dev (lse_dev may be NULL). */
+int g4a_lse_merge(g4a_ctx *ctx, int32_t n_parts, const float *const *parts_out_host,
+                  const float *const *parts_lse_host, int64_t rows, int32_t n_heads,
+                  int32_t head_dim, float *out_dev, float *lse_dev);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* G4ATTN_H */

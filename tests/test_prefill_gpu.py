@@ -1,0 +1,166 @@
+"""Prefill parity on the GPU: the tcgen05 kernel through the C ABI against the
+oracle's token-at-a-time attention (the reference's prompt loop) on the same
+bf16-rounded inputs.
+
+Tolerance: max |diff| <= 2e-3 (bf16 inputs, f32 accumulation, fp16 P).
+"""
+import numpy as np
+import pytest
+
+from helpers import max_abs_diff, rng, unit_rms_rows
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+@pytest.fixture(scope="module")
+def ctx(torch_cuda):
+    import g4attn
+    c = g4attn.Context(0)
+    yield c
+    c.close()
+
+
+def make_qkv(oracle, seed, n_q, n_kv, hd):
+    """Unit-RMS Q (per head) and K rows, N(0,1) V, rounded to bf16."""
+    r = rng(seed)
+    q = unit_rms_rows(r.standard_normal((n_q, 8, hd)).astype(np.float32))
+    k = unit_rms_rows(r.standard_normal((n_kv, hd)).astype(np.float32))
+    v = r.standard_normal((n_kv, hd)).astype(np.float32)
+    return oracle.round_bf16(q), oracle.round_bf16(k), oracle.round_bf16(v)
+
+
+def to_dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda().to(torch.bfloat16)
+
+
+def reference(q, k, v, window, q_pos0=0, kv_pos0=0):
+    """float64 statement of the per-position attention with absolute
+    positions (eng/mod.rs:10-36 per query position) plus the log-sum-exp."""
+    n_q, H, hd = q.shape
+    n_kv = k.shape[0]
+    qpos = q_pos0 + np.arange(n_q)
+    kpos = kv_pos0 + np.arange(n_kv)
+    s = np.einsum("thd,kd->thk", q.astype(np.float64), k.astype(np.float64))
+    vis = (kpos[None, :] <= qpos[:, None])
+    if window:
+        vis &= (qpos[:, None] - kpos[None, :]) < window
+    s = np.where(vis[:, None, :], s, -np.inf)
+    m = s.max(-1, keepdims=True)
+    has = np.isfinite(m)
+    e = np.where(has, np.exp(s - np.where(has, m, 0)), 0.0)
+    l = e.sum(-1, keepdims=True)
+    out = np.where(has, (e @ v.astype(np.float64)) / np.where(has, l, 1), 0.0)
+    lse = np.where(has[..., 0], (m + np.log(np.where(has, l, 1)))[..., 0], -np.inf)
+    return out, lse
+
+
+def run(ctx, torch, q, k, v, hd, window, q_pos0=0, kv_pos0=0, lse=False):
+    n_q, n_kv = q.shape[0], k.shape[0]
+    out = torch.full((n_q, 8, hd), float("nan"), device="cuda")
+    lse_t = torch.full((n_q, 8), float("nan"), device="cuda") if lse else None
+    ctx.prefill([dict(head_dim=hd, window=window, n_q=n_q, q_pos0=q_pos0, n_kv=n_kv, kv_pos0=kv_pos0,
+                      q=to_dev(torch, q), k=to_dev(torch, k), v=to_dev(torch, v), out=out, lse=lse_t)])
+    ctx.sync()
+    return out.cpu().numpy(), (lse_t.cpu().numpy() if lse else None)
+
+
+@pytest.mark.parametrize("hd,T,window", [(256, 1, 512), (256, 17, 512), (256, 200, 64), (512, 200, 0),
+                                          (512, 130, 0), (256, 628, 512)])
+def test_prefill_matches_oracle(oracle, ctx, torch_cuda, hd, T, window):
+    q, k, v = make_qkv(oracle, hd * 1000 + T, T, T, hd)
+    got, _ = run(ctx, torch_cuda, q, k, v, hd, window)
+    want = oracle.prefill_attend(q, k, v, 8, window)
+    assert max_abs_diff(got, want) <= TOL
+
+
+def test_prefill_global_628(oracle, ctx, torch_cuda):
+    """Config 1's global layer shape: 628 tokens, 512-wide heads, full causal."""
+    q, k, v = make_qkv(oracle, 628, 628, 628, 512)
+    got, _ = run(ctx, torch_cuda, q, k, v, 512, 0)
+    want = oracle.prefill_attend(q, k, v, 8, 0)
+    assert max_abs_diff(got, want) <= TOL
+
+
+@pytest.mark.parametrize("hd,window,n_q,q_pos0,n_kv,kv_pos0", [
+    (512, 0, 100, 300, 400, 0),    # a chunk of queries against the whole prefix
+    (512, 0, 64, 128, 128, 256),   # keys all in the future: no visible key
+    (256, 512, 90, 700, 300, 500), # window crossing the key block start
+    (512, 0, 40, 1000, 200, 900),  # keys of a later shard only partly visible
+])
+def test_prefill_offsets_and_lse(oracle, ctx, torch_cuda, hd, window, n_q, q_pos0, n_kv, kv_pos0):
+    q, k, v = make_qkv(oracle, n_q + n_kv, n_q, n_kv, hd)
+    got, lse = run(ctx, torch_cuda, q, k, v, hd, window, q_pos0, kv_pos0, lse=True)
+    want, want_lse = reference(q, k, v, window, q_pos0, kv_pos0)
+    assert max_abs_diff(got, want) <= TOL
+    fin = np.isfinite(want_lse)
+    assert np.array_equal(np.isfinite(lse), fin)
+    if fin.any():
+        assert np.max(np.abs(lse[fin] - want_lse[fin])) <= 1e-3
+
+
+def test_prefill_rescale_path(oracle, ctx, torch_cuda):
+    """Scores that grow along the keys force the running max up by more than
+    2^8 several times (the lazy O rescale); the result still matches."""
+    hd, T = 256, 512
+    q, k, v = make_qkv(oracle, 7, T, T, hd)
+    ramp = np.linspace(0.2, 3.0, T, dtype=np.float32)[:, None]
+    k = oracle.round_bf16(k * ramp)
+    got, _ = run(ctx, torch_cuda, q, k, v, hd, 0)
+    want = oracle.prefill_attend(q, k, v, 8, 0)
+    assert max_abs_diff(got, want) <= TOL
+
+
+def test_prefill_35_layers_one_launch(oracle, ctx, torch_cuda):
+    """Config 1: all 35 layer-equivalents in one call, layers 15-34 reusing
+    the K/V of layer 13 (local) or 14 (global). Each layer equals the same
+    problem run alone, bit for bit, and two layers match the oracle."""
+    import g4attn
+    torch = torch_cuda
+    hp = g4attn.hparams_e2b()
+    T = 628
+    kvs = {}
+    probs, qs = [], []
+    for layer in range(35):
+        src, _ = g4attn.kv_source_layer(hp, layer)
+        hd = g4attn.head_dim(hp, layer)
+        glob = g4attn.layer_is_global(hp, layer)
+        if src not in kvs:
+            _, k, v = make_qkv(oracle, 500 + src, 1, T, hd)
+            kvs[src] = (k, v, to_dev(torch, k), to_dev(torch, v))
+        q, _, _ = make_qkv(oracle, 900 + layer, T, 1, hd)
+        qs.append(q)
+        probs.append(dict(head_dim=hd, window=0 if glob else 512, n_q=T, n_kv=T, q=to_dev(torch, q),
+                          k=kvs[src][2], v=kvs[src][3], out=torch.empty(T, 8, hd, device="cuda")))
+    ctx.prefill(probs)
+    ctx.sync()
+    for layer in (0, 14, 33, 34):
+        p = probs[layer]
+        alone = torch.empty_like(p["out"])
+        ctx.prefill([dict(p, out=alone)])
+        ctx.sync()
+        assert torch.equal(alone, p["out"]), layer
+    for layer in (13, 34):
+        src, _ = g4attn.kv_source_layer(hp, layer)
+        k, v = kvs[src][0], kvs[src][1]
+        want = oracle.prefill_attend(qs[layer], k, v, 8, probs[layer]["window"])
+        assert max_abs_diff(probs[layer]["out"].cpu().numpy(), want) <= TOL
+
+
+def test_prefill_rejects_bad_shapes(ctx, torch_cuda):
+    import g4attn
+    torch = torch_cuda
+    x = torch.zeros(16, 8, 128, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(16, 8, 128, device="cuda")
+    with pytest.raises(g4attn.EngError) as e:
+        ctx.prefill([dict(head_dim=128, n_q=16, n_kv=16, q=x, k=x, v=x, out=out)])
+    assert e.value.code == g4attn.COMPUTE
