@@ -1,0 +1,579 @@
+#!/usr/bin/env python
+"""Benchmark of the Gemma 4 E2B attention path on B200.
+
+Primary line (the driver's contract): configuration 2 of BASELINE.json, a
+paged batched decode step — 64 sequences per GPU with context lengths drawn
+uniformly from [1, 4096] (seeded), each running one sliding-window layer
+(13) and one global layer (14) of E2B shape over an f16 paged KV cache
+(64-token pages), f32 queries. A step is one decode step of every sequence
+on both layers: fused q/k RMSNorm + RoPE + KV append + split-KV attention.
+Sequences are sharded across GPUs (weak scaling: 64 per GPU, longest-first
+balanced by K/V bytes), with no collective on the data path.
+
+The same line carries:
+  * roofline  — achieved HBM bandwidth of the dominant kernel (the global
+    layer's decode kernel) from CUDA events around each of its launches;
+  * e2e       — the same metric through the public C ABI (g4a_decode) with
+    host inputs copied in and results copied out every step;
+  * cpu_baseline — the reference's attention path restated in C (the oracle
+    port, pool.rs-shaped thread pool) timed on this host;
+  * decode_batch1 — configuration 0 (batch 1, context 628) latency;
+  * prefill   — configurations 1 (628-token prompt, 35 layers) and 3
+    (32,768-token global prefill, one GPU) in TFLOP/s against the tensor peak.
+
+`--impl reference` times the reference's own CPU path instead (the oracle
+port on all host cores; the Rust reference cannot be built here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT / "gemma4-rs_b200", ROOT / "oracle"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+METRIC = ("decode attn tokens/s + HBM GB/s (% of 8 TB/s); prefill attn TFLOP/s (% peak)")
+SEQS_PER_GPU = 64
+MAX_CTX = 4096
+LOCAL_LAYER, GLOBAL_LAYER = 13, 14
+HD_L, HD_G = 256, 512
+HEADS = 8
+NOMINAL_HBM_GBS = 8000.0
+
+
+def peaks():
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return {"hbm": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    except Exception:
+        return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------
+# workload
+# --------------------------------------------------------------------------
+
+def global_lengths(n_gpus: int, seed: int = 2026) -> np.ndarray:
+    """Context lengths of all sequences: U[1, 4096], seeded."""
+    return np.random.default_rng(seed).integers(1, MAX_CTX + 1, size=SEQS_PER_GPU * n_gpus)
+
+
+def kv_bytes(c: int) -> int:
+    """f16 K+V bytes a decode step at context c reads: min(c,512) local rows
+    of 256 and c global rows of 512 (the new row included)."""
+    return 2 * min(c, 512) * HD_L * 2 + 2 * c * HD_G * 2
+
+
+def shard(lengths: np.ndarray, n: int, rank: int) -> np.ndarray:
+    """Longest-processing-time assignment by K/V bytes; equal counts per rank."""
+    order = np.argsort(-np.array([kv_bytes(int(c)) for c in lengths]), kind="stable")
+    load = [0] * n
+    count = [0] * n
+    owner = np.empty(len(lengths), np.int64)
+    per = len(lengths) // n
+    for i in order:
+        cand = [r for r in range(n) if count[r] < per]
+        r = min(cand, key=lambda x: load[x])
+        owner[i] = r
+        load[r] += kv_bytes(int(lengths[i]))
+        count[r] += 1
+    return lengths[owner == rank]
+
+
+def step_bytes(ctx_lens) -> dict:
+    """Algorithmic bytes of one decode step per layer: K/V rows read (f16),
+    q read and output written (f32), raw k/v read (f32) and the appended
+    row written (f16)."""
+    n = len(ctx_lens)
+    glob = sum(2 * c * HD_G * 2 for c in ctx_lens) + n * (2 * HEADS * HD_G * 4 + 2 * HD_G * 4 + 2 * HD_G * 2)
+    loc = sum(2 * min(c, 512) * HD_L * 2 for c in ctx_lens) + n * (2 * HEADS * HD_L * 4 + 2 * HD_L * 4 + 2 * HD_L * 2)
+    return {"global": glob, "local": loc, "total": glob + loc}
+
+
+def prefill_pairs(T: int, window: int) -> int:
+    return sum(min(t + 1, window) if window else t + 1 for t in range(T))
+
+
+# --------------------------------------------------------------------------
+# clocks
+# --------------------------------------------------------------------------
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device: int):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(0.002)
+
+    def start(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self.nv:
+            self._sample()
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        names = [k for k, v in self.REASONS.items() if self.reasons & v and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------
+# CPU baseline (the oracle port of the reference's attention path)
+# --------------------------------------------------------------------------
+
+def cpu_decode_rate(ctx_lens, budget_s: float, threads: int = 0, max_seqs: int = 16):
+    """Reference decode steps (local + global attention block per sequence,
+    model.rs:393-410 with the reference's concat copy and head-parallel
+    pool) on a stratified sample of the sequences, repeated until the time
+    budget is spent. Returns (tokens/s, cores, sample description)."""
+    import oracle
+    cores = oracle.pool_init(threads)
+    hp = oracle.hparams_e2b()
+    ff = oracle.proportional_rope_freq_factors(HD_G, hp.global_p)
+    lens = sorted(int(c) for c in ctx_lens)
+    stride = max(1, len(lens) // max_seqs)
+    sample = lens[::stride][:max_seqs]
+    r = np.random.default_rng(7)
+    work = []
+    for c in sample:
+        kv = oracle.KvCache()
+        hist = c - 1
+        for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+            if hist:
+                kv.append_rows(layer, r.standard_normal((hist, hd)).astype(np.float32),
+                               r.standard_normal((hist, hd)).astype(np.float32))
+        inputs = {hd: (r.standard_normal(HEADS * hd).astype(np.float32), r.standard_normal(hd).astype(np.float32),
+                       r.standard_normal(hd).astype(np.float32), np.ones(hd, np.float32)) for hd in (HD_L, HD_G)}
+        work.append((c, kv, inputs))
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        for c, kv, inputs in work:
+            for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+                q, k, v, w = inputs[hd]
+                kv.attention_block(hp, layer, c - 1, q, k, v, w, w, ff)
+            # a repeat appends one more row past the attended range (the
+            # position stays c-1), so every repeat does the same attention work
+            done += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    desc = (f"{len(sample)} of {len(lens)} sequences (every {stride}th by context length, contexts "
+            f"{sample[0]}..{sample[-1]}), one decode step each on layers 13 and 14, repeated for {el:.1f} s")
+    return done / el, cores, desc
+
+
+# --------------------------------------------------------------------------
+# GPU measurements
+# --------------------------------------------------------------------------
+
+def build_decode(torch, g4a, ctx, ctx_lens, extra_rows, seed):
+    """Cache filled with each sequence's history (positions 0..c-2), inputs
+    for one decode step at position c-1 on layers 13 and 14."""
+    n = len(ctx_lens)
+    kv = g4a.KvCache(ctx, n, MAX_CTX + extra_rows, dtype=g4a.KV_F16, layers=[LOCAL_LAYER, GLOBAL_LAYER])
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    weights = {}
+    for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+        weights[layer] = (1 + 0.1 * torch.randn(hd, device="cuda", generator=gen),
+                          1 + 0.1 * torch.randn(hd, device="cuda", generator=gen))
+    for s, c in enumerate(ctx_lens):
+        hist = int(c) - 1
+        for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+            if hist:
+                k = torch.randn(hist, hd, device="cuda", generator=gen)
+                v = torch.randn(hist, hd, device="cuda", generator=gen)
+                kv.append_tokens(s, layer, k, v, weights[layer][1])
+    args = {}
+    for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+        args[layer] = dict(layer=layer, q_raw=torch.randn(n, HEADS * hd, device="cuda", generator=gen),
+                           k_raw=torch.randn(n, hd, device="cuda", generator=gen),
+                           v_raw=torch.randn(n, hd, device="cuda", generator=gen),
+                           q_norm_w=weights[layer][0], k_norm_w=weights[layer][1],
+                           out=torch.empty(n, HEADS * hd, device="cuda"))
+    ctx.sync()
+    return kv, args
+
+
+def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, device):
+    n = len(ctx_lens)
+    seqs = list(range(n))
+    positions = [int(c) - 1 for c in ctx_lens]
+    e2e_steps = min(steps, 50)
+    kv, args = build_decode(torch, g4a, ctx, ctx_lens, e2e_steps + 8, 1234 + device)
+    plan_l = ctx.decode_plan(kv, [args[LOCAL_LAYER]], seqs, positions)
+    plan_g = ctx.decode_plan(kv, [args[GLOBAL_LAYER]], seqs, positions)
+    for _ in range(warmup):
+        plan_l.run()
+        plan_g.run()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    clocks = ClockSampler(device)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(steps):
+        ev[k][0].record(stream)
+        plan_l.run()
+        ev[k][1].record(stream)
+        plan_g.run()
+        ev[k][2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks.stop()
+    if dist is not None:
+        dist.barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    g_ms = [ev[k][1].elapsed_time(ev[k][2]) for k in range(steps)]
+    l_ms = [ev[k][0].elapsed_time(ev[k][1]) for k in range(steps)]
+    plan_l.close()
+    plan_g.close()
+
+    # ---- e2e through g4a_decode with host buffers ----
+    pin = {}
+    for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+        a = args[layer]
+        pin[layer] = {k: a[k].cpu().pin_memory() for k in ("q_raw", "k_raw", "v_raw")}
+        pin[layer]["out"] = torch.empty_like(a["out"], device="cpu").pin_memory()
+    h2d = sum(t.numel() * 4 for layer in pin for k, t in pin[layer].items() if k != "out")
+    d2h = sum(pin[layer]["out"].numel() * 4 for layer in pin)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for k in range(e2e_steps):
+            for layer in (LOCAL_LAYER, GLOBAL_LAYER):
+                for name in ("q_raw", "k_raw", "v_raw"):
+                    args[layer][name].copy_(pin[layer][name], non_blocking=True)
+            pos = [p + 1 + k for p in positions]  # each call appends: the context advances
+            ctx.decode(kv, [args[LOCAL_LAYER], args[GLOBAL_LAYER]], seqs, pos)
+            for layer in (LOCAL_LAYER, GLOBAL_LAYER):
+                pin[layer]["out"].copy_(args[layer]["out"], non_blocking=True)
+            stream.synchronize()  # the caller reads this step's attention output
+        e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end)
+    ctx.sync()
+    kv.close()
+    return {"total_ms": total_ms, "global_ms": statistics.mean(g_ms), "local_ms": statistics.mean(l_ms),
+            "clocks": clocks.summary(), "e2e_ms": e2e_ms, "e2e_steps": e2e_steps, "h2d": h2d, "d2h": d2h}
+
+
+def measure_batch1(torch, g4a, ctx, stream, reps=200):
+    """Configuration 0: one decode step, batch 1, context 628, f32 KV; plan
+    runs timed per layer (kernel launches only)."""
+    kv, args = None, None
+    ctx_lens = [628]
+    n = 1
+    kv = g4a.KvCache(ctx, 1, 1024, dtype=g4a.KV_F32, layers=[LOCAL_LAYER, GLOBAL_LAYER])
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(628)
+    out = {}
+    for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+        w = torch.ones(hd, device="cuda")
+        kv.append_tokens(0, layer, torch.randn(627, hd, device="cuda", generator=gen),
+                         torch.randn(627, hd, device="cuda", generator=gen), w)
+        a = dict(layer=layer, q_raw=torch.randn(n, HEADS * hd, device="cuda", generator=gen),
+                 k_raw=torch.randn(n, hd, device="cuda", generator=gen),
+                 v_raw=torch.randn(n, hd, device="cuda", generator=gen), q_norm_w=w, k_norm_w=w,
+                 out=torch.empty(n, HEADS * hd, device="cuda"))
+        plan = ctx.decode_plan(kv, [a], [0], [627])
+        for _ in range(20):
+            plan.run()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        torch.cuda.synchronize()
+        for e0, e1 in evs:
+            e0.record(stream)
+            plan.run()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+        rows = 512 if hd == HD_L else 628
+        nbytes = 2 * rows * hd * 4 + 2 * HEADS * hd * 4 + 2 * hd * 4 + 2 * hd * 4
+        out["local" if hd == HD_L else "global"] = {"us_median": round(us, 2), "bytes": nbytes,
+                                                    "GB_s": round(nbytes / us / 1e3, 1)}
+        plan.close()
+    kv.close()
+    return out
+
+
+def flush_l2(torch, buf):
+    buf.add_(1.0)
+
+
+def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2):
+    """Configurations 1 and 3 on one GPU: tcgen05 prefill, CUDA events around
+    each launch, L2 flushed (256 MB write) between launches."""
+    hp = g4a.hparams_e2b()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(31)
+    flush = torch.empty(64 * 1024 * 1024, device="cuda")
+    res = {}
+
+    def unit(shape):
+        x = torch.randn(*shape, device="cuda", generator=gen)
+        return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
+
+    def timed(problems):
+        for _ in range(warmup):
+            ctx.prefill(problems)
+        ts = []
+        for _ in range(reps):
+            flush_l2(torch, flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ctx.prefill(problems)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ctx.sync()
+        return statistics.median(ts)
+
+    # configuration 1: 628 tokens, 35 layers, layers 15-34 reuse 13/14's K/V
+    T = 628
+    kvs, probs = {}, []
+    for layer in range(35):
+        src, _ = g4a.kv_source_layer(hp, layer)
+        hd = g4a.head_dim(hp, layer)
+        glob = g4a.layer_is_global(hp, layer)
+        if src not in kvs:
+            kvs[src] = (unit((T, hd)), torch.randn(T, hd, device="cuda", generator=gen).to(torch.bfloat16))
+        probs.append(dict(head_dim=hd, window=0 if glob else 512, n_q=T, n_kv=T, q=unit((T, HEADS, hd)),
+                          k=kvs[src][0], v=kvs[src][1], out=torch.empty(T, HEADS, hd, device="cuda")))
+    ms = timed(probs)
+    flops = sum(4 * HEADS * p["head_dim"] * prefill_pairs(T, p["window"]) for p in probs)
+    tf = flops / ms / 1e9
+    res["cfg1_628x35"] = {"ms": round(ms, 4), "gflop": round(flops / 1e9, 3), "TFLOP_s": round(tf, 1),
+                          "frac_of_peak": round(tf / pk["bf16"], 4)}
+    del probs, kvs
+    # configuration 3: 32,768-token global layer on one GPU
+    T = 32768
+    q, k = unit((T, HEADS, HD_G)), unit((T, HD_G))
+    v = torch.randn(T, HD_G, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.empty(T, HEADS, HD_G, device="cuda")
+    ms = timed([dict(head_dim=HD_G, window=0, n_q=T, n_kv=T, q=q, k=k, v=v, out=out)])
+    flops = 4 * HEADS * HD_G * (T * (T + 1) // 2)
+    tf = flops / ms / 1e9
+    res["cfg3_32768_global_1gpu"] = {"ms": round(ms, 3), "tflop": round(flops / 1e12, 3), "TFLOP_s": round(tf, 1),
+                                     "frac_of_peak": round(tf / pk["bf16"], 4)}
+    return res
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of the global decode kernel from the committed
+    ncu summary, scaled by the workload ratio recorded there (or None)."""
+    f = ROOT / "profiles" / "decode_global_f16_cfg2.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":")[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------------------
+# main
+# --------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
+    ap.add_argument("--no-extras", action="store_true", help="skip the batch-1 and prefill sub-measurements")
+    a = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n_gpus = max(a.gpus, world)
+    lengths = global_lengths(n_gpus)
+    pk = peaks()
+
+    if a.impl == "reference":
+        if rank != 0:
+            return
+        # each timed step is a bounded sample of the workload: one sequence's
+        # decode step (both layers), cycling through a stratified sample.
+        budget = max(5.0, min(120.0, 0.05 * (a.steps + a.warmup)))
+        rate, cores, desc = cpu_decode_rate(shard(lengths, n_gpus, 0), budget, threads=0)
+        line = {"impl": "reference", "metric": METRIC, "value": round(rate, 2), "unit": "tokens/s",
+                "n_gpus": n_gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(1e3 / rate, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": "cfg2 paged batched decode (reference CPU path)", "seqs_per_gpu": SEQS_PER_GPU,
+                           "context": "U[1,4096] seeded", "layers": [LOCAL_LAYER, GLOBAL_LAYER]},
+                "cpu_baseline": {"value": round(rate, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": desc},
+                "e2e": {"value": round(rate, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import g4attn as g4a
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist_mod.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+        dist = dist_mod
+    device = local_rank
+    torch.cuda.set_device(device)
+    my_lens = shard(lengths, n_gpus, rank)
+    ctx = g4a.Context(device, max_positions=MAX_CTX + 128)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+
+    d = measure_decode(torch, g4a, ctx, stream, [int(c) for c in my_lens], a.steps, a.warmup, dist, device)
+    sb = step_bytes([int(c) for c in my_lens])
+    total_s = d["total_ms"] / 1e3
+    e2e_s = d["e2e_ms"] / 1e3
+    if dist is not None:
+        t = torch.tensor([total_s, e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_s, e2e_s = float(t[0]), float(t[1])
+        byt = torch.tensor([float(sb["total"])], device="cuda", dtype=torch.float64)
+        dist.all_reduce(byt)
+        job_bytes = float(byt[0])
+        clocks_all = [None] * world
+        dist.all_gather_object(clocks_all, d["clocks"])
+    else:
+        job_bytes = float(sb["total"])
+        clocks_all = [d["clocks"]]
+    tokens = SEQS_PER_GPU * n_gpus
+    value = tokens * a.steps / total_s
+    e2e_value = tokens * d["e2e_steps"] / e2e_s
+
+    extras = {}
+    if rank == 0 and not a.no_extras:
+        extras["decode_batch1"] = measure_batch1(torch, g4a, ctx, stream)
+        extras["prefill"] = measure_prefill(torch, g4a, ctx, stream, pk)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu_rate, cores, desc = None, None, None
+    if n_gpus == 1:
+        cpu_rate, cores, desc = cpu_decode_rate(my_lens, a.cpu_budget, threads=0)
+
+    achieved = sb["global"] / (d["global_ms"] / 1e3) / 1e9
+    sm = [c["sm_mhz"] for c in clocks_all if c and c["sm_mhz"]]
+    reasons = sorted({r for c in clocks_all if c for r in c["reasons"]})
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": n_gpus,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(total_s * 1e3 / a.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 KV / f32 compute",
+        "data": "synthetic",
+        "config": {
+            "workload": "cfg2: paged batched decode, 64 sequences per GPU, context U[1,4096] (seeded), "
+                        "E2B layers 13 (sliding, 256-d) and 14 (global, 512-d), 8 q heads / 1 KV head, "
+                        "f16 KV in 64-token pages, f32 q",
+            "seqs_per_gpu": SEQS_PER_GPU,
+            "global_batch": tokens,
+            "hbm_GB_s_whole_step": round(job_bytes / n_gpus / (total_s / a.steps) / 1e9, 1),
+            "frac_of_nominal_8TBs_whole_step": round(job_bytes / n_gpus / (total_s / a.steps) / 1e9 / NOMINAL_HBM_GBS, 4),
+            "bytes_per_step_job": int(job_bytes),
+            "l2": "inputs larger than L2 (K/V read per step per GPU >> 126 MB)",
+            "parallelism": f"sequence-sharded x{n_gpus}, no collective",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "decode_kernel<512, f16> (global layer 14)",
+            "achieved": round(achieved, 1),
+            "peak": pk["hbm"],
+            "unit": "GB/s",
+            "frac": round(achieved / pk["hbm"], 4),
+            "peak_source": pk["source"],
+            "traffic": traffic_from_profile(),
+            "algorithmic_bytes_per_launch": sb["global"],
+            "launch_us": round(d["global_ms"] * 1e3, 2),
+            "local_kernel_us": round(d["local_ms"] * 1e3, 2),
+        },
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": d["h2d"],
+                "d2h_bytes_per_step": d["d2h"], "steps": d["e2e_steps"],
+                "api": "g4a_decode (C ABI) with pinned host inputs/outputs, stream sync per step"},
+        "gpu_launches": 2 * a.steps,
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
+                   "sm_max_mhz": clocks_all[0]["sm_max_mhz"] if clocks_all[0] else None, "reasons": reasons},
+    }
+    if cpu_rate is not None:
+        line["cpu_baseline"] = {"value": round(cpu_rate, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": desc}
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

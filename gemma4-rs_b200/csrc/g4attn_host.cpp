@@ -381,11 +381,6 @@ extern "C" int g4a_kv_create(g4a_ctx *ctx, int32_t n_seqs, int32_t max_tokens, i
         g4a_kv_destroy(kv);
         return fail(ctx, G4A_CUDA, "compute: out of device memory for the block table");
     }
-    int rc = ensure_rope(ctx, std::max(ctx->max_positions, max_tokens));
-    if (rc != G4A_OK) {
-        g4a_kv_destroy(kv);
-        return rc;
-    }
     *out = kv;
     return G4A_OK;
 }
@@ -544,44 +539,91 @@ void add_items(Plan &plan, DecodeTask &t, int32_t task_index, int32_t rows_per, 
     }
 }
 
-int run_plan(g4a_ctx *ctx, Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens, int kv_f16) {
+// Device-side form of a plan: metadata, split-KV partials and tickets, and
+// the kernel parameters of the two head-width launches.
+struct Staged {
+    uint8_t *meta = nullptr;
+    float *part_o = nullptr;
+    float *part_ml = nullptr;
+    unsigned *tickets = nullptr;
+    DecodeParams params{};
+    int32_t n_items[2] = {0, 0};
+    size_t items_offset = 0;
+    int kv_f16 = 0;
+};
+
+// Copies a plan's metadata to the device. With own_buffers the buffers are
+// allocated for this plan alone; otherwise the context's reusable ones are
+// grown as needed.
+int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens,
+               int kv_f16, bool own_buffers, Staged *st) {
     const size_t n_tasks = plan.tasks.size();
     const size_t n_items = plan.items[0].size() + plan.items[1].size();
     const size_t bytes_tasks = n_tasks * sizeof(DecodeTask);
     const size_t bytes = bytes_tasks + n_items * sizeof(DecodeItem);
+    const size_t n_po = (size_t)std::max(plan.slots, 1) * kHeads * 512;
+    const size_t n_ml = (size_t)std::max(plan.slots, 1) * 2 * kHeads;
+    const size_t n_tk = std::max<size_t>(n_tasks, 1);
     int rc;
-    if ((rc = grow(ctx, &ctx->d_meta, &ctx->meta_cap, bytes, false))) return rc;
-    if ((rc = grow(ctx, &ctx->d_part_o, &ctx->part_o_cap, (size_t)std::max(plan.slots, 1) * kHeads * 512, false)))
-        return rc;
-    if ((rc = grow(ctx, &ctx->d_part_ml, &ctx->part_ml_cap, (size_t)std::max(plan.slots, 1) * 2 * kHeads, false)))
-        return rc;
-    if ((rc = grow(ctx, &ctx->d_tickets, &ctx->tickets_cap, std::max<size_t>(n_tasks, 1), true))) return rc;
-    ctx->h_meta.resize(bytes);
+    if (own_buffers) {
+        G4A_CUDA_TRY(ctx, cudaMalloc(&st->meta, std::max<size_t>(bytes, 16)));
+        G4A_CUDA_TRY(ctx, cudaMalloc(&st->part_o, n_po * sizeof(float)));
+        G4A_CUDA_TRY(ctx, cudaMalloc(&st->part_ml, n_ml * sizeof(float)));
+        G4A_CUDA_TRY(ctx, cudaMalloc(&st->tickets, n_tk * sizeof(unsigned)));
+        G4A_CUDA_TRY(ctx, cudaMemsetAsync(st->tickets, 0, n_tk * sizeof(unsigned), ctx->stream));
+    } else {
+        if ((rc = grow(ctx, &ctx->d_meta, &ctx->meta_cap, bytes, false))) return rc;
+        if ((rc = grow(ctx, &ctx->d_part_o, &ctx->part_o_cap, n_po, false))) return rc;
+        if ((rc = grow(ctx, &ctx->d_part_ml, &ctx->part_ml_cap, n_ml, false))) return rc;
+        if ((rc = grow(ctx, &ctx->d_tickets, &ctx->tickets_cap, n_tk, true))) return rc;
+        st->meta = ctx->d_meta;
+        st->part_o = ctx->d_part_o;
+        st->part_ml = ctx->d_part_ml;
+        st->tickets = ctx->d_tickets;
+    }
+    ctx->h_meta.resize(std::max<size_t>(bytes, 1));
     std::memcpy(ctx->h_meta.data(), plan.tasks.data(), bytes_tasks);
     std::memcpy(ctx->h_meta.data() + bytes_tasks, plan.items[0].data(), plan.items[0].size() * sizeof(DecodeItem));
     std::memcpy(ctx->h_meta.data() + bytes_tasks + plan.items[0].size() * sizeof(DecodeItem), plan.items[1].data(),
                 plan.items[1].size() * sizeof(DecodeItem));
-    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->d_meta, ctx->h_meta.data(), bytes, cudaMemcpyHostToDevice, ctx->stream));
-    DecodeParams p{};
-    p.tasks = reinterpret_cast<const DecodeTask *>(ctx->d_meta);
+    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(st->meta, ctx->h_meta.data(), bytes, cudaMemcpyHostToDevice, ctx->stream));
+    DecodeParams &p = st->params;
+    p = DecodeParams{};
+    p.tasks = reinterpret_cast<const DecodeTask *>(st->meta);
     p.block_table = d_bt;
     p.max_pages = max_pages;
     p.page_tokens = page_tokens;
     p.rope_local = ctx->d_rope_local;
     p.rope_global = ctx->d_rope_global;
     p.eps = ctx->hp.rms_norm_eps;
-    p.part_o = ctx->d_part_o;
-    p.part_ml = ctx->d_part_ml;
-    p.tickets = ctx->d_tickets;
+    p.part_o = st->part_o;
+    p.part_ml = st->part_ml;
+    p.tickets = st->tickets;
     p.err_flag = ctx->d_err;
-    const DecodeItem *items = reinterpret_cast<const DecodeItem *>(ctx->d_meta + bytes_tasks);
+    st->n_items[0] = (int32_t)plan.items[0].size();
+    st->n_items[1] = (int32_t)plan.items[1].size();
+    st->items_offset = bytes_tasks;
+    st->kv_f16 = kv_f16;
+    return G4A_OK;
+}
+
+int launch_staged(g4a_ctx *ctx, const Staged &st) {
+    DecodeParams p = st.params;
+    const DecodeItem *items = reinterpret_cast<const DecodeItem *>(st.meta + st.items_offset);
     for (int which = 0; which < 2; which++) {
         p.items = items;
-        p.n_items = (int32_t)plan.items[which].size();
-        G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, kv_f16, true, ctx->stream));
-        items += plan.items[which].size();
+        p.n_items = st.n_items[which];
+        G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream));
+        items += st.n_items[which];
     }
     return G4A_OK;
+}
+
+int run_plan(g4a_ctx *ctx, Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens, int kv_f16) {
+    Staged st;
+    int rc = stage_plan(ctx, plan, d_bt, max_pages, page_tokens, kv_f16, false, &st);
+    if (rc) return rc;
+    return launch_staged(ctx, st);
 }
 
 }  // namespace
@@ -616,8 +658,12 @@ extern "C" int g4a_attend(g4a_ctx *ctx, const float *q, const float *keys, const
     return G4A_OK;
 }
 
-extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
-                          const int32_t *seq_ids, const int32_t *positions) {
+namespace {
+
+// Validates one decode step, allocates the pages its appends need, advances
+// the cache lengths and fills `plan` (model.rs:393-410 per sequence and layer).
+int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
+                 const int32_t *seq_ids, const int32_t *positions, Plan &plan) {
     if (!ctx || !kv || kv->ctx != ctx) return fail(ctx, G4A_COMPUTE, "compute: cache belongs to another context");
     cudaSetDevice(ctx->device);
     const g4a_hparams &hp = ctx->hp;
@@ -685,9 +731,7 @@ extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_
             }
     int rc = upload_bt(kv);
     if (rc) return rc;
-    Plan plan;
     int64_t weighted = 0;
-    std::vector<int64_t> lo_hi;
     for (int32_t i = 0; i < n_layers; i++)
         for (int32_t j = 0; j < n_seqs; j++) {
             int64_t lo, hi;
@@ -727,11 +771,60 @@ extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_
             plan.tasks.push_back(t);
         }
     }
-    if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16))) return rc;
     for (int32_t i = 0; i < n_layers; i++)
         if (owner[i])
             for (int32_t j = 0; j < n_seqs; j++) kv_len(kv, seq_ids[j], layers[i].layer) += 1;
     return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
+                          const int32_t *seq_ids, const int32_t *positions) {
+    Plan plan;
+    int rc = build_decode(ctx, kv, n_layers, layers, n_seqs, seq_ids, positions, plan);
+    if (rc) return rc;
+    return run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16);
+}
+
+struct g4a_plan {
+    g4a_ctx *ctx = nullptr;
+    Staged st;
+};
+
+extern "C" int g4a_decode_plan(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers,
+                               int32_t n_seqs, const int32_t *seq_ids, const int32_t *positions, g4a_plan **out) {
+    if (!out) return fail(ctx, G4A_COMPUTE, "compute: null plan output");
+    *out = nullptr;
+    Plan plan;
+    int rc = build_decode(ctx, kv, n_layers, layers, n_seqs, seq_ids, positions, plan);
+    if (rc) return rc;
+    auto *pl = new g4a_plan();
+    pl->ctx = ctx;
+    rc = stage_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16, true, &pl->st);
+    if (rc) {
+        g4a_plan_destroy(pl);
+        return rc;
+    }
+    *out = pl;
+    return G4A_OK;
+}
+
+extern "C" int g4a_plan_run(g4a_plan *plan) {
+    if (!plan) return G4A_COMPUTE;
+    cudaSetDevice(plan->ctx->device);
+    return launch_staged(plan->ctx, plan->st);
+}
+
+extern "C" void g4a_plan_destroy(g4a_plan *plan) {
+    if (!plan) return;
+    cudaSetDevice(plan->ctx->device);
+    cudaStreamSynchronize(plan->ctx->stream);
+    cudaFree(plan->st.meta);
+    cudaFree(plan->st.part_o);
+    cudaFree(plan->st.part_ml);
+    cudaFree(plan->st.tickets);
+    delete plan;
 }
 
 extern "C" int g4a_lse_merge(g4a_ctx *ctx, int32_t n_parts, const float *const *parts_out, const float *const *parts_lse,

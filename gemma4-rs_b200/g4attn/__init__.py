@@ -96,6 +96,11 @@ def _load():
     L.g4a_kv_view.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, _vp, _vp]
     L.g4a_kv_append_tokens.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp, ctypes.c_int64]
     L.g4a_decode.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(DecodeLayer), ctypes.c_int32, _i32p, _i32p]
+    L.g4a_decode_plan.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(DecodeLayer), ctypes.c_int32, _i32p,
+                                  _i32p, ctypes.POINTER(_vp)]
+    L.g4a_plan_run.argtypes = [_vp]
+    L.g4a_plan_destroy.argtypes = [_vp]
+    L.g4a_plan_destroy.restype = None
     L.g4a_prefill.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(PrefillProblem)]
     L.g4a_lse_merge.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int64,
                                 ctypes.c_int32, ctypes.c_int32, _vp, _vp]
@@ -113,7 +118,7 @@ _exiting = False
 
 def _close_all():
     global _exiting
-    for obj in sorted(list(_live), key=lambda o: isinstance(o, Context)):  # caches before contexts
+    for obj in sorted(list(_live), key=lambda o: (isinstance(o, KvCache), isinstance(o, Context))):  # plans, caches, contexts
         try:
             obj.close()
         except Exception:
@@ -190,8 +195,8 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None) and not _exiting:
-            for kv in [o for o in _live if isinstance(o, KvCache) and o.ctx is self]:
-                kv.close()
+            for o in [o for o in _live if not isinstance(o, Context) and o.ctx is self]:
+                o.close()
             lib.g4a_ctx_destroy(self.h)
         self.h = None
 
@@ -217,7 +222,8 @@ class Context:
                                   _ptr(values) if length else None, length, n_heads, n_kv_heads, hd, scale,
                                   _ptr(out)))
 
-    def decode(self, kv: "KvCache", layers: list[dict], seq_ids: list[int], positions: list[int]):
+    @staticmethod
+    def _decode_args(layers, seq_ids, positions):
         arr = (DecodeLayer * max(1, len(layers)))()
         for i, a in enumerate(layers):
             arr[i] = DecodeLayer(a["layer"], _ptr(a["q_raw"]), _ptr(a.get("k_raw")), _ptr(a.get("v_raw")),
@@ -225,7 +231,17 @@ class Context:
         n = len(seq_ids)
         s = (ctypes.c_int32 * max(1, n))(*seq_ids)
         p = (ctypes.c_int32 * max(1, n))(*positions)
+        return arr, n, s, p
+
+    def decode(self, kv: "KvCache", layers: list[dict], seq_ids: list[int], positions: list[int]):
+        arr, n, s, p = self._decode_args(layers, seq_ids, positions)
         self.check(lib.g4a_decode(self.h, kv.h, len(layers), arr, n, s, p))
+
+    def decode_plan(self, kv: "KvCache", layers: list[dict], seq_ids: list[int], positions: list[int]) -> "Plan":
+        arr, n, s, p = self._decode_args(layers, seq_ids, positions)
+        h = _vp()
+        self.check(lib.g4a_decode_plan(self.h, kv.h, len(layers), arr, n, s, p, ctypes.byref(h)))
+        return Plan(self, h)
 
     def prefill(self, problems: list[dict]):
         arr = (PrefillProblem * max(1, len(problems)))()
@@ -240,6 +256,26 @@ class Context:
         po = (_vp * n)(*[_ptr(t) for t in outs])
         pl = (_vp * n)(*[_ptr(t) for t in lses])
         self.check(lib.g4a_lse_merge(self.h, n, po, pl, rows, n_heads, hd, _ptr(out), _ptr(lse)))
+
+
+class Plan:
+    """g4a_plan: a staged decode step that can be launched repeatedly."""
+
+    def __init__(self, ctx: Context, h):
+        self.ctx = ctx
+        self.h = h
+        _live.add(self)
+
+    def run(self):
+        self.ctx.check(lib.g4a_plan_run(self.h))
+
+    def close(self):
+        if getattr(self, "h", None) and not _exiting:
+            lib.g4a_plan_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 class KvCache:

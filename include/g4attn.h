@@ -169,6 +169,19 @@ typedef struct g4a_decode_layer {
 int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers_host,
                int32_t n_seqs, const int32_t *seq_ids_host, const int32_t *positions_host);
 
+/* A decode step staged for repeated launches: g4a_decode's validation, page
+ * allocation and cache-length update happen here once; the plan owns device
+ * copies of its work list and its split-KV scratch. */
+typedef struct g4a_plan g4a_plan;
+int g4a_decode_plan(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers_host,
+                    int32_t n_seqs, const int32_t *seq_ids_host, const int32_t *positions_host,
+                    g4a_plan **out);
+/* Launches a staged step on the context's stream (kernel launches only, no
+ * host-device copies, so it can be captured into a CUDA graph). Running a
+ * plan again recomputes the same step and rewrites the same appended rows. */
+int g4a_plan_run(g4a_plan *plan);
+void g4a_plan_destroy(g4a_plan *plan);
+
 /* ---- prefill attention (tcgen05 tensor cores) -------------------------- */
 
 /* One causal attention problem over bf16 inputs that are already normalised

@@ -497,6 +497,15 @@ int orc_kv_append(orc_kv *kv, size_t layer, const float *k, const float *v, size
     return ORC_OK;
 }
 
+/* n appends of consecutive rows (k, v each [n][width]). */
+int orc_kv_append_rows(orc_kv *kv, size_t layer, const float *k, const float *v, size_t width, size_t n) {
+    for (size_t i = 0; i < n; i++) {
+        int rc = orc_kv_append(kv, layer, k + i * width, v + i * width, width);
+        if (rc) return rc;
+    }
+    return ORC_OK;
+}
+
 /* context_memory.rs:53-69 view: a missing layer is fine only for len 0;
  * asking for more rows than stored is ContextTooLong. A layer that exists
  * only because a later one was appended (resize_with) has zero rows. */
@@ -578,7 +587,15 @@ int orc_attention_block(orc_kv *kv, const orc_hparams *hp, int32_t layer, size_t
         size_t lo, hi;                                                       /* :408 */
         if (global) { lo = 0; hi = position + 1; }
         else orc_windowed_len(position + 1, (size_t)hp->sliding_window, &lo, &hi);
-        rc = orc_attend(q, keys + lo * width, values + lo * width, hi - lo, nh, nkv, hd, 1.0f, out); /* :410 */
+        /* model.rs:352-353: attend concatenates the windowed rows into fresh
+         * buffers on every call; the copy is part of the reference's cost. */
+        size_t n = (hi - lo) * width;
+        float *kc = malloc((n ? n : 1) * sizeof(float)), *vc = malloc((n ? n : 1) * sizeof(float));
+        memcpy(kc, keys + lo * width, n * sizeof(float));
+        memcpy(vc, values + lo * width, n * sizeof(float));
+        rc = orc_attend(q, kc, vc, hi - lo, nh, nkv, hd, 1.0f, out);         /* :410 */
+        free(kc);
+        free(vc);
     }
     free(q);
     return rc;

@@ -71,6 +71,7 @@ orc_kv *orc_kv_create(void);
 void orc_kv_destroy(orc_kv *kv);
 void orc_kv_clear(orc_kv *kv);
 int orc_kv_append(orc_kv *kv, size_t layer, const float *k, const float *v, size_t width);
+int orc_kv_append_rows(orc_kv *kv, size_t layer, const float *k, const float *v, size_t width, size_t n);
 int orc_kv_view(const orc_kv *kv, size_t layer, size_t len, const float **keys,
                 const float **values, size_t *width, size_t *max_len);
 

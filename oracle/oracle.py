@@ -66,6 +66,7 @@ def lib():
         L.orc_kv_destroy.argtypes = [ctypes.c_void_p]
         L.orc_kv_clear.argtypes = [ctypes.c_void_p]
         L.orc_kv_append.argtypes = [ctypes.c_void_p, sz, _f32p, _f32p, sz]
+        L.orc_kv_append_rows.argtypes = [ctypes.c_void_p, sz, _f32p, _f32p, sz, sz]
         L.orc_kv_view.argtypes = [ctypes.c_void_p, sz, sz, ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
                                   ctypes.POINTER(sz), ctypes.POINTER(sz)]
         L.orc_attention_block.argtypes = [ctypes.c_void_p, ctypes.POINTER(HParams), ctypes.c_int32, sz,
@@ -226,6 +227,10 @@ class KvCache:
     def append(self, layer, k, v):
         k, v = f32(k), f32(v)
         _check(lib().orc_kv_append(self.h, layer, _p(k), _p(v), k.size), "append")
+
+    def append_rows(self, layer, k, v):
+        k, v = f32(k), f32(v)
+        _check(lib().orc_kv_append_rows(self.h, layer, _p(k), _p(v), k.shape[-1], k.shape[0]), "append_rows")
 
     def view(self, layer, length):
         kp, vp, w, m = _f32p(), _f32p(), ctypes.c_size_t(), ctypes.c_size_t()

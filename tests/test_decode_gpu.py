@@ -328,3 +328,38 @@ def test_decode_position_zero_and_nonfinite(g4a, oracle, ctx, torch_cuda):
         ctx.sync()
     assert e.value.code == g4a.NONFINITE
     kv.close()
+
+
+def test_plan_runs_match_decode(g4a, oracle, ctx, torch_cuda):
+    """A staged plan gives the oracle's result, on every repeated run."""
+    torch = torch_cuda
+    hp = oracle.hparams_e2b()
+    ff = oracle.proportional_rope_freq_factors(512, 0.25)
+    r = rng(77)
+    lengths = [5, 300, 900]
+    kv = g4a.KvCache(ctx, 3, 1024, dtype=1, layers=[14])
+    okvs = [oracle.KvCache() for _ in lengths]
+    wq, wk = norm_weight(r, 512), norm_weight(r, 512)
+    for s, L in enumerate(lengths):
+        _fill_history(g4a, oracle, torch, kv, okvs[s], hp, s, 14, L, r, wk, ff)
+    q_raw, k_raw, v_raw = normal(r, 3, 8 * 512), normal(r, 3, 512), normal(r, 3, 512)
+    out = torch.empty(3, 8 * 512, device="cuda")
+    a = dict(layer=14, q_raw=dev(torch, q_raw), k_raw=dev(torch, k_raw), v_raw=dev(torch, v_raw),
+             q_norm_w=dev(torch, wq), k_norm_w=dev(torch, wk), out=out)
+    plan = ctx.decode_plan(kv, [a], [0, 1, 2], lengths)
+    assert kv.len(1, 14) == 301
+    refs = [okvs[s].attention_block(hp, 14, L, q_raw[s], k_raw[s], v_raw[s], wq, wk, ff, kv_store=1)
+            for s, L in enumerate(lengths)]
+    first = None
+    for _ in range(3):
+        out.fill_(float("nan"))
+        plan.run()
+        ctx.sync()
+        got = host(out)
+        for s in range(3):
+            assert max_abs_diff(got[s], refs[s]) <= TOL
+        if first is None:
+            first = got.copy()
+        assert np.array_equal(got, first)  # deterministic combine order
+    plan.close()
+    kv.close()
