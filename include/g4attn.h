@@ -110,6 +110,21 @@ int g4a_attend(g4a_ctx *ctx, const float *q_dev, const float *keys_dev, const fl
                int64_t len, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, float scale,
                float *out_dev);
 
+/* No counterpart in the reference. The same attention as g4a_attend for the
+ * E2B shape (n_heads 8, n_kv_heads 1, head_dim 256 or 512), for callers that
+ * cannot allocate device memory when they call it (e.g. a server that gave
+ * its device memory to its own pools at start-up). It allocates nothing: its
+ * scratch is a file-scope device array of about 1 MiB (64 row ranges x 8
+ * heads x 512 columns of f32 plus their max/sum), held by every GPU that
+ * loads the library until exit. Other shapes return G4A_COMPUTE. The first
+ * call on a device (that device current) looks the array up; make it before
+ * any stream capture. Calls share the array, so calls that overlap on the
+ * GPU race; queue them on one stream. Queued on cuda_stream; no context is
+ * used, and a non-finite softmax shows as NaN in out_dev. */
+int g4a_attend_static(void *cuda_stream, const float *q_dev, const float *keys_dev,
+                      const float *values_dev, int64_t len, int32_t n_heads, int32_t n_kv_heads,
+                      int32_t head_dim, float scale, float *out_dev);
+
 /* ---- paged KV cache: ContextMemory (context_memory.rs:11-18) ------------ */
 
 /* A paged cache for n_seqs sequences of up to max_tokens rows per layer.
