@@ -309,28 +309,38 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     __syncthreads();
     if (!last_s) return;
     __threadfence();
+    // Merge: per (split, head) weights computed in parallel into shared
+    // memory (q_s is free now), then every thread sums its columns over the
+    // splits in split order.
+    const int ns = tk.n_splits;
     const float *pml = p.part_ml + (size_t)tk.partial_base * 2 * kHeads;
     const float *pall = p.part_o + (size_t)tk.partial_base * kHeads * HD;
-#pragma unroll 1
-    for (int h = 0; h < kHeads; h++) {
+    float *wsm = &q_s[0][0];  // [ns][8] weights, then [8] 1/L; ns*8+8 <= 8*HD
+    {
+        const int h = warp;
         float M = -CUDART_INF_F;
-        for (int s = 0; s < tk.n_splits; s++) M = fmaxf(M, __ldcg(pml + (size_t)s * 2 * kHeads + h));
+        for (int s = lane; s < ns; s += 32) M = fmaxf(M, __ldcg(pml + (size_t)s * 2 * kHeads + h));
+        M = warp_max(M);
         float L = 0.0f;
-        float o[CPT];
-#pragma unroll
-        for (int u = 0; u < CPT; u++) o[u] = 0.0f;
-        for (int s = 0; s < tk.n_splits; s++) {
+        for (int s = lane; s < ns; s += 32) {
             const float ms = __ldcg(pml + (size_t)s * 2 * kHeads + h);
-            const float ls = __ldcg(pml + (size_t)s * 2 * kHeads + kHeads + h);
             const float w = ms == -CUDART_INF_F ? 0.0f : expf(ms - M);
-            L = fmaf(ls, w, L);
-#pragma unroll
-            for (int u = 0; u < CPT; u++)
-                o[u] = fmaf(__ldcg(pall + ((size_t)s * kHeads + h) * HD + threadIdx.x + kDecodeThreads * u), w, o[u]);
+            wsm[s * kHeads + h] = w;
+            L = fmaf(__ldcg(pml + (size_t)s * 2 * kHeads + kHeads + h), w, L);
         }
-        if (threadIdx.x == 0 && !(L > 0.0f)) atomicOr(p.err_flag, 1);
-#pragma unroll
-        for (int u = 0; u < CPT; u++) tk.out[(size_t)h * HD + threadIdx.x + kDecodeThreads * u] = o[u] / L;
+        L = warp_sum(L);
+        if (lane == 0) {
+            wsm[ns * kHeads + h] = 1.0f / L;
+            if (!(L > 0.0f)) atomicOr(p.err_flag, 1);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kHeads * HD; e += kDecodeThreads) {
+        const int h = e / HD;
+        float o = 0.0f;
+#pragma unroll 4
+        for (int s = 0; s < ns; s++) o = fmaf(__ldcg(pall + (size_t)s * kHeads * HD + e), wsm[s * kHeads + h], o);
+        tk.out[e] = o * wsm[ns * kHeads + h];
     }
     if (threadIdx.x == 0) p.tickets[it.task] = 0u;  // ready for the next call
 }

@@ -108,6 +108,7 @@ struct g4a_ctx {
     size_t meta_cap = 0;
     std::vector<uint8_t> h_meta;
     PrefillScratch *prefill = nullptr;
+    int n_sm = 148;
 };
 
 namespace {
@@ -214,6 +215,8 @@ extern "C" int g4a_ctx_create(int device, const g4a_hparams *hp, const float *ro
         return G4A_CUDA;
     }
     ctx->prefill = prefill_scratch_new();
+    cudaDeviceGetAttribute(&ctx->n_sm, cudaDevAttrMultiProcessorCount, device);
+    if (ctx->n_sm <= 0) ctx->n_sm = 148;
     int rc = ensure_rope(ctx, max_positions);
     if (rc == G4A_OK) {
         e = cudaMalloc(&ctx->d_err, sizeof(int));
@@ -284,6 +287,7 @@ struct g4a_kv {
     std::vector<int64_t> len;        // [n_seqs][n_layers] rows stored
     std::vector<int32_t> seq_pages;  // logical pages assigned per sequence
     std::vector<int32_t> free_pages;
+    uint8_t *d_tmaps = nullptr;  // f16 caches: [n_layers][K, V] 128-byte TMA descriptors
 };
 
 namespace {
@@ -371,6 +375,30 @@ extern "C" int g4a_kv_create(g4a_ctx *ctx, int32_t n_seqs, int32_t max_tokens, i
             g4a_kv_destroy(kv);
             return fail(ctx, G4A_CUDA, "compute: out of device memory for the KV cache");
         }
+        // rows never written stay finite (zero), so masked rows cannot turn into NaN
+        cudaMemset(L.k, 0, bytes);
+        cudaMemset(L.v, 0, bytes);
+    }
+    if (dtype == G4A_KV_F16) {
+        // TMA descriptors of each held layer's pools: [n_pages * page_tokens][hd] f16,
+        // boxes of 64 columns x one decode stage of rows.
+        std::vector<uint8_t> maps((size_t)hp.n_layers * 2 * 128, 0);
+        bool ok = page_tokens % 64 == 0;
+        for (int32_t l = 0; l < hp.n_layers && ok; l++) {
+            const auto &L = kv->layers[l];
+            if (!L.held) continue;
+            if (L.hd != 256 && L.hd != 512) continue;
+            const uint64_t rows = (uint64_t)kv->n_pages * page_tokens;
+            const uint32_t box = (uint32_t)f16_stage_rows(L.hd);
+            ok = encode_tmap_2d(maps.data() + (size_t)l * 256, 1, L.k, L.hd, rows, box) &&
+                 encode_tmap_2d(maps.data() + (size_t)l * 256 + 128, 1, L.v, L.hd, rows, box);
+        }
+        if (ok && cudaMalloc(&kv->d_tmaps, maps.size()) == cudaSuccess &&
+            cudaMemcpy(kv->d_tmaps, maps.data(), maps.size(), cudaMemcpyHostToDevice) == cudaSuccess) {
+        } else if (page_tokens % 64 == 0) {
+            g4a_kv_destroy(kv);
+            return fail(ctx, G4A_CUDA, "compute: TMA descriptors for the KV cache could not be created");
+        }
     }
     kv->h_bt.assign((size_t)n_seqs * kv->max_pages, -1);
     kv->len.assign((size_t)n_seqs * hp.n_layers, 0);
@@ -394,6 +422,7 @@ extern "C" void g4a_kv_destroy(g4a_kv *kv) {
         cudaFree(L.v);
     }
     cudaFree(kv->d_bt);
+    cudaFree(kv->d_tmaps);
     delete kv;
 }
 
@@ -511,6 +540,7 @@ struct Plan {
     std::vector<DecodeTask> tasks;
     std::vector<DecodeItem> items[2];  // by head width: [0] 256, [1] 512
     int32_t slots = 0;
+    bool f16_fast = false;             // f16 paged cache: the TMA / tensor-core kernel
 };
 
 // Rows per work item. Aims at about two items per SM over the whole call,
@@ -550,6 +580,7 @@ struct Staged {
     int32_t n_items[2] = {0, 0};
     size_t items_offset = 0;
     int kv_f16 = 0;
+    bool f16_fast = false;
 };
 
 // Copies a plan's metadata to the device. With own_buffers the buffers are
@@ -604,6 +635,7 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
     st->n_items[1] = (int32_t)plan.items[1].size();
     st->items_offset = bytes_tasks;
     st->kv_f16 = kv_f16;
+    st->f16_fast = plan.f16_fast;
     return G4A_OK;
 }
 
@@ -613,10 +645,31 @@ int launch_staged(g4a_ctx *ctx, const Staged &st) {
     for (int which = 0; which < 2; which++) {
         p.items = items;
         p.n_items = st.n_items[which];
-        G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream));
+        if (st.f16_fast)
+            G4A_CUDA_TRY(ctx, launch_decode_f16(p, which ? 512 : 256, ctx->n_sm, ctx->stream));
+        else
+            G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream));
         items += st.n_items[which];
     }
     return G4A_OK;
+}
+
+// Splits for the f16 kernel: boundaries at absolute multiples of rows_per (a
+// multiple of 64, so items start on stage boundaries), at most
+// kF16MaxSplits items per task.
+void add_items_aligned(Plan &plan, DecodeTask &t, int32_t task_index, int32_t rows_per, int which) {
+    const int32_t n_rows = t.hi - t.lo;
+    int64_t rp = std::max<int64_t>(rows_per, 64);
+    rp = std::max<int64_t>(rp, (n_rows + kF16MaxSplits - 2) / (kF16MaxSplits - 1));  // +1 for the unaligned start
+    rp = (rp + 63) / 64 * 64;
+    std::vector<int32_t> cuts{t.lo};
+    for (int64_t b = ((int64_t)t.lo / rp + 1) * rp; b < t.hi; b += rp) cuts.push_back((int32_t)b);
+    cuts.push_back(t.hi);
+    const int32_t n = (int32_t)cuts.size() - 1;
+    t.n_splits = n;
+    t.partial_base = n > 1 ? plan.slots : 0;
+    if (n > 1) plan.slots += n;
+    for (int32_t s = 0; s < n; s++) plan.items[which].push_back(DecodeItem{task_index, s, cuts[s], cuts[s + 1]});
 }
 
 int run_plan(g4a_ctx *ctx, Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens, int kv_f16) {
@@ -739,6 +792,7 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
             else g4a_windowed_len((int64_t)positions[j] + 1, hp.sliding_window, &lo, &hi);
             weighted += (hi - lo) * (hd[i] / 256);
         }
+    plan.f16_fast = kv->dtype == G4A_KV_F16 && kv->d_tmaps != nullptr;
     for (int32_t i = 0; i < n_layers; i++) {
         const g4a_decode_layer &a = layers[i];
         const auto &L = kv->layers[src[i]];
@@ -767,10 +821,21 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
             t.global = global[i];
             t.q_ready = 0;
             t.scale = 1.0f;
-            add_items(plan, t, (int32_t)plan.tasks.size(), rows_per, which);
+            if (plan.f16_fast) {
+                t.tmap_k = kv->d_tmaps + (size_t)src[i] * 256;
+                t.tmap_v = kv->d_tmaps + (size_t)src[i] * 256 + 128;
+                add_items_aligned(plan, t, (int32_t)plan.tasks.size(), rows_per, which);
+            } else {
+                add_items(plan, t, (int32_t)plan.tasks.size(), rows_per, which);
+            }
             plan.tasks.push_back(t);
         }
     }
+    if (plan.f16_fast)  // longest first: the persistent CTAs take items round-robin
+        for (auto &v : plan.items)
+            std::stable_sort(v.begin(), v.end(), [](const DecodeItem &x, const DecodeItem &y) {
+                return x.row_hi - x.row_lo > y.row_hi - y.row_lo;
+            });
     for (int32_t i = 0; i < n_layers; i++)
         if (owner[i])
             for (int32_t j = 0; j < n_seqs; j++) kv_len(kv, seq_ids[j], layers[i].layer) += 1;

@@ -34,6 +34,8 @@ struct DecodeTask {
     int32_t q_ready;      // 1 = q is already normalised and rotated
     float scale;          // score scale (1.0 in the model, model.rs:409)
     int32_t pad;
+    const void *tmap_k;   // f16 paged caches: TMA descriptors of the layer's pools
+    const void *tmap_v;
 };
 
 // One CTA's share of a task: cache rows [row_lo, row_hi).
@@ -77,12 +79,20 @@ struct ViewParams {
 
 // Launchers (decode.cu).
 cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, cudaStream_t s);
+// f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
+constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
+cudaError_t launch_decode_f16(const DecodeParams &p, int hd, int n_sm, cudaStream_t s);
+inline int f16_stage_rows(int hd) { return 16384 / hd; }
 cudaError_t launch_attend_generic(const float *q, const float *k, const float *v, int64_t len, int n_heads,
                                   int n_kv, int hd, float scale, float *out, int *err_flag, cudaStream_t s);
 cudaError_t launch_append(const AppendParams &p, int kv_f16, cudaStream_t s);
 cudaError_t launch_view(const ViewParams &p, int kv_f16, cudaStream_t s);
 cudaError_t launch_lse_merge(int n_parts, const float *const *parts_o, const float *const *parts_lse,
                              int64_t rows, int n_heads, int hd, float *out, float *lse, cudaStream_t s);
+
+// 2D TMA descriptor (128 B) over a row-major [rows][cols] 16-bit tensor with
+// 64 x box_rows boxes and the 128-byte swizzle. dtype: 0 bf16, 1 f16.
+bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows);
 
 // Prefill (prefill_sm100.cu): per-context scratch and the launcher behind
 // g4a_prefill. Returns a g4a_status and points *msg at a description.

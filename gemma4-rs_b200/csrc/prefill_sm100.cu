@@ -392,13 +392,19 @@ __global__ void bf16_to_f16_kernel(const __nv_bfloat16 *__restrict__ src, __half
     for (; i < n; i += stride) dst[i] = __float2half_rn(__bfloat162float(src[i]));
 }
 
+bool encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows) {
+    return encode_tmap_2d(map, dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT16 ? 1 : 0, base, cols, rows, 128);
+}
+
+}  // namespace
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                     const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 // The driver's tensor-map encoder, looked up at run time so that the library
 // loads (for symbol checks) on machines without a driver.
-EncodeTiledFn encode_fn() {
+static EncodeTiledFn encode_fn() {
     static EncodeTiledFn fn = nullptr;
     if (!fn) {
         void *p = nullptr;
@@ -410,20 +416,19 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-bool encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows) {
+bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
+    const CUtensorMapDataType dt = dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
-                                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(reinterpret_cast<CUtensorMap *>(map), dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
-
-}  // namespace
 
 // Host-side state the prefill keeps in the context between calls.
 struct PrefillScratch {
