@@ -197,6 +197,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     for (int b0 = it.row_lo; b0 < it.row_hi; b0 += BLK) {
         const int nb = min(BLK, it.row_hi - b0);
         // ---- scores: warp w takes rows w, w+8, ... of the block ----
+#pragma unroll 2
         for (int r = warp; r < nb; r += kHeads) {
             const int row = b0 + r;
             float part[kHeads];
@@ -257,6 +258,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
 #pragma unroll
             for (int u = 0; u < CPT; u++) acc[h][u] *= a;
         }
+#pragma unroll 8
         for (int r = 0; r < nb; r++) {
             const int row = b0 + r;
             float v[CPT];

@@ -2,24 +2,31 @@
 //
 // Replaces, for batched decoding, crates/llm-gemma4/src/impl_/model.rs:393-410
 // (q/k norms, RoPE, append, view, window, attend) and :326-366 (attend_head).
-// Fused per (sequence, layer) task: q RMSNorm + RoPE, the appended token's
-// k/v norm + RoPE + store, attention over the window of the paged cache, and
-// for split tasks a log-sum-exp merge by the last CTA to finish.
+// Sliding (256-wide) and global (512-wide) layers run in the same launches.
 //
-// Structure (one persistent CTA per SM, items taken round-robin):
-//   warp 4      producer: for every 64 KB stage (S rows of K and of V, S =
-//               16384 / head width, page-aligned so a stage never crosses a
-//               page) it issues head_width/64 TMA box loads per tensor into a
-//               3-slot ring (64 x S boxes, 128-byte swizzle, no multicast).
-//   warps 0-3   q prep (2 heads per warp), the new row, then per stage:
-//               S = Q K^T on tensor cores (mma.sync m16n8k16, f16 inputs, f32
-//               accumulate): the 16 MMA rows are the 8 heads' q split into a
-//               high and a low f16 half, so the two partial scores add up to
-//               the f32 score to about 2^-22 relative; keys are split across
-//               the 4 warps. The stage's softmax statistics are computed by
-//               every warp (same inputs, same result), P is split hi/lo the
-//               same way, and O^T += V^T P^T runs with the head dimension split
-//               across the warps (O stays in 32 registers per thread).
+// Three kernels per step:
+//   prep     one CTA per (sequence, layer) task: q RMSNorm + RoPE, split into
+//            a high and a low f16 half and stored in the layout the main
+//            kernel's shared memory uses; on KV-owning layers the new token's
+//            k (norm + RoPE) and v (norm) are stored into the paged cache.
+//   main     one persistent CTA per SM, items (row ranges of tasks) assigned
+//            by the host longest-processing-time first.
+//            warp 8    producer: per item one bulk copy of the task's q block,
+//                      then every 64 KB stage (S rows of K and of V, S = 16384
+//                      / head width, page-aligned) as head_width/64 TMA box
+//                      loads per tensor (64 columns x S rows, 128-byte
+//                      swizzle, no multicast) into a 3-slot ring.
+//            warps 0-7 S = Q K^T with mma.sync m16n8k16 (f16 in, f32
+//                      accumulate); the 16 MMA rows are the hi and lo halves
+//                      of the 8 heads' q, so the two partial scores add up to
+//                      the f32 score to about 2^-22 relative. Warp w takes key
+//                      half w/4 and head-dimension quarter w%4 (MMA chains 4
+//                      deep); quarter sums meet in shared memory; every warp
+//                      computes the stage's softmax statistics (same inputs,
+//                      same result), splits P hi/lo the same way and
+//                      accumulates O^T += V^T P^T for its eighth of the head
+//                      dimension. Items of split tasks store (O, max, sum).
+//   combine  one CTA per split task: log-sum-exp merge of its items.
 // Accuracy: within 1e-4 of the reference's f32 attention on the same f16 rows.
 // All mbarrier waits are bounded; a time-out sets bit 2 of the error flag and
 // the CTA leaves its loops at the next common barrier.
@@ -33,31 +40,43 @@
 namespace g4a {
 namespace {
 
-constexpr int kWarpsC = 4;                 // compute warps
+constexpr int kWarpsC = 8;                      // compute warps
 constexpr int kThreadsF16 = 32 * (kWarpsC + 1);
 constexpr int kSlots = 3;
-constexpr int kStageBytes = 65536;         // K + V of one stage
+constexpr int kStageBytes = 65536;              // K + V of one stage
+// q hi/lo block at [0, 16 KB), two score-partial buffers at [16 KB, 32 KB):
+// the same places for both head widths, so the producer's copy of the next
+// item's q never lands on partials the compute warps are still reading.
+constexpr int kQRegion = 16384;
+constexpr int kRegionBytes = 32768;
 constexpr uint32_t kPollLimit = 1u << 22;
 
 template <int HD>
 struct F16Cfg {
-    static constexpr int S = 16384 / HD;          // rows per stage: 64 (hd 256) or 32 (hd 512)
-    static constexpr int kBoxBytes = S * 128;     // one 64-column box of S rows
+    static constexpr int S = 16384 / HD;        // rows per stage: 64 (hd 256) or 32 (hd 512)
+    static constexpr int kBoxBytes = S * 128;   // one 64-column box of S rows
     static constexpr int kBoxes = HD / 64;
-    static constexpr int kKeysPerWarp = S / kWarpsC;   // 16 or 8
-    static constexpr int kNT = kKeysPerWarp / 8;       // QK n-tiles per warp
-    static constexpr int kKS = HD / 16;                // k-steps over the head width
-    static constexpr int kMT = HD / 16 / kWarpsC;      // PV m-tiles per warp
-    static constexpr int kPVK = S / 16;                // PV k-steps per stage
-    static constexpr int kSmemQ = 16 * HD * 2;         // hi/lo q, f16
+    static constexpr int kKeysQ = S / 4;        // keys per QK warp (a key quarter)
+    static constexpr int kNT = kKeysQ / 8;      // QK n-tiles per warp: 2 or 1
+    static constexpr int kKSH = HD / 32;        // k-steps per head-dimension half: 8 or 16
+    static constexpr int kNCH = 4 / kNT;        // accumulator chains per n-tile (4 chains of 4)
+    static constexpr int kMT = HD / 128;        // PV m-tiles per warp (an eighth of hd): 2 or 4
+    static constexpr int kPVK = S / 16;         // PV k-steps per stage
+    static constexpr int kQBytes = 16 * HD * 2; // hi/lo q, f16
+    // [half][head][key ^ 4*head] f32, one buffer: the XOR keeps the
+    // partial-score accesses at most 2-way bank-conflicted
+    static constexpr int kSPartBytes = 2 * 8 * S * 4;
     static_assert(2 * kBoxes * kBoxBytes == kStageBytes, "a stage is 32 KB of K and 32 KB of V");
-    static_assert(S <= 64, "score buffer holds 64 keys per head");
-    static constexpr int kSmemBytes = kSlots * kStageBytes + kSmemQ + 2 * 8 * 64 * 4 + 2 * HD * 2 + 1024 + 1024;
+    static_assert(kQBytes <= kQRegion && kQRegion + 2 * kSPartBytes <= kRegionBytes, "region layout");
+    static_assert(kKSH % kNCH == 0, "chains divide the k-steps");
 };
+
+constexpr int kSmemBytes = kSlots * kStageBytes + kRegionBytes + 128 + 1024;
 
 struct F16Bars {
     uint64_t full[kSlots];
     uint64_t empty[kSlots];
+    uint64_t q_full, q_empty;
     int abort;
 };
 
@@ -65,9 +84,6 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -84,7 +100,15 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 __device__ __forceinline__ uint32_t pack2(__half lo, __half hi) {
     return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
-__device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier of the 8 compute warps (the producer never takes part)
+__device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     ptx::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(ptx::smem_u32(bar))
+                 : "memory");
+}
 
 // Byte offset of element (row, col) inside a stage tensor stored as HD/64
 // boxes of [S rows][128 B] with the 128-byte swizzle (16-byte chunk index
@@ -94,6 +118,13 @@ __device__ __forceinline__ uint32_t box_off(int row, int col) {
     using C = F16Cfg<HD>;
     const int box = col >> 6, chunk = (col >> 3) & 7;
     return box * C::kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4) + (col & 7) * 2;
+}
+
+// Byte offset of (row, col) in a [16][HD] f16 q block: 16-byte chunks of a
+// row XOR-ed with row % 8 (conflict-free ldmatrix).
+template <int HD>
+__device__ __forceinline__ uint32_t q_off(int row, int col) {
+    return row * HD * 2 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2;
 }
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -131,396 +162,455 @@ __device__ __forceinline__ void norm_rope(float (&x)[HD / 32], const float *w, c
     }
 }
 
+// norm_rope with the weight and the RoPE row fetched before the reduction,
+// so the three global reads overlap.
 template <int HD>
-__global__ void __launch_bounds__(kThreadsF16, 1) decode_f16_kernel(DecodeParams p) {
+__device__ __forceinline__ void norm_rope_pre(float (&x)[HD / 32], const float *w, const float2 *rope_row, float eps,
+                                              int lane) {
+    constexpr int PL = HD / 32;
+    float wv[PL];
+    float2 sc[PL / 2];
+#pragma unroll
+    for (int k = 0; k < PL; k++) wv[k] = w ? __ldg(w + lane + 32 * k) : 1.0f;
+#pragma unroll
+    for (int k = 0; k < PL / 2; k++) sc[k] = rope_row ? __ldg(rope_row + lane + 32 * k) : make_float2(0.f, 1.f);
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < PL; k++) ss += (double)__fmul_rn(x[k], x[k]);
+    ss = warp_sum_d(ss);
+    const float mean = (float)(ss / (double)HD);
+    const float scale = 1.0f / sqrtf(mean + eps);
+#pragma unroll
+    for (int k = 0; k < PL; k++) {
+        float y = __fmul_rn(x[k], scale);
+        if (w) y = __fmul_rn(y, wv[k]);
+        x[k] = y;
+    }
+    if (rope_row) {
+#pragma unroll
+        for (int k = 0; k < PL / 2; k++) {
+            const float a = x[k], b = x[k + PL / 2];
+            x[k] = __fsub_rn(__fmul_rn(a, sc[k].y), __fmul_rn(b, sc[k].x));
+            x[k + PL / 2] = __fadd_rn(__fmul_rn(a, sc[k].x), __fmul_rn(b, sc[k].y));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// prep: q hi/lo blocks and the appended rows
+// ---------------------------------------------------------------------------
+
+template <int HD>
+__device__ __forceinline__ void prep_task(const DecodeParams &p, const DecodeTask &tk, int task) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float2 *rope = (tk.global ? p.rope_global : p.rope_local) + (size_t)tk.position * (HD / 2);
+    uint8_t *qblk = reinterpret_cast<uint8_t *>(p.q_blocks) + (size_t)task * kQBlockBytes;
+    {  // q of head `warp` (model.rs:395-396)
+        const int h = warp;
+        float x[HD / 32];
+#pragma unroll
+        for (int k = 0; k < HD / 32; k++) x[k] = __ldg(tk.q_raw + (size_t)h * HD + lane + 32 * k);
+        if (!tk.q_ready) norm_rope_pre<HD>(x, tk.q_w, rope, p.eps, lane);
+#pragma unroll
+        for (int k = 0; k < HD / 32; k++) {
+            const int col = lane + 32 * k;
+            const float v = x[k] * tk.scale;
+            const __half hi = __float2half_rn(v);
+            const __half lo = __float2half_rn(v - __half2float(hi));
+            *reinterpret_cast<__half *>(qblk + q_off<HD>(h, col)) = hi;
+            *reinterpret_cast<__half *>(qblk + q_off<HD>(h + 8, col)) = lo;
+        }
+    }
+    if (tk.new_row >= 0 && warp < 2) {  // the appended token (model.rs:400-405)
+        float x[HD / 32];
+        const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
+#pragma unroll
+        for (int k = 0; k < HD / 32; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (warp == 0)
+            norm_rope_pre<HD>(x, tk.k_w, rope, p.eps, lane);
+        else
+            norm_rope_pre<HD>(x, nullptr, nullptr, p.eps, lane);
+        const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
+        const int page = bt[tk.new_row / p.page_tokens];
+        __half *dst = const_cast<__half *>(reinterpret_cast<const __half *>(warp == 0 ? tk.k_base : tk.v_base)) +
+                      ((size_t)page * p.page_tokens + (tk.new_row % p.page_tokens)) * HD;
+#pragma unroll
+        for (int k = 0; k < HD / 32; k++) dst[lane + 32 * k] = __float2half_rn(x[k]);
+    }
+}
+
+__global__ void __launch_bounds__(256) decode_f16_prep(DecodeParams p) {
+    const DecodeTask &tk = p.tasks[blockIdx.x];
+    if (tk.hd == 256) prep_task<256>(p, tk, blockIdx.x);
+    else prep_task<512>(p, tk, blockIdx.x);
+}
+
+// ---------------------------------------------------------------------------
+// main
+// ---------------------------------------------------------------------------
+
+struct Shared {
+    uint8_t *stages;
+    uint8_t *region;   // q hi/lo block, then two score-partial buffers
+    F16Bars *bars;
+};
+
+__device__ __forceinline__ bool wait_poll(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
+    for (uint32_t i = 0; i < kPollLimit; i++) {
+        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023) == 1023 && *abort) return false;
+    }
+    if (!*abort) atomicOr(err, 4);
+    *abort = 1;
+    return false;
+}
+
+// Producer side of one item: its q block, then its stages.
+template <int HD>
+__device__ __forceinline__ bool produce_item(const DecodeParams &p, const DecodeItem &it, const DecodeTask &tk,
+                                             const Shared &sh, uint32_t &st, uint32_t ic) {
+    using C = F16Cfg<HD>;
+    volatile int *abort = &sh.bars->abort;
+    if (!wait_poll(&sh.bars->q_empty, (ic & 1u) ^ 1u, abort, p.err_flag)) return false;
+    ptx::mbar_arrive_expect_tx(&sh.bars->q_full, C::kQBytes);
+    bulk_load(sh.region, reinterpret_cast<const uint8_t *>(p.q_blocks) + (size_t)it.task * kQBlockBytes, C::kQBytes,
+              &sh.bars->q_full);
+    const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
+    for (int r0 = it.row_lo / C::S * C::S; r0 < it.row_hi; r0 += C::S, st++) {
+        const int slot = st % kSlots;
+        if (!wait_poll(&sh.bars->empty[slot], ((st / kSlots) & 1u) ^ 1u, abort, p.err_flag)) return false;
+        const int page = __ldg(bt + r0 / p.page_tokens);
+        const int y = page * p.page_tokens + (r0 % p.page_tokens);
+        uint8_t *dst = sh.stages + slot * kStageBytes;
+        ptx::mbar_arrive_expect_tx(&sh.bars->full[slot], kStageBytes);
+#pragma unroll
+        for (int c = 0; c < C::kBoxes; c++) {
+            ptx::tma_load_2d(dst + c * C::kBoxBytes, tk.tmap_k, &sh.bars->full[slot], 64 * c, y);
+            ptx::tma_load_2d(dst + kStageBytes / 2 + c * C::kBoxBytes, tk.tmap_v, &sh.bars->full[slot], 64 * c, y);
+        }
+    }
+    return true;
+}
+
+// Compute side of one item. Returns false if the CTA aborted.
+template <int HD>
+__device__ __forceinline__ bool compute_item(const DecodeParams &p, const DecodeItem &it, const DecodeTask &tk,
+                                             const Shared &sh, uint32_t &st, uint32_t ic) {
     using C = F16Cfg<HD>;
     constexpr int S = C::S;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *stages = smem;                                 // kSlots x 64 KB
-    uint8_t *q_smem = stages + kSlots * kStageBytes;        // [16][HD] f16, swizzled
-    float *s_smem = reinterpret_cast<float *>(q_smem + C::kSmemQ);  // [2][8][S]
-    __half *new_kv = reinterpret_cast<__half *>(s_smem + 2 * 8 * 64);  // k then v, [HD] each
-    F16Bars *bars = reinterpret_cast<F16Bars *>(new_kv + 2 * HD);
-    __shared__ int last_s;
-
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
+    const int kq = warp >> 1, dh = warp & 1;  // QK: key quarter, head-dimension half
+    volatile int *abort = &sh.bars->abort;
+    float *s_part = reinterpret_cast<float *>(sh.region + kQRegion);
 
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kSlots; i++) {
-            ptx::mbar_init(&bars->full[i], 1);
-            ptx::mbar_init(&bars->empty[i], kWarpsC);
-        }
-        bars->abort = 0;
-        ptx::fence_mbar_init();
+    // -- A fragments of this warp's half of q, then hand the q buffer back
+    const bool qok = wait_poll(&sh.bars->q_full, ic & 1u, abort, p.err_flag);
+    const uint32_t q_base = ptx::smem_u32(sh.region);
+    uint32_t qa[C::kKSH][4];
+#pragma unroll
+    for (int i = 0; i < C::kKSH; i++) {
+        const int ks = dh * C::kKSH + i;
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = ks * 16 + (lane >> 4) * 8;
+        ldsm_x4(q_base + q_off<HD>(row, col), qa[i][0], qa[i][1], qa[i][2], qa[i][3]);
     }
-    __syncthreads();
-    volatile int *abort = &bars->abort;
-
-    if (warp == kWarpsC) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            uint32_t st = 0;  // global stage counter across items
-            for (int item = blockIdx.x; item < p.n_items && !*abort; item += gridDim.x) {
-                const DecodeItem it = p.items[item];
-                const DecodeTask &tk = p.tasks[it.task];
-                const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
-                const int first = it.row_lo / S * S;
-                for (int r0 = first; r0 < it.row_hi; r0 += S, st++) {
-                    const int slot = st % kSlots;
-                    const uint32_t ph = (st / kSlots) & 1u;
-                    bool got = false;
-                    for (uint32_t i = 0; i < kPollLimit; i++) {
-                        if (ptx::mbar_try_wait(&bars->empty[slot], ph ^ 1u)) {
-                            got = true;
-                            break;
-                        }
-                        if ((i & 1023) == 1023 && *abort) break;
-                    }
-                    if (!got) {
-                        if (!*abort) atomicOr(p.err_flag, 4);
-                        *abort = 1;
-                        break;
-                    }
-                    const int page = __ldg(bt + r0 / p.page_tokens);
-                    const int y = page * p.page_tokens + (r0 % p.page_tokens);
-                    uint8_t *dst = stages + slot * kStageBytes;
-                    ptx::mbar_arrive_expect_tx(&bars->full[slot], kStageBytes);
-#pragma unroll
-                    for (int c = 0; c < C::kBoxes; c++) {
-                        ptx::tma_load_2d(dst + c * C::kBoxBytes, tk.tmap_k, &bars->full[slot], 64 * c, y);
-                        ptx::tma_load_2d(dst + kStageBytes / 2 + c * C::kBoxBytes, tk.tmap_v, &bars->full[slot],
-                                         64 * c, y);
-                    }
-                }
-            }
-            // every issued load lands before the CTA may exit
-            for (uint32_t s2 = (st > kSlots ? st - kSlots : 0); s2 < st; s2++) {
-                for (uint32_t i = 0; i < kPollLimit && !ptx::mbar_try_wait(&bars->full[s2 % kSlots], (s2 / kSlots) & 1u);
-                     i++) {
-                }
-            }
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------------- compute
-    const uint32_t q_base = ptx::smem_u32(q_smem);
-    const uint32_t st_base = ptx::smem_u32(stages);
-    uint32_t st = 0;
-    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
-        const DecodeItem it = p.items[item];
-        const DecodeTask &tk = p.tasks[it.task];
-        const float2 *rope = tk.global ? p.rope_global : p.rope_local;
-        // -- q: norm + RoPE (model.rs:395-396), hi/lo f16 split into smem
-        for (int hh = 0; hh < 2; hh++) {
-            const int h = warp * 2 + hh;
-            float x[HD / 32];
-#pragma unroll
-            for (int k = 0; k < HD / 32; k++) x[k] = __ldg(tk.q_raw + (size_t)h * HD + lane + 32 * k);
-            if (!tk.q_ready) norm_rope<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
-#pragma unroll
-            for (int k = 0; k < HD / 32; k++) {
-                const int col = lane + 32 * k;
-                const float v = x[k] * tk.scale;
-                const __half hi = __float2half_rn(v);
-                const __half lo = __float2half_rn(v - __half2float(hi));
-                const int chunk = col >> 3;
-                *reinterpret_cast<__half *>(q_smem + h * HD * 2 + (((chunk ^ (h & 7)) << 4) | ((col & 7) * 2))) = hi;
-                const int r2 = h + 8;
-                *reinterpret_cast<__half *>(q_smem + r2 * HD * 2 + (((chunk ^ (r2 & 7)) << 4) | ((col & 7) * 2))) = lo;
-            }
-        }
-        // -- the appended token (model.rs:400-405), by the item holding its row
-        const bool has_new = tk.new_row >= 0 && ((tk.new_row >= it.row_lo && tk.new_row < it.row_hi) ||
-                                                 (it.split == tk.n_splits - 1 && tk.new_row >= it.row_hi));
-        if (has_new && warp < 2) {
-            float x[HD / 32];
-            const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
-#pragma unroll
-            for (int k = 0; k < HD / 32; k++) x[k] = __ldg(src + lane + 32 * k);
-            if (warp == 0)
-                norm_rope<HD>(x, tk.k_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
-            else
-                norm_rope<HD>(x, nullptr, nullptr, p.eps, lane);
-            const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
-            const int page = bt[tk.new_row / p.page_tokens];
-            __half *dst = const_cast<__half *>(reinterpret_cast<const __half *>(warp == 0 ? tk.k_base : tk.v_base)) +
-                          ((size_t)page * p.page_tokens + (tk.new_row % p.page_tokens)) * HD;
-#pragma unroll
-            for (int k = 0; k < HD / 32; k++) {
-                const __half h16 = __float2half_rn(x[k]);
-                dst[lane + 32 * k] = h16;
-                new_kv[warp * HD + lane + 32 * k] = h16;
-            }
-        }
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&sh.bars->q_empty);
+    if (!qok) {
         compute_bar();
-        // -- A fragments of Q (hi rows 0-7, lo rows 8-15) for every k-step
-        uint32_t qa[C::kKS][4];
+        return false;
+    }
+    float m_run = -CUDART_INF_F, l_run = 0.0f;  // head g, identical in every warp
+    float acc[C::kMT][4];
 #pragma unroll
-        for (int ks = 0; ks < C::kKS; ks++) {
-            const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-            const int chunk = ks * 2 + (lane >> 4);
-            ldsm_x4(q_base + row * HD * 2 + ((chunk ^ (row & 7)) << 4), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
-        }
-        // per-head running stats for head g (identical in every warp)
-        float m_run = -CUDART_INF_F, l_run = 0.0f;
-        float acc[C::kMT][4];
+    for (int mt = 0; mt < C::kMT; mt++)
 #pragma unroll
-        for (int mt = 0; mt < C::kMT; mt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[mt][i] = 0.0f;
-        bool bad = false;
-        const int first = it.row_lo / S * S;
-        bool aborted = false;
-        for (int r0 = first; r0 < it.row_hi; r0 += S, st++) {
-            const int slot = st % kSlots;
-            const uint32_t ph = (st / kSlots) & 1u;
-            bool got = false;
-            for (uint32_t i = 0; i < kPollLimit; i++) {
-                if (ptx::mbar_try_wait(&bars->full[slot], ph)) {
-                    got = true;
-                    break;
-                }
-                if ((i & 1023) == 1023 && *abort) break;
-            }
-            if (!got && !*abort) {
-                atomicOr(p.err_flag, 4);
-                *abort = 1;
-            }
-            const uint32_t kb = st_base + slot * kStageBytes;
-            const uint32_t vb = kb + kStageBytes / 2;
-            uint8_t *vgen = stages + slot * kStageBytes + kStageBytes / 2;
-            uint8_t *kgen = stages + slot * kStageBytes;
-            // rows of this stage outside [row_lo, row_hi) are masked; their V
-            // rows are zeroed (a masked weight is 0, and 0 * garbage could be
-            // NaN); the appended row is patched in from the computed values.
-            const bool partial = r0 < it.row_lo || r0 + S > it.row_hi;
-            const bool patch = tk.new_row >= r0 && tk.new_row < r0 + S && tk.new_row >= it.row_lo &&
-                               tk.new_row < it.row_hi;
-            if (got && (partial || patch)) {
+        for (int i = 0; i < 4; i++) acc[mt][i] = 0.0f;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const uint32_t st_base = ptx::smem_u32(sh.stages);
+
+    for (int r0 = it.row_lo / S * S; r0 < it.row_hi; r0 += S, st++) {
+        const int slot = st % kSlots;
+        const bool got = wait_poll(&sh.bars->full[slot], (st / kSlots) & 1u, abort, p.err_flag);
+        const uint32_t kb = st_base + slot * kStageBytes;
+        const uint32_t vb = kb + kStageBytes / 2;
+        // Rows outside [row_lo, row_hi) are masked and their V rows zeroed (a
+        // zero weight times stale data could be NaN). Same decision in every warp.
+        const bool partial = r0 < it.row_lo || r0 + S > it.row_hi;
+        if (partial) {
+            if (got) {
+                uint8_t *vgen = sh.stages + slot * kStageBytes + kStageBytes / 2;
                 for (int e = threadIdx.x; e < S * (HD / 8); e += 32 * kWarpsC) {
                     const int row = e / (HD / 8), c8 = (e % (HD / 8)) * 8;
                     const int r = r0 + row;
-                    if (r < it.row_lo || r >= it.row_hi) {
+                    if (r < it.row_lo || r >= it.row_hi)
                         *reinterpret_cast<uint4 *>(vgen + box_off<HD>(row, c8)) = make_uint4(0, 0, 0, 0);
-                    } else if (r == tk.new_row) {
-                        *reinterpret_cast<uint4 *>(kgen + box_off<HD>(row, c8)) =
-                            *reinterpret_cast<const uint4 *>(new_kv + c8);
-                        *reinterpret_cast<uint4 *>(vgen + box_off<HD>(row, c8)) =
-                            *reinterpret_cast<const uint4 *>(new_kv + HD + c8);
-                    }
                 }
-                // these generic-proxy writes must be ordered before the TMA
-                // that later refills this slot
+                // generic-proxy writes, ordered before the TMA that refills the slot
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             }
             compute_bar();
-            if (*abort) {
-                aborted = true;
-                break;
-            }
-            float *s_buf = s_smem + (st & 1) * 8 * 64;
-            // -- S = Q K^T for this warp's keys
-            {
-                float sc[C::kNT][4];
-#pragma unroll
-                for (int n = 0; n < C::kNT; n++)
-#pragma unroll
-                    for (int i = 0; i < 4; i++) sc[n][i] = 0.0f;
-                const int key0 = warp * C::kKeysPerWarp;
-#pragma unroll
-                for (int ks = 0; ks < C::kKS; ks++) {
-                    if constexpr (C::kNT == 2) {
-                        // matrices: keys key0..+7 at d 16ks, +8; keys key0+8..+15 at d 16ks, +8
-                        const int row = key0 + (lane & 7) + ((lane >> 4) << 3);
-                        const int col = ks * 16 + ((lane >> 3) & 1) * 8;
-                        uint32_t b0, b1, b2, b3;
-                        ldsm_x4(kb + box_off<HD>(row, col), b0, b1, b2, b3);
-                        mma16816(sc[0], qa[ks], b0, b1);
-                        mma16816(sc[1], qa[ks], b2, b3);
-                    } else {
-                        const int row = key0 + (lane & 7);
-                        const int col = ks * 16 + ((lane >> 3) & 1) * 8;
-                        uint32_t b0, b1;
-                        ldsm_x2(kb + box_off<HD>(row, col), b0, b1);
-                        mma16816(sc[0], qa[ks], b0, b1);
-                    }
-                }
-#pragma unroll
-                for (int n = 0; n < C::kNT; n++) {
-#pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        const int key = key0 + n * 8 + 2 * t + j;
-                        const int r = r0 + key;
-                        float s = sc[n][j] + sc[n][j + 2];  // hi + lo rows
-                        if (r < it.row_lo || r >= it.row_hi) s = -CUDART_INF_F;
-                        else if (isnan(s) || s == CUDART_INF_F) bad = true;
-                        s_buf[g * 64 + key] = s;
-                    }
-                }
-            }
-            compute_bar();
-            // -- online softmax of head g over this stage (every warp alike)
-            float pv[C::kPVK][4];
-            float smax = -CUDART_INF_F;
-#pragma unroll
-            for (int kk = 0; kk < C::kPVK; kk++) {
-                pv[kk][0] = s_buf[g * 64 + kk * 16 + 2 * t];
-                pv[kk][1] = s_buf[g * 64 + kk * 16 + 2 * t + 1];
-                pv[kk][2] = s_buf[g * 64 + kk * 16 + 2 * t + 8];
-                pv[kk][3] = s_buf[g * 64 + kk * 16 + 2 * t + 9];
-#pragma unroll
-                for (int i = 0; i < 4; i++) smax = fmaxf(smax, pv[kk][i]);
-            }
-            smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 1));
-            smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 2));
-            const float m_new = fmaxf(m_run, smax);
-            const float alpha = m_new == -CUDART_INF_F ? 1.0f : expf(m_run - m_new);
-            float lsum = 0.0f;
-            uint32_t bhi[C::kPVK][2], blo[C::kPVK][2];
-#pragma unroll
-            for (int kk = 0; kk < C::kPVK; kk++) {
-                __half hi[4], lo[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float e = m_new == -CUDART_INF_F ? 0.0f : expf(pv[kk][i] - m_new);
-                    lsum += e;
-                    hi[i] = __float2half_rn(e);
-                    lo[i] = __float2half_rn(e - __half2float(hi[i]));
-                }
-                bhi[kk][0] = pack2(hi[0], hi[1]);
-                bhi[kk][1] = pack2(hi[2], hi[3]);
-                blo[kk][0] = pack2(lo[0], lo[1]);
-                blo[kk][1] = pack2(lo[2], lo[3]);
-            }
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-            l_run = l_run * alpha + lsum;
-            m_run = m_new;
-            // -- O^T += V^T P^T for this warp's head-dimension quarter
-            const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * t);      // head 2t
-            const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * t + 4);  // head 2t+1
-#pragma unroll
-            for (int mt = 0; mt < C::kMT; mt++) {
-                acc[mt][0] *= a0;
-                acc[mt][1] *= a1;
-                acc[mt][2] *= a0;
-                acc[mt][3] *= a1;
-            }
-#pragma unroll
-            for (int kk = 0; kk < C::kPVK; kk++) {
-#pragma unroll
-                for (int mt = 0; mt < C::kMT; mt++) {
-                    const int dm = (warp * C::kMT + mt) * 16;
-                    const int row = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
-                    const int col = dm + ((lane >> 3) & 1) * 8;
-                    uint32_t a[4];
-                    ldsm_x4_t(vb + box_off<HD>(row, col), a[0], a[1], a[2], a[3]);
-                    mma16816(acc[mt], a, bhi[kk][0], bhi[kk][1]);
-                    mma16816(acc[mt], a, blo[kk][0], blo[kk][1]);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&bars->empty[slot]);
         }
-        if (aborted) return;
-        if (bad) atomicOr(p.err_flag, 1);
-        // ---- output: O[h][d] for h = 2t, 2t+1 and d = dm + g (+8)
-        const float l0 = __shfl_sync(0xffffffffu, l_run, 8 * t), l1 = __shfl_sync(0xffffffffu, l_run, 8 * t + 4);
-        if (tk.n_splits == 1) {
-            const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+        float *sp = s_part + (st & 1) * (C::kSPartBytes / 4);
+        // -- partial S = Q K^T over this warp's half of the head width
+        {
+            float sc[C::kNT][C::kNCH][4];
+#pragma unroll
+            for (int n = 0; n < C::kNT; n++)
+#pragma unroll
+                for (int c = 0; c < C::kNCH; c++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) sc[n][c][i] = 0.0f;
+            const int key0 = kq * C::kKeysQ;
+            if constexpr (C::kNT == 2) {
+#pragma unroll
+                for (int i = 0; i < C::kKSH; i++) {
+                    // matrices: keys +0..7 at d 16ks, 16ks+8; keys +8..15 likewise
+                    const int ks = dh * C::kKSH + i;
+                    const int row = key0 + (lane & 7) + ((lane >> 4) << 3);
+                    const int col = ks * 16 + ((lane >> 3) & 1) * 8;
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(kb + box_off<HD>(row, col), b0, b1, b2, b3);
+                    mma16816(sc[0][i % C::kNCH], qa[i], b0, b1);
+                    mma16816(sc[1][i % C::kNCH], qa[i], b2, b3);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < C::kKSH; i += 2) {
+                    // matrices: keys +0..7 at d 16ks, +8, +16, +24 (two k-steps)
+                    const int ks = dh * C::kKSH + i;
+                    const int row = key0 + (lane & 7);
+                    const int col = ks * 16 + (lane >> 3) * 8;
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(kb + box_off<HD>(row, col), b0, b1, b2, b3);
+                    mma16816(sc[0][i % C::kNCH], qa[i], b0, b1);
+                    mma16816(sc[0][(i + 1) % C::kNCH], qa[i + 1], b2, b3);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < C::kNT; n++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < C::kNCH; c++) s += sc[n][c][j] + sc[n][c][j + 2];  // hi + lo rows
+                    sp[(dh * 8 + g) * S + ((key0 + n * 8 + 2 * t + j) ^ (4 * g))] = s * kLog2e;
+                }
+        }
+        compute_bar();
+        if (*abort) return false;
+        // -- online softmax of head g over this stage (every warp alike), in
+        // base-2 units: the scores carry a factor log2(e)
+        float pv[C::kPVK][4];
+        float smax = -CUDART_INF_F;
+#pragma unroll
+        for (int kk = 0; kk < C::kPVK; kk++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int key = kk * 16 + 2 * t + (i & 1) + (i >> 1) * 8;
+                const int kx = key ^ (4 * g);
+                float s = sp[g * S + kx] + sp[(8 + g) * S + kx];
+                if (partial && (r0 + key < it.row_lo || r0 + key >= it.row_hi)) s = -CUDART_INF_F;
+                pv[kk][i] = s;
+                smax = fmaxf(smax, s);
+            }
+        smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 1));
+        smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 2));
+        // A NaN or +inf score makes the sum NaN, which the output check reports.
+        const float m_new = fmaxf(m_run, smax);
+        const float alpha = m_new == -CUDART_INF_F ? 1.0f : ptx::ex2(m_run - m_new);
+        float lsum = 0.0f;
+        uint32_t bhi[C::kPVK][2], blo[C::kPVK][2];
+#pragma unroll
+        for (int kk = 0; kk < C::kPVK; kk++) {
+            __half hi[4], lo[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float e = ptx::ex2(pv[kk][i] - m_new);  // ex2(-inf) = 0
+                lsum += e;
+                hi[i] = __float2half_rn(e);
+                lo[i] = __float2half_rn(e - __half2float(hi[i]));
+            }
+            bhi[kk][0] = pack2(hi[0], hi[1]);
+            bhi[kk][1] = pack2(hi[2], hi[3]);
+            blo[kk][0] = pack2(lo[0], lo[1]);
+            blo[kk][1] = pack2(lo[2], lo[3]);
+        }
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+        l_run = l_run * alpha + lsum;
+        m_run = m_new;
+        // -- O^T += V^T P^T for this warp's eighth of the head width
+        const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * t);      // head 2t
+        const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * t + 4);  // head 2t+1
+#pragma unroll
+        for (int mt = 0; mt < C::kMT; mt++) {
+            acc[mt][0] *= a0;
+            acc[mt][1] *= a1;
+            acc[mt][2] *= a0;
+            acc[mt][3] *= a1;
+        }
+#pragma unroll
+        for (int kk = 0; kk < C::kPVK; kk++)
 #pragma unroll
             for (int mt = 0; mt < C::kMT; mt++) {
                 const int dm = (warp * C::kMT + mt) * 16;
-                tk.out[(2 * t) * HD + dm + g] = acc[mt][0] * i0;
-                tk.out[(2 * t + 1) * HD + dm + g] = acc[mt][1] * i1;
-                tk.out[(2 * t) * HD + dm + g + 8] = acc[mt][2] * i0;
-                tk.out[(2 * t + 1) * HD + dm + g + 8] = acc[mt][3] * i1;
+                const int row = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
+                const int col = dm + ((lane >> 3) & 1) * 8;
+                uint32_t a[4];
+                ldsm_x4_t(vb + box_off<HD>(row, col), a[0], a[1], a[2], a[3]);
+                mma16816(acc[mt], a, bhi[kk][0], bhi[kk][1]);
+                mma16816(acc[mt], a, blo[kk][0], blo[kk][1]);
             }
-            if (warp == 0 && t == 0 && !(l_run > 0.0f)) atomicOr(p.err_flag, 1);
-            continue;
-        }
-        const int slot_p = tk.partial_base + it.split;
-        float *po = p.part_o + (size_t)slot_p * kHeads * 512;
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sh.bars->empty[slot]);
+    }
+    // ---- O[h][d] for h = 2t, 2t+1 and d = dm + g (+8): final, or a partial
+    const float l0 = __shfl_sync(0xffffffffu, l_run, 8 * t), l1 = __shfl_sync(0xffffffffu, l_run, 8 * t + 4);
+    const bool final_out = tk.n_splits == 1;
+    float *dst = final_out ? tk.out : p.part_o + (size_t)(tk.partial_base + it.split) * kHeads * 512;
+    const float i0 = final_out ? 1.0f / l0 : 1.0f, i1 = final_out ? 1.0f / l1 : 1.0f;
 #pragma unroll
-        for (int mt = 0; mt < C::kMT; mt++) {
-            const int dm = (warp * C::kMT + mt) * 16;
-            po[(2 * t) * HD + dm + g] = acc[mt][0];
-            po[(2 * t + 1) * HD + dm + g] = acc[mt][1];
-            po[(2 * t) * HD + dm + g + 8] = acc[mt][2];
-            po[(2 * t + 1) * HD + dm + g + 8] = acc[mt][3];
+    for (int mt = 0; mt < C::kMT; mt++) {
+        const int dm = (warp * C::kMT + mt) * 16;
+        dst[(2 * t) * HD + dm + g] = acc[mt][0] * i0;
+        dst[(2 * t + 1) * HD + dm + g] = acc[mt][1] * i1;
+        dst[(2 * t) * HD + dm + g + 8] = acc[mt][2] * i0;
+        dst[(2 * t + 1) * HD + dm + g + 8] = acc[mt][3] * i1;
+    }
+    if (warp == 0 && t == 0) {
+        if (final_out) {
+            if (!(l_run > 0.0f) || !(l_run < CUDART_INF_F)) atomicOr(p.err_flag, 1);
+        } else {
+            const size_t slot_p = (size_t)(tk.partial_base + it.split);
+            p.part_ml[slot_p * 2 * kHeads + g] = m_run;
+            p.part_ml[slot_p * 2 * kHeads + kHeads + g] = l_run;
         }
-        if (warp == 0 && t == 0) {
-            p.part_ml[(size_t)slot_p * 2 * kHeads + g] = m_run;
-            p.part_ml[(size_t)slot_p * 2 * kHeads + kHeads + g] = l_run;
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kThreadsF16, 1) decode_f16_kernel(DecodeParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Shared sh;
+    sh.stages = smem;
+    sh.region = smem + kSlots * kStageBytes;
+    sh.bars = reinterpret_cast<F16Bars *>(sh.region + kRegionBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kSlots; i++) {
+            ptx::mbar_init(&sh.bars->full[i], 1);
+            ptx::mbar_init(&sh.bars->empty[i], kWarpsC);
         }
-        __threadfence();
-        compute_bar();
-        if (threadIdx.x == 0) last_s = atomicAdd(p.tickets + it.task, 1u) == (unsigned)(tk.n_splits - 1);
-        compute_bar();
-        if (last_s) {
-            __threadfence();
-            // merge: weights per (split, head) in parallel, then each thread
-            // sums its columns over the splits
-            const int ns = tk.n_splits;
-            const float *pml = p.part_ml + (size_t)tk.partial_base * 2 * kHeads;
-            const float *pall = p.part_o + (size_t)tk.partial_base * kHeads * 512;
-            float *wsm = s_smem;  // reuse: [ns][8] weights then [8] 1/L, ns <= 96
-            for (int h = warp; h < kHeads; h += kWarpsC) {
-                float M = -CUDART_INF_F;
-                for (int s = lane; s < ns; s += 32) M = fmaxf(M, __ldcg(pml + (size_t)s * 2 * kHeads + h));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-                float L = 0.0f;
-                for (int s = lane; s < ns; s += 32) {
-                    const float ms = __ldcg(pml + (size_t)s * 2 * kHeads + h);
-                    const float w = ms == -CUDART_INF_F ? 0.0f : expf(ms - M);
-                    wsm[s * 8 + h] = w;
-                    L = fmaf(__ldcg(pml + (size_t)s * 2 * kHeads + kHeads + h), w, L);
+        ptx::mbar_init(&sh.bars->q_full, 1);
+        ptx::mbar_init(&sh.bars->q_empty, kWarpsC);
+        sh.bars->abort = 0;
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    const int i0 = p.cta_start[blockIdx.x], i1 = p.cta_start[blockIdx.x + 1];
+    uint32_t st = 0;  // stage counter over this CTA's items
+    if (warp == kWarpsC) {
+        if (lane == 0) {
+            uint32_t ic = 0;
+            for (int i = i0; i < i1 && !sh.bars->abort; i++, ic++) {
+                const DecodeItem it = p.items[i];
+                const DecodeTask &tk = p.tasks[it.task];
+                const bool ok = tk.hd == 256 ? produce_item<256>(p, it, tk, sh, st, ic)
+                                             : produce_item<512>(p, it, tk, sh, st, ic);
+                if (!ok) break;
+            }
+            // every issued load lands before the CTA may exit
+            for (uint32_t s2 = (st > kSlots ? st - kSlots : 0); s2 < st; s2++)
+                for (uint32_t i = 0; i < kPollLimit && !ptx::mbar_try_wait(&sh.bars->full[s2 % kSlots], (s2 / kSlots) & 1u);
+                     i++) {
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-                if (lane == 0) {
-                    wsm[ns * 8 + h] = 1.0f / L;
-                    if (!(L > 0.0f)) atomicOr(p.err_flag, 1);
+            if (ic > 0)
+                for (uint32_t i = 0; i < kPollLimit && !ptx::mbar_try_wait(&sh.bars->q_full, (ic - 1) & 1u); i++) {
                 }
-            }
-            compute_bar();
-            for (int e = threadIdx.x; e < kHeads * HD; e += 32 * kWarpsC) {
-                const int h = e / HD;
-                float o = 0.0f;
-                for (int s = 0; s < ns; s++) o = fmaf(__ldcg(pall + (size_t)s * kHeads * 512 + e), wsm[s * 8 + h], o);
-                tk.out[e] = o * wsm[ns * 8 + h];
-            }
-            if (threadIdx.x == 0) p.tickets[it.task] = 0u;
-            compute_bar();
         }
+        return;
+    }
+    uint32_t ic = 0;
+    for (int i = i0; i < i1; i++, ic++) {
+        const DecodeItem it = p.items[i];
+        const DecodeTask &tk = p.tasks[it.task];
+        const bool ok = tk.hd == 256 ? compute_item<256>(p, it, tk, sh, st, ic)
+                                     : compute_item<512>(p, it, tk, sh, st, ic);
+        if (!ok) return;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// combine: out = sum_i w_i O_i / sum_i w_i l_i, w_i = exp(m_i - max_j m_j)
+// ---------------------------------------------------------------------------
+
+// max values of the partials are in base-2 units (scores times log2 e)
+__global__ void __launch_bounds__(256) decode_f16_combine(DecodeParams p) {
+    const int task = p.split_tasks[blockIdx.x >> 3];
+    const int h = blockIdx.x & 7;
+    const DecodeTask &tk = p.tasks[task];
+    const int ns = tk.n_splits, hd = tk.hd;
+    __shared__ float wsm[kF16MaxSplits + 1];
+    const float *pml = p.part_ml + (size_t)tk.partial_base * 2 * kHeads;
+    const float *pall = p.part_o + (size_t)tk.partial_base * kHeads * 512 + (size_t)h * hd;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float mv[3], lv[3];
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int k = 0; k < 3; k++) {  // ns <= 96
+            const int s = lane + 32 * k;
+            mv[k] = s < ns ? pml[(size_t)s * 2 * kHeads + h] : -CUDART_INF_F;
+            lv[k] = s < ns ? pml[(size_t)s * 2 * kHeads + kHeads + h] : 0.0f;
+            M = fmaxf(M, mv[k]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int s = lane + 32 * k;
+            const float w = mv[k] == -CUDART_INF_F ? 0.0f : exp2f(mv[k] - M);
+            if (s < ns) wsm[s] = w;
+            L = fmaf(lv[k], w, L);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (lane == 0) {
+            wsm[ns] = 1.0f / L;
+            if (!(L > 0.0f) || !(L < CUDART_INF_F)) atomicOr(p.err_flag, 1);
+        }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < hd; c += 256) {
+        float o = 0.0f;
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[k] = s0 + k < ns ? pall[(size_t)(s0 + k) * kHeads * 512 + c] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (s0 + k < ns) o = fmaf(v[k], wsm[s0 + k], o);
+        }
+        tk.out[h * hd + c] = o * wsm[ns];
     }
 }
 
 }  // namespace
 
-int decode_f16_smem_bytes(int hd) { return hd == 256 ? F16Cfg<256>::kSmemBytes : F16Cfg<512>::kSmemBytes; }
-
-cudaError_t launch_decode_f16(const DecodeParams &p, int hd, int n_sm, cudaStream_t s) {
-    if (p.n_items == 0) return cudaSuccess;
+cudaError_t launch_decode_f16(const DecodeParams &p, int n_tasks, int n_ctas, int n_split_tasks, cudaStream_t s) {
+    if (n_tasks == 0) return cudaSuccess;
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(decode_f16_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             F16Cfg<256>::kSmemBytes);
-        cudaFuncSetAttribute(decode_f16_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             F16Cfg<512>::kSmemBytes);
+        cudaFuncSetAttribute(decode_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         attr = true;
     }
-    const int grid = p.n_items < n_sm ? p.n_items : n_sm;
-    if (hd == 256)
-        decode_f16_kernel<256><<<grid, kThreadsF16, F16Cfg<256>::kSmemBytes, s>>>(p);
-    else if (hd == 512)
-        decode_f16_kernel<512><<<grid, kThreadsF16, F16Cfg<512>::kSmemBytes, s>>>(p);
-    else
-        return cudaErrorInvalidValue;
+    decode_f16_prep<<<n_tasks, 256, 0, s>>>(p);
+    if (n_ctas > 0) decode_f16_kernel<<<n_ctas, kThreadsF16, kSmemBytes, s>>>(p);
+    if (n_split_tasks > 0) decode_f16_combine<<<n_split_tasks * kHeads, 256, 0, s>>>(p);
     return cudaGetLastError();
 }
 

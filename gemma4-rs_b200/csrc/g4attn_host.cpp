@@ -109,6 +109,8 @@ struct g4a_ctx {
     std::vector<uint8_t> h_meta;
     PrefillScratch *prefill = nullptr;
     int n_sm = 148;
+    uint8_t *d_qblocks = nullptr;
+    size_t qblocks_cap = 0;
 };
 
 namespace {
@@ -242,6 +244,7 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
     cudaFree(ctx->d_part_ml);
     cudaFree(ctx->d_tickets);
     cudaFree(ctx->d_meta);
+    cudaFree(ctx->d_qblocks);
     prefill_scratch_free(ctx->prefill);
     delete ctx;
 }
@@ -262,6 +265,8 @@ extern "C" int g4a_sync(g4a_ctx *ctx) {
     G4A_CUDA_TRY(ctx, cudaMemcpy(&flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (flag) {
         G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+        if (flag & 6)  // bit 1: a prefill wait ran out, bit 2: a decode wait ran out
+            return fail(ctx, G4A_TIMEOUT, "compute: a device wait ran out (flag %d)", flag);
         return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
     }
     return G4A_OK;
@@ -541,6 +546,7 @@ struct Plan {
     std::vector<DecodeItem> items[2];  // by head width: [0] 256, [1] 512
     int32_t slots = 0;
     bool f16_fast = false;             // f16 paged cache: the TMA / tensor-core kernel
+    std::vector<int32_t> cta_start;    // f16 kernel: per-CTA item ranges (items[0] holds all items)
 };
 
 // Rows per work item. Aims at about two items per SM over the whole call,
@@ -581,6 +587,10 @@ struct Staged {
     size_t items_offset = 0;
     int kv_f16 = 0;
     bool f16_fast = false;
+    int32_t n_ctas = 0;
+    int32_t n_tasks = 0;
+    int32_t n_split_tasks = 0;
+    uint8_t *q_blocks = nullptr;  // f16 kernel scratch
 };
 
 // Copies a plan's metadata to the device. With own_buffers the buffers are
@@ -591,12 +601,20 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
     const size_t n_tasks = plan.tasks.size();
     const size_t n_items = plan.items[0].size() + plan.items[1].size();
     const size_t bytes_tasks = n_tasks * sizeof(DecodeTask);
-    const size_t bytes = bytes_tasks + n_items * sizeof(DecodeItem);
+    const size_t bytes_items = n_items * sizeof(DecodeItem);
+    std::vector<int32_t> split_tasks;
+    if (plan.f16_fast)
+        for (size_t i = 0; i < n_tasks; i++)
+            if (plan.tasks[i].n_splits > 1) split_tasks.push_back((int32_t)i);
+    const size_t bytes_cta = plan.cta_start.size() * sizeof(int32_t);
+    const size_t bytes = bytes_tasks + bytes_items + bytes_cta + split_tasks.size() * sizeof(int32_t);
+    const size_t n_qb = plan.f16_fast ? std::max<size_t>(n_tasks, 1) * kQBlockBytes : 0;
     const size_t n_po = (size_t)std::max(plan.slots, 1) * kHeads * 512;
     const size_t n_ml = (size_t)std::max(plan.slots, 1) * 2 * kHeads;
     const size_t n_tk = std::max<size_t>(n_tasks, 1);
     int rc;
     if (own_buffers) {
+        if (n_qb) G4A_CUDA_TRY(ctx, cudaMalloc(&st->q_blocks, n_qb));
         G4A_CUDA_TRY(ctx, cudaMalloc(&st->meta, std::max<size_t>(bytes, 16)));
         G4A_CUDA_TRY(ctx, cudaMalloc(&st->part_o, n_po * sizeof(float)));
         G4A_CUDA_TRY(ctx, cudaMalloc(&st->part_ml, n_ml * sizeof(float)));
@@ -607,6 +625,8 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
         if ((rc = grow(ctx, &ctx->d_part_o, &ctx->part_o_cap, n_po, false))) return rc;
         if ((rc = grow(ctx, &ctx->d_part_ml, &ctx->part_ml_cap, n_ml, false))) return rc;
         if ((rc = grow(ctx, &ctx->d_tickets, &ctx->tickets_cap, n_tk, true))) return rc;
+        if (n_qb && (rc = grow(ctx, &ctx->d_qblocks, &ctx->qblocks_cap, n_qb, false))) return rc;
+        st->q_blocks = ctx->d_qblocks;
         st->meta = ctx->d_meta;
         st->part_o = ctx->d_part_o;
         st->part_ml = ctx->d_part_ml;
@@ -617,6 +637,11 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
     std::memcpy(ctx->h_meta.data() + bytes_tasks, plan.items[0].data(), plan.items[0].size() * sizeof(DecodeItem));
     std::memcpy(ctx->h_meta.data() + bytes_tasks + plan.items[0].size() * sizeof(DecodeItem), plan.items[1].data(),
                 plan.items[1].size() * sizeof(DecodeItem));
+    if (!plan.cta_start.empty())
+        std::memcpy(ctx->h_meta.data() + bytes_tasks + bytes_items, plan.cta_start.data(), bytes_cta);
+    if (!split_tasks.empty())
+        std::memcpy(ctx->h_meta.data() + bytes_tasks + bytes_items + bytes_cta, split_tasks.data(),
+                    split_tasks.size() * sizeof(int32_t));
     G4A_CUDA_TRY(ctx, cudaMemcpyAsync(st->meta, ctx->h_meta.data(), bytes, cudaMemcpyHostToDevice, ctx->stream));
     DecodeParams &p = st->params;
     p = DecodeParams{};
@@ -636,19 +661,30 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
     st->items_offset = bytes_tasks;
     st->kv_f16 = kv_f16;
     st->f16_fast = plan.f16_fast;
+    p.cta_start = plan.cta_start.empty()
+                      ? nullptr
+                      : reinterpret_cast<const int32_t *>(st->meta + bytes_tasks + bytes_items);
+    st->n_ctas = plan.cta_start.empty() ? 0 : (int32_t)plan.cta_start.size() - 1;
+    p.q_blocks = st->q_blocks;
+    p.split_tasks = reinterpret_cast<const int32_t *>(st->meta + bytes_tasks + bytes_items + bytes_cta);
+    st->n_tasks = (int32_t)n_tasks;
+    st->n_split_tasks = (int32_t)split_tasks.size();
     return G4A_OK;
 }
 
 int launch_staged(g4a_ctx *ctx, const Staged &st) {
     DecodeParams p = st.params;
     const DecodeItem *items = reinterpret_cast<const DecodeItem *>(st.meta + st.items_offset);
+    if (st.f16_fast) {  // both head widths in one launch
+        p.items = items;
+        p.n_items = st.n_items[0] + st.n_items[1];
+        G4A_CUDA_TRY(ctx, launch_decode_f16(p, st.n_tasks, st.n_ctas, st.n_split_tasks, ctx->stream));
+        return G4A_OK;
+    }
     for (int which = 0; which < 2; which++) {
         p.items = items;
         p.n_items = st.n_items[which];
-        if (st.f16_fast)
-            G4A_CUDA_TRY(ctx, launch_decode_f16(p, which ? 512 : 256, ctx->n_sm, ctx->stream));
-        else
-            G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream));
+        G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream));
         items += st.n_items[which];
     }
     return G4A_OK;
@@ -670,6 +706,37 @@ void add_items_aligned(Plan &plan, DecodeTask &t, int32_t task_index, int32_t ro
     t.partial_base = n > 1 ? plan.slots : 0;
     if (n > 1) plan.slots += n;
     for (int32_t s = 0; s < n; s++) plan.items[which].push_back(DecodeItem{task_index, s, cuts[s], cuts[s + 1]});
+}
+
+// Longest-processing-time assignment of the f16 kernel's items to persistent
+// CTAs: cost = K/V bytes of the rows (in units of a 256-wide row) plus a fixed
+// per-item charge for the q preparation and, for split tasks, the partial
+// write. Items are then stored CTA by CTA with a start table.
+void assign_ctas(Plan &plan, int n_sm) {
+    std::vector<DecodeItem> all(plan.items[0]);
+    all.insert(all.end(), plan.items[1].begin(), plan.items[1].end());
+    plan.items[0].clear();
+    plan.items[1].clear();
+    auto cost = [&](const DecodeItem &it) {
+        const DecodeTask &t = plan.tasks[it.task];
+        return (int64_t)(it.row_hi - it.row_lo) * (t.hd / 256) + 64 + (t.n_splits > 1 ? 32 : 0);
+    };
+    std::stable_sort(all.begin(), all.end(), [&](const DecodeItem &a, const DecodeItem &b) { return cost(a) > cost(b); });
+    const int n_ctas = std::max(1, std::min<int>(n_sm, (int)all.size()));
+    std::vector<int64_t> load(n_ctas, 0);
+    std::vector<std::vector<DecodeItem>> per(n_ctas);
+    for (const auto &it : all) {
+        int best = 0;
+        for (int b = 1; b < n_ctas; b++)
+            if (load[b] < load[best]) best = b;
+        load[best] += cost(it);
+        per[best].push_back(it);
+    }
+    plan.cta_start.assign(1, 0);
+    for (int b = 0; b < n_ctas; b++) {
+        plan.items[0].insert(plan.items[0].end(), per[b].begin(), per[b].end());
+        plan.cta_start.push_back((int32_t)plan.items[0].size());
+    }
 }
 
 int run_plan(g4a_ctx *ctx, Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens, int kv_f16) {
@@ -793,6 +860,9 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
             weighted += (hi - lo) * (hd[i] / 256);
         }
     plan.f16_fast = kv->dtype == G4A_KV_F16 && kv->d_tmaps != nullptr;
+    // f16 kernel: about three items per SM over the whole call, by K/V bytes
+    const int64_t weighted_all = weighted;
+    const int64_t item_weight = std::max<int64_t>(64, (weighted_all + 3 * ctx->n_sm - 1) / (3 * ctx->n_sm));
     for (int32_t i = 0; i < n_layers; i++) {
         const g4a_decode_layer &a = layers[i];
         const auto &L = kv->layers[src[i]];
@@ -821,21 +891,18 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
             t.global = global[i];
             t.q_ready = 0;
             t.scale = 1.0f;
+            t.hd = hd[i];
             if (plan.f16_fast) {
                 t.tmap_k = kv->d_tmaps + (size_t)src[i] * 256;
                 t.tmap_v = kv->d_tmaps + (size_t)src[i] * 256 + 128;
-                add_items_aligned(plan, t, (int32_t)plan.tasks.size(), rows_per, which);
+                add_items_aligned(plan, t, (int32_t)plan.tasks.size(), (int32_t)(item_weight / (hd[i] / 256)), which);
             } else {
                 add_items(plan, t, (int32_t)plan.tasks.size(), rows_per, which);
             }
             plan.tasks.push_back(t);
         }
     }
-    if (plan.f16_fast)  // longest first: the persistent CTAs take items round-robin
-        for (auto &v : plan.items)
-            std::stable_sort(v.begin(), v.end(), [](const DecodeItem &x, const DecodeItem &y) {
-                return x.row_hi - x.row_lo > y.row_hi - y.row_lo;
-            });
+    if (plan.f16_fast) assign_ctas(plan, ctx->n_sm);
     for (int32_t i = 0; i < n_layers; i++)
         if (owner[i])
             for (int32_t j = 0; j < n_seqs; j++) kv_len(kv, seq_ids[j], layers[i].layer) += 1;
@@ -889,6 +956,7 @@ extern "C" void g4a_plan_destroy(g4a_plan *plan) {
     cudaFree(plan->st.part_o);
     cudaFree(plan->st.part_ml);
     cudaFree(plan->st.tickets);
+    cudaFree(plan->st.q_blocks);
     delete plan;
 }
 

@@ -33,7 +33,7 @@ struct DecodeTask {
     int32_t global;       // 1 = global RoPE table
     int32_t q_ready;      // 1 = q is already normalised and rotated
     float scale;          // score scale (1.0 in the model, model.rs:409)
-    int32_t pad;
+    int32_t hd;           // head width of this task's layer
     const void *tmap_k;   // f16 paged caches: TMA descriptors of the layer's pools
     const void *tmap_v;
 };
@@ -57,6 +57,9 @@ struct DecodeParams {
     unsigned *tickets;           // [tasks] arrival counters, zero between calls
     int *err_flag;               // bit 0: non-finite softmax
     int32_t n_items;
+    const int32_t *cta_start;    // f16 kernel: CTA b runs items [cta_start[b], cta_start[b+1])
+    void *q_blocks;              // f16 kernel: [tasks][kQBlockBytes] q hi/lo blocks
+    const int32_t *split_tasks;  // f16 kernel: tasks whose items are merged by the combine kernel
 };
 
 // Bulk append of already processed rows, or norm+RoPE of raw rows.
@@ -81,7 +84,10 @@ struct ViewParams {
 cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, cudaStream_t s);
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
-cudaError_t launch_decode_f16(const DecodeParams &p, int hd, int n_sm, cudaStream_t s);
+constexpr size_t kQBlockBytes = 16 * 512 * 2;  // q hi/lo block of one task (f16 kernel)
+// prep (q blocks + appended rows), main (persistent, per-CTA item lists),
+// combine (merges split tasks).
+cudaError_t launch_decode_f16(const DecodeParams &p, int n_tasks, int n_ctas, int n_split_tasks, cudaStream_t s);
 inline int f16_stage_rows(int hd) { return 16384 / hd; }
 cudaError_t launch_attend_generic(const float *q, const float *k, const float *v, int64_t len, int n_heads,
                                   int n_kv, int hd, float scale, float *out, int *err_flag, cudaStream_t s);

@@ -363,3 +363,42 @@ def test_plan_runs_match_decode(g4a, oracle, ctx, torch_cuda):
         assert np.array_equal(got, first)  # deterministic combine order
     plan.close()
     kv.close()
+
+
+def test_decode_both_widths_long_contexts(g4a, oracle, ctx, torch_cuda):
+    """Both layer kinds in one call at long contexts: tasks split across many
+    items, items of both head widths interleaved on the same CTAs, combined
+    by the merge kernel; two consecutive steps."""
+    torch = torch_cuda
+    hp = oracle.hparams_e2b()
+    ff = oracle.proportional_rope_freq_factors(512, 0.25)
+    r = rng(4242)
+    lengths = [4000, 3100, 2600, 1999, 1500, 1024, 777, 513, 300, 64, 33, 2]
+    n = len(lengths)
+    kv = g4a.KvCache(ctx, n, 4100, dtype=1, layers=[13, 14])
+    okvs = [oracle.KvCache() for _ in range(n)]
+    w = {l: (norm_weight(r, oracle.head_dim(hp, l)), norm_weight(r, oracle.head_dim(hp, l))) for l in (13, 14)}
+    for s, L in enumerate(lengths):
+        for layer in (13, 14):
+            _fill_history(g4a, oracle, torch, kv, okvs[s], hp, s, layer, L, r, w[layer][1], ff)
+    for step in range(2):
+        args, raws = [], {}
+        for layer in (13, 14):
+            hd = oracle.head_dim(hp, layer)
+            q_raw, k_raw, v_raw = normal(r, n, 8 * hd), normal(r, n, hd), normal(r, n, hd)
+            raws[layer] = (q_raw, k_raw, v_raw)
+            args.append(dict(layer=layer, q_raw=dev(torch, q_raw), k_raw=dev(torch, k_raw),
+                             v_raw=dev(torch, v_raw), q_norm_w=dev(torch, w[layer][0]),
+                             k_norm_w=dev(torch, w[layer][1]), out=torch.empty(n, 8 * hd, device="cuda")))
+        pos = [L + step for L in lengths]
+        ctx.decode(kv, args, list(range(n)), pos)
+        ctx.sync()
+        for a in args:
+            layer = a["layer"]
+            q_raw, k_raw, v_raw = raws[layer]
+            got = host(a["out"])
+            for s in range(n):
+                ref = okvs[s].attention_block(hp, layer, pos[s], q_raw[s], k_raw[s], v_raw[s], w[layer][0],
+                                              w[layer][1], ff, kv_store=1)
+                assert max_abs_diff(got[s], ref) <= TOL, (step, layer, lengths[s])
+    kv.close()
