@@ -100,6 +100,13 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 __device__ __forceinline__ uint32_t pack2(__half lo, __half hi) {
     return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start before its predecessor ends; it
+// must wait here before touching what the predecessor writes. Without the
+// attribute both instructions do nothing.
+__device__ __forceinline__ void wait_prerequisite() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void release_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // named barrier of the 8 compute warps (the producer never takes part)
 __device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
@@ -240,6 +247,7 @@ __device__ __forceinline__ void prep_task(const DecodeParams &p, const DecodeTas
 }
 
 __global__ void __launch_bounds__(256) decode_f16_prep(DecodeParams p) {
+    release_dependents();  // the main kernel may be scheduled now; it waits for our writes
     const DecodeTask &tk = p.tasks[blockIdx.x];
     if (tk.hd == 256) prep_task<256>(p, tk, blockIdx.x);
     else prep_task<512>(p, tk, blockIdx.x);
@@ -266,18 +274,36 @@ __device__ __forceinline__ bool wait_poll(uint64_t *bar, uint32_t parity, volati
 }
 
 // Producer side of one item: its q block, then its stages.
+// Stages are issued first; the q block (written by the prep kernel) follows
+// once the stages that fit in the ring are under way, and any stage holding
+// an appended row (also written by prep) waits for the prep kernel to end.
 template <int HD>
 __device__ __forceinline__ bool produce_item(const DecodeParams &p, const DecodeItem &it, const DecodeTask &tk,
-                                             const Shared &sh, uint32_t &st, uint32_t ic) {
+                                             const Shared &sh, uint32_t &st, uint32_t ic, bool &prereq_done) {
     using C = F16Cfg<HD>;
     volatile int *abort = &sh.bars->abort;
-    if (!wait_poll(&sh.bars->q_empty, (ic & 1u) ^ 1u, abort, p.err_flag)) return false;
-    ptx::mbar_arrive_expect_tx(&sh.bars->q_full, C::kQBytes);
-    bulk_load(sh.region, reinterpret_cast<const uint8_t *>(p.q_blocks) + (size_t)it.task * kQBlockBytes, C::kQBytes,
-              &sh.bars->q_full);
+    bool q_issued = false;
+    auto issue_q = [&]() -> bool {
+        if (!prereq_done) {
+            wait_prerequisite();
+            prereq_done = true;
+        }
+        if (!wait_poll(&sh.bars->q_empty, (ic & 1u) ^ 1u, abort, p.err_flag)) return false;
+        ptx::mbar_arrive_expect_tx(&sh.bars->q_full, C::kQBytes);
+        bulk_load(sh.region, reinterpret_cast<const uint8_t *>(p.q_blocks) + (size_t)it.task * kQBlockBytes,
+                  C::kQBytes, &sh.bars->q_full);
+        q_issued = true;
+        return true;
+    };
     const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
-    for (int r0 = it.row_lo / C::S * C::S; r0 < it.row_hi; r0 += C::S, st++) {
+    int issued = 0;
+    for (int r0 = it.row_lo / C::S * C::S; r0 < it.row_hi; r0 += C::S, st++, issued++) {
         const int slot = st % kSlots;
+        if (!q_issued && issued == kSlots - 1 && !issue_q()) return false;
+        if (!prereq_done && tk.new_row >= r0 && tk.new_row < r0 + C::S) {
+            wait_prerequisite();
+            prereq_done = true;
+        }
         if (!wait_poll(&sh.bars->empty[slot], ((st / kSlots) & 1u) ^ 1u, abort, p.err_flag)) return false;
         const int page = __ldg(bt + r0 / p.page_tokens);
         const int y = page * p.page_tokens + (r0 % p.page_tokens);
@@ -289,6 +315,7 @@ __device__ __forceinline__ bool produce_item(const DecodeParams &p, const Decode
             ptx::tma_load_2d(dst + kStageBytes / 2 + c * C::kBoxBytes, tk.tmap_v, &sh.bars->full[slot], 64 * c, y);
         }
     }
+    if (!q_issued && !issue_q()) return false;
     return true;
 }
 
@@ -510,18 +537,21 @@ __global__ void __launch_bounds__(kThreadsF16, 1) decode_f16_kernel(DecodeParams
         ptx::fence_mbar_init();
     }
     __syncthreads();
+    release_dependents();  // the combine kernel may be scheduled; it waits for our end
     const int i0 = p.cta_start[blockIdx.x], i1 = p.cta_start[blockIdx.x + 1];
     uint32_t st = 0;  // stage counter over this CTA's items
     if (warp == kWarpsC) {
         if (lane == 0) {
             uint32_t ic = 0;
+            bool prereq_done = false;
             for (int i = i0; i < i1 && !sh.bars->abort; i++, ic++) {
                 const DecodeItem it = p.items[i];
                 const DecodeTask &tk = p.tasks[it.task];
-                const bool ok = tk.hd == 256 ? produce_item<256>(p, it, tk, sh, st, ic)
-                                             : produce_item<512>(p, it, tk, sh, st, ic);
+                const bool ok = tk.hd == 256 ? produce_item<256>(p, it, tk, sh, st, ic, prereq_done)
+                                             : produce_item<512>(p, it, tk, sh, st, ic, prereq_done);
                 if (!ok) break;
             }
+            if (!prereq_done) wait_prerequisite();
             // every issued load lands before the CTA may exit
             for (uint32_t s2 = (st > kSlots ? st - kSlots : 0); s2 < st; s2++)
                 for (uint32_t i = 0; i < kPollLimit && !ptx::mbar_try_wait(&sh.bars->full[s2 % kSlots], (s2 / kSlots) & 1u);
@@ -549,6 +579,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1) decode_f16_kernel(DecodeParams
 
 // max values of the partials are in base-2 units (scores times log2 e)
 __global__ void __launch_bounds__(256) decode_f16_combine(DecodeParams p) {
+    wait_prerequisite();  // every partial of the main kernel is written
     const int task = p.split_tasks[blockIdx.x >> 3];
     const int h = blockIdx.x & 7;
     const DecodeTask &tk = p.tasks[task];
@@ -601,17 +632,34 @@ __global__ void __launch_bounds__(256) decode_f16_combine(DecodeParams p) {
 
 }  // namespace
 
-cudaError_t launch_decode_f16(const DecodeParams &p, int n_tasks, int n_ctas, int n_split_tasks, cudaStream_t s) {
-    if (n_tasks == 0) return cudaSuccess;
+cudaError_t launch_decode_f16(const DecodeParams &p, int stage, int n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(decode_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         attr = true;
     }
-    decode_f16_prep<<<n_tasks, 256, 0, s>>>(p);
-    if (n_ctas > 0) decode_f16_kernel<<<n_ctas, kThreadsF16, kSmemBytes, s>>>(p);
-    if (n_split_tasks > 0) decode_f16_combine<<<n_split_tasks * kHeads, 256, 0, s>>>(p);
-    return cudaGetLastError();
+    if (stage == 0) {
+        decode_f16_prep<<<n, 256, 0, s>>>(p);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cfg.stream = s;
+    if (stage == 1) {
+        cfg.gridDim = dim3(n);
+        cfg.blockDim = dim3(kThreadsF16);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        return cudaLaunchKernelEx(&cfg, decode_f16_kernel, p);
+    }
+    cfg.gridDim = dim3(n * kHeads);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, decode_f16_combine, p);
 }
 
 }  // namespace g4a

@@ -111,6 +111,16 @@ struct g4a_ctx {
     int n_sm = 148;
     uint8_t *d_qblocks = nullptr;
     size_t qblocks_cap = 0;
+    // per-kernel timing (g4a_profile_enable): events around each launch
+    bool profiling = false;
+    struct Rec {
+        int kernel;
+        cudaEvent_t a, b;
+    };
+    std::vector<Rec> recs;
+    std::vector<cudaEvent_t> spare;
+    double prof_ms[G4A_K_COUNT] = {};
+    int64_t prof_n[G4A_K_COUNT] = {};
 };
 
 namespace {
@@ -193,7 +203,60 @@ int grow(g4a_ctx *ctx, T **ptr, size_t *cap, size_t need, bool zero) {
     return G4A_OK;
 }
 
+// Runs `launch` between two events on the context's stream when profiling.
+template <typename F>
+cudaError_t timed(g4a_ctx *ctx, int kernel, F launch) {
+    if (!ctx->profiling) return launch();
+    cudaEvent_t ev[2];
+    for (auto &e : ev) {
+        if (!ctx->spare.empty()) {
+            e = ctx->spare.back();
+            ctx->spare.pop_back();
+        } else {
+            cudaEventCreate(&e);
+        }
+    }
+    cudaEventRecord(ev[0], ctx->stream);
+    cudaError_t err = launch();
+    cudaEventRecord(ev[1], ctx->stream);
+    ctx->recs.push_back({kernel, ev[0], ev[1]});
+    return err;
+}
+
+void collect_profile(g4a_ctx *ctx) {
+    if (ctx->recs.empty()) return;
+    cudaStreamSynchronize(ctx->stream);
+    for (auto &r : ctx->recs) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+            ctx->prof_ms[r.kernel] += ms;
+            ctx->prof_n[r.kernel] += 1;
+        }
+        ctx->spare.push_back(r.a);
+        ctx->spare.push_back(r.b);
+    }
+    ctx->recs.clear();
+}
+
 }  // namespace
+
+extern "C" int g4a_profile_enable(g4a_ctx *ctx, int enable) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    collect_profile(ctx);
+    for (int k = 0; k < G4A_K_COUNT; k++) ctx->prof_ms[k] = 0.0, ctx->prof_n[k] = 0;
+    ctx->profiling = enable != 0;
+    return G4A_OK;
+}
+
+extern "C" int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches) {
+    if (!ctx || kernel < 0 || kernel >= G4A_K_COUNT || !total_ms || !launches) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    collect_profile(ctx);
+    *total_ms = ctx->prof_ms[kernel];
+    *launches = ctx->prof_n[kernel];
+    return G4A_OK;
+}
 
 extern "C" int g4a_ctx_create(int device, const g4a_hparams *hp, const float *rope_freqs, int32_t max_positions,
                               g4a_ctx **out) {
@@ -245,6 +308,8 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
     cudaFree(ctx->d_tickets);
     cudaFree(ctx->d_meta);
     cudaFree(ctx->d_qblocks);
+    for (auto &r : ctx->recs) cudaEventDestroy(r.a), cudaEventDestroy(r.b);
+    for (auto e : ctx->spare) cudaEventDestroy(e);
     prefill_scratch_free(ctx->prefill);
     delete ctx;
 }
@@ -678,13 +743,17 @@ int launch_staged(g4a_ctx *ctx, const Staged &st) {
     if (st.f16_fast) {  // both head widths in one launch
         p.items = items;
         p.n_items = st.n_items[0] + st.n_items[1];
-        G4A_CUDA_TRY(ctx, launch_decode_f16(p, st.n_tasks, st.n_ctas, st.n_split_tasks, ctx->stream));
+        G4A_CUDA_TRY(ctx, timed(ctx, G4A_K_DECODE_PREP, [&] { return launch_decode_f16(p, 0, st.n_tasks, ctx->stream); }));
+        G4A_CUDA_TRY(ctx, timed(ctx, G4A_K_DECODE_MAIN, [&] { return launch_decode_f16(p, 1, st.n_ctas, ctx->stream); }));
+        G4A_CUDA_TRY(ctx,
+                     timed(ctx, G4A_K_DECODE_COMBINE, [&] { return launch_decode_f16(p, 2, st.n_split_tasks, ctx->stream); }));
         return G4A_OK;
     }
     for (int which = 0; which < 2; which++) {
         p.items = items;
         p.n_items = st.n_items[which];
-        G4A_CUDA_TRY(ctx, launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream));
+        G4A_CUDA_TRY(ctx, timed(ctx, G4A_K_DECODE_SPLITKV,
+                                [&] { return launch_decode(p, which ? 512 : 256, st.kv_f16, true, ctx->stream); }));
         items += st.n_items[which];
     }
     return G4A_OK;
@@ -723,14 +792,16 @@ void assign_ctas(Plan &plan, int n_sm) {
     };
     std::stable_sort(all.begin(), all.end(), [&](const DecodeItem &a, const DecodeItem &b) { return cost(a) > cost(b); });
     const int n_ctas = std::max(1, std::min<int>(n_sm, (int)all.size()));
-    std::vector<int64_t> load(n_ctas, 0);
     std::vector<std::vector<DecodeItem>> per(n_ctas);
+    // min-heap of (load, cta): each item goes to the least loaded CTA
+    std::vector<std::pair<int64_t, int>> heap;
+    for (int b = 0; b < n_ctas; b++) heap.push_back({0, b});
+    auto greater = [](const std::pair<int64_t, int> &x, const std::pair<int64_t, int> &y) { return x > y; };
     for (const auto &it : all) {
-        int best = 0;
-        for (int b = 1; b < n_ctas; b++)
-            if (load[b] < load[best]) best = b;
-        load[best] += cost(it);
-        per[best].push_back(it);
+        std::pop_heap(heap.begin(), heap.end(), greater);
+        heap.back().first += cost(it);
+        per[heap.back().second].push_back(it);
+        std::push_heap(heap.begin(), heap.end(), greater);
     }
     plan.cta_start.assign(1, 0);
     for (int b = 0; b < n_ctas; b++) {
@@ -976,7 +1047,12 @@ extern "C" int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *p
     if (ctx->hp.n_heads != kHeads || ctx->hp.n_kv_heads != 1)
         return fail(ctx, G4A_COMPUTE, "compute: prefill serves %d query heads over 1 KV head", kHeads);
     const char *msg = "";
-    const int rc = prefill_run(ctx->prefill, ctx->d_err, n, problems, ctx->stream, &msg);
+    int rc = G4A_OK;
+    const cudaError_t e = timed(ctx, G4A_K_PREFILL, [&] {
+        rc = prefill_run(ctx->prefill, ctx->d_err, n, problems, ctx->stream, &msg);
+        return cudaSuccess;
+    });
+    (void)e;
     if (rc != G4A_OK) return fail(ctx, rc, "compute: %s", msg);
     return G4A_OK;
 }

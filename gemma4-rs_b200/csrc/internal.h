@@ -85,9 +85,9 @@ cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, 
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
 constexpr size_t kQBlockBytes = 16 * 512 * 2;  // q hi/lo block of one task (f16 kernel)
-// prep (q blocks + appended rows), main (persistent, per-CTA item lists),
-// combine (merges split tasks).
-cudaError_t launch_decode_f16(const DecodeParams &p, int n_tasks, int n_ctas, int n_split_tasks, cudaStream_t s);
+// stage 0: prep, n tasks (q blocks + appended rows); stage 1: main, n
+// persistent CTAs with per-CTA item lists; stage 2: combine, n split tasks.
+cudaError_t launch_decode_f16(const DecodeParams &p, int stage, int n, cudaStream_t s);
 inline int f16_stage_rows(int hd) { return 16384 / hd; }
 cudaError_t launch_attend_generic(const float *q, const float *k, const float *v, int64_t len, int n_heads,
                                   int n_kv, int hd, float scale, float *out, int *err_flag, cudaStream_t s);

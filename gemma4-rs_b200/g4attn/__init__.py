@@ -26,6 +26,7 @@ HEADER = HERE.parent.parent / "include" / "g4attn.h"
 OK, CONTEXT_TOO_LONG, MISSING_LAYER, MISSING_WEIGHT, COMPUTE, NONFINITE, BAD_LAYER, CUDA, NCCL, TIMEOUT, \
     OUT_OF_PAGES = range(11)
 KV_F32, KV_F16 = 0, 1
+K_DECODE_PREP, K_DECODE_MAIN, K_DECODE_COMBINE, K_DECODE_SPLITKV, K_PREFILL = range(5)
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -102,6 +103,9 @@ def _load():
     L.g4a_plan_destroy.argtypes = [_vp]
     L.g4a_plan_destroy.restype = None
     L.g4a_prefill.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(PrefillProblem)]
+    L.g4a_profile_enable.argtypes = [_vp, ctypes.c_int]
+    L.g4a_profile_read.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(ctypes.c_double),
+                                   ctypes.POINTER(ctypes.c_int64)]
     L.g4a_lse_merge.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int64,
                                 ctypes.c_int32, ctypes.c_int32, _vp, _vp]
     return L
@@ -212,6 +216,15 @@ class Context:
 
     def sync(self):
         self.check(lib.g4a_sync(self.h))
+
+    def profile(self, enable: bool):
+        self.check(lib.g4a_profile_enable(self.h, int(enable)))
+
+    def profile_read(self, kernel: int):
+        """(total device ms, launches) of one kernel since profiling was enabled."""
+        ms, n = ctypes.c_double(), ctypes.c_int64()
+        self.check(lib.g4a_profile_read(self.h, kernel, ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
 
     # model.rs:348 attend
     def attend(self, q, keys, values, n_heads: int, n_kv_heads: int, scale: float, out, length: int | None = None):

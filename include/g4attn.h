@@ -100,6 +100,22 @@ int g4a_ctx_set_stream(g4a_ctx *ctx, void *cuda_stream);
  * last g4a_sync saw a non-finite input (the flag is then cleared). */
 int g4a_sync(g4a_ctx *ctx);
 
+/* Per-kernel device timing (no counterpart in the reference, which logs one
+ * wall-clock line per token, crates/llm-cli/src/main.rs:82-90): when enabled,
+ * every kernel launch of the context is bracketed by CUDA events on its
+ * stream. Enabling (or disabling) clears the totals; reading waits for the
+ * stream and returns the summed device milliseconds and launch count. */
+typedef enum g4a_kernel {
+    G4A_K_DECODE_PREP = 0,     /* f16 decode: q blocks + appended rows */
+    G4A_K_DECODE_MAIN = 1,     /* f16 decode: TMA / tensor-core attention */
+    G4A_K_DECODE_COMBINE = 2,  /* f16 decode: merge of split tasks */
+    G4A_K_DECODE_SPLITKV = 3,  /* f32 caches and g4a_attend */
+    G4A_K_PREFILL = 4,         /* tcgen05 prefill (with its V conversion) */
+    G4A_K_COUNT = 5
+} g4a_kernel;
+int g4a_profile_enable(g4a_ctx *ctx, int enable);
+int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches);
+
 /* ---- attention primitive ---------------------------------------------- */
 
 /* model.rs:348-366 attend: grouped-query attention for one query position.
