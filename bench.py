@@ -412,6 +412,55 @@ def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2):
     return res
 
 
+def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, warmup=3):
+    """Configuration 3 across ranks: the 32,768-token global layer split in
+    zigzag chunks (context parallel: NCCL all-gather of K/V overlapped with
+    the diagonal blocks, then the off-diagonal blocks and a log-sum-exp
+    merge). CUDA events on the library's stream, barrier and synchronize
+    around each repetition, max over ranks."""
+    from g4attn import cp
+    T = 32768
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(77 + rank)
+
+    def unit(shape):
+        x = torch.randn(*shape, device="cuda", generator=gen)
+        return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
+
+    chunks = cp.zigzag_chunks(T, world, rank)
+    c = chunks[0][1] - chunks[0][0]
+    qc = [unit((c, HEADS, HD_G)) for _ in chunks]
+    kc = [unit((c, HD_G)) for _ in chunks]
+    vc = [torch.randn(c, HD_G, device="cuda", generator=gen).to(torch.bfloat16) for _ in chunks]
+    side = torch.cuda.Stream()
+    gather = cp.torch_gather_kv(dist, torch, side)
+    attend = cp.g4a_attend(ctx, torch, HD_G)
+    merge = cp.g4a_merge(ctx, torch, HD_G)
+    ts = []
+    with torch.cuda.stream(stream):
+        for i in range(warmup + reps):
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            outs = cp.cp_prefill(qc, kc, vc, T, world, rank, gather, attend, merge)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if i >= warmup:
+                ts.append(e0.elapsed_time(e1))
+    ctx.sync()
+    del outs
+    t = torch.tensor([statistics.median(ts)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    flops = 4 * HEADS * HD_G * (T * (T + 1) // 2)
+    tf = flops / ms / 1e9
+    return {"ms": round(ms, 3), "tflop": round(flops / 1e12, 3), "TFLOP_s_job": round(tf, 1),
+            "frac_of_peak_per_gpu": round(tf / world / pk["bf16"], 4), "ranks": world,
+            "schedule": "zigzag 2W chunks, NCCL all-gather of K/V on a side stream, LSE merge",
+            "timing": "CUDA events per repetition, median over reps, max over ranks"}
+
+
 def traffic_from_profile():
     """DRAM bytes per launch of the global decode kernel from the committed
     ncu summary, scaled by the workload ratio recorded there (or None)."""
@@ -507,6 +556,8 @@ def main():
     e2e_value = tokens * d["e2e_steps"] / e2e_s
 
     extras = {}
+    if dist is not None and not a.no_extras:
+        extras["prefill_cp"] = measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk)
     if rank == 0 and not a.no_extras:
         extras["decode_batch1"] = measure_batch1(torch, g4a, ctx, stream)
         extras["prefill"] = measure_prefill(torch, g4a, ctx, stream, pk)

@@ -1,0 +1,64 @@
+"""Context-parallel prefill on one GPU: every rank of a W-rank zigzag schedule
+is run in turn in this process, with the all-gather replaced by handing each
+rank the whole key/value sequence directly. The partial attention and the
+log-sum-exp merge are the CUDA library's (g4a_prefill with position offsets,
+g4a_lse_merge); the result must match the oracle's causal prefill of the whole
+sequence.
+
+Tolerance: max |diff| <= 2e-3 (bf16 inputs, as the single-launch prefill).
+"""
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helpers import max_abs_diff, rng, unit_rms_rows
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+@pytest.fixture(scope="module")
+def ctx(torch_cuda):
+    import g4attn
+    c = g4attn.Context(0)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("world,T", [(2, 512), (4, 512), (8, 1024)])
+def test_cp_prefill_matches_oracle(oracle, ctx, torch_cuda, world, T):
+    from g4attn import cp
+    torch = torch_cuda
+    hd = 512
+    r = rng(4000 + world)
+    q = oracle.round_bf16(unit_rms_rows(r.standard_normal((T, 8, hd)).astype(np.float32)))
+    k = oracle.round_bf16(unit_rms_rows(r.standard_normal((T, hd)).astype(np.float32)))
+    v = oracle.round_bf16(r.standard_normal((T, hd)).astype(np.float32))
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda().to(torch.bfloat16)
+    chunks = [cp.zigzag_chunks(T, world, rank) for rank in range(world)]
+    keys, values = dev(k), dev(v)
+    attend = cp.g4a_attend(ctx, torch, hd)
+    merge = cp.g4a_merge(ctx, torch, hd)
+    got = np.full((T, 8, hd), np.nan, np.float32)
+    for rank in range(world):
+        qc = [dev(q[a:b]) for a, b in chunks[rank]]
+        kc = [dev(k[a:b]) for a, b in chunks[rank]]
+        vc = [dev(v[a:b]) for a, b in chunks[rank]]
+        gather = lambda kc, vc: ((lambda: None), keys, values)
+        outs = cp.cp_prefill(qc, kc, vc, T, world, rank, gather, attend, merge)
+        ctx.sync()
+        for (a, b), o in zip(chunks[rank], outs):
+            got[a:b] = o.cpu().numpy()
+    want = oracle.prefill_attend(q, k, v, 8, 0)
+    assert max_abs_diff(got, want) <= TOL
