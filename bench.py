@@ -461,6 +461,42 @@ def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, w
             "timing": "CUDA events per repetition, median over reps, max over ranks"}
 
 
+def run_case(torch, g4a, spec: str, reps: int, warmup: int):
+    """One prefill problem on its own (for profiling one kernel on a small
+    case): spec "prefill:<head width>:<tokens>:<window>"."""
+    kind, hd, T, window = spec.split(":")
+    assert kind == "prefill", spec
+    hd, T, window = int(hd), int(T), int(window)
+    ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+
+    def unit(shape):
+        x = torch.randn(*shape, device="cuda", generator=gen)
+        return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
+
+    prob = dict(head_dim=hd, window=window, n_q=T, n_kv=T, q=unit((T, HEADS, hd)), k=unit((T, hd)),
+                v=torch.randn(T, hd, device="cuda", generator=gen).to(torch.bfloat16),
+                out=torch.empty(T, HEADS, hd, device="cuda"))
+    for _ in range(warmup):
+        ctx.prefill([prob])
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.prefill([prob])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ctx.sync()
+    ctx.close()
+    ms = statistics.median(ts)
+    flops = 4 * HEADS * hd * prefill_pairs(T, window)
+    print(json.dumps({"case": spec, "ms": round(ms, 4), "TFLOP_s": round(flops / ms / 1e9, 1)}), flush=True)
+
+
 def traffic_from_profile():
     """DRAM bytes per launch of the global decode kernel from the committed
     ncu summary, scaled by the workload ratio recorded there (or None)."""
@@ -488,7 +524,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-extras", action="store_true", help="skip the batch-1 and prefill sub-measurements")
+    ap.add_argument("--case", default=None,
+                    help='run one small case instead of the benchmark, e.g. "prefill:512:4096:0"')
     a = ap.parse_args()
+    if a.case:
+        import torch
+        import g4attn as g4a
+        run_case(torch, g4a, a.case, a.steps, a.warmup)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

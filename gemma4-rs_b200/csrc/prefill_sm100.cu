@@ -11,17 +11,20 @@
 // the head dimension of the output (head width 512 runs two CTAs per row tile
 // that each recompute S over the full width). Keys come in tiles of 128.
 //
-// Roles (192 threads):
+// Roles (320 threads):
 //   warp 0      TMA producer: Q once, then K and V boxes (64 columns x 128
 //               rows, 128-byte swizzle) through a ring of 16 KB slots.
 //   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma:
 //               S = Q K^T (bf16, f32 in TMEM, double-buffered 2 x 128 cols),
 //               O += P V (P fp16 read from TMEM, V fp16 from shared memory,
 //               N = 256, f32 accumulator in TMEM cols 0-255).
-//   warps 2-5   softmax: one TMEM lane (row) per thread; mask, row max,
-//               exp2, P written back into the S columns as fp16; the running
-//               max is rescaled lazily (only when it grows by more than 2^8),
-//               then the epilogue divides by the row sum and stores f32.
+//   warps 2-9   softmax: two threads per TMEM lane (row), each over 64 of
+//               the tile's 128 scores; mask (edge tiles only), row max
+//               agreed through a shared-memory mailbox, one FFMA + EX2 per
+//               score, P written back into the S columns as fp16; the
+//               running max is rescaled lazily (only when it grows by more
+//               than 2^8), then the epilogue divides by the row sum and
+//               stores f32, each thread 128 of the 256 output columns.
 // Every mbarrier wait is bounded; on time-out the CTA records an error flag,
 // drains its own TMA loads and MMAs, frees TMEM and exits.
 #include <cuda.h>
@@ -30,6 +33,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <vector>
 
@@ -45,7 +49,7 @@ constexpr int kTokensPerTile = 16;
 constexpr int kKeysPerTile = 128;   // tcgen05 N of S
 constexpr int kDV = 256;            // output columns per CTA
 constexpr int kBoxBytes = 128 * 128;  // 64 bf16 columns x 128 rows
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS0 = 256, kColS1 = 384;
 constexpr uint32_t kWaitLimit = 1u << 22;  // polls; far above any legitimate wait
@@ -67,10 +71,16 @@ struct Cfg {
     static constexpr int kRing = HD == 256 ? 8 : 4;  // slots; a multiple of 4 (V groups never wrap)
     static constexpr int kSmemQ = kQBoxes * kBoxBytes;
     static constexpr int kSmemRing = kRing * kBoxBytes;
-    static constexpr int kSmemBytes = kSmemQ + kSmemRing + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+    static constexpr int kSmemBytes = kSmemQ + kSmemRing + 5120 /*barriers, mailboxes*/ + 1024 /*alignment slack*/;
+};
+
+struct alignas(8) Mailbox {
+    int seq;  // tile index the value belongs to
+    float v;
 };
 
 struct Barriers {
+    Mailbox box[2][2][128];  // [seq parity][column half][row]
     uint64_t q_full;
     uint64_t s_full[2];
     uint64_t p_full[2];
@@ -94,6 +104,8 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     return false;
 }
 
+static_assert(sizeof(Barriers) <= 5120, "barrier region");
+
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
@@ -114,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_init(&bars->q_full, 1);
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&bars->s_full[i], 1);
-            ptx::mbar_init(&bars->p_full[i], 128);
+            ptx::mbar_init(&bars->p_full[i], 256);
         }
         ptx::mbar_init(&bars->o_done, 1);
         ptx::mbar_init(&bars->mma_done, 1);
@@ -124,6 +136,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         bars->abort = 0;
         ptx::fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < 2 * 2 * kRows; i += blockDim.x) {
+        bars->box[i / (2 * kRows)][(i / kRows) & 1][i % kRows] = Mailbox{-1, 0.0f};
     }
     if (warp == 1) {
         ptx::tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -261,17 +276,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ softmax + epilogue
+        // Two warpgroups: warp w reaches TMEM lanes 32*(w%4).., so warps w and
+        // w+4 share a quadrant of rows and split each row's 128 scores (and
+        // its 256 output columns) in halves. They agree on the row max
+        // through a per-row shared-memory mailbox (no named barrier, so that
+        // either side can give up alone after a bounded wait).
         const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
+        const int half = (warp - 2) >> 2;           // column half of S and of O
         const int row = quad * 32 + lane;           // tile row = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const int tok = it.q_tile * kTokensPerTile + row / 8;
         const int head = row % 8;
         const bool row_valid = tok < pb.n_q;
         const int qpos = pb.q_pos0 + tok;
+        // visible key indices of this row: [vis_lo, vis_hi]
+        const int vis_hi = min(qpos - pb.kv_pos0, pb.n_kv - 1);
+        const int vis_lo = pb.window > 0 ? qpos - pb.window + 1 - pb.kv_pos0 : INT_MIN / 2;
+        // the CTA's first and last query positions (rows past n_q included)
+        const int q_first = pb.q_pos0 + it.q_tile * kTokensPerTile;
+        const int q_last = q_first + kTokensPerTile - 1;
         const float kLog2e = 1.4426950408889634f;
-        float m_used = -CUDART_INF_F;  // running max in log2 units
-        float l = 0.0f;
+        float m_used = -CUDART_INF_F;  // running reference max, log2 units
+        float l = 0.0f;                // this half's row sum
         bool ok = true;
+        Mailbox *my_box = &bars->box[0][half][row];
+        Mailbox *other_box = &bars->box[0][half ^ 1][row];
+        // Post (seq, v) and read the partner's value for the same seq.
+        auto swap = [&](int seq, float v, float *out) -> bool {
+            const int par = seq & 1;
+            const uint32_t mine = ptx::smem_u32(my_box + par * 2 * kRows);
+            const uint32_t theirs = ptx::smem_u32(other_box + par * 2 * kRows);
+            // one 8-byte store: the partner sees seq and value together
+            asm volatile("st.volatile.shared.v2.b32 [%0], {%1, %2};" ::"r"(mine), "r"(seq), "f"(v) : "memory");
+            for (uint32_t i = 0; i < kWaitLimit; i++) {
+                int ts;
+                float tv;
+                asm volatile("ld.volatile.shared.v2.b32 {%0, %1}, [%2];" : "=r"(ts), "=f"(tv) : "r"(theirs) : "memory");
+                if (ts == seq) {
+                    *out = tv;
+                    return true;
+                }
+                if ((i & 255) == 255 && *abort) return false;
+            }
+            *abort = 1;
+            atomicOr(err, 2);
+            return false;
+        };
         // tcgen05.ld/st are warp-collective (.sync.aligned): every branch that
         // contains one is decided by a warp vote, never per row.
         for (int j = 0; j < n_tiles && ok; j++) {
@@ -281,26 +331,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             ptx::tc_fence_after();
             const uint32_t s_addr = tmem + lane_addr + ((j & 1) ? kColS1 : kColS0);
-            float s[kKeysPerTile];
+            uint32_t r0[32], r1[32];
+            ptx::tmem_ld32(s_addr + 64 * half, r0);
+            ptx::tmem_ld32(s_addr + 64 * half + 32, r1);
+            ptx::tmem_wait_ld();
+            ptx::tmem_ld_fence(r0);
+            ptx::tmem_ld_fence(r1);
+            float s[64];
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                uint32_t r[32];
-                ptx::tmem_ld32(s_addr + 32 * c, r);
-                ptx::tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; i++) s[32 * c + i] = __uint_as_float(r[i]);
+            for (int i = 0; i < 32; i++) {
+                s[i] = __uint_as_float(r0[i]);
+                s[32 + i] = __uint_as_float(r1[i]);
             }
-            const int k0 = (it.kv_tile_lo + j) * kKeysPerTile;
-            float mx = -CUDART_INF_F;
+            const int k0 = (it.kv_tile_lo + j) * kKeysPerTile;  // first key index of the tile
+            // Masking only where some key of the tile is invisible to some row.
+            const int kp0 = pb.kv_pos0 + k0;
+            const bool edge = k0 + kKeysPerTile > pb.n_kv || kp0 + kKeysPerTile - 1 > q_first ||
+                              (pb.window > 0 && q_last - kp0 >= pb.window);
+            if (edge) {
+                const int kb = k0 + 64 * half;
+                const int lo = vis_lo - kb, hi = vis_hi - kb;  // visible i in [lo, hi]
 #pragma unroll
-            for (int i = 0; i < kKeysPerTile; i++) {
-                const int kidx = k0 + i;
-                const int kpos = pb.kv_pos0 + kidx;
-                const bool valid =
-                    row_valid && kidx < pb.n_kv && kpos <= qpos && (pb.window == 0 || qpos - kpos < pb.window);
-                s[i] = valid ? s[i] * kLog2e : -CUDART_INF_F;
-                mx = fmaxf(mx, s[i]);
+                for (int i = 0; i < 64; i++) s[i] = (i >= lo && i <= hi) ? s[i] : -CUDART_INF_F;
             }
+            float mx = s[0];
+#pragma unroll
+            for (int i = 1; i < 64; i++) mx = fmaxf(mx, s[i]);
+            float mo;
+            if (!__all_sync(0xffffffffu, swap(j, mx, &mo))) {
+                ok = false;
+                break;
+            }
+            mx = fmaxf(mx, mo) * kLog2e;
             // Lazy rescale: move this row's reference max only when the tile
             // max exceeds it by more than 8 (P then stays below 2^8).
             const bool grow = mx > m_used + 8.0f;
@@ -313,53 +375,60 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ptx::tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < kDV / 32; c++) {
+                for (int c = 0; c < kDV / 64; c++) {
                     uint32_t r[32];
-                    ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
+                    const uint32_t o_addr = tmem + lane_addr + kColO + 128 * half + 32 * c;
+                    ptx::tmem_ld32(o_addr, r);
                     ptx::tmem_wait_ld();
+                    ptx::tmem_ld_fence(r);
 #pragma unroll
                     for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-                    ptx::tmem_st32(tmem + lane_addr + kColO + 32 * c, r);
+                    ptx::tmem_st32(o_addr, r);
                 }
                 ptx::tmem_wait_st();
                 l *= f;
             }
             if (grow) m_used = mx;
-            uint32_t pk[kKeysPerTile / 2];
-            float rs = 0.0f;
+            // p = 2^(s*log2e - m); masked scores are -inf and give 0. A row
+            // with no visible key so far keeps m = -inf; subtract 0 then.
+            const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
+            uint32_t pk[32];
+            float rs0 = 0.0f, rs1 = 0.0f;
 #pragma unroll
-            for (int i = 0; i < kKeysPerTile / 2; i++) {
-                const float p0 = s[2 * i] == -CUDART_INF_F ? 0.0f : ptx::ex2(s[2 * i] - m_used);
-                const float p1 = s[2 * i + 1] == -CUDART_INF_F ? 0.0f : ptx::ex2(s[2 * i + 1] - m_used);
-                rs += p0 + p1;
+            for (int i = 0; i < 32; i++) {
+                const float p0 = ptx::ex2(fmaf(s[2 * i], kLog2e, neg_m));
+                const float p1 = ptx::ex2(fmaf(s[2 * i + 1], kLog2e, neg_m));
+                rs0 += p0;
+                rs1 += p1;
                 pk[i] = ptx::pack_half2(p0, p1);
             }
-            l += rs;
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                uint32_t r[32];
-#pragma unroll
-                for (int i = 0; i < 32; i++) r[i] = pk[32 * c + i];
-                ptx::tmem_st32(s_addr + 32 * c, r);
-            }
+            l += rs0 + rs1;
+            // P (fp16 pairs) goes over the first 64 columns of this S buffer;
+            // half 1's columns 32-63 were read by half 0 before it posted its
+            // max, which half 1 has seen.
+            ptx::tmem_st32(s_addr + 32 * half, pk);
             ptx::tmem_wait_st();
             ptx::tc_fence_before();
             ptx::mbar_arrive(&bars->p_full[j & 1]);
         }
         // ---- epilogue: O / l (TMEM loads by the whole warp, stores per row) ----
+        float lo_ = 0.0f;
+        if (ok && !__all_sync(0xffffffffu, swap(n_tiles, l, &lo_))) ok = false;
+        l += lo_;
         if (ok && n_tiles > 0 &&
             !__all_sync(0xffffffffu, wait_bar(&bars->o_done, (uint32_t)(n_tiles - 1) & 1u, abort, err)))
             ok = false;
         ptx::tc_fence_after();
         if (ok) {
-            float *dst = pb.out + ((size_t)tok * 8 + head) * HD + it.dv_half * kDV;
+            float *dst = pb.out + ((size_t)tok * 8 + head) * HD + it.dv_half * kDV + 128 * half;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll 1
-            for (int c = 0; c < kDV / 32; c++) {
+            for (int c = 0; c < kDV / 64; c++) {
                 uint32_t r[32];
                 if (n_tiles > 0) {
-                    ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
+                    ptx::tmem_ld32(tmem + lane_addr + kColO + 128 * half + 32 * c, r);
                     ptx::tmem_wait_ld();
+                    ptx::tmem_ld_fence(r);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i++) r[i] = 0u;
@@ -373,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            if (row_valid && pb.lse && it.dv_half == 0)
+            if (row_valid && pb.lse && it.dv_half == 0 && half == 0)
                 pb.lse[(size_t)tok * 8 + head] = l > 0.0f ? (m_used + log2f(l)) * 0.6931471805599453f : -CUDART_INF_F;
         }
     }

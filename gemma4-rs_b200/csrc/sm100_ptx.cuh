@@ -116,6 +116,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Orders every use of registers filled by tcgen05.ld after the preceding
+// tcgen05.wait::ld: the empty volatile asm statements stay in program order
+// with the wait, and each one "redefines" its register.
+__device__ __forceinline__ void tmem_ld_fence(uint32_t (&r)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---- descriptors ----
