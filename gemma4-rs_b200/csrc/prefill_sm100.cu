@@ -5,28 +5,42 @@
 // keys [max(0, t+1-window), t] (crates/llm-gemma4/src/eng/mod.rs:10-36), with
 // one batched kernel over bf16 inputs and f32 accumulation.
 //
-// Tiling. A CTA owns 16 query tokens x 8 heads = 128 rows (the tcgen05 M
-// dimension), so each K/V tile it loads serves all 8 heads of the single KV
-// head (grouped-query reuse without any multicast), and one 256-wide half of
-// the head dimension of the output (head width 512 runs two CTAs per row tile
-// that each recompute S over the full width). Keys come in tiles of 128.
+// Tiling. A cluster of two CTAs (a "pair", one per SM) owns 32 query tokens x
+// 8 heads = 256 rows and runs the CTA-pair form of tcgen05.mma (M = 256):
+// each CTA holds 128 rows (16 tokens x 8 heads) of Q in its shared memory and
+// of S and O in its TMEM, and each CTA loads only HALF of every K/V tile (its
+// 64 of the tile's 128 keys for S = Q K^T, its 128 of the pair's 256 output
+// columns for O += P V); the tensor cores of the pair exchange the B halves.
+// All 8 heads of a row tile share the single KV head (grouped-query reuse, no
+// multicast anywhere). Head width 512 runs two pairs per row tile, one per
+// 256-wide half of the output, each recomputing S over the full width.
 //
-// Roles (320 threads):
-//   warp 0      TMA producer: Q once, then K and V boxes (64 columns x 128
-//               rows, 128-byte swizzle) through a ring of 16 KB slots.
-//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma:
-//               S = Q K^T (bf16, f32 in TMEM, double-buffered 2 x 128 cols),
-//               O += P V (P fp16 read from TMEM, V fp16 from shared memory,
-//               N = 256, f32 accumulator in TMEM cols 0-255).
-//   warps 2-9   softmax: two threads per TMEM lane (row), each over 64 of
-//               the tile's 128 scores; mask (edge tiles only), row max
-//               agreed through a shared-memory mailbox, one FFMA + EX2 per
-//               score, P written back into the S columns as fp16; the
+// Roles (352 threads per CTA):
+//   warp 0      TMA producer: Q once, then K and V boxes (64 columns x 64
+//               rows, 128-byte swizzle) through a ring of 8 KB slots in the
+//               fixed order K(0), K(1), V(0), K(2), V(1), ... Both CTAs fill
+//               the same slot sequence; every load signals the LEADER CTA's
+//               ring barrier, which expects the pair's bytes.
+//   warp 1      allocates 512 TMEM columns (pair allocation); in the leader,
+//               one thread issues S(j) = Q K(j)^T (bf16, f32 in TMEM,
+//               double-buffered 2 x 128 columns).
+//   warp 10     in the leader, one thread issues O += P(j) V(j) (P fp16 from
+//               TMEM, V fp16 from shared memory, N = 256, f32 accumulator in
+//               TMEM columns 0-255). Two issuing threads keep the tensor pipe
+//               fed while either one waits on a barrier: a barrier wait in
+//               the issuing thread stalls its MMA stream for about a hundred
+//               cycles, as long as an M = 128, N = 128 MMA.
+//   warps 2-9   softmax on the CTA's own rows: two threads per TMEM lane
+//               (row), each over 64 of the tile's 128 scores; mask (edge
+//               tiles only), row max agreed through a shared-memory mailbox,
+//               one FFMA + EX2 per score, P written back into the S columns
+//               as fp16, then an arrive on the leader's P barrier; the
 //               running max is rescaled lazily (only when it grows by more
-//               than 2^8), then the epilogue divides by the row sum and
-//               stores f32, each thread 128 of the 256 output columns.
+//               than 2^8); the epilogue divides by the row sum and stores
+//               f32, each thread 128 of the 256 output columns.
 // Every mbarrier wait is bounded; on time-out the CTA records an error flag,
-// drains its own TMA loads and MMAs, frees TMEM and exits.
+// drains what it can, frees TMEM and exits (after the pair's final cluster
+// barrier, so that no MMA still reads its shared memory).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -44,34 +58,48 @@
 namespace g4a {
 namespace {
 
-constexpr int kRows = 128;          // tcgen05 M: 16 tokens x 8 heads
-constexpr int kTokensPerTile = 16;
-constexpr int kKeysPerTile = 128;   // tcgen05 N of S
-constexpr int kDV = 256;            // output columns per CTA
-constexpr int kBoxBytes = 128 * 128;  // 64 bf16 columns x 128 rows
-constexpr int kThreads = 320;
+constexpr int kRows = 128;            // rows per CTA: 16 tokens x 8 heads
+constexpr int kTokensPerCta = 16;
+constexpr int kTokensPerPair = 32;
+constexpr int kKeysPerTile = 128;     // N of S for the pair
+constexpr int kDV = 256;              // output columns per pair
+constexpr int kQBoxBytes = 128 * 128; // 64 bf16 columns x 128 rows
+constexpr int kSlotBytes = 64 * 128;  // 64 columns x 64 rows (bf16 / fp16)
+constexpr int kThreads = 352;
+constexpr int kPvWarp = 10;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS0 = 256, kColS1 = 384;
 constexpr uint32_t kWaitLimit = 1u << 22;  // polls; far above any legitimate wait
+constexpr uint16_t kBothCtas = 0x3;
 
 struct alignas(64) ProblemDev {
-    CUtensorMap tq, tk, tv;  // Q [n_q*8, hd] bf16, K [n_kv, hd] bf16, V [n_kv, hd] fp16
+    CUtensorMap tq, tk, tv;  // Q [n_q*8, hd] bf16 (128-row boxes), K [n_kv, hd] bf16, V [n_kv, hd] fp16 (64-row boxes)
     int32_t hd, window, n_q, q_pos0, n_kv, kv_pos0;
     float *out;
     float *lse;
 };
 
 struct WorkItem {
-    int32_t problem, q_tile, dv_half, kv_tile_lo, n_kv_tiles, pad;
+    int32_t problem, q_tile, dv_half, kv_tile_lo, n_kv_tiles, pad;  // q_tile: 32-token tile of the pair
 };
 
 template <int HD>
 struct Cfg {
-    static constexpr int kQBoxes = HD / 64;
-    static constexpr int kRing = HD == 256 ? 8 : 4;  // slots; a multiple of 4 (V groups never wrap)
-    static constexpr int kSmemQ = kQBoxes * kBoxBytes;
-    static constexpr int kSmemRing = kRing * kBoxBytes;
+    static constexpr int kQBoxes = HD / 64;   // Q boxes per CTA
+    static constexpr int kKBoxes = HD / 64;   // K boxes per CTA per tile (64 keys each)
+    static constexpr int kVBoxes = 4;         // 2 column atoms x 2 key halves
+    // Slots: even, so that the two column atoms of a V half (pushed as an
+    // aligned pair after an even number of K boxes) never wrap.
+    static constexpr int kRing = HD == 256 ? 18 : 10;
+    static constexpr int kSmemQ = kQBoxes * kQBoxBytes;
+    static constexpr int kSmemRing = kRing * kSlotBytes;
     static constexpr int kSmemBytes = kSmemQ + kSmemRing + 5120 /*barriers, mailboxes*/ + 1024 /*alignment slack*/;
+    static_assert(kKBoxes % 2 == 0 && kRing % 2 == 0, "V atom pairs must not wrap");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    // Position of the first box of K(j) / V(j) in the push sequence
+    // K(0), K(1), V(0), K(2), V(1), ..., K(n-1), V(n-2), V(n-1).
+    __device__ static int k_pos(int j) { return j == 0 ? 0 : kKBoxes + (j - 1) * (kKBoxes + kVBoxes); }
+    __device__ static int v_pos(int j, int n) { return kKBoxes + j * (kKBoxes + kVBoxes) + (j + 1 < n ? kKBoxes : 0); }
 };
 
 struct alignas(8) Mailbox {
@@ -81,22 +109,26 @@ struct alignas(8) Mailbox {
 
 struct Barriers {
     Mailbox box[2][2][128];  // [seq parity][column half][row]
-    uint64_t q_full;
-    uint64_t s_full[2];
-    uint64_t p_full[2];
-    uint64_t o_done;
-    uint64_t mma_done;
-    uint64_t ring_full[8];
-    uint64_t ring_empty[8];
+    uint64_t q_full;         // leader: both CTAs' Q bytes
+    uint64_t s_full[2];      // both: S buffer ready (pair commit)
+    uint64_t p_full[2];      // leader: 256 arrivals from each CTA
+    uint64_t pv_done[2];     // leader: PV of the tile in this S buffer done (P buffer free)
+    uint64_t o_done;         // both: PV of the latest tile done (pair commit)
+    uint64_t mma_done;       // both: every MMA of the pair done (one commit per issuer)
+    uint64_t ring_full[18];  // leader: both CTAs' bytes of the slot
+    uint64_t ring_empty[18]; // both: slot consumed (pair commit)
     uint32_t tmem_base;
     int abort;
 };
 
+static_assert(sizeof(Barriers) <= 5120, "barrier region");
+
 // Bounded wait: false if another role aborted or the limit ran out (which
 // aborts the CTA and records bit 1 of the error flag).
+template <bool kCluster = false>
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
     for (uint32_t i = 0; i < kWaitLimit; i++) {
-        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if (kCluster ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity)) return true;
         if ((i & 1023) == 1023 && *abort) return false;
     }
     *abort = 1;
@@ -104,10 +136,8 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     return false;
 }
 
-static_assert(sizeof(Barriers) <= 5120, "barrier region");
-
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
     using C = Cfg<HD>;
     extern __shared__ uint8_t smem_raw[];
@@ -117,7 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     Barriers *bars = reinterpret_cast<Barriers *>(ring + C::kSmemRing);
     volatile int *abort = &bars->abort;
 
-    const WorkItem it = items[blockIdx.x];
+    const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader
+    const WorkItem it = items[blockIdx.x >> 1];
     const ProblemDev &pb = problems[it.problem];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = it.n_kv_tiles;
@@ -126,10 +157,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_init(&bars->q_full, 1);
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&bars->s_full[i], 1);
-            ptx::mbar_init(&bars->p_full[i], 256);
+            ptx::mbar_init(&bars->p_full[i], 2 * 256);
+            ptx::mbar_init(&bars->pv_done[i], 1);
         }
         ptx::mbar_init(&bars->o_done, 1);
-        ptx::mbar_init(&bars->mma_done, 1);
+        ptx::mbar_init(&bars->mma_done, 2);
         for (int i = 0; i < C::kRing; i++) {
             ptx::mbar_init(&bars->ring_full[i], 1);
             ptx::mbar_init(&bars->ring_empty[i], 1);
@@ -137,17 +169,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->abort = 0;
         ptx::fence_mbar_init();
     }
-    for (int i = threadIdx.x; i < 2 * 2 * kRows; i += blockDim.x) {
+    for (int i = threadIdx.x; i < 2 * 2 * kRows; i += blockDim.x)
         bars->box[i / (2 * kRows)][(i / kRows) & 1][i % kRows] = Mailbox{-1, 0.0f};
-    }
     if (warp == 1) {
-        ptx::tmem_alloc(&bars->tmem_base, kTmemCols);
-        ptx::tmem_relinquish();
+        ptx::tmem_alloc2(&bars->tmem_base, kTmemCols);
+        ptx::tmem_relinquish2();
     }
     ptx::tc_fence_before();
     __syncthreads();
+    ptx::cluster_sync();  // barrier inits of both CTAs visible before any remote signal
     ptx::tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+
+    // slot / phase of push-sequence position pos
+    auto slot_of = [](int pos) { return pos % C::kRing; };
+    auto phase_of = [](int pos) { return (uint32_t)(pos / C::kRing) & 1u; };
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -155,9 +191,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::prefetch_tmap(&pb.tq);
             ptx::prefetch_tmap(&pb.tk);
             ptx::prefetch_tmap(&pb.tv);
-            ptx::mbar_arrive_expect_tx(&bars->q_full, C::kSmemQ);
+            if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * C::kSmemQ);
+            const uint32_t q_full_l = ptx::mapa(&bars->q_full, 0);
             for (int c = 0; c < C::kQBoxes; c++)
-                ptx::tma_load_2d(q_smem + c * kBoxBytes, &pb.tq, &bars->q_full, 64 * c, it.q_tile * kRows);
+                ptx::tma_load_2d_pair(q_smem + c * kQBoxBytes, &pb.tq, q_full_l, 64 * c,
+                                      it.q_tile * 2 * kRows + (int)rank * kRows);
             int slot = 0;
             uint32_t phase = 0;
             uint32_t issued = 0;  // bit s: slot s received at least one load
@@ -168,110 +206,121 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     return;
                 }
-                ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], kBoxBytes);
-                ptx::tma_load_2d(ring + slot * kBoxBytes, m, &bars->ring_full[slot], x, y);
+                if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * kSlotBytes);
+                ptx::tma_load_2d_pair(ring + slot * kSlotBytes, m, ptx::mapa(&bars->ring_full[slot], 0), x, y);
                 issued |= 1u << slot;
                 if (++slot == C::kRing) {
                     slot = 0;
                     phase ^= 1u;
                 }
             };
+            // K: this CTA's 64 keys of the tile, all HD columns
             auto push_k = [&](int j) {
-                for (int c = 0; c < C::kQBoxes; c++) push(&pb.tk, 64 * c, (it.kv_tile_lo + j) * kKeysPerTile);
+                const int y = (it.kv_tile_lo + j) * kKeysPerTile + 64 * (int)rank;
+                for (int c = 0; c < C::kKBoxes; c++) push(&pb.tk, 64 * c, y);
             };
+            // V: this CTA's 128 output columns (two 64-column atoms), keys in two halves
             auto push_v = [&](int j) {
-                for (int c = 0; c < kDV / 64; c++)
-                    push(&pb.tv, it.dv_half * kDV + 64 * c, (it.kv_tile_lo + j) * kKeysPerTile);
+                const int x = it.dv_half * kDV + 128 * (int)rank;
+                for (int kh = 0; kh < 2; kh++)
+                    for (int a = 0; a < 2; a++) push(&pb.tv, x + 64 * a, (it.kv_tile_lo + j) * kKeysPerTile + 64 * kh);
             };
             push_k(0);
             for (int j = 0; j < n_tiles && ok; j++) {
                 if (j + 1 < n_tiles) push_k(j + 1);
                 push_v(j);
             }
-            // Drain: no TMA write may land after the CTA exits. Normally the
-            // MMA thread already waited for every load; after an abort, wait
-            // here (bounded) for Q and for each slot's latest load.
-            for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->q_full, 0); i++) {
-            }
-            if (!ok || *abort) {
-                for (int s = 0; s < C::kRing; s++) {
-                    if (!(issued >> s & 1u)) continue;
-                    const uint32_t ph = s < slot ? phase : phase ^ 1u;
-                    for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->ring_full[s], ph); i++) {
+            // Drain (leader): every load of both CTAs signals the leader's
+            // barriers; no TMA write may land after the pair exits. Normally
+            // the MMA threads already waited for every load; after an abort,
+            // wait here (bounded) for Q and for each slot's latest load.
+            if (rank == 0) {
+                for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->q_full, 0); i++) {
+                }
+                if (!ok || *abort) {
+                    for (int s = 0; s < C::kRing; s++) {
+                        if (!(issued >> s & 1u)) continue;
+                        const uint32_t ph = s < slot ? phase : phase ^ 1u;
+                        for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->ring_full[s], ph); i++) {
+                        }
                     }
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, kRows, kKeysPerTile);
-            constexpr uint32_t kIdescPV = ptx::idesc_f16(0, 0, 1, kRows, kDV);
-            const uint32_t q_base = ptx::smem_u32(q_smem);
-            const uint32_t ring_base = ptx::smem_u32(ring);
-            int slot = 0;
-            uint32_t phase = 0;
+    } else if (warp == 1 || warp == kPvWarp) {
+        // ------------------------------------------------------------ MMA issuers (leader)
+        // Base descriptors: the address field holds (address >> 4) in its low
+        // 14 bits and every operand lies below 256 KB of shared memory, so a
+        // byte offset is added as (offset >> 4) without a carry out of it.
+        const uint64_t q_desc = ptx::smem_desc(ptx::smem_u32(q_smem), 16, 1024);
+        const uint64_t k_desc = ptx::smem_desc(ptx::smem_u32(ring), 16, 1024);
+        const uint64_t v_desc = ptx::smem_desc(ptx::smem_u32(ring), kSlotBytes, 1024);
+        if (lane == 0 && rank == 0) {
             bool ok = n_tiles > 0 && wait_bar(&bars->q_full, 0, abort, err);
-            if (ok) ptx::tc_fence_after();
-            auto advance = [&](int n) {
-                slot += n;
-                if (slot >= C::kRing) {
-                    slot -= C::kRing;
-                    phase ^= 1u;
-                }
-            };
-            auto issue_s = [&](int j) {
-                const uint32_t d = tmem + ((j & 1) ? kColS1 : kColS0);
-                for (int c = 0; c < C::kQBoxes && ok; c++) {
-                    if (!wait_bar(&bars->ring_full[slot], phase, abort, err)) {
+            if (warp == 1) {
+                // S(j) = Q K(j)^T into S buffer j&1, once PV(j-2) has read P(j-2) from it
+                constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, 2 * kRows, kKeysPerTile);
+                for (int j = 0; j < n_tiles && ok; j++) {
+                    if (j >= 2 && !wait_bar(&bars->pv_done[j & 1], (uint32_t)((j - 2) >> 1) & 1u, abort, err)) {
                         ok = false;
-                        return;
+                        break;
                     }
                     ptx::tc_fence_after();
-                    const uint32_t kb = ring_base + slot * kBoxBytes;
-                    const uint32_t qb = q_base + c * kBoxBytes;
+                    const uint32_t d = tmem + ((j & 1) ? kColS1 : kColS0);
+                    const int pos = C::k_pos(j);
+                    for (int c = 0; c < C::kKBoxes && ok; c++) {
+                        const int slot = slot_of(pos + c);
+                        if (!wait_bar(&bars->ring_full[slot], phase_of(pos + c), abort, err)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        const uint64_t kd = k_desc + (uint64_t)(slot * (kSlotBytes >> 4));
+                        const uint64_t qd = q_desc + (uint64_t)(c * (kQBoxBytes >> 4));
+                        ptx::mma2_ss(d, qd, kd, kIdescS, c != 0);
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        ptx::mma_ss(d, ptx::smem_desc(qb + 32 * kk, 16, 1024), ptx::smem_desc(kb + 32 * kk, 16, 1024),
-                                    kIdescS, (c | kk) != 0);
+                        for (int kk = 1; kk < 4; kk++) ptx::mma2_ss(d, qd + 2 * kk, kd + 2 * kk, kIdescS, 1);
+                        ptx::mma2_commit_pair(&bars->ring_empty[slot], kBothCtas);
                     }
-                    ptx::mma_commit(&bars->ring_empty[slot]);
-                    advance(1);
+                    if (ok) ptx::mma2_commit_pair(&bars->s_full[j & 1], kBothCtas);
                 }
-                ptx::mma_commit(&bars->s_full[j & 1]);
-            };
-            auto issue_pv = [&](int j) {
-                if (!wait_bar(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, abort, err)) {
-                    ok = false;
-                    return;
-                }
-                for (int c = 0; c < 4; c++)
-                    if (!wait_bar(&bars->ring_full[slot + c], phase, abort, err)) {
-                        ok = false;
-                        return;
-                    }
-                ptx::tc_fence_after();
-                const uint32_t vb = ring_base + slot * kBoxBytes;
-                const uint32_t p_tmem = tmem + ((j & 1) ? kColS1 : kColS0);
-#pragma unroll
-                for (int ks = 0; ks < kKeysPerTile / 16; ks++) {
-                    ptx::mma_ts(tmem + kColO, p_tmem + 8 * ks, ptx::smem_desc(vb + 2048 * ks, kBoxBytes, 1024),
-                                kIdescPV, (j > 0 || ks > 0));
-                }
-                for (int c = 0; c < 4; c++) ptx::mma_commit(&bars->ring_empty[slot + c]);
-                ptx::mma_commit(&bars->o_done);
-                advance(4);
-            };
-            if (ok) {
-                issue_s(0);
+            } else {
+                // O += P(j) V(j) once the softmax of both CTAs published P(j)
+                constexpr uint32_t kIdescPV = ptx::idesc_f16(0, 0, 1, 2 * kRows, kDV);
                 for (int j = 0; j < n_tiles && ok; j++) {
-                    if (j + 1 < n_tiles) issue_s(j + 1);
-                    if (ok) issue_pv(j);
+                    if (!wait_bar<true>(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, abort, err)) {
+                        ok = false;
+                        break;
+                    }
+                    const int pos = C::v_pos(j, n_tiles);
+                    for (int c = 0; c < C::kVBoxes && ok; c++)
+                        ok = wait_bar(&bars->ring_full[slot_of(pos + c)], phase_of(pos + c), abort, err);
+                    if (!ok) break;
+                    ptx::tc_fence_after();
+                    const uint32_t p_tmem = tmem + ((j & 1) ? kColS1 : kColS0);
+                    // keys 16ks.. live in V half ks/4: slots pos + 2*(ks/4) (+1 = second column atom)
+                    const uint64_t vd0 = v_desc + (uint64_t)(slot_of(pos) * (kSlotBytes >> 4));
+                    const uint64_t vd1 = v_desc + (uint64_t)(slot_of(pos + 2) * (kSlotBytes >> 4));
+                    ptx::mma2_ts(tmem + kColO, p_tmem, vd0, kIdescPV, j > 0);
+#pragma unroll
+                    for (int ks = 1; ks < kKeysPerTile / 16; ks++)
+                        ptx::mma2_ts(tmem + kColO, p_tmem + 8 * ks, (ks < 4 ? vd0 : vd1) + (2048 >> 4) * (ks & 3),
+                                     kIdescPV, 1);
+                    for (int c = 0; c < C::kVBoxes; c++)
+                        ptx::mma2_commit_pair(&bars->ring_empty[slot_of(pos + c)], kBothCtas);
+                    ptx::mma2_commit_pair(&bars->pv_done[j & 1], 0x1);
+                    ptx::mma2_commit_pair(&bars->o_done, kBothCtas);
                 }
             }
-            // Every issued MMA completes before TMEM is released.
-            ptx::mma_commit(&bars->mma_done);
+            // Every MMA this thread issued completes before either CTA
+            // releases TMEM or exits (mma_done expects one commit per issuer).
+            ptx::mma2_commit_pair(&bars->mma_done, kBothCtas);
             for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->mma_done, 0); i++) {
+            }
+        } else if (warp == 1 && lane == 0 && n_tiles > 0) {
+            // non-leader: wait (bounded) for the leader's final commits
+            for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->mma_done, 0); i++) {
+                if ((i & 1023) == 1023 && *abort) break;
             }
         }
     } else {
@@ -285,17 +334,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = (warp - 2) >> 2;           // column half of S and of O
         const int row = quad * 32 + lane;           // tile row = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-        const int tok = it.q_tile * kTokensPerTile + row / 8;
+        const int tok0 = it.q_tile * kTokensPerPair + (int)rank * kTokensPerCta;  // this CTA's first token
+        const int tok = tok0 + row / 8;
         const int head = row % 8;
         const bool row_valid = tok < pb.n_q;
         const int qpos = pb.q_pos0 + tok;
         // visible key indices of this row: [vis_lo, vis_hi]
         const int vis_hi = min(qpos - pb.kv_pos0, pb.n_kv - 1);
         const int vis_lo = pb.window > 0 ? qpos - pb.window + 1 - pb.kv_pos0 : INT_MIN / 2;
-        // the CTA's first and last query positions (rows past n_q included)
-        const int q_first = pb.q_pos0 + it.q_tile * kTokensPerTile;
-        const int q_last = q_first + kTokensPerTile - 1;
+        // this CTA's first and last query positions (rows past n_q included)
+        const int q_first = pb.q_pos0 + tok0;
+        const int q_last = q_first + kTokensPerCta - 1;
         const float kLog2e = 1.4426950408889634f;
+        const uint32_t p_full_l0 = ptx::mapa(&bars->p_full[0], 0), p_full_l1 = ptx::mapa(&bars->p_full[1], 0);
         float m_used = -CUDART_INF_F;  // running reference max, log2 units
         float l = 0.0f;                // this half's row sum
         bool ok = true;
@@ -306,14 +357,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int par = seq & 1;
             const uint32_t mine = ptx::smem_u32(my_box + par * 2 * kRows);
             const uint32_t theirs = ptx::smem_u32(other_box + par * 2 * kRows);
-            // one 8-byte store: the partner sees seq and value together
-            asm volatile("st.volatile.shared.v2.b32 [%0], {%1, %2};" ::"r"(mine), "r"(seq), "f"(v) : "memory");
+            // one 8-byte scalar store: the partner sees seq and value together
+            const uint64_t word = (uint64_t)(uint32_t)seq | ((uint64_t)__float_as_uint(v) << 32);
+            asm volatile("st.volatile.shared.b64 [%0], %1;" ::"r"(mine), "l"(word) : "memory");
             for (uint32_t i = 0; i < kWaitLimit; i++) {
-                int ts;
-                float tv;
-                asm volatile("ld.volatile.shared.v2.b32 {%0, %1}, [%2];" : "=r"(ts), "=f"(tv) : "r"(theirs) : "memory");
-                if (ts == seq) {
-                    *out = tv;
+                uint64_t t;
+                asm volatile("ld.volatile.shared.b64 %0, [%1];" : "=l"(t) : "r"(theirs) : "memory");
+                if ((int)(uint32_t)t == seq) {
+                    *out = __uint_as_float((uint32_t)(t >> 32));
                     return true;
                 }
                 if ((i & 255) == 255 && *abort) return false;
@@ -344,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 s[32 + i] = __uint_as_float(r1[i]);
             }
             const int k0 = (it.kv_tile_lo + j) * kKeysPerTile;  // first key index of the tile
-            // Masking only where some key of the tile is invisible to some row.
+            // Masking only where some key of the tile is invisible to some row of this CTA.
             const int kp0 = pb.kv_pos0 + k0;
             const bool edge = k0 + kKeysPerTile > pb.n_kv || kp0 + kKeysPerTile - 1 > q_first ||
                               (pb.window > 0 && q_last - kp0 >= pb.window);
@@ -409,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tmem_st32(s_addr + 32 * half, pk);
             ptx::tmem_wait_st();
             ptx::tc_fence_before();
-            ptx::mbar_arrive(&bars->p_full[j & 1]);
+            ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);  // the leader's barrier (release, cluster scope)
         }
         // ---- epilogue: O / l (TMEM loads by the whole warp, stores per row) ----
         float lo_ = 0.0f;
@@ -448,10 +499,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::tc_fence_before();
     __syncthreads();
+    ptx::cluster_sync();  // no MMA or load of the pair still touches either CTA
     if (warp == 1) {
         __syncwarp();
         ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, kTmemCols);
+        ptx::tmem_dealloc2(tmem, kTmemCols);
     }
 }
 
@@ -461,8 +513,9 @@ __global__ void bf16_to_f16_kernel(const __nv_bfloat16 *__restrict__ src, __half
     for (; i < n; i += stride) dst[i] = __float2half_rn(__bfloat162float(src[i]));
 }
 
-bool encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows) {
-    return encode_tmap_2d(map, dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT16 ? 1 : 0, base, cols, rows, 128);
+bool encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows,
+               uint32_t box_rows) {
+    return encode_tmap_2d(map, dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT16 ? 1 : 0, base, cols, rows, box_rows);
 }
 
 }  // namespace
@@ -611,22 +664,22 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         d.out = p.out_dev;
         d.lse = p.lse_dev;
         if (p.n_q == 0) continue;
-        if (!encode_2d(&d.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8)) {
+        if (!encode_2d(&d.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8, kRows)) {
             *msg = "cuTensorMapEncodeTiled failed for Q";
             return G4A_CUDA;
         }
         if (p.n_kv > 0) {
             size_t k = std::find(v_src.begin(), v_src.end(), p.v_dev) - v_src.begin();
-            if (!encode_2d(&d.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.k_dev, p.head_dim, p.n_kv) ||
-                !encode_2d(&d.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, S->v16 + v_off[k], p.head_dim, p.n_kv)) {
+            if (!encode_2d(&d.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.k_dev, p.head_dim, p.n_kv, 64) ||
+                !encode_2d(&d.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, S->v16 + v_off[k], p.head_dim, p.n_kv, 64)) {
                 *msg = "cuTensorMapEncodeTiled failed for K/V";
                 return G4A_CUDA;
             }
         }
-        const int n_qt = (p.n_q + kTokensPerTile - 1) / kTokensPerTile;
+        const int n_qt = (p.n_q + kTokensPerPair - 1) / kTokensPerPair;
         for (int t = 0; t < n_qt; t++) {
-            const int64_t q_lo = (int64_t)p.q_pos0 + (int64_t)t * kTokensPerTile;
-            const int64_t q_hi = (int64_t)p.q_pos0 + std::min<int64_t>((int64_t)(t + 1) * kTokensPerTile, p.n_q) - 1;
+            const int64_t q_lo = (int64_t)p.q_pos0 + (int64_t)t * kTokensPerPair;
+            const int64_t q_hi = (int64_t)p.q_pos0 + std::min<int64_t>((int64_t)(t + 1) * kTokensPerPair, p.n_q) - 1;
             int64_t k_lo = p.window > 0 ? q_lo - p.window + 1 : 0;  // first key position any row may see
             int64_t klo = std::max<int64_t>(0, k_lo - p.kv_pos0);
             int64_t khi = std::min<int64_t>((int64_t)p.n_kv - 1, q_hi - p.kv_pos0);
@@ -670,11 +723,12 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
         S->attr_set = true;
     }
+    // two CTAs (one cluster) per work item
     if (!work[0].empty())
-        prefill_kernel<256><<<(unsigned)work[0].size(), kThreads, Cfg<256>::kSmemBytes, st>>>(S->d_problems, S->d_items,
-                                                                                            d_err);
+        prefill_kernel<256><<<2 * (unsigned)work[0].size(), kThreads, Cfg<256>::kSmemBytes, st>>>(
+            S->d_problems, S->d_items, d_err);
     if (!work[1].empty())
-        prefill_kernel<512><<<(unsigned)work[1].size(), kThreads, Cfg<512>::kSmemBytes, st>>>(
+        prefill_kernel<512><<<2 * (unsigned)work[1].size(), kThreads, Cfg<512>::kSmemBytes, st>>>(
             S->d_problems, S->d_items + work[0].size(), d_err);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         *msg = cudaGetErrorString(e);
