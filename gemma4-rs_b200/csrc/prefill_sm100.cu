@@ -16,11 +16,13 @@
 // 256-wide half of the output, each recomputing S over the full width.
 //
 // Roles (352 threads per CTA):
-//   warp 0      TMA producer: Q once, then K and V boxes (64 columns x 64
-//               rows, 128-byte swizzle) through a ring of 8 KB slots in the
-//               fixed order K(0), K(1), V(0), K(2), V(1), ... Both CTAs fill
-//               the same slot sequence; every load signals the LEADER CTA's
-//               ring barrier, which expects the pair's bytes.
+//   warp 0      TMA producer: Q once, then K and V in stages of two boxes
+//               (each 64 columns x 64 rows, 128-byte swizzle; 16 KB per
+//               stage) through a ring, in the fixed order K(0), K(1), V(0),
+//               K(2), V(1), ... Both CTAs fill the same stage sequence; every
+//               load signals the LEADER CTA's stage barrier, which expects
+//               the pair's bytes. One barrier per two boxes halves the
+//               barrier waits of the MMA threads.
 //   warp 1      allocates 512 TMEM columns (pair allocation); in the leader,
 //               one thread issues S(j) = Q K(j)^T (bf16, f32 in TMEM,
 //               double-buffered 2 x 128 columns).
@@ -64,7 +66,8 @@ constexpr int kTokensPerPair = 32;
 constexpr int kKeysPerTile = 128;     // N of S for the pair
 constexpr int kDV = 256;              // output columns per pair
 constexpr int kQBoxBytes = 128 * 128; // 64 bf16 columns x 128 rows
-constexpr int kSlotBytes = 64 * 128;  // 64 columns x 64 rows (bf16 / fp16)
+constexpr int kBoxBytes = 64 * 128;   // 64 columns x 64 rows (bf16 / fp16)
+constexpr int kStageBytes = 2 * kBoxBytes;
 constexpr int kThreads = 352;
 constexpr int kPvWarp = 10;
 constexpr uint32_t kTmemCols = 512;
@@ -85,21 +88,20 @@ struct WorkItem {
 
 template <int HD>
 struct Cfg {
-    static constexpr int kQBoxes = HD / 64;   // Q boxes per CTA
-    static constexpr int kKBoxes = HD / 64;   // K boxes per CTA per tile (64 keys each)
-    static constexpr int kVBoxes = 4;         // 2 column atoms x 2 key halves
-    // Slots: even, so that the two column atoms of a V half (pushed as an
-    // aligned pair after an even number of K boxes) never wrap.
-    static constexpr int kRing = HD == 256 ? 18 : 10;
+    static constexpr int kQBoxes = HD / 64;    // Q boxes per CTA
+    static constexpr int kKStages = HD / 128;  // K stages per CTA per tile: 64 keys x 128 columns each
+    static constexpr int kVStages = 2;         // V stages per tile: one per 64-key half, both column atoms
+    static constexpr int kRing = HD == 256 ? 9 : 5;  // stages
     static constexpr int kSmemQ = kQBoxes * kQBoxBytes;
-    static constexpr int kSmemRing = kRing * kSlotBytes;
+    static constexpr int kSmemRing = kRing * kStageBytes;
     static constexpr int kSmemBytes = kSmemQ + kSmemRing + 5120 /*barriers, mailboxes*/ + 1024 /*alignment slack*/;
-    static_assert(kKBoxes % 2 == 0 && kRing % 2 == 0, "V atom pairs must not wrap");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
-    // Position of the first box of K(j) / V(j) in the push sequence
+    // Position of the first stage of K(j) / V(j) in the push sequence
     // K(0), K(1), V(0), K(2), V(1), ..., K(n-1), V(n-2), V(n-1).
-    __device__ static int k_pos(int j) { return j == 0 ? 0 : kKBoxes + (j - 1) * (kKBoxes + kVBoxes); }
-    __device__ static int v_pos(int j, int n) { return kKBoxes + j * (kKBoxes + kVBoxes) + (j + 1 < n ? kKBoxes : 0); }
+    __device__ static int k_pos(int j) { return j == 0 ? 0 : kKStages + (j - 1) * (kKStages + kVStages); }
+    __device__ static int v_pos(int j, int n) {
+        return kKStages + j * (kKStages + kVStages) + (j + 1 < n ? kKStages : 0);
+    }
 };
 
 struct alignas(8) Mailbox {
@@ -115,8 +117,8 @@ struct Barriers {
     uint64_t pv_done[2];     // leader: PV of the tile in this S buffer done (P buffer free)
     uint64_t o_done;         // both: PV of the latest tile done (pair commit)
     uint64_t mma_done;       // both: every MMA of the pair done (one commit per issuer)
-    uint64_t ring_full[18];  // leader: both CTAs' bytes of the slot
-    uint64_t ring_empty[18]; // both: slot consumed (pair commit)
+    uint64_t ring_full[9];   // leader: both CTAs' bytes of the stage
+    uint64_t ring_empty[9];  // both: stage consumed (pair commit)
     uint32_t tmem_base;
     int abort;
 };
@@ -200,30 +202,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0;  // bit s: slot s received at least one load
             bool ok = true;
+            // one stage: boxes at columns x and x + 64 of rows [y, y + 64)
             auto push = [&](const CUtensorMap *m, int x, int y) {
                 if (!ok) return;
                 if (!wait_bar(&bars->ring_empty[slot], phase ^ 1u, abort, err)) {
                     ok = false;
                     return;
                 }
-                if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * kSlotBytes);
-                ptx::tma_load_2d_pair(ring + slot * kSlotBytes, m, ptx::mapa(&bars->ring_full[slot], 0), x, y);
+                if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * kStageBytes);
+                const uint32_t bar_l = ptx::mapa(&bars->ring_full[slot], 0);
+                ptx::tma_load_2d_pair(ring + slot * kStageBytes, m, bar_l, x, y);
+                ptx::tma_load_2d_pair(ring + slot * kStageBytes + kBoxBytes, m, bar_l, x + 64, y);
                 issued |= 1u << slot;
                 if (++slot == C::kRing) {
                     slot = 0;
                     phase ^= 1u;
                 }
             };
-            // K: this CTA's 64 keys of the tile, all HD columns
+            // K: this CTA's 64 keys of the tile, all HD columns (128 per stage)
             auto push_k = [&](int j) {
                 const int y = (it.kv_tile_lo + j) * kKeysPerTile + 64 * (int)rank;
-                for (int c = 0; c < C::kKBoxes; c++) push(&pb.tk, 64 * c, y);
+                for (int st = 0; st < C::kKStages; st++) push(&pb.tk, 128 * st, y);
             };
-            // V: this CTA's 128 output columns (two 64-column atoms), keys in two halves
+            // V: this CTA's 128 output columns (two 64-column atoms), one stage per 64-key half
             auto push_v = [&](int j) {
                 const int x = it.dv_half * kDV + 128 * (int)rank;
-                for (int kh = 0; kh < 2; kh++)
-                    for (int a = 0; a < 2; a++) push(&pb.tv, x + 64 * a, (it.kv_tile_lo + j) * kKeysPerTile + 64 * kh);
+                for (int kh = 0; kh < 2; kh++) push(&pb.tv, x, (it.kv_tile_lo + j) * kKeysPerTile + 64 * kh);
             };
             push_k(0);
             for (int j = 0; j < n_tiles && ok; j++) {
@@ -254,7 +258,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // byte offset is added as (offset >> 4) without a carry out of it.
         const uint64_t q_desc = ptx::smem_desc(ptx::smem_u32(q_smem), 16, 1024);
         const uint64_t k_desc = ptx::smem_desc(ptx::smem_u32(ring), 16, 1024);
-        const uint64_t v_desc = ptx::smem_desc(ptx::smem_u32(ring), kSlotBytes, 1024);
+        const uint64_t v_desc = ptx::smem_desc(ptx::smem_u32(ring), kBoxBytes, 1024);
         if (lane == 0 && rank == 0) {
             bool ok = n_tiles > 0 && wait_bar(&bars->q_full, 0, abort, err);
             if (warp == 1) {
@@ -268,18 +272,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     ptx::tc_fence_after();
                     const uint32_t d = tmem + ((j & 1) ? kColS1 : kColS0);
                     const int pos = C::k_pos(j);
-                    for (int c = 0; c < C::kKBoxes && ok; c++) {
-                        const int slot = slot_of(pos + c);
-                        if (!wait_bar(&bars->ring_full[slot], phase_of(pos + c), abort, err)) {
+                    for (int st = 0; st < C::kKStages && ok; st++) {
+                        const int slot = slot_of(pos + st);
+                        if (!wait_bar(&bars->ring_full[slot], phase_of(pos + st), abort, err)) {
                             ok = false;
                             break;
                         }
                         ptx::tc_fence_after();
-                        const uint64_t kd = k_desc + (uint64_t)(slot * (kSlotBytes >> 4));
-                        const uint64_t qd = q_desc + (uint64_t)(c * (kQBoxBytes >> 4));
-                        ptx::mma2_ss(d, qd, kd, kIdescS, c != 0);
 #pragma unroll
-                        for (int kk = 1; kk < 4; kk++) ptx::mma2_ss(d, qd + 2 * kk, kd + 2 * kk, kIdescS, 1);
+                        for (int b = 0; b < 2; b++) {
+                            const uint64_t kd = k_desc + (uint64_t)((slot * kStageBytes + b * kBoxBytes) >> 4);
+                            const uint64_t qd = q_desc + (uint64_t)((2 * st + b) * (kQBoxBytes >> 4));
+                            ptx::mma2_ss(d, qd, kd, kIdescS, (st | b) != 0);
+#pragma unroll
+                            for (int kk = 1; kk < 4; kk++) ptx::mma2_ss(d, qd + 2 * kk, kd + 2 * kk, kIdescS, 1);
+                        }
                         ptx::mma2_commit_pair(&bars->ring_empty[slot], kBothCtas);
                     }
                     if (ok) ptx::mma2_commit_pair(&bars->s_full[j & 1], kBothCtas);
@@ -293,20 +300,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const int pos = C::v_pos(j, n_tiles);
-                    for (int c = 0; c < C::kVBoxes && ok; c++)
+                    for (int c = 0; c < C::kVStages && ok; c++)
                         ok = wait_bar(&bars->ring_full[slot_of(pos + c)], phase_of(pos + c), abort, err);
                     if (!ok) break;
                     ptx::tc_fence_after();
                     const uint32_t p_tmem = tmem + ((j & 1) ? kColS1 : kColS0);
-                    // keys 16ks.. live in V half ks/4: slots pos + 2*(ks/4) (+1 = second column atom)
-                    const uint64_t vd0 = v_desc + (uint64_t)(slot_of(pos) * (kSlotBytes >> 4));
-                    const uint64_t vd1 = v_desc + (uint64_t)(slot_of(pos + 2) * (kSlotBytes >> 4));
+                    // keys 16ks.. live in V half ks/4: stage pos + ks/4 (its second box = second column atom)
+                    const uint64_t vd0 = v_desc + (uint64_t)(slot_of(pos) * (kStageBytes >> 4));
+                    const uint64_t vd1 = v_desc + (uint64_t)(slot_of(pos + 1) * (kStageBytes >> 4));
                     ptx::mma2_ts(tmem + kColO, p_tmem, vd0, kIdescPV, j > 0);
 #pragma unroll
                     for (int ks = 1; ks < kKeysPerTile / 16; ks++)
                         ptx::mma2_ts(tmem + kColO, p_tmem + 8 * ks, (ks < 4 ? vd0 : vd1) + (2048 >> 4) * (ks & 3),
                                      kIdescPV, 1);
-                    for (int c = 0; c < C::kVBoxes; c++)
+                    for (int c = 0; c < C::kVStages; c++)
                         ptx::mma2_commit_pair(&bars->ring_empty[slot_of(pos + c)], kBothCtas);
                     ptx::mma2_commit_pair(&bars->pv_done[j & 1], 0x1);
                     ptx::mma2_commit_pair(&bars->o_done, kBothCtas);
