@@ -16,13 +16,13 @@
 // 256-wide half of the output, each recomputing S over the full width.
 //
 // Roles (352 threads per CTA):
-//   warp 0      TMA producer: Q once, then K and V in stages of two boxes
-//               (each 64 columns x 64 rows, 128-byte swizzle; 16 KB per
-//               stage) through a ring, in the fixed order K(0), K(1), V(0),
-//               K(2), V(1), ... Both CTAs fill the same stage sequence; every
-//               load signals the LEADER CTA's stage barrier, which expects
-//               the pair's bytes. One barrier per two boxes halves the
-//               barrier waits of the MMA threads.
+//   warp 0      TMA producer: Q once, then K and V in stages of two or four
+//               boxes (each 64 columns x 64 rows, 128-byte swizzle) under
+//               one barrier, through a ring, in the fixed order K(0), K(1),
+//               V(0), K(2), V(1), ... Both CTAs fill the same stage sequence;
+//               every load signals the LEADER CTA's stage barrier, which
+//               expects the pair's bytes. Few, large stages keep the barrier
+//               waits of the MMA threads rare.
 //   warp 1      allocates 512 TMEM columns (pair allocation); in the leader,
 //               one thread issues S(j) = Q K(j)^T (bf16, f32 in TMEM,
 //               double-buffered 2 x 128 columns).
@@ -67,7 +67,6 @@ constexpr int kKeysPerTile = 128;     // N of S for the pair
 constexpr int kDV = 256;              // output columns per pair
 constexpr int kQBoxBytes = 128 * 128; // 64 bf16 columns x 128 rows
 constexpr int kBoxBytes = 64 * 128;   // 64 columns x 64 rows (bf16 / fp16)
-constexpr int kStageBytes = 2 * kBoxBytes;
 constexpr int kThreads = 352;
 constexpr int kPvWarp = 10;
 constexpr uint32_t kTmemCols = 512;
@@ -89,9 +88,15 @@ struct WorkItem {
 template <int HD>
 struct Cfg {
     static constexpr int kQBoxes = HD / 64;    // Q boxes per CTA
-    static constexpr int kKStages = HD / 128;  // K stages per CTA per tile: 64 keys x 128 columns each
-    static constexpr int kVStages = 2;         // V stages per tile: one per 64-key half, both column atoms
-    static constexpr int kRing = HD == 256 ? 9 : 5;  // stages
+    // A stage is kStageBoxes boxes under one barrier: K(j) is HD/64 boxes
+    // (64 keys x 64 columns each), V(j) four (2 key halves x 2 column atoms,
+    // atoms adjacent). Width 512 keeps 16 KB stages (Q takes 128 KB of shared
+    // memory), width 256 takes 32 KB stages: one wait each for K(j) and V(j).
+    static constexpr int kStageBoxes = HD == 256 ? 4 : 2;
+    static constexpr int kStageBytes = kStageBoxes * kBoxBytes;
+    static constexpr int kKStages = HD / 64 / kStageBoxes;
+    static constexpr int kVStages = 4 / kStageBoxes;
+    static constexpr int kRing = HD == 256 ? 4 : 5;  // stages
     static constexpr int kSmemQ = kQBoxes * kQBoxBytes;
     static constexpr int kSmemRing = kRing * kStageBytes;
     static constexpr int kSmemBytes = kSmemQ + kSmemRing + 5120 /*barriers, mailboxes*/ + 1024 /*alignment slack*/;
@@ -117,8 +122,8 @@ struct Barriers {
     uint64_t pv_done[2];     // leader: PV of the tile in this S buffer done (P buffer free)
     uint64_t o_done;         // both: PV of the latest tile done (pair commit)
     uint64_t mma_done;       // both: every MMA of the pair done (one commit per issuer)
-    uint64_t ring_full[9];   // leader: both CTAs' bytes of the stage
-    uint64_t ring_empty[9];  // both: stage consumed (pair commit)
+    uint64_t ring_full[8];   // leader: both CTAs' bytes of the stage
+    uint64_t ring_empty[8];  // both: stage consumed (pair commit)
     uint32_t tmem_base;
     int abort;
 };
@@ -202,32 +207,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0;  // bit s: slot s received at least one load
             bool ok = true;
-            // one stage: boxes at columns x and x + 64 of rows [y, y + 64)
-            auto push = [&](const CUtensorMap *m, int x, int y) {
+            // one stage: box b at (xs[b], ys[b])
+            auto push = [&](const CUtensorMap *m, const int *xs, const int *ys) {
                 if (!ok) return;
                 if (!wait_bar(&bars->ring_empty[slot], phase ^ 1u, abort, err)) {
                     ok = false;
                     return;
                 }
-                if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * kStageBytes);
+                if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * C::kStageBytes);
                 const uint32_t bar_l = ptx::mapa(&bars->ring_full[slot], 0);
-                ptx::tma_load_2d_pair(ring + slot * kStageBytes, m, bar_l, x, y);
-                ptx::tma_load_2d_pair(ring + slot * kStageBytes + kBoxBytes, m, bar_l, x + 64, y);
+                for (int b = 0; b < C::kStageBoxes; b++)
+                    ptx::tma_load_2d_pair(ring + slot * C::kStageBytes + b * kBoxBytes, m, bar_l, xs[b], ys[b]);
                 issued |= 1u << slot;
                 if (++slot == C::kRing) {
                     slot = 0;
                     phase ^= 1u;
                 }
             };
-            // K: this CTA's 64 keys of the tile, all HD columns (128 per stage)
+            // K: this CTA's 64 keys of the tile, all HD columns
             auto push_k = [&](int j) {
                 const int y = (it.kv_tile_lo + j) * kKeysPerTile + 64 * (int)rank;
-                for (int st = 0; st < C::kKStages; st++) push(&pb.tk, 128 * st, y);
+                for (int st = 0; st < C::kKStages; st++) {
+                    int xs[C::kStageBoxes], ys[C::kStageBoxes];
+                    for (int b = 0; b < C::kStageBoxes; b++) {
+                        xs[b] = 64 * (st * C::kStageBoxes + b);
+                        ys[b] = y;
+                    }
+                    push(&pb.tk, xs, ys);
+                }
             };
-            // V: this CTA's 128 output columns (two 64-column atoms), one stage per 64-key half
+            // V: this CTA's 128 output columns (two 64-column atoms) of both
+            // 64-key halves; box q = 2 * key half + atom
             auto push_v = [&](int j) {
                 const int x = it.dv_half * kDV + 128 * (int)rank;
-                for (int kh = 0; kh < 2; kh++) push(&pb.tv, x, (it.kv_tile_lo + j) * kKeysPerTile + 64 * kh);
+                const int y = (it.kv_tile_lo + j) * kKeysPerTile;
+                for (int st = 0; st < C::kVStages; st++) {
+                    int xs[C::kStageBoxes], ys[C::kStageBoxes];
+                    for (int b = 0; b < C::kStageBoxes; b++) {
+                        const int q = st * C::kStageBoxes + b;
+                        xs[b] = x + 64 * (q & 1);
+                        ys[b] = y + 64 * (q >> 1);
+                    }
+                    push(&pb.tv, xs, ys);
+                }
             };
             push_k(0);
             for (int j = 0; j < n_tiles && ok; j++) {
@@ -280,9 +302,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         ptx::tc_fence_after();
 #pragma unroll
-                        for (int b = 0; b < 2; b++) {
-                            const uint64_t kd = k_desc + (uint64_t)((slot * kStageBytes + b * kBoxBytes) >> 4);
-                            const uint64_t qd = q_desc + (uint64_t)((2 * st + b) * (kQBoxBytes >> 4));
+                        for (int b = 0; b < C::kStageBoxes; b++) {
+                            const uint64_t kd = k_desc + (uint64_t)((slot * C::kStageBytes + b * kBoxBytes) >> 4);
+                            const uint64_t qd = q_desc + (uint64_t)((C::kStageBoxes * st + b) * (kQBoxBytes >> 4));
                             ptx::mma2_ss(d, qd, kd, kIdescS, (st | b) != 0);
 #pragma unroll
                             for (int kk = 1; kk < 4; kk++) ptx::mma2_ss(d, qd + 2 * kk, kd + 2 * kk, kIdescS, 1);
@@ -305,9 +327,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                     ptx::tc_fence_after();
                     const uint32_t p_tmem = tmem + ((j & 1) ? kColS1 : kColS0);
-                    // keys 16ks.. live in V half ks/4: stage pos + ks/4 (its second box = second column atom)
-                    const uint64_t vd0 = v_desc + (uint64_t)(slot_of(pos) * (kStageBytes >> 4));
-                    const uint64_t vd1 = v_desc + (uint64_t)(slot_of(pos + 1) * (kStageBytes >> 4));
+                    // keys 16ks.. live in V half h = ks/4: box 2h of the V sequence (the
+                    // next box holds its second column atom)
+                    const uint64_t vd0 = v_desc + (uint64_t)((slot_of(pos) * C::kStageBytes) >> 4);
+                    const uint64_t vd1 =
+                        v_desc + (uint64_t)((slot_of(pos + 2 / C::kStageBoxes) * C::kStageBytes +
+                                             (2 % C::kStageBoxes) * kBoxBytes) >> 4);
                     ptx::mma2_ts(tmem + kColO, p_tmem, vd0, kIdescPV, j > 0);
 #pragma unroll
                     for (int ks = 1; ks < kKeysPerTile / 16; ks++)
