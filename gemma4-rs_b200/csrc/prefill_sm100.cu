@@ -119,8 +119,10 @@ struct Barriers {
     uint64_t q_full;         // leader: both CTAs' Q bytes
     uint64_t s_full[2];      // both: S buffer ready (pair commit)
     uint64_t p_full[2];      // leader: 256 arrivals from each CTA
-    uint64_t pv_done[2];     // leader: PV of the tile in this S buffer done (P buffer free)
-    uint64_t o_done;         // both: PV of the latest tile done (pair commit)
+    uint64_t o_done[2];      // both: PV of the tile in this S buffer done (pair commit): O
+                             // updated, P buffer free. A wait by phase parity is exact
+                             // only while its barrier is at most one phase behind the
+                             // awaited one; a barrier per S buffer keeps that true.
     uint64_t mma_done;       // both: every MMA of the pair done (one commit per issuer)
     uint64_t ring_full[8];   // leader: both CTAs' bytes of the stage
     uint64_t ring_empty[8];  // both: stage consumed (pair commit)
@@ -165,9 +167,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&bars->s_full[i], 1);
             ptx::mbar_init(&bars->p_full[i], 2 * 256);
-            ptx::mbar_init(&bars->pv_done[i], 1);
+            ptx::mbar_init(&bars->o_done[i], 1);
         }
-        ptx::mbar_init(&bars->o_done, 1);
         ptx::mbar_init(&bars->mma_done, 2);
         for (int i = 0; i < C::kRing; i++) {
             ptx::mbar_init(&bars->ring_full[i], 1);
@@ -287,7 +288,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // S(j) = Q K(j)^T into S buffer j&1, once PV(j-2) has read P(j-2) from it
                 constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, 2 * kRows, kKeysPerTile);
                 for (int j = 0; j < n_tiles && ok; j++) {
-                    if (j >= 2 && !wait_bar(&bars->pv_done[j & 1], (uint32_t)((j - 2) >> 1) & 1u, abort, err)) {
+                    if (j >= 2 && !wait_bar(&bars->o_done[j & 1], (uint32_t)((j - 2) >> 1) & 1u, abort, err)) {
                         ok = false;
                         break;
                     }
@@ -340,8 +341,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                      kIdescPV, 1);
                     for (int c = 0; c < C::kVStages; c++)
                         ptx::mma2_commit_pair(&bars->ring_empty[slot_of(pos + c)], kBothCtas);
-                    ptx::mma2_commit_pair(&bars->pv_done[j & 1], 0x1);
-                    ptx::mma2_commit_pair(&bars->o_done, kBothCtas);
+                    ptx::mma2_commit_pair(&bars->o_done[j & 1], kBothCtas);
                 }
             }
             // Every MMA this thread issued completes before either CTA
@@ -450,9 +450,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // max exceeds it by more than 8 (P then stays below 2^8).
             const bool grow = mx > m_used + 8.0f;
             const bool o_live = grow && m_used != -CUDART_INF_F;  // O holds weights of the old max
+            const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
+            if (grow) m_used = mx;
+            // p = 2^(s*log2e - m); masked scores are -inf and give 0. A row
+            // with no visible key so far keeps m = -inf; subtract 0 then.
+            const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
+            uint32_t pk[32];
+            float rs0 = 0.0f, rs1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float p0 = ptx::ex2(fmaf(s[2 * i], kLog2e, neg_m));
+                const float p1 = ptx::ex2(fmaf(s[2 * i + 1], kLog2e, neg_m));
+                rs0 += p0;
+                rs1 += p1;
+                pk[i] = ptx::pack_half2(p0, p1);
+            }
+            l = l * f + (rs0 + rs1);
+            // P (fp16 pairs) goes over the first 64 columns of this S buffer;
+            // half 1's columns 32-63 were read by half 0 before it posted its
+            // max, which half 1 has seen.
+            ptx::tmem_st32(s_addr + 32 * half, pk);
+            // O rescale after P is out of the registers: the wait for PV(j-1)
+            // then overlaps the exponentials above. PV(j) reads neither O's
+            // new scale nor P(j) before the arrive below.
             if (__any_sync(0xffffffffu, o_live)) {
-                const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
-                if (!__all_sync(0xffffffffu, wait_bar(&bars->o_done, (uint32_t)(j - 1) & 1u, abort, err))) {
+                if (!__all_sync(0xffffffffu,
+                                wait_bar(&bars->o_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort, err))) {
                     ok = false;
                     break;
                 }
@@ -468,28 +491,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
                     ptx::tmem_st32(o_addr, r);
                 }
-                ptx::tmem_wait_st();
-                l *= f;
             }
-            if (grow) m_used = mx;
-            // p = 2^(s*log2e - m); masked scores are -inf and give 0. A row
-            // with no visible key so far keeps m = -inf; subtract 0 then.
-            const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
-            uint32_t pk[32];
-            float rs0 = 0.0f, rs1 = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
-                const float p0 = ptx::ex2(fmaf(s[2 * i], kLog2e, neg_m));
-                const float p1 = ptx::ex2(fmaf(s[2 * i + 1], kLog2e, neg_m));
-                rs0 += p0;
-                rs1 += p1;
-                pk[i] = ptx::pack_half2(p0, p1);
-            }
-            l += rs0 + rs1;
-            // P (fp16 pairs) goes over the first 64 columns of this S buffer;
-            // half 1's columns 32-63 were read by half 0 before it posted its
-            // max, which half 1 has seen.
-            ptx::tmem_st32(s_addr + 32 * half, pk);
             ptx::tmem_wait_st();
             ptx::tc_fence_before();
             ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);  // the leader's barrier (release, cluster scope)
@@ -499,7 +501,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (ok && !__all_sync(0xffffffffu, swap(n_tiles, l, &lo_))) ok = false;
         l += lo_;
         if (ok && n_tiles > 0 &&
-            !__all_sync(0xffffffffu, wait_bar(&bars->o_done, (uint32_t)(n_tiles - 1) & 1u, abort, err)))
+            !__all_sync(0xffffffffu,
+                        wait_bar(&bars->o_done[(n_tiles - 1) & 1], (uint32_t)((n_tiles - 1) >> 1) & 1u, abort, err)))
             ok = false;
         ptx::tc_fence_after();
         if (ok) {
