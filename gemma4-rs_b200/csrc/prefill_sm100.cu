@@ -38,7 +38,7 @@
 //               one FFMA + EX2 per score, P written back into the S columns
 //               as fp16, then an arrive on the leader's P barrier; the
 //               running max is rescaled lazily (only when it grows by more
-//               than 2^8); the epilogue divides by the row sum and stores
+//               than 2^15); the epilogue divides by the row sum and stores
 //               f32, each thread 128 of the 256 output columns.
 // Every mbarrier wait is bounded; on time-out the CTA records an error flag,
 // drains what it can, frees TMEM and exits (after the pair's final cluster
@@ -447,8 +447,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             mx = fmaxf(mx, mo) * kLog2e;
             // Lazy rescale: move this row's reference max only when the tile
-            // max exceeds it by more than 8 (P then stays below 2^8).
-            const bool grow = mx > m_used + 8.0f;
+            // max exceeds it by more than 15 (log2 units), so that P stays at
+            // or below 2^15 and fits fp16 (max 65504). With scores of unit-RMS
+            // rows spread over tens of bits, a smaller margin would rescale O
+            // on most tiles; this one rarely does.
+            const bool grow = mx > m_used + 15.0f;
             const bool o_live = grow && m_used != -CUDART_INF_F;  // O holds weights of the old max
             const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
             if (grow) m_used = mx;
@@ -480,16 +483,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     break;
                 }
                 ptx::tc_fence_after();
+                // this thread's 128 columns of O, 64 at a time
 #pragma unroll 1
-                for (int c = 0; c < kDV / 64; c++) {
-                    uint32_t r[32];
-                    const uint32_t o_addr = tmem + lane_addr + kColO + 128 * half + 32 * c;
-                    ptx::tmem_ld32(o_addr, r);
+                for (int c = 0; c < kDV / 128; c++) {
+                    uint32_t r0[32], r1[32];
+                    const uint32_t o_addr = tmem + lane_addr + kColO + 128 * half + 64 * c;
+                    ptx::tmem_ld32(o_addr, r0);
+                    ptx::tmem_ld32(o_addr + 32, r1);
                     ptx::tmem_wait_ld();
-                    ptx::tmem_ld_fence(r);
+                    ptx::tmem_ld_fence(r0);
+                    ptx::tmem_ld_fence(r1);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-                    ptx::tmem_st32(o_addr, r);
+                    for (int i = 0; i < 32; i++) {
+                        r0[i] = __float_as_uint(__uint_as_float(r0[i]) * f);
+                        r1[i] = __float_as_uint(__uint_as_float(r1[i]) * f);
+                    }
+                    ptx::tmem_st32(o_addr, r0);
+                    ptx::tmem_st32(o_addr + 32, r1);
                 }
             }
             ptx::tmem_wait_st();

@@ -110,7 +110,7 @@ def test_prefill_offsets_and_lse(oracle, ctx, torch_cuda, hd, window, n_q, q_pos
 
 def test_prefill_rescale_path(oracle, ctx, torch_cuda):
     """Scores that grow along the keys force the running max up by more than
-    2^8 several times (the lazy O rescale); the result still matches."""
+    2^15 several times (the lazy O rescale); the result still matches."""
     hd, T = 256, 512
     q, k, v = make_qkv(oracle, 7, T, T, hd)
     ramp = np.linspace(0.2, 3.0, T, dtype=np.float32)[:, None]
