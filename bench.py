@@ -498,9 +498,10 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
 
 
 def traffic_from_profile():
-    """DRAM bytes per launch of the global decode kernel from the committed
-    ncu summary, scaled by the workload ratio recorded there (or None)."""
-    f = ROOT / "profiles" / "decode_global_f16_cfg2.md"
+    """DRAM bytes (read + write) per launch of the main decode kernel (both
+    layers of the configuration 2 step) from the committed ncu summary, or
+    None when the summary is missing."""
+    f = ROOT / "profiles" / "decode_f16_main_cfg2.md"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
