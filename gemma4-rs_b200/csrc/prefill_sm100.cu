@@ -67,6 +67,7 @@ constexpr int kKeysPerTile = 128;     // N of S for the pair
 constexpr int kDV = 256;              // output columns per pair
 constexpr int kQBoxBytes = 128 * 128; // 64 bf16 columns x 128 rows
 constexpr int kBoxBytes = 64 * 128;   // 64 columns x 64 rows (bf16 / fp16)
+constexpr int kOutBoxBytes = 128 * 128;  // 32 f32 columns x 128 rows
 constexpr int kThreads = 352;
 constexpr int kPvWarp = 10;
 constexpr uint32_t kTmemCols = 512;
@@ -76,6 +77,7 @@ constexpr uint16_t kBothCtas = 0x3;
 
 struct alignas(64) ProblemDev {
     CUtensorMap tq, tk, tv;  // Q [n_q*8, hd] bf16 (128-row boxes), K [n_kv, hd] bf16, V [n_kv, hd] fp16 (64-row boxes)
+    CUtensorMap to;          // out [n_q*8, hd] f32, 32-column x 128-row boxes, 128-byte swizzle
     int32_t hd, window, n_q, q_pos0, n_kv, kv_pos0;
     float *out;
     float *lse;
@@ -101,6 +103,7 @@ struct Cfg {
     static constexpr int kSmemRing = kRing * kStageBytes;
     static constexpr int kSmemBytes = kSmemQ + kSmemRing + 5120 /*barriers, mailboxes*/ + 1024 /*alignment slack*/;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kSmemQ + kSmemRing >= 8 * kOutBoxBytes, "output staging reuses the Q and K/V stages");
     // Position of the first stage of K(j) / V(j) in the push sequence
     // K(0), K(1), V(0), K(2), V(1), ..., K(n-1), V(n-2), V(n-1).
     __device__ static int k_pos(int j) { return j == 0 ? 0 : kKStages + (j - 1) * (kKStages + kVStages); }
@@ -199,6 +202,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::prefetch_tmap(&pb.tq);
             ptx::prefetch_tmap(&pb.tk);
             ptx::prefetch_tmap(&pb.tv);
+            ptx::prefetch_tmap(&pb.to);
             if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * C::kSmemQ);
             const uint32_t q_full_l = ptx::mapa(&bars->q_full, 0);
             for (int c = 0; c < C::kQBoxes; c++)
@@ -506,7 +510,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::tc_fence_before();
             ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);  // the leader's barrier (release, cluster scope)
         }
-        // ---- epilogue: O / l (TMEM loads by the whole warp, stores per row) ----
+        // ---- epilogue: O / l, staged in shared memory, written by TMA ----
         float lo_ = 0.0f;
         if (ok && !__all_sync(0xffffffffu, swap(n_tiles, l, &lo_))) ok = false;
         l += lo_;
@@ -515,8 +519,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         wait_bar(&bars->o_done[(n_tiles - 1) & 1], (uint32_t)((n_tiles - 1) >> 1) & 1u, abort, err)))
             ok = false;
         ptx::tc_fence_after();
+        // The CTA's Q and K/V stages are idle by now (every load was consumed,
+        // every MMA reading them completed), so O / l is staged there as eight
+        // 32-column x 128-row f32 boxes in the 128-byte-swizzled layout (16-byte
+        // chunk j of row r at chunk j ^ (r % 8)) and written by TMA stores: full
+        // lines to L2 instead of 16-byte pieces of 128 different rows.
+        uint8_t *stage = smem;
         if (ok) {
-            float *dst = pb.out + ((size_t)tok * 8 + head) * HD + it.dv_half * kDV + 128 * half;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll 1
             for (int c = 0; c < kDV / 64; c++) {
@@ -529,17 +538,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 32; i++) r[i] = 0u;
                 }
-                if (row_valid) {
+                uint8_t *row_p = stage + (4 * half + c) * kOutBoxBytes + row * 128;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                               __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-                        *reinterpret_cast<float4 *>(dst + 32 * c + i) = v;
-                    }
+                for (int jj = 0; jj < 8; jj++) {
+                    const float4 v = make_float4(__uint_as_float(r[4 * jj]) * inv, __uint_as_float(r[4 * jj + 1]) * inv,
+                                                 __uint_as_float(r[4 * jj + 2]) * inv,
+                                                 __uint_as_float(r[4 * jj + 3]) * inv);
+                    *reinterpret_cast<float4 *>(row_p + ((jj ^ (row & 7)) << 4)) = v;
                 }
             }
             if (row_valid && pb.lse && it.dv_half == 0 && half == 0)
                 pb.lse[(size_t)tok * 8 + head] = l > 0.0f ? (m_used + log2f(l)) * 0.6931471805599453f : -CUDART_INF_F;
+        }
+        ptx::fence_proxy_async_smem();
+        // All eight softmax warps reach this barrier on every path (an aborted
+        // warp only skips its staging writes above).
+        ptx::named_bar_sync(1, 256);
+        if (threadIdx.x == 64 && !*abort && tok0 < pb.n_q) {
+            // rows past n_q * 8 are clipped by the tensor map; a box starting past them is not issued
+            for (int k = 0; k < 8; k++)
+                ptx::tma_store_2d(&pb.to, stage + k * kOutBoxBytes, it.dv_half * kDV + 32 * k, tok0 * 8);
+            ptx::bulk_commit_group();
+            ptx::bulk_wait_read_all();
         }
     }
     ptx::tc_fence_before();
@@ -595,6 +615,19 @@ bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint6
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+// Output map: f32 [rows, cols], 32-column x 128-row boxes, 128-byte swizzle.
+static bool encode_out_f32(CUtensorMap *map, const float *base, uint64_t cols, uint64_t rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {32, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Host-side state the prefill keeps in the context between calls.
@@ -711,6 +744,10 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         if (p.n_q == 0) continue;
         if (!encode_2d(&d.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8, kRows)) {
             *msg = "cuTensorMapEncodeTiled failed for Q";
+            return G4A_CUDA;
+        }
+        if (!encode_out_f32(&d.to, p.out_dev, p.head_dim, (uint64_t)p.n_q * 8)) {
+            *msg = "cuTensorMapEncodeTiled failed for the output";
             return G4A_CUDA;
         }
         if (p.n_kv > 0) {
