@@ -354,7 +354,7 @@ def flush_l2(torch, buf):
     buf.add_(1.0)
 
 
-def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2):
+def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2, include_long=True):
     """Configurations 1 and 3 on one GPU: tcgen05 prefill, CUDA events around
     each launch, L2 flushed (256 MB write) between launches."""
     hp = g4a.hparams_e2b()
@@ -399,6 +399,8 @@ def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2):
     res["cfg1_628x35"] = {"ms": round(ms, 4), "gflop": round(flops / 1e9, 3), "TFLOP_s": round(tf, 1),
                           "frac_of_peak": round(tf / pk["bf16"], 4)}
     del probs, kvs
+    if not include_long:
+        return res
     # configuration 3: 32,768-token global layer on one GPU
     T = 32768
     q, k = unit((T, HEADS, HD_G)), unit((T, HD_G))
@@ -463,11 +465,20 @@ def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, w
 
 def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     """One prefill problem on its own (for profiling one kernel on a small
-    case): spec "prefill:<head width>:<tokens>:<window>"."""
+    case): spec "prefill:<head width>:<tokens>:<window>", or "prefill-cfg1"
+    for configuration 1 alone (35 layer-equivalents in one call)."""
+    ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
+    if spec == "prefill-cfg1":
+        stream = torch.cuda.Stream()
+        ctx.set_stream(stream.cuda_stream)
+        res = measure_prefill(torch, g4a, ctx, stream, peaks(), reps=max(reps, 1), warmup=max(warmup, 1),
+                              include_long=False)
+        ctx.close()
+        print(json.dumps({"case": spec, **res["cfg1_628x35"]}), flush=True)
+        return
     kind, hd, T, window = spec.split(":")
     assert kind == "prefill", spec
     hd, T, window = int(hd), int(T), int(window)
-    ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     gen = torch.Generator(device="cuda")

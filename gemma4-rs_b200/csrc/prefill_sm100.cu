@@ -51,6 +51,7 @@
 #include <algorithm>
 #include <climits>
 #include <cstring>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/g4attn.h"
@@ -572,15 +573,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
-__global__ void bf16_to_f16_kernel(const __nv_bfloat16 *__restrict__ src, __half *__restrict__ dst, size_t n) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (; i < n; i += stride) dst[i] = __float2half_rn(__bfloat162float(src[i]));
-}
+// bf16 -> fp16 copies of up to kMaxSegs V arrays in one launch (blockIdx.y =
+// segment); 8 elements per thread and step. Every count is a multiple of 8
+// (a head width) and every address 16-byte aligned (checked on the host).
+constexpr int kMaxSegs = 32;
+struct ConvSegs {
+    const __nv_bfloat16 *src[kMaxSegs];
+    __half *dst[kMaxSegs];
+    uint64_t n8[kMaxSegs];  // elements / 8
+};
 
-bool encode_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows,
-               uint32_t box_rows) {
-    return encode_tmap_2d(map, dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT16 ? 1 : 0, base, cols, rows, box_rows);
+__global__ void bf16_to_f16_kernel(ConvSegs segs) {
+    const int sg = blockIdx.y;
+    const uint4 *src = reinterpret_cast<const uint4 *>(segs.src[sg]);
+    uint4 *dst = reinterpret_cast<uint4 *>(segs.dst[sg]);
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < segs.n8[sg];
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        uint4 v = src[i];
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162 *>(&w[k]);
+            const __half2 h = __floats2half2_rn(__bfloat162float(b.x), __bfloat162float(b.y));
+            w[k] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
 }
 
 }  // namespace
@@ -639,7 +657,41 @@ struct PrefillScratch {
     WorkItem *d_items = nullptr;
     size_t items_cap = 0;
     bool attr_set = false;
+    // Tensor maps by (kind, base, columns, rows): the encoder is a driver call
+    // per map, and repeated calls (a model's layers, every prompt of a batch)
+    // name the same buffers.
+    struct MapKey {
+        int kind;
+        const void *base;
+        uint64_t cols, rows;
+        bool operator==(const MapKey &o) const {
+            return kind == o.kind && base == o.base && cols == o.cols && rows == o.rows;
+        }
+    };
+    struct MapHash {
+        size_t operator()(const MapKey &k) const {
+            return std::hash<const void *>()(k.base) ^ (k.cols * 0x9E3779B97F4A7C15ull) ^ (k.rows << 7) ^ (size_t)k.kind;
+        }
+    };
+    std::unordered_map<MapKey, CUtensorMap, MapHash> maps;
 };
+
+// kind 0: bf16 Q (128-row boxes), 1: bf16 K (64-row boxes), 2: fp16 V (64-row boxes), 3: f32 output
+static bool cached_map(PrefillScratch *S, int kind, const void *base, uint64_t cols, uint64_t rows, CUtensorMap *out) {
+    const PrefillScratch::MapKey key{kind, base, cols, rows};
+    auto f = S->maps.find(key);
+    if (f != S->maps.end()) {
+        *out = f->second;
+        return true;
+    }
+    bool ok;
+    if (kind == 3) ok = encode_out_f32(out, static_cast<const float *>(base), cols, rows);
+    else ok = encode_tmap_2d(out, kind == 2 ? 1 : 0, base, cols, rows, kind == 0 ? kRows : 64);
+    if (!ok) return false;
+    if (S->maps.size() > 4096) S->maps.clear();
+    S->maps.emplace(key, *out);
+    return true;
+}
 
 PrefillScratch *prefill_scratch_new() { return new PrefillScratch(); }
 void prefill_scratch_free(PrefillScratch *s) {
@@ -675,10 +727,9 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         *msg = "invalid prefill problem list";
         return G4A_COMPUTE;
     }
-    // distinct V arrays -> fp16 copies
+    // distinct V arrays -> fp16 copies, each sized for the most rows any problem reads
     std::vector<const void *> v_src;
-    std::vector<size_t> v_off;
-    size_t v_total = 0;
+    std::vector<size_t> v_len;
     for (int32_t i = 0; i < n; i++) {
         const g4a_prefill_problem &p = pr[i];
         if (p.head_dim != 256 && p.head_dim != 512) {
@@ -703,29 +754,38 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
             *msg = "prefill buffers must be 16-byte aligned";
             return G4A_COMPUTE;
         }
-        if (p.n_kv > 0 && std::find(v_src.begin(), v_src.end(), p.v_dev) == v_src.end()) {
-            v_src.push_back(p.v_dev);
-            v_off.push_back(v_total);
-            v_total += (size_t)p.n_kv * p.head_dim;
+        if (p.n_kv > 0) {
+            const size_t k = std::find(v_src.begin(), v_src.end(), p.v_dev) - v_src.begin();
+            if (k == v_src.size()) {
+                v_src.push_back(p.v_dev);
+                v_len.push_back(0);
+            }
+            v_len[k] = std::max(v_len[k], (size_t)p.n_kv * p.head_dim);
         }
+    }
+    std::vector<size_t> v_off(v_src.size(), 0);
+    size_t v_total = 0;
+    for (size_t k = 0; k < v_src.size(); k++) {
+        v_off[k] = v_total;
+        v_total += v_len[k];  // multiples of 256 elements: every copy stays 16-byte aligned
     }
     cudaError_t e = grow_buf(&S->v16, &S->v16_cap, std::max<size_t>(v_total, 1), st);
     if (e != cudaSuccess) {
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
-    // one fp16 copy per distinct V (sizes from the first problem naming it)
-    std::vector<size_t> v_len(v_src.size(), 0);
-    for (int32_t i = 0; i < n; i++) {
-        if (pr[i].n_kv == 0) continue;
-        size_t k = std::find(v_src.begin(), v_src.end(), pr[i].v_dev) - v_src.begin();
-        v_len[k] = std::max(v_len[k], (size_t)pr[i].n_kv * pr[i].head_dim);
-    }
-    for (size_t k = 0; k < v_src.size(); k++) {
-        const size_t cnt = v_len[k];
-        const int blocks = (int)std::min<size_t>((cnt + 255) / 256, 148 * 16);
-        bf16_to_f16_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(v_src[k]), S->v16 + v_off[k],
-                                                   cnt);
+    for (size_t k0 = 0; k0 < v_src.size(); k0 += kMaxSegs) {
+        ConvSegs segs{};
+        const int cnt = (int)std::min<size_t>(kMaxSegs, v_src.size() - k0);
+        uint64_t most = 0;
+        for (int q = 0; q < cnt; q++) {
+            segs.src[q] = reinterpret_cast<const __nv_bfloat16 *>(v_src[k0 + q]);
+            segs.dst[q] = S->v16 + v_off[k0 + q];
+            segs.n8[q] = v_len[k0 + q] / 8;
+            most = std::max(most, segs.n8[q]);
+        }
+        const unsigned bx = (unsigned)std::min<uint64_t>((most + 255) / 256, 1024);
+        bf16_to_f16_kernel<<<dim3(bx, cnt), 256, 0, st>>>(segs);
     }
     std::vector<ProblemDev> hp(std::max(n, 1));
     std::vector<WorkItem> work[2];
@@ -742,18 +802,18 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         d.out = p.out_dev;
         d.lse = p.lse_dev;
         if (p.n_q == 0) continue;
-        if (!encode_2d(&d.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8, kRows)) {
+        if (!cached_map(S, 0, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8, &d.tq)) {
             *msg = "cuTensorMapEncodeTiled failed for Q";
             return G4A_CUDA;
         }
-        if (!encode_out_f32(&d.to, p.out_dev, p.head_dim, (uint64_t)p.n_q * 8)) {
+        if (!cached_map(S, 3, p.out_dev, p.head_dim, (uint64_t)p.n_q * 8, &d.to)) {
             *msg = "cuTensorMapEncodeTiled failed for the output";
             return G4A_CUDA;
         }
         if (p.n_kv > 0) {
             size_t k = std::find(v_src.begin(), v_src.end(), p.v_dev) - v_src.begin();
-            if (!encode_2d(&d.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.k_dev, p.head_dim, p.n_kv, 64) ||
-                !encode_2d(&d.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, S->v16 + v_off[k], p.head_dim, p.n_kv, 64)) {
+            if (!cached_map(S, 1, p.k_dev, p.head_dim, p.n_kv, &d.tk) ||
+                !cached_map(S, 2, S->v16 + v_off[k], p.head_dim, p.n_kv, &d.tv)) {
                 *msg = "cuTensorMapEncodeTiled failed for K/V";
                 return G4A_CUDA;
             }

@@ -164,3 +164,27 @@ def test_prefill_rejects_bad_shapes(ctx, torch_cuda):
     with pytest.raises(g4attn.EngError) as e:
         ctx.prefill([dict(head_dim=128, n_q=16, n_kv=16, q=x, k=x, v=x, out=out)])
     assert e.value.code == g4attn.COMPUTE
+
+
+def test_prefill_shared_values_of_different_lengths(oracle, ctx, torch_cuda):
+    """Problems that read one K/V pair over different key counts (the longer
+    one listed second) and a problem with its own K/V, in one call: the fp16
+    copy of a shared V covers the longest use, and every result matches."""
+    torch = torch_cuda
+    hd = 256
+    q1, k, v = make_qkv(oracle, 11, 100, 300, hd)
+    q2, _, _ = make_qkv(oracle, 12, 300, 1, hd)
+    q3, k3, v3 = make_qkv(oracle, 13, 80, 80, 512)
+    kd, vd = to_dev(torch, k), to_dev(torch, v)
+    outs = [torch.full((n, 8, d), float("nan"), device="cuda") for n, d in ((100, hd), (300, hd), (80, 512))]
+    ctx.prefill([
+        dict(head_dim=hd, window=0, n_q=100, n_kv=100, q=to_dev(torch, q1), k=kd, v=vd, out=outs[0]),
+        dict(head_dim=hd, window=64, n_q=300, n_kv=300, q=to_dev(torch, q2), k=kd, v=vd, out=outs[1]),
+        dict(head_dim=512, window=0, n_q=80, n_kv=80, q=to_dev(torch, q3), k=to_dev(torch, k3), v=to_dev(torch, v3),
+             out=outs[2]),
+    ])
+    ctx.sync()
+    wants = [oracle.prefill_attend(q1, k[:100], v[:100], 8, 0), oracle.prefill_attend(q2, k, v, 8, 64),
+             oracle.prefill_attend(q3, k3, v3, 8, 0)]
+    for got, want in zip(outs, wants):
+        assert max_abs_diff(got.cpu().numpy(), want) <= TOL
