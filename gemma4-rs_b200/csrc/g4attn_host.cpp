@@ -615,12 +615,15 @@ struct Plan {
 };
 
 // Rows per work item. Aims at about two items per SM over the whole call,
-// weighting rows by head width, with at least 16 rows per item.
+// weighting rows by head width, with at least 64 rows per item: the last CTA
+// of a split task merges every partial alone, so a small call (one sequence of
+// a few hundred rows) is faster with a few long items than with many short
+// ones.
 int32_t rows_per_item(int64_t weighted_total, int32_t weight) {
     const int64_t target_items = 2 * 148;
     int64_t w = (weighted_total + target_items - 1) / target_items;
     int64_t rows = (w + weight - 1) / weight;
-    rows = std::max<int64_t>(16, (rows + 15) / 16 * 16);
+    rows = std::max<int64_t>(64, (rows + 15) / 16 * 16);
     return (int32_t)std::min<int64_t>(rows, 1 << 20);
 }
 

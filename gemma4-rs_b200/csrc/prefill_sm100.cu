@@ -674,7 +674,38 @@ struct PrefillScratch {
         }
     };
     std::unordered_map<MapKey, CUtensorMap, MapHash> maps;
+    // The last problem list and what it needs at launch: a call that repeats
+    // it exactly (a model's prompt loop, a benchmark) skips validation, map
+    // encoding, work-list construction and uploads. Everything launched from
+    // here reads only buffers this struct owns or the caller's pointers in the
+    // list, so equal lists mean equal launches.
+    struct ConvLaunch {
+        ConvSegs segs;
+        unsigned bx;
+        int cnt;
+    };
+    std::vector<g4a_prefill_problem> last;
+    bool last_valid = false;
+    std::vector<ConvLaunch> conv;
+    size_t n_work[2] = {0, 0};
 };
+
+static cudaError_t launch_prepared(PrefillScratch *S, int *d_err, cudaStream_t st) {
+    for (const auto &c : S->conv) bf16_to_f16_kernel<<<dim3(c.bx, c.cnt), 256, 0, st>>>(c.segs);
+    if (!S->attr_set) {
+        cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
+        S->attr_set = true;
+    }
+    // two CTAs (one cluster) per work item
+    if (S->n_work[0])
+        prefill_kernel<256><<<2 * (unsigned)S->n_work[0], kThreads, Cfg<256>::kSmemBytes, st>>>(S->d_problems,
+                                                                                             S->d_items, d_err);
+    if (S->n_work[1])
+        prefill_kernel<512><<<2 * (unsigned)S->n_work[1], kThreads, Cfg<512>::kSmemBytes, st>>>(
+            S->d_problems, S->d_items + S->n_work[0], d_err);
+    return cudaGetLastError();
+}
 
 // kind 0: bf16 Q (128-row boxes), 1: bf16 K (64-row boxes), 2: fp16 V (64-row boxes), 3: f32 output
 static bool cached_map(PrefillScratch *S, int kind, const void *base, uint64_t cols, uint64_t rows, CUtensorMap *out) {
@@ -727,6 +758,17 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         *msg = "invalid prefill problem list";
         return G4A_COMPUTE;
     }
+    if (S->last_valid && (size_t)n == S->last.size() &&
+        (n == 0 || std::memcmp(pr, S->last.data(), (size_t)n * sizeof(g4a_prefill_problem)) == 0)) {
+        const cudaError_t e = launch_prepared(S, d_err, st);
+        if (e != cudaSuccess) {
+            *msg = cudaGetErrorString(e);
+            return G4A_CUDA;
+        }
+        return G4A_OK;
+    }
+    S->last_valid = false;
+    S->conv.clear();
     // distinct V arrays -> fp16 copies, each sized for the most rows any problem reads
     std::vector<const void *> v_src;
     std::vector<size_t> v_len;
@@ -785,7 +827,7 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
             most = std::max(most, segs.n8[q]);
         }
         const unsigned bx = (unsigned)std::min<uint64_t>((most + 255) / 256, 1024);
-        bf16_to_f16_kernel<<<dim3(bx, cnt), 256, 0, st>>>(segs);
+        S->conv.push_back({segs, bx, cnt});
     }
     std::vector<ProblemDev> hp(std::max(n, 1));
     std::vector<WorkItem> work[2];
@@ -860,22 +902,14 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
-    if (!S->attr_set) {
-        cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
-        cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
-        S->attr_set = true;
-    }
-    // two CTAs (one cluster) per work item
-    if (!work[0].empty())
-        prefill_kernel<256><<<2 * (unsigned)work[0].size(), kThreads, Cfg<256>::kSmemBytes, st>>>(
-            S->d_problems, S->d_items, d_err);
-    if (!work[1].empty())
-        prefill_kernel<512><<<2 * (unsigned)work[1].size(), kThreads, Cfg<512>::kSmemBytes, st>>>(
-            S->d_problems, S->d_items + work[0].size(), d_err);
-    if ((e = cudaGetLastError()) != cudaSuccess) {
+    S->n_work[0] = work[0].size();
+    S->n_work[1] = work[1].size();
+    if ((e = launch_prepared(S, d_err, st)) != cudaSuccess) {
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
+    S->last.assign(pr, pr + n);
+    S->last_valid = true;
     return G4A_OK;
 }
 

@@ -256,19 +256,35 @@ class Context:
         self.check(lib.g4a_decode_plan(self.h, kv.h, len(layers), arr, n, s, p, ctypes.byref(h)))
         return Plan(self, h)
 
-    def prefill(self, problems: list[dict]):
+    @staticmethod
+    def prefill_args(problems: list[dict]) -> "PrefillArgs":
+        """Packs a problem list once; pass the result to prefill() to skip the
+        per-call packing (the tensors must stay alive)."""
         arr = (PrefillProblem * max(1, len(problems)))()
         for i, a in enumerate(problems):
             arr[i] = PrefillProblem(a["head_dim"], a.get("window", 0), a["n_q"], a.get("q_pos0", 0), a["n_kv"],
                                     a.get("kv_pos0", 0), _ptr(a["q"]), _ptr(a["k"]), _ptr(a["v"]), _ptr(a["out"]),
                                     _ptr(a.get("lse")))
-        self.check(lib.g4a_prefill(self.h, len(problems), arr))
+        return PrefillArgs(arr, len(problems))
+
+    def prefill(self, problems):
+        """g4a_prefill over a list of problem dicts or a prefill_args() result."""
+        args = problems if isinstance(problems, PrefillArgs) else self.prefill_args(problems)
+        self.check(lib.g4a_prefill(self.h, args.n, args.arr))
 
     def lse_merge(self, outs, lses, rows: int, n_heads: int, hd: int, out, lse=None):
         n = len(outs)
         po = (_vp * n)(*[_ptr(t) for t in outs])
         pl = (_vp * n)(*[_ptr(t) for t in lses])
         self.check(lib.g4a_lse_merge(self.h, n, po, pl, rows, n_heads, hd, _ptr(out), _ptr(lse)))
+
+
+class PrefillArgs:
+    """A packed g4a_prefill problem array (see Context.prefill_args)."""
+
+    def __init__(self, arr, n: int):
+        self.arr = arr
+        self.n = n
 
 
 class Plan:

@@ -188,3 +188,28 @@ def test_prefill_shared_values_of_different_lengths(oracle, ctx, torch_cuda):
              oracle.prefill_attend(q3, k3, v3, 8, 0)]
     for got, want in zip(outs, wants):
         assert max_abs_diff(got.cpu().numpy(), want) <= TOL
+
+
+def test_prefill_repeated_list_reads_current_values(oracle, ctx, torch_cuda):
+    """The library reuses its prepared launch for a repeated problem list;
+    the inputs are still read afresh on every call (V changed in place between
+    two identical calls is seen), and a different list afterwards is prepared
+    anew."""
+    torch = torch_cuda
+    hd, T = 256, 150
+    q, k, v = make_qkv(oracle, 21, T, T, hd)
+    _, _, v2 = make_qkv(oracle, 22, 1, T, hd)
+    qd, kd, vd = to_dev(torch, q), to_dev(torch, k), to_dev(torch, v)
+    out = torch.empty(T, 8, hd, device="cuda")
+    args = ctx.prefill_args([dict(head_dim=hd, window=0, n_q=T, n_kv=T, q=qd, k=kd, v=vd, out=out)])
+    ctx.prefill(args)
+    ctx.sync()
+    assert max_abs_diff(out.cpu().numpy(), oracle.prefill_attend(q, k, v, 8, 0)) <= TOL
+    vd.copy_(to_dev(torch, v2))
+    ctx.prefill(args)
+    ctx.sync()
+    assert max_abs_diff(out.cpu().numpy(), oracle.prefill_attend(q, k, v2, 8, 0)) <= TOL
+    out2 = torch.empty(T, 8, hd, device="cuda")
+    ctx.prefill([dict(head_dim=hd, window=64, n_q=T, n_kv=T, q=qd, k=kd, v=vd, out=out2)])
+    ctx.sync()
+    assert max_abs_diff(out2.cpu().numpy(), oracle.prefill_attend(q, k, v2, 8, 64)) <= TOL
