@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     __shared__ __align__(16) float knew_s[HD];
     __shared__ __align__(16) float vnew_s[HD];
     __shared__ float alpha_s[kHeads], m_s[kHeads], l_s[kHeads];
+    __shared__ const KT *krow_s[BLK], *vrow_s[BLK];  // this block's row addresses
     __shared__ int last_s;
 
     const DecodeItem it = p.items[blockIdx.x];
@@ -196,6 +197,13 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
 
     for (int b0 = it.row_lo; b0 < it.row_hi; b0 += BLK) {
         const int nb = min(BLK, it.row_hi - b0);
+        // Row addresses first (one block-table read per row, in parallel), so
+        // that the row loads below do not each wait for their page number.
+        if (threadIdx.x < nb) {
+            krow_s[threadIdx.x] = row_ptr<KT>(tk.k_base, bt, p.page_tokens, HD, b0 + threadIdx.x);
+            vrow_s[threadIdx.x] = row_ptr<KT>(tk.v_base, bt, p.page_tokens, HD, b0 + threadIdx.x);
+        }
+        __syncthreads();
         // ---- scores: warp w takes rows w, w+8, ... of the block ----
 #pragma unroll 4
         for (int r = warp; r < nb; r += kHeads) {
@@ -212,7 +220,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
                     for (int h = 0; h < kHeads; h++) part[h] = fmaf(q_s[h][e], kv, part[h]);
                 }
             } else {
-                const KT *krow = row_ptr<KT>(tk.k_base, bt, p.page_tokens, HD, row);
+                const KT *krow = krow_s[r];
 #pragma unroll
                 for (int k = 0; k < PL; k++) {
                     const int e = lane + 32 * k;
@@ -266,7 +274,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
 #pragma unroll
                 for (int u = 0; u < CPT; u++) v[u] = vnew_s[threadIdx.x + kDecodeThreads * u];
             } else {
-                const KT *vrow = row_ptr<KT>(tk.v_base, bt, p.page_tokens, HD, row);
+                const KT *vrow = vrow_s[r];
 #pragma unroll
                 for (int u = 0; u < CPT; u++) v[u] = load_elem(vrow + threadIdx.x + kDecodeThreads * u);
             }
@@ -337,20 +345,26 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
         }
     }
     __syncthreads();
-    // splits in groups of 8 with every load of a group issued before its sums
-    for (int e = threadIdx.x; e < kHeads * HD; e += kDecodeThreads) {
-        const int h = e / HD;
-        float o = 0.0f;
-        for (int s0 = 0; s0 < ns; s0 += 8) {
-            float x[8];
+    // Each thread owns kHeads*HD/256 output elements and walks the splits in
+    // order, loading all of its elements of a split (and of the next one) at
+    // once: a few rounds of independent loads instead of one round per element.
+    constexpr int EPT = kHeads * HD / kDecodeThreads;
+    float o[EPT];
 #pragma unroll
-            for (int q = 0; q < 8; q++)
-                x[q] = s0 + q < ns ? __ldcg(pall + (size_t)(s0 + q) * kHeads * HD + e) : 0.0f;
+    for (int q = 0; q < EPT; q++) o[q] = 0.0f;
+#pragma unroll 2
+    for (int s = 0; s < ns; s++) {
+        const float *ps = pall + (size_t)s * kHeads * HD + threadIdx.x;
+        float x[EPT];
 #pragma unroll
-            for (int q = 0; q < 8; q++)
-                if (s0 + q < ns) o = fmaf(x[q], wsm[(s0 + q) * kHeads + h], o);
-        }
-        tk.out[e] = o * wsm[ns * kHeads + h];
+        for (int q = 0; q < EPT; q++) x[q] = __ldcg(ps + kDecodeThreads * q);
+#pragma unroll
+        for (int q = 0; q < EPT; q++) o[q] = fmaf(x[q], wsm[s * kHeads + (threadIdx.x + kDecodeThreads * q) / HD], o[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < EPT; q++) {
+        const int e = threadIdx.x + kDecodeThreads * q;
+        tk.out[e] = o[q] * wsm[ns * kHeads + e / HD];
     }
     if (threadIdx.x == 0) p.tickets[it.task] = 0u;  // ready for the next call
 }
