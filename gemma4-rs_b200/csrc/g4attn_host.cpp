@@ -121,9 +121,53 @@ struct g4a_ctx {
     std::vector<cudaEvent_t> spare;
     double prof_ms[G4A_K_COUNT] = {};
     int64_t prof_n[G4A_K_COUNT] = {};
+    // Pinned staging for the small per-call uploads (decode metadata, block
+    // tables): a copy from pageable memory goes through the driver's own
+    // staging and costs tens of microseconds per call. Slots are reused in
+    // turn; an event per slot keeps a slot from being rewritten before the
+    // GPU has read its previous contents.
+    struct PinnedSlot {
+        uint8_t *p = nullptr;
+        size_t cap = 0;
+        cudaEvent_t ev = nullptr;
+        bool pending = false;
+    };
+    PinnedSlot pin[4];
+    int pin_next = 0;
 };
 
 namespace {
+
+int fail(g4a_ctx *ctx, int code, const char *fmt, ...);
+
+// Host-to-device copy of `bytes` from `src` on the context's stream through
+// a pinned staging slot (falls back to a pageable copy if pinning fails).
+cudaError_t upload(g4a_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    if (!bytes) return cudaSuccess;
+    g4a_ctx::PinnedSlot &sl = ctx->pin[ctx->pin_next];
+    ctx->pin_next = (ctx->pin_next + 1) % 4;
+    if (sl.pending) {
+        cudaError_t e = cudaEventSynchronize(sl.ev);
+        if (e != cudaSuccess) return e;
+        sl.pending = false;
+    }
+    if (!sl.ev && cudaEventCreateWithFlags(&sl.ev, cudaEventDisableTiming) != cudaSuccess) sl.ev = nullptr;
+    if (sl.cap < bytes) {
+        if (sl.p) cudaFreeHost(sl.p);
+        sl.p = nullptr;
+        sl.cap = 0;
+        const size_t want = std::max<size_t>(bytes, 1 << 16);
+        if (cudaHostAlloc(reinterpret_cast<void **>(&sl.p), want, cudaHostAllocDefault) == cudaSuccess) sl.cap = want;
+        else sl.p = nullptr;
+    }
+    if (!sl.p || !sl.ev) return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    std::memcpy(sl.p, src, bytes);
+    cudaError_t e = cudaMemcpyAsync(dst, sl.p, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return e;
+    e = cudaEventRecord(sl.ev, ctx->stream);
+    sl.pending = e == cudaSuccess;
+    return e;
+}
 
 int fail(g4a_ctx *ctx, int code, const char *fmt, ...) {
     if (ctx) {
@@ -310,6 +354,10 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
     cudaFree(ctx->d_qblocks);
     for (auto &r : ctx->recs) cudaEventDestroy(r.a), cudaEventDestroy(r.b);
     for (auto e : ctx->spare) cudaEventDestroy(e);
+    for (auto &sl : ctx->pin) {
+        if (sl.p) cudaFreeHost(sl.p);
+        if (sl.ev) cudaEventDestroy(sl.ev);
+    }
     prefill_scratch_free(ctx->prefill);
     delete ctx;
 }
@@ -380,8 +428,7 @@ int ensure_rows(g4a_kv *kv, int32_t seq, int64_t rows) {
 
 int upload_bt(g4a_kv *kv) {
     if (!kv->bt_dirty) return G4A_OK;
-    G4A_CUDA_TRY(kv->ctx, cudaMemcpyAsync(kv->d_bt, kv->h_bt.data(), kv->h_bt.size() * sizeof(int32_t),
-                                          cudaMemcpyHostToDevice, kv->ctx->stream));
+    G4A_CUDA_TRY(kv->ctx, upload(kv->ctx, kv->d_bt, kv->h_bt.data(), kv->h_bt.size() * sizeof(int32_t)));
     kv->bt_dirty = false;
     return G4A_OK;
 }
@@ -710,7 +757,7 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
     if (!split_tasks.empty())
         std::memcpy(ctx->h_meta.data() + bytes_tasks + bytes_items + bytes_cta, split_tasks.data(),
                     split_tasks.size() * sizeof(int32_t));
-    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(st->meta, ctx->h_meta.data(), bytes, cudaMemcpyHostToDevice, ctx->stream));
+    G4A_CUDA_TRY(ctx, upload(ctx, st->meta, ctx->h_meta.data(), bytes));
     DecodeParams &p = st->params;
     p = DecodeParams{};
     p.tasks = reinterpret_cast<const DecodeTask *>(st->meta);
