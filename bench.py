@@ -586,6 +586,8 @@ def main():
 
     dist = None
     if world > 1:
+        # NCCL's version banner goes to stdout by default; stdout carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         import torch.distributed as dist_mod
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
