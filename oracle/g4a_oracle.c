@@ -615,3 +615,149 @@ int orc_prefill_attend(const float *q, const float *k, const float *v, size_t T,
     }
     return ORC_OK;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Q8_0 mat-vec: crates/llm-backend-cpu/src/matvec.rs                         */
+/* ------------------------------------------------------------------------ */
+
+#define Q8_BLOCK 32       /* matvec.rs:15 Q8_0_BLOCK_VALUES */
+#define Q8_BLOCK_BYTES 34 /* matvec.rs:16 Q8_0_BLOCK_BYTES */
+#define MATVEC_PARALLEL_MIN_WORK ((size_t)1 << 20) /* matvec.rs:223 */
+
+/* f32 -> i8 as Rust's `as i8` does: saturating, NaN -> 0. */
+static int8_t sat_i8(float v) {
+    if (v != v) return 0;
+    if (v >= 127.0f) return 127;
+    if (v <= -128.0f) return -128;
+    return (int8_t)v;
+}
+
+static float f16_le(const uint8_t *b) {
+    uint16_t bits = (uint16_t)(b[0] | (b[1] << 8));
+    _Float16 h;
+    memcpy(&h, &bits, 2);
+    return (float)h;
+}
+
+/* matvec.rs:36-54 quantize_q8_0: per 32 values, scale = max|x| / 127 (f32),
+ * inverse = 1 / scale (0 for a zero scale), stored scale rounded to f16,
+ * quants = round_ties_even(x * inverse) cast to i8. */
+int orc_quantize_q8_0(const float *x, size_t n, float *scales, int8_t *quants) {
+    if (n % Q8_BLOCK) return ORC_COMPUTE;
+    for (size_t b = 0; b < n / Q8_BLOCK; b++) {
+        const float *blk = x + b * Q8_BLOCK;
+        float max = 0.0f;
+        for (int i = 0; i < Q8_BLOCK; i++) max = fmaxf(max, fabsf(blk[i]));
+        float scale = max / 127.0f;
+        float inverse = scale == 0.0f ? 0.0f : 1.0f / scale;
+        scales[b] = (float)(_Float16)scale;
+        for (int i = 0; i < Q8_BLOCK; i++) quants[b * Q8_BLOCK + i] = sat_i8(rintf(blk[i] * inverse));
+    }
+    return ORC_OK;
+}
+
+/* matvec.rs:137-150 dot_q8_0: integer dot per block, times (w_scale *
+ * x_scale), summed over blocks in order. Rust's f32 `Sum` starts from -0.0. */
+static float dot_q8_0(const uint8_t *row, size_t nb, const float *scales, const int8_t *quants) {
+    float sum = -0.0f;
+    for (size_t b = 0; b < nb; b++) {
+        const uint8_t *blk = row + b * Q8_BLOCK_BYTES;
+        float ws = f16_le(blk);
+        int32_t dot = 0;
+        for (int i = 0; i < Q8_BLOCK; i++) dot += (int32_t)(int8_t)blk[2 + i] * (int32_t)quants[b * Q8_BLOCK + i];
+        sum = sum + (float)dot * (ws * scales[b]);
+    }
+    return sum;
+}
+
+/* ops.rs:85-89 gelu_tanh, evaluated left to right without fused multiply-adds. */
+float orc_gelu_tanh(float x) {
+    const float sqrt_2_over_pi = 0.7978846f, coef_a = 0.044715f;
+    return 0.5f * x * (1.0f + tanhf(sqrt_2_over_pi * x * (1.0f + coef_a * x * x)));
+}
+
+/* ops.rs:79-81 softcap: tanh(value / cap) * cap, with the division as a
+ * multiplication by the reciprocal. */
+float orc_softcap(float v, float cap) { return tanhf(v * (1.0f / cap)) * cap; }
+
+typedef struct {
+    const uint8_t *w, *w2;
+    size_t cols;
+    const float *scales;
+    const int8_t *quants;
+    float cap;
+    int kind; /* 0 matvec, 1 geglu, 2 softcap */
+    float *out;
+} q8_job;
+
+static void q8_rows(void *c, size_t lo, size_t hi) {
+    const q8_job *j = (const q8_job *)c;
+    const size_t nb = j->cols / Q8_BLOCK, row_len = nb * Q8_BLOCK_BYTES;
+    for (size_t r = lo; r < hi; r++) {
+        float v = dot_q8_0(j->w + r * row_len, nb, j->scales, j->quants);
+        if (j->kind == 1) v = orc_gelu_tanh(v) * dot_q8_0(j->w2 + r * row_len, nb, j->scales, j->quants);
+        else if (j->kind == 2) v = orc_softcap(v, j->cap);
+        j->out[r] = v;
+    }
+}
+
+/* matvec.rs:58-63 / :88-103 / :67-80, rows split over the pool.rs workers
+ * above 2^20 multiply-adds (matvec.rs:223), as map_rows / map_indices do. */
+static int q8_run(const uint8_t *w, const uint8_t *w2, size_t rows, size_t cols, const float *scales,
+                  const int8_t *quants, float cap, int kind, float *out) {
+    if (cols % Q8_BLOCK || !w || (kind == 1 && !w2)) return ORC_COMPUTE;
+    q8_job j = {w, w2, cols, scales, quants, cap, kind, out};
+    run_chunks(rows, kind == 1 ? 2 * cols : cols, MATVEC_PARALLEL_MIN_WORK, q8_rows, &j);
+    return ORC_OK;
+}
+
+int orc_matvec_q8_0(const uint8_t *w, size_t rows, size_t cols, const float *scales, const int8_t *quants,
+                    float *out) {
+    return q8_run(w, NULL, rows, cols, scales, quants, 0.0f, 0, out);
+}
+int orc_geglu_q8_0(const uint8_t *gate, const uint8_t *up, size_t rows, size_t cols, const float *scales,
+                   const int8_t *quants, float *out) {
+    return q8_run(gate, up, rows, cols, scales, quants, 0.0f, 1, out);
+}
+int orc_matvec_q8_0_softcap(const uint8_t *w, size_t rows, size_t cols, const float *scales,
+                            const int8_t *quants, float cap, float *out) {
+    return q8_run(w, NULL, rows, cols, scales, quants, cap, 2, out);
+}
+
+/* dequant.rs:13-24 */
+int orc_dequant_q8_0(const uint8_t *bytes, size_t n_bytes, float *out) {
+    if (n_bytes % Q8_BLOCK_BYTES) return ORC_COMPUTE;
+    for (size_t b = 0; b < n_bytes / Q8_BLOCK_BYTES; b++) {
+        const uint8_t *blk = bytes + b * Q8_BLOCK_BYTES;
+        float scale = f16_le(blk);
+        for (int i = 0; i < Q8_BLOCK; i++) out[b * Q8_BLOCK + i] = (float)(int8_t)blk[2 + i] * scale;
+    }
+    return ORC_OK;
+}
+
+/* tests/matvec.rs:10-18 values(): an LCG, top 24 bits mapped to [-1, 1). */
+void orc_test_values(uint64_t seed, size_t len, float *out) {
+    uint64_t state = seed;
+    for (size_t i = 0; i < len; i++) {
+        state = state * 6364136223846793005ull + 1ull;
+        out[i] = (float)(state >> 40) / (float)(1u << 23) - 1.0f;
+    }
+}
+
+/* tests/matvec.rs:21-31 q8_0_bytes(): scale = max|w| / 127, bytes of its f16,
+ * then round-half-away(w / scale) cast to i8. */
+void orc_test_q8_0_bytes(const float *w, size_t n, uint8_t *out) {
+    for (size_t b = 0; b < n / Q8_BLOCK; b++) {
+        const float *blk = w + b * Q8_BLOCK;
+        float max = 0.0f;
+        for (int i = 0; i < Q8_BLOCK; i++) max = fmaxf(max, fabsf(blk[i]));
+        float scale = max / 127.0f;
+        _Float16 h = (_Float16)scale;
+        uint16_t bits;
+        memcpy(&bits, &h, 2);
+        uint8_t *o = out + b * Q8_BLOCK_BYTES;
+        o[0] = (uint8_t)(bits & 0xff);
+        o[1] = (uint8_t)(bits >> 8);
+        for (int i = 0; i < Q8_BLOCK; i++) o[2 + i] = (uint8_t)sat_i8(roundf(blk[i] / scale));
+    }
+}

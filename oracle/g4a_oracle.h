@@ -99,6 +99,25 @@ float orc_round_bf16(float x);
 int orc_prefill_attend(const float *q, const float *k, const float *v, size_t T, size_t n_heads,
                        size_t head_dim, size_t window, float *out);
 
+/* ---- Q8_0 mat-vec: crates/llm-backend-cpu/src/matvec.rs ----
+ * Weights are GGUF Q8_0 rows: cols/32 blocks of (f16 scale little-endian,
+ * 32 int8 values). The activation is quantized first (quantize_q8_0), then
+ * every row is an int8 dot product per block, scaled, summed over blocks in
+ * order. All functions return ORC_COMPUTE on shape errors. */
+int orc_quantize_q8_0(const float *x, size_t n, float *scales, int8_t *quants);
+int orc_matvec_q8_0(const uint8_t *w, size_t rows, size_t cols, const float *scales, const int8_t *quants,
+                    float *out);
+int orc_geglu_q8_0(const uint8_t *gate, const uint8_t *up, size_t rows, size_t cols, const float *scales,
+                   const int8_t *quants, float *out);
+int orc_matvec_q8_0_softcap(const uint8_t *w, size_t rows, size_t cols, const float *scales,
+                            const int8_t *quants, float cap, float *out);
+float orc_gelu_tanh(float x);
+float orc_softcap(float v, float cap);
+int orc_dequant_q8_0(const uint8_t *bytes, size_t n_bytes, float *out);
+/* The reference test file's fixtures (crates/llm-backend-cpu/tests/matvec.rs). */
+void orc_test_values(uint64_t seed, size_t len, float *out);
+void orc_test_q8_0_bytes(const float *w, size_t n, uint8_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -76,6 +76,20 @@ def lib():
         L.orc_round_bf16.argtypes = [ctypes.c_float]
         L.orc_round_bf16.restype = ctypes.c_float
         L.orc_prefill_attend.argtypes = [_f32p, _f32p, _f32p, sz, sz, sz, sz, _f32p]
+        u8p, i8p = ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(ctypes.c_int8)
+        L.orc_quantize_q8_0.argtypes = [_f32p, sz, _f32p, i8p]
+        L.orc_matvec_q8_0.argtypes = [u8p, sz, sz, _f32p, i8p, _f32p]
+        L.orc_geglu_q8_0.argtypes = [u8p, u8p, sz, sz, _f32p, i8p, _f32p]
+        L.orc_matvec_q8_0_softcap.argtypes = [u8p, sz, sz, _f32p, i8p, ctypes.c_float, _f32p]
+        L.orc_gelu_tanh.argtypes = [ctypes.c_float]
+        L.orc_gelu_tanh.restype = ctypes.c_float
+        L.orc_softcap.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.orc_softcap.restype = ctypes.c_float
+        L.orc_dequant_q8_0.argtypes = [u8p, sz, _f32p]
+        L.orc_test_values.argtypes = [ctypes.c_uint64, sz, _f32p]
+        L.orc_test_values.restype = None
+        L.orc_test_q8_0_bytes.argtypes = [_f32p, sz, u8p]
+        L.orc_test_q8_0_bytes.restype = None
         _lib = L
     return _lib
 
@@ -258,3 +272,75 @@ class KvCache:
 
 if __name__ == "__main__":  # pragma: no cover
     print(LIB_PATH, os.path.exists(LIB_PATH))
+
+
+# ---------------------------------------------------------------------------
+# Q8_0 mat-vec (crates/llm-backend-cpu/src/matvec.rs)
+# ---------------------------------------------------------------------------
+
+def _u8(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))
+
+
+def _i8(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_int8))
+
+
+def quantize_q8_0(x):
+    """(scales f32 [n/32], quants int8 [n]) as quantize_q8_0 (matvec.rs:36-54)."""
+    x = f32(x).ravel()
+    scales = np.empty(len(x) // 32, np.float32)
+    quants = np.empty(len(x), np.int8)
+    _check(lib().orc_quantize_q8_0(_p(x), len(x), _p(scales), _i8(quants)), "quantize_q8_0")
+    return scales, quants
+
+
+def _q8_call(fn, args, rows):
+    out = np.empty(rows, np.float32)
+    _check(fn(*args, _p(out)), fn.__name__)
+    return out
+
+
+def matvec_q8_0(w: np.ndarray, rows: int, cols: int, scales, quants):
+    w = np.ascontiguousarray(w, np.uint8)
+    return _q8_call(lib().orc_matvec_q8_0, (_u8(w), rows, cols, _p(scales), _i8(quants)), rows)
+
+
+def geglu_q8_0(gate: np.ndarray, up: np.ndarray, rows: int, cols: int, scales, quants):
+    gate, up = np.ascontiguousarray(gate, np.uint8), np.ascontiguousarray(up, np.uint8)
+    return _q8_call(lib().orc_geglu_q8_0, (_u8(gate), _u8(up), rows, cols, _p(scales), _i8(quants)), rows)
+
+
+def matvec_q8_0_softcap(w: np.ndarray, rows: int, cols: int, scales, quants, cap: float):
+    w = np.ascontiguousarray(w, np.uint8)
+    return _q8_call(lib().orc_matvec_q8_0_softcap, (_u8(w), rows, cols, _p(scales), _i8(quants), cap), rows)
+
+
+def gelu_tanh(x):
+    return np.array([lib().orc_gelu_tanh(float(v)) for v in np.ravel(x)], np.float32)
+
+
+def softcap(x, cap: float):
+    return np.array([lib().orc_softcap(float(v), cap) for v in np.ravel(x)], np.float32)
+
+
+def dequant_q8_0(b: np.ndarray):
+    b = np.ascontiguousarray(b, np.uint8)
+    out = np.empty(len(b) // 34 * 32, np.float32)
+    _check(lib().orc_dequant_q8_0(_u8(b), len(b), _p(out)), "dequant_q8_0")
+    return out
+
+
+def lcg_values(seed: int, n: int):
+    """The reference test file's LCG values in [-1, 1) (tests/matvec.rs:10-18)."""
+    out = np.empty(n, np.float32)
+    lib().orc_test_values(seed, n, _p(out))
+    return out
+
+
+def q8_0_bytes_of(w):
+    """The reference test file's Q8_0 quantizer for weights (tests/matvec.rs:21-31)."""
+    w = f32(w).ravel()
+    out = np.empty(len(w) // 32 * 34, np.uint8)
+    lib().orc_test_q8_0_bytes(_p(w), len(w), _u8(out))
+    return out
