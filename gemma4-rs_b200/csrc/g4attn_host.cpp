@@ -134,6 +134,11 @@ struct g4a_ctx {
     };
     PinnedSlot pin[4];
     int pin_next = 0;
+    // Q8_0 mat-vec: the quantized activations of the current call
+    int8_t *d_q8x = nullptr;
+    size_t q8x_cap = 0;
+    float *d_q8s = nullptr;
+    size_t q8s_cap = 0;
 };
 
 namespace {
@@ -354,6 +359,8 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
     cudaFree(ctx->d_qblocks);
     for (auto &r : ctx->recs) cudaEventDestroy(r.a), cudaEventDestroy(r.b);
     for (auto e : ctx->spare) cudaEventDestroy(e);
+    cudaFree(ctx->d_q8x);
+    cudaFree(ctx->d_q8s);
     for (auto &sl : ctx->pin) {
         if (sl.p) cudaFreeHost(sl.p);
         if (sl.ev) cudaEventDestroy(sl.ev);
@@ -1104,5 +1111,67 @@ extern "C" int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *p
     });
     (void)e;
     if (rc != G4A_OK) return fail(ctx, rc, "compute: %s", msg);
+    return G4A_OK;
+}
+
+// ---- Q8_0 mat-vec family (matvec.rs) -------------------------------------
+
+namespace {
+
+int q8_entry(g4a_ctx *ctx, int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x,
+             int32_t n_vec, float cap, float *out) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (cols <= 0 || cols % 32 != 0)  // matvec.rs:37-42
+        return fail(ctx, G4A_COMPUTE, "Q8_0 activation length %lld is not a multiple of 32", (long long)cols);
+    if (rows < 0 || n_vec < 1 || n_vec > 65535 || cols > (1LL << 30) || !x || (rows > 0 && (!w || !out)) ||
+        (kind == 1 && rows > 0 && !w2))
+        return fail(ctx, G4A_COMPUTE, "compute: invalid Q8_0 mat-vec arguments");
+    int rc;
+    if ((rc = grow(ctx, &ctx->d_q8x, &ctx->q8x_cap, (size_t)n_vec * cols, false)) ||
+        (rc = grow(ctx, &ctx->d_q8s, &ctx->q8s_cap, (size_t)n_vec * cols / 32, false)))
+        return rc;
+    const char *msg = "";
+    int status = G4A_OK;
+    const cudaError_t e = timed(ctx, G4A_K_MATVEC_Q8, [&] {
+        status = q8_run(kind, w, w2, rows, cols, x, n_vec, cap, out, ctx->d_q8x, ctx->d_q8s, ctx->d_err, ctx->n_sm,
+                        ctx->stream, &msg);
+        return cudaSuccess;
+    });
+    (void)e;
+    if (status != G4A_OK) return fail(ctx, status, "compute: %s", msg);
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_matvec_q8_0(g4a_ctx *ctx, const uint8_t *w_dev, int64_t rows, int64_t cols, const float *x_dev,
+                               int32_t n_vec, float *out_dev) {
+    return q8_entry(ctx, 0, w_dev, nullptr, rows, cols, x_dev, n_vec, 0.0f, out_dev);
+}
+
+extern "C" int g4a_geglu_q8_0(g4a_ctx *ctx, const uint8_t *gate_dev, const uint8_t *up_dev, int64_t rows, int64_t cols,
+                              const float *x_dev, int32_t n_vec, float *out_dev) {
+    return q8_entry(ctx, 1, gate_dev, up_dev, rows, cols, x_dev, n_vec, 0.0f, out_dev);
+}
+
+extern "C" int g4a_matvec_q8_0_softcap(g4a_ctx *ctx, const uint8_t *w_dev, int64_t rows, int64_t cols,
+                                       const float *x_dev, int32_t n_vec, float cap, float *out_dev) {
+    if (!(cap != 0.0f)) return fail(ctx, G4A_COMPUTE, "compute: soft-cap of zero");
+    return q8_entry(ctx, 2, w_dev, nullptr, rows, cols, x_dev, n_vec, cap, out_dev);
+}
+
+extern "C" int g4a_quantize_q8_0(g4a_ctx *ctx, const float *x_dev, int64_t n, float *scales_dev, int8_t *quants_dev) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (n < 0 || n % 32 != 0)
+        return fail(ctx, G4A_COMPUTE, "Q8_0 activation length %lld is not a multiple of 32", (long long)n);
+    if (n == 0) return G4A_OK;
+    if (!x_dev || !scales_dev || !quants_dev) return fail(ctx, G4A_COMPUTE, "compute: null Q8_0 buffers");
+    const char *msg = "";
+    // rows = 0: quantize only
+    int status = q8_run(0, nullptr, nullptr, 0, n, x_dev, 1, 0.0f, nullptr, quants_dev, scales_dev, ctx->d_err,
+                        ctx->n_sm, ctx->stream, &msg);
+    if (status != G4A_OK) return fail(ctx, status, "compute: %s", msg);
     return G4A_OK;
 }

@@ -102,6 +102,10 @@ bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint6
 
 // Prefill (prefill_sm100.cu): per-context scratch and the launcher behind
 // g4a_prefill. Returns a g4a_status and points *msg at a description.
+// Q8_0 mat-vec family (q8_0_sm100.cu); kind 0 plain, 1 GEGLU (w2 = up), 2 soft-cap.
+int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
+           float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg);
+
 struct PrefillScratch;
 PrefillScratch *prefill_scratch_new();
 void prefill_scratch_free(PrefillScratch *s);

@@ -91,6 +91,15 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const void *tmap, ui
         "l"(tmap), "r"(bar_cl), "r"(x), "r"(y)
         : "memory");
 }
+// 1-D bulk copy global -> this CTA's shared memory (no multicast); both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // TMA 2D tiled store from this CTA's shared memory (bulk-group completion).
 // x must keep x * element size a multiple of 16 bytes and x, y >= 0.
 __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int32_t x, int32_t y) {

@@ -26,7 +26,7 @@ HEADER = HERE.parent.parent / "include" / "g4attn.h"
 OK, CONTEXT_TOO_LONG, MISSING_LAYER, MISSING_WEIGHT, COMPUTE, NONFINITE, BAD_LAYER, CUDA, NCCL, TIMEOUT, \
     OUT_OF_PAGES = range(11)
 KV_F32, KV_F16 = 0, 1
-K_DECODE_PREP, K_DECODE_MAIN, K_DECODE_COMBINE, K_DECODE_SPLITKV, K_PREFILL = range(5)
+K_DECODE_PREP, K_DECODE_MAIN, K_DECODE_COMBINE, K_DECODE_SPLITKV, K_PREFILL, K_MATVEC_Q8 = range(6)
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -108,6 +108,11 @@ def _load():
                                    ctypes.POINTER(ctypes.c_int64)]
     L.g4a_lse_merge.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.c_int64,
                                 ctypes.c_int32, ctypes.c_int32, _vp, _vp]
+    L.g4a_matvec_q8_0.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int32, _vp]
+    L.g4a_geglu_q8_0.argtypes = [_vp, _vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int32, _vp]
+    L.g4a_matvec_q8_0_softcap.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int32,
+                                          ctypes.c_float, _vp]
+    L.g4a_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64, _vp, _vp]
     return L
 
 
@@ -271,6 +276,19 @@ class Context:
         """g4a_prefill over a list of problem dicts or a prefill_args() result."""
         args = problems if isinstance(problems, PrefillArgs) else self.prefill_args(problems)
         self.check(lib.g4a_prefill(self.h, args.n, args.arr))
+
+    # ---- Q8_0 mat-vec (matvec.rs): w is a uint8 tensor of GGUF Q8_0 rows ----
+    def matvec_q8_0(self, w, rows: int, cols: int, x, out, n_vec: int = 1):
+        self.check(lib.g4a_matvec_q8_0(self.h, _ptr(w), rows, cols, _ptr(x), n_vec, _ptr(out)))
+
+    def geglu_q8_0(self, gate, up, rows: int, cols: int, x, out, n_vec: int = 1):
+        self.check(lib.g4a_geglu_q8_0(self.h, _ptr(gate), _ptr(up), rows, cols, _ptr(x), n_vec, _ptr(out)))
+
+    def matvec_q8_0_softcap(self, w, rows: int, cols: int, x, cap: float, out, n_vec: int = 1):
+        self.check(lib.g4a_matvec_q8_0_softcap(self.h, _ptr(w), rows, cols, _ptr(x), n_vec, cap, _ptr(out)))
+
+    def quantize_q8_0(self, x, n: int, scales, quants):
+        self.check(lib.g4a_quantize_q8_0(self.h, _ptr(x), n, _ptr(scales), _ptr(quants)))
 
     def lse_merge(self, outs, lses, rows: int, n_heads: int, hd: int, out, lse=None):
         n = len(outs)

@@ -111,7 +111,8 @@ typedef enum g4a_kernel {
     G4A_K_DECODE_COMBINE = 2,  /* f16 decode: merge of split tasks */
     G4A_K_DECODE_SPLITKV = 3,  /* f32 caches and g4a_attend */
     G4A_K_PREFILL = 4,         /* tcgen05 prefill (with its V conversion) */
-    G4A_K_COUNT = 5
+    G4A_K_MATVEC_Q8 = 5,       /* Q8_0 mat-vec family (with its activation quantization) */
+    G4A_K_COUNT = 6
 } g4a_kernel;
 int g4a_profile_enable(g4a_ctx *ctx, int enable);
 int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches);
@@ -244,6 +245,32 @@ int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *problems_hos
 int g4a_lse_merge(g4a_ctx *ctx, int32_t n_parts, const float *const *parts_out_host,
                   const float *const *parts_lse_host, int64_t rows, int32_t n_heads,
                   int32_t head_dim, float *out_dev, float *lse_dev);
+
+/* ---- Q8_0 mat-vec: the projections either side of attention ------------
+ * crates/llm-backend-cpu/src/matvec.rs with the model's default numerics
+ * (quantized activations, model.rs:46-63). Weights are GGUF Q8_0 rows as the
+ * reference reads them: `rows` rows of cols/32 blocks of [f16 scale (little
+ * endian), 32 x int8], in device memory. x_dev holds n_vec activation vectors
+ * [n_vec][cols] f32; each is quantized like quantize_q8_0 (matvec.rs:36-54)
+ * and out_dev receives [n_vec][rows] f32. cols must be a multiple of 32
+ * (G4A_COMPUTE otherwise, as the reference's error). Results equal the
+ * reference's bit for bit for the plain mat-vec (integer block dot products,
+ * block values summed in order); GEGLU and soft-cap add the device tanhf. */
+
+/* matvec.rs:58-63 matvec_q8_0(w, rows, quantize_q8_0(x)) */
+int g4a_matvec_q8_0(g4a_ctx *ctx, const uint8_t *w_dev, int64_t rows, int64_t cols, const float *x_dev,
+                    int32_t n_vec, float *out_dev);
+/* matvec.rs:88-103 geglu_q8_0 with gelu_tanh (ops.rs:85-89), as
+ * model.rs:229-240 gated_ffn_input calls it */
+int g4a_geglu_q8_0(g4a_ctx *ctx, const uint8_t *gate_dev, const uint8_t *up_dev, int64_t rows, int64_t cols,
+                   const float *x_dev, int32_t n_vec, float *out_dev);
+/* matvec.rs:67-80 matvec_q8_0_then with softcap (ops.rs:79-81), as
+ * model.rs:438-449 logits calls it */
+int g4a_matvec_q8_0_softcap(g4a_ctx *ctx, const uint8_t *w_dev, int64_t rows, int64_t cols, const float *x_dev,
+                            int32_t n_vec, float cap, float *out_dev);
+/* matvec.rs:36-54 quantize_q8_0 alone: n values (a multiple of 32) to
+ * n/32 scales and n int8 quants. */
+int g4a_quantize_q8_0(g4a_ctx *ctx, const float *x_dev, int64_t n, float *scales_dev, int8_t *quants_dev);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop
