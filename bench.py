@@ -464,16 +464,84 @@ def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, w
             "timing": "CUDA events per repetition, median over reps, max over ranks"}
 
 
+def q8_head_weights(torch, rows: int, cols: int, seed: int = 1):
+    """The reference's mat-vec benchmark input (crates/llm-backend-cpu/
+    examples/bench_matvec.rs): Q8_0 rows whose block scales are all f16(0.01)
+    and whose quants are pseudo-random bytes, built on the device."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    n_blocks = rows * cols // 32
+    blocks = torch.empty(n_blocks, 34, dtype=torch.uint8, device="cuda")
+    scale = torch.tensor([0.01], dtype=torch.float16).view(torch.uint8)
+    blocks[:, 0] = scale[0]
+    blocks[:, 1] = scale[1]
+    blocks[:, 2:] = torch.randint(0, 256, (n_blocks, 32), dtype=torch.uint8, device="cuda", generator=gen)
+    return blocks.view(-1)
+
+
+def measure_q8_head(torch, g4a, ctx, stream, pk, reps=10, warmup=3, cpu_rows=8192):
+    """The output head's mat-vec at the reference benchmark's shape (262,144 x
+    1,536 Q8_0, 428 MB): device time per call (CUDA events, weights larger than
+    L2) against the measured HBM copy bandwidth, and the oracle port on the
+    host cores over a row sample of the same weights."""
+    import oracle
+    rows, cols = 262_144, 1536
+    w = q8_head_weights(torch, rows, cols)
+    x = torch.sin(torch.arange(cols, dtype=torch.float32, device="cuda") * 0.37)[None, :]
+    out = torch.empty(1, rows, device="cuda")
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            ctx.matvec_q8_0(w, rows, cols, x, out)
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ctx.matvec_q8_0(w, rows, cols, x, out)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+    ctx.sync()
+    ms = statistics.median(ts)
+    nbytes = rows * cols // 32 * 34 + cols * 4 + rows * 4
+    gbs = nbytes / ms / 1e6
+    # CPU: the oracle's pool-threaded restatement on the first cpu_rows rows
+    row_len = cols // 32 * 34
+    w_host = w[: cpu_rows * row_len].cpu().numpy()
+    s, q = oracle.quantize_q8_0(x[0].cpu().numpy())
+    cores = oracle.pool_init(0)
+    oracle.matvec_q8_0(w_host, cpu_rows, cols, s, q)
+    t0 = time.perf_counter()
+    n_cpu = 0
+    while time.perf_counter() - t0 < 1.0:
+        oracle.matvec_q8_0(w_host, cpu_rows, cols, s, q)
+        n_cpu += 1
+    cpu_s = (time.perf_counter() - t0) / n_cpu
+    cpu_gbs = cpu_rows * row_len / cpu_s / 1e9
+    del w
+    return {"shape": [rows, cols], "ms": round(ms, 4), "GB_s": round(gbs, 1), "frac_of_hbm": round(gbs / pk["hbm"], 4),
+            "bytes": nbytes, "timing": "CUDA events, median of %d calls (activation quantization included)" % reps,
+            "cpu_port": {"GB_s": round(cpu_gbs, 2), "cores": cores, "sample_rows": cpu_rows,
+                         "ms_full_equiv": round(rows * row_len / cpu_gbs / 1e6, 2)}}
+
+
 def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     """One prefill problem on its own (for profiling one kernel on a small
     case): spec "prefill:<head width>:<tokens>:<window>", "prefill-cfg1"
     for configuration 1 alone (35 layer-equivalents in one call), or
-    "decode-batch1" for configuration 0's latency."""
+    "decode-batch1" for configuration 0's latency, or "q8-head" for the
+    Q8_0 output-head mat-vec."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
     if spec == "decode-batch1":
         stream = torch.cuda.Stream()
         ctx.set_stream(stream.cuda_stream)
         res = measure_batch1(torch, g4a, ctx, stream)
+        ctx.close()
+        print(json.dumps({"case": spec, **res}), flush=True)
+        return
+    if spec == "q8-head":
+        stream = torch.cuda.Stream()
+        ctx.set_stream(stream.cuda_stream)
+        res = measure_q8_head(torch, g4a, ctx, stream, peaks(), reps=max(reps, 1), warmup=max(warmup, 1))
         ctx.close()
         print(json.dumps({"case": spec, **res}), flush=True)
         return
@@ -627,6 +695,7 @@ def main():
     if rank == 0 and not a.no_extras:
         extras["decode_batch1"] = measure_batch1(torch, g4a, ctx, stream)
         extras["prefill"] = measure_prefill(torch, g4a, ctx, stream, pk)
+        extras["q8_0_matvec_head"] = measure_q8_head(torch, g4a, ctx, stream, pk)
     ctx.close()
     if dist is not None:
         dist.barrier()

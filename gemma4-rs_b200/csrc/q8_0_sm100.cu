@@ -12,11 +12,17 @@
 //
 // Weights stay in the GGUF Q8_0 byte layout the reference reads (rows of
 // cols/32 blocks of [f16 scale, 32 x int8]); nothing is repacked. The kernel
-// streams them: persistent CTAs take tiles of consecutive rows (one
-// contiguous span of bytes) through a 4-stage ring of 1-D bulk copies, so the
-// weights cross HBM once per call whatever the number of activation vectors
-// (up to 8 per pass). Warps 0-7 compute every block value of a tile into
-// shared memory; then one thread per (vector, row) adds them in order.
+// streams them: persistent CTAs (several per SM) take tiles of consecutive
+// rows (one contiguous span of bytes, about 16 KB) through a 4-stage ring of
+// 1-D bulk copies, so the weights cross HBM once per call whatever the number
+// of activation vectors (up to 8 per pass). Roles per CTA:
+//   warps 0-7  every block's dot product and value, into a double-buffered
+//              shared-memory table (one padded row per matrix row);
+//   warp 8     the bulk copies;
+//   warp 9     the in-order sums, one lane per (vector, row), overlapping the
+//              next tile's dot products.
+// Hand-offs are mbarriers (stage full / empty, table full / empty); no
+// barrier spans the CTA inside the loop.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -33,10 +39,13 @@ constexpr int kQ8Block = 32;
 constexpr int kQ8BlockBytes = 34;
 constexpr int kMaxVec = 8;
 constexpr int kStages = 4;
-constexpr int kStageBytes = 32 * 1024;  // per stage (split between the matrices of a GEGLU)
-constexpr int kConsumers = 256;         // warps 0-7
-constexpr int kThreadsQ8 = kConsumers + 32;
+constexpr int kConsumers = 256;         // warps 0-7: block dot products
+constexpr int kProducerWarp = 8;        // bulk copies
+constexpr int kSumWarp = 9;             // in-order row sums
+constexpr int kThreadsQ8 = kConsumers + 64;
 constexpr uint32_t kQ8WaitLimit = 1u << 24;
+constexpr int64_t kStageTarget = 16 * 1024;  // weight bytes per stage
+
 
 enum { KIND_PLAIN = 0, KIND_GEGLU = 1, KIND_SOFTCAP = 2 };
 
@@ -111,30 +120,46 @@ __device__ __forceinline__ float block_value(const uint32_t (&wq)[8], float ws, 
     return __fmul_rn(__int2float_rn(dot), __fmul_rn(ws, xs));  // exact dot (|dot| < 2^24)
 }
 
+// Activation quants in shared memory: 36 bytes per block of 32 (9 words),
+// so that 32 lanes reading word k of 32 consecutive blocks hit 32 banks.
+constexpr int kXqStride = 36;
+
 struct Q8Shared {
-    uint64_t full[kStages], empty[kStages];
-    int bad;
+    uint64_t full[kStages], empty[kStages];  // weight stages: producer -> compute warps
+    uint64_t vfull[2], vempty[2];            // block-value buffers: compute warps -> sum warp
 };
 
 // Shared-memory layout of one launch (host and device agree on it):
-// ring [stages][n_mat][mat_bytes] | x quants [n_vec][cols] | x scales [n_vec][nb]
-// | block values [n_mat][n_vec][tile_rows][nb] f32 | barriers (8-byte aligned).
+// ring [stages][n_mat][mat_bytes] | x quants [n_vec][nb][36 B] | x scales [n_vec][nb]
+// | block values [2][n_mat][n_vec][tile_rows][nb + 1] f32 | barriers (16-byte aligned).
+// The block-value rows are padded by one float so that the sum warp's lanes
+// (one row each) read different banks.
 struct Q8Layout {
-    size_t mat_bytes, xq, xs, vals, bars, total;
+    size_t mat_bytes, xq, xs, vals, vals_buf, bars, total;
     __host__ __device__ Q8Layout(int n_mat, int n_vec, int cols, int tile_rows) {
         const size_t nb = (size_t)cols / kQ8Block;
-        mat_bytes = (size_t)kStageBytes / n_mat;
+        mat_bytes = ((size_t)tile_rows * nb * kQ8BlockBytes + 127) & ~(size_t)127;
         xq = (size_t)kStages * n_mat * mat_bytes;
-        xs = xq + (size_t)n_vec * cols;
+        xs = xq + (size_t)n_vec * nb * kXqStride;
         vals = xs + (size_t)n_vec * nb * 4;
-        bars = (vals + (size_t)n_mat * n_vec * tile_rows * nb * 4 + 15) & ~(size_t)15;
+        vals_buf = (size_t)n_mat * n_vec * tile_rows * (nb + 1);  // floats per buffer
+        bars = (vals + 2 * vals_buf * 4 + 15) & ~(size_t)15;
         total = bars + sizeof(Q8Shared);
     }
 };
 
-__global__ void __launch_bounds__(kThreadsQ8, 1) q8_matvec_kernel(Q8Params p) {
+// Bounded mbarrier wait; a time-out sets the error bit and returns (the
+// caller goes on, so that every barrier still receives its arrivals).
+__device__ __forceinline__ void q8_wait(uint64_t *bar, uint32_t parity, int *err) {
+    for (uint32_t i = 0; i < kQ8WaitLimit; i++)
+        if (ptx::mbar_try_wait(bar, parity)) return;
+    atomicOr(err, 2);
+}
+
+__global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int nb = p.cols / kQ8Block;
+    const int nbp = nb + 1;
     const int n_mat = p.kind == KIND_GEGLU ? 2 : 1;
     const Q8Layout L(n_mat, p.n_vec, p.cols, p.tile_rows);
     uint8_t *ring = sm;
@@ -147,104 +172,114 @@ __global__ void __launch_bounds__(kThreadsQ8, 1) q8_matvec_kernel(Q8Params p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             ptx::mbar_init(&bars->full[s], 1);
-            ptx::mbar_init(&bars->empty[s], 1);
+            ptx::mbar_init(&bars->empty[s], kConsumers / 32);
         }
-        bars->bad = 0;
+        for (int b = 0; b < 2; b++) {
+            ptx::mbar_init(&bars->vfull[b], kConsumers / 32);
+            ptx::mbar_init(&bars->vempty[b], 1);
+        }
         ptx::fence_mbar_init();
     }
-    // activation quants and scales, once per CTA
-    for (int i = threadIdx.x; i < p.n_vec * p.cols / 16; i += blockDim.x)
-        reinterpret_cast<uint4 *>(xq_s)[i] = reinterpret_cast<const uint4 *>(p.xq)[i];
+    // activation quants (padded to 36 bytes per block) and scales, once per CTA
+    for (int i = threadIdx.x; i < p.n_vec * p.cols / 4; i += blockDim.x) {
+        const int blk = i >> 3, k = i & 7;  // word k of block blk (over all vectors)
+        reinterpret_cast<uint32_t *>(xq_s)[blk * (kXqStride / 4) + k] = reinterpret_cast<const uint32_t *>(p.xq)[i];
+    }
     for (int i = threadIdx.x; i < p.n_vec * nb; i += blockDim.x) xs_s[i] = p.xs[i];
     __syncthreads();
 
     const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    if (warp == kConsumers / 32) {
+    auto rows_of = [&](int k, int64_t *r0) {
+        const int64_t t = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
+        *r0 = t * p.tile_rows;
+        return (int)(p.rows - *r0 < p.tile_rows ? p.rows - *r0 : p.tile_rows);
+    };
+
+    if (warp == kProducerWarp) {
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
-            int issued = 0;
             for (int k = 0; k < my_tiles; k++) {
                 const int s = k % kStages;
-                const uint32_t ph = (uint32_t)(k / kStages) & 1u;
-                bool ok = true;
-                if (k >= kStages) {
-                    uint32_t i = 0;
-                    while (!ptx::mbar_try_wait(&bars->empty[s], ph ^ 1u) && ++i < kQ8WaitLimit) {
-                    }
-                    ok = i < kQ8WaitLimit;
-                }
-                if (!ok) {
-                    atomicOr(p.err, 2);
-                    break;
-                }
-                const int64_t t = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
-                const int64_t r0 = t * p.tile_rows;
-                const int rows_here = (int)(p.rows - r0 < p.tile_rows ? p.rows - r0 : p.tile_rows);
+                if (k >= kStages) q8_wait(&bars->empty[s], ((uint32_t)(k / kStages) & 1u) ^ 1u, p.err);
+                int64_t r0;
+                const int rows_here = rows_of(k, &r0);
                 const uint32_t bytes = (uint32_t)rows_here * p.row_len;
                 ptx::mbar_arrive_expect_tx(&bars->full[s], bytes * n_mat);
                 ptx::bulk_load_1d(ring + (size_t)s * n_mat * L.mat_bytes, p.w + r0 * p.row_len, bytes, &bars->full[s]);
                 if (n_mat == 2)
                     ptx::bulk_load_1d(ring + (size_t)s * n_mat * L.mat_bytes + L.mat_bytes, p.w2 + r0 * p.row_len,
                                       bytes, &bars->full[s]);
-                issued = k + 1;
             }
             // No copy may land after the CTA exits: wait (bounded) for the
             // last stages issued (normally long consumed already).
-            for (int k = max(0, issued - kStages); k < issued; k++)
-                for (uint32_t i = 0;
-                     i < kQ8WaitLimit && !ptx::mbar_try_wait(&bars->full[k % kStages], (uint32_t)(k / kStages) & 1u); i++) {
+            for (int k = max(0, my_tiles - kStages); k < my_tiles; k++)
+                q8_wait(&bars->full[k % kStages], (uint32_t)(k / kStages) & 1u, p.err);
+        }
+    } else if (warp == kSumWarp) {
+        // ---------------------------------------------------------------- in-order sums
+        // lane = (vector, row): the block values of the row in block order,
+        // from -0.0 (Rust's f32 Sum), loads of each group of 8 issued first
+        for (int k = 0; k < my_tiles; k++) {
+            const int buf = k & 1;
+            q8_wait(&bars->vfull[buf], (uint32_t)(k >> 1) & 1u, p.err);
+            int64_t r0;
+            const int rows_here = rows_of(k, &r0);
+            const float *vals_k = val_s + (size_t)buf * L.vals_buf;
+            for (int e = lane; e < p.n_vec * rows_here; e += 32) {
+                const int v = e / rows_here, r = e - v * rows_here;
+                float sums[2];
+                for (int m = 0; m < n_mat; m++) {
+                    const float *vr = vals_k + (((size_t)m * p.n_vec + v) * p.tile_rows + r) * nbp;
+                    float sum = -0.0f;
+                    int b = 0;
+                    for (; b + 8 <= nb; b += 8) {
+                        float x[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) x[i] = vr[b + i];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) sum = __fadd_rn(sum, x[i]);
+                    }
+                    for (; b < nb; b++) sum = __fadd_rn(sum, vr[b]);
+                    sums[m] = sum;
                 }
+                float res = sums[0];
+                if (p.kind == KIND_GEGLU) res = __fmul_rn(gelu_tanh(sums[0]), sums[1]);
+                else if (p.kind == KIND_SOFTCAP) res = softcap(sums[0], p.cap);
+                p.out[(size_t)v * p.rows + r0 + r] = res;
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&bars->vempty[buf]);
         }
     } else {
-        // ---------------------------------------------------------------- consumers
+        // ---------------------------------------------------------------- block dot products
+        const int step_r = kConsumers / nb, step_b = kConsumers - (kConsumers / nb) * nb;  // 256 = step_r*nb + step_b
         for (int k = 0; k < my_tiles; k++) {
-            const int s = k % kStages;
-            const uint32_t ph = (uint32_t)(k / kStages) & 1u;
-            uint32_t i = 0;
-            while (!ptx::mbar_try_wait(&bars->full[s], ph) && ++i < kQ8WaitLimit) {
-            }
-            if (i >= kQ8WaitLimit) atomicOr(&bars->bad, 1);
-            ptx::named_bar_sync(1, kConsumers);  // consumers only: the producer warp never joins
-            if (*(volatile int *)&bars->bad) {
-                if (threadIdx.x == 0) atomicOr(p.err, 2);
-                break;
-            }
-            const int64_t t = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
-            const int64_t r0 = t * p.tile_rows;
-            const int rows_here = (int)(p.rows - r0 < p.tile_rows ? p.rows - r0 : p.tile_rows);
+            const int s = k % kStages, buf = k & 1;
+            q8_wait(&bars->full[s], (uint32_t)(k / kStages) & 1u, p.err);
+            if (k >= 2) q8_wait(&bars->vempty[buf], (uint32_t)((k - 2) >> 1) & 1u, p.err);
+            int64_t r0;
+            const int rows_here = rows_of(k, &r0);
             const uint8_t *stage = ring + (size_t)s * n_mat * L.mat_bytes;
-            // every (matrix, row, block): its value for every vector
-            const int n_blocks = n_mat * rows_here * nb;
-            for (int e = threadIdx.x; e < n_blocks; e += kConsumers) {
-                const int m = e / (rows_here * nb);
-                const int rb = e - m * rows_here * nb;
-                const int r = rb / nb, b = rb - r * nb;
+            float *vals_k = val_s + (size_t)buf * L.vals_buf;
+            // (m, r, b) of element threadIdx.x + 256 j, stepped without divisions
+            int m = 0, r = threadIdx.x / nb, b = threadIdx.x - (threadIdx.x / nb) * nb;
+            while (r >= rows_here && m < n_mat) r -= rows_here, m++;
+            while (m < n_mat) {
                 uint32_t wq[8];
                 const float ws = load_block(stage + (size_t)m * L.mat_bytes + (size_t)r * p.row_len, b, wq);
                 for (int v = 0; v < p.n_vec; v++)
-                    val_s[(((size_t)m * p.n_vec + v) * p.tile_rows + r) * nb + b] =
-                        block_value(wq, ws, xq_s + (size_t)v * p.cols + b * kQ8Block, xs_s[v * nb + b]);
+                    vals_k[(((size_t)m * p.n_vec + v) * p.tile_rows + r) * nbp + b] =
+                        block_value(wq, ws, xq_s + ((size_t)v * nb + b) * kXqStride, xs_s[v * nb + b]);
+                b += step_b;
+                r += step_r;
+                if (b >= nb) b -= nb, r++;
+                while (r >= rows_here && m < n_mat) r -= rows_here, m++;
             }
-            ptx::named_bar_sync(1, kConsumers);
-            // the stage's bytes are no longer read: hand it back to the producer
-            if (threadIdx.x == 0) ptx::mbar_arrive(&bars->empty[s]);
-            // one thread per (vector, row): the blocks in order, from -0.0
-            for (int e = threadIdx.x; e < p.n_vec * rows_here; e += kConsumers) {
-                const int v = e / rows_here, r = e - v * rows_here;
-                const float *vals = val_s + ((size_t)v * p.tile_rows + r) * nb;
-                float sum = -0.0f;
-                for (int b = 0; b < nb; b++) sum = __fadd_rn(sum, vals[b]);
-                if (p.kind == KIND_GEGLU) {
-                    const float *vals2 = val_s + (((size_t)p.n_vec + v) * p.tile_rows + r) * nb;
-                    float sum2 = -0.0f;
-                    for (int b = 0; b < nb; b++) sum2 = __fadd_rn(sum2, vals2[b]);
-                    sum = __fmul_rn(gelu_tanh(sum), sum2);
-                } else if (p.kind == KIND_SOFTCAP) {
-                    sum = softcap(sum, p.cap);
-                }
-                p.out[(size_t)v * p.rows + r0 + r] = sum;
+            __syncwarp();
+            if (lane == 0) {
+                ptx::mbar_arrive(&bars->empty[s]);   // this warp no longer reads the stage
+                ptx::mbar_arrive(&bars->vfull[buf]); // this warp's block values are written
             }
-            ptx::named_bar_sync(1, kConsumers);  // val_s is rewritten by the next tile
         }
     }
     __syncthreads();
@@ -308,7 +343,8 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
     const int n_mat = kind == KIND_GEGLU ? 2 : 1;
     const int64_t row_len = nb * kQ8BlockBytes;
     const bool aligned = ((uintptr_t)w % 16 == 0) && (!w2 || (uintptr_t)w2 % 16 == 0);
-    const bool fast = aligned && row_len % 16 == 0 && row_len <= kStageBytes / n_mat;
+    const bool fast = aligned && row_len % 16 == 0 && row_len * n_mat <= kStageTarget &&
+                      Q8Layout(n_mat, 1, (int)cols, 1).total <= 227 * 1024;
     Q8Params p{};
     p.w = w;
     p.w2 = w2;
@@ -331,14 +367,15 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
             cudaFuncSetAttribute(q8_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
             attr_set = true;
         }
-        p.tile_rows = (int32_t)std::max<int64_t>(1, std::min<int64_t>(32, (kStageBytes / n_mat) / row_len));
+        // rows per stage: as many as fit the stage target (about 16 KB, up to
+        // 32 rows); several CTAs per SM keep enough copies in flight
+        p.tile_rows = (int32_t)std::max<int64_t>(1, std::min<int64_t>(32, kStageTarget / (row_len * n_mat)));
         const int64_t n_tiles = (rows + p.tile_rows - 1) / p.tile_rows;
         if (n_tiles > INT32_MAX) {
             *msg = "Q8_0 mat-vec too large";
             return G4A_COMPUTE;
         }
         p.n_tiles = (int32_t)n_tiles;
-        const int grid = (int)std::min<int64_t>(n_tiles, std::max(1, n_sm));
         for (int32_t v0 = 0; v0 < n_vec;) {
             int g = std::min<int32_t>(kMaxVec, n_vec - v0);
             while (g > 1 && Q8Layout(n_mat, g, (int)cols, p.tile_rows).total > 227 * 1024) g--;
@@ -350,7 +387,15 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
             p.xq = xq + (size_t)v0 * cols;
             p.xs = xs + (size_t)v0 * nb;
             p.out = out + (size_t)v0 * rows;
-            q8_matvec_kernel<<<grid, kThreadsQ8, Q8Layout(n_mat, g, (int)cols, p.tile_rows).total, st>>>(p);
+            // as many resident CTAs per SM as shared memory allows (up to 4):
+            // more warps hide the shared-memory latency of the block dots
+            const size_t smem = Q8Layout(n_mat, g, (int)cols, p.tile_rows).total;
+            int per_sm = 1;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, q8_matvec_kernel, kThreadsQ8, smem) != cudaSuccess ||
+                per_sm < 1)
+                per_sm = 1;
+            const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)std::max(1, n_sm) * std::min(per_sm, 4));
+            q8_matvec_kernel<<<grid, kThreadsQ8, smem, st>>>(p);
             v0 += g;
         }
     }
