@@ -479,13 +479,13 @@ def q8_head_weights(torch, rows: int, cols: int, seed: int = 1):
     return blocks.view(-1)
 
 
-def measure_q8_head(torch, g4a, ctx, stream, pk, reps=10, warmup=3, cpu_rows=8192):
+def measure_q8_head(torch, g4a, ctx, stream, pk, reps=10, warmup=3, cpu_rows=8192, rows=262_144):
     """The output head's mat-vec at the reference benchmark's shape (262,144 x
     1,536 Q8_0, 428 MB): device time per call (CUDA events, weights larger than
     L2) against the measured HBM copy bandwidth, and the oracle port on the
     host cores over a row sample of the same weights."""
     import oracle
-    rows, cols = 262_144, 1536
+    cols = 1536
     w = q8_head_weights(torch, rows, cols)
     x = torch.sin(torch.arange(cols, dtype=torch.float32, device="cuda") * 0.37)[None, :]
     out = torch.empty(1, rows, device="cuda")
@@ -528,8 +528,8 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     """One prefill problem on its own (for profiling one kernel on a small
     case): spec "prefill:<head width>:<tokens>:<window>", "prefill-cfg1"
     for configuration 1 alone (35 layer-equivalents in one call), or
-    "decode-batch1" for configuration 0's latency, or "q8-head" for the
-    Q8_0 output-head mat-vec."""
+    "decode-batch1" for configuration 0's latency, or "q8-head[:rows]" for
+    the Q8_0 output-head mat-vec (262,144 rows unless given)."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
     if spec == "decode-batch1":
         stream = torch.cuda.Stream()
@@ -538,10 +538,12 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
         ctx.close()
         print(json.dumps({"case": spec, **res}), flush=True)
         return
-    if spec == "q8-head":
+    if spec.startswith("q8-head"):
         stream = torch.cuda.Stream()
         ctx.set_stream(stream.cuda_stream)
-        res = measure_q8_head(torch, g4a, ctx, stream, peaks(), reps=max(reps, 1), warmup=max(warmup, 1))
+        rows = int(spec.split(":")[1]) if ":" in spec else 262_144
+        res = measure_q8_head(torch, g4a, ctx, stream, peaks(), reps=max(reps, 1), warmup=max(warmup, 1),
+                              cpu_rows=min(8192, rows), rows=rows)
         ctx.close()
         print(json.dumps({"case": spec, **res}), flush=True)
         return

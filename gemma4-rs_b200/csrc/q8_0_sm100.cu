@@ -99,30 +99,31 @@ __device__ __forceinline__ float load_block(const uint8_t *row, int b, uint32_t 
     uint32_t r[9];
 #pragma unroll
     for (int k = 0; k < 9; k++) r[k] = w[k];
-    uint32_t sbits;
-    if (off & 2) {  // scale in the upper half of word 0, quants aligned from word 1
-        sbits = r[0] >> 16;
+    // Odd blocks start 2 bytes into a word: the scale is the upper half of
+    // word 0 and the quants are words 1-8; even blocks have the scale in the
+    // lower half and the quants straddle words. Neighbouring lanes differ in
+    // parity, so this is done without a branch: a clamped funnel shift by 32
+    // returns the upper word, by 16 the straddling one.
+    const uint32_t sh = (off & 2) ? 32u : 16u;
+    const uint32_t sbits = (r[0] >> (sh - 16u)) & 0xffffu;
 #pragma unroll
-        for (int k = 0; k < 8; k++) q[k] = r[k + 1];
-    } else {        // scale in the lower half, quants start two bytes into word 0
-        sbits = r[0] & 0xffffu;
-#pragma unroll
-        for (int k = 0; k < 8; k++) q[k] = __funnelshift_r(r[k], r[k + 1], 16);
-    }
+    for (int k = 0; k < 8; k++) q[k] = __funnelshift_rc(r[k], r[k + 1], sh);
     return __half2float(__ushort_as_half((unsigned short)sbits));
 }
 
 __device__ __forceinline__ float block_value(const uint32_t (&wq)[8], float ws, const int8_t *xq, float xs) {
-    const uint32_t *x = reinterpret_cast<const uint32_t *>(xq);
+    const uint4 x0 = reinterpret_cast<const uint4 *>(xq)[0], x1 = reinterpret_cast<const uint4 *>(xq)[1];
+    const uint32_t x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
     int dot = 0;
 #pragma unroll
     for (int k = 0; k < 8; k++) dot = __dp4a((int)wq[k], (int)x[k], dot);
     return __fmul_rn(__int2float_rn(dot), __fmul_rn(ws, xs));  // exact dot (|dot| < 2^24)
 }
 
-// Activation quants in shared memory: 36 bytes per block of 32 (9 words),
-// so that 32 lanes reading word k of 32 consecutive blocks hit 32 banks.
-constexpr int kXqStride = 36;
+// Activation quants in shared memory: 48 bytes per block of 32, read as two
+// 16-byte loads; the eight lanes of a quarter warp then cover 32 distinct
+// banks (block stride of 12 words).
+constexpr int kXqStride = 48;
 
 struct Q8Shared {
     uint64_t full[kStages], empty[kStages];  // weight stages: producer -> compute warps
@@ -253,6 +254,22 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
     } else {
         // ---------------------------------------------------------------- block dot products
         const int step_r = kConsumers / nb, step_b = kConsumers - (kConsumers / nb) * nb;  // 256 = step_r*nb + step_b
+        // One vector and at most 256 blocks per row: thread t owns block column
+        // t % nb for the whole call (its activation quants and scale live in
+        // registers) and walks rows t / nb, + G, + 2G, ... (G = 256 / nb).
+        const bool column_mode = p.n_vec == 1 && nb <= kConsumers;
+        const int G = column_mode ? kConsumers / nb : 0;
+        const int my_b = column_mode ? (int)threadIdx.x % nb : 0;
+        const int my_g = column_mode ? (int)threadIdx.x / nb : 0;
+        uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float my_xs = 0.0f;
+        if (column_mode && my_g < G) {
+            const uint4 x0 = reinterpret_cast<const uint4 *>(xq_s + (size_t)my_b * kXqStride)[0];
+            const uint4 x1 = reinterpret_cast<const uint4 *>(xq_s + (size_t)my_b * kXqStride)[1];
+            xw[0] = x0.x, xw[1] = x0.y, xw[2] = x0.z, xw[3] = x0.w, xw[4] = x1.x, xw[5] = x1.y, xw[6] = x1.z,
+            xw[7] = x1.w;
+            my_xs = xs_s[my_b];
+        }
         for (int k = 0; k < my_tiles; k++) {
             const int s = k % kStages, buf = k & 1;
             q8_wait(&bars->full[s], (uint32_t)(k / kStages) & 1u, p.err);
@@ -261,6 +278,30 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
             const int rows_here = rows_of(k, &r0);
             const uint8_t *stage = ring + (size_t)s * n_mat * L.mat_bytes;
             float *vals_k = val_s + (size_t)buf * L.vals_buf;
+            if (column_mode) {
+                if (my_g < G) {
+                    for (int m = 0; m < n_mat; m++) {
+                        const uint8_t *wrow = stage + (size_t)m * L.mat_bytes + (size_t)my_g * p.row_len;
+                        float *vout = vals_k + ((size_t)m * p.tile_rows + my_g) * nbp + my_b;
+                        for (int r = my_g; r < rows_here; r += G) {
+                            uint32_t wq[8];
+                            const float ws = load_block(wrow, my_b, wq);
+                            int dot = 0;
+#pragma unroll
+                            for (int k2 = 0; k2 < 8; k2++) dot = __dp4a((int)wq[k2], (int)xw[k2], dot);
+                            *vout = __fmul_rn(__int2float_rn(dot), __fmul_rn(ws, my_xs));
+                            wrow += (size_t)G * p.row_len;
+                            vout += (size_t)G * nbp;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::mbar_arrive(&bars->empty[s]);
+                    ptx::mbar_arrive(&bars->vfull[buf]);
+                }
+                continue;
+            }
             // (m, r, b) of element threadIdx.x + 256 j, stepped without divisions
             int m = 0, r = threadIdx.x / nb, b = threadIdx.x - (threadIdx.x / nb) * nb;
             while (r >= rows_here && m < n_mat) r -= rows_here, m++;
