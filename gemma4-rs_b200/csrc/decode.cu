@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     __shared__ int last_s;
 
     const DecodeItem it = p.items[blockIdx.x];
+    if (it.task < 0) return;  // an unused slot of a fixed-size (captured) launch
     const DecodeTask &tk = p.tasks[it.task];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;

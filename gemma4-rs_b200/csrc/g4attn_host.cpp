@@ -18,6 +18,7 @@
 
 #include "../../include/g4attn.h"
 #include "internal.h"
+#include "host_internal.h"
 
 using namespace g4a;
 
@@ -88,62 +89,8 @@ extern "C" void g4a_proportional_rope_freq_factors(int32_t head_dim, float p, fl
 // context
 // --------------------------------------------------------------------------
 
-struct g4a_ctx {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    g4a_hparams hp{};
-    std::vector<float> rope_freqs;  // head_dim_global / 2 divisors
-    int32_t max_positions = 0;
-    float2 *d_rope_local = nullptr;
-    float2 *d_rope_global = nullptr;
-    int *d_err = nullptr;
-    std::string last_error;
-    float *d_part_o = nullptr;
-    size_t part_o_cap = 0;  // floats
-    float *d_part_ml = nullptr;
-    size_t part_ml_cap = 0;
-    unsigned *d_tickets = nullptr;
-    size_t tickets_cap = 0;
-    uint8_t *d_meta = nullptr;
-    size_t meta_cap = 0;
-    std::vector<uint8_t> h_meta;
-    PrefillScratch *prefill = nullptr;
-    int n_sm = 148;
-    uint8_t *d_qblocks = nullptr;
-    size_t qblocks_cap = 0;
-    // per-kernel timing (g4a_profile_enable): events around each launch
-    bool profiling = false;
-    struct Rec {
-        int kernel;
-        cudaEvent_t a, b;
-    };
-    std::vector<Rec> recs;
-    std::vector<cudaEvent_t> spare;
-    double prof_ms[G4A_K_COUNT] = {};
-    int64_t prof_n[G4A_K_COUNT] = {};
-    // Pinned staging for the small per-call uploads (decode metadata, block
-    // tables): a copy from pageable memory goes through the driver's own
-    // staging and costs tens of microseconds per call. Slots are reused in
-    // turn; an event per slot keeps a slot from being rewritten before the
-    // GPU has read its previous contents.
-    struct PinnedSlot {
-        uint8_t *p = nullptr;
-        size_t cap = 0;
-        cudaEvent_t ev = nullptr;
-        bool pending = false;
-    };
-    PinnedSlot pin[4];
-    int pin_next = 0;
-    // Q8_0 mat-vec: the quantized activations of the current call
-    int8_t *d_q8x = nullptr;
-    size_t q8x_cap = 0;
-    float *d_q8s = nullptr;
-    size_t q8s_cap = 0;
-};
 
 namespace {
-
-int fail(g4a_ctx *ctx, int code, const char *fmt, ...);
 
 // Host-to-device copy of `bytes` from `src` on the context's stream through
 // a pinned staging slot (falls back to a pageable copy if pinning fails).
@@ -174,27 +121,6 @@ cudaError_t upload(g4a_ctx *ctx, void *dst, const void *src, size_t bytes) {
     return e;
 }
 
-int fail(g4a_ctx *ctx, int code, const char *fmt, ...) {
-    if (ctx) {
-        char buf[512];
-        va_list ap;
-        va_start(ap, fmt);
-        vsnprintf(buf, sizeof buf, fmt, ap);
-        va_end(ap);
-        ctx->last_error = buf;
-    }
-    return code;
-}
-
-int cuda_fail(g4a_ctx *ctx, cudaError_t e, const char *what) {
-    return fail(ctx, G4A_CUDA, "compute: %s: %s", what, cudaGetErrorString(e));
-}
-
-#define G4A_CUDA_TRY(ctx, call)                              \
-    do {                                                     \
-        cudaError_t e_ = (call);                             \
-        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
-    } while (0)
 
 // Builds (sin, cos) of every pair at positions [0, n_pos) exactly as
 // ops.rs:150-159 does: theta_scale = base^(-2/n_rot) by powf, theta grows by

@@ -106,6 +106,37 @@ bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint6
 int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
            float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg);
 
+// E2B decoder step (e2b_sm100.cu).
+// One layer of the model as the attention planner sees it; the caches are
+// [max_seqs][max_tokens][hd] f32 of the layer's KV source.
+struct E2bLayerDesc {
+    const float *q_w, *k_w;
+    float *k_cache, *v_cache;
+    int32_t hd, global, owner;
+};
+struct E2bPlanArgs {
+    const E2bLayerDesc *layers;
+    int32_t n_layers, n, task_stride;
+    const int32_t *seqs, *pos;
+    int32_t max_tokens, window, rows_per_item, max_splits_local, max_splits_global;
+    const float *q, *k, *v;
+    float *att;
+    DecodeTask *tasks;  // [n_layers][task_stride]
+    DecodeItem *items_local, *items_global;
+};
+cudaError_t e2b_synth_q8(void *dst, int64_t n_blocks, uint64_t seed, uint64_t tensor, float sigma, cudaStream_t st);
+cudaError_t e2b_synth_norm(float *dst, int64_t n, uint64_t seed, uint64_t tensor, float center, float spread,
+                           cudaStream_t st);
+cudaError_t e2b_embed(const uint8_t *table, int d, const int32_t *tokens, int n, float scale, float *x, cudaStream_t st);
+cudaError_t e2b_ple_inputs(const float *P, const uint8_t *table, const int32_t *tokens, const float *w, int L, int ple,
+                           float ps, float ts, float is, float eps, float *out, int n, cudaStream_t st);
+cudaError_t e2b_resid(float *x, const float *y, const float *w_post, float post, const float *w_next, int d, float eps,
+                      int8_t *xq, float *xs, int n, cudaStream_t st);
+cudaError_t e2b_gelu_quant(const float *gate, const float *pli, int layer, int L, int ple, int8_t *xq, float *xs, int n,
+                           cudaStream_t st);
+cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, int32_t *out, cudaStream_t st);
+cudaError_t e2b_plan(const E2bPlanArgs &a, cudaStream_t st);
+
 struct PrefillScratch;
 PrefillScratch *prefill_scratch_new();
 void prefill_scratch_free(PrefillScratch *s);

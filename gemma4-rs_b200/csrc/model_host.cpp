@@ -1,0 +1,470 @@
+// Host side of the E2B decoder (include/g4attn.h, g4a_model_*): one token per
+// sequence through embed, the 35 layers and the logits of
+// crates/llm-gemma4/src/impl_/model.rs:252-449, and the prompt-then-greedy
+// loop of generate.rs:15-64, for many sequences at once.
+//
+// A step is one fixed sequence of launches on the model's own stream (about
+// 16 per layer): the attention plan, embedding, per-layer inputs, then per
+// layer the fused residual/norm/quantize kernels, the Q8_0 mat-vecs and the
+// fused decode attention, then the soft-capped head and the argmax. Nothing
+// in it depends on the host values of the step (tokens and positions are read
+// on the device), so after one eager run per batch size the step is captured
+// into a CUDA graph with its input upload and result download, and every
+// later step of that size is one graph launch.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/g4attn.h"
+#include "host_internal.h"
+#include "internal.h"
+
+using namespace g4a;
+
+struct g4a_model {
+    g4a_ctx *ctx = nullptr;
+    g4a_model_weights w{};
+    int32_t S = 0, T = 0;  // max sequences, max positions per sequence
+    int32_t L = 0, d = 0, d_ff = 0, ple = 0, vocab = 0, hd_max = 0, qd_max = 0, cmax = 0;
+    int32_t rows_per_item = 64, ms_local = 1, ms_global = 1;
+    std::vector<int32_t> len, source, hd, global;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev = nullptr;
+    std::vector<void *> allocs;
+    int32_t *d_in = nullptr;  // [3][S]: sequence ids, tokens, positions
+    int32_t *d_next = nullptr;
+    int32_t *h_in = nullptr, *h_out = nullptr;  // pinned: [3][S] and [S + 1] (tokens, error flags)
+    float *x = nullptr, *y = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
+    float *gate = nullptr, *gated = nullptr, *P = nullptr, *pli = nullptr, *logits = nullptr;
+    int8_t *xq = nullptr;
+    float *xs = nullptr;
+    E2bLayerDesc *d_layers = nullptr;
+    DecodeTask *d_tasks = nullptr;
+    DecodeItem *d_items_local = nullptr, *d_items_global = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned *tickets = nullptr;
+    std::map<int32_t, cudaGraphExec_t> graphs;
+    std::map<int32_t, int> eager_runs;
+    int32_t last_n = 0;
+};
+
+namespace {
+
+template <typename T>
+T *dalloc(g4a_model *m, size_t n) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)) != cudaSuccess) return nullptr;
+    m->allocs.push_back(p);
+    return static_cast<T *>(p);
+}
+
+// The weights a layer needs (model.rs:386-435); the name of the first one
+// missing, or nullptr.
+const char *missing_weight(const g4a_model_weights &w, int32_t layer, bool owner) {
+    const g4a_layer_weights &l = w.layers[layer];
+    if (!l.attn_norm) return "attn_norm";
+    if (!l.attn_q) return "attn_q";
+    if (!l.attn_q_norm) return "attn_q_norm";
+    if (owner && !l.attn_k) return "attn_k";
+    if (owner && !l.attn_v) return "attn_v";
+    if (owner && !l.attn_k_norm) return "attn_k_norm";
+    if (!l.attn_output) return "attn_output";
+    if (!l.post_attention_norm) return "post_attention_norm";
+    if (!l.ffn_norm) return "ffn_norm";
+    if (!l.ffn_gate) return "ffn_gate";
+    if (!l.ffn_up) return "ffn_up";
+    if (!l.ffn_down) return "ffn_down";
+    if (!l.post_ffw_norm) return "post_ffw_norm";
+    if (w.ple_dim > 0 && !l.inp_gate) return "inp_gate";
+    if (w.ple_dim > 0 && !l.proj) return "proj";
+    if (w.ple_dim > 0 && !l.post_norm) return "post_norm";
+    return nullptr;
+}
+
+int mv(g4a_model *m, int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int n,
+       float cap, float *out) {
+    const char *msg = "";
+    const int rc = q8_run(kind, w, w2, rows, cols, x, n, cap, out, m->xq, m->xs, m->ctx->d_err, m->ctx->n_sm, m->st,
+                          &msg);
+    return rc == G4A_OK ? G4A_OK : fail(m->ctx, rc, "compute: %s", msg);
+}
+
+#define MODEL_TRY(call)                                                   \
+    do {                                                                  \
+        cudaError_t e_ = (call);                                          \
+        if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);       \
+    } while (0)
+
+// The kernels of one step for rows 0..n-1 of d_in.
+int enqueue_step(g4a_model *m, int32_t n) {
+    g4a_ctx *ctx = m->ctx;
+    const g4a_model_weights &w = m->w;
+    const float eps = ctx->hp.rms_norm_eps;
+    const int32_t *d_seq = m->d_in, *d_tok = m->d_in + m->S, *d_pos = m->d_in + 2 * m->S;
+    const int d = m->d, L = m->L, ple = m->ple;
+
+    E2bPlanArgs pa{};
+    pa.layers = m->d_layers;
+    pa.n_layers = L;
+    pa.n = n;
+    pa.task_stride = m->S;
+    pa.seqs = d_seq;
+    pa.pos = d_pos;
+    pa.max_tokens = m->T;
+    pa.window = ctx->hp.sliding_window;
+    pa.rows_per_item = m->rows_per_item;
+    pa.max_splits_local = m->ms_local;
+    pa.max_splits_global = m->ms_global;
+    pa.q = m->q;
+    pa.k = m->k;
+    pa.v = m->v;
+    pa.att = m->att;
+    pa.tasks = m->d_tasks;
+    pa.items_local = m->d_items_local;
+    pa.items_global = m->d_items_global;
+    MODEL_TRY(e2b_plan(pa, m->st));
+
+    // embed (model.rs:376-384) and per-layer inputs (:252-270)
+    MODEL_TRY(e2b_embed(w.token_embd, d, d_tok, n, std::sqrt((float)d), m->x, m->st));
+    int rc;
+    if (ple > 0) {
+        if ((rc = mv(m, 0, w.ple_model_proj, nullptr, (int64_t)L * ple, d, m->x, n, 0.0f, m->P))) return rc;
+        MODEL_TRY(e2b_ple_inputs(m->P, w.ple_token_embd, d_tok, w.ple_proj_norm, L, ple, 1.0f / std::sqrt((float)d),
+                                 std::sqrt((float)ple), 1.0f / std::sqrt(2.0f), eps, m->pli, n, m->st));
+    }
+    MODEL_TRY(e2b_resid(m->x, nullptr, nullptr, 1.0f, w.layers[0].attn_norm, d, eps, m->xq, m->xs, n, m->st));
+
+    for (int l = 0; l < L; l++) {
+        const g4a_layer_weights &lw = w.layers[l];
+        const int hd = m->hd[l], qd = kHeads * hd;
+        const bool owner = m->source[l] == l;
+        // q, k, v of the normalized input (model.rs:392-401)
+        if ((rc = mv(m, 0, lw.attn_q, nullptr, qd, d, nullptr, n, 0.0f, m->q))) return rc;
+        if (owner) {
+            if ((rc = mv(m, 0, lw.attn_k, nullptr, hd, d, nullptr, n, 0.0f, m->k))) return rc;
+            if ((rc = mv(m, 0, lw.attn_v, nullptr, hd, d, nullptr, n, 0.0f, m->v))) return rc;
+        }
+        // q/k/v norms, RoPE, append, window and attention (:394-410)
+        DecodeParams p{};
+        p.tasks = m->d_tasks + (size_t)l * m->S;
+        p.items = m->global[l] ? m->d_items_global : m->d_items_local;
+        p.block_table = nullptr;
+        p.page_tokens = 1;
+        p.rope_local = ctx->d_rope_local;
+        p.rope_global = ctx->d_rope_global;
+        p.eps = eps;
+        p.part_o = m->part_o;
+        p.part_ml = m->part_ml;
+        p.tickets = m->tickets;
+        p.err_flag = ctx->d_err;
+        p.n_items = n * (m->global[l] ? m->ms_global : m->ms_local);
+        MODEL_TRY(launch_decode(p, hd, 0, true, m->st));
+        // output projection, post-attention norm, residual, FFN norm (:411-415)
+        if ((rc = mv(m, 0, lw.attn_output, nullptr, d, qd, m->att, n, 0.0f, m->y))) return rc;
+        MODEL_TRY(e2b_resid(m->x, m->y, lw.post_attention_norm, 1.0f, lw.ffn_norm, d, eps, m->xq, m->xs, n, m->st));
+        // GEGLU, down projection, post-FFN norm, residual (:416-420)
+        if ((rc = mv(m, 1, lw.ffn_gate, lw.ffn_up, m->d_ff, d, nullptr, n, 0.0f, m->gated))) return rc;
+        if ((rc = mv(m, 0, lw.ffn_down, nullptr, d, m->d_ff, m->gated, n, 0.0f, m->y))) return rc;
+        const float *next_norm = l + 1 < L ? w.layers[l + 1].attn_norm : w.output_norm;
+        if (ple > 0) {
+            // per-layer embedding (:422-432), then layer_output_scale (:433-435)
+            MODEL_TRY(e2b_resid(m->x, m->y, lw.post_ffw_norm, 1.0f, nullptr, d, eps, m->xq, m->xs, n, m->st));
+            if ((rc = mv(m, 0, lw.inp_gate, nullptr, ple, d, nullptr, n, 0.0f, m->gate))) return rc;
+            MODEL_TRY(e2b_gelu_quant(m->gate, m->pli, l, L, ple, m->xq, m->xs, n, m->st));
+            if ((rc = mv(m, 0, lw.proj, nullptr, d, ple, nullptr, n, 0.0f, m->y))) return rc;
+            MODEL_TRY(e2b_resid(m->x, m->y, lw.post_norm, lw.layer_output_scale, next_norm, d, eps, m->xq, m->xs, n,
+                                m->st));
+        } else {
+            MODEL_TRY(e2b_resid(m->x, m->y, lw.post_ffw_norm, lw.layer_output_scale, next_norm, d, eps, m->xq, m->xs,
+                                n, m->st));
+        }
+    }
+    // logits (:438-449) and greedy sampling (sample.rs:27-36)
+    if ((rc = mv(m, 2, w.token_embd, nullptr, m->vocab, d, nullptr, n, w.final_logit_softcap, m->logits))) return rc;
+    MODEL_TRY(e2b_argmax(m->logits, m->vocab, n, m->d_next, m->st));
+    return G4A_OK;
+}
+
+// Upload of the step's inputs, the step, download of its tokens and flags.
+int record_step(g4a_model *m, int32_t n) {
+    MODEL_TRY(cudaMemcpyAsync(m->d_in, m->h_in, 3 * (size_t)m->S * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+    const int rc = enqueue_step(m, n);
+    if (rc) return rc;
+    MODEL_TRY(cudaMemcpyAsync(m->h_out, m->d_next, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    MODEL_TRY(cudaMemcpyAsync(m->h_out + m->S, m->ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    return G4A_OK;
+}
+
+int run_step(g4a_model *m, int32_t n) {
+    auto it = m->graphs.find(n);
+    if (it != m->graphs.end()) {
+        MODEL_TRY(cudaGraphLaunch(it->second, m->st));
+        return G4A_OK;
+    }
+    if (m->eager_runs[n]++ == 0) return record_step(m, n);  // first step of this size: eager
+    cudaGraph_t g = nullptr;
+    MODEL_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    const int rc = record_step(m, n);
+    const cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return rc ? rc : cuda_fail(m->ctx, e, "cudaStreamEndCapture");
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) return cuda_fail(m->ctx, ei, "cudaGraphInstantiate");
+    m->graphs[n] = exec;
+    MODEL_TRY(cudaGraphLaunch(exec, m->st));
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_synth_q8_0(g4a_ctx *ctx, uint8_t *dst_dev, int64_t n_values, uint64_t seed, uint64_t tensor,
+                              float sigma) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (n_values < 0 || n_values % 32 || (n_values && !dst_dev))
+        return fail(ctx, G4A_COMPUTE, "compute: Q8_0 tensor of %lld values", (long long)n_values);
+    G4A_CUDA_TRY(ctx, e2b_synth_q8(dst_dev, n_values / 32, seed, tensor, sigma, ctx->stream));
+    return G4A_OK;
+}
+
+extern "C" int g4a_synth_norm(g4a_ctx *ctx, float *dst_dev, int64_t n, uint64_t seed, uint64_t tensor, float center,
+                              float spread) {
+    if (!ctx) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (n < 0 || (n && !dst_dev)) return fail(ctx, G4A_COMPUTE, "compute: invalid norm tensor");
+    G4A_CUDA_TRY(ctx, e2b_synth_norm(dst_dev, n, seed, tensor, center, spread, ctx->stream));
+    return G4A_OK;
+}
+
+extern "C" void g4a_model_destroy(g4a_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    if (m->st) cudaStreamSynchronize(m->st);
+    for (auto &g : m->graphs) cudaGraphExecDestroy(g.second);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->h_in) cudaFreeHost(m->h_in);
+    if (m->h_out) cudaFreeHost(m->h_out);
+    if (m->ev) cudaEventDestroy(m->ev);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+}
+
+extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_t max_seqs, int32_t max_tokens,
+                                g4a_model **out) {
+    if (!ctx || !w || !out) return G4A_COMPUTE;
+    *out = nullptr;
+    cudaSetDevice(ctx->device);
+    const g4a_hparams &hp = ctx->hp;
+    if (hp.n_heads != kHeads || hp.n_kv_heads != 1)
+        return fail(ctx, G4A_COMPUTE, "compute: the decoder serves %d query heads over 1 KV head", kHeads);
+    if ((hp.head_dim_local != 256 && hp.head_dim_local != 512) ||
+        (hp.head_dim_global != 256 && hp.head_dim_global != 512))
+        return fail(ctx, G4A_COMPUTE, "compute: head widths must be 256 or 512");
+    if (hp.n_layers > G4A_MAX_LAYERS) return fail(ctx, G4A_COMPUTE, "compute: more than %d layers", G4A_MAX_LAYERS);
+    if (w->d_model <= 0 || w->d_model % 32 || w->d_model > 4096 || w->d_ff <= 0 || w->d_ff % 32 || w->ple_dim < 0 ||
+        w->ple_dim % 32 || w->ple_dim > 1024 || w->vocab_size <= 0 || !(w->final_logit_softcap != 0.0f))
+        return fail(ctx, G4A_COMPUTE, "compute: unsupported model dimensions");
+    if (max_seqs <= 0 || max_tokens <= 0) return fail(ctx, G4A_COMPUTE, "compute: empty model capacity");
+    if (max_tokens > ctx->max_positions)
+        return fail(ctx, G4A_COMPUTE, "compute: max_tokens %d exceeds the context's %d RoPE positions", max_tokens,
+                    ctx->max_positions);
+    if (!w->token_embd) return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `token_embd.weight`");
+    if (!w->output_norm) return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `output_norm.weight`");
+    if (w->ple_dim > 0 && !w->ple_token_embd)
+        return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `per_layer_token_embd.weight`");
+    if (w->ple_dim > 0 && !w->ple_model_proj)
+        return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `per_layer_model_proj.weight`");
+    if (w->ple_dim > 0 && !w->ple_proj_norm)
+        return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `per_layer_proj_norm.weight`");
+
+    auto *m = new g4a_model();
+    m->ctx = ctx;
+    m->w = *w;
+    m->S = max_seqs;
+    m->T = max_tokens;
+    m->L = hp.n_layers;
+    m->d = w->d_model;
+    m->d_ff = w->d_ff;
+    m->ple = w->ple_dim;
+    m->vocab = w->vocab_size;
+    m->len.assign(max_seqs, 0);
+    m->source.resize(m->L);
+    m->hd.resize(m->L);
+    m->global.resize(m->L);
+    for (int l = 0; l < m->L; l++) {
+        int32_t src = -1, detail = 0;
+        const int rc = g4a_kv_source_layer(&hp, l, &src, &detail);
+        if (rc != G4A_OK) {
+            g4a_model_destroy(m);
+            return fail(ctx, rc, "layer %d has no KV source (kind %d)", l, detail);
+        }
+        m->source[l] = src;
+        m->hd[l] = g4a_head_dim(&hp, l);
+        m->global[l] = g4a_layer_is_global(&hp, l);
+        if (const char *name = missing_weight(*w, l, src == l)) {
+            g4a_model_destroy(m);
+            return fail(ctx, G4A_MISSING_WEIGHT, "missing weight `blk.%d.%s.weight`", l, name);
+        }
+    }
+    m->hd_max = std::max(hp.head_dim_local, hp.head_dim_global);
+    m->qd_max = kHeads * m->hd_max;
+    m->cmax = std::max(std::max(m->d, m->d_ff), std::max(m->qd_max, m->ple));
+    const int32_t R = m->rows_per_item;
+    m->ms_local = (std::min(hp.sliding_window, max_tokens) + R - 1) / R;
+    m->ms_global = (max_tokens + R - 1) / R;
+    const int32_t ms = std::max(m->ms_local, m->ms_global);
+    const size_t S = (size_t)max_seqs;
+
+    bool ok = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming) == cudaSuccess &&
+              cudaHostAlloc(reinterpret_cast<void **>(&m->h_in), 3 * S * sizeof(int32_t), cudaHostAllocDefault) ==
+                  cudaSuccess &&
+              cudaHostAlloc(reinterpret_cast<void **>(&m->h_out), (S + 1) * sizeof(int32_t), cudaHostAllocDefault) ==
+                  cudaSuccess;
+    if (ok) {
+        ok = (m->d_in = dalloc<int32_t>(m, 3 * S)) && (m->d_next = dalloc<int32_t>(m, S)) &&
+             (m->x = dalloc<float>(m, S * m->d)) && (m->y = dalloc<float>(m, S * m->d)) &&
+             (m->q = dalloc<float>(m, S * m->qd_max)) && (m->att = dalloc<float>(m, S * m->qd_max)) &&
+             (m->k = dalloc<float>(m, S * m->hd_max)) && (m->v = dalloc<float>(m, S * m->hd_max)) &&
+             (m->gated = dalloc<float>(m, S * m->d_ff)) && (m->gate = dalloc<float>(m, S * std::max(m->ple, 1))) &&
+             (m->P = dalloc<float>(m, S * m->L * std::max(m->ple, 1))) &&
+             (m->pli = dalloc<float>(m, S * m->L * std::max(m->ple, 1))) &&
+             (m->logits = dalloc<float>(m, S * m->vocab)) && (m->xq = dalloc<int8_t>(m, S * m->cmax)) &&
+             (m->xs = dalloc<float>(m, S * m->cmax / 32)) && (m->d_layers = dalloc<E2bLayerDesc>(m, m->L)) &&
+             (m->d_tasks = dalloc<DecodeTask>(m, (size_t)m->L * S)) &&
+             (m->d_items_local = dalloc<DecodeItem>(m, S * m->ms_local)) &&
+             (m->d_items_global = dalloc<DecodeItem>(m, S * m->ms_global)) &&
+             (m->part_o = dalloc<float>(m, S * ms * kHeads * m->hd_max)) &&
+             (m->part_ml = dalloc<float>(m, S * ms * 2 * kHeads)) && (m->tickets = dalloc<unsigned>(m, S));
+    }
+    // K/V caches of the owner layers: [max_seqs][max_tokens][hd] f32 each
+    std::vector<E2bLayerDesc> desc(m->L);
+    std::vector<float *> kc(m->L, nullptr), vc(m->L, nullptr);
+    for (int l = 0; ok && l < m->L; l++) {
+        if (m->source[l] != l) continue;
+        const size_t n = S * max_tokens * m->hd[l];
+        ok = (kc[l] = dalloc<float>(m, n)) && (vc[l] = dalloc<float>(m, n));
+    }
+    if (!ok) {
+        g4a_model_destroy(m);
+        return fail(ctx, G4A_CUDA, "compute: out of device memory for the decoder");
+    }
+    for (int l = 0; l < m->L; l++) {
+        desc[l].q_w = w->layers[l].attn_q_norm;
+        desc[l].k_w = w->layers[m->source[l]].attn_k_norm;
+        desc[l].k_cache = kc[m->source[l]];
+        desc[l].v_cache = vc[m->source[l]];
+        desc[l].hd = m->hd[l];
+        desc[l].global = m->global[l];
+        desc[l].owner = m->source[l] == l;
+    }
+    cudaError_t e = cudaMemcpy(m->d_layers, desc.data(), desc.size() * sizeof(E2bLayerDesc), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(m->tickets, 0, S * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        g4a_model_destroy(m);
+        return cuda_fail(ctx, e, "model setup");
+    }
+    *out = m;
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_clear(g4a_model *m, int32_t seq) {
+    if (!m) return G4A_COMPUTE;
+    if (seq < 0 || seq >= m->S) return fail(m->ctx, G4A_COMPUTE, "compute: sequence %d out of range", seq);
+    m->len[seq] = 0;  // rows past the length are never read before they are rewritten
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_len(const g4a_model *m, int32_t seq, int32_t *len) {
+    if (!m || !len || seq < 0 || seq >= m->S) return G4A_COMPUTE;
+    *len = m->len[seq];
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t *next) {
+    if (!m) return G4A_COMPUTE;
+    g4a_ctx *ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    if (n < 1 || n > m->S || !seq_ids || !tokens)
+        return fail(ctx, G4A_COMPUTE, "compute: step of %d sequences (capacity %d)", n, m->S);
+    std::vector<char> used(m->S, 0);
+    for (int i = 0; i < n; i++) {
+        const int32_t s = seq_ids[i];
+        if (s < 0 || s >= m->S || used[s]) return fail(ctx, G4A_COMPUTE, "compute: bad or repeated sequence id %d", s);
+        used[s] = 1;
+        if (tokens[i] < 0 || tokens[i] >= m->vocab)  // model.rs:378
+            return fail(ctx, G4A_COMPUTE, "compute: token %d exceeds vocabulary", tokens[i]);
+        if (m->len[s] >= m->T)  // ContextMemory::view past capacity
+            return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", m->len[s] + 1, m->T);
+    }
+    for (int i = 0; i < n; i++) {
+        m->h_in[i] = seq_ids[i];
+        m->h_in[m->S + i] = tokens[i];
+        m->h_in[2 * m->S + i] = m->len[seq_ids[i]];
+    }
+    G4A_CUDA_TRY(ctx, cudaEventRecord(m->ev, ctx->stream));  // after the caller's work on the context
+    G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(m->st, m->ev, 0));
+    const int rc = run_step(m, n);
+    if (rc) {
+        cudaStreamSynchronize(m->st);
+        return rc;
+    }
+    G4A_CUDA_TRY(ctx, cudaStreamSynchronize(m->st));
+    m->last_n = n;
+    const int32_t flags = m->h_out[m->S];
+    if (flags) {
+        cudaMemset(ctx->d_err, 0, sizeof(int));
+        if (flags & 1) return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
+        return fail(ctx, G4A_TIMEOUT, "compute: a device wait timed out (flags %d)", flags);
+    }
+    for (int i = 0; i < n; i++) m->len[seq_ids[i]]++;
+    if (next) std::memcpy(next, m->h_out, (size_t)n * sizeof(int32_t));
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_logits(g4a_model *m, const float **logits_dev) {
+    if (!m || !logits_dev) return G4A_COMPUTE;
+    *logits_dev = m->logits;
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompts, int32_t prompt_len, int32_t max_new,
+                                  int32_t max_context, int32_t *out) {
+    if (!m) return G4A_COMPUTE;
+    g4a_ctx *ctx = m->ctx;
+    if (n < 1 || n > m->S || prompt_len < 0 || max_new < 0 || (prompt_len && !prompts) || (max_new && !out))
+        return fail(ctx, G4A_COMPUTE, "compute: invalid generate arguments");
+    if (prompt_len > max_context)  // generate.rs:23-28
+        return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", prompt_len, max_context);
+    if (max_new == 0) return G4A_OK;
+    if (prompt_len == 0) return fail(ctx, G4A_COMPUTE, "generation requires at least one prompt token");
+    std::vector<int32_t> ids(n), tok(n), next(n);
+    for (int i = 0; i < n; i++) {
+        ids[i] = i;
+        m->len[i] = 0;  // clear_context
+    }
+    int rc;
+    for (int t = 0; t < prompt_len; t++) {  // generate.rs:38-42
+        for (int i = 0; i < n; i++) tok[i] = prompts[(size_t)i * prompt_len + t];
+        if ((rc = g4a_model_step(m, n, ids.data(), tok.data(), next.data()))) return rc;
+    }
+    for (int index = 0; index < max_new; index++) {  // generate.rs:45-70
+        if (prompt_len + index >= max_context)
+            return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", prompt_len + index + 1,
+                        max_context);
+        for (int i = 0; i < n; i++) out[(size_t)i * max_new + index] = next[i];
+        if (index + 1 == max_new) break;
+        tok = next;
+        if ((rc = g4a_model_step(m, n, ids.data(), tok.data(), next.data()))) return rc;
+    }
+    return G4A_OK;
+}

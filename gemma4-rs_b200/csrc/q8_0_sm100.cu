@@ -370,13 +370,15 @@ __global__ void __launch_bounds__(256) q8_matvec_generic_kernel(Q8Params p) {
 
 // Quantizes x ([n_vec][cols] f32) into the caller's scratch, then runs the
 // mat-vec of `kind` (0 plain, 1 GEGLU with w2, 2 soft-cap) into out
-// ([n_vec][rows]). Returns a g4a_status; *msg names a failure.
+// ([n_vec][rows]). With x == nullptr the scratch already holds the quantized
+// activations (several projections of one input). Returns a g4a_status;
+// *msg names a failure.
 int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
            float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg) {
     *msg = "";
     const int64_t nb = cols / kQ8Block;
     const int64_t n_blocks = nb * n_vec;
-    if (n_blocks > 0) {
+    if (x && n_blocks > 0) {
         const int64_t threads = n_blocks * 32;
         q8_quantize_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, n_blocks, xs, xq);
     }

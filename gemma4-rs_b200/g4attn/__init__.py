@@ -113,6 +113,18 @@ def _load():
     L.g4a_matvec_q8_0_softcap.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int32,
                                           ctypes.c_float, _vp]
     L.g4a_quantize_q8_0.argtypes = [_vp, _vp, ctypes.c_int64, _vp, _vp]
+    L.g4a_synth_q8_0.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]
+    L.g4a_synth_norm.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
+                                 ctypes.c_float]
+    L.g4a_model_create.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(_vp)]
+    L.g4a_model_destroy.argtypes = [_vp]
+    L.g4a_model_destroy.restype = None
+    L.g4a_model_clear.argtypes = [_vp, ctypes.c_int32]
+    L.g4a_model_len.argtypes = [_vp, ctypes.c_int32, _i32p]
+    L.g4a_model_step.argtypes = [_vp, ctypes.c_int32, _i32p, _i32p, _i32p]
+    L.g4a_model_logits.argtypes = [_vp, ctypes.POINTER(_vp)]
+    L.g4a_model_generate.argtypes = [_vp, ctypes.c_int32, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                     _i32p]
     return L
 
 

@@ -272,6 +272,76 @@ int g4a_matvec_q8_0_softcap(g4a_ctx *ctx, const uint8_t *w_dev, int64_t rows, in
  * n/32 scales and n int8 quants. */
 int g4a_quantize_q8_0(g4a_ctx *ctx, const float *x_dev, int64_t n, float *scales_dev, int8_t *quants_dev);
 
+/* ---- E2B decoder: one token per sequence through the whole model --------
+ * crates/llm-gemma4/src/impl_/model.rs:252-449 (TransformerSpec::{embed,
+ * layer, logits} of Gemma4CpuModel with the default numerics) and
+ * generate.rs:15-64 (generate_cpu with greedy sampling, sample.rs:27-36), for
+ * many sequences at once. Every step runs on the device: the Q8_0 mat-vecs
+ * above, the fused decode attention over an f32 K/V cache per owner layer,
+ * and the norms, residual adds, per-layer embeddings and argmax. */
+
+#define G4A_MAX_LAYERS 64
+
+/* Weights of blk.N (GGUF names without the prefix; model.rs:123-141).
+ * Matrices are GGUF Q8_0 bytes [out][in] in device memory; norms are f32
+ * device arrays (the reference widens F32/BF16 norm tensors to f32). */
+typedef struct g4a_layer_weights {
+    const float *attn_norm, *attn_q_norm, *attn_k_norm, *post_attention_norm;
+    const float *ffn_norm, *post_ffw_norm, *post_norm;
+    const uint8_t *attn_q, *attn_k, *attn_v, *attn_output;  /* k, v unused on shared-KV layers */
+    const uint8_t *ffn_gate, *ffn_up, *ffn_down;
+    const uint8_t *inp_gate, *proj;                         /* per-layer embedding (ple_dim > 0) */
+    float layer_output_scale;                               /* the scalar tensor; 1 when absent */
+} g4a_layer_weights;
+
+typedef struct g4a_model_weights {
+    int32_t vocab_size, d_model, d_ff, ple_dim;
+    float final_logit_softcap;
+    const uint8_t *token_embd;     /* [vocab][d_model] Q8_0; also the tied output head */
+    const float *output_norm;      /* [d_model] */
+    const uint8_t *ple_token_embd; /* [vocab][n_layers * ple_dim] Q8_0 */
+    const uint8_t *ple_model_proj; /* [n_layers * ple_dim][d_model] Q8_0 */
+    const float *ple_proj_norm;    /* [ple_dim] */
+    g4a_layer_weights layers[G4A_MAX_LAYERS];
+} g4a_model_weights;
+
+typedef struct g4a_model g4a_model;
+
+/* Fills a device buffer with seeded synthetic weights (no reference
+ * counterpart; stands in for a GGUF file): Q8_0 blocks of N(0, sigma) values
+ * (n_values a multiple of 32, the buffer n_values/32*34 bytes), or f32 norm
+ * scales center + spread * N(0, 1) rounded to bf16. `tensor` separates the
+ * streams of different tensors of one seed. */
+int g4a_synth_q8_0(g4a_ctx *ctx, uint8_t *dst_dev, int64_t n_values, uint64_t seed, uint64_t tensor, float sigma);
+int g4a_synth_norm(g4a_ctx *ctx, float *dst_dev, int64_t n, uint64_t seed, uint64_t tensor, float center,
+                   float spread);
+
+/* A decoder over `w` (the pointers are borrowed and must outlive the model)
+ * for up to max_seqs sequences of up to max_tokens positions each; the
+ * context's hyperparameters give the layer pattern and its RoPE tables must
+ * cover max_tokens positions. The model owns its K/V caches. */
+int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_t max_seqs, int32_t max_tokens,
+                     g4a_model **out);
+void g4a_model_destroy(g4a_model *m);
+/* Gemma4CpuModel::clear_context for one sequence (its length back to 0). */
+int g4a_model_clear(g4a_model *m, int32_t seq);
+int g4a_model_len(const g4a_model *m, int32_t seq, int32_t *len);
+/* One forward pass: token tokens_host[i] of sequence seq_ids_host[i] (ids
+ * distinct) at position = that sequence's length, which then grows by one.
+ * next_host (optional) receives each row's greedy token. Blocks until the
+ * step is done. G4A_CONTEXT_TOO_LONG when a sequence is full. */
+int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids_host, const int32_t *tokens_host,
+                   int32_t *next_host);
+/* Device pointer to the soft-capped logits of the last step, [n][vocab]. */
+int g4a_model_logits(g4a_model *m, const float **logits_dev);
+/* generate_cpu (generate.rs:15-64) with greedy sampling for sequences
+ * 0..n-1 at once: clears them, feeds the prompts [n][prompt_len] token by
+ * token, then samples max_new tokens each into out_host [n][max_new]
+ * (the last one is not fed back). max_context bounds prompt + generated as
+ * the reference's max_context does. */
+int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompts_host, int32_t prompt_len, int32_t max_new,
+                       int32_t max_context, int32_t *out_host);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

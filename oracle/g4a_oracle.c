@@ -761,3 +761,120 @@ void orc_test_q8_0_bytes(const float *w, size_t n, uint8_t *out) {
         for (int i = 0; i < Q8_BLOCK; i++) o[2 + i] = (uint8_t)sat_i8(roundf(blk[i] / scale));
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* E2B decoder, one token: crates/llm-gemma4/src/impl_/model.rs:252-449       */
+/* ------------------------------------------------------------------------ */
+
+/* model.rs:208-216 project() with the default numerics: W @ quantize_q8_0(x). */
+static int dec_project(const uint8_t *w, size_t rows, const float *x, size_t cols, float *out) {
+    float *s = malloc((cols / Q8_BLOCK) * sizeof(float));
+    int8_t *q = malloc(cols);
+    int rc = orc_quantize_q8_0(x, cols, s, q);
+    if (!rc) rc = orc_matvec_q8_0(w, rows, cols, s, q, out);
+    free(s);
+    free(q);
+    return rc;
+}
+
+/* dequant of row `index` of a [rows][cols] Q8_0 matrix (model.rs:196-200) */
+static void dec_row(const uint8_t *w, size_t index, size_t cols, float *out) {
+    size_t row_bytes = cols / Q8_BLOCK * Q8_BLOCK_BYTES;
+    orc_dequant_q8_0(w + index * row_bytes, row_bytes, out);
+}
+
+int32_t orc_argmax_total(const float *x, size_t n) {
+    size_t best = 0;
+    for (size_t i = 1; i < n; i++)
+        if (total_key(x[i]) >= total_key(x[best])) best = i; /* max_by keeps the last maximum */
+    return (int32_t)best;
+}
+
+int orc_dec_forward(orc_kv *kv, const orc_hparams *hp, const orc_dec_w *w, int32_t token, size_t position,
+                    float *logits) {
+    const size_t d = (size_t)w->d_model, ple = (size_t)w->ple_dim, L = (size_t)hp->n_layers;
+    const float eps = hp->rms_norm_eps;
+    if (token < 0 || token >= w->vocab) return ORC_COMPUTE;
+    int rc = ORC_OK;
+    /* embed (model.rs:376-384): the token's row times sqrt(d_model) */
+    float *x = malloc(d * sizeof(float));
+    dec_row(w->token_embd, (size_t)token, d, x);
+    const float scale = sqrtf((float)d);
+    for (size_t i = 0; i < d; i++) x[i] = x[i] * scale;
+    /* per_layer_inputs (model.rs:252-270) */
+    const size_t width = L * ple;
+    float *pli = malloc((width ? width : 1) * sizeof(float));
+    if (ple) {
+        float *projected = malloc(width * sizeof(float)), *table = malloc(width * sizeof(float));
+        float *scaled = malloc(ple * sizeof(float)), *normed = malloc(ple * sizeof(float));
+        rc = dec_project(w->ple_model_proj, width, x, d, projected);
+        dec_row(w->ple_token_embd, (size_t)token, width, table);
+        const float projection_scale = 1.0f / sqrtf((float)d);
+        const float table_scale = sqrtf((float)ple);
+        const float input_scale = 1.0f / sqrtf(2.0f);
+        for (size_t l = 0; l < L && !rc; l++) {
+            for (size_t i = 0; i < ple; i++) scaled[i] = projected[l * ple + i] * projection_scale;
+            rc = orc_rms_norm(scaled, ple, w->ple_proj_norm, eps, normed);
+            for (size_t i = 0; i < ple; i++) pli[l * ple + i] = (normed[i] + table[l * ple + i] * table_scale) * input_scale;
+        }
+        free(projected); free(table); free(scaled); free(normed);
+    }
+    const size_t qmax = (size_t)hp->n_heads * (size_t)hp->head_dim_global;
+    float *normalized = malloc(d * sizeof(float)), *q = malloc(qmax * sizeof(float));
+    float *k = malloc((size_t)hp->head_dim_global * sizeof(float)), *v = malloc((size_t)hp->head_dim_global * sizeof(float));
+    float *att = malloc(qmax * sizeof(float)), *proj = malloc(d * sizeof(float)), *tmp = malloc(d * sizeof(float));
+    float *gated = malloc((size_t)w->d_ff * sizeof(float)), *gate = malloc((ple ? ple : 1) * sizeof(float));
+    for (size_t l = 0; l < L && !rc; l++) {
+        const orc_dec_layer_w *lw = &w->layers[l];
+        const size_t hd = (size_t)orc_head_dim(hp, (int32_t)l), qd = (size_t)hp->n_heads * hd;
+        int32_t source = -1;
+        rc = orc_kv_source_layer(hp, (int32_t)l, &source, NULL);
+        if (rc) break;
+        rc = orc_rms_norm(x, d, lw->attn_norm, eps, normalized);                       /* :392 */
+        if (!rc) rc = dec_project(lw->attn_q, qd, normalized, d, q);                    /* :393 */
+        if (!rc && source == (int32_t)l) {                                              /* :399-401 */
+            rc = dec_project(lw->attn_k, hd, normalized, d, k);
+            if (!rc) rc = dec_project(lw->attn_v, hd, normalized, d, v);
+        }
+        /* :394-396, :402-410: norms, RoPE, append, view, window, attend */
+        if (!rc) rc = orc_attention_block(kv, hp, (int32_t)l, position, q, k, v, lw->attn_q_norm, lw->attn_k_norm,
+                                          w->rope_freqs, 0, att);
+        if (!rc) rc = dec_project(lw->attn_output, d, att, qd, proj);                  /* :411 */
+        if (!rc) rc = orc_rms_norm(proj, d, lw->post_attention_norm, eps, tmp);        /* :412 */
+        for (size_t i = 0; i < d; i++) x[i] = x[i] + tmp[i];                            /* :413 residual */
+        if (!rc) rc = orc_rms_norm(x, d, lw->ffn_norm, eps, normalized);               /* :415 */
+        if (!rc) {                                                                      /* :416-417 */
+            float *s = malloc((d / Q8_BLOCK) * sizeof(float));
+            int8_t *qq = malloc(d);
+            rc = orc_quantize_q8_0(normalized, d, s, qq);
+            if (!rc) rc = orc_geglu_q8_0(lw->ffn_gate, lw->ffn_up, (size_t)w->d_ff, d, s, qq, gated);
+            free(s);
+            free(qq);
+        }
+        if (!rc) rc = dec_project(lw->ffn_down, d, gated, (size_t)w->d_ff, proj);     /* :418 */
+        if (!rc) rc = orc_rms_norm(proj, d, lw->post_ffw_norm, eps, tmp);              /* :419 */
+        for (size_t i = 0; i < d; i++) x[i] = x[i] + tmp[i];                            /* :420 */
+        if (!rc && ple) {                                                               /* :422-432 */
+            rc = dec_project(lw->inp_gate, ple, x, d, gate);
+            for (size_t i = 0; i < ple; i++) gate[i] = orc_gelu_tanh(gate[i]) * pli[l * ple + i];
+            if (!rc) rc = dec_project(lw->proj, d, gate, ple, proj);
+            if (!rc) rc = orc_rms_norm(proj, d, lw->post_norm, eps, tmp);
+            for (size_t i = 0; i < d; i++) x[i] = x[i] + tmp[i];
+        }
+        if (lw->layer_output_scale != 1.0f)                                            /* :433-435 */
+            for (size_t i = 0; i < d; i++) x[i] = x[i] * lw->layer_output_scale;
+    }
+    /* logits (model.rs:438-449): output norm, tied head, soft-cap */
+    if (!rc) rc = orc_rms_norm(x, d, w->output_norm, eps, normalized);
+    if (!rc) {
+        float *s = malloc((d / Q8_BLOCK) * sizeof(float));
+        int8_t *qq = malloc(d);
+        rc = orc_quantize_q8_0(normalized, d, s, qq);
+        if (!rc) rc = orc_matvec_q8_0_softcap(w->token_embd, (size_t)w->vocab, d, s, qq, w->final_logit_softcap, logits);
+        free(s);
+        free(qq);
+    }
+    free(x); free(pli); free(normalized); free(q); free(k); free(v); free(att); free(proj); free(tmp); free(gated);
+    free(gate);
+    return rc;
+}

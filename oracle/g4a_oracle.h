@@ -118,6 +118,32 @@ int orc_dequant_q8_0(const uint8_t *bytes, size_t n_bytes, float *out);
 void orc_test_values(uint64_t seed, size_t len, float *out);
 void orc_test_q8_0_bytes(const float *w, size_t n, uint8_t *out);
 
+/* ---- the E2B decoder, one token per call: crates/llm-gemma4/src/impl_/model.rs:252-449 ----
+ * Weights in the reference's GGUF layout: Q8_0 matrices (rows of
+ * cols/32 blocks) and f32 norm scales. The output head is tied to the token
+ * embeddings (model.rs:247-250). The K/V memory is an orc_kv. */
+typedef struct orc_dec_layer_w {
+    const uint8_t *attn_q, *attn_k, *attn_v, *attn_output, *ffn_gate, *ffn_up, *ffn_down, *inp_gate, *proj;
+    const float *attn_norm, *attn_q_norm, *attn_k_norm, *post_attention_norm, *ffn_norm, *post_ffw_norm, *post_norm;
+    float layer_output_scale; /* model.rs:433-435; 1.0 when absent */
+} orc_dec_layer_w;
+
+typedef struct orc_dec_w {
+    int32_t d_model, vocab, ple_dim, d_ff;
+    float final_logit_softcap;
+    const uint8_t *token_embd, *ple_token_embd, *ple_model_proj;
+    const float *ple_proj_norm, *output_norm, *rope_freqs;
+    orc_dec_layer_w layers[64];
+} orc_dec_w;
+
+/* Forward pass of `token` at `position` (model.rs:376-449 through
+ * transformer::prefill / decode_step): writes vocab logits. */
+int orc_dec_forward(orc_kv *kv, const orc_hparams *hp, const orc_dec_w *w, int32_t token, size_t position,
+                    float *logits);
+/* sample.rs:27-36 with temperature 0: index of the largest logit under
+ * total_cmp, the last one on ties. */
+int32_t orc_argmax_total(const float *x, size_t n);
+
 #ifdef __cplusplus
 }
 #endif

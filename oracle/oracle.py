@@ -344,3 +344,112 @@ def q8_0_bytes_of(w):
     out = np.empty(len(w) // 32 * 34, np.uint8)
     lib().orc_test_q8_0_bytes(_p(w), len(w), _u8(out))
     return out
+
+
+# ---------------------------------------------------------------------------
+# E2B decoder, one token per call (crates/llm-gemma4/src/impl_/model.rs:252-449)
+# ---------------------------------------------------------------------------
+
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+_DEC_MATS = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down", "inp_gate", "proj")
+_DEC_NORMS = ("attn_norm", "attn_q_norm", "attn_k_norm", "post_attention_norm", "ffn_norm", "post_ffw_norm",
+              "post_norm")
+
+
+class DecLayerW(ctypes.Structure):
+    _fields_ = [(n, _u8p) for n in _DEC_MATS] + [(n, _f32p) for n in _DEC_NORMS] + \
+        [("layer_output_scale", ctypes.c_float)]
+
+
+class DecW(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_int32), ("vocab", ctypes.c_int32), ("ple_dim", ctypes.c_int32),
+                ("d_ff", ctypes.c_int32), ("final_logit_softcap", ctypes.c_float),
+                ("token_embd", _u8p), ("ple_token_embd", _u8p), ("ple_model_proj", _u8p),
+                ("ple_proj_norm", _f32p), ("output_norm", _f32p), ("rope_freqs", _f32p),
+                ("layers", DecLayerW * 64)]
+
+
+def _dec_bind():
+    L = lib()
+    if not getattr(L, "_dec_bound", False):
+        L.orc_dec_forward.argtypes = [ctypes.c_void_p, ctypes.POINTER(HParams), ctypes.POINTER(DecW), ctypes.c_int32,
+                                      ctypes.c_size_t, _f32p]
+        L.orc_argmax_total.argtypes = [_f32p, ctypes.c_size_t]
+        L.orc_argmax_total.restype = ctypes.c_int32
+        L._dec_bound = True
+    return L
+
+
+def argmax_total(x) -> int:
+    """sample.rs:27-36 at temperature 0: the last maximum under total_cmp."""
+    x = f32(x).ravel()
+    return int(_dec_bind().orc_argmax_total(_p(x), len(x)))
+
+
+class Decoder:
+    """Gemma4CpuModel's forward pass over host weights given by GGUF name
+    (uint8 Q8_0 bytes for matrices, f32 for norms), with its own KvCache."""
+
+    def __init__(self, hp: HParams, weights: dict, d_model: int, vocab: int, ple_dim: int, d_ff: int,
+                 softcap: float, rope_freqs, layer_output_scales: dict):
+        _dec_bind()
+        self.hp, self.vocab = hp, vocab
+        self._keep = []
+        w = DecW()
+        w.d_model, w.vocab, w.ple_dim, w.d_ff, w.final_logit_softcap = d_model, vocab, ple_dim, d_ff, softcap
+
+        def u8(name):
+            a = weights.get(name)
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a, np.uint8)
+            self._keep.append(a)
+            return a.ctypes.data_as(_u8p)
+
+        def fl(name_or_array):
+            a = weights.get(name_or_array) if isinstance(name_or_array, str) else name_or_array
+            if a is None:
+                return None
+            a = f32(a)
+            self._keep.append(a)
+            return _p(a)
+
+        w.token_embd = u8("token_embd.weight")
+        w.ple_token_embd = u8("per_layer_token_embd.weight")
+        w.ple_model_proj = u8("per_layer_model_proj.weight")
+        w.ple_proj_norm = fl("per_layer_proj_norm.weight")
+        w.output_norm = fl("output_norm.weight")
+        w.rope_freqs = fl(np.asarray(rope_freqs, np.float32))
+        for l in range(hp.n_layers):
+            lw = w.layers[l]
+            for n in _DEC_MATS:
+                setattr(lw, n, u8(f"blk.{l}.{n}.weight"))
+            for n in _DEC_NORMS:
+                setattr(lw, n, fl(f"blk.{l}.{n}.weight"))
+            lw.layer_output_scale = layer_output_scales.get(l, 1.0)
+        self.w = w
+        self.kv = KvCache()
+
+    def clear(self):
+        self.kv.clear()
+
+    def forward(self, token: int, position: int) -> np.ndarray:
+        logits = np.empty(self.vocab, np.float32)
+        _check(lib().orc_dec_forward(self.kv.h, ctypes.byref(self.hp), ctypes.byref(self.w), token, position,
+                                     _p(logits)), "dec_forward")
+        return logits
+
+    def generate(self, prompt, max_new: int) -> list[int]:
+        """generate_cpu (generate.rs:15-64) with greedy sampling."""
+        self.clear()
+        logits = None
+        for pos, tok in enumerate(prompt):
+            logits = self.forward(int(tok), pos)
+        out = []
+        for index in range(max_new):
+            out.append(argmax_total(logits))
+            if index + 1 == max_new:
+                break
+            logits = self.forward(out[-1], len(prompt) + len(out) - 1)
+        return out
