@@ -524,13 +524,79 @@ def measure_q8_head(torch, g4a, ctx, stream, pk, reps=10, warmup=3, cpu_rows=819
                          "ms_full_equiv": round(rows * row_len / cpu_gbs / 1e6, 2)}}
 
 
+DEC_PROMPT, DEC_NEW = 19, 94
+
+
+def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0):
+    """Configuration 4: the whole E2B decoder (35 layers, vocab 262,144, Q8_0
+    weights from N(0, 0.02), bf16-rounded norms; synthetic, seeded) through
+    g4a_model_generate: a 19-token prompt of random ids, then 94 greedy
+    tokens (generate.rs:15-64: 19 + 93 forward passes per sequence), at each
+    batch size. Wall-clock around the public call, which uploads each step's
+    tokens and downloads its picks. The oracle's decoder runs the same
+    weights on the host cores for the CPU rate and a top-1 check of the
+    batch-1 run's first steps."""
+    import g4attn.model as gm
+    import oracle
+    w = gm.synthetic_weights(ctx, seed=4)
+    passes = DEC_PROMPT + DEC_NEW - 1
+    res = {"model": "E2B, 35 layers, d_model 1536, d_ff 3072, ple 256, vocab 262144, Q8_0 (synthetic)",
+           "weights_GB": round(w.nbytes() / 1e9, 3), "prompt": DEC_PROMPT, "new_tokens": DEC_NEW,
+           "forward_passes_per_seq": passes, "timing": "wall clock around g4a_model_generate (per-step H2D/D2H)"}
+    first = None
+    for n in batches:
+        m = gm.Model(ctx, w, max_seqs=n, max_tokens=DEC_PROMPT + DEC_NEW + 1)
+        prompts = np.random.default_rng(40 + n).integers(0, w.vocab, (n, DEC_PROMPT)).astype(np.int32)
+        m.generate(prompts, 4)  # eager first step and the graph capture of this batch size
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = m.generate(prompts, DEC_NEW)
+        dt = time.perf_counter() - t0
+        m.close()
+        if first is None:
+            first = (prompts[0].tolist(), out[0].tolist())
+        res[f"batch{n}"] = {"s": round(dt, 4), "tokens_per_s": round(n * passes / dt, 1),
+                            "generated_tokens_per_s": round(n * DEC_NEW / dt, 1),
+                            "ms_per_step": round(dt / passes * 1e3, 3),
+                            "h2d_bytes_per_step": 12 * n, "d2h_bytes_per_step": 4 * n + 4}
+    # host cores: the oracle decoder on the same bytes, teacher-forced with the
+    # device's batch-1 tokens; top-1 agreement of every step it reaches
+    host = {name: w.host(name) for name in w.tensors}
+    cores = oracle.pool_init(0)
+    dec = oracle.Decoder(w.hp, host, w.d_model, w.vocab, w.ple_dim, w.d_ff, w.softcap, gm.rope_freqs(w.hp), w.scales)
+    prompt, gen = first
+    seq = prompt + gen
+    agree, steps = 0, 0
+    t0 = time.perf_counter()
+    for p in range(passes):
+        logits = dec.forward(seq[p], p)
+        steps += 1
+        if p >= DEC_PROMPT - 1:
+            agree += int(oracle.argmax_total(logits) == gen[p - DEC_PROMPT + 1])
+        if time.perf_counter() - t0 > cpu_budget:
+            break
+    cpu_dt = time.perf_counter() - t0
+    res["cpu_port"] = {"tokens_per_s": round(steps / cpu_dt, 2), "cores": cores, "forward_passes": steps,
+                       "sample": "oracle decoder, batch 1 (the reference decodes one sequence at a time)"}
+    res["top1_vs_oracle"] = {"agree": agree, "compared": max(0, steps - DEC_PROMPT + 1)}
+    del w
+    return res
+
+
 def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     """One prefill problem on its own (for profiling one kernel on a small
     case): spec "prefill:<head width>:<tokens>:<window>", "prefill-cfg1"
     for configuration 1 alone (35 layer-equivalents in one call), or
-    "decode-batch1" for configuration 0's latency, or "q8-head[:rows]" for
-    the Q8_0 output-head mat-vec (262,144 rows unless given)."""
+    "decode-batch1" for configuration 0's latency, "q8-head[:rows]" for
+    the Q8_0 output-head mat-vec (262,144 rows unless given), or
+    "decoder[:b1,b2,...]" for configuration 4's decoder at those batch sizes."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
+    if spec.startswith("decoder"):
+        batches = tuple(int(b) for b in spec.split(":")[1].split(",")) if ":" in spec else (1, 256)
+        res = measure_decoder(torch, g4a, ctx, batches=batches)
+        ctx.close()
+        print(json.dumps({"case": spec, **res}), flush=True)
+        return
     if spec == "decode-batch1":
         stream = torch.cuda.Stream()
         ctx.set_stream(stream.cuda_stream)
@@ -698,6 +764,8 @@ def main():
         extras["decode_batch1"] = measure_batch1(torch, g4a, ctx, stream)
         extras["prefill"] = measure_prefill(torch, g4a, ctx, stream, pk)
         extras["q8_0_matvec_head"] = measure_q8_head(torch, g4a, ctx, stream, pk)
+        if dist is None:
+            extras["e2e_decoder"] = measure_decoder(torch, g4a, ctx)
     ctx.close()
     if dist is not None:
         dist.barrier()

@@ -18,6 +18,7 @@
 #include <math_constants.h>
 
 #include "internal.h"
+#include "libm_glibc.cuh"
 
 namespace g4a {
 namespace {
@@ -370,6 +371,142 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     if (threadIdx.x == 0) p.tickets[it.task] = 0u;  // ready for the next call
 }
 
+// Attention of one task per CTA in the reference's order of operations
+// (model.rs:323-343 attend_head; ops.rs:62-76 dot_f32, :105-127
+// softmax_f32), so that each output is the reference's bit for bit:
+//   score_j = dot_f32(q_h, k_j) * scale: 16 accumulators, element i into
+//             accumulator i % 16 (multiply, then add), the 16 summed in
+//             order from -0.0;
+//   p_j     = exp(score_j - max) / sum, exp as glibc's expf, the sum
+//             sequential in key order from -0.0;
+//   out     = sum_j p_j * v_j in key order from +0.0 (multiply, then add).
+// The q/k norms, RoPE and append are the fused kernel's (bit-exact already).
+template <int HD>
+__global__ void __launch_bounds__(kDecodeThreads) decode_exact_kernel(DecodeParams p) {
+    constexpr int PL = HD / 32;
+    constexpr int CPT = HD / kDecodeThreads;  // value columns per thread
+    extern __shared__ float sc[];             // [kHeads][max_rows]: scores, then probabilities
+    __shared__ __align__(16) float q_s[kHeads][HD];
+    __shared__ __align__(16) float knew_s[HD];
+    __shared__ __align__(16) float vnew_s[HD];
+    __shared__ int bad_s;
+
+    const DecodeItem it = p.items[blockIdx.x];
+    if (it.task < 0) return;  // an unused slot of a fixed-size (captured) launch
+    const DecodeTask &tk = p.tasks[it.task];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
+    const float2 *rope = tk.global ? p.rope_global : p.rope_local;
+    const int lo = tk.lo, rows = tk.hi - tk.lo;
+    if (threadIdx.x == 0) bad_s = rows > p.max_rows || rows <= 0;
+    {
+        float x[PL];
+        const float *src = tk.q_raw + (size_t)warp * HD;
+#pragma unroll
+        for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (!tk.q_ready) norm_rope_warp<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+#pragma unroll
+        for (int k = 0; k < PL; k++) q_s[warp][lane + 32 * k] = x[k];
+    }
+    if (tk.new_row >= 0 && warp < 2) {
+        float x[PL];
+        const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
+#pragma unroll
+        for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (warp == 0)
+            norm_rope_warp<HD>(x, tk.k_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+        else
+            norm_rope_warp<HD>(x, nullptr, nullptr, p.eps, lane);
+        float *dst = const_cast<float *>(row_ptr<float>(warp == 0 ? tk.k_base : tk.v_base, bt, p.page_tokens, HD,
+                                                        tk.new_row));
+        float *sm = warp == 0 ? knew_s : vnew_s;
+#pragma unroll
+        for (int k = 0; k < PL; k++) {
+            dst[lane + 32 * k] = x[k];
+            sm[lane + 32 * k] = x[k];
+        }
+    }
+    __syncthreads();
+    if (bad_s) {  // more rows than the launch's score buffer: report, skip
+        if (threadIdx.x == 0) atomicOr(p.err_flag, 4);
+        return;
+    }
+    // ---- scores: thread per (head, row), heads outer so a warp shares q ----
+    for (int pr = threadIdx.x; pr < kHeads * rows; pr += kDecodeThreads) {
+        const int h = pr / rows, r = pr - h * rows;
+        const int row = lo + r;
+        const float *kr = row == tk.new_row ? knew_s : row_ptr<float>(tk.k_base, bt, p.page_tokens, HD, row);
+        float acc[16];
+#pragma unroll
+        for (int l = 0; l < 16; l++) acc[l] = 0.0f;
+#pragma unroll 4
+        for (int m = 0; m < HD / 16; m++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float4 kv = *reinterpret_cast<const float4 *>(kr + 16 * m + 4 * c);
+                const float4 qv = *reinterpret_cast<const float4 *>(&q_s[h][16 * m + 4 * c]);
+                acc[4 * c + 0] = __fadd_rn(acc[4 * c + 0], __fmul_rn(qv.x, kv.x));
+                acc[4 * c + 1] = __fadd_rn(acc[4 * c + 1], __fmul_rn(qv.y, kv.y));
+                acc[4 * c + 2] = __fadd_rn(acc[4 * c + 2], __fmul_rn(qv.z, kv.z));
+                acc[4 * c + 3] = __fadd_rn(acc[4 * c + 3], __fmul_rn(qv.w, kv.w));
+            }
+        }
+        float s = -0.0f;
+#pragma unroll
+        for (int l = 0; l < 16; l++) s = __fadd_rn(s, acc[l]);
+        sc[(size_t)h * p.max_rows + r] = __fmul_rn(s, tk.scale);
+    }
+    __syncthreads();
+    // ---- softmax of head `warp` (ops.rs:105-127) ----
+    {
+        float *sh = sc + (size_t)warp * p.max_rows;
+        float m = -CUDART_INF_F;
+        bool finite = true;
+        for (int r = lane; r < rows; r += 32) {
+            const float v = sh[r];
+            finite = finite && isfinite(v);
+            m = fmaxf(m, v);
+        }
+        m = warp_max(m);
+        finite = __all_sync(kFull, finite);
+        for (int r = lane; r < rows; r += 32) sh[r] = glibc::expf(__fsub_rn(sh[r], m));
+        __syncwarp();
+        float total = -0.0f;
+        if (lane == 0)
+            for (int r = 0; r < rows; r++) total = __fadd_rn(total, sh[r]);
+        total = __shfl_sync(kFull, total, 0);
+        if (!finite || !isfinite(total) || total == 0.0f) {
+            if (lane == 0) atomicOr(p.err_flag, 1);
+            total = CUDART_NAN_F;
+        }
+        for (int r = lane; r < rows; r += 32) sh[r] = __fdiv_rn(sh[r], total);
+    }
+    __syncthreads();
+    // ---- out[h][i] = sum_j p[h][j] * v[j][i] in key order ----
+    float acc[kHeads][CPT];
+#pragma unroll
+    for (int h = 0; h < kHeads; h++)
+#pragma unroll
+        for (int u = 0; u < CPT; u++) acc[h][u] = 0.0f;
+    for (int r = 0; r < rows; r++) {
+        const int row = lo + r;
+        const float *vr = row == tk.new_row ? vnew_s : row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, row);
+        float v[CPT];
+#pragma unroll
+        for (int u = 0; u < CPT; u++) v[u] = vr[threadIdx.x + kDecodeThreads * u];
+#pragma unroll
+        for (int h = 0; h < kHeads; h++) {
+            const float pr = sc[(size_t)h * p.max_rows + r];
+#pragma unroll
+            for (int u = 0; u < CPT; u++) acc[h][u] = __fadd_rn(acc[h][u], __fmul_rn(pr, v[u]));
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < kHeads; h++)
+#pragma unroll
+        for (int u = 0; u < CPT; u++) tk.out[(size_t)h * HD + threadIdx.x + kDecodeThreads * u] = acc[h][u];
+}
+
 // Generic attend for any (n_heads, n_kv, hd <= 1024): one CTA per query
 // head, online softmax over blocks of 256 rows. Used for shapes the fused
 // E2B kernels do not serve (e.g. the reference's small synthetic models).
@@ -531,6 +668,24 @@ cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool /*fast
     } else if (hd == 512) {
         if (kv_f16) decode_kernel<512, __half><<<grid, block, 0, s>>>(p);
         else decode_kernel<512, float><<<grid, block, 0, s>>>(p);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode_exact(const DecodeParams &p, int hd, cudaStream_t s) {
+    if (p.n_items == 0) return cudaSuccess;
+    if (p.max_rows <= 0 || p.max_rows > kExactMaxRows) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kHeads * p.max_rows * sizeof(float);
+    if (hd == 256) {
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(decode_exact_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        decode_exact_kernel<256><<<p.n_items, kDecodeThreads, smem, s>>>(p);
+    } else if (hd == 512) {
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(decode_exact_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        decode_exact_kernel<512><<<p.n_items, kDecodeThreads, smem, s>>>(p);
     } else {
         return cudaErrorInvalidValue;
     }

@@ -10,14 +10,15 @@
 // after the cast agrees unless the two f64 sums straddle an f32 rounding
 // boundary), scale = 1 / sqrt(mean + eps) in f32, y = (x * scale) * w. The
 // quantization is matvec.rs:36-54 as in the Q8_0 kernels. Every f32 step is
-// a round-to-nearest intrinsic, never a fused multiply-add, so each value is
-// the reference's bit for bit apart from tanh (the device's tanhf).
+// a round-to-nearest intrinsic, never a fused multiply-add, and tanh is
+// glibc's, so each value is the reference's bit for bit.
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
 #include <cstdint>
 
 #include "internal.h"
+#include "libm_glibc.cuh"
 
 namespace g4a {
 namespace {
@@ -58,13 +59,14 @@ __global__ void synth_q8_kernel(uint8_t *dst, int64_t n_blocks, uint64_t seed, u
     const float scale = m / 127.0f;
     float q = roundf(w / scale);
     q = q != q ? 0.0f : fminf(fmaxf(q, -128.0f), 127.0f);
-    uint8_t *b = dst + blk * kQ8BlockBytes;
-    b[2 + lane] = (uint8_t)(int8_t)(int)q;
-    if (lane == 0) {
-        const unsigned short bits = __half_as_ushort(__float2half_rn(scale));
-        b[0] = (uint8_t)(bits & 0xff);
-        b[1] = (uint8_t)(bits >> 8);
-    }
+    // The block's 34 bytes as 17 little-endian halfwords (the block start is
+    // 2-byte aligned): halfword 0 the f16 scale, halfword k the quants of
+    // lanes 2k-2 and 2k-1.
+    const uint32_t qb = (uint32_t)(uint8_t)(int8_t)(int)q;
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, qb, 1);
+    uint16_t *h = reinterpret_cast<uint16_t *>(dst + blk * kQ8BlockBytes);
+    if ((lane & 1) == 0) h[1 + lane / 2] = (uint16_t)(qb | (hi << 8));
+    if (lane == 0) h[0] = __half_as_ushort(__float2half_rn(scale));
 }
 
 // Norm scales: center + spread * N(0, 1), rounded to bf16 (stored as f32,
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(kRowThreads) resid_kernel(ResidArgs a) {
 // ops.rs:85-89 gelu_tanh, left to right without fused multiply-adds
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float inner = __fmul_rn(__fmul_rn(0.7978846f, x), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, x), x)));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, glibc::tanhf(inner)));
 }
 
 // model.rs:426-428: gelu(gate) * this layer's per-layer input, quantized for

@@ -60,6 +60,7 @@ struct DecodeParams {
     const int32_t *cta_start;    // f16 kernel: CTA b runs items [cta_start[b], cta_start[b+1])
     void *q_blocks;              // f16 kernel: [tasks][kQBlockBytes] q hi/lo blocks
     const int32_t *split_tasks;  // f16 kernel: tasks whose items are merged by the combine kernel
+    int32_t max_rows;            // exact kernel: the most rows a task attends (scores in shared memory)
 };
 
 // Bulk append of already processed rows, or norm+RoPE of raw rows.
@@ -82,6 +83,11 @@ struct ViewParams {
 
 // Launchers (decode.cu).
 cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, cudaStream_t s);
+// f32 caches, one CTA per task (items never split a task): the reference's
+// own order of operations and glibc's expf, so the output is the reference's
+// bit for bit. Up to kExactMaxRows rows per task.
+constexpr int kExactMaxRows = 4096;
+cudaError_t launch_decode_exact(const DecodeParams &p, int hd, cudaStream_t s);
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
 constexpr size_t kQBlockBytes = 16 * 512 * 2;  // q hi/lo block of one task (f16 kernel)

@@ -6,13 +6,17 @@
 // A step is one fixed sequence of launches on the model's own stream (about
 // 16 per layer): the attention plan, embedding, per-layer inputs, then per
 // layer the fused residual/norm/quantize kernels, the Q8_0 mat-vecs and the
-// fused decode attention, then the soft-capped head and the argmax. Nothing
+// fused decode attention, then the soft-capped head and the argmax. Every
+// kernel rounds as the reference does (integer Q8_0 dots summed in block
+// order, attention in the reference's order with glibc's expf, glibc's
+// tanhf), so the logits are the reference's bit for bit. Nothing
 // in it depends on the host values of the step (tokens and positions are read
 // on the device), so after one eager run per batch size the step is captured
 // into a CUDA graph with its input upload and result download, and every
 // later step of that size is one graph launch.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <vector>
@@ -31,6 +35,7 @@ struct g4a_model {
     int32_t S = 0, T = 0;  // max sequences, max positions per sequence
     int32_t L = 0, d = 0, d_ff = 0, ple = 0, vocab = 0, hd_max = 0, qd_max = 0, cmax = 0;
     int32_t rows_per_item = 64, ms_local = 1, ms_global = 1;
+    bool exact = true;  // attention in the reference's order (one CTA per task); up to kExactMaxRows positions
     std::vector<int32_t> len, source, hd, global;
     cudaStream_t st = nullptr;
     cudaEvent_t ev = nullptr;
@@ -49,6 +54,8 @@ struct g4a_model {
     unsigned *tickets = nullptr;
     std::map<int32_t, cudaGraphExec_t> graphs;
     std::map<int32_t, int> eager_runs;
+    bool use_graphs = true;  // G4A_NO_GRAPH=1 in the environment: every step eager
+    std::vector<float *> k_cache, v_cache;  // per layer: its KV source's caches
     int32_t last_n = 0;
 };
 
@@ -162,7 +169,12 @@ int enqueue_step(g4a_model *m, int32_t n) {
         p.tickets = m->tickets;
         p.err_flag = ctx->d_err;
         p.n_items = n * (m->global[l] ? m->ms_global : m->ms_local);
-        MODEL_TRY(launch_decode(p, hd, 0, true, m->st));
+        if (m->exact) {
+            p.max_rows = m->global[l] ? m->T : std::min(ctx->hp.sliding_window, m->T);
+            MODEL_TRY(launch_decode_exact(p, hd, m->st));
+        } else {
+            MODEL_TRY(launch_decode(p, hd, 0, true, m->st));
+        }
         // output projection, post-attention norm, residual, FFN norm (:411-415)
         if ((rc = mv(m, 0, lw.attn_output, nullptr, d, qd, m->att, n, 0.0f, m->y))) return rc;
         MODEL_TRY(e2b_resid(m->x, m->y, lw.post_attention_norm, 1.0f, lw.ffn_norm, d, eps, m->xq, m->xs, n, m->st));
@@ -205,7 +217,7 @@ int run_step(g4a_model *m, int32_t n) {
         MODEL_TRY(cudaGraphLaunch(it->second, m->st));
         return G4A_OK;
     }
-    if (m->eager_runs[n]++ == 0) return record_step(m, n);  // first step of this size: eager
+    if (!m->use_graphs || m->eager_runs[n]++ == 0) return record_step(m, n);  // first step of a size: eager
     cudaGraph_t g = nullptr;
     MODEL_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
     const int rc = record_step(m, n);
@@ -317,6 +329,11 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
     m->hd_max = std::max(hp.head_dim_local, hp.head_dim_global);
     m->qd_max = kHeads * m->hd_max;
     m->cmax = std::max(std::max(m->d, m->d_ff), std::max(m->qd_max, m->ple));
+    // Up to kExactMaxRows positions every task is one CTA in the reference's
+    // order of operations (bit-exact logits); longer caches split tasks
+    // across CTAs (split-KV, within the decode tolerance).
+    m->exact = max_tokens <= kExactMaxRows;
+    if (m->exact) m->rows_per_item = max_tokens;
     const int32_t R = m->rows_per_item;
     m->ms_local = (std::min(hp.sliding_window, max_tokens) + R - 1) / R;
     m->ms_global = (max_tokens + R - 1) / R;
@@ -357,7 +374,13 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
         g4a_model_destroy(m);
         return fail(ctx, G4A_CUDA, "compute: out of device memory for the decoder");
     }
+    const char *no_graph = std::getenv("G4A_NO_GRAPH");
+    m->use_graphs = !(no_graph && no_graph[0] == '1');
+    m->k_cache.resize(m->L);
+    m->v_cache.resize(m->L);
     for (int l = 0; l < m->L; l++) {
+        m->k_cache[l] = kc[m->source[l]];
+        m->v_cache[l] = vc[m->source[l]];
         desc[l].q_w = w->layers[l].attn_q_norm;
         desc[l].k_w = w->layers[m->source[l]].attn_k_norm;
         desc[l].k_cache = kc[m->source[l]];
@@ -466,5 +489,22 @@ extern "C" int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompt
         tok = next;
         if ((rc = g4a_model_step(m, n, ids.data(), tok.data(), next.data()))) return rc;
     }
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_kv_view(const g4a_model *m, int32_t seq, int32_t layer, int32_t len, float *keys_dev,
+                                 float *values_dev) {
+    if (!m) return G4A_COMPUTE;
+    g4a_ctx *ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    if (seq < 0 || seq >= m->S || layer < 0 || layer >= m->L || len < 0 || (len && (!keys_dev || !values_dev)))
+        return fail(ctx, G4A_COMPUTE, "compute: invalid view arguments");
+    const int32_t src = m->source[layer];
+    if (len > m->len[seq])  // context_memory.rs:53-69
+        return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", len, m->len[seq]);
+    const size_t hd = (size_t)m->hd[src], off = (size_t)seq * m->T * hd, bytes = (size_t)len * hd * sizeof(float);
+    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(keys_dev, m->k_cache[layer] + off, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(values_dev, m->v_cache[layer] + off, bytes, cudaMemcpyDeviceToDevice,
+                                      ctx->stream));
     return G4A_OK;
 }

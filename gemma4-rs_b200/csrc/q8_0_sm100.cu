@@ -30,6 +30,7 @@
 
 #include "../../include/g4attn.h"
 #include "internal.h"
+#include "libm_glibc.cuh"
 #include "sm100_ptx.cuh"
 
 namespace g4a {
@@ -53,12 +54,12 @@ enum { KIND_PLAIN = 0, KIND_GEGLU = 1, KIND_SOFTCAP = 2 };
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float sqrt_2_over_pi = 0.7978846f, coef_a = 0.044715f;
     const float inner = __fmul_rn(__fmul_rn(sqrt_2_over_pi, x), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(coef_a, x), x)));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, glibc::tanhf(inner)));
 }
 
 // ops.rs:79-81
 __device__ __forceinline__ float softcap(float v, float cap) {
-    return __fmul_rn(tanhf(__fmul_rn(v, __fdiv_rn(1.0f, cap))), cap);
+    return __fmul_rn(glibc::tanhf(__fmul_rn(v, __fdiv_rn(1.0f, cap))), cap);
 }
 
 // One warp per block of 32 values: matvec.rs:36-54.

@@ -176,6 +176,17 @@ class Model:
         self.ctx.check(lib.g4a_model_len(self.h, seq, ctypes.byref(n)))
         return n.value
 
+    def kv_view(self, seq: int, layer: int, length: int):
+        """(keys, values) rows [0, length) of layer's K/V source, torch [length][hd]."""
+        import torch
+        src, _ = kv_source_layer(self.ctx.hp, layer)
+        hd = head_dim(self.ctx.hp, src)
+        k = torch.empty(length, hd, device=torch.device("cuda", self.ctx.device))
+        v = torch.empty_like(k)
+        self.ctx.check(lib.g4a_model_kv_view(self.h, seq, layer, length, k.data_ptr(), v.data_ptr()))
+        self.ctx.sync()
+        return k, v
+
     def step(self, seq_ids, tokens) -> list[int]:
         """One token per sequence; returns the greedy next tokens."""
         n = len(seq_ids)
@@ -194,7 +205,7 @@ class Model:
 
         class _View:
             __cuda_array_interface__ = {"shape": (self._n, self.weights.vocab), "typestr": "<f4",
-                                        "data": (p.value, True), "version": 3, "strides": None}
+                                        "data": (p.value, False), "version": 3, "strides": None}
         return torch.as_tensor(_View(), device=torch.device("cuda", self.ctx.device)).clone()
 
     def generate(self, prompts, max_new: int, max_context: int | None = None) -> np.ndarray:

@@ -332,6 +332,11 @@ int g4a_model_len(const g4a_model *m, int32_t seq, int32_t *len);
  * step is done. G4A_CONTEXT_TOO_LONG when a sequence is full. */
 int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids_host, const int32_t *tokens_host,
                    int32_t *next_host);
+/* ContextMemory::view (context_memory.rs:53-69) of the model's cache: rows
+ * [0, len) of `layer`'s K/V source for one sequence, [len][head_dim] f32
+ * each, copied into caller device buffers on the context's stream. */
+int g4a_model_kv_view(const g4a_model *m, int32_t seq, int32_t layer, int32_t len, float *keys_dev,
+                      float *values_dev);
 /* Device pointer to the soft-capped logits of the last step, [n][vocab]. */
 int g4a_model_logits(g4a_model *m, const float **logits_dev);
 /* generate_cpu (generate.rs:15-64) with greedy sampling for sequences

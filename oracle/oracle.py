@@ -394,7 +394,10 @@ class Decoder:
     def __init__(self, hp: HParams, weights: dict, d_model: int, vocab: int, ple_dim: int, d_ff: int,
                  softcap: float, rope_freqs, layer_output_scales: dict):
         _dec_bind()
-        self.hp, self.vocab = hp, vocab
+        own = HParams()  # the same fields, possibly from another binding's struct type
+        for name, _ in HParams._fields_:
+            setattr(own, name, getattr(hp, name))
+        self.hp, self.vocab = own, vocab
         self._keep = []
         w = DecW()
         w.d_model, w.vocab, w.ple_dim, w.d_ff, w.final_logit_softcap = d_model, vocab, ple_dim, d_ff, softcap
