@@ -527,7 +527,7 @@ def measure_q8_head(torch, g4a, ctx, stream, pk, reps=10, warmup=3, cpu_rows=819
 DEC_PROMPT, DEC_NEW = 19, 94
 
 
-def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0):
+def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0, new_tokens=DEC_NEW):
     """Configuration 4: the whole E2B decoder (35 layers, vocab 262,144, Q8_0
     weights from N(0, 0.02), bf16-rounded norms; synthetic, seeded) through
     g4a_model_generate: a 19-token prompt of random ids, then 94 greedy
@@ -539,9 +539,9 @@ def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0):
     import g4attn.model as gm
     import oracle
     w = gm.synthetic_weights(ctx, seed=4)
-    passes = DEC_PROMPT + DEC_NEW - 1
+    passes = DEC_PROMPT + new_tokens - 1
     res = {"model": "E2B, 35 layers, d_model 1536, d_ff 3072, ple 256, vocab 262144, Q8_0 (synthetic)",
-           "weights_GB": round(w.nbytes() / 1e9, 3), "prompt": DEC_PROMPT, "new_tokens": DEC_NEW,
+           "weights_GB": round(w.nbytes() / 1e9, 3), "prompt": DEC_PROMPT, "new_tokens": new_tokens,
            "forward_passes_per_seq": passes, "timing": "wall clock around g4a_model_generate (per-step H2D/D2H)"}
     first = None
     for n in batches:
@@ -550,7 +550,7 @@ def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0):
         m.generate(prompts, 4)  # eager first step and the graph capture of this batch size
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        out = m.generate(prompts, DEC_NEW)
+        out = m.generate(prompts, new_tokens)
         dt = time.perf_counter() - t0
         m.close()
         if first is None:
@@ -559,6 +559,9 @@ def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0):
                             "generated_tokens_per_s": round(n * DEC_NEW / dt, 1),
                             "ms_per_step": round(dt / passes * 1e3, 3),
                             "h2d_bytes_per_step": 12 * n, "d2h_bytes_per_step": 4 * n + 4}
+    if new_tokens != DEC_NEW:  # a short run (profiling): no host-core leg
+        del w
+        return res
     # host cores: the oracle decoder on the same bytes, teacher-forced with the
     # device's batch-1 tokens; top-1 agreement of every step it reaches
     host = {name: w.host(name) for name in w.tensors}
@@ -589,11 +592,14 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     for configuration 1 alone (35 layer-equivalents in one call), or
     "decode-batch1" for configuration 0's latency, "q8-head[:rows]" for
     the Q8_0 output-head mat-vec (262,144 rows unless given), or
-    "decoder[:b1,b2,...]" for configuration 4's decoder at those batch sizes."""
+    "decoder[:b1,b2,...[:new_tokens]]" for configuration 4's decoder at
+    those batch sizes (a short run when new_tokens is given)."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
     if spec.startswith("decoder"):
-        batches = tuple(int(b) for b in spec.split(":")[1].split(",")) if ":" in spec else (1, 256)
-        res = measure_decoder(torch, g4a, ctx, batches=batches)
+        parts = spec.split(":")
+        batches = tuple(int(b) for b in parts[1].split(",")) if len(parts) > 1 else (1, 256)
+        new_tokens = int(parts[2]) if len(parts) > 2 else DEC_NEW
+        res = measure_decoder(torch, g4a, ctx, batches=batches, new_tokens=new_tokens)
         ctx.close()
         print(json.dumps({"case": spec, **res}), flush=True)
         return

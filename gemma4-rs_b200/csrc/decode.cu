@@ -19,6 +19,7 @@
 
 #include "internal.h"
 #include "libm_glibc.cuh"
+#include "sm100_ptx.cuh"
 
 namespace g4a {
 namespace {
@@ -371,25 +372,31 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
     if (threadIdx.x == 0) p.tickets[it.task] = 0u;  // ready for the next call
 }
 
-// Attention of one task per CTA in the reference's order of operations
-// (model.rs:323-343 attend_head; ops.rs:62-76 dot_f32, :105-127
-// softmax_f32), so that each output is the reference's bit for bit:
-//   score_j = dot_f32(q_h, k_j) * scale: 16 accumulators, element i into
-//             accumulator i % 16 (multiply, then add), the 16 summed in
-//             order from -0.0;
-//   p_j     = exp(score_j - max) / sum, exp as glibc's expf, the sum
-//             sequential in key order from -0.0;
-//   out     = sum_j p_j * v_j in key order from +0.0 (multiply, then add).
-// The q/k norms, RoPE and append are the fused kernel's (bit-exact already).
+// Attention in the reference's order of operations (model.rs:323-343
+// attend_head; ops.rs:62-76 dot_f32, :105-127 softmax_f32), so that each
+// output is the reference's bit for bit, in two launches:
+//   scores  one CTA per (task, chunk of kExactChunk rows): q norm + RoPE, the
+//           append (the CTA holding the new row), the chunk's K rows staged
+//           in shared memory, then one thread per (head, row):
+//           dot_f32 = 16 accumulators (element i into accumulator i % 16,
+//           multiply then add), summed in order from -0.0, times the scale;
+//   pv      one CTA per (task, head, 128 value columns): max, p_j =
+//           exp(s_j - max) / sum with glibc's expf and the sum sequential in
+//           key order from -0.0, then out = sum_j p_j * v_j in key order from
+//           +0.0 (multiply then add), one thread per column.
+// The q/k norms, RoPE and the stored rows are the fused kernel's (bit-exact).
+constexpr int kExactChunk = 32;
+constexpr int kPvCols = 128;
+
 template <int HD>
-__global__ void __launch_bounds__(kDecodeThreads) decode_exact_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads) exact_scores_kernel(DecodeParams p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
     constexpr int PL = HD / 32;
-    constexpr int CPT = HD / kDecodeThreads;  // value columns per thread
-    extern __shared__ float sc[];             // [kHeads][max_rows]: scores, then probabilities
+    constexpr int KS = HD + 4;  // padded row stride: the 8 lanes of a float4 phase hit distinct banks
+    extern __shared__ float4 k_s4[];  // [kExactChunk][KS]
+    float *k_s = reinterpret_cast<float *>(k_s4);
     __shared__ __align__(16) float q_s[kHeads][HD];
-    __shared__ __align__(16) float knew_s[HD];
-    __shared__ __align__(16) float vnew_s[HD];
-    __shared__ int bad_s;
 
     const DecodeItem it = p.items[blockIdx.x];
     if (it.task < 0) return;  // an unused slot of a fixed-size (captured) launch
@@ -397,8 +404,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_exact_kernel(DecodePara
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
     const float2 *rope = tk.global ? p.rope_global : p.rope_local;
-    const int lo = tk.lo, rows = tk.hi - tk.lo;
-    if (threadIdx.x == 0) bad_s = rows > p.max_rows || rows <= 0;
+    const int nr = it.row_hi - it.row_lo;
     {
         float x[PL];
         const float *src = tk.q_raw + (size_t)warp * HD;
@@ -408,7 +414,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_exact_kernel(DecodePara
 #pragma unroll
         for (int k = 0; k < PL; k++) q_s[warp][lane + 32 * k] = x[k];
     }
-    if (tk.new_row >= 0 && warp < 2) {
+    const bool in_chunk = tk.new_row >= it.row_lo && tk.new_row < it.row_hi;
+    const bool has_new = tk.new_row >= 0 && (in_chunk || (it.split == tk.n_splits - 1 && tk.new_row >= it.row_hi));
+    if (has_new && warp < 2) {
         float x[PL];
         const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
 #pragma unroll
@@ -419,92 +427,107 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_exact_kernel(DecodePara
             norm_rope_warp<HD>(x, nullptr, nullptr, p.eps, lane);
         float *dst = const_cast<float *>(row_ptr<float>(warp == 0 ? tk.k_base : tk.v_base, bt, p.page_tokens, HD,
                                                         tk.new_row));
-        float *sm = warp == 0 ? knew_s : vnew_s;
 #pragma unroll
-        for (int k = 0; k < PL; k++) {
-            dst[lane + 32 * k] = x[k];
-            sm[lane + 32 * k] = x[k];
+        for (int k = 0; k < PL; k++) dst[lane + 32 * k] = x[k];
+        if (warp == 0 && in_chunk) {
+            float *ks = k_s + (size_t)(tk.new_row - it.row_lo) * KS;
+#pragma unroll
+            for (int k = 0; k < PL; k++) ks[lane + 32 * k] = x[k];
         }
     }
-    __syncthreads();
-    if (bad_s) {  // more rows than the launch's score buffer: report, skip
-        if (threadIdx.x == 0) atomicOr(p.err_flag, 4);
-        return;
+    // the chunk's other K rows, every load of the chunk in flight at once
+    for (int e = threadIdx.x; e < nr * (HD / 4); e += kDecodeThreads) {
+        const int r = e / (HD / 4), c = e - r * (HD / 4);
+        if (it.row_lo + r == tk.new_row) continue;
+        const float4 v = *(reinterpret_cast<const float4 *>(row_ptr<float>(tk.k_base, bt, p.page_tokens, HD,
+                                                                            it.row_lo + r)) + c);
+        *reinterpret_cast<float4 *>(k_s + (size_t)r * KS + 4 * c) = v;
     }
-    // ---- scores: thread per (head, row), heads outer so a warp shares q ----
-    for (int pr = threadIdx.x; pr < kHeads * rows; pr += kDecodeThreads) {
-        const int h = pr / rows, r = pr - h * rows;
-        const int row = lo + r;
-        const float *kr = row == tk.new_row ? knew_s : row_ptr<float>(tk.k_base, bt, p.page_tokens, HD, row);
+    __syncthreads();
+    // thread = (head warp, row lane)
+    if (lane < nr) {
+        const float *kr = k_s + (size_t)lane * KS;
+        const float *qh = q_s[warp];
         float acc[16];
 #pragma unroll
         for (int l = 0; l < 16; l++) acc[l] = 0.0f;
-#pragma unroll 4
+#pragma unroll 2
         for (int m = 0; m < HD / 16; m++) {
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float4 kv = *reinterpret_cast<const float4 *>(kr + 16 * m + 4 * c);
-                const float4 qv = *reinterpret_cast<const float4 *>(&q_s[h][16 * m + 4 * c]);
+                const float4 qv = *reinterpret_cast<const float4 *>(qh + 16 * m + 4 * c);
                 acc[4 * c + 0] = __fadd_rn(acc[4 * c + 0], __fmul_rn(qv.x, kv.x));
                 acc[4 * c + 1] = __fadd_rn(acc[4 * c + 1], __fmul_rn(qv.y, kv.y));
                 acc[4 * c + 2] = __fadd_rn(acc[4 * c + 2], __fmul_rn(qv.z, kv.z));
                 acc[4 * c + 3] = __fadd_rn(acc[4 * c + 3], __fmul_rn(qv.w, kv.w));
             }
         }
-        float s = -0.0f;
+        float sum = -0.0f;
 #pragma unroll
-        for (int l = 0; l < 16; l++) s = __fadd_rn(s, acc[l]);
-        sc[(size_t)h * p.max_rows + r] = __fmul_rn(s, tk.scale);
+        for (int l = 0; l < 16; l++) sum = __fadd_rn(sum, acc[l]);
+        p.scores[((size_t)it.task * kHeads + warp) * p.max_rows + (it.row_lo - tk.lo + lane)] = __fmul_rn(sum, tk.scale);
     }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPvCols) exact_pv_kernel(DecodeParams p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int CH = HD / kPvCols;  // column chunks per head
+    extern __shared__ float pr[];     // [max_rows]: scores, then probabilities
+    __shared__ float red[kPvCols / 32];
+    __shared__ int flag_s;
+    const int task = blockIdx.x / (kHeads * CH);
+    const int h = (blockIdx.x / CH) % kHeads, chunk = blockIdx.x % CH;
+    const DecodeTask &tk = p.tasks[task];
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
+    const int rows = tk.hi - tk.lo, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const float *sc = p.scores + ((size_t)task * kHeads + h) * p.max_rows;
+    float m = -CUDART_INF_F;
+    bool finite = true;
+    for (int r = t; r < rows; r += kPvCols) {
+        const float v = sc[r];
+        pr[r] = v;
+        finite = finite && isfinite(v);
+        m = fmaxf(m, v);
+    }
+    m = warp_max(m);
+    finite = __all_sync(kFull, finite);
+    if (t == 0) flag_s = 1;
+    if (lane == 0) red[warp] = m;
     __syncthreads();
-    // ---- softmax of head `warp` (ops.rs:105-127) ----
-    {
-        float *sh = sc + (size_t)warp * p.max_rows;
-        float m = -CUDART_INF_F;
-        bool finite = true;
-        for (int r = lane; r < rows; r += 32) {
-            const float v = sh[r];
-            finite = finite && isfinite(v);
-            m = fmaxf(m, v);
-        }
-        m = warp_max(m);
-        finite = __all_sync(kFull, finite);
-        for (int r = lane; r < rows; r += 32) sh[r] = glibc::expf(__fsub_rn(sh[r], m));
-        __syncwarp();
+    if (lane == 0 && !finite) flag_s = 0;
+    m = red[0];
+#pragma unroll
+    for (int w = 1; w < kPvCols / 32; w++) m = fmaxf(m, red[w]);
+    for (int r = t; r < rows; r += kPvCols) pr[r] = glibc::expf(__fsub_rn(pr[r], m));
+    __syncthreads();
+    if (t == 0) {
         float total = -0.0f;
-        if (lane == 0)
-            for (int r = 0; r < rows; r++) total = __fadd_rn(total, sh[r]);
-        total = __shfl_sync(kFull, total, 0);
-        if (!finite || !isfinite(total) || total == 0.0f) {
-            if (lane == 0) atomicOr(p.err_flag, 1);
+        for (int r = 0; r < rows; r++) total = __fadd_rn(total, pr[r]);
+        if (!flag_s || !isfinite(total) || total == 0.0f) {  // softmax_f32's error
+            if (chunk == 0) atomicOr(p.err_flag, 1);
             total = CUDART_NAN_F;
         }
-        for (int r = lane; r < rows; r += 32) sh[r] = __fdiv_rn(sh[r], total);
+        red[0] = total;
     }
     __syncthreads();
-    // ---- out[h][i] = sum_j p[h][j] * v[j][i] in key order ----
-    float acc[kHeads][CPT];
+    const float total = red[0];
+    for (int r = t; r < rows; r += kPvCols) pr[r] = __fdiv_rn(pr[r], total);
+    __syncthreads();
+    const int col = chunk * kPvCols + t;
+    float acc = 0.0f;
+    int r = 0;
+    for (; r + 16 <= rows; r += 16) {
+        float v[16];
 #pragma unroll
-    for (int h = 0; h < kHeads; h++)
+        for (int u = 0; u < 16; u++) v[u] = row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, tk.lo + r + u)[col];
 #pragma unroll
-        for (int u = 0; u < CPT; u++) acc[h][u] = 0.0f;
-    for (int r = 0; r < rows; r++) {
-        const int row = lo + r;
-        const float *vr = row == tk.new_row ? vnew_s : row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, row);
-        float v[CPT];
-#pragma unroll
-        for (int u = 0; u < CPT; u++) v[u] = vr[threadIdx.x + kDecodeThreads * u];
-#pragma unroll
-        for (int h = 0; h < kHeads; h++) {
-            const float pr = sc[(size_t)h * p.max_rows + r];
-#pragma unroll
-            for (int u = 0; u < CPT; u++) acc[h][u] = __fadd_rn(acc[h][u], __fmul_rn(pr, v[u]));
-        }
+        for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(pr[r + u], v[u]));
     }
-#pragma unroll
-    for (int h = 0; h < kHeads; h++)
-#pragma unroll
-        for (int u = 0; u < CPT; u++) tk.out[(size_t)h * HD + threadIdx.x + kDecodeThreads * u] = acc[h][u];
+    for (; r < rows; r++) acc = __fadd_rn(acc, __fmul_rn(pr[r], row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, tk.lo + r)[col]));
+    tk.out[(size_t)h * HD + col] = acc;
 }
 
 // Generic attend for any (n_heads, n_kv, hd <= 1024): one CTA per query
@@ -674,18 +697,26 @@ cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool /*fast
     return cudaGetLastError();
 }
 
-cudaError_t launch_decode_exact(const DecodeParams &p, int hd, cudaStream_t s) {
-    if (p.n_items == 0) return cudaSuccess;
-    if (p.max_rows <= 0 || p.max_rows > kExactMaxRows) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)kHeads * p.max_rows * sizeof(float);
+cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl) {
+    if (p.n_items == 0 || n_tasks == 0) return cudaSuccess;
+    if (p.max_rows <= 0 || p.max_rows > kExactMaxRows || !p.scores) return cudaErrorInvalidValue;
+    const size_t pv_smem = (size_t)p.max_rows * sizeof(float);
     if (hd == 256) {
-        if (smem > 48 * 1024)
-            cudaFuncSetAttribute(decode_exact_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        decode_exact_kernel<256><<<p.n_items, kDecodeThreads, smem, s>>>(p);
+        const size_t smem = (size_t)kExactChunk * (256 + 4) * sizeof(float);
+        cudaFuncSetAttribute(exact_scores_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = launch_k(pdl, exact_scores_kernel<256>, dim3(p.n_items), dim3(kDecodeThreads), smem, s, p);
+        if (e == cudaSuccess)
+            e = launch_k(pdl, exact_pv_kernel<256>, dim3(n_tasks * kHeads * (256 / kPvCols)), dim3(kPvCols), pv_smem,
+                         s, p);
+        if (e != cudaSuccess) return e;
     } else if (hd == 512) {
-        if (smem > 48 * 1024)
-            cudaFuncSetAttribute(decode_exact_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        decode_exact_kernel<512><<<p.n_items, kDecodeThreads, smem, s>>>(p);
+        const size_t smem = (size_t)kExactChunk * (512 + 4) * sizeof(float);
+        cudaFuncSetAttribute(exact_scores_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = launch_k(pdl, exact_scores_kernel<512>, dim3(p.n_items), dim3(kDecodeThreads), smem, s, p);
+        if (e == cudaSuccess)
+            e = launch_k(pdl, exact_pv_kernel<512>, dim3(n_tasks * kHeads * (512 / kPvCols)), dim3(kPvCols), pv_smem,
+                         s, p);
+        if (e != cudaSuccess) return e;
     } else {
         return cudaErrorInvalidValue;
     }

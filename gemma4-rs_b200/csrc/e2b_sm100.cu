@@ -19,6 +19,7 @@
 
 #include "internal.h"
 #include "libm_glibc.cuh"
+#include "sm100_ptx.cuh"
 
 namespace g4a {
 namespace {
@@ -26,7 +27,7 @@ namespace {
 constexpr int kQ8Block = 32;
 constexpr int kQ8BlockBytes = 34;
 constexpr int kRowThreads = 256;
-constexpr int kMaxRow = 4096;  // widest row a fused row kernel holds in shared memory
+constexpr int kMaxRow = 4096;  // widest row of the fused row kernels (one float4 per thread)
 
 // ---- synthetic weights ---------------------------------------------------
 
@@ -101,23 +102,6 @@ __device__ __forceinline__ float rms_scale(const float *x, int n, float eps, dou
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
-// matvec.rs:36-54 on a row in shared memory, a warp per block of 32
-__device__ __forceinline__ void quantize_row(const float *a, int n, int8_t *xq, float *xs) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int b = warp; b < n / kQ8Block; b += nw) {
-        const float v = a[b * kQ8Block + lane];
-        float m = fabsf(v);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float scale = __fdiv_rn(m, 127.0f);
-        const float inverse = scale == 0.0f ? 0.0f : __fdiv_rn(1.0f, scale);
-        float q = rintf(__fmul_rn(v, inverse));
-        q = q != q ? 0.0f : fminf(fmaxf(q, -128.0f), 127.0f);  // Rust's saturating `as i8`
-        xq[b * kQ8Block + lane] = (int8_t)(int)q;
-        if (lane == 0) xs[b] = __half2float(__float2half_rn(scale));
-    }
-}
-
 __device__ __forceinline__ float q8_elem(const uint8_t *row, int64_t e) {  // dequant.rs:13-24
     const uint8_t *blk = row + (e / kQ8Block) * kQ8BlockBytes;
     const float sc = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
@@ -129,6 +113,8 @@ __device__ __forceinline__ float q8_elem(const uint8_t *row, int64_t e) {  // de
 // model.rs:376-384: the token's embedding row times sqrt(d_model)
 __global__ void embed_kernel(const uint8_t *__restrict__ table, int d, const int32_t *__restrict__ tokens, float scale,
                              float *__restrict__ x) {
+    ptx::pdl_trigger();  // a dependent may launch; it waits for this grid itself
+    ptx::pdl_wait();
     const int s = blockIdx.x;
     const uint8_t *row = table + (int64_t)tokens[s] * (d / kQ8Block) * kQ8BlockBytes;
     for (int i = threadIdx.x; i < d; i += blockDim.x) x[(int64_t)s * d + i] = __fmul_rn(q8_elem(row, i), scale);
@@ -139,6 +125,8 @@ __global__ void embed_kernel(const uint8_t *__restrict__ table, int d, const int
 __global__ void ple_inputs_kernel(const float *__restrict__ P, const uint8_t *__restrict__ table,
                                   const int32_t *__restrict__ tokens, const float *__restrict__ w, int L, int ple,
                                   float ps, float ts, float is, float eps, float *__restrict__ out) {
+    ptx::pdl_trigger();  // a dependent may launch; it waits for this grid itself
+    ptx::pdl_wait();
     __shared__ double red[32];
     __shared__ float scaled[1024];
     const int s = blockIdx.x / L, l = blockIdx.x % L;
@@ -169,30 +157,77 @@ struct ResidArgs {
     float eps, post;
 };
 
-__global__ void __launch_bounds__(kRowThreads) resid_kernel(ResidArgs a) {
+// matvec.rs:36-54 for the four values a thread holds; the 8 consecutive
+// threads of a block of 32 share its maximum through shuffles.
+__device__ __forceinline__ void quant4(float4 v, int t, bool on, int8_t *xq_row, float *xs_row) {
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    const float scale = __fdiv_rn(m, 127.0f);
+    const float inverse = scale == 0.0f ? 0.0f : __fdiv_rn(1.0f, scale);
+    auto q = [&](float x) {
+        float r = rintf(__fmul_rn(x, inverse));
+        r = r != r ? 0.0f : fminf(fmaxf(r, -128.0f), 127.0f);  // Rust's saturating `as i8`
+        return (uint32_t)(uint8_t)(int8_t)(int)r;
+    };
+    if (!on) return;  // a whole group of 8 past the row's end (d a multiple of 32)
+    reinterpret_cast<uint32_t *>(xq_row)[t] = q(v.x) | (q(v.y) << 8) | (q(v.z) << 16) | (q(v.w) << 24);
+    if ((t & 7) == 0) xs_row[t >> 3] = __half2float(__float2half_rn(scale));
+}
+
+__device__ __forceinline__ double sq4(float4 v) {  // the f32 squares, widened and summed in f64
+    double s = (double)__fmul_rn(v.x, v.x);
+    s += (double)__fmul_rn(v.y, v.y);
+    s += (double)__fmul_rn(v.z, v.z);
+    s += (double)__fmul_rn(v.w, v.w);
+    return s;
+}
+
+__device__ __forceinline__ float scale_of(double sum, int n, float eps) {  // ops.rs:50-51
+    const float mean = (float)(sum / (double)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// One CTA per row, one float4 per thread (d / 4 threads, rounded up to
+// whole warps): no loops, two block reductions at most.
+__global__ void __launch_bounds__(1024) resid_kernel(ResidArgs a) {
+    ptx::pdl_trigger();  // a dependent may launch; it waits for this grid itself
+    ptx::pdl_wait();
     __shared__ double red[32];
-    __shared__ float v[kMaxRow];
-    const int s = blockIdx.x, d = a.d;
-    float *xr = a.x + (int64_t)s * d;
+    const int s = blockIdx.x, d = a.d, t = threadIdx.x;
+    const bool on = 4 * t < d;
+    float4 *xr = reinterpret_cast<float4 *>(a.x + (int64_t)s * d);
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 v;
     if (a.y) {
-        const float *yr = a.y + (int64_t)s * d;
-        const float sc = rms_scale(yr, d, a.eps, red);
-        for (int i = threadIdx.x; i < d; i += blockDim.x) {
-            float t = __fadd_rn(xr[i], __fmul_rn(__fmul_rn(yr[i], sc), a.w_post[i]));
-            if (a.post != 1.0f) t = __fmul_rn(t, a.post);
-            v[i] = t;
-            xr[i] = t;
+        const float4 y = on ? __ldg(reinterpret_cast<const float4 *>(a.y + (int64_t)s * d) + t) : zero;
+        const float4 x = on ? xr[t] : zero;
+        const float4 w = on ? __ldg(reinterpret_cast<const float4 *>(a.w_post) + t) : zero;
+        const float sc = scale_of(block_sum_f64(sq4(y), red), d, a.eps);
+        v.x = __fadd_rn(x.x, __fmul_rn(__fmul_rn(y.x, sc), w.x));
+        v.y = __fadd_rn(x.y, __fmul_rn(__fmul_rn(y.y, sc), w.y));
+        v.z = __fadd_rn(x.z, __fmul_rn(__fmul_rn(y.z, sc), w.z));
+        v.w = __fadd_rn(x.w, __fmul_rn(__fmul_rn(y.w, sc), w.w));
+        if (a.post != 1.0f) {
+            v.x = __fmul_rn(v.x, a.post);
+            v.y = __fmul_rn(v.y, a.post);
+            v.z = __fmul_rn(v.z, a.post);
+            v.w = __fmul_rn(v.w, a.post);
         }
+        if (on) xr[t] = v;
     } else {
-        for (int i = threadIdx.x; i < d; i += blockDim.x) v[i] = xr[i];
+        v = on ? xr[t] : zero;
     }
-    __syncthreads();
     if (a.w_next) {
-        const float sc = rms_scale(v, d, a.eps, red);
-        for (int i = threadIdx.x; i < d; i += blockDim.x) v[i] = __fmul_rn(__fmul_rn(v[i], sc), a.w_next[i]);
-        __syncthreads();
+        const float4 w = on ? __ldg(reinterpret_cast<const float4 *>(a.w_next) + t) : zero;
+        const float sc = scale_of(block_sum_f64(sq4(v), red), d, a.eps);
+        v.x = __fmul_rn(__fmul_rn(v.x, sc), w.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, sc), w.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, sc), w.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, sc), w.w);
     }
-    quantize_row(v, d, a.xq + (int64_t)s * d, a.xs + (int64_t)s * (d / kQ8Block));
+    quant4(v, t, on, a.xq + (int64_t)s * d, a.xs + (int64_t)s * (d / kQ8Block));
 }
 
 // ops.rs:85-89 gelu_tanh, left to right without fused multiply-adds
@@ -202,47 +237,60 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 }
 
 // model.rs:426-428: gelu(gate) * this layer's per-layer input, quantized for
-// the `proj` mat-vec
-__global__ void __launch_bounds__(kRowThreads) gelu_quant_kernel(const float *__restrict__ gate,
-                                                                 const float *__restrict__ pli, int layer, int L,
-                                                                 int ple, int8_t *xq, float *xs) {
-    __shared__ float v[1024];
-    const int s = blockIdx.x;
-    for (int i = threadIdx.x; i < ple; i += blockDim.x)
-        v[i] = __fmul_rn(gelu_tanh(gate[(int64_t)s * ple + i]), pli[((int64_t)s * L + layer) * ple + i]);
-    __syncthreads();
-    quantize_row(v, ple, xq + (int64_t)s * ple, xs + (int64_t)s * (ple / kQ8Block));
+// the `proj` mat-vec; one float4 per thread
+__global__ void __launch_bounds__(256) gelu_quant_kernel(const float *__restrict__ gate, const float *__restrict__ pli,
+                                                         int layer, int L, int ple, int8_t *xq, float *xs) {
+    ptx::pdl_trigger();  // a dependent may launch; it waits for this grid itself
+    ptx::pdl_wait();
+    const int s = blockIdx.x, t = threadIdx.x;
+    const float4 g = __ldg(reinterpret_cast<const float4 *>(gate + (int64_t)s * ple) + t);
+    const float4 e = __ldg(reinterpret_cast<const float4 *>(pli + ((int64_t)s * L + layer) * ple) + t);
+    float4 v;
+    v.x = __fmul_rn(gelu_tanh(g.x), e.x);
+    v.y = __fmul_rn(gelu_tanh(g.y), e.y);
+    v.z = __fmul_rn(gelu_tanh(g.z), e.z);
+    v.w = __fmul_rn(gelu_tanh(g.w), e.w);
+    quant4(v, t, true, xq + (int64_t)s * ple, xs + (int64_t)s * (ple / kQ8Block));
 }
 
 // Greedy sampling (crates/llm-eng/src/sample.rs:27-36): the maximum under
 // f32::total_cmp, the last index among equal maxima (Iterator::max_by). The
 // total order as an unsigned key, packed above the index, so one unsigned
-// maximum decides both.
+// maximum decides both; each CTA scans a chunk of the row and folds its
+// result into the row's slot with a 64-bit atomic maximum (slots zeroed by
+// the step's plan kernel).
 __device__ __forceinline__ uint32_t total_key(float f) {
     int32_t b = __float_as_int(f);
     b ^= (int32_t)(((uint32_t)(b >> 31)) >> 1);
     return (uint32_t)b ^ 0x80000000u;
 }
 
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits, int64_t vocab,
-                                                      int32_t *__restrict__ out) {
-    __shared__ unsigned long long best_s[32];
-    const float *row = logits + (int64_t)blockIdx.x * vocab;
-    unsigned long long best = 0;
-    for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+constexpr int kArgmaxChunk = 4096;
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ logits, int64_t vocab,
+                                                     unsigned long long *__restrict__ best) {
+    ptx::pdl_trigger();  // a dependent may launch; it waits for this grid itself
+    ptx::pdl_wait();
+    __shared__ unsigned long long best_s[8];
+    const int s = blockIdx.y;
+    const float *row = logits + (int64_t)s * vocab;
+    const int64_t i0 = (int64_t)blockIdx.x * kArgmaxChunk;
+    const int64_t i1 = i0 + kArgmaxChunk < vocab ? i0 + kArgmaxChunk : vocab;
+    unsigned long long b = 0;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
         const unsigned long long packed = ((unsigned long long)total_key(row[i]) << 32) | (unsigned long long)i;
-        best = packed > best ? packed : best;
+        b = packed > b ? packed : b;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+        b = other > b ? other : b;
     }
-    if ((threadIdx.x & 31) == 0) best_s[threadIdx.x >> 5] = best;
+    if ((threadIdx.x & 31) == 0) best_s[threadIdx.x >> 5] = b;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int i = 1; i < (int)(blockDim.x >> 5); i++) best = best_s[i] > best ? best_s[i] : best;
-        out[blockIdx.x] = (int32_t)(best & 0xFFFFFFFFull);
+        for (int i = 1; i < (int)(blockDim.x >> 5); i++) b = best_s[i] > b ? best_s[i] : b;
+        atomicMax(best + s, b);
     }
 }
 
@@ -254,8 +302,11 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 // split each task's rows in pieces of rows_per_item; unused item slots get
 // task -1 (the kernel returns at once for them).
 __global__ void e2b_plan_kernel(E2bPlanArgs a) {
+    ptx::pdl_trigger();  // a dependent may launch; it waits for this grid itself
+    ptx::pdl_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     const int n_tasks = a.n_layers * a.n;
+    if (t < a.n) a.best[t] = 0;
     if (t < n_tasks) {
         const int l = t / a.n, i = t % a.n;
         const E2bLayerDesc &ld = a.layers[l];
@@ -320,36 +371,35 @@ cudaError_t e2b_synth_norm(float *dst, int64_t n, uint64_t seed, uint64_t tensor
     return cudaGetLastError();
 }
 
-cudaError_t e2b_embed(const uint8_t *table, int d, const int32_t *tokens, int n, float scale, float *x, cudaStream_t st) {
-    embed_kernel<<<n, kRowThreads, 0, st>>>(table, d, tokens, scale, x);
-    return cudaGetLastError();
+cudaError_t e2b_embed(const uint8_t *table, int d, const int32_t *tokens, int n, float scale, float *x, cudaStream_t st,
+                      bool pdl) {
+    return launch_k(pdl, embed_kernel, dim3(n), dim3(kRowThreads), 0, st, table, d, tokens, scale, x);
 }
 
 cudaError_t e2b_ple_inputs(const float *P, const uint8_t *table, const int32_t *tokens, const float *w, int L, int ple,
-                           float ps, float ts, float is, float eps, float *out, int n, cudaStream_t st) {
+                           float ps, float ts, float is, float eps, float *out, int n, cudaStream_t st, bool pdl) {
     if (ple > 1024) return cudaErrorInvalidValue;
-    ple_inputs_kernel<<<n * L, kRowThreads, 0, st>>>(P, table, tokens, w, L, ple, ps, ts, is, eps, out);
-    return cudaGetLastError();
+    return launch_k(pdl, ple_inputs_kernel, dim3(n * L), dim3(kRowThreads), 0, st, P, table, tokens, w, L, ple, ps, ts,
+                    is, eps, out);
 }
 
 cudaError_t e2b_resid(float *x, const float *y, const float *w_post, float post, const float *w_next, int d, float eps,
-                      int8_t *xq, float *xs, int n, cudaStream_t st) {
+                      int8_t *xq, float *xs, int n, cudaStream_t st, bool pdl) {
     if (d > kMaxRow || d % kQ8Block) return cudaErrorInvalidValue;
     ResidArgs a{x, y, w_post, w_next, xq, xs, d, eps, post};
-    resid_kernel<<<n, kRowThreads, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_k(pdl, resid_kernel, dim3(n), dim3((d / 4 + 31) / 32 * 32), 0, st, a);
 }
 
 cudaError_t e2b_gelu_quant(const float *gate, const float *pli, int layer, int L, int ple, int8_t *xq, float *xs, int n,
-                           cudaStream_t st) {
-    if (ple > 1024 || ple % kQ8Block) return cudaErrorInvalidValue;
-    gelu_quant_kernel<<<n, kRowThreads, 0, st>>>(gate, pli, layer, L, ple, xq, xs);
-    return cudaGetLastError();
+                           cudaStream_t st, bool pdl) {
+    if (ple > 1024 || ple % 128) return cudaErrorInvalidValue;  // whole warps of float4s
+    return launch_k(pdl, gelu_quant_kernel, dim3(n), dim3(ple / 4), 0, st, gate, pli, layer, L, ple, xq, xs);
 }
 
-cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, int32_t *out, cudaStream_t st) {
-    argmax_kernel<<<n, 1024, 0, st>>>(logits, vocab, out);
-    return cudaGetLastError();
+cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, unsigned long long *best, cudaStream_t st,
+                       bool pdl) {
+    const dim3 grid((unsigned)((vocab + kArgmaxChunk - 1) / kArgmaxChunk), (unsigned)n);
+    return launch_k(pdl, argmax_kernel, grid, dim3(256), 0, st, logits, vocab, best);
 }
 
 cudaError_t e2b_plan(const E2bPlanArgs &a, cudaStream_t st) {

@@ -8,6 +8,27 @@
 
 namespace g4a {
 
+// Launches `kernel`, with programmatic stream serialization when `pdl` is set:
+// the kernel may then start while its predecessor on the stream is still
+// running, so it must call ptx::pdl_wait() before it touches any memory a
+// predecessor writes or reads (only constant inputs such as weights may be
+// read before). Every kernel of the decoder step follows that rule.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? attr : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Query heads per KV head served by the fused E2B kernels (idea/mod.rs:53-54:
 // 8 query heads, 1 KV head).
 constexpr int kHeads = 8;
@@ -60,7 +81,8 @@ struct DecodeParams {
     const int32_t *cta_start;    // f16 kernel: CTA b runs items [cta_start[b], cta_start[b+1])
     void *q_blocks;              // f16 kernel: [tasks][kQBlockBytes] q hi/lo blocks
     const int32_t *split_tasks;  // f16 kernel: tasks whose items are merged by the combine kernel
-    int32_t max_rows;            // exact kernel: the most rows a task attends (scores in shared memory)
+    int32_t max_rows;            // exact kernels: the most rows a task attends
+    float *scores;               // exact kernels: [tasks][kHeads][max_rows]
 };
 
 // Bulk append of already processed rows, or norm+RoPE of raw rows.
@@ -83,11 +105,13 @@ struct ViewParams {
 
 // Launchers (decode.cu).
 cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, cudaStream_t s);
-// f32 caches, one CTA per task (items never split a task): the reference's
-// own order of operations and glibc's expf, so the output is the reference's
-// bit for bit. Up to kExactMaxRows rows per task.
+// f32 caches in the reference's own order of operations with glibc's expf,
+// so the output is the reference's bit for bit: items are (task, chunk of
+// kExactRowsPerItem rows) for the scores launch; tasks 0..n_tasks-1 then get
+// one CTA per (head, 128 columns). Up to kExactMaxRows rows per task.
 constexpr int kExactMaxRows = 4096;
-cudaError_t launch_decode_exact(const DecodeParams &p, int hd, cudaStream_t s);
+constexpr int kExactRowsPerItem = 32;
+cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl = false);
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
 constexpr size_t kQBlockBytes = 16 * 512 * 2;  // q hi/lo block of one task (f16 kernel)
@@ -105,12 +129,26 @@ cudaError_t launch_lse_merge(int n_parts, const float *const *parts_o, const flo
 // 2D TMA descriptor (128 B) over a row-major [rows][cols] 16-bit tensor with
 // 64 x box_rows boxes and the 128-byte swizzle. dtype: 0 bf16, 1 f16.
 bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows);
+// 2D descriptor over [outer][inner] elements of 1 (u8), 2 (u16) or 4 (f32)
+// bytes, rows row_bytes apart; boxes box_inner x box_outer; optional 128-byte
+// swizzle (box_inner * elem_bytes must then be 128).
+bool encode_tmap_2d_raw(void *map, int elem_bytes, const void *base, uint64_t inner, uint64_t outer,
+                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+// Batched Q8_0 mat-vec (q8_0_gemm_sm100.cu) over pre-quantized activations
+// xq [n_vec][cols] int8, xs [n_vec][cols/32] f32; kind as q8_run. Needs cols
+// a multiple of 256 and 16-byte aligned pointers; returns false when the
+// shape does not fit (the caller falls back).
+bool q8_gemm_fits(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const int8_t *xq,
+                  const float *xs);
+cudaError_t q8_gemm_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const int8_t *xq,
+                        const float *xs, int32_t n_vec, float cap, float *out, int *d_err, cudaStream_t st, bool pdl);
 
 // Prefill (prefill_sm100.cu): per-context scratch and the launcher behind
 // g4a_prefill. Returns a g4a_status and points *msg at a description.
 // Q8_0 mat-vec family (q8_0_sm100.cu); kind 0 plain, 1 GEGLU (w2 = up), 2 soft-cap.
 int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
-           float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg);
+           float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg,
+           bool pdl = false);
 
 // E2B decoder step (e2b_sm100.cu).
 // One layer of the model as the attention planner sees it; the caches are
@@ -129,18 +167,21 @@ struct E2bPlanArgs {
     float *att;
     DecodeTask *tasks;  // [n_layers][task_stride]
     DecodeItem *items_local, *items_global;
+    unsigned long long *best;  // [n] argmax slots, zeroed here
 };
 cudaError_t e2b_synth_q8(void *dst, int64_t n_blocks, uint64_t seed, uint64_t tensor, float sigma, cudaStream_t st);
 cudaError_t e2b_synth_norm(float *dst, int64_t n, uint64_t seed, uint64_t tensor, float center, float spread,
                            cudaStream_t st);
-cudaError_t e2b_embed(const uint8_t *table, int d, const int32_t *tokens, int n, float scale, float *x, cudaStream_t st);
+cudaError_t e2b_embed(const uint8_t *table, int d, const int32_t *tokens, int n, float scale, float *x, cudaStream_t st,
+                      bool pdl = false);
 cudaError_t e2b_ple_inputs(const float *P, const uint8_t *table, const int32_t *tokens, const float *w, int L, int ple,
-                           float ps, float ts, float is, float eps, float *out, int n, cudaStream_t st);
+                           float ps, float ts, float is, float eps, float *out, int n, cudaStream_t st, bool pdl = false);
 cudaError_t e2b_resid(float *x, const float *y, const float *w_post, float post, const float *w_next, int d, float eps,
-                      int8_t *xq, float *xs, int n, cudaStream_t st);
+                      int8_t *xq, float *xs, int n, cudaStream_t st, bool pdl = false);
 cudaError_t e2b_gelu_quant(const float *gate, const float *pli, int layer, int L, int ple, int8_t *xq, float *xs, int n,
-                           cudaStream_t st);
-cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, int32_t *out, cudaStream_t st);
+                           cudaStream_t st, bool pdl = false);
+cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, unsigned long long *best, cudaStream_t st,
+                       bool pdl = false);
 cudaError_t e2b_plan(const E2bPlanArgs &a, cudaStream_t st);
 
 struct PrefillScratch;

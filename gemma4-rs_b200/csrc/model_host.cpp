@@ -41,8 +41,9 @@ struct g4a_model {
     cudaEvent_t ev = nullptr;
     std::vector<void *> allocs;
     int32_t *d_in = nullptr;  // [3][S]: sequence ids, tokens, positions
-    int32_t *d_next = nullptr;
-    int32_t *h_in = nullptr, *h_out = nullptr;  // pinned: [3][S] and [S + 1] (tokens, error flags)
+    int32_t *h_in = nullptr;              // pinned [3][S]
+    unsigned long long *h_out = nullptr;  // pinned [S]: the argmax slots (index in the low 32 bits)
+    int32_t *h_err = nullptr;             // pinned: the device error flags after the step
     float *x = nullptr, *y = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
     float *gate = nullptr, *gated = nullptr, *P = nullptr, *pli = nullptr, *logits = nullptr;
     int8_t *xq = nullptr;
@@ -50,11 +51,13 @@ struct g4a_model {
     E2bLayerDesc *d_layers = nullptr;
     DecodeTask *d_tasks = nullptr;
     DecodeItem *d_items_local = nullptr, *d_items_global = nullptr;
-    float *part_o = nullptr, *part_ml = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr, *scores = nullptr;
     unsigned *tickets = nullptr;
+    unsigned long long *d_best = nullptr;  // [S] packed (total-order key, index) of each row's argmax
     std::map<int32_t, cudaGraphExec_t> graphs;
     std::map<int32_t, int> eager_runs;
     bool use_graphs = true;  // G4A_NO_GRAPH=1 in the environment: every step eager
+    bool pdl = true;         // programmatic dependent launch along the step (G4A_NO_PDL=1: off)
     std::vector<float *> k_cache, v_cache;  // per layer: its KV source's caches
     int32_t last_n = 0;
 };
@@ -96,7 +99,7 @@ int mv(g4a_model *m, int kind, const uint8_t *w, const uint8_t *w2, int64_t rows
        float cap, float *out) {
     const char *msg = "";
     const int rc = q8_run(kind, w, w2, rows, cols, x, n, cap, out, m->xq, m->xs, m->ctx->d_err, m->ctx->n_sm, m->st,
-                          &msg);
+                          &msg, m->pdl);
     return rc == G4A_OK ? G4A_OK : fail(m->ctx, rc, "compute: %s", msg);
 }
 
@@ -133,17 +136,18 @@ int enqueue_step(g4a_model *m, int32_t n) {
     pa.tasks = m->d_tasks;
     pa.items_local = m->d_items_local;
     pa.items_global = m->d_items_global;
+    pa.best = m->d_best;
     MODEL_TRY(e2b_plan(pa, m->st));
 
     // embed (model.rs:376-384) and per-layer inputs (:252-270)
-    MODEL_TRY(e2b_embed(w.token_embd, d, d_tok, n, std::sqrt((float)d), m->x, m->st));
+    MODEL_TRY(e2b_embed(w.token_embd, d, d_tok, n, std::sqrt((float)d), m->x, m->st, m->pdl));
     int rc;
     if (ple > 0) {
         if ((rc = mv(m, 0, w.ple_model_proj, nullptr, (int64_t)L * ple, d, m->x, n, 0.0f, m->P))) return rc;
         MODEL_TRY(e2b_ple_inputs(m->P, w.ple_token_embd, d_tok, w.ple_proj_norm, L, ple, 1.0f / std::sqrt((float)d),
-                                 std::sqrt((float)ple), 1.0f / std::sqrt(2.0f), eps, m->pli, n, m->st));
+                                 std::sqrt((float)ple), 1.0f / std::sqrt(2.0f), eps, m->pli, n, m->st, m->pdl));
     }
-    MODEL_TRY(e2b_resid(m->x, nullptr, nullptr, 1.0f, w.layers[0].attn_norm, d, eps, m->xq, m->xs, n, m->st));
+    MODEL_TRY(e2b_resid(m->x, nullptr, nullptr, 1.0f, w.layers[0].attn_norm, d, eps, m->xq, m->xs, n, m->st, m->pdl));
 
     for (int l = 0; l < L; l++) {
         const g4a_layer_weights &lw = w.layers[l];
@@ -170,34 +174,36 @@ int enqueue_step(g4a_model *m, int32_t n) {
         p.err_flag = ctx->d_err;
         p.n_items = n * (m->global[l] ? m->ms_global : m->ms_local);
         if (m->exact) {
-            p.max_rows = m->global[l] ? m->T : std::min(ctx->hp.sliding_window, m->T);
-            MODEL_TRY(launch_decode_exact(p, hd, m->st));
+            p.max_rows = m->T;
+            p.scores = m->scores;
+            MODEL_TRY(launch_decode_exact(p, hd, n, m->st, m->pdl));
         } else {
             MODEL_TRY(launch_decode(p, hd, 0, true, m->st));
         }
         // output projection, post-attention norm, residual, FFN norm (:411-415)
         if ((rc = mv(m, 0, lw.attn_output, nullptr, d, qd, m->att, n, 0.0f, m->y))) return rc;
-        MODEL_TRY(e2b_resid(m->x, m->y, lw.post_attention_norm, 1.0f, lw.ffn_norm, d, eps, m->xq, m->xs, n, m->st));
+        MODEL_TRY(e2b_resid(m->x, m->y, lw.post_attention_norm, 1.0f, lw.ffn_norm, d, eps, m->xq, m->xs, n, m->st,
+                            m->pdl));
         // GEGLU, down projection, post-FFN norm, residual (:416-420)
         if ((rc = mv(m, 1, lw.ffn_gate, lw.ffn_up, m->d_ff, d, nullptr, n, 0.0f, m->gated))) return rc;
         if ((rc = mv(m, 0, lw.ffn_down, nullptr, d, m->d_ff, m->gated, n, 0.0f, m->y))) return rc;
         const float *next_norm = l + 1 < L ? w.layers[l + 1].attn_norm : w.output_norm;
         if (ple > 0) {
             // per-layer embedding (:422-432), then layer_output_scale (:433-435)
-            MODEL_TRY(e2b_resid(m->x, m->y, lw.post_ffw_norm, 1.0f, nullptr, d, eps, m->xq, m->xs, n, m->st));
+            MODEL_TRY(e2b_resid(m->x, m->y, lw.post_ffw_norm, 1.0f, nullptr, d, eps, m->xq, m->xs, n, m->st, m->pdl));
             if ((rc = mv(m, 0, lw.inp_gate, nullptr, ple, d, nullptr, n, 0.0f, m->gate))) return rc;
-            MODEL_TRY(e2b_gelu_quant(m->gate, m->pli, l, L, ple, m->xq, m->xs, n, m->st));
+            MODEL_TRY(e2b_gelu_quant(m->gate, m->pli, l, L, ple, m->xq, m->xs, n, m->st, m->pdl));
             if ((rc = mv(m, 0, lw.proj, nullptr, d, ple, nullptr, n, 0.0f, m->y))) return rc;
             MODEL_TRY(e2b_resid(m->x, m->y, lw.post_norm, lw.layer_output_scale, next_norm, d, eps, m->xq, m->xs, n,
-                                m->st));
+                                m->st, m->pdl));
         } else {
             MODEL_TRY(e2b_resid(m->x, m->y, lw.post_ffw_norm, lw.layer_output_scale, next_norm, d, eps, m->xq, m->xs,
-                                n, m->st));
+                                n, m->st, m->pdl));
         }
     }
     // logits (:438-449) and greedy sampling (sample.rs:27-36)
     if ((rc = mv(m, 2, w.token_embd, nullptr, m->vocab, d, nullptr, n, w.final_logit_softcap, m->logits))) return rc;
-    MODEL_TRY(e2b_argmax(m->logits, m->vocab, n, m->d_next, m->st));
+    MODEL_TRY(e2b_argmax(m->logits, m->vocab, n, m->d_best, m->st, m->pdl));
     return G4A_OK;
 }
 
@@ -206,8 +212,9 @@ int record_step(g4a_model *m, int32_t n) {
     MODEL_TRY(cudaMemcpyAsync(m->d_in, m->h_in, 3 * (size_t)m->S * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
     const int rc = enqueue_step(m, n);
     if (rc) return rc;
-    MODEL_TRY(cudaMemcpyAsync(m->h_out, m->d_next, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
-    MODEL_TRY(cudaMemcpyAsync(m->h_out + m->S, m->ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    MODEL_TRY(cudaMemcpyAsync(m->h_out, m->d_best, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                              m->st));
+    MODEL_TRY(cudaMemcpyAsync(m->h_err, m->ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
     return G4A_OK;
 }
 
@@ -264,6 +271,7 @@ extern "C" void g4a_model_destroy(g4a_model *m) {
     for (void *p : m->allocs) cudaFree(p);
     if (m->h_in) cudaFreeHost(m->h_in);
     if (m->h_out) cudaFreeHost(m->h_out);
+    if (m->h_err) cudaFreeHost(m->h_err);
     if (m->ev) cudaEventDestroy(m->ev);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
@@ -333,7 +341,7 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
     // order of operations (bit-exact logits); longer caches split tasks
     // across CTAs (split-KV, within the decode tolerance).
     m->exact = max_tokens <= kExactMaxRows;
-    if (m->exact) m->rows_per_item = max_tokens;
+    if (m->exact) m->rows_per_item = kExactRowsPerItem;
     const int32_t R = m->rows_per_item;
     m->ms_local = (std::min(hp.sliding_window, max_tokens) + R - 1) / R;
     m->ms_global = (max_tokens + R - 1) / R;
@@ -344,10 +352,11 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
               cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming) == cudaSuccess &&
               cudaHostAlloc(reinterpret_cast<void **>(&m->h_in), 3 * S * sizeof(int32_t), cudaHostAllocDefault) ==
                   cudaSuccess &&
-              cudaHostAlloc(reinterpret_cast<void **>(&m->h_out), (S + 1) * sizeof(int32_t), cudaHostAllocDefault) ==
-                  cudaSuccess;
+              cudaHostAlloc(reinterpret_cast<void **>(&m->h_out), S * sizeof(unsigned long long),
+                            cudaHostAllocDefault) == cudaSuccess &&
+              cudaHostAlloc(reinterpret_cast<void **>(&m->h_err), sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
     if (ok) {
-        ok = (m->d_in = dalloc<int32_t>(m, 3 * S)) && (m->d_next = dalloc<int32_t>(m, S)) &&
+        ok = (m->d_in = dalloc<int32_t>(m, 3 * S)) &&
              (m->x = dalloc<float>(m, S * m->d)) && (m->y = dalloc<float>(m, S * m->d)) &&
              (m->q = dalloc<float>(m, S * m->qd_max)) && (m->att = dalloc<float>(m, S * m->qd_max)) &&
              (m->k = dalloc<float>(m, S * m->hd_max)) && (m->v = dalloc<float>(m, S * m->hd_max)) &&
@@ -360,7 +369,9 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
              (m->d_items_local = dalloc<DecodeItem>(m, S * m->ms_local)) &&
              (m->d_items_global = dalloc<DecodeItem>(m, S * m->ms_global)) &&
              (m->part_o = dalloc<float>(m, S * ms * kHeads * m->hd_max)) &&
-             (m->part_ml = dalloc<float>(m, S * ms * 2 * kHeads)) && (m->tickets = dalloc<unsigned>(m, S));
+             (m->part_ml = dalloc<float>(m, S * ms * 2 * kHeads)) && (m->tickets = dalloc<unsigned>(m, S)) &&
+             (m->scores = dalloc<float>(m, m->exact ? S * kHeads * max_tokens : 1)) &&
+             (m->d_best = dalloc<unsigned long long>(m, S));
     }
     // K/V caches of the owner layers: [max_seqs][max_tokens][hd] f32 each
     std::vector<E2bLayerDesc> desc(m->L);
@@ -376,6 +387,8 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
     }
     const char *no_graph = std::getenv("G4A_NO_GRAPH");
     m->use_graphs = !(no_graph && no_graph[0] == '1');
+    const char *no_pdl = std::getenv("G4A_NO_PDL");
+    m->pdl = !(no_pdl && no_pdl[0] == '1');
     m->k_cache.resize(m->L);
     m->v_cache.resize(m->L);
     for (int l = 0; l < m->L; l++) {
@@ -443,14 +456,15 @@ extern "C" int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids, c
     }
     G4A_CUDA_TRY(ctx, cudaStreamSynchronize(m->st));
     m->last_n = n;
-    const int32_t flags = m->h_out[m->S];
+    const int32_t flags = *m->h_err;
     if (flags) {
         cudaMemset(ctx->d_err, 0, sizeof(int));
         if (flags & 1) return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
         return fail(ctx, G4A_TIMEOUT, "compute: a device wait timed out (flags %d)", flags);
     }
     for (int i = 0; i < n; i++) m->len[seq_ids[i]]++;
-    if (next) std::memcpy(next, m->h_out, (size_t)n * sizeof(int32_t));
+    if (next)
+        for (int i = 0; i < n; i++) next[i] = (int32_t)(m->h_out[i] & 0xFFFFFFFFull);
     return G4A_OK;
 }
 

@@ -635,6 +635,22 @@ bool encode_tmap_2d(void *map, int dtype, const void *base, uint64_t cols, uint6
     return r == CUDA_SUCCESS;
 }
 
+bool encode_tmap_2d_raw(void *map, int elem_bytes, const void *base, uint64_t inner, uint64_t outer,
+                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const CUtensorMapDataType dt = elem_bytes == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(reinterpret_cast<CUtensorMap *>(map), dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Output map: f32 [rows, cols], 32-column x 128-row boxes, 128-byte swizzle.
 static bool encode_out_f32(CUtensorMap *map, const float *base, uint64_t cols, uint64_t rows) {
     EncodeTiledFn enc = encode_fn();

@@ -65,6 +65,8 @@ __device__ __forceinline__ float softcap(float v, float cap) {
 // One warp per block of 32 values: matvec.rs:36-54.
 __global__ void __launch_bounds__(256) q8_quantize_kernel(const float *__restrict__ x, int64_t n_blocks,
                                                           float *__restrict__ scales, int8_t *__restrict__ quants) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
     const int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= n_blocks) return;  // whole warps exit together
@@ -85,6 +87,7 @@ struct Q8Params {
     const uint8_t *w2;     // second matrix (GEGLU up), same shape
     const int8_t *xq;      // [n_vec][cols] activation quants
     const float *xs;       // [n_vec][cols / 32] activation scales
+    const float *xf;       // [n_vec][cols] f32 activations quantized in the prologue (then xq/xs unused)
     float *out;            // [n_vec][rows]
     int64_t rows;
     int32_t cols, row_len, n_vec, tile_rows, n_tiles, kind;
@@ -182,13 +185,12 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
         }
         ptx::fence_mbar_init();
     }
-    // activation quants (padded to 36 bytes per block) and scales, once per CTA
-    for (int i = threadIdx.x; i < p.n_vec * p.cols / 4; i += blockDim.x) {
-        const int blk = i >> 3, k = i & 7;  // word k of block blk (over all vectors)
-        reinterpret_cast<uint32_t *>(xq_s)[blk * (kXqStride / 4) + k] = reinterpret_cast<const uint32_t *>(p.xq)[i];
-    }
-    for (int i = threadIdx.x; i < p.n_vec * nb; i += blockDim.x) xs_s[i] = p.xs[i];
     __syncthreads();
+    // The weights are constant: the producer starts streaming them at once,
+    // even before the grid this one depends on has finished. Everything that
+    // reads or writes the activations and outputs waits for it (the compute
+    // warps below; the sum warp only after them).
+    ptx::pdl_trigger();
 
     const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     auto rows_of = [&](int k, int64_t *r0) {
@@ -254,6 +256,43 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
         }
     } else {
         // ---------------------------------------------------------------- block dot products
+        ptx::pdl_wait();
+        if (p.xf) {
+            // matvec.rs:36-54 on the f32 inputs, a float4 per thread: the 8
+            // consecutive lanes of a block of 32 share its maximum
+            const int total = p.n_vec * p.cols / 4;
+            for (int base = warp * 32; base < total; base += kConsumers) {
+                const int e = base + lane;
+                const bool in = e < total;  // whole groups of 8 (cols a multiple of 32)
+                const float4 v = in ? __ldg(reinterpret_cast<const float4 *>(p.xf) + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+                const float scale = __fdiv_rn(m, 127.0f);
+                const float inverse = scale == 0.0f ? 0.0f : __fdiv_rn(1.0f, scale);
+                auto q = [&](float x) {
+                    float r = rintf(__fmul_rn(x, inverse));
+                    r = r != r ? 0.0f : fminf(fmaxf(r, -128.0f), 127.0f);
+                    return (uint32_t)(uint8_t)(int8_t)(int)r;
+                };
+                if (in) {
+                    const int blk = e >> 3, k = e & 7;
+                    reinterpret_cast<uint32_t *>(xq_s)[blk * (kXqStride / 4) + k] =
+                        q(v.x) | (q(v.y) << 8) | (q(v.z) << 16) | (q(v.w) << 24);
+                    if (k == 0) xs_s[blk] = __half2float(__float2half_rn(scale));
+                }
+            }
+        } else {
+            // activation quants (padded to 48 bytes per block) and scales, once per CTA
+            for (int i = threadIdx.x; i < p.n_vec * p.cols / 4; i += kConsumers) {
+                const int blk = i >> 3, k = i & 7;  // word k of block blk (over all vectors)
+                reinterpret_cast<uint32_t *>(xq_s)[blk * (kXqStride / 4) + k] =
+                    reinterpret_cast<const uint32_t *>(p.xq)[i];
+            }
+            for (int i = threadIdx.x; i < p.n_vec * nb; i += kConsumers) xs_s[i] = p.xs[i];
+        }
+        ptx::named_bar_sync(1, kConsumers);
         const int step_r = kConsumers / nb, step_b = kConsumers - (kConsumers / nb) * nb;  // 256 = step_r*nb + step_b
         // One vector and at most 256 blocks per row: thread t owns block column
         // t % nb for the whole call (its activation quants and scale live in
@@ -331,6 +370,8 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
 // 256): one warp per (vector, row), blocks read byte-wise from global memory,
 // lane 0 adds the block values in order.
 __global__ void __launch_bounds__(256) q8_matvec_generic_kernel(Q8Params p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (gw >= p.rows * p.n_vec) return;
@@ -375,20 +416,42 @@ __global__ void __launch_bounds__(256) q8_matvec_generic_kernel(Q8Params p) {
 // activations (several projections of one input). Returns a g4a_status;
 // *msg names a failure.
 int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
-           float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg) {
+           float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg,
+           bool pdl) {
     *msg = "";
     const int64_t nb = cols / kQ8Block;
     const int64_t n_blocks = nb * n_vec;
-    if (x && n_blocks > 0) {
-        const int64_t threads = n_blocks * 32;
-        q8_quantize_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, n_blocks, xs, xq);
-    }
-    if (rows == 0) return cudaGetLastError() == cudaSuccess ? G4A_OK : G4A_CUDA;
     const int n_mat = kind == KIND_GEGLU ? 2 : 1;
     const int64_t row_len = nb * kQ8BlockBytes;
-    const bool aligned = ((uintptr_t)w % 16 == 0) && (!w2 || (uintptr_t)w2 % 16 == 0);
-    const bool fast = aligned && row_len % 16 == 0 && row_len * n_mat <= kStageTarget &&
+    const bool aligned = ((uintptr_t)w % 16 == 0) && (!w2 || (uintptr_t)w2 % 16 == 0) && ((uintptr_t)x % 16 == 0);
+    const bool fast = rows > 0 && aligned && row_len % 16 == 0 && row_len * n_mat <= kStageTarget &&
                       Q8Layout(n_mat, 1, (int)cols, 1).total <= 227 * 1024;
+    // One pass of the streaming kernel quantizes its own inputs; otherwise
+    // (several passes, the generic kernel, or quantization alone) a separate
+    // kernel fills xq/xs first.
+    // Many vectors: the tensor-core kernel over quantized activations.
+    const bool gemm = n_vec > kMaxVec && rows > 0 && q8_gemm_fits(kind, w, w2, rows, cols, xq, xs);
+    const bool fused_quant = !gemm && x && fast && n_vec <= kMaxVec &&
+                             Q8Layout(n_mat, n_vec, (int)cols, (int)std::max<int64_t>(1, std::min<int64_t>(
+                                 32, kStageTarget / (row_len * n_mat)))).total <= 227 * 1024;
+    if (x && n_blocks > 0 && !fused_quant) {
+        const int64_t threads = n_blocks * 32;
+        const cudaError_t e = launch_k(pdl, q8_quantize_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0,
+                                       st, x, n_blocks, xs, xq);
+        if (e != cudaSuccess) {
+            *msg = cudaGetErrorString(e);
+            return G4A_CUDA;
+        }
+    }
+    if (rows == 0) return cudaGetLastError() == cudaSuccess ? G4A_OK : G4A_CUDA;
+    if (gemm) {
+        const cudaError_t e = q8_gemm_run(kind, w, w2, rows, cols, xq, xs, n_vec, cap, out, d_err, st, pdl);
+        if (e != cudaSuccess) {
+            *msg = cudaGetErrorString(e);
+            return G4A_CUDA;
+        }
+        return G4A_OK;
+    }
     Q8Params p{};
     p.w = w;
     p.w2 = w2;
@@ -404,7 +467,12 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
         p.out = out;
         p.n_vec = n_vec;
         const int64_t threads = rows * n_vec * 32;
-        q8_matvec_generic_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(p);
+        const cudaError_t e = launch_k(pdl, q8_matvec_generic_kernel, dim3((unsigned)((threads + 255) / 256)),
+                                       dim3(256), 0, st, p);
+        if (e != cudaSuccess) {
+            *msg = cudaGetErrorString(e);
+            return G4A_CUDA;
+        }
     } else {
         static bool attr_set = false;  // per process; the attribute is per function
         if (!attr_set) {
@@ -430,6 +498,7 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
             p.n_vec = g;
             p.xq = xq + (size_t)v0 * cols;
             p.xs = xs + (size_t)v0 * nb;
+            p.xf = fused_quant ? x + (size_t)v0 * cols : nullptr;
             p.out = out + (size_t)v0 * rows;
             // as many resident CTAs per SM as shared memory allows (up to 4):
             // more warps hide the shared-memory latency of the block dots
@@ -439,7 +508,11 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
                 per_sm < 1)
                 per_sm = 1;
             const int grid = (int)std::min<int64_t>(n_tiles, (int64_t)std::max(1, n_sm) * std::min(per_sm, 4));
-            q8_matvec_kernel<<<grid, kThreadsQ8, smem, st>>>(p);
+            const cudaError_t e = launch_k(pdl, q8_matvec_kernel, dim3(grid), dim3(kThreadsQ8), smem, st, p);
+            if (e != cudaSuccess) {
+                *msg = cudaGetErrorString(e);
+                return G4A_CUDA;
+            }
             v0 += g;
         }
     }

@@ -69,6 +69,9 @@ def test_quantize_bit_exact(oracle, ctx, torch_cuda):
     (257, 512, 9),     # more vectors than one pass holds
     (33, 96, 2),       # cols not a multiple of 256: the generic kernel
     (0, 256, 1),       # no rows
+    (1000, 1536, 100), # many vectors: the tensor-core kernel, ragged row and vector tiles
+    (64, 256, 64),     # one stage of K, whole tiles
+    (200, 3072, 17),   # d_ff-wide rows
 ])
 def test_matvec_bit_exact(oracle, ctx, torch_cuda, rows, cols, n_vec):
     torch = torch_cuda
@@ -112,7 +115,7 @@ def close(got, want):
     return np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("rows,cols,n_vec", [(300, 256, 1), (1000, 1536, 2), (50, 96, 1)])
+@pytest.mark.parametrize("rows,cols,n_vec", [(300, 256, 1), (1000, 1536, 2), (50, 96, 1), (333, 1536, 70)])
 def test_geglu(oracle, ctx, torch_cuda, rows, cols, n_vec):
     torch = torch_cuda
     gate, up = weights(oracle, 7, rows, cols), weights(oracle, 8, rows, cols)
@@ -131,6 +134,18 @@ def test_softcap_logits(oracle, ctx, torch_cuda):
     x = rng(11).standard_normal((1, cols)).astype(np.float32)
     out = torch.empty(1, rows, device="cuda")
     ctx.matvec_q8_0_softcap(dev(torch, w), rows, cols, dev(torch, x), 30.0, out)
+    ctx.sync()
+    assert close(out.cpu().numpy(), oracle_rows(oracle, oracle.matvec_q8_0_softcap, (w,), rows, cols, x, 30.0))
+
+
+def test_softcap_logits_batched(oracle, ctx, torch_cuda):
+    """The head over many sequences at once (the batched decoder's form)."""
+    torch = torch_cuda
+    rows, cols, n_vec = 777, 1536, 40
+    w = weights(oracle, 12, rows, cols, scale=0.5)
+    x = rng(13).standard_normal((n_vec, cols)).astype(np.float32)
+    out = torch.empty(n_vec, rows, device="cuda")
+    ctx.matvec_q8_0_softcap(dev(torch, w), rows, cols, dev(torch, x), 30.0, out, n_vec=n_vec)
     ctx.sync()
     assert close(out.cpu().numpy(), oracle_rows(oracle, oracle.matvec_q8_0_softcap, (w,), rows, cols, x, 30.0))
 
