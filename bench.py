@@ -593,7 +593,8 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     "decode-batch1" for configuration 0's latency, "q8-head[:rows]" for
     the Q8_0 output-head mat-vec (262,144 rows unless given), or
     "decoder[:b1,b2,...[:new_tokens]]" for configuration 4's decoder at
-    those batch sizes (a short run when new_tokens is given)."""
+    those batch sizes (a short run when new_tokens is given), or
+    "q8-gemm:rows:cols:n_vec[:geglu]" for the batched Q8_0 kernel alone."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
     if spec.startswith("decoder"):
         parts = spec.split(":")
@@ -602,6 +603,38 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
         res = measure_decoder(torch, g4a, ctx, batches=batches, new_tokens=new_tokens)
         ctx.close()
         print(json.dumps({"case": spec, **res}), flush=True)
+        return
+    if spec.startswith("q8-gemm"):
+        # q8-gemm:rows:cols:n_vec[:geglu] -- the batched Q8_0 kernel alone
+        parts = spec.split(":")
+        rows, cols, n_vec = int(parts[1]), int(parts[2]), int(parts[3])
+        geglu = len(parts) > 4 and parts[4] == "geglu"
+        w = q8_head_weights(torch, rows, cols)
+        w2 = q8_head_weights(torch, rows, cols, seed=2) if geglu else None
+        x = torch.sin(torch.arange(n_vec * cols, dtype=torch.float32, device="cuda") * 0.37).view(n_vec, cols)
+        out = torch.empty(n_vec, rows, device="cuda")
+        stream = torch.cuda.Stream()
+        ctx.set_stream(stream.cuda_stream)
+        call = (lambda: ctx.geglu_q8_0(w, w2, rows, cols, x, out, n_vec=n_vec)) if geglu else \
+            (lambda: ctx.matvec_q8_0(w, rows, cols, x, out, n_vec=n_vec))
+        with torch.cuda.stream(stream):
+            for _ in range(max(warmup, 1)):
+                call()
+            ts = []
+            for _ in range(max(reps, 1)):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                call()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+        ctx.sync()
+        ctx.close()
+        ms = statistics.median(ts)
+        block_dots = rows * (cols // 32) * n_vec * (2 if geglu else 1)
+        print(json.dumps({"case": spec, "ms": round(ms, 4), "block_dots_per_s": round(block_dots / ms * 1e3, 1),
+                          "weight_GB_s": round(rows * cols // 32 * 34 * (2 if geglu else 1) / ms / 1e6, 1),
+                          "timing": "CUDA events, median, activation quantization included"}), flush=True)
         return
     if spec == "decode-batch1":
         stream = torch.cuda.Stream()
