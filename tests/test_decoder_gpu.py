@@ -142,6 +142,28 @@ def test_steps_match_oracle(ctx, small_vocab, oracle):
     m.close()
 
 
+def test_batched_steps_match_oracle(ctx, small_vocab, oracle):
+    """Twelve sequences per step: the batched path (tensor-core Q8_0 GEMMs,
+    separate residual kernels), bit-identical to the oracle too."""
+    import g4attn.model as gm
+    w, make = small_vocab
+    n = 12
+    m = gm.Model(ctx, w, max_seqs=n, max_tokens=32)
+    decs = [make() for _ in range(n)]
+    toks = rng(15).integers(0, w.vocab, (n, 6))
+    stats = {"max_diff": 0.0, "bit_identical": 0, "top1_agree": 0, "steps": 0}
+    cur = [int(t) for t in toks[:, 0]]
+    for p in range(8):
+        nxt = m.step(list(range(n)), cur)
+        logits = m.logits().cpu().numpy()
+        for i in range(n):
+            compare_step(logits[i], decs[i].forward(cur[i], p), nxt[i], stats, oracle)
+        cur = [int(toks[i, p + 1]) if p + 1 < 6 else nxt[i] for i in range(n)]
+    print(f"batched steps vs oracle: {stats}")
+    check(stats)
+    m.close()
+
+
 def test_generate_matches_oracle(ctx, small_vocab):
     """g4a_model_generate (generate.rs:15-64, greedy) against the oracle's
     generate, token for token."""
