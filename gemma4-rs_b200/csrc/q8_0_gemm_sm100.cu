@@ -14,7 +14,8 @@
 // would add a TMEM read per block on the same path.
 //
 // Tiles: 64 rows x 64, 32 or 16 vectors per CTA (the widest that still
-// gives two CTAs per SM), 8 blocks (256 columns) per stage, two CTAs per SM.
+// gives two CTAs per SM; at most 32 for GEGLU's two matrices), 8 blocks (256
+// columns) per stage, two CTAs per SM.
 // Weights stay in the GGUF layout: a 2-D TMA box of 64 rows x 272 bytes (8
 // blocks of [f16 scale, 32 quants]) per stage; activation quants come in two
 // 128-byte-swizzled boxes of 128 bytes per vector, their f32 scales in a
@@ -141,15 +142,16 @@ __device__ __forceinline__ float softcap(float v, float cap) {
     return __fmul_rn(glibc::tanhf(__fmul_rn(v, __fdiv_rn(1.0f, cap))), cap);
 }
 
-// NJ n8 tiles per warp: a CTA covers 64 rows x (16 * NJ) vectors.
-template <int NJ>
+// NJ n8 tiles per warp: a CTA covers 64 rows x (16 * NJ) vectors; NMAT
+// weight matrices (2: GEGLU's gate and up).
+template <int NJ, int NMAT>
 __global__ void __launch_bounds__(kGemmThreads, 2) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
     constexpr int BN = 16 * NJ;
     constexpr int BST = b_stage(BN);
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     // the swizzled boxes need 1024-byte aligned destinations
     uint8_t *sm = sm_raw + ((1024u - (ptx::smem_u32(sm_raw) & 1023u)) & 1023u);
-    const int n_mat = p.kind == KIND_GEGLU ? 2 : 1;
+    constexpr int n_mat = NMAT;
     const int sb = stage_bytes(BN, n_mat);
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + (size_t)p.stages * sb);
     uint64_t *empty = full + p.stages;
@@ -206,10 +208,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q8_gemm_kernel(const __grid_c
     const int g = lane >> 2, t = lane & 3;
     const int ra = wm * 16 + g;  // this thread's rows in the tile: ra, ra + 8
     // accumulators: [matrix][n8 tile][(row ra | ra + 8) x (vector 2t | 2t + 1)]
-    float acc[2][NJ][4];
+    float acc[NMAT][NJ][4];
     const uint64_t magic = pk(12582912.0f, 12582912.0f);
 #pragma unroll
-    for (int m = 0; m < 2; m++)
+    for (int m = 0; m < NMAT; m++)
 #pragma unroll
         for (int j = 0; j < NJ; j++)
 #pragma unroll
@@ -222,7 +224,9 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q8_gemm_kernel(const __grid_c
         gemm_wait(&full[s], (uint32_t)(k / p.stages) & 1u, p.err);
         const float *xs = reinterpret_cast<const float *>(st + BST + n_mat * kAStage);
         const uint32_t bst = ptx::smem_u32(st);
-#pragma unroll 2
+        // fully unrolled (every offset an immediate) where the registers allow
+        constexpr int kUnroll = NJ * NMAT >= 4 ? 4 : kKB;
+#pragma unroll kUnroll
         for (int kb = 0; kb < kKB; kb++) {
             // activation fragments (ldmatrix from the swizzled rows) and scales
             uint32_t b[NJ][2];
@@ -253,8 +257,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q8_gemm_kernel(const __grid_c
                 xsc[j] = pk(xs[vo * kKB + kb], xs[(vo + 1) * kKB + kb]);
             }
 #pragma unroll
-            for (int m = 0; m < 2; m++) {
-                if (m == n_mat) break;
+            for (int m = 0; m < NMAT; m++) {
                 const uint8_t *row0 = st + BST + m * kAStage + (size_t)ra * kRowBytes;
                 const uint8_t *row1 = row0 + 8 * kRowBytes;
                 const int off = kb * 34;
@@ -298,9 +301,9 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q8_gemm_kernel(const __grid_c
             for (int e = 0; e < 2; e++) {
                 const int v = v0 + wn * 8 * NJ + j * 8 + 2 * t + e;
                 if (r >= p.rows || v >= p.n_vec) continue;
-                const float gate = acc[0][j][2 * h + e], up = acc[1][j][2 * h + e];
+                const float gate = acc[0][j][2 * h + e];
                 float res = gate;
-                if (p.kind == KIND_GEGLU) res = __fmul_rn(gelu_tanh(gate), up);
+                if constexpr (NMAT == 2) res = __fmul_rn(gelu_tanh(gate), acc[NMAT - 1][j][2 * h + e]);
                 else if (p.kind == KIND_SOFTCAP) res = softcap(gate, p.cap);
                 p.out[(int64_t)v * p.rows + r] = res;
             }
@@ -314,18 +317,18 @@ int gemm_stages(int bn, int n_mat) {
     return st;
 }
 
-template <int NJ>
-cudaError_t gemm_launch(GemmParams &p, int n_mat, int64_t rows, int32_t n_vec, cudaStream_t st, bool pdl) {
+template <int NJ, int NMAT>
+cudaError_t gemm_launch(GemmParams &p, int64_t rows, int32_t n_vec, cudaStream_t st, bool pdl) {
     constexpr int BN = 16 * NJ;
-    p.stages = gemm_stages(BN, n_mat);
-    const size_t smem = 1024 + (size_t)p.stages * stage_bytes(BN, n_mat) + 2 * p.stages * sizeof(uint64_t);
+    p.stages = gemm_stages(BN, NMAT);
+    const size_t smem = 1024 + (size_t)p.stages * stage_bytes(BN, NMAT) + 2 * p.stages * sizeof(uint64_t);
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(q8_gemm_kernel<NJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(q8_gemm_kernel<NJ, NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_set = true;
     }
     const dim3 grid((unsigned)((n_vec + BN - 1) / BN), (unsigned)((rows + kBM - 1) / kBM));
-    return launch_k(pdl, q8_gemm_kernel<NJ>, grid, dim3(kGemmThreads), smem, st, p);
+    return launch_k(pdl, q8_gemm_kernel<NJ, NMAT>, grid, dim3(kGemmThreads), smem, st, p);
 }
 
 }  // namespace
@@ -343,7 +346,7 @@ cudaError_t q8_gemm_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t r
     const int64_t nb = cols / 32, row_len = nb * 34;
     // vector tile: the widest (64, 32, 16) that still gives two CTAs per SM
     const int64_t row_tiles = (rows + kBM - 1) / kBM;
-    int nj = 4;
+    int nj = n_mat == 2 ? 2 : 4;
     while (nj > 1 && row_tiles * ((n_vec + 16 * nj - 1) / (16 * nj)) < 2 * 148) nj >>= 1;
     GemmParams p;
     bool ok = encode_tmap_2d_raw(&p.ta, 2, w, (uint64_t)row_len / 2, (uint64_t)rows, (uint64_t)row_len, kKB * 17, kBM,
@@ -363,9 +366,10 @@ cudaError_t q8_gemm_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t r
     p.kind = kind;
     p.cap = cap;
     p.err = d_err;
-    if (nj == 4) return gemm_launch<4>(p, n_mat, rows, n_vec, st, pdl);
-    if (nj == 2) return gemm_launch<2>(p, n_mat, rows, n_vec, st, pdl);
-    return gemm_launch<1>(p, n_mat, rows, n_vec, st, pdl);
+    if (n_mat == 2) return nj == 2 ? gemm_launch<2, 2>(p, rows, n_vec, st, pdl) : gemm_launch<1, 2>(p, rows, n_vec, st, pdl);
+    if (nj == 4) return gemm_launch<4, 1>(p, rows, n_vec, st, pdl);
+    if (nj == 2) return gemm_launch<2, 1>(p, rows, n_vec, st, pdl);
+    return gemm_launch<1, 1>(p, rows, n_vec, st, pdl);
 }
 
 }  // namespace g4a
