@@ -380,10 +380,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(DecodeParams p) 
 //           in shared memory, then one thread per (head, row):
 //           dot_f32 = 16 accumulators (element i into accumulator i % 16,
 //           multiply then add), summed in order from -0.0, times the scale;
-//   pv      one CTA per (task, head, 128 value columns): max, p_j =
+//   pv      one CTA per (task, 128 value columns): per head max, p_j =
 //           exp(s_j - max) / sum with glibc's expf and the sum sequential in
 //           key order from -0.0, then out = sum_j p_j * v_j in key order from
-//           +0.0 (multiply then add), one thread per column.
+//           +0.0 (multiply then add), one thread per column for all eight
+//           heads (each V row read once); with few tasks, one CTA per head.
 // The q/k norms, RoPE and the stored rows are the fused kernel's (bit-exact).
 constexpr int kExactChunk = 32;
 constexpr int kPvCols = 128;
@@ -470,12 +471,14 @@ __global__ void __launch_bounds__(kDecodeThreads) exact_scores_kernel(DecodePara
     }
 }
 
+// The same per (task, head, 128 columns): more CTAs for few tasks (one
+// sequence), each V row then read once per head.
 template <int HD>
-__global__ void __launch_bounds__(kPvCols) exact_pv_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(kPvCols) exact_pv_head_kernel(DecodeParams p) {
     ptx::pdl_trigger();
     ptx::pdl_wait();
-    constexpr int CH = HD / kPvCols;  // column chunks per head
-    extern __shared__ float pr[];     // [max_rows]: scores, then probabilities
+    constexpr int CH = HD / kPvCols;
+    extern __shared__ float pr[];  // [max_rows]
     __shared__ float red[kPvCols / 32];
     __shared__ int flag_s;
     const int task = blockIdx.x / (kHeads * CH);
@@ -528,6 +531,76 @@ __global__ void __launch_bounds__(kPvCols) exact_pv_kernel(DecodeParams p) {
     }
     for (; r < rows; r++) acc = __fadd_rn(acc, __fmul_rn(pr[r], row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, tk.lo + r)[col]));
     tk.out[(size_t)h * HD + col] = acc;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPvCols) exact_pv_kernel(DecodeParams p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int CH = HD / kPvCols;  // column chunks per task
+    extern __shared__ float pr[];     // [kHeads][max_rows]: scores, then probabilities
+    __shared__ float tot_s[kHeads];
+    __shared__ int bad_s[kHeads];
+    const int task = blockIdx.x / CH, chunk = blockIdx.x % CH;
+    const DecodeTask &tk = p.tasks[task];
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
+    const int rows = tk.hi - tk.lo, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const float *sc = p.scores + (size_t)task * kHeads * p.max_rows;
+    for (int i = t; i < kHeads * p.max_rows; i += kPvCols) {
+        const int h = i / p.max_rows, r = i - h * p.max_rows;
+        if (r < rows) pr[i] = sc[i];
+    }
+    __syncthreads();
+    // softmax_f32 per head: warp w takes heads w and w + 4
+    for (int h = warp; h < kHeads; h += kPvCols / 32) {
+        float *ph = pr + (size_t)h * p.max_rows;
+        float m = -CUDART_INF_F;
+        bool finite = true;
+        for (int r = lane; r < rows; r += 32) {
+            finite = finite && isfinite(ph[r]);
+            m = fmaxf(m, ph[r]);
+        }
+        m = warp_max(m);
+        finite = __all_sync(kFull, finite);
+        for (int r = lane; r < rows; r += 32) ph[r] = glibc::expf(__fsub_rn(ph[r], m));
+        __syncwarp();
+        if (lane == 0) {
+            float total = -0.0f;  // sequential in key order, as f32 Sum
+            for (int r = 0; r < rows; r++) total = __fadd_rn(total, ph[r]);
+            const bool bad = !finite || !isfinite(total) || total == 0.0f;
+            bad_s[h] = bad;
+            tot_s[h] = bad ? CUDART_NAN_F : total;
+        }
+        __syncwarp();
+        const float total = tot_s[h];
+        for (int r = lane; r < rows; r += 32) ph[r] = __fdiv_rn(ph[r], total);
+    }
+    __syncthreads();
+    if (t < kHeads && chunk == 0 && bad_s[t]) atomicOr(p.err_flag, 1);
+    // out[h][col] = sum_j p[h][j] * v[j][col] in key order; each V row is
+    // loaded once and serves the eight heads
+    const int col = chunk * kPvCols + t;
+    float acc[kHeads];
+#pragma unroll
+    for (int h = 0; h < kHeads; h++) acc[h] = 0.0f;
+    int r = 0;
+    for (; r + 8 <= rows; r += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, tk.lo + r + u)[col];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+#pragma unroll
+            for (int h = 0; h < kHeads; h++)
+                acc[h] = __fadd_rn(acc[h], __fmul_rn(pr[(size_t)h * p.max_rows + r + u], v[u]));
+    }
+    for (; r < rows; r++) {
+        const float v = row_ptr<float>(tk.v_base, bt, p.page_tokens, HD, tk.lo + r)[col];
+#pragma unroll
+        for (int h = 0; h < kHeads; h++) acc[h] = __fadd_rn(acc[h], __fmul_rn(pr[(size_t)h * p.max_rows + r], v));
+    }
+#pragma unroll
+    for (int h = 0; h < kHeads; h++) tk.out[(size_t)h * HD + col] = acc[h];
 }
 
 // Generic attend for any (n_heads, n_kv, hd <= 1024): one CTA per query
@@ -700,22 +773,33 @@ cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool /*fast
 cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl) {
     if (p.n_items == 0 || n_tasks == 0) return cudaSuccess;
     if (p.max_rows <= 0 || p.max_rows > kExactMaxRows || !p.scores) return cudaErrorInvalidValue;
-    const size_t pv_smem = (size_t)p.max_rows * sizeof(float);
+    const size_t pv_smem = (size_t)kHeads * p.max_rows * sizeof(float);
+    if (pv_smem > 48 * 1024) {
+        cudaFuncSetAttribute(exact_pv_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem);
+        cudaFuncSetAttribute(exact_pv_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem);
+    }
+    // few tasks: a CTA per head as well, so that the GPU has work to spread
+    const bool per_head = n_tasks * (hd / kPvCols) < 148;
+    const size_t head_smem = (size_t)p.max_rows * sizeof(float);
     if (hd == 256) {
         const size_t smem = (size_t)kExactChunk * (256 + 4) * sizeof(float);
         cudaFuncSetAttribute(exact_scores_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaError_t e = launch_k(pdl, exact_scores_kernel<256>, dim3(p.n_items), dim3(kDecodeThreads), smem, s, p);
         if (e == cudaSuccess)
-            e = launch_k(pdl, exact_pv_kernel<256>, dim3(n_tasks * kHeads * (256 / kPvCols)), dim3(kPvCols), pv_smem,
-                         s, p);
+            e = per_head ? launch_k(pdl, exact_pv_head_kernel<256>, dim3(n_tasks * kHeads * (256 / kPvCols)),
+                                    dim3(kPvCols), head_smem, s, p)
+                         : launch_k(pdl, exact_pv_kernel<256>, dim3(n_tasks * (256 / kPvCols)), dim3(kPvCols),
+                                    pv_smem, s, p);
         if (e != cudaSuccess) return e;
     } else if (hd == 512) {
         const size_t smem = (size_t)kExactChunk * (512 + 4) * sizeof(float);
         cudaFuncSetAttribute(exact_scores_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaError_t e = launch_k(pdl, exact_scores_kernel<512>, dim3(p.n_items), dim3(kDecodeThreads), smem, s, p);
         if (e == cudaSuccess)
-            e = launch_k(pdl, exact_pv_kernel<512>, dim3(n_tasks * kHeads * (512 / kPvCols)), dim3(kPvCols), pv_smem,
-                         s, p);
+            e = per_head ? launch_k(pdl, exact_pv_head_kernel<512>, dim3(n_tasks * kHeads * (512 / kPvCols)),
+                                    dim3(kPvCols), head_smem, s, p)
+                         : launch_k(pdl, exact_pv_kernel<512>, dim3(n_tasks * (512 / kPvCols)), dim3(kPvCols),
+                                    pv_smem, s, p);
         if (e != cudaSuccess) return e;
     } else {
         return cudaErrorInvalidValue;
