@@ -19,7 +19,10 @@ The same line carries:
     port, pool.rs-shaped thread pool) timed on this host;
   * decode_batch1 — configuration 0 (batch 1, context 628) latency;
   * prefill   — configurations 1 (628-token prompt, 35 layers) and 3
-    (32,768-token global prefill, one GPU) in TFLOP/s against the tensor peak.
+    (32,768-token global prefill, one GPU) in TFLOP/s against the tensor peak;
+  * e2e_decoder — configuration 4, the whole E2B decoder through
+    g4a_model_generate (batch 1 and 256 on one GPU with the oracle decoder's
+    host rate and top-1 agreement; at N > 1 batch 256 sharded by sequence).
 
 `--impl reference` times the reference's own CPU path instead (the oracle
 port on all host cores; the Rust reference cannot be built here).
@@ -535,6 +538,37 @@ def measure_q8_head(torch, g4a, ctx, stream, pk, reps=10, warmup=3, cpu_rows=819
 DEC_PROMPT, DEC_NEW = 19, 94
 
 
+def measure_decoder_sharded(torch, g4a, ctx, dist, world, rank, batch=256, new_tokens=DEC_NEW):
+    """Configuration 4 at batch 256 over `world` GPUs: the sequences are
+    independent, so each rank decodes its contiguous share (same seeded
+    prompts, the same seeded weights on every GPU) with no collective; the
+    job's tokens/s is all sequences' forward passes over the slowest rank's
+    wall time (barrier on both sides)."""
+    import g4attn.model as gm
+    w = gm.synthetic_weights(ctx, seed=4)
+    prompts = np.random.default_rng(40 + batch).integers(0, w.vocab, (batch, DEC_PROMPT)).astype(np.int32)
+    mine = np.array_split(np.arange(batch), world)[rank]
+    m = gm.Model(ctx, w, max_seqs=len(mine), max_tokens=DEC_PROMPT + DEC_NEW + 1)
+    m.generate(prompts[mine], 4)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    m.generate(prompts[mine], new_tokens)
+    dt = time.perf_counter() - t0
+    dist.barrier()
+    m.close()
+    t = torch.tensor([dt], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t[0])
+    passes = DEC_PROMPT + new_tokens - 1
+    del w
+    return {"model": "E2B, 35 layers, vocab 262144, Q8_0 (synthetic)", "batch": batch, "ranks": world,
+            "seqs_per_rank": int(len(mine)), "s_slowest_rank": round(dt, 4),
+            "tokens_per_s": round(batch * passes / dt, 1), "generated_tokens_per_s": round(batch * new_tokens / dt, 1),
+            "parallelism": f"sequence-sharded x{world}, no collective",
+            "timing": "wall clock around g4a_model_generate on every rank, max over ranks"}
+
+
 def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0, new_tokens=DEC_NEW):
     """Configuration 4: the whole E2B decoder (35 layers, vocab 262,144, Q8_0
     weights from N(0, 0.02), bf16-rounded norms; synthetic, seeded) through
@@ -807,6 +841,7 @@ def main():
     extras = {}
     if dist is not None and not a.no_extras:
         extras["prefill_cp"] = measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk)
+        extras["e2e_decoder"] = measure_decoder_sharded(torch, g4a, ctx, dist, world, rank)
     if rank == 0 and not a.no_extras:
         extras["decode_batch1"] = measure_batch1(torch, g4a, ctx, stream)
         extras["prefill"] = measure_prefill(torch, g4a, ctx, stream, pk)
