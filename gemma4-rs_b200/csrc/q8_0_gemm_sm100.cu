@@ -344,10 +344,20 @@ cudaError_t q8_gemm_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t r
                         const float *xs, int32_t n_vec, float cap, float *out, int *d_err, cudaStream_t st, bool pdl) {
     const int n_mat = kind == KIND_GEGLU ? 2 : 1;
     const int64_t nb = cols / 32, row_len = nb * 34;
-    // vector tile: the widest (64, 32, 16) that still gives two CTAs per SM
+    // vector tile (64, 32 or 16 vectors): the least estimated time, waves of
+    // two CTAs per SM times the tile's work over its relative efficiency
+    // (wider tiles reuse each weight fragment for more vectors; measured on
+    // the E2B shapes)
     const int64_t row_tiles = (rows + kBM - 1) / kBM;
-    int nj = n_mat == 2 ? 2 : 4;
-    while (nj > 1 && row_tiles * ((n_vec + 16 * nj - 1) / (16 * nj)) < 2 * 148) nj >>= 1;
+    int nj = 1;
+    double best = 1e300;
+    for (int cand = n_mat == 2 ? 2 : 4; cand >= 1; cand >>= 1) {
+        const double eff = cand == 4 ? 1.0 : cand == 2 ? 0.8 : 0.55;
+        const int64_t ctas = row_tiles * ((n_vec + 16 * cand - 1) / (16 * cand));
+        const double waves = (double)((ctas + 2 * 148 - 1) / (2 * 148));
+        const double cost = waves * cand / eff;
+        if (cost < best - 1e-9) best = cost, nj = cand;
+    }
     GemmParams p;
     bool ok = encode_tmap_2d_raw(&p.ta, 2, w, (uint64_t)row_len / 2, (uint64_t)rows, (uint64_t)row_len, kKB * 17, kBM,
                                  false);
