@@ -603,6 +603,180 @@ __global__ void __launch_bounds__(kPvCols) exact_pv_kernel(DecodeParams p) {
     for (int h = 0; h < kHeads; h++) tk.out[(size_t)h * HD + col] = acc[h];
 }
 
+// Few tasks (a batch of a few sequences): the whole attention of one
+// (task, head) in one CTA, in the same order of operations as the two
+// kernels above: q norm + RoPE of the head, the new row's k/v (stored by the
+// head-0 CTA; every CTA uses its own copy for that row), then K in chunks of
+// kExactChunk rows staged in shared memory by cp.async (double-buffered):
+// eight threads per row each run two of dot_f32's sixteen accumulators, one
+// thread per row sums them in order; softmax_f32 with glibc's expf and the
+// sequential sum; then V in chunks the same way, one thread per column.
+constexpr int kHeadThreads = 256;
+
+template <int HD>
+__global__ void __launch_bounds__(kHeadThreads) exact_head_kernel(DecodeParams p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int PL = HD / 32, KS = HD + 4, RC = kExactChunk, CPT = HD / kHeadThreads;
+    extern __shared__ float4 dyn4[];
+    float *buf = reinterpret_cast<float *>(dyn4);  // [2][RC][KS]
+    float *sc = buf + 2 * RC * KS;                 // [max_rows]
+    float *accs = sc + p.max_rows;                 // [RC][17]
+    __shared__ __align__(16) float q_s[HD];
+    __shared__ __align__(16) float knew_s[HD];
+    __shared__ __align__(16) float vnew_s[HD];
+    __shared__ float red[kHeadThreads / 32];
+    __shared__ int flag_s;
+    const int task = blockIdx.x / kHeads, h = blockIdx.x % kHeads;
+    const DecodeTask &tk = p.tasks[task];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
+    const float2 *rope = tk.global ? p.rope_global : p.rope_local;
+    const int lo = tk.lo, rows = tk.hi - tk.lo;
+    if (warp == 0) {
+        float x[PL];
+        const float *src = tk.q_raw + (size_t)h * HD;
+#pragma unroll
+        for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (!tk.q_ready) norm_rope_warp<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+#pragma unroll
+        for (int k = 0; k < PL; k++) q_s[lane + 32 * k] = x[k];
+    } else if (tk.new_row >= 0 && warp < 3) {
+        float x[PL];
+        const float *src = warp == 1 ? tk.k_raw : tk.v_raw;
+#pragma unroll
+        for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+        if (warp == 1)
+            norm_rope_warp<HD>(x, tk.k_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+        else
+            norm_rope_warp<HD>(x, nullptr, nullptr, p.eps, lane);
+        float *sm = warp == 1 ? knew_s : vnew_s;
+        float *dst = h == 0 ? const_cast<float *>(row_ptr<float>(warp == 1 ? tk.k_base : tk.v_base, bt, p.page_tokens,
+                                                                 HD, tk.new_row))
+                            : nullptr;
+#pragma unroll
+        for (int k = 0; k < PL; k++) {
+            sm[lane + 32 * k] = x[k];
+            if (dst) dst[lane + 32 * k] = x[k];
+        }
+    }
+    if (tid == 0) flag_s = rows > 0 && rows <= p.max_rows;
+    __syncthreads();
+    if (!flag_s) {  // more rows than the launch's score buffer: report, skip
+        if (tid == 0 && h == 0) atomicOr(p.err_flag, 4);
+        return;
+    }
+    const int n_chunks = (rows + RC - 1) / RC;
+    // rows [c*RC, ...) of K (which = 0) or V (1) into buffer b; the new row from shared memory
+    auto stage = [&](int which, int c, int b) {
+        const int r0 = c * RC, nr = min(RC, rows - r0);
+        float *dst = buf + (size_t)b * RC * KS;
+        for (int e = tid; e < nr * (HD / 4); e += kHeadThreads) {
+            const int r = e / (HD / 4), q4 = e - r * (HD / 4);
+            const int row = lo + r0 + r;
+            float *d = dst + (size_t)r * KS + 4 * q4;
+            if (row == tk.new_row)
+                *reinterpret_cast<float4 *>(d) = reinterpret_cast<const float4 *>(which ? vnew_s : knew_s)[q4];
+            else
+                ptx::cp_async16(d, row_ptr<float>(which ? tk.v_base : tk.k_base, bt, p.page_tokens, HD, row) + 4 * q4);
+        }
+        ptx::cp_async_commit();
+    };
+    // ---- scores ----
+    stage(0, 0, 0);
+    for (int c = 0; c < n_chunks; c++) {
+        if (c + 1 < n_chunks) {
+            stage(0, c + 1, (c + 1) & 1);
+            ptx::cp_async_wait<1>();
+        } else {
+            ptx::cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int r0 = c * RC, nr = min(RC, rows - r0);
+        const float *kb = buf + (size_t)(c & 1) * RC * KS;
+        {
+            const int r = tid >> 3, sub = tid & 7;  // accumulators 2 sub, 2 sub + 1
+            if (r < nr) {
+                const float *kr = kb + (size_t)r * KS;
+                float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 8
+                for (int m = 0; m < HD / 16; m++) {
+                    const float2 kv = *reinterpret_cast<const float2 *>(kr + 16 * m + 2 * sub);
+                    const float2 qv = *reinterpret_cast<const float2 *>(q_s + 16 * m + 2 * sub);
+                    a0 = __fadd_rn(a0, __fmul_rn(qv.x, kv.x));
+                    a1 = __fadd_rn(a1, __fmul_rn(qv.y, kv.y));
+                }
+                accs[r * 17 + 2 * sub] = a0;
+                accs[r * 17 + 2 * sub + 1] = a1;
+            }
+        }
+        __syncthreads();
+        if (tid < nr) {
+            float s = -0.0f;
+#pragma unroll
+            for (int l = 0; l < 16; l++) s = __fadd_rn(s, accs[tid * 17 + l]);
+            sc[r0 + tid] = __fmul_rn(s, tk.scale);
+        }
+        __syncthreads();  // the buffer is restaged two chunks on
+    }
+    // V's first chunk streams in while the softmax runs
+    stage(1, 0, 0);
+    // ---- softmax_f32 (ops.rs:105-127) ----
+    float m = -CUDART_INF_F;
+    bool finite = true;
+    for (int r = tid; r < rows; r += kHeadThreads) {
+        finite = finite && isfinite(sc[r]);
+        m = fmaxf(m, sc[r]);
+    }
+    m = warp_max(m);
+    finite = __all_sync(kFull, finite);
+    if (lane == 0) red[warp] = m;
+    if (tid == 0) flag_s = 1;
+    __syncthreads();
+    if (lane == 0 && !finite) flag_s = 0;
+    m = red[0];
+#pragma unroll
+    for (int w = 1; w < kHeadThreads / 32; w++) m = fmaxf(m, red[w]);
+    for (int r = tid; r < rows; r += kHeadThreads) sc[r] = glibc::expf(__fsub_rn(sc[r], m));
+    __syncthreads();
+    if (tid == 0) {
+        float total = -0.0f;
+        for (int r = 0; r < rows; r++) total = __fadd_rn(total, sc[r]);
+        if (!flag_s || !isfinite(total) || total == 0.0f) {
+            atomicOr(p.err_flag, 1);
+            total = CUDART_NAN_F;
+        }
+        red[0] = total;
+    }
+    __syncthreads();
+    const float total = red[0];
+    for (int r = tid; r < rows; r += kHeadThreads) sc[r] = __fdiv_rn(sc[r], total);
+    // ---- out = sum_j p_j v_j in key order ----
+    float acc[CPT];
+#pragma unroll
+    for (int u = 0; u < CPT; u++) acc[u] = 0.0f;
+    for (int c = 0; c < n_chunks; c++) {
+        if (c + 1 < n_chunks) {
+            stage(1, c + 1, (c + 1) & 1);
+            ptx::cp_async_wait<1>();
+        } else {
+            ptx::cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int r0 = c * RC, nr = min(RC, rows - r0);
+        const float *vb = buf + (size_t)(c & 1) * RC * KS;
+        for (int r = 0; r < nr; r++) {
+            const float pr = sc[r0 + r];
+#pragma unroll
+            for (int u = 0; u < CPT; u++)
+                acc[u] = __fadd_rn(acc[u], __fmul_rn(pr, vb[(size_t)r * KS + tid + kHeadThreads * u]));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < CPT; u++) tk.out[(size_t)h * HD + tid + kHeadThreads * u] = acc[u];
+}
+
 // Generic attend for any (n_heads, n_kv, hd <= 1024): one CTA per query
 // head, online softmax over blocks of 256 rows. Used for shapes the fused
 // E2B kernels do not serve (e.g. the reference's small synthetic models).
@@ -773,6 +947,18 @@ cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool /*fast
 cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl) {
     if (p.n_items == 0 || n_tasks == 0) return cudaSuccess;
     if (p.max_rows <= 0 || p.max_rows > kExactMaxRows || !p.scores) return cudaErrorInvalidValue;
+    if (n_tasks * kHeads <= 148) {  // few tasks: one launch, a CTA per (task, head)
+        const size_t smem = ((size_t)2 * kExactChunk * (hd + 4) + p.max_rows + kExactChunk * 17) * sizeof(float);
+        if (hd == 256) {
+            cudaFuncSetAttribute(exact_head_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            return launch_k(pdl, exact_head_kernel<256>, dim3(n_tasks * kHeads), dim3(kHeadThreads), smem, s, p);
+        }
+        if (hd == 512) {
+            cudaFuncSetAttribute(exact_head_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            return launch_k(pdl, exact_head_kernel<512>, dim3(n_tasks * kHeads), dim3(kHeadThreads), smem, s, p);
+        }
+        return cudaErrorInvalidValue;
+    }
     const size_t pv_smem = (size_t)kHeads * p.max_rows * sizeof(float);
     if (pv_smem > 48 * 1024) {
         cudaFuncSetAttribute(exact_pv_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem);
