@@ -146,9 +146,20 @@ cudaError_t q8_gemm_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t r
 // Prefill (prefill_sm100.cu): per-context scratch and the launcher behind
 // g4a_prefill. Returns a g4a_status and points *msg at a description.
 // Q8_0 mat-vec family (q8_0_sm100.cu); kind 0 plain, 1 GEGLU (w2 = up), 2 soft-cap.
+// With pli (small batches, one pass): the input quantized is gelu(x) * pli
+// (vector v's per-layer input at pli + v * pli_stride), the PLE gate of
+// model.rs:426-428 fused into the `proj` mat-vec.
+// With extra (kind 0, small batches, one pass): up to two more matrices of
+// the same width over the same input in the same launch (q, k and v).
+struct Q8Seg {
+    const uint8_t *w;
+    int64_t rows;
+    float *out;  // [n_vec][rows]
+};
 int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
            float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg,
-           bool pdl = false);
+           bool pdl = false, const float *pli = nullptr, int32_t pli_stride = 0, const Q8Seg *extra = nullptr,
+           int n_extra = 0);
 
 // E2B decoder step (e2b_sm100.cu).
 // One layer of the model as the attention planner sees it; the caches are

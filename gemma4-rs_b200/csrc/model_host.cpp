@@ -96,10 +96,11 @@ const char *missing_weight(const g4a_model_weights &w, int32_t layer, bool owner
 }
 
 int mv(g4a_model *m, int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int n,
-       float cap, float *out) {
+       float cap, float *out, const float *pli = nullptr, int32_t pli_stride = 0, const Q8Seg *extra = nullptr,
+       int n_extra = 0) {
     const char *msg = "";
     const int rc = q8_run(kind, w, w2, rows, cols, x, n, cap, out, m->xq, m->xs, m->ctx->d_err, m->ctx->n_sm, m->st,
-                          &msg, m->pdl);
+                          &msg, m->pdl, pli, pli_stride, extra, n_extra);
     return rc == G4A_OK ? G4A_OK : fail(m->ctx, rc, "compute: %s", msg);
 }
 
@@ -153,11 +154,17 @@ int enqueue_step(g4a_model *m, int32_t n) {
         const g4a_layer_weights &lw = w.layers[l];
         const int hd = m->hd[l], qd = kHeads * hd;
         const bool owner = m->source[l] == l;
-        // q, k, v of the normalized input (model.rs:392-401)
-        if ((rc = mv(m, 0, lw.attn_q, nullptr, qd, d, nullptr, n, 0.0f, m->q))) return rc;
-        if (owner) {
-            if ((rc = mv(m, 0, lw.attn_k, nullptr, hd, d, nullptr, n, 0.0f, m->k))) return rc;
-            if ((rc = mv(m, 0, lw.attn_v, nullptr, hd, d, nullptr, n, 0.0f, m->v))) return rc;
+        // q, k, v of the normalized input (model.rs:392-401); small batches
+        // stream the three matrices in one launch
+        if (owner && n <= 8) {
+            const Q8Seg kv[2] = {{lw.attn_k, hd, m->k}, {lw.attn_v, hd, m->v}};
+            if ((rc = mv(m, 0, lw.attn_q, nullptr, qd, d, nullptr, n, 0.0f, m->q, nullptr, 0, kv, 2))) return rc;
+        } else {
+            if ((rc = mv(m, 0, lw.attn_q, nullptr, qd, d, nullptr, n, 0.0f, m->q))) return rc;
+            if (owner) {
+                if ((rc = mv(m, 0, lw.attn_k, nullptr, hd, d, nullptr, n, 0.0f, m->k))) return rc;
+                if ((rc = mv(m, 0, lw.attn_v, nullptr, hd, d, nullptr, n, 0.0f, m->v))) return rc;
+            }
         }
         // q/k/v norms, RoPE, append, window and attention (:394-410)
         DecodeParams p{};
@@ -192,8 +199,14 @@ int enqueue_step(g4a_model *m, int32_t n) {
             // per-layer embedding (:422-432), then layer_output_scale (:433-435)
             MODEL_TRY(e2b_resid(m->x, m->y, lw.post_ffw_norm, 1.0f, nullptr, d, eps, m->xq, m->xs, n, m->st, m->pdl));
             if ((rc = mv(m, 0, lw.inp_gate, nullptr, ple, d, nullptr, n, 0.0f, m->gate))) return rc;
-            MODEL_TRY(e2b_gelu_quant(m->gate, m->pli, l, L, ple, m->xq, m->xs, n, m->st, m->pdl));
-            if ((rc = mv(m, 0, lw.proj, nullptr, d, ple, nullptr, n, 0.0f, m->y))) return rc;
+            if (n <= 8) {  // the gate rides on the proj mat-vec's input quantization
+                if ((rc = mv(m, 0, lw.proj, nullptr, d, ple, m->gate, n, 0.0f, m->y, m->pli + (size_t)l * ple,
+                             L * ple)))
+                    return rc;
+            } else {
+                MODEL_TRY(e2b_gelu_quant(m->gate, m->pli, l, L, ple, m->xq, m->xs, n, m->st, m->pdl));
+                if ((rc = mv(m, 0, lw.proj, nullptr, d, ple, nullptr, n, 0.0f, m->y))) return rc;
+            }
             MODEL_TRY(e2b_resid(m->x, m->y, lw.post_norm, lw.layer_output_scale, next_norm, d, eps, m->xq, m->xs, n,
                                 m->st, m->pdl));
         } else {

@@ -49,6 +49,7 @@ constexpr int64_t kStageTarget = 16 * 1024;  // weight bytes per stage
 
 
 enum { KIND_PLAIN = 0, KIND_GEGLU = 1, KIND_SOFTCAP = 2 };
+constexpr int kMaxSeg = 3;
 
 // ops.rs:85-89, left to right, no fused multiply-adds.
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -88,11 +89,21 @@ struct Q8Params {
     const int8_t *xq;      // [n_vec][cols] activation quants
     const float *xs;       // [n_vec][cols / 32] activation scales
     const float *xf;       // [n_vec][cols] f32 activations quantized in the prologue (then xq/xs unused)
+    const float *pli;      // with xf: quantize gelu(xf) * the layer's per-layer input instead (model.rs:426-428)
+    int32_t pli_stride;    // floats between consecutive vectors' per-layer inputs
     float *out;            // [n_vec][rows]
     int64_t rows;
     int32_t cols, row_len, n_vec, tile_rows, n_tiles, kind;
     float cap;
     int *err;
+    // Up to three matrices of the same width over one input in one launch
+    // (q, k, v): row tiles are numbered across them; segment i holds tiles
+    // [seg_tile0[i], seg_tile0[i + 1]). Segment 0 is (w, rows, out).
+    int32_t n_seg;
+    const uint8_t *seg_w[kMaxSeg];
+    float *seg_out[kMaxSeg];
+    int64_t seg_rows[kMaxSeg];
+    int32_t seg_tile0[kMaxSeg + 1];
 };
 
 // Block b of a row at `row` (shared memory, row start 16-byte aligned): the
@@ -193,10 +204,15 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
     ptx::pdl_trigger();
 
     const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    auto rows_of = [&](int k, int64_t *r0) {
-        const int64_t t = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
-        *r0 = t * p.tile_rows;
-        return (int)(p.rows - *r0 < p.tile_rows ? p.rows - *r0 : p.tile_rows);
+    // tile k of this CTA: its segment, first row and row count
+    auto rows_of = [&](int k, int64_t *r0, int *seg) {
+        const int t = (int)blockIdx.x + k * (int)gridDim.x;
+        int sg = 0;
+        while (sg + 1 < p.n_seg && t >= p.seg_tile0[sg + 1]) sg++;
+        *seg = sg;
+        *r0 = (int64_t)(t - p.seg_tile0[sg]) * p.tile_rows;
+        const int64_t rows = p.seg_rows[sg];
+        return (int)(rows - *r0 < p.tile_rows ? rows - *r0 : p.tile_rows);
     };
 
     if (warp == kProducerWarp) {
@@ -206,10 +222,12 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
                 const int s = k % kStages;
                 if (k >= kStages) q8_wait(&bars->empty[s], ((uint32_t)(k / kStages) & 1u) ^ 1u, p.err);
                 int64_t r0;
-                const int rows_here = rows_of(k, &r0);
+                int sg;
+                const int rows_here = rows_of(k, &r0, &sg);
                 const uint32_t bytes = (uint32_t)rows_here * p.row_len;
                 ptx::mbar_arrive_expect_tx(&bars->full[s], bytes * n_mat);
-                ptx::bulk_load_1d(ring + (size_t)s * n_mat * L.mat_bytes, p.w + r0 * p.row_len, bytes, &bars->full[s]);
+                ptx::bulk_load_1d(ring + (size_t)s * n_mat * L.mat_bytes, p.seg_w[sg] + r0 * p.row_len, bytes,
+                                  &bars->full[s]);
                 if (n_mat == 2)
                     ptx::bulk_load_1d(ring + (size_t)s * n_mat * L.mat_bytes + L.mat_bytes, p.w2 + r0 * p.row_len,
                                       bytes, &bars->full[s]);
@@ -227,7 +245,10 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
             const int buf = k & 1;
             q8_wait(&bars->vfull[buf], (uint32_t)(k >> 1) & 1u, p.err);
             int64_t r0;
-            const int rows_here = rows_of(k, &r0);
+            int sg;
+            const int rows_here = rows_of(k, &r0, &sg);
+            const int64_t seg_rows = p.seg_rows[sg];
+            float *seg_out = p.seg_out[sg];
             const float *vals_k = val_s + (size_t)buf * L.vals_buf;
             for (int e = lane; e < p.n_vec * rows_here; e += 32) {
                 const int v = e / rows_here, r = e - v * rows_here;
@@ -249,7 +270,7 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
                 float res = sums[0];
                 if (p.kind == KIND_GEGLU) res = __fmul_rn(gelu_tanh(sums[0]), sums[1]);
                 else if (p.kind == KIND_SOFTCAP) res = softcap(sums[0], p.cap);
-                p.out[(size_t)v * p.rows + r0 + r] = res;
+                seg_out[(size_t)v * seg_rows + r0 + r] = res;
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&bars->vempty[buf]);
@@ -264,7 +285,15 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
             for (int base = warp * 32; base < total; base += kConsumers) {
                 const int e = base + lane;
                 const bool in = e < total;  // whole groups of 8 (cols a multiple of 32)
-                const float4 v = in ? __ldg(reinterpret_cast<const float4 *>(p.xf) + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                float4 v = in ? __ldg(reinterpret_cast<const float4 *>(p.xf) + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (p.pli && in) {  // the PLE gate: gelu(gate) * per-layer input
+                    const int vec = e / (p.cols / 4), c4 = e - vec * (p.cols / 4);
+                    const float4 g = __ldg(reinterpret_cast<const float4 *>(p.pli + (size_t)vec * p.pli_stride) + c4);
+                    v.x = __fmul_rn(gelu_tanh(v.x), g.x);
+                    v.y = __fmul_rn(gelu_tanh(v.y), g.y);
+                    v.z = __fmul_rn(gelu_tanh(v.z), g.z);
+                    v.w = __fmul_rn(gelu_tanh(v.w), g.w);
+                }
                 float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
                 m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
                 m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
@@ -315,7 +344,8 @@ __global__ void __launch_bounds__(kThreadsQ8, 3) q8_matvec_kernel(Q8Params p) {
             q8_wait(&bars->full[s], (uint32_t)(k / kStages) & 1u, p.err);
             if (k >= 2) q8_wait(&bars->vempty[buf], (uint32_t)((k - 2) >> 1) & 1u, p.err);
             int64_t r0;
-            const int rows_here = rows_of(k, &r0);
+            int sg;
+            const int rows_here = rows_of(k, &r0, &sg);
             const uint8_t *stage = ring + (size_t)s * n_mat * L.mat_bytes;
             float *vals_k = val_s + (size_t)buf * L.vals_buf;
             if (column_mode) {
@@ -417,8 +447,12 @@ __global__ void __launch_bounds__(256) q8_matvec_generic_kernel(Q8Params p) {
 // *msg names a failure.
 int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t cols, const float *x, int32_t n_vec,
            float cap, float *out, int8_t *xq, float *xs, int *d_err, int n_sm, cudaStream_t st, const char **msg,
-           bool pdl) {
+           bool pdl, const float *pli, int32_t pli_stride, const Q8Seg *extra, int n_extra) {
     *msg = "";
+    if (n_extra < 0 || n_extra > kMaxSeg - 1 || (n_extra && (kind != KIND_PLAIN || !extra))) {
+        *msg = "invalid extra mat-vec segments";
+        return G4A_COMPUTE;
+    }
     const int64_t nb = cols / kQ8Block;
     const int64_t n_blocks = nb * n_vec;
     const int n_mat = kind == KIND_GEGLU ? 2 : 1;
@@ -442,6 +476,14 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
             *msg = cudaGetErrorString(e);
             return G4A_CUDA;
         }
+    }
+    if (pli && !fused_quant) {
+        *msg = "the gelu-gate input needs the single-pass streaming kernel";
+        return G4A_COMPUTE;
+    }
+    if (n_extra && (!fast || gemm || n_vec > kMaxVec)) {
+        *msg = "several matrices in one launch need the single-pass streaming kernel";
+        return G4A_COMPUTE;
     }
     if (rows == 0) return cudaGetLastError() == cudaSuccess ? G4A_OK : G4A_CUDA;
     if (gemm) {
@@ -482,11 +524,25 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
         // rows per stage: as many as fit the stage target (about 16 KB, up to
         // 32 rows); several CTAs per SM keep enough copies in flight
         p.tile_rows = (int32_t)std::max<int64_t>(1, std::min<int64_t>(32, kStageTarget / (row_len * n_mat)));
-        const int64_t n_tiles = (rows + p.tile_rows - 1) / p.tile_rows;
+        // segments: (w, rows, out) and the extra matrices, tiles numbered across them
+        p.n_seg = 1 + n_extra;
+        int64_t n_tiles = 0;
+        for (int sg = 0; sg < p.n_seg; sg++) {
+            const int64_t seg_rows = sg == 0 ? rows : extra[sg - 1].rows;
+            p.seg_w[sg] = sg == 0 ? w : extra[sg - 1].w;
+            p.seg_rows[sg] = seg_rows;
+            p.seg_tile0[sg] = (int32_t)n_tiles;
+            n_tiles += (seg_rows + p.tile_rows - 1) / p.tile_rows;
+            if (sg > 0 && (!p.seg_w[sg] || (uintptr_t)p.seg_w[sg] % 16 || !extra[sg - 1].out || seg_rows <= 0)) {
+                *msg = "invalid extra mat-vec segment";
+                return G4A_COMPUTE;
+            }
+        }
         if (n_tiles > INT32_MAX) {
             *msg = "Q8_0 mat-vec too large";
             return G4A_COMPUTE;
         }
+        p.seg_tile0[p.n_seg] = (int32_t)n_tiles;
         p.n_tiles = (int32_t)n_tiles;
         for (int32_t v0 = 0; v0 < n_vec;) {
             int g = std::min<int32_t>(kMaxVec, n_vec - v0);
@@ -499,7 +555,11 @@ int q8_run(int kind, const uint8_t *w, const uint8_t *w2, int64_t rows, int64_t 
             p.xq = xq + (size_t)v0 * cols;
             p.xs = xs + (size_t)v0 * nb;
             p.xf = fused_quant ? x + (size_t)v0 * cols : nullptr;
+            p.pli = pli;
+            p.pli_stride = pli_stride;
             p.out = out + (size_t)v0 * rows;
+            for (int sg = 0; sg < p.n_seg; sg++)
+                p.seg_out[sg] = (sg == 0 ? out : extra[sg - 1].out) + (size_t)v0 * p.seg_rows[sg];
             // as many resident CTAs per SM as shared memory allows (up to 4):
             // more warps hide the shared-memory latency of the block dots
             const size_t smem = Q8Layout(n_mat, g, (int)cols, p.tile_rows).total;
