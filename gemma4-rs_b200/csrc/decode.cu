@@ -877,6 +877,36 @@ __global__ void __launch_bounds__(64) append_kernel(AppendParams p) {
     for (int k = 0; k < PL; k++) store_elem(dst + lane + 32 * k, x[k]);
 }
 
+// The K/V rows of a step's tokens stored before any attention of the step
+// reads them (a prompt chunk holds several positions of one sequence): k-norm
+// and RoPE of K, the unweighted norm of V (model.rs:398-404), the arithmetic
+// of the attention kernels' own append, so the rows are the same bits. One
+// CTA of two warps per task; a task without k_raw (a layer reading another
+// layer's cache) stores nothing. The row is the task's position.
+template <int HD>
+__global__ void __launch_bounds__(64) task_append_kernel(DecodeParams p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int PL = HD / 32;
+    const DecodeTask &tk = p.tasks[blockIdx.x];
+    if (!tk.k_raw) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)tk.seq * p.max_pages : nullptr;
+    const float2 *rope = tk.global ? p.rope_global : p.rope_local;
+    float x[PL];
+    const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
+#pragma unroll
+    for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+    if (warp == 0)
+        norm_rope_warp<HD>(x, tk.k_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+    else
+        norm_rope_warp<HD>(x, nullptr, nullptr, p.eps, lane);
+    float *dst =
+        const_cast<float *>(row_ptr<float>(warp == 0 ? tk.k_base : tk.v_base, bt, p.page_tokens, HD, tk.position));
+#pragma unroll
+    for (int k = 0; k < PL; k++) dst[lane + 32 * k] = x[k];
+}
+
 template <typename KT>
 __global__ void append_any_kernel(AppendParams p) {
     const int row = blockIdx.x;
@@ -991,6 +1021,13 @@ cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cuda
         return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_task_append(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl) {
+    if (n_tasks == 0) return cudaSuccess;
+    if (hd == 256) return launch_k(pdl, task_append_kernel<256>, dim3(n_tasks), dim3(64), 0, s, p);
+    if (hd == 512) return launch_k(pdl, task_append_kernel<512>, dim3(n_tasks), dim3(64), 0, s, p);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_attend_generic(const float *q, const float *k, const float *v, int64_t len, int n_heads, int n_kv,

@@ -306,7 +306,7 @@ __global__ void e2b_plan_kernel(E2bPlanArgs a) {
     ptx::pdl_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     const int n_tasks = a.n_layers * a.n;
-    if (t < a.n) a.best[t] = 0;
+    if (t < a.n_best) a.best[t] = 0;
     if (t < n_tasks) {
         const int l = t / a.n, i = t % a.n;
         const E2bLayerDesc &ld = a.layers[l];
@@ -326,7 +326,7 @@ __global__ void e2b_plan_kernel(E2bPlanArgs a) {
         tk.position = pos;
         tk.lo = lo;
         tk.hi = hi;
-        tk.new_row = ld.owner ? pos : -1;
+        tk.new_row = ld.owner && a.fused_append ? pos : -1;
         tk.n_splits = (hi - lo + a.rows_per_item - 1) / a.rows_per_item;
         tk.partial_base = i * (ld.global ? a.max_splits_global : a.max_splits_local);
         tk.global = ld.global;
@@ -351,6 +351,21 @@ __global__ void e2b_plan_kernel(E2bPlanArgs a) {
     it.row_lo = r0;
     it.row_hi = min(hi, r0 + a.rows_per_item);
     (global ? a.items_global : a.items_local)[v] = it;
+}
+
+// Row rows[blockIdx.x] of xq/xs to row blockIdx.x of xq_out/xs_out; cols is
+// a multiple of 32, so a row is cols/16 16-byte pieces and cols/32 scales.
+__global__ void gather_rows_kernel(const int8_t *__restrict__ xq, const float *__restrict__ xs, int cols,
+                                   const int32_t *__restrict__ rows, int8_t *__restrict__ xq_out,
+                                   float *__restrict__ xs_out) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    const int j = blockIdx.x, r = rows[j];
+    const int4 *src = reinterpret_cast<const int4 *>(xq + (size_t)r * cols);
+    int4 *dst = reinterpret_cast<int4 *>(xq_out + (size_t)j * cols);
+    for (int e = threadIdx.x; e < cols / 16; e += blockDim.x) dst[e] = src[e];
+    for (int e = threadIdx.x; e < cols / kQ8Block; e += blockDim.x)
+        xs_out[(size_t)j * (cols / kQ8Block) + e] = xs[(size_t)r * (cols / kQ8Block) + e];
 }
 
 }  // namespace
@@ -400,6 +415,13 @@ cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, unsigned long 
                        bool pdl) {
     const dim3 grid((unsigned)((vocab + kArgmaxChunk - 1) / kArgmaxChunk), (unsigned)n);
     return launch_k(pdl, argmax_kernel, grid, dim3(256), 0, st, logits, vocab, best);
+}
+
+cudaError_t e2b_gather_rows(const int8_t *xq, const float *xs, int cols, const int32_t *rows, int n, int8_t *xq_out,
+                            float *xs_out, cudaStream_t st, bool pdl) {
+    if (n == 0) return cudaSuccess;
+    if (cols % kQ8Block) return cudaErrorInvalidValue;
+    return launch_k(pdl, gather_rows_kernel, dim3(n), dim3(kRowThreads), 0, st, xq, xs, cols, rows, xq_out, xs_out);
 }
 
 cudaError_t e2b_plan(const E2bPlanArgs &a, cudaStream_t st) {

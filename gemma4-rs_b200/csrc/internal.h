@@ -112,6 +112,9 @@ cudaError_t launch_decode(const DecodeParams &p, int hd, int kv_f16, bool fast, 
 constexpr int kExactMaxRows = 4096;
 constexpr int kExactRowsPerItem = 32;
 cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl = false);
+// K/V rows of tasks 0..n_tasks-1 (norms, RoPE at the task's position, stored
+// at that row) ahead of an attention launch whose tasks have new_row = -1.
+cudaError_t launch_task_append(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl = false);
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
 constexpr size_t kQBlockBytes = 16 * 512 * 2;  // q hi/lo block of one task (f16 kernel)
@@ -178,7 +181,9 @@ struct E2bPlanArgs {
     float *att;
     DecodeTask *tasks;  // [n_layers][task_stride]
     DecodeItem *items_local, *items_global;
-    unsigned long long *best;  // [n] argmax slots, zeroed here
+    unsigned long long *best;  // [n_best] argmax slots, zeroed here
+    int32_t n_best;
+    int32_t fused_append;      // 1: each attention task stores its token's K/V row; 0: stored before
 };
 cudaError_t e2b_synth_q8(void *dst, int64_t n_blocks, uint64_t seed, uint64_t tensor, float sigma, cudaStream_t st);
 cudaError_t e2b_synth_norm(float *dst, int64_t n, uint64_t seed, uint64_t tensor, float center, float spread,
@@ -194,6 +199,11 @@ cudaError_t e2b_gelu_quant(const float *gate, const float *pli, int layer, int L
 cudaError_t e2b_argmax(const float *logits, int64_t vocab, int n, unsigned long long *best, cudaStream_t st,
                        bool pdl = false);
 cudaError_t e2b_plan(const E2bPlanArgs &a, cudaStream_t st);
+// Rows rows[j] of the quantized activations xq [.][cols] / xs [.][cols/32]
+// copied to row j of xq_out / xs_out, j < n (the rows whose logits a step
+// returns).
+cudaError_t e2b_gather_rows(const int8_t *xq, const float *xs, int cols, const int32_t *rows, int n, int8_t *xq_out,
+                            float *xs_out, cudaStream_t st, bool pdl = false);
 
 struct PrefillScratch;
 PrefillScratch *prefill_scratch_new();

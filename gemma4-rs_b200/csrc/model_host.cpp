@@ -1,7 +1,10 @@
 // Host side of the E2B decoder (include/g4attn.h, g4a_model_*): one token per
 // sequence through embed, the 35 layers and the logits of
 // crates/llm-gemma4/src/impl_/model.rs:252-449, and the prompt-then-greedy
-// loop of generate.rs:15-64, for many sequences at once.
+// loop of generate.rs:15-64, for many sequences at once. A prompt goes
+// through in chunks of many positions per step (rows), each row's arithmetic
+// the same as in a one-token step, so the result does not depend on the
+// chunking.
 //
 // A step is one fixed sequence of launches on the model's own stream (about
 // 16 per layer): the attention plan, embedding, per-layer inputs, then per
@@ -33,6 +36,7 @@ struct g4a_model {
     g4a_ctx *ctx = nullptr;
     g4a_model_weights w{};
     int32_t S = 0, T = 0;  // max sequences, max positions per sequence
+    int32_t R = 0;         // max rows (tokens) of one step: S, or more for prompt chunks
     int32_t L = 0, d = 0, d_ff = 0, ple = 0, vocab = 0, hd_max = 0, qd_max = 0, cmax = 0;
     int32_t rows_per_item = 64, ms_local = 1, ms_global = 1;
     bool exact = true;  // attention in the reference's order (one CTA per task); up to kExactMaxRows positions
@@ -40,14 +44,16 @@ struct g4a_model {
     cudaStream_t st = nullptr;
     cudaEvent_t ev = nullptr;
     std::vector<void *> allocs;
-    int32_t *d_in = nullptr;  // [3][S]: sequence ids, tokens, positions
-    int32_t *h_in = nullptr;              // pinned [3][S]
+    // a step of n rows and n_out result rows: sequence ids [n], tokens [n],
+    // positions [n], the rows whose logits are returned [n_out]
+    int32_t *d_in = nullptr;  // [3R + S]
+    int32_t *h_in = nullptr;              // pinned [3R + S]
     unsigned long long *h_out = nullptr;  // pinned [S]: the argmax slots (index in the low 32 bits)
     int32_t *h_err = nullptr;             // pinned: the device error flags after the step
     float *x = nullptr, *y = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
     float *gate = nullptr, *gated = nullptr, *P = nullptr, *pli = nullptr, *logits = nullptr;
-    int8_t *xq = nullptr;
-    float *xs = nullptr;
+    int8_t *xq = nullptr, *xq_out = nullptr;  // xq_out/xs_out: the head's input rows of a prompt chunk
+    float *xs = nullptr, *xs_out = nullptr;
     E2bLayerDesc *d_layers = nullptr;
     DecodeTask *d_tasks = nullptr;
     DecodeItem *d_items_local = nullptr, *d_items_global = nullptr;
@@ -63,6 +69,11 @@ struct g4a_model {
 };
 
 namespace {
+
+// Rows of a prompt chunk (all sequences' positions together): enough for the
+// batched Q8_0 kernel to reach its weight-streaming rate, a few hundred MB
+// of activations.
+constexpr int64_t kChunkRows = 2048;
 
 template <typename T>
 T *dalloc(g4a_model *m, size_t n) {
@@ -110,19 +121,24 @@ int mv(g4a_model *m, int kind, const uint8_t *w, const uint8_t *w2, int64_t rows
         if (e_ != cudaSuccess) return cuda_fail(m->ctx, e_, #call);       \
     } while (0)
 
-// The kernels of one step for rows 0..n-1 of d_in.
-int enqueue_step(g4a_model *m, int32_t n) {
+// The kernels of one step over the n rows of d_in. A decode step (chunk
+// false) has one row per sequence, and each attention task stores its own
+// token's K/V row; its logits are every row's. A prompt chunk (chunk true)
+// may hold several positions of a sequence: all K/V rows are stored first,
+// and the logits are those of the n_out rows listed after the positions
+// (none for a chunk that does not end a prompt).
+int enqueue_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
     g4a_ctx *ctx = m->ctx;
     const g4a_model_weights &w = m->w;
     const float eps = ctx->hp.rms_norm_eps;
-    const int32_t *d_seq = m->d_in, *d_tok = m->d_in + m->S, *d_pos = m->d_in + 2 * m->S;
+    const int32_t *d_seq = m->d_in, *d_tok = m->d_in + n, *d_pos = m->d_in + 2 * n, *d_sel = m->d_in + 3 * n;
     const int d = m->d, L = m->L, ple = m->ple;
 
     E2bPlanArgs pa{};
     pa.layers = m->d_layers;
     pa.n_layers = L;
     pa.n = n;
-    pa.task_stride = m->S;
+    pa.task_stride = m->R;
     pa.seqs = d_seq;
     pa.pos = d_pos;
     pa.max_tokens = m->T;
@@ -138,6 +154,8 @@ int enqueue_step(g4a_model *m, int32_t n) {
     pa.items_local = m->d_items_local;
     pa.items_global = m->d_items_global;
     pa.best = m->d_best;
+    pa.n_best = n_out;
+    pa.fused_append = chunk ? 0 : 1;
     MODEL_TRY(e2b_plan(pa, m->st));
 
     // embed (model.rs:376-384) and per-layer inputs (:252-270)
@@ -168,7 +186,7 @@ int enqueue_step(g4a_model *m, int32_t n) {
         }
         // q/k/v norms, RoPE, append, window and attention (:394-410)
         DecodeParams p{};
-        p.tasks = m->d_tasks + (size_t)l * m->S;
+        p.tasks = m->d_tasks + (size_t)l * m->R;
         p.items = m->global[l] ? m->d_items_global : m->d_items_local;
         p.block_table = nullptr;
         p.page_tokens = 1;
@@ -180,6 +198,7 @@ int enqueue_step(g4a_model *m, int32_t n) {
         p.tickets = m->tickets;
         p.err_flag = ctx->d_err;
         p.n_items = n * (m->global[l] ? m->ms_global : m->ms_local);
+        if (chunk && owner) MODEL_TRY(launch_task_append(p, hd, n, m->st, m->pdl));
         if (m->exact) {
             p.max_rows = m->T;
             p.scores = m->scores;
@@ -215,32 +234,48 @@ int enqueue_step(g4a_model *m, int32_t n) {
         }
     }
     // logits (:438-449) and greedy sampling (sample.rs:27-36)
-    if ((rc = mv(m, 2, w.token_embd, nullptr, m->vocab, d, nullptr, n, w.final_logit_softcap, m->logits))) return rc;
-    MODEL_TRY(e2b_argmax(m->logits, m->vocab, n, m->d_best, m->st, m->pdl));
+    if (!chunk) {
+        if ((rc = mv(m, 2, w.token_embd, nullptr, m->vocab, d, nullptr, n, w.final_logit_softcap, m->logits)))
+            return rc;
+    } else if (n_out > 0) {
+        MODEL_TRY(e2b_gather_rows(m->xq, m->xs, d, d_sel, n_out, m->xq_out, m->xs_out, m->st, m->pdl));
+        const char *msg = "";
+        rc = q8_run(2, w.token_embd, nullptr, m->vocab, d, nullptr, n_out, w.final_logit_softcap, m->logits,
+                    m->xq_out, m->xs_out, ctx->d_err, ctx->n_sm, m->st, &msg, m->pdl);
+        if (rc) return fail(ctx, rc, "compute: %s", msg);
+    }
+    if (n_out > 0) MODEL_TRY(e2b_argmax(m->logits, m->vocab, n_out, m->d_best, m->st, m->pdl));
     return G4A_OK;
 }
 
 // Upload of the step's inputs, the step, download of its tokens and flags.
-int record_step(g4a_model *m, int32_t n) {
-    MODEL_TRY(cudaMemcpyAsync(m->d_in, m->h_in, 3 * (size_t)m->S * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
-    const int rc = enqueue_step(m, n);
+int record_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
+    const size_t n_in = 3 * (size_t)n + (chunk ? n_out : 0);
+    MODEL_TRY(cudaMemcpyAsync(m->d_in, m->h_in, n_in * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+    const int rc = enqueue_step(m, n, n_out, chunk);
     if (rc) return rc;
-    MODEL_TRY(cudaMemcpyAsync(m->h_out, m->d_best, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
-                              m->st));
+    if (n_out > 0)
+        MODEL_TRY(cudaMemcpyAsync(m->h_out, m->d_best, (size_t)n_out * sizeof(unsigned long long),
+                                  cudaMemcpyDeviceToHost, m->st));
     MODEL_TRY(cudaMemcpyAsync(m->h_err, m->ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
     return G4A_OK;
 }
 
-int run_step(g4a_model *m, int32_t n) {
+// A decode step of n sequences: eager the first time a size is seen, then
+// captured, then one graph launch per step of that size. Prompt chunks are
+// eager (their row counts vary and each runs once per prompt).
+int run_step(g4a_model *m, int32_t n, int32_t n_out = -1, bool chunk = false) {
+    if (chunk) return record_step(m, n, n_out, true);
+    n_out = n;
     auto it = m->graphs.find(n);
     if (it != m->graphs.end()) {
         MODEL_TRY(cudaGraphLaunch(it->second, m->st));
         return G4A_OK;
     }
-    if (!m->use_graphs || m->eager_runs[n]++ == 0) return record_step(m, n);  // first step of a size: eager
+    if (!m->use_graphs || m->eager_runs[n]++ == 0) return record_step(m, n, n_out, false);  // first of a size: eager
     cudaGraph_t g = nullptr;
     MODEL_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    const int rc = record_step(m, n);
+    const int rc = record_step(m, n, n_out, false);
     const cudaError_t e = cudaStreamEndCapture(m->st, &g);
     if (rc || e != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -355,35 +390,45 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
     // across CTAs (split-KV, within the decode tolerance).
     m->exact = max_tokens <= kExactMaxRows;
     if (m->exact) m->rows_per_item = kExactRowsPerItem;
-    const int32_t R = m->rows_per_item;
-    m->ms_local = (std::min(hp.sliding_window, max_tokens) + R - 1) / R;
-    m->ms_global = (max_tokens + R - 1) / R;
+    const int32_t per_item = m->rows_per_item;
+    m->ms_local = (std::min(hp.sliding_window, max_tokens) + per_item - 1) / per_item;
+    m->ms_global = (max_tokens + per_item - 1) / per_item;
     const int32_t ms = std::max(m->ms_local, m->ms_global);
     const size_t S = (size_t)max_seqs;
+    // Rows of a step: a prompt chunk takes up to kChunkRows positions (all
+    // sequences' together; G4A_CHUNK_ROWS=<n> in the environment sets
+    // another bound) in exact mode; the split-KV path keeps one partial
+    // buffer per sequence, so its steps hold S rows.
+    int64_t chunk_rows = kChunkRows;
+    if (const char *cr = std::getenv("G4A_CHUNK_ROWS")) chunk_rows = std::max(1L, std::strtol(cr, nullptr, 10));
+    m->R = m->exact ? (int32_t)std::max<int64_t>(max_seqs, std::min<int64_t>(chunk_rows, (int64_t)max_seqs * max_tokens))
+                    : max_seqs;
+    const size_t R = (size_t)m->R;
 
     bool ok = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) == cudaSuccess &&
               cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming) == cudaSuccess &&
-              cudaHostAlloc(reinterpret_cast<void **>(&m->h_in), 3 * S * sizeof(int32_t), cudaHostAllocDefault) ==
-                  cudaSuccess &&
+              cudaHostAlloc(reinterpret_cast<void **>(&m->h_in), (3 * R + S) * sizeof(int32_t),
+                            cudaHostAllocDefault) == cudaSuccess &&
               cudaHostAlloc(reinterpret_cast<void **>(&m->h_out), S * sizeof(unsigned long long),
                             cudaHostAllocDefault) == cudaSuccess &&
               cudaHostAlloc(reinterpret_cast<void **>(&m->h_err), sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
     if (ok) {
-        ok = (m->d_in = dalloc<int32_t>(m, 3 * S)) &&
-             (m->x = dalloc<float>(m, S * m->d)) && (m->y = dalloc<float>(m, S * m->d)) &&
-             (m->q = dalloc<float>(m, S * m->qd_max)) && (m->att = dalloc<float>(m, S * m->qd_max)) &&
-             (m->k = dalloc<float>(m, S * m->hd_max)) && (m->v = dalloc<float>(m, S * m->hd_max)) &&
-             (m->gated = dalloc<float>(m, S * m->d_ff)) && (m->gate = dalloc<float>(m, S * std::max(m->ple, 1))) &&
-             (m->P = dalloc<float>(m, S * m->L * std::max(m->ple, 1))) &&
-             (m->pli = dalloc<float>(m, S * m->L * std::max(m->ple, 1))) &&
-             (m->logits = dalloc<float>(m, S * m->vocab)) && (m->xq = dalloc<int8_t>(m, S * m->cmax)) &&
-             (m->xs = dalloc<float>(m, S * m->cmax / 32)) && (m->d_layers = dalloc<E2bLayerDesc>(m, m->L)) &&
-             (m->d_tasks = dalloc<DecodeTask>(m, (size_t)m->L * S)) &&
-             (m->d_items_local = dalloc<DecodeItem>(m, S * m->ms_local)) &&
-             (m->d_items_global = dalloc<DecodeItem>(m, S * m->ms_global)) &&
-             (m->part_o = dalloc<float>(m, S * ms * kHeads * m->hd_max)) &&
-             (m->part_ml = dalloc<float>(m, S * ms * 2 * kHeads)) && (m->tickets = dalloc<unsigned>(m, S)) &&
-             (m->scores = dalloc<float>(m, m->exact ? S * kHeads * max_tokens : 1)) &&
+        ok = (m->d_in = dalloc<int32_t>(m, 3 * R + S)) &&
+             (m->x = dalloc<float>(m, R * m->d)) && (m->y = dalloc<float>(m, R * m->d)) &&
+             (m->q = dalloc<float>(m, R * m->qd_max)) && (m->att = dalloc<float>(m, R * m->qd_max)) &&
+             (m->k = dalloc<float>(m, R * m->hd_max)) && (m->v = dalloc<float>(m, R * m->hd_max)) &&
+             (m->gated = dalloc<float>(m, R * m->d_ff)) && (m->gate = dalloc<float>(m, R * std::max(m->ple, 1))) &&
+             (m->P = dalloc<float>(m, R * m->L * std::max(m->ple, 1))) &&
+             (m->pli = dalloc<float>(m, R * m->L * std::max(m->ple, 1))) &&
+             (m->logits = dalloc<float>(m, S * m->vocab)) && (m->xq = dalloc<int8_t>(m, R * m->cmax)) &&
+             (m->xs = dalloc<float>(m, R * m->cmax / 32)) && (m->xq_out = dalloc<int8_t>(m, S * m->d)) &&
+             (m->xs_out = dalloc<float>(m, S * m->d / 32)) && (m->d_layers = dalloc<E2bLayerDesc>(m, m->L)) &&
+             (m->d_tasks = dalloc<DecodeTask>(m, (size_t)m->L * R)) &&
+             (m->d_items_local = dalloc<DecodeItem>(m, R * m->ms_local)) &&
+             (m->d_items_global = dalloc<DecodeItem>(m, R * m->ms_global)) &&
+             (m->part_o = dalloc<float>(m, R * ms * kHeads * m->hd_max)) &&
+             (m->part_ml = dalloc<float>(m, R * ms * 2 * kHeads)) && (m->tickets = dalloc<unsigned>(m, R)) &&
+             (m->scores = dalloc<float>(m, m->exact ? R * kHeads * max_tokens : 1)) &&
              (m->d_best = dalloc<unsigned long long>(m, S));
     }
     // K/V caches of the owner layers: [max_seqs][max_tokens][hd] f32 each
@@ -416,7 +461,7 @@ extern "C" int g4a_model_create(g4a_ctx *ctx, const g4a_model_weights *w, int32_
         desc[l].owner = m->source[l] == l;
     }
     cudaError_t e = cudaMemcpy(m->d_layers, desc.data(), desc.size() * sizeof(E2bLayerDesc), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset(m->tickets, 0, S * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(m->tickets, 0, R * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         g4a_model_destroy(m);
@@ -439,43 +484,101 @@ extern "C" int g4a_model_len(const g4a_model *m, int32_t seq, int32_t *len) {
     return G4A_OK;
 }
 
-extern "C" int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t *next) {
-    if (!m) return G4A_COMPUTE;
+namespace {
+
+// Runs a step whose inputs are in h_in, after the caller's work on the
+// context's stream, and reads its flags.
+int submit(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
     g4a_ctx *ctx = m->ctx;
-    cudaSetDevice(ctx->device);
-    if (n < 1 || n > m->S || !seq_ids || !tokens)
-        return fail(ctx, G4A_COMPUTE, "compute: step of %d sequences (capacity %d)", n, m->S);
-    std::vector<char> used(m->S, 0);
-    for (int i = 0; i < n; i++) {
-        const int32_t s = seq_ids[i];
-        if (s < 0 || s >= m->S || used[s]) return fail(ctx, G4A_COMPUTE, "compute: bad or repeated sequence id %d", s);
-        used[s] = 1;
-        if (tokens[i] < 0 || tokens[i] >= m->vocab)  // model.rs:378
-            return fail(ctx, G4A_COMPUTE, "compute: token %d exceeds vocabulary", tokens[i]);
-        if (m->len[s] >= m->T)  // ContextMemory::view past capacity
-            return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", m->len[s] + 1, m->T);
-    }
-    for (int i = 0; i < n; i++) {
-        m->h_in[i] = seq_ids[i];
-        m->h_in[m->S + i] = tokens[i];
-        m->h_in[2 * m->S + i] = m->len[seq_ids[i]];
-    }
-    G4A_CUDA_TRY(ctx, cudaEventRecord(m->ev, ctx->stream));  // after the caller's work on the context
+    G4A_CUDA_TRY(ctx, cudaEventRecord(m->ev, ctx->stream));
     G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(m->st, m->ev, 0));
-    const int rc = run_step(m, n);
+    const int rc = run_step(m, n, n_out, chunk);
     if (rc) {
         cudaStreamSynchronize(m->st);
         return rc;
     }
     G4A_CUDA_TRY(ctx, cudaStreamSynchronize(m->st));
-    m->last_n = n;
+    m->last_n = n_out;
     const int32_t flags = *m->h_err;
     if (flags) {
         cudaMemset(ctx->d_err, 0, sizeof(int));
         if (flags & 1) return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
         return fail(ctx, G4A_TIMEOUT, "compute: a device wait timed out (flags %d)", flags);
     }
+    return G4A_OK;
+}
+
+// Sequence ids distinct and in range; tokens in the vocabulary (model.rs:378);
+// room for `adding` more positions in every sequence.
+int check_batch(g4a_model *m, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int64_t n_tokens,
+                int32_t adding) {
+    g4a_ctx *ctx = m->ctx;
+    std::vector<char> used(m->S, 0);
+    for (int i = 0; i < n; i++) {
+        const int32_t s = seq_ids[i];
+        if (s < 0 || s >= m->S || used[s]) return fail(ctx, G4A_COMPUTE, "compute: bad or repeated sequence id %d", s);
+        used[s] = 1;
+        if ((int64_t)m->len[s] + adding > m->T)  // ContextMemory::view past capacity
+            return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %lld, max %d",
+                        (long long)m->len[s] + adding, m->T);
+    }
+    for (int64_t i = 0; i < n_tokens; i++)
+        if (tokens[i] < 0 || tokens[i] >= m->vocab)
+            return fail(ctx, G4A_COMPUTE, "compute: token %d exceeds vocabulary", tokens[i]);
+    return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t *next) {
+    if (!m) return G4A_COMPUTE;
+    g4a_ctx *ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    if (n < 1 || n > m->S || !seq_ids || !tokens)
+        return fail(ctx, G4A_COMPUTE, "compute: step of %d sequences (capacity %d)", n, m->S);
+    int rc = check_batch(m, n, seq_ids, tokens, n, 1);
+    if (rc) return rc;
+    for (int i = 0; i < n; i++) {
+        m->h_in[i] = seq_ids[i];
+        m->h_in[n + i] = tokens[i];
+        m->h_in[2 * n + i] = m->len[seq_ids[i]];
+    }
+    if ((rc = submit(m, n, n, false))) return rc;
     for (int i = 0; i < n; i++) m->len[seq_ids[i]]++;
+    if (next)
+        for (int i = 0; i < n; i++) next[i] = (int32_t)(m->h_out[i] & 0xFFFFFFFFull);
+    return G4A_OK;
+}
+
+extern "C" int g4a_model_prefill(g4a_model *m, int32_t n, const int32_t *seq_ids, const int32_t *tokens, int32_t len,
+                                 int32_t *next) {
+    if (!m) return G4A_COMPUTE;
+    g4a_ctx *ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    if (n < 1 || n > m->S || len < 1 || !seq_ids || !tokens)
+        return fail(ctx, G4A_COMPUTE, "compute: prompt of %d tokens for %d sequences (capacity %d)", len, n, m->S);
+    int rc = check_batch(m, n, seq_ids, tokens, (int64_t)n * len, len);
+    if (rc) return rc;
+    // chunks of C positions of every sequence, rows sequence-major
+    const int32_t C = std::max<int32_t>(1, m->R / n);
+    for (int32_t c0 = 0; c0 < len; c0 += C) {
+        const int32_t cl = std::min(C, len - c0), rows = n * cl;
+        const bool last = c0 + cl == len;
+        for (int i = 0; i < n; i++) {
+            const int32_t s = seq_ids[i];
+            for (int j = 0; j < cl; j++) {
+                const int32_t r = i * cl + j;
+                m->h_in[r] = s;
+                m->h_in[rows + r] = tokens[(size_t)i * len + c0 + j];
+                m->h_in[2 * rows + r] = m->len[s] + j;
+            }
+            m->h_in[3 * rows + i] = i * cl + cl - 1;  // the sequence's last row of the chunk
+        }
+        // one position per sequence: a decode step (its graph)
+        rc = cl == 1 ? submit(m, n, n, false) : submit(m, rows, last ? n : 0, true);
+        if (rc) return rc;
+        for (int i = 0; i < n; i++) m->len[seq_ids[i]] += cl;
+    }
     if (next)
         for (int i = 0; i < n; i++) next[i] = (int32_t)(m->h_out[i] & 0xFFFFFFFFull);
     return G4A_OK;
@@ -503,10 +606,9 @@ extern "C" int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompt
         m->len[i] = 0;  // clear_context
     }
     int rc;
-    for (int t = 0; t < prompt_len; t++) {  // generate.rs:38-42
-        for (int i = 0; i < n; i++) tok[i] = prompts[(size_t)i * prompt_len + t];
-        if ((rc = g4a_model_step(m, n, ids.data(), tok.data(), next.data()))) return rc;
-    }
+    // the prompt (generate.rs:38-42, one position per forward pass there) in
+    // chunks of many positions; the same logits
+    if ((rc = g4a_model_prefill(m, n, ids.data(), prompts, prompt_len, next.data()))) return rc;
     for (int index = 0; index < max_new; index++) {  // generate.rs:45-70
         if (prompt_len + index >= max_context)
             return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", prompt_len + index + 1,

@@ -197,6 +197,20 @@ class Model:
         self._n = n
         return list(nxt)
 
+    def prefill(self, seq_ids, tokens) -> list[int]:
+        """A prompt per sequence, tokens [n][len], appended at each sequence's
+        length in chunks of many positions; returns the greedy token after
+        each prompt (logits() then gives those n rows)."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        n, length = tokens.shape
+        if len(seq_ids) != n:
+            raise ValueError("one prompt per sequence id")
+        ids = (ctypes.c_int32 * n)(*seq_ids)
+        nxt = (ctypes.c_int32 * n)()
+        self.ctx.check(lib.g4a_model_prefill(self.h, n, ids, tokens.ctypes.data_as(_i32p), length, nxt))
+        self._n = n
+        return list(nxt)
+
     def logits(self):
         """A copy of the last step's soft-capped logits, torch [n][vocab] on the device."""
         import torch

@@ -332,6 +332,18 @@ int g4a_model_len(const g4a_model *m, int32_t seq, int32_t *len);
  * step is done. G4A_CONTEXT_TOO_LONG when a sequence is full. */
 int g4a_model_step(g4a_model *m, int32_t n, const int32_t *seq_ids_host, const int32_t *tokens_host,
                    int32_t *next_host);
+/* A prompt of `len` tokens for each of n sequences (tokens_host [n][len]),
+ * appended at each sequence's length. The reference feeds a prompt through
+ * transformer::prefill one token per call (transformer.rs:40-52 from
+ * generate.rs:38-42); here a step takes many positions (up to a few
+ * thousand rows over all sequences), every row computed as in a one-token
+ * step, so the caches and logits are those of len g4a_model_step calls.
+ * next_host (optional) receives each sequence's greedy token after its last
+ * prompt token, and g4a_model_logits then gives those n rows. On an error
+ * the chunks already done stay in the caches (g4a_model_len tells how
+ * far). */
+int g4a_model_prefill(g4a_model *m, int32_t n, const int32_t *seq_ids_host, const int32_t *tokens_host, int32_t len,
+                      int32_t *next_host);
 /* ContextMemory::view (context_memory.rs:53-69) of the model's cache: rows
  * [0, len) of `layer`'s K/V source for one sequence, [len][head_dim] f32
  * each, copied into caller device buffers on the context's stream. */
@@ -340,8 +352,8 @@ int g4a_model_kv_view(const g4a_model *m, int32_t seq, int32_t layer, int32_t le
 /* Device pointer to the soft-capped logits of the last step, [n][vocab]. */
 int g4a_model_logits(g4a_model *m, const float **logits_dev);
 /* generate_cpu (generate.rs:15-64) with greedy sampling for sequences
- * 0..n-1 at once: clears them, feeds the prompts [n][prompt_len] token by
- * token, then samples max_new tokens each into out_host [n][max_new]
+ * 0..n-1 at once: clears them, feeds the prompts [n][prompt_len] through
+ * g4a_model_prefill (the same logits as token by token), then samples max_new tokens each into out_host [n][max_new]
  * (the last one is not fed back). max_context bounds prompt + generated as
  * the reference's max_context does. */
 int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompts_host, int32_t prompt_len, int32_t max_new,

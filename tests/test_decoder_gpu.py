@@ -204,6 +204,99 @@ def test_generate_matches_oracle(ctx, small_vocab):
     m.close()
 
 
+def test_prefill_chunks_match_steps_and_oracle(ctx, small_vocab, oracle, monkeypatch):
+    """g4a_model_prefill in chunks of many positions (rows bounded to 14 here,
+    so two prompts go through as chunks of 7, 7, ..., 5 positions, and one
+    prompt continues a sequence that already holds 5 tokens): the caches
+    are bit-identical to token-by-token steps of the same tokens, and the
+    logits after each prompt and of the steps that follow are the oracle's
+    bit for bit."""
+    import g4attn.model as gm
+    w, make = small_vocab
+    monkeypatch.setenv("G4A_CHUNK_ROWS", "14")
+    m = gm.Model(ctx, w, max_seqs=4, max_tokens=96)
+    r = rng(17)
+    p0, p1 = r.integers(0, w.vocab, 40).astype(np.int32), r.integers(0, w.vocab, 40).astype(np.int32)
+    head = [int(t) for t in r.integers(0, w.vocab, 5)]
+    for t in head:  # sequence 1 holds 5 tokens before its prompt
+        m.step([1], [t])
+    nxt = m.prefill([0, 1], np.stack([p0, p1]))
+    assert [m.len(0), m.len(1)] == [40, 45]
+    got = m.logits().cpu().numpy()
+    decs = [make(), make()]
+    seqs = [p0.tolist(), head + p1.tolist()]
+    stats = {"max_diff": 0.0, "bit_identical": 0, "top1_agree": 0, "steps": 0}
+    for i in range(2):
+        for p, t in enumerate(seqs[i][:-1]):
+            decs[i].forward(t, p)
+        compare_step(got[i], decs[i].forward(seqs[i][-1], len(seqs[i]) - 1), nxt[i], stats, oracle)
+    # the same tokens step by step in sequences 2 and 3: the same K/V rows
+    for t in p0:
+        m.step([2], [int(t)])
+    for t in seqs[1]:
+        m.step([3], [int(t)])
+    for layer in (0, 4, 13, 14):
+        for a, b, n in ((0, 2, 40), (1, 3, 45)):
+            ka, va = m.kv_view(a, layer, n)
+            kb, vb = m.kv_view(b, layer, n)
+            assert ka.cpu().numpy().tobytes() == kb.cpu().numpy().tobytes(), (layer, a)
+            assert va.cpu().numpy().tobytes() == vb.cpu().numpy().tobytes(), (layer, a)
+    # decoding continues from the chunked caches
+    cur = list(nxt)
+    for _ in range(6):
+        nxt = m.step([0, 1], cur)
+        logits = m.logits().cpu().numpy()
+        for i in range(2):
+            compare_step(logits[i], decs[i].forward(cur[i], m.len(i) - 1), nxt[i], stats, oracle)
+        cur = list(nxt)
+    print(f"chunked prefill vs oracle: {stats}")
+    check(stats)
+    m.close()
+
+
+def test_prefill_one_position_chunks(ctx, small_vocab, monkeypatch):
+    """Rows for only one position per sequence: each chunk is a decode step
+    (its captured graph); the tokens are those of the many-position chunks."""
+    import g4attn.model as gm
+    w, _ = small_vocab
+    prompts = rng(18).integers(0, w.vocab, (3, 9)).astype(np.int32)
+    monkeypatch.setenv("G4A_CHUNK_ROWS", "4")
+    m1 = gm.Model(ctx, w, max_seqs=3, max_tokens=16)
+    a = m1.prefill([0, 1, 2], prompts)
+    la = m1.logits().cpu().numpy()
+    m1.close()
+    monkeypatch.delenv("G4A_CHUNK_ROWS")
+    m2 = gm.Model(ctx, w, max_seqs=3, max_tokens=16)
+    b = m2.prefill([2, 0, 1], prompts[[2, 0, 1]])
+    lb = m2.logits().cpu().numpy()
+    m2.close()
+    assert a == [b[1], b[2], b[0]]
+    assert la.tobytes() == lb[[1, 2, 0]].tobytes()
+
+
+def test_prefill_past_the_window(ctx, small_vocab, oracle):
+    """A 600-token prompt in one chunk: the local layers' rows attend their
+    512-row window (eng/mod.rs:10-36), the global ones all rows; the logits
+    after the prompt and of the next steps are the oracle's bit for bit."""
+    import g4attn.model as gm
+    w, make = small_vocab
+    m = gm.Model(ctx, w, max_seqs=1, max_tokens=640)
+    prompt = rng(19).integers(0, w.vocab, 600).astype(np.int32)
+    nxt = m.prefill([0], prompt[None, :])[0]
+    dec = make()
+    for p, t in enumerate(prompt[:-1].tolist()):
+        dec.forward(t, p)
+    stats = {"max_diff": 0.0, "bit_identical": 0, "top1_agree": 0, "steps": 0}
+    compare_step(m.logits().cpu().numpy()[0], dec.forward(int(prompt[-1]), 599), nxt, stats, oracle)
+    for p in range(600, 603):
+        tok = nxt
+        nxt = m.step([0], [tok])[0]
+        compare_step(m.logits().cpu().numpy()[0], dec.forward(tok, p), nxt, stats, oracle)
+    print(f"600-token prefill vs oracle: {stats}")
+    check(stats)
+    m.close()
+
+
 def test_full_e2b_top1(ctx, oracle):
     """Config 4's model at full size (vocab 262,144, 3.9 GB of Q8_0 weights):
     a 19-token prompt and greedy steps, logits against the oracle."""
@@ -248,6 +341,19 @@ def test_errors(ctx, small_vocab, torch_cuda):
     with pytest.raises(g4attn.EngError) as e:
         m.generate(np.zeros((1, 5), np.int32), 2, max_context=4)
     assert e.value.code == g4attn.CONTEXT_TOO_LONG
+    m.clear(0)
+    with pytest.raises(g4attn.EngError) as e:  # a prompt past the capacity: nothing runs
+        m.prefill([0], np.zeros((1, 4), np.int32))
+    assert e.value.code == g4attn.CONTEXT_TOO_LONG and "got 4, max 3" in e.value.message
+    with pytest.raises(g4attn.EngError) as e:
+        m.prefill([0], np.full((1, 2), w.vocab, np.int32))
+    assert e.value.code == g4attn.COMPUTE and "exceeds vocabulary" in e.value.message
+    with pytest.raises(g4attn.EngError) as e:
+        m.prefill([0, 0], np.zeros((2, 2), np.int32))
+    assert e.value.code == g4attn.COMPUTE
+    assert m.len(0) == 0
+    m.prefill([0], np.zeros((1, 3), np.int32))
+    assert m.len(0) == 3
     m.close()
     missing = gm.Weights(w.hp, w.vocab, w.d_model, w.d_ff, w.ple_dim, w.softcap)
     missing.tensors = dict(w.tensors)
