@@ -13,8 +13,8 @@ balanced by K/V bytes), with no collective on the data path.
 The same line carries:
   * roofline  — achieved HBM bandwidth of the dominant kernel (the global
     layer's decode kernel) from CUDA events around each of its launches;
-  * e2e       — the same metric through the public C ABI (g4a_decode) with
-    host inputs copied in and results copied out every step;
+  * e2e       — the same metric through the public C ABI (g4a_decode_host)
+    with host inputs copied in and results copied out every step;
   * cpu_baseline — the reference's attention path restated in C (the oracle
     port, pool.rs-shaped thread pool) timed on this host;
   * decode_batch1 — configuration 0 (batch 1, context 628) latency;
@@ -290,14 +290,20 @@ def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, devic
         pin[layer]["out"] = torch.empty_like(a["out"], device="cpu").pin_memory()
     h2d = sum(t.numel() * 4 for layer in pin for k, t in pin[layer].items() if k != "out")
     d2h = sum(pin[layer]["out"].numel() * 4 for layer in pin)
-    # untimed warm-up of this API: its first calls in a process load kernels
-    # and allocate the pinned staging slots
+    # g4a_decode_host: the caller's page-locked q/k/v in, the step, the
+    # attention output back in host memory, one C call per step
+    host_args = g4a.DecodeHostArgs([dict(layer=layer, q_raw=pin[layer]["q_raw"], k_raw=pin[layer]["k_raw"],
+                                         v_raw=pin[layer]["v_raw"], q_norm_w=args[layer]["q_norm_w"],
+                                         k_norm_w=args[layer]["k_norm_w"], out=pin[layer]["out"])
+                                    for layer in (LOCAL_LAYER, GLOBAL_LAYER)])
+    # untimed warm-up of this API: its first calls in a process allocate its
+    # device slots and pinned staging
     e2e_warm = 3
+    pos_np = np.asarray(positions, np.int32)
     with torch.cuda.stream(stream):
         for k in range(e2e_warm):
-            ctx.decode(kv, [args[LOCAL_LAYER], args[GLOBAL_LAYER]], seqs, [p + 1 + k for p in positions])
-        stream.synchronize()
-    positions = [p + e2e_warm for p in positions]
+            ctx.decode_host(kv, host_args, seqs, pos_np + 1 + k)
+    pos_np = pos_np + e2e_warm
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -306,14 +312,9 @@ def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, devic
     with torch.cuda.stream(stream):
         e_start.record(stream)
         for k in range(e2e_steps):
-            for layer in (LOCAL_LAYER, GLOBAL_LAYER):
-                for name in ("q_raw", "k_raw", "v_raw"):
-                    args[layer][name].copy_(pin[layer][name], non_blocking=True)
-            pos = [p + 1 + k for p in positions]  # each call appends: the context advances
-            ctx.decode(kv, [args[LOCAL_LAYER], args[GLOBAL_LAYER]], seqs, pos)
-            for layer in (LOCAL_LAYER, GLOBAL_LAYER):
-                pin[layer]["out"].copy_(args[layer]["out"], non_blocking=True)
-            stream.synchronize()  # the caller reads this step's attention output
+            # each call appends: the context advances; it returns with this
+            # step's attention output in the host buffers
+            ctx.decode_host(kv, host_args, seqs, pos_np + 1 + k)
         e_end.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_end)
@@ -569,6 +570,44 @@ def measure_decoder_sharded(torch, g4a, ctx, dist, world, rank, batch=256, new_t
             "timing": "wall clock around g4a_model_generate on every rank, max over ranks"}
 
 
+def measure_prompt(torch, gm, ctx, w, batch=1, length=628, token_by_token=True):
+    """A prompt of `length` tokens (configuration 1's 628) per sequence
+    through g4a_model_prefill, in chunks of many positions per step, against
+    the same prompt fed one token per step on the same GPU as the reference
+    feeds it (generate.rs:38-42); the two leave bit-identical logits, so the
+    greedy tokens after the prompt must agree. Wall clock around the public
+    calls; the host oracle's rate for one prompt token is its decoder rate
+    (the reference's prefill is a forward pass per token)."""
+    m = gm.Model(ctx, w, max_seqs=batch, max_tokens=length + 1)
+    ids = list(range(batch))
+    prompts = np.random.default_rng(60 + batch).integers(0, w.vocab, (batch, length)).astype(np.int32)
+
+    def clear():
+        for s_ in ids:
+            m.clear(s_)
+    m.prefill(ids, prompts)  # warm-up: the chunk sizes' first runs
+    clear()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    nxt = m.prefill(ids, prompts)
+    dt = time.perf_counter() - t0
+    rows = max(batch, min(2048, batch * (length + 1)))  # the model's rows per step
+    per_chunk = max(1, rows // batch)
+    res = {"batch": batch, "prompt_tokens": length, "chunks": -(-length // per_chunk),
+           "s": round(dt, 4), "tokens_per_s": round(batch * length / dt, 1),
+           "timing": "wall clock around g4a_model_prefill (token upload, pick download)"}
+    if token_by_token:
+        clear()
+        t0 = time.perf_counter()
+        for p in range(length):
+            step_next = m.step(ids, prompts[:, p].tolist())
+        dt2 = time.perf_counter() - t0
+        res["one_token_per_step"] = {"s": round(dt2, 4), "tokens_per_s": round(batch * length / dt2, 1),
+                                     "same_next_tokens": step_next == nxt}
+    m.close()
+    return res
+
+
 def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0, new_tokens=DEC_NEW):
     """Configuration 4: the whole E2B decoder (35 layers, vocab 262,144, Q8_0
     weights from N(0, 0.02), bf16-rounded norms; synthetic, seeded) through
@@ -604,6 +643,7 @@ def measure_decoder(torch, g4a, ctx, batches=(1, 256), cpu_budget=10.0, new_toke
     if new_tokens != DEC_NEW:  # a short run (profiling): no host-core leg
         del w
         return res
+    res["prompt_prefill"] = measure_prompt(torch, gm, ctx, w)
     # host cores: the oracle decoder on the same bytes, teacher-forced with the
     # device's batch-1 tokens; top-1 agreement of every step it reaches
     host = {name: w.host(name) for name in w.tensors}
@@ -634,10 +674,23 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     for configuration 1 alone (35 layer-equivalents in one call), or
     "decode-batch1" for configuration 0's latency, "q8-head[:rows]" for
     the Q8_0 output-head mat-vec (262,144 rows unless given), or
+    "decoder-prompt[:batch[:length]]" for g4a_model_prefill alone,
     "decoder[:b1,b2,...[:new_tokens]]" for configuration 4's decoder at
     those batch sizes (a short run when new_tokens is given), or
     "q8-gemm:rows:cols:n_vec[:geglu]" for the batched Q8_0 kernel alone."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
+    if spec.startswith("decoder-prompt"):
+        # decoder-prompt[:batch[:length]] -- g4a_model_prefill alone
+        import g4attn.model as gm
+        parts = spec.split(":")
+        batch = int(parts[1]) if len(parts) > 1 else 1
+        length = int(parts[2]) if len(parts) > 2 else 628
+        w = gm.synthetic_weights(ctx, seed=4)
+        res = measure_prompt(torch, gm, ctx, w, batch=batch, length=length, token_by_token=False)
+        del w
+        ctx.close()
+        print(json.dumps({"case": spec, **res}), flush=True)
+        return
     if spec.startswith("decoder"):
         parts = spec.split(":")
         batches = tuple(int(b) for b in parts[1].split(",")) if len(parts) > 1 else (1, 256)
@@ -905,7 +958,7 @@ def main():
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": d["h2d"],
                 "d2h_bytes_per_step": d["d2h"], "steps": d["e2e_steps"],
-                "api": "g4a_decode (C ABI) with pinned host inputs/outputs, stream sync per step"},
+                "api": "g4a_decode_host (C ABI): pinned host q/k/v copied in, output copied back, one call per step"},
         "gpu_launches": sum(v[1] for v in d["kernels"].values()),  # the timed pass launches the same kernels
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
                    "sm_max_mhz": clocks_all[0]["sm_max_mhz"] if clocks_all[0] else None, "reasons": reasons},

@@ -877,6 +877,280 @@ __global__ void __launch_bounds__(64) append_kernel(AppendParams p) {
     for (int k = 0; k < PL; k++) store_elem(dst + lane + 32 * k, x[k]);
 }
 
+// ---- prompt chunks ----------------------------------------------------------
+// A prompt chunk holds, for each of its sequences, cl consecutive positions:
+// tasks s*cl .. s*cl + cl - 1 of sequence s, their K/V rows already stored
+// (task_append_kernel). The queries of one sequence read the same key and
+// value rows, so a CTA serves a block of kPromptQ consecutive queries x 8
+// heads from each staged row. Per (query, head) the arithmetic is that of the
+// exact kernels above, in the same order, so the bits are the same:
+//   scores  dot_f32's 16 accumulators, lane l summing q[16m+l] * k[16m+l]
+//           over m (multiply then add, from +0.0), the lanes added in order
+//           from -0.0, times the scale;
+//   softmax max, glibc's expf, the sequential sum, the division;
+//   pv      out += p_j * v_j in key order from +0.0 (multiply then add).
+// The PV loop runs over the union of the block's key ranges; a key outside a
+// query's range has p = 0, and adding the zero product leaves the (never
+// negative-zero) accumulator's bits unchanged.
+constexpr int kPromptQ = 8;                  // queries per block
+constexpr int kPromptQH = kPromptQ * kHeads;  // 64 (query, head) rows
+constexpr int kPromptKeys = 8;               // keys per staged chunk (scores)
+constexpr int kPromptRed = 20;               // floats per (row, key) of the lane table: 16 + pad
+constexpr int kPromptPvKeys = 32;            // keys per staged chunk (pv)
+
+struct PromptBlock {
+    int t0, nq;
+};
+__device__ __forceinline__ PromptBlock prompt_block(int b, int cl) {
+    const int bps = (cl + kPromptQ - 1) / kPromptQ;
+    const int seq = b / bps, q0 = (b - seq * bps) * kPromptQ;
+    return {seq * cl + q0, min(kPromptQ, cl - q0)};
+}
+
+// grid (blocks, splits): CTA (b, y) takes key chunks y, y + splits, ... of
+// block b. 256 threads: warp w holds query w's eight heads; within a warp,
+// lanes 0-15 and 16-31 take keys 0-3 and 4-7 of the chunk, lane & 15 being
+// the dot_f32 accumulator lane.
+template <int HD>
+__global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int cl) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int PL = HD / 32, KS = HD + 4;
+    extern __shared__ float4 dyn4[];
+    float *q_s = reinterpret_cast<float *>(dyn4);  // [64][KS]
+    float *k_s = q_s + kPromptQH * KS;            // [2][kPromptKeys][KS]
+    float *red = k_s + 2 * kPromptKeys * KS;      // [64 * kPromptKeys][kPromptRed]
+    const PromptBlock blk = prompt_block(blockIdx.x, cl);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const DecodeTask &first = p.tasks[blk.t0];
+    const int klo = first.lo, khi = p.tasks[blk.t0 + blk.nq - 1].hi;
+    const int n_chunks = (khi - klo + kPromptKeys - 1) / kPromptKeys;
+    if ((int)blockIdx.y >= n_chunks) return;  // uniform over the CTA, before any barrier
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)first.seq * p.max_pages : nullptr;
+    if (warp < blk.nq) {
+        const DecodeTask &tk = p.tasks[blk.t0 + warp];
+        const float2 *rope = tk.global ? p.rope_global : p.rope_local;
+        for (int h = 0; h < kHeads; h++) {
+            float x[PL];
+            const float *src = tk.q_raw + (size_t)h * HD;
+#pragma unroll
+            for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
+            if (!tk.q_ready) norm_rope_warp<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+#pragma unroll
+            for (int k = 0; k < PL; k++) q_s[(warp * kHeads + h) * KS + lane + 32 * k] = x[k];
+        }
+    } else {
+        for (int e = lane; e < kHeads * KS; e += 32) q_s[warp * kHeads * KS + e] = 0.0f;
+    }
+    auto stage = [&](int c, int b) {
+        const int r0 = klo + c * kPromptKeys, nr = min(kPromptKeys, khi - r0);
+        float *dst = k_s + (size_t)b * kPromptKeys * KS;
+        for (int e = tid; e < kPromptKeys * (HD / 4); e += 256) {
+            const int r = e / (HD / 4), q4 = e - r * (HD / 4);
+            float *d = dst + (size_t)r * KS + 4 * q4;
+            if (r < nr)
+                ptx::cp_async16(d, row_ptr<float>(first.k_base, bt, p.page_tokens, HD, r0 + r) + 4 * q4);
+            else
+                *reinterpret_cast<float4 *>(d) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        ptx::cp_async_commit();
+    };
+    const int kg = lane >> 4, l = lane & 15;
+    const float *qb = q_s + (size_t)(warp * kHeads) * KS + l;
+    int b = 0;
+    stage(blockIdx.y, 0);
+    for (int c = blockIdx.y; c < n_chunks; c += gridDim.y) {
+        if (c + (int)gridDim.y < n_chunks) {
+            stage(c + gridDim.y, b ^ 1);
+            ptx::cp_async_wait<1>();
+        } else {
+            ptx::cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float *kb = k_s + ((size_t)b * kPromptKeys + kg * 4) * KS + l;
+        float acc[kHeads][4];
+#pragma unroll
+        for (int j = 0; j < kHeads; j++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[j][i] = 0.0f;
+#pragma unroll 2
+        for (int m = 0; m < HD / 16; m++) {
+            float qv[kHeads], kv[4];
+#pragma unroll
+            for (int j = 0; j < kHeads; j++) qv[j] = qb[j * KS + 16 * m];
+#pragma unroll
+            for (int i = 0; i < 4; i++) kv[i] = kb[i * KS + 16 * m];
+#pragma unroll
+            for (int j = 0; j < kHeads; j++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[j][i] = __fadd_rn(acc[j][i], __fmul_rn(qv[j], kv[i]));
+        }
+#pragma unroll
+        for (int j = 0; j < kHeads; j++)
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                red[((warp * kHeads + j) * kPromptKeys + kg * 4 + i) * kPromptRed + l] = acc[j][i];
+        __syncthreads();
+        // lanes added in order, one (row, key) pair at a time per thread
+        const int r0 = klo + c * kPromptKeys;
+        for (int pr = tid; pr < kPromptQH * kPromptKeys; pr += 256) {
+            const int qh = pr / kPromptKeys, q = qh / kHeads, h = qh - q * kHeads, k = r0 + (pr - qh * kPromptKeys);
+            if (q >= blk.nq) continue;
+            const DecodeTask &tk = p.tasks[blk.t0 + q];
+            if (k < tk.lo || k >= tk.hi) continue;
+            const float4 *rp = reinterpret_cast<const float4 *>(red + (size_t)pr * kPromptRed);
+            float s = -0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 v = rp[u];
+                s = __fadd_rn(s, v.x);
+                s = __fadd_rn(s, v.y);
+                s = __fadd_rn(s, v.z);
+                s = __fadd_rn(s, v.w);
+            }
+            p.scores[((size_t)(blk.t0 + q) * kHeads + h) * p.max_rows + (k - tk.lo)] = __fmul_rn(s, tk.scale);
+        }
+        __syncthreads();  // the lane table and this chunk's buffer are rewritten next
+        b ^= 1;
+    }
+}
+
+// softmax_f32 (ops.rs:105-127) of every (task, head) row of the scores, in
+// place: one warp per row; the same arithmetic as the exact kernels.
+__global__ void __launch_bounds__(256) prompt_softmax_kernel(DecodeParams p, int n_rows) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= n_rows) return;
+    const DecodeTask &tk = p.tasks[row / kHeads];
+    const int rows = tk.hi - tk.lo;
+    float *s = p.scores + (size_t)row * p.max_rows;
+    float m = -CUDART_INF_F;
+    bool finite = true;
+    for (int r = lane; r < rows; r += 32) {
+        const float v = s[r];
+        finite = finite && isfinite(v);
+        m = fmaxf(m, v);
+    }
+    m = warp_max(m);
+    finite = __all_sync(kFull, finite);
+    for (int r = lane; r < rows; r += 32) s[r] = glibc::expf(__fsub_rn(s[r], m));
+    __syncwarp();
+    float total = -0.0f;
+    if (lane == 0)
+        for (int r = 0; r < rows; r++) total = __fadd_rn(total, s[r]);
+    total = __shfl_sync(kFull, total, 0);
+    if (!finite || !isfinite(total) || total == 0.0f) {
+        if (lane == 0) atomicOr(p.err_flag, 1);
+        total = CUDART_NAN_F;
+    }
+    for (int r = lane; r < rows; r += 32) s[r] = __fdiv_rn(s[r], total);
+}
+
+// grid (blocks, HD / 128): warp w accumulates query w's eight heads over 128
+// columns, lane = a quad of columns; V rows and the probabilities of the
+// block's 64 rows are staged per chunk of kPromptPvKeys keys.
+template <int HD>
+__global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int VC = kPvCols, KC = kPromptPvKeys;
+    extern __shared__ float4 dyn4[];
+    float *v_s = reinterpret_cast<float *>(dyn4);  // [2][KC][VC]
+    float *p_s = v_s + 2 * KC * VC;                // [2][KC][64]
+    const PromptBlock blk = prompt_block(blockIdx.x, cl);
+    const int col0 = blockIdx.y * VC;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const DecodeTask &first = p.tasks[blk.t0];
+    const int klo = first.lo, khi = p.tasks[blk.t0 + blk.nq - 1].hi;
+    const int n_chunks = (khi - klo + KC - 1) / KC;
+    const int32_t *bt = p.block_table ? p.block_table + (size_t)first.seq * p.max_pages : nullptr;
+    // probability gather: thread = (row gq, keys gk .. gk + 7 of the chunk)
+    const int gq = tid & (kPromptQH - 1), gk = (tid / kPromptQH) * 8;
+    const int gq_q = gq / kHeads;
+    int g_lo = 0, g_hi = 0;
+    const float *g_row = p.scores;
+    if (gq_q < blk.nq) {
+        const DecodeTask &gt = p.tasks[blk.t0 + gq_q];
+        g_lo = gt.lo;
+        g_hi = gt.hi;
+        g_row = p.scores + ((size_t)(blk.t0 + gq_q) * kHeads + (gq - gq_q * kHeads)) * p.max_rows;
+    }
+    float pf[8];
+    auto load_p = [&](int c) {
+        const int k0 = klo + c * KC + gk;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int k = k0 + j;
+            pf[j] = (k >= g_lo && k < g_hi) ? g_row[k - g_lo] : 0.0f;
+        }
+    };
+    auto store_p = [&](int b) {
+        float *d = p_s + (size_t)b * KC * kPromptQH;
+#pragma unroll
+        for (int j = 0; j < 8; j++) d[(gk + j) * kPromptQH + gq] = pf[j];
+    };
+    auto stage_v = [&](int c, int b) {
+        const int r0 = klo + c * KC, nr = min(KC, khi - r0);
+        float *dst = v_s + (size_t)b * KC * VC;
+        for (int e = tid; e < KC * (VC / 4); e += 256) {
+            const int r = e / (VC / 4), q4 = e - r * (VC / 4);
+            float *d = dst + (size_t)r * VC + 4 * q4;
+            if (r < nr)
+                ptx::cp_async16(d, row_ptr<float>(first.v_base, bt, p.page_tokens, HD, r0 + r) + col0 + 4 * q4);
+            else
+                *reinterpret_cast<float4 *>(d) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        ptx::cp_async_commit();
+    };
+    float acc[kHeads][4];
+#pragma unroll
+    for (int h = 0; h < kHeads; h++)
+#pragma unroll
+        for (int u = 0; u < 4; u++) acc[h][u] = 0.0f;
+    load_p(0);
+    store_p(0);
+    stage_v(0, 0);
+    int b = 0;
+    for (int c = 0; c < n_chunks; c++) {
+        const bool more = c + 1 < n_chunks;
+        if (more) {
+            stage_v(c + 1, b ^ 1);
+            load_p(c + 1);
+            ptx::cp_async_wait<1>();
+        } else {
+            ptx::cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float *vb = v_s + (size_t)b * KC * VC + 4 * lane;
+        const float *pb = p_s + (size_t)b * KC * kPromptQH + warp * kHeads;
+#pragma unroll 4
+        for (int k = 0; k < KC; k++) {  // key order
+            const float4 v = *reinterpret_cast<const float4 *>(vb + (size_t)k * VC);
+            const float4 p0 = *reinterpret_cast<const float4 *>(pb + (size_t)k * kPromptQH);
+            const float4 p1 = *reinterpret_cast<const float4 *>(pb + (size_t)k * kPromptQH + 4);
+            const float pp[kHeads] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+            for (int h = 0; h < kHeads; h++) {
+                acc[h][0] = __fadd_rn(acc[h][0], __fmul_rn(pp[h], v.x));
+                acc[h][1] = __fadd_rn(acc[h][1], __fmul_rn(pp[h], v.y));
+                acc[h][2] = __fadd_rn(acc[h][2], __fmul_rn(pp[h], v.z));
+                acc[h][3] = __fadd_rn(acc[h][3], __fmul_rn(pp[h], v.w));
+            }
+        }
+        __syncthreads();  // both buffers of this chunk are free
+        if (more) store_p(b ^ 1);
+        b ^= 1;
+    }
+    if (warp < blk.nq) {
+        const DecodeTask &tk = p.tasks[blk.t0 + warp];
+#pragma unroll
+        for (int h = 0; h < kHeads; h++)
+            *reinterpret_cast<float4 *>(tk.out + (size_t)h * HD + col0 + 4 * lane) =
+                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    }
+}
+
 // The K/V rows of a step's tokens stored before any attention of the step
 // reads them (a prompt chunk holds several positions of one sequence): k-norm
 // and RoPE of K, the unweighted norm of V (model.rs:398-404), the arithmetic
@@ -1021,6 +1295,38 @@ cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cuda
         return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_prompt_hd(const DecodeParams &p, int n_tasks, int cl, int n_blocks, int splits, cudaStream_t s,
+                             bool pdl) {
+    constexpr int KS = HD + 4;
+    const size_t sc_smem = ((size_t)(kPromptQH + 2 * kPromptKeys) * KS + kPromptQH * kPromptKeys * kPromptRed) *
+                           sizeof(float);
+    const size_t pv_smem = (size_t)2 * kPromptPvKeys * (kPvCols + kPromptQH) * sizeof(float);
+    cudaFuncSetAttribute(prompt_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem);
+    cudaFuncSetAttribute(prompt_pv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem);
+    cudaError_t e = launch_k(pdl, prompt_scores_kernel<HD>, dim3(n_blocks, splits), dim3(256), sc_smem, s, p, cl);
+    if (e == cudaSuccess)
+        e = launch_k(pdl, prompt_softmax_kernel, dim3(n_tasks), dim3(256), 0, s, p, n_tasks * kHeads);
+    if (e == cudaSuccess)
+        e = launch_k(pdl, prompt_pv_kernel<HD>, dim3(n_blocks, HD / kPvCols), dim3(256), pv_smem, s, p, cl);
+    return e;
+}
+
+cudaError_t launch_prompt_exact(const DecodeParams &p, int hd, int n_tasks, int cl, cudaStream_t s, bool pdl) {
+    if (n_tasks == 0) return cudaSuccess;
+    if (cl < 1 || n_tasks % cl || p.max_rows <= 0 || p.max_rows > kExactMaxRows || !p.scores)
+        return cudaErrorInvalidValue;
+    const int n_blocks = (n_tasks / cl) * ((cl + kPromptQ - 1) / kPromptQ);
+    // key chunks of one block: at most max_rows rows; splits spread them over
+    // about four CTAs per SM in all (a CTA with no chunk exits at once)
+    const int max_chunks = (p.max_rows + kPromptKeys - 1) / kPromptKeys;
+    int splits = (4 * 148 + n_blocks - 1) / n_blocks;
+    splits = splits < 1 ? 1 : (splits > max_chunks ? max_chunks : splits);
+    if (hd == 256) return launch_prompt_hd<256>(p, n_tasks, cl, n_blocks, splits, s, pdl);
+    if (hd == 512) return launch_prompt_hd<512>(p, n_tasks, cl, n_blocks, splits, s, pdl);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_task_append(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl) {

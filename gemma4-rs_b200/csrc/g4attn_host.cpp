@@ -287,6 +287,8 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
     for (auto e : ctx->spare) cudaEventDestroy(e);
     cudaFree(ctx->d_q8x);
     cudaFree(ctx->d_q8s);
+    cudaFree(ctx->d_io);
+    if (ctx->h_flag) cudaFreeHost(ctx->h_flag);
     for (auto &sl : ctx->pin) {
         if (sl.p) cudaFreeHost(sl.p);
         if (sl.ev) cudaEventDestroy(sl.ev);
@@ -971,6 +973,74 @@ extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_
     int rc = build_decode(ctx, kv, n_layers, layers, n_seqs, seq_ids, positions, plan);
     if (rc) return rc;
     return run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16);
+}
+
+extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer_host *layers,
+                               int32_t n_seqs, const int32_t *seq_ids, const int32_t *positions) {
+    if (!ctx || !kv) return G4A_COMPUTE;
+    cudaSetDevice(ctx->device);
+    if (n_layers < 0 || n_seqs < 0 || (n_layers > 0 && !layers))
+        return fail(ctx, G4A_COMPUTE, "compute: invalid decode arguments");
+    // device slots: per layer q [n][8 hd], k and v [n][hd], out [n][8 hd]
+    std::vector<size_t> off(n_layers);
+    std::vector<int32_t> width(n_layers);
+    size_t total = 0;
+    for (int32_t i = 0; i < n_layers; i++) {
+        width[i] = g4a_head_dim(&ctx->hp, layers[i].layer);  // the layer itself is checked by build_decode
+        off[i] = total;
+        total += (size_t)n_seqs * width[i] * (2 * kHeads + 2);
+    }
+    int rc = grow(ctx, &ctx->d_io, &ctx->io_cap, std::max<size_t>(total, 1), false);
+    if (rc) return rc;
+    if (!ctx->h_flag) G4A_CUDA_TRY(ctx, cudaHostAlloc(reinterpret_cast<void **>(&ctx->h_flag), sizeof(int),
+                                                      cudaHostAllocDefault));
+    std::vector<g4a_decode_layer> dev(n_layers);
+    for (int32_t i = 0; i < n_layers; i++) {
+        const size_t qn = (size_t)n_seqs * kHeads * width[i], kn = (size_t)n_seqs * width[i];
+        float *base = ctx->d_io + off[i];
+        const g4a_decode_layer_host &h = layers[i];
+        dev[i] = g4a_decode_layer{h.layer,          h.q_raw_host ? base : nullptr,
+                                  h.k_raw_host ? base + qn : nullptr, h.v_raw_host ? base + qn + kn : nullptr,
+                                  h.q_norm_w_dev,  h.k_norm_w_dev, h.out_host ? base + qn + 2 * kn : nullptr};
+    }
+    // The inputs go first, into the context's own slots, so that the copies
+    // overlap the host-side validation and planning; on a rejected call the
+    // stream is drained before returning (no copy still reads the caller's
+    // buffers) and neither the cache nor out_host has been touched.
+    for (int32_t i = 0; i < n_layers; i++) {
+        const size_t qb = (size_t)n_seqs * kHeads * width[i] * sizeof(float), kb = (size_t)n_seqs * width[i] * sizeof(float);
+        const g4a_decode_layer_host &h = layers[i];
+        int32_t src = -1;
+        const bool owner = g4a_kv_source_layer(&ctx->hp, h.layer, &src, nullptr) == G4A_OK && src == h.layer;
+        if (h.q_raw_host && qb)
+            G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].q_raw_dev), h.q_raw_host, qb,
+                                              cudaMemcpyHostToDevice, ctx->stream));
+        if (owner && h.k_raw_host && h.v_raw_host && kb) {
+            G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].k_raw_dev), h.k_raw_host, kb,
+                                              cudaMemcpyHostToDevice, ctx->stream));
+            G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].v_raw_dev), h.v_raw_host, kb,
+                                              cudaMemcpyHostToDevice, ctx->stream));
+        }
+    }
+    Plan plan;
+    if ((rc = build_decode(ctx, kv, n_layers, dev.data(), n_seqs, seq_ids, positions, plan))) {
+        cudaStreamSynchronize(ctx->stream);
+        return rc;
+    }
+    if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16))) return rc;
+    for (int32_t i = 0; i < n_layers; i++)
+        G4A_CUDA_TRY(ctx, cudaMemcpyAsync(layers[i].out_host, dev[i].out_dev,
+                                          (size_t)n_seqs * kHeads * width[i] * sizeof(float), cudaMemcpyDeviceToHost,
+                                          ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->h_flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    const int flag = *ctx->h_flag;
+    if (flag) {
+        G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+        if (flag & 6) return fail(ctx, G4A_TIMEOUT, "compute: a device wait ran out (flag %d)", flag);
+        return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
+    }
+    return G4A_OK;
 }
 
 struct g4a_plan {

@@ -63,6 +63,11 @@ struct g4a_ctx {
     size_t q8x_cap = 0;
     float *d_q8s = nullptr;
     size_t q8s_cap = 0;
+    // g4a_decode_host: device copies of the callers' host q/k/v/out, and a
+    // pinned word receiving the error flag at the end of the call
+    float *d_io = nullptr;
+    size_t io_cap = 0;  // floats
+    int *h_flag = nullptr;
 };
 
 namespace g4a {

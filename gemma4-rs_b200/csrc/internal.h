@@ -115,6 +115,11 @@ cudaError_t launch_decode_exact(const DecodeParams &p, int hd, int n_tasks, cuda
 // K/V rows of tasks 0..n_tasks-1 (norms, RoPE at the task's position, stored
 // at that row) ahead of an attention launch whose tasks have new_row = -1.
 cudaError_t launch_task_append(const DecodeParams &p, int hd, int n_tasks, cudaStream_t s, bool pdl = false);
+// The exact attention of a prompt chunk: tasks s*cl .. s*cl + cl - 1 are cl
+// consecutive positions of one sequence (rows stored beforehand, new_row -1),
+// each task's output the exact kernels' bit for bit. Scores, softmax and
+// probabilities in p.scores ([tasks][heads][max_rows]).
+cudaError_t launch_prompt_exact(const DecodeParams &p, int hd, int n_tasks, int cl, cudaStream_t s, bool pdl = false);
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
 constexpr size_t kQBlockBytes = 16 * 512 * 2;  // q hi/lo block of one task (f16 kernel)

@@ -126,8 +126,9 @@ int mv(g4a_model *m, int kind, const uint8_t *w, const uint8_t *w2, int64_t rows
 // token's K/V row; its logits are every row's. A prompt chunk (chunk true)
 // may hold several positions of a sequence: all K/V rows are stored first,
 // and the logits are those of the n_out rows listed after the positions
-// (none for a chunk that does not end a prompt).
-int enqueue_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
+// (none for a chunk that does not end a prompt). A chunk's rows are cl
+// consecutive positions of each of its sequences, sequence-major.
+int enqueue_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk, int32_t cl) {
     g4a_ctx *ctx = m->ctx;
     const g4a_model_weights &w = m->w;
     const float eps = ctx->hp.rms_norm_eps;
@@ -202,7 +203,10 @@ int enqueue_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
         if (m->exact) {
             p.max_rows = m->T;
             p.scores = m->scores;
-            MODEL_TRY(launch_decode_exact(p, hd, n, m->st, m->pdl));
+            if (chunk && cl > 1)  // positions of one sequence share their key rows
+                MODEL_TRY(launch_prompt_exact(p, hd, n, cl, m->st, m->pdl));
+            else
+                MODEL_TRY(launch_decode_exact(p, hd, n, m->st, m->pdl));
         } else {
             MODEL_TRY(launch_decode(p, hd, 0, true, m->st));
         }
@@ -249,10 +253,10 @@ int enqueue_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
 }
 
 // Upload of the step's inputs, the step, download of its tokens and flags.
-int record_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
+int record_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk, int32_t cl) {
     const size_t n_in = 3 * (size_t)n + (chunk ? n_out : 0);
     MODEL_TRY(cudaMemcpyAsync(m->d_in, m->h_in, n_in * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
-    const int rc = enqueue_step(m, n, n_out, chunk);
+    const int rc = enqueue_step(m, n, n_out, chunk, cl);
     if (rc) return rc;
     if (n_out > 0)
         MODEL_TRY(cudaMemcpyAsync(m->h_out, m->d_best, (size_t)n_out * sizeof(unsigned long long),
@@ -264,18 +268,18 @@ int record_step(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
 // A decode step of n sequences: eager the first time a size is seen, then
 // captured, then one graph launch per step of that size. Prompt chunks are
 // eager (their row counts vary and each runs once per prompt).
-int run_step(g4a_model *m, int32_t n, int32_t n_out = -1, bool chunk = false) {
-    if (chunk) return record_step(m, n, n_out, true);
+int run_step(g4a_model *m, int32_t n, int32_t n_out = -1, bool chunk = false, int32_t cl = 1) {
+    if (chunk) return record_step(m, n, n_out, true, cl);
     n_out = n;
     auto it = m->graphs.find(n);
     if (it != m->graphs.end()) {
         MODEL_TRY(cudaGraphLaunch(it->second, m->st));
         return G4A_OK;
     }
-    if (!m->use_graphs || m->eager_runs[n]++ == 0) return record_step(m, n, n_out, false);  // first of a size: eager
+    if (!m->use_graphs || m->eager_runs[n]++ == 0) return record_step(m, n, n_out, false, 1);  // first of a size: eager
     cudaGraph_t g = nullptr;
     MODEL_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    const int rc = record_step(m, n, n_out, false);
+    const int rc = record_step(m, n, n_out, false, 1);
     const cudaError_t e = cudaStreamEndCapture(m->st, &g);
     if (rc || e != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -488,11 +492,11 @@ namespace {
 
 // Runs a step whose inputs are in h_in, after the caller's work on the
 // context's stream, and reads its flags.
-int submit(g4a_model *m, int32_t n, int32_t n_out, bool chunk) {
+int submit(g4a_model *m, int32_t n, int32_t n_out, bool chunk, int32_t cl = 1) {
     g4a_ctx *ctx = m->ctx;
     G4A_CUDA_TRY(ctx, cudaEventRecord(m->ev, ctx->stream));
     G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(m->st, m->ev, 0));
-    const int rc = run_step(m, n, n_out, chunk);
+    const int rc = run_step(m, n, n_out, chunk, cl);
     if (rc) {
         cudaStreamSynchronize(m->st);
         return rc;
@@ -575,7 +579,7 @@ extern "C" int g4a_model_prefill(g4a_model *m, int32_t n, const int32_t *seq_ids
             m->h_in[3 * rows + i] = i * cl + cl - 1;  // the sequence's last row of the chunk
         }
         // one position per sequence: a decode step (its graph)
-        rc = cl == 1 ? submit(m, n, n, false) : submit(m, rows, last ? n : 0, true);
+        rc = cl == 1 ? submit(m, n, n, false) : submit(m, rows, last ? n : 0, true, cl);
         if (rc) return rc;
         for (int i = 0; i < n; i++) m->len[seq_ids[i]] += cl;
     }

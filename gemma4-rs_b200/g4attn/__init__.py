@@ -19,6 +19,8 @@ import re
 import weakref
 from pathlib import Path
 
+import numpy as np
+
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libg4attn.so"
 HEADER = HERE.parent.parent / "include" / "g4attn.h"
@@ -46,6 +48,11 @@ class HParams(ctypes.Structure):
 class DecodeLayer(ctypes.Structure):
     _fields_ = [("layer", ctypes.c_int32), ("q_raw_dev", _vp), ("k_raw_dev", _vp), ("v_raw_dev", _vp),
                 ("q_norm_w_dev", _vp), ("k_norm_w_dev", _vp), ("out_dev", _vp)]
+
+
+class DecodeLayerHost(ctypes.Structure):
+    _fields_ = [("layer", ctypes.c_int32), ("q_raw_host", _vp), ("k_raw_host", _vp), ("v_raw_host", _vp),
+                ("q_norm_w_dev", _vp), ("k_norm_w_dev", _vp), ("out_host", _vp)]
 
 
 class PrefillProblem(ctypes.Structure):
@@ -97,6 +104,8 @@ def _load():
     L.g4a_kv_view.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, _vp, _vp]
     L.g4a_kv_append_tokens.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp, ctypes.c_int64]
     L.g4a_decode.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(DecodeLayer), ctypes.c_int32, _i32p, _i32p]
+    L.g4a_decode_host.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(DecodeLayerHost), ctypes.c_int32, _i32p,
+                                  _i32p]
     L.g4a_decode_plan.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(DecodeLayer), ctypes.c_int32, _i32p,
                                   _i32p, ctypes.POINTER(_vp)]
     L.g4a_plan_run.argtypes = [_vp]
@@ -199,6 +208,29 @@ def _ptr(t) -> int | None:
     return t.data_ptr()
 
 
+def _hptr(t) -> int | None:
+    """Address of a contiguous float32 host buffer (numpy array or CPU tensor)."""
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        assert t.dtype == np.float32 and t.flags["C_CONTIGUOUS"], "host buffers must be contiguous float32"
+        return t.ctypes.data
+    assert not t.is_cuda and t.is_contiguous(), "host buffers must be contiguous CPU tensors"
+    return t.data_ptr()
+
+
+class DecodeHostArgs:
+    """A packed g4a_decode_host layer list (the buffers must stay alive)."""
+
+    def __init__(self, layers: list[dict]):
+        self.n = len(layers)
+        self.arr = (DecodeLayerHost * max(1, self.n))()
+        for i, a in enumerate(layers):
+            self.arr[i] = DecodeLayerHost(a["layer"], _hptr(a["q_raw"]), _hptr(a.get("k_raw")),
+                                          _hptr(a.get("v_raw")), _ptr(a.get("q_norm_w")), _ptr(a.get("k_norm_w")),
+                                          _hptr(a["out"]))
+
+
 class Context:
     """g4a_ctx: one device, one stream, RoPE tables and decode scratch."""
 
@@ -268,6 +300,16 @@ class Context:
     def decode(self, kv: "KvCache", layers: list[dict], seq_ids: list[int], positions: list[int]):
         arr, n, s, p = self._decode_args(layers, seq_ids, positions)
         self.check(lib.g4a_decode(self.h, kv.h, len(layers), arr, n, s, p))
+
+    def decode_host(self, kv: "KvCache", layers, seq_ids, positions):
+        """g4a_decode_host: q/k/v/out in host memory (dicts as decode(), with
+        numpy arrays or CPU tensors, or a DecodeHostArgs); returns when the
+        outputs are in the host buffers."""
+        args = layers if isinstance(layers, DecodeHostArgs) else DecodeHostArgs(layers)
+        s = np.ascontiguousarray(seq_ids, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        self.check(lib.g4a_decode_host(self.h, kv.h, args.n, args.arr, len(s), s.ctypes.data_as(_i32p),
+                                       p.ctypes.data_as(_i32p)))
 
     def decode_plan(self, kv: "KvCache", layers: list[dict], seq_ids: list[int], positions: list[int]) -> "Plan":
         arr, n, s, p = self._decode_args(layers, seq_ids, positions)

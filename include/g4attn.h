@@ -201,6 +201,28 @@ typedef struct g4a_decode_layer {
 int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers_host,
                int32_t n_seqs, const int32_t *seq_ids_host, const int32_t *positions_host);
 
+/* g4a_decode for a caller whose vectors live in host memory, as the
+ * reference's attend (model.rs:345-366) takes host slices: q_raw_host
+ * [n][n_heads*hd], k_raw_host/v_raw_host [n][hd] (owner layers; may be NULL
+ * on KV-shared layers) are copied in on the context's stream, the step runs,
+ * out_host [n][n_heads*hd] is copied back, and the call returns when it is
+ * there, with the device's softmax/timeout flags checked (G4A_NONFINITE,
+ * G4A_TIMEOUT). Page-locked host buffers copy asynchronously by DMA;
+ * pageable ones are staged by the driver. The norm weights stay device
+ * pointers (model weights are resident). Validation happens before any
+ * copy, so a rejected call leaves the cache and the outputs untouched. */
+typedef struct g4a_decode_layer_host {
+    int32_t layer;
+    const float *q_raw_host;
+    const float *k_raw_host;
+    const float *v_raw_host;
+    const float *q_norm_w_dev;
+    const float *k_norm_w_dev;
+    float *out_host;
+} g4a_decode_layer_host;
+int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer_host *layers_host,
+                    int32_t n_seqs, const int32_t *seq_ids_host, const int32_t *positions_host);
+
 /* A decode step staged for repeated launches: g4a_decode's validation, page
  * allocation and cache-length update happen here once; the plan owns device
  * copies of its work list and its split-KV scratch. */

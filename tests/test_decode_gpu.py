@@ -266,6 +266,84 @@ def test_decode_batched_paged(g4a, oracle, ctx, torch_cuda, dtype):
     kv.close()
 
 
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_decode_host_buffers(g4a, oracle, ctx, torch_cuda, dtype):
+    """g4a_decode_host (q/k/v/out in page-locked host memory, one call per
+    step): the outputs are g4a_decode's bit for bit on a cache with the same
+    history, and the oracle's within the f32 decode bar; a KV-shared layer
+    takes no k/v; a rejected call copies nothing and leaves the lengths; a
+    non-finite score is reported by the call itself."""
+    torch = torch_cuda
+    hp = oracle.hparams_e2b()
+    ff = oracle.proportional_rope_freq_factors(512, 0.25)
+    lengths = [0, 63, 64, 511, 512, 700, 1]
+    n = len(lengths)
+    caches = []
+    for _ in range(2):
+        r = rng(321 + dtype)
+        kv = g4a.KvCache(ctx, n, 1024, dtype=dtype, layers=[13, 14])
+        okvs = [oracle.KvCache() for _ in range(n)]
+        w = {l: (norm_weight(r, oracle.head_dim(hp, l)), norm_weight(r, oracle.head_dim(hp, l))) for l in (13, 14)}
+        for s, L in enumerate(lengths):
+            for layer in (13, 14):
+                _fill_history(g4a, oracle, torch, kv, okvs[s], hp, s, layer, L, r, w[layer][1], ff)
+        caches.append((kv, okvs))
+    r = rng(400 + dtype)
+    raws, dev_args, host_args = {}, [], []
+    for layer in (13, 14):
+        hd = oracle.head_dim(hp, layer)
+        q_raw, k_raw, v_raw = normal(r, n, 8 * hd), normal(r, n, hd), normal(r, n, hd)
+        raws[layer] = (q_raw, k_raw, v_raw)
+        wq, wk = dev(torch, w[layer][0]), dev(torch, w[layer][1])
+        dev_args.append(dict(layer=layer, q_raw=dev(torch, q_raw), k_raw=dev(torch, k_raw), v_raw=dev(torch, v_raw),
+                             q_norm_w=wq, k_norm_w=wk, out=torch.empty(n, 8 * hd, device="cuda")))
+        pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        host_args.append(dict(layer=layer, q_raw=pin(q_raw), k_raw=pin(k_raw), v_raw=pin(v_raw), q_norm_w=wq,
+                              k_norm_w=wk, out=torch.full((n, 8 * hd), float("nan")).pin_memory()))
+    seqs = list(range(n))
+    ctx.decode(caches[0][0], dev_args, seqs, lengths)
+    ctx.sync()
+    args = g4a.DecodeHostArgs(host_args)
+    ctx.decode_host(caches[1][0], args, seqs, lengths)
+    for a, h in zip(dev_args, host_args):
+        layer = a["layer"]
+        got = h["out"].numpy()
+        assert np.array_equal(got, host(a["out"])), layer
+        q_raw, k_raw, v_raw = raws[layer]
+        for s, L in enumerate(lengths):
+            ref = caches[1][1][s].attention_block(hp, layer, L, q_raw[s], k_raw[s], v_raw[s], w[layer][0],
+                                                  w[layer][1], ff, kv_store=dtype)
+            assert max_abs_diff(got[s], ref) <= TOL, (layer, L)
+    kv = caches[1][0]
+    # a KV-shared layer (33 reads 13) from host buffers, no k/v
+    q33 = normal(r, n, 8 * 256)
+    out33 = np.full((n, 8 * 256), np.nan, np.float32)
+    ctx.decode_host(kv, [dict(layer=33, q_raw=q33, q_norm_w=dev_args[0]["q_norm_w"], out=out33)], seqs,
+                    [L for L in lengths])
+    ctx.decode(caches[0][0], [dict(layer=33, q_raw=dev(torch, q33), q_norm_w=dev_args[0]["q_norm_w"],
+                                   out=dev_args[0]["out"])], seqs, [L for L in lengths])
+    ctx.sync()
+    assert np.array_equal(out33, host(dev_args[0]["out"]))
+    # rejected: position past the cache (view of more rows than held)
+    before = [kv.len(s, 13) for s in seqs]
+    out_bad = np.full((1, 8 * 256), 7.0, np.float32)
+    with pytest.raises(g4a.EngError) as e:
+        ctx.decode_host(kv, [dict(layer=13, q_raw=q33[:1].copy(), k_raw=raws[13][1][:1].copy(),
+                                  v_raw=raws[13][2][:1].copy(), q_norm_w=dev_args[0]["q_norm_w"],
+                                  k_norm_w=dev_args[0]["k_norm_w"], out=out_bad)], [0], [lengths[0] + 5])
+    assert e.value.code == g4a.CONTEXT_TOO_LONG
+    assert np.all(out_bad == 7.0) and [kv.len(s, 13) for s in seqs] == before
+    # non-finite q: the call itself raises
+    bad = q33[:1].copy()
+    bad[:] = np.inf
+    with pytest.raises(g4a.EngError) as e:
+        ctx.decode_host(kv, [dict(layer=33, q_raw=bad, q_norm_w=dev_args[0]["q_norm_w"], out=out_bad)], [1],
+                        [lengths[1]])
+    assert e.value.code == g4a.NONFINITE
+    for kv_, _ in caches:
+        kv_.close()
+
+
 def test_decode_errors(g4a, oracle, ctx, torch_cuda):
     torch = torch_cuda
     kv = g4a.KvCache(ctx, 2, 64, layers=[13])
