@@ -7,6 +7,7 @@
 // (crates/llm-gemma4/src/impl_/model.rs:393-410) as one fused device call.
 // Error statuses and messages follow crates/llm-eng/src/error.rs.
 #include <algorithm>
+#include <functional>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -594,7 +595,28 @@ struct Plan {
     int32_t slots = 0;
     bool f16_fast = false;             // f16 paged cache: the TMA / tensor-core kernel
     std::vector<int32_t> cta_start;    // f16 kernel: per-CTA item ranges (items[0] holds all items)
+    // assign_ctas scratch
+    std::vector<DecodeItem> all;
+    std::vector<uint64_t> keys, heap;
+    std::vector<int32_t> cta_of, fill;
+    void clear() {
+        tasks.clear();
+        items[0].clear();
+        items[1].clear();
+        slots = 0;
+        f16_fast = false;
+        cta_start.clear();
+    }
 };
+
+// A plan per thread, its vectors' capacity kept from call to call (a call
+// plans about a hundred tasks and several hundred items; allocating them
+// anew cost more than the planning).
+Plan &scratch_plan() {
+    static thread_local Plan plan;
+    plan.clear();
+    return plan;
+}
 
 // Rows per work item. Aims at about two items per SM over the whole call,
 // weighting rows by head width, with at least 64 rows per item: the last CTA
@@ -752,47 +774,65 @@ void add_items_aligned(Plan &plan, DecodeTask &t, int32_t task_index, int32_t ro
     int64_t rp = std::max<int64_t>(rows_per, 64);
     rp = std::max<int64_t>(rp, (n_rows + kF16MaxSplits - 2) / (kF16MaxSplits - 1));  // +1 for the unaligned start
     rp = (rp + 63) / 64 * 64;
-    std::vector<int32_t> cuts{t.lo};
-    for (int64_t b = ((int64_t)t.lo / rp + 1) * rp; b < t.hi; b += rp) cuts.push_back((int32_t)b);
-    cuts.push_back(t.hi);
-    const int32_t n = (int32_t)cuts.size() - 1;
+    // cuts: lo, then every multiple of rp above lo and below hi, then hi
+    const int64_t first = ((int64_t)t.lo / rp + 1) * rp;
+    const int32_t n = 1 + (first < t.hi ? (int32_t)((t.hi - 1 - first) / rp + 1) : 0);
     t.n_splits = n;
     t.partial_base = n > 1 ? plan.slots : 0;
     if (n > 1) plan.slots += n;
-    for (int32_t s = 0; s < n; s++) plan.items[which].push_back(DecodeItem{task_index, s, cuts[s], cuts[s + 1]});
+    int32_t a = t.lo;
+    for (int32_t s = 0; s < n; s++) {
+        const int32_t b = s + 1 < n ? (int32_t)(first + (int64_t)s * rp) : t.hi;
+        plan.items[which].push_back(DecodeItem{task_index, s, a, b});
+        a = b;
+    }
 }
 
 // Longest-processing-time assignment of the f16 kernel's items to persistent
 // CTAs: cost = K/V bytes of the rows (in units of a 256-wide row) plus a fixed
 // per-item charge for the q preparation and, for split tasks, the partial
-// write. Items are then stored CTA by CTA with a start table.
+// write. Items are taken longest first (ties in list order), each to the
+// least loaded CTA (ties to the lower index), then stored CTA by CTA, in
+// the order they were assigned, with a start table.
 void assign_ctas(Plan &plan, int n_sm) {
-    std::vector<DecodeItem> all(plan.items[0]);
+    std::vector<DecodeItem> &all = plan.all;
+    all.assign(plan.items[0].begin(), plan.items[0].end());
     all.insert(all.end(), plan.items[1].begin(), plan.items[1].end());
     plan.items[0].clear();
     plan.items[1].clear();
-    auto cost = [&](const DecodeItem &it) {
+    const size_t n = all.size();
+    // (~cost, position) packed: an ascending sort is longest first, stable
+    std::vector<uint64_t> &keys = plan.keys;
+    keys.resize(n);
+    for (size_t i = 0; i < n; i++) {
+        const DecodeItem &it = all[i];
         const DecodeTask &t = plan.tasks[it.task];
-        return (int64_t)(it.row_hi - it.row_lo) * (t.hd / 256) + 64 + (t.n_splits > 1 ? 32 : 0);
-    };
-    std::stable_sort(all.begin(), all.end(), [&](const DecodeItem &a, const DecodeItem &b) { return cost(a) > cost(b); });
-    const int n_ctas = std::max(1, std::min<int>(n_sm, (int)all.size()));
-    std::vector<std::vector<DecodeItem>> per(n_ctas);
-    // min-heap of (load, cta): each item goes to the least loaded CTA
-    std::vector<std::pair<int64_t, int>> heap;
-    for (int b = 0; b < n_ctas; b++) heap.push_back({0, b});
-    auto greater = [](const std::pair<int64_t, int> &x, const std::pair<int64_t, int> &y) { return x > y; };
-    for (const auto &it : all) {
-        std::pop_heap(heap.begin(), heap.end(), greater);
-        heap.back().first += cost(it);
-        per[heap.back().second].push_back(it);
-        std::push_heap(heap.begin(), heap.end(), greater);
+        const uint64_t cost = (uint64_t)((int64_t)(it.row_hi - it.row_lo) * (t.hd / 256) + 64 + (t.n_splits > 1 ? 32 : 0));
+        keys[i] = ((~cost & 0xFFFFFFFFFFull) << 24) | (uint64_t)i;
     }
-    plan.cta_start.assign(1, 0);
-    for (int b = 0; b < n_ctas; b++) {
-        plan.items[0].insert(plan.items[0].end(), per[b].begin(), per[b].end());
-        plan.cta_start.push_back((int32_t)plan.items[0].size());
+    std::sort(keys.begin(), keys.end());
+    const int n_ctas = std::max(1, std::min<int>(n_sm, (int)n));
+    // min-heap of (load, cta) packed
+    std::vector<uint64_t> &heap = plan.heap;
+    heap.resize(n_ctas);
+    for (int b = 0; b < n_ctas; b++) heap[b] = (uint64_t)b;
+    std::vector<int32_t> &cta_of = plan.cta_of;
+    cta_of.resize(n);
+    plan.cta_start.assign(n_ctas + 1, 0);
+    for (size_t j = 0; j < n; j++) {
+        const uint64_t cost = ~(keys[j] >> 24) & 0xFFFFFFFFFFull;
+        std::pop_heap(heap.begin(), heap.end(), std::greater<uint64_t>());
+        const int b = (int)(heap.back() & 0xFFFFFFull);
+        heap.back() += cost << 24;
+        std::push_heap(heap.begin(), heap.end(), std::greater<uint64_t>());
+        cta_of[j] = b;
+        plan.cta_start[b + 1]++;
     }
+    for (int b = 0; b < n_ctas; b++) plan.cta_start[b + 1] += plan.cta_start[b];
+    std::vector<int32_t> &fill = plan.fill;
+    fill.assign(plan.cta_start.begin(), plan.cta_start.end() - 1);
+    plan.items[0].resize(n);
+    for (size_t j = 0; j < n; j++) plan.items[0][fill[cta_of[j]]++] = all[keys[j] & 0xFFFFFFull];
 }
 
 int run_plan(g4a_ctx *ctx, Plan &plan, const int32_t *d_bt, int32_t max_pages, int32_t page_tokens, int kv_f16) {
@@ -813,7 +853,7 @@ extern "C" int g4a_attend(g4a_ctx *ctx, const float *q, const float *keys, const
     if (len == 0) return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");  // model.rs:337,362-364
     if (!keys || !values) return fail(ctx, G4A_COMPUTE, "compute: null keys or values");
     if (n_heads == kHeads && n_kv == 1 && (hd == 256 || hd == 512) && len < (1LL << 31)) {
-        Plan plan;
+        Plan &plan = scratch_plan();
         DecodeTask t{};
         t.k_base = keys;
         t.v_base = values;
@@ -969,7 +1009,7 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
 
 extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
                           const int32_t *seq_ids, const int32_t *positions) {
-    Plan plan;
+    Plan &plan = scratch_plan();
     int rc = build_decode(ctx, kv, n_layers, layers, n_seqs, seq_ids, positions, plan);
     if (rc) return rc;
     return run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16);
@@ -1022,7 +1062,7 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
                                               cudaMemcpyHostToDevice, ctx->stream));
         }
     }
-    Plan plan;
+    Plan &plan = scratch_plan();
     if ((rc = build_decode(ctx, kv, n_layers, dev.data(), n_seqs, seq_ids, positions, plan))) {
         cudaStreamSynchronize(ctx->stream);
         return rc;
@@ -1052,7 +1092,7 @@ extern "C" int g4a_decode_plan(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
                                int32_t n_seqs, const int32_t *seq_ids, const int32_t *positions, g4a_plan **out) {
     if (!out) return fail(ctx, G4A_COMPUTE, "compute: null plan output");
     *out = nullptr;
-    Plan plan;
+    Plan &plan = scratch_plan();
     int rc = build_decode(ctx, kv, n_layers, layers, n_seqs, seq_ids, positions, plan);
     if (rc) return rc;
     auto *pl = new g4a_plan();

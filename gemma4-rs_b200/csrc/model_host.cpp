@@ -66,6 +66,7 @@ struct g4a_model {
     bool pdl = true;         // programmatic dependent launch along the step (G4A_NO_PDL=1: off)
     std::vector<float *> k_cache, v_cache;  // per layer: its KV source's caches
     int32_t last_n = 0;
+    std::vector<int32_t> eos;  // eos_token_ids (model.rs:88): a sequence ends after emitting one
 };
 
 namespace {
@@ -594,6 +595,12 @@ extern "C" int g4a_model_logits(g4a_model *m, const float **logits_dev) {
     return G4A_OK;
 }
 
+extern "C" int g4a_model_set_eos(g4a_model *m, const int32_t *ids, int32_t n) {
+    if (!m || n < 0 || (n && !ids)) return G4A_COMPUTE;
+    m->eos.assign(ids, ids + n);
+    return G4A_OK;
+}
+
 extern "C" int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompts, int32_t prompt_len, int32_t max_new,
                                   int32_t max_context, int32_t *out) {
     if (!m) return G4A_COMPUTE;
@@ -604,23 +611,38 @@ extern "C" int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompt
         return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", prompt_len, max_context);
     if (max_new == 0) return G4A_OK;
     if (prompt_len == 0) return fail(ctx, G4A_COMPUTE, "generation requires at least one prompt token");
-    std::vector<int32_t> ids(n), tok(n), next(n);
+    std::vector<int32_t> ids(n), next(n), act_ids, act_tok, act_next;
     for (int i = 0; i < n; i++) {
         ids[i] = i;
         m->len[i] = 0;  // clear_context
     }
+    for (size_t e = 0; e < (size_t)n * max_new; e++) out[e] = -1;  // slots after an eos stay -1
     int rc;
     // the prompt (generate.rs:38-42, one position per forward pass there) in
     // chunks of many positions; the same logits
     if ((rc = g4a_model_prefill(m, n, ids.data(), prompts, prompt_len, next.data()))) return rc;
+    std::vector<char> active(n, 1);
     for (int index = 0; index < max_new; index++) {  // generate.rs:45-70
         if (prompt_len + index >= max_context)
             return fail(ctx, G4A_CONTEXT_TOO_LONG, "context too long: got %d, max %d", prompt_len + index + 1,
                         max_context);
-        for (int i = 0; i < n; i++) out[(size_t)i * max_new + index] = next[i];
-        if (index + 1 == max_new) break;
-        tok = next;
-        if ((rc = g4a_model_step(m, n, ids.data(), tok.data(), next.data()))) return rc;
+        act_ids.clear();
+        act_tok.clear();
+        for (int i = 0; i < n; i++) {
+            if (!active[i]) continue;
+            out[(size_t)i * max_new + index] = next[i];
+            if (std::find(m->eos.begin(), m->eos.end(), next[i]) != m->eos.end()) {
+                active[i] = 0;  // the eos token is kept, then the sequence stops
+                continue;
+            }
+            act_ids.push_back(i);
+            act_tok.push_back(next[i]);
+        }
+        if (index + 1 == max_new || act_ids.empty()) break;
+        act_next.resize(act_ids.size());
+        if ((rc = g4a_model_step(m, (int32_t)act_ids.size(), act_ids.data(), act_tok.data(), act_next.data())))
+            return rc;
+        for (size_t j = 0; j < act_ids.size(); j++) next[act_ids[j]] = act_next[j];
     }
     return G4A_OK;
 }

@@ -134,6 +134,7 @@ def _load():
     L.g4a_model_prefill.argtypes = [_vp, ctypes.c_int32, _i32p, _i32p, ctypes.c_int32, _i32p]
     L.g4a_model_logits.argtypes = [_vp, ctypes.POINTER(_vp)]
     L.g4a_model_kv_view.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp, _vp]
+    L.g4a_model_set_eos.argtypes = [_vp, _i32p, ctypes.c_int32]
     L.g4a_model_generate.argtypes = [_vp, ctypes.c_int32, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                      _i32p]
     return L

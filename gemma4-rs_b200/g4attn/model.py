@@ -222,8 +222,14 @@ class Model:
                                         "data": (p.value, False), "version": 3, "strides": None}
         return torch.as_tensor(_View(), device=torch.device("cuda", self.ctx.device)).clone()
 
+    def set_eos(self, ids) -> None:
+        """eos_token_ids: generate() ends a sequence after emitting one."""
+        arr = (ctypes.c_int32 * max(1, len(ids)))(*ids)
+        self.ctx.check(lib.g4a_model_set_eos(self.h, arr, len(ids)))
+
     def generate(self, prompts, max_new: int, max_context: int | None = None) -> np.ndarray:
-        """generate_cpu with greedy sampling for rows 0..n-1: [n][max_new] tokens."""
+        """generate_cpu with greedy sampling for rows 0..n-1: [n][max_new]
+        tokens (-1 after a sequence's eos token)."""
         prompts = np.ascontiguousarray(prompts, np.int32)
         n, plen = prompts.shape
         out = np.zeros((n, max_new), np.int32)

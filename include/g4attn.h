@@ -373,11 +373,18 @@ int g4a_model_kv_view(const g4a_model *m, int32_t seq, int32_t layer, int32_t le
                       float *values_dev);
 /* Device pointer to the soft-capped logits of the last step, [n][vocab]. */
 int g4a_model_logits(g4a_model *m, const float **logits_dev);
+/* eos_token_ids (model.rs:88,159-164: `<eos>`, and `<turn|>` for chat,
+ * tokenizer.rs:127-130): g4a_model_generate keeps such a token and ends that
+ * sequence (generate.rs:58-60). Empty by default, as the reference's
+ * synthetic model. */
+int g4a_model_set_eos(g4a_model *m, const int32_t *ids_host, int32_t n);
 /* generate_cpu (generate.rs:15-64) with greedy sampling for sequences
  * 0..n-1 at once: clears them, feeds the prompts [n][prompt_len] through
- * g4a_model_prefill (the same logits as token by token), then samples max_new tokens each into out_host [n][max_new]
- * (the last one is not fed back). max_context bounds prompt + generated as
- * the reference's max_context does. */
+ * g4a_model_prefill (the same logits as token by token), then samples up to
+ * max_new tokens each into out_host [n][max_new] (the last one is not fed
+ * back; a sequence that emits an eos token stops there and its later slots
+ * are -1). max_context bounds prompt + generated as the reference's
+ * max_context does. */
 int g4a_model_generate(g4a_model *m, int32_t n, const int32_t *prompts_host, int32_t prompt_len, int32_t max_new,
                        int32_t max_context, int32_t *out_host);
 

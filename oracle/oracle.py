@@ -443,8 +443,10 @@ class Decoder:
                                      _p(logits)), "dec_forward")
         return logits
 
-    def generate(self, prompt, max_new: int) -> list[int]:
-        """generate_cpu (generate.rs:15-64) with greedy sampling."""
+    def generate(self, prompt, max_new: int, eos=()) -> list[int]:
+        """generate_cpu (generate.rs:15-64) with greedy sampling; a token in
+        `eos` (the model's eos_token_ids, model.rs:164) is kept and ends the
+        generation (generate.rs:58-60)."""
         self.clear()
         logits = None
         for pos, tok in enumerate(prompt):
@@ -452,6 +454,8 @@ class Decoder:
         out = []
         for index in range(max_new):
             out.append(argmax_total(logits))
+            if out[-1] in eos:
+                break
             if index + 1 == max_new:
                 break
             logits = self.forward(out[-1], len(prompt) + len(out) - 1)

@@ -204,6 +204,30 @@ def test_generate_matches_oracle(ctx, small_vocab):
     m.close()
 
 
+def test_generate_stops_at_eos(ctx, small_vocab):
+    """With eos_token_ids set, a sequence keeps its eos token and stops
+    (generate.rs:58-60) while the others go on; each row is the oracle's
+    generate with the same eos, then -1."""
+    import g4attn.model as gm
+    w, make = small_vocab
+    m = gm.Model(ctx, w, max_seqs=3, max_tokens=64)
+    prompts = rng(23).integers(0, w.vocab, (3, 11)).astype(np.int32)
+    free = m.generate(prompts, 14)
+    eos = [int(free[0, 5]), int(free[1, 9])]
+    m.set_eos(eos)
+    out = m.generate(prompts, 14)
+    stopped = 0
+    for i in range(3):
+        want = make().generate(prompts[i].tolist(), 14, eos=tuple(eos))
+        assert out[i, :len(want)].tolist() == want, i
+        assert np.all(out[i, len(want):] == -1), i
+        stopped += len(want) < 14
+    assert stopped >= 2
+    m.set_eos([])
+    assert np.array_equal(m.generate(prompts, 14), free)
+    m.close()
+
+
 def test_prefill_chunks_match_steps_and_oracle(ctx, small_vocab, oracle, monkeypatch):
     """g4a_model_prefill in chunks of many positions (rows bounded to 14 here,
     so two prompts go through as chunks of 7, 7, ..., 5 positions, and one

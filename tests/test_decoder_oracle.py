@@ -168,6 +168,17 @@ def test_generate_greedy_loop(oracle, tiny):
     assert out == want and len(out) == 6
 
 
+def test_generate_eos_stops(oracle, tiny):
+    """An eos token is kept and ends the loop (generate.rs:58-60); without
+    eos ids the loop runs to max_new."""
+    prompt = [int(t) for t in rng(7).integers(0, VOCAB, 5)]
+    full = decoder(oracle, tiny).generate(prompt, 6)
+    stop = full[2]
+    first = full.index(stop)
+    assert decoder(oracle, tiny).generate(prompt, 6, eos=(stop,)) == full[:first + 1]
+    assert decoder(oracle, tiny).generate(prompt, 6, eos=()) == full
+
+
 def test_argmax_total_last_maximum(oracle):
     x = np.array([0.5, 2.0, -1.0, 2.0, np.float32(-0.0), 1.0], np.float32)
     assert oracle.argmax_total(x) == 3  # equal maxima: max_by keeps the last
