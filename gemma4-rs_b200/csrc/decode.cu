@@ -907,6 +907,27 @@ __device__ __forceinline__ PromptBlock prompt_block(int b, int cl) {
     return {seq * cl + q0, min(kPromptQ, cl - q0)};
 }
 
+// q-norm and RoPE of every task's q (model.rs:395-396), in place, once per
+// task (the scores kernel's CTAs of a block then read it ready): one CTA per
+// task, warp h on head h; the exact kernels' arithmetic.
+template <int HD>
+__global__ void __launch_bounds__(256) prompt_q_kernel(DecodeParams p) {
+    ptx::pdl_trigger();
+    ptx::pdl_wait();
+    constexpr int PL = HD / 32;
+    const DecodeTask &tk = p.tasks[blockIdx.x];
+    if (tk.q_ready) return;
+    const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *q = const_cast<float *>(tk.q_raw) + (size_t)h * HD;
+    const float2 *rope = tk.global ? p.rope_global : p.rope_local;
+    float x[PL];
+#pragma unroll
+    for (int k = 0; k < PL; k++) x[k] = q[lane + 32 * k];
+    norm_rope_warp<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
+#pragma unroll
+    for (int k = 0; k < PL; k++) q[lane + 32 * k] = x[k];
+}
+
 // grid (blocks, splits): CTA (b, y) takes key chunks y, y + splits, ... of
 // block b. 256 threads: warp w holds query w's eight heads; within a warp,
 // lanes 0-15 and 16-31 take keys 0-3 and 4-7 of the chunk, lane & 15 being
@@ -915,7 +936,7 @@ template <int HD>
 __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int cl) {
     ptx::pdl_trigger();
     ptx::pdl_wait();
-    constexpr int PL = HD / 32, KS = HD + 4;
+    constexpr int KS = HD + 4;
     extern __shared__ float4 dyn4[];
     float *q_s = reinterpret_cast<float *>(dyn4);  // [64][KS]
     float *k_s = q_s + kPromptQH * KS;            // [2][kPromptKeys][KS]
@@ -927,20 +948,13 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
     const int n_chunks = (khi - klo + kPromptKeys - 1) / kPromptKeys;
     if ((int)blockIdx.y >= n_chunks) return;  // uniform over the CTA, before any barrier
     const int32_t *bt = p.block_table ? p.block_table + (size_t)first.seq * p.max_pages : nullptr;
-    if (warp < blk.nq) {
-        const DecodeTask &tk = p.tasks[blk.t0 + warp];
-        const float2 *rope = tk.global ? p.rope_global : p.rope_local;
-        for (int h = 0; h < kHeads; h++) {
-            float x[PL];
-            const float *src = tk.q_raw + (size_t)h * HD;
-#pragma unroll
-            for (int k = 0; k < PL; k++) x[k] = __ldg(src + lane + 32 * k);
-            if (!tk.q_ready) norm_rope_warp<HD>(x, tk.q_w, rope + (size_t)tk.position * (HD / 2), p.eps, lane);
-#pragma unroll
-            for (int k = 0; k < PL; k++) q_s[(warp * kHeads + h) * KS + lane + 32 * k] = x[k];
-        }
-    } else {
-        for (int e = lane; e < kHeads * KS; e += 32) q_s[warp * kHeads * KS + e] = 0.0f;
+    // q rows, normalized and rotated by prompt_q_kernel; zeros past the block
+    for (int e = tid; e < kPromptQH * (HD / 4); e += 256) {
+        const int r = e / (HD / 4), q4 = e - r * (HD / 4), q = r / kHeads;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (q < blk.nq)
+            v = *reinterpret_cast<const float4 *>(p.tasks[blk.t0 + q].q_raw + (size_t)(r - q * kHeads) * HD + 4 * q4);
+        *reinterpret_cast<float4 *>(q_s + (size_t)r * KS + 4 * q4) = v;
     }
     auto stage = [&](int c, int b) {
         const int r0 = klo + c * kPromptKeys, nr = min(kPromptKeys, khi - r0);
@@ -1016,7 +1030,10 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
 }
 
 // softmax_f32 (ops.rs:105-127) of every (task, head) row of the scores, in
-// place: one warp per row; the same arithmetic as the exact kernels.
+// place: one warp per row; the same arithmetic as the exact kernels. The
+// sequential sum runs in key order over chunks of 128 keys held four per
+// lane: each value is broadcast in turn and every lane adds them all, so no
+// lane waits on a memory load per element.
 __global__ void __launch_bounds__(256) prompt_softmax_kernel(DecodeParams p, int n_rows) {
     ptx::pdl_trigger();
     ptx::pdl_wait();
@@ -1034,12 +1051,27 @@ __global__ void __launch_bounds__(256) prompt_softmax_kernel(DecodeParams p, int
     }
     m = warp_max(m);
     finite = __all_sync(kFull, finite);
-    for (int r = lane; r < rows; r += 32) s[r] = glibc::expf(__fsub_rn(s[r], m));
-    __syncwarp();
     float total = -0.0f;
-    if (lane == 0)
-        for (int r = 0; r < rows; r++) total = __fadd_rn(total, s[r]);
-    total = __shfl_sync(kFull, total, 0);
+    for (int c0 = 0; c0 < rows; c0 += 128) {
+        float e[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int r = c0 + 32 * u + lane;
+            e[u] = 0.0f;
+            if (r < rows) {
+                e[u] = glibc::expf(__fsub_rn(s[r], m));
+                s[r] = e[u];
+            }
+        }
+        const int nr = min(128, rows - c0);
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const float v = __shfl_sync(kFull, e[u], j);
+                if (32 * u + j < nr) total = __fadd_rn(total, v);
+            }
+    }
     if (!finite || !isfinite(total) || total == 0.0f) {
         if (lane == 0) atomicOr(p.err_flag, 1);
         total = CUDART_NAN_F;
@@ -1047,26 +1079,30 @@ __global__ void __launch_bounds__(256) prompt_softmax_kernel(DecodeParams p, int
     for (int r = lane; r < rows; r += 32) s[r] = __fdiv_rn(s[r], total);
 }
 
-// grid (blocks, HD / 128): warp w accumulates query w's eight heads over 128
-// columns, lane = a quad of columns; V rows and the probabilities of the
-// block's 64 rows are staged per chunk of kPromptPvKeys keys.
+// grid (blocks, HD / 64), 128 threads: warp w accumulates queries 2w and
+// 2w + 1 (a half-warp each) over 64 columns, lane & 15 = a quad of columns,
+// all eight heads; V rows and the probabilities of the block's 64 rows are
+// staged per chunk of kPromptPvKeys keys.
+constexpr int kPromptPvCols = 64;
+
 template <int HD>
-__global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) {
+__global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) {
     ptx::pdl_trigger();
     ptx::pdl_wait();
-    constexpr int VC = kPvCols, KC = kPromptPvKeys;
+    constexpr int VC = kPromptPvCols, KC = kPromptPvKeys;
     extern __shared__ float4 dyn4[];
     float *v_s = reinterpret_cast<float *>(dyn4);  // [2][KC][VC]
     float *p_s = v_s + 2 * KC * VC;                // [2][KC][64]
     const PromptBlock blk = prompt_block(blockIdx.x, cl);
     const int col0 = blockIdx.y * VC;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = warp * 2 + (lane >> 4), cq = lane & 15;
     const DecodeTask &first = p.tasks[blk.t0];
     const int klo = first.lo, khi = p.tasks[blk.t0 + blk.nq - 1].hi;
     const int n_chunks = (khi - klo + KC - 1) / KC;
     const int32_t *bt = p.block_table ? p.block_table + (size_t)first.seq * p.max_pages : nullptr;
-    // probability gather: thread = (row gq, keys gk .. gk + 7 of the chunk)
-    const int gq = tid & (kPromptQH - 1), gk = (tid / kPromptQH) * 8;
+    // probability gather: thread = (row gq, keys gk .. gk + 15 of the chunk)
+    const int gq = tid & (kPromptQH - 1), gk = (tid / kPromptQH) * 16;
     const int gq_q = gq / kHeads;
     int g_lo = 0, g_hi = 0;
     const float *g_row = p.scores;
@@ -1076,11 +1112,11 @@ __global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) 
         g_hi = gt.hi;
         g_row = p.scores + ((size_t)(blk.t0 + gq_q) * kHeads + (gq - gq_q * kHeads)) * p.max_rows;
     }
-    float pf[8];
+    float pf[16];
     auto load_p = [&](int c) {
         const int k0 = klo + c * KC + gk;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < 16; j++) {
             const int k = k0 + j;
             pf[j] = (k >= g_lo && k < g_hi) ? g_row[k - g_lo] : 0.0f;
         }
@@ -1088,12 +1124,12 @@ __global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) 
     auto store_p = [&](int b) {
         float *d = p_s + (size_t)b * KC * kPromptQH;
 #pragma unroll
-        for (int j = 0; j < 8; j++) d[(gk + j) * kPromptQH + gq] = pf[j];
+        for (int j = 0; j < 16; j++) d[(gk + j) * kPromptQH + gq] = pf[j];
     };
     auto stage_v = [&](int c, int b) {
         const int r0 = klo + c * KC, nr = min(KC, khi - r0);
         float *dst = v_s + (size_t)b * KC * VC;
-        for (int e = tid; e < KC * (VC / 4); e += 256) {
+        for (int e = tid; e < KC * (VC / 4); e += 128) {
             const int r = e / (VC / 4), q4 = e - r * (VC / 4);
             float *d = dst + (size_t)r * VC + 4 * q4;
             if (r < nr)
@@ -1122,8 +1158,8 @@ __global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) 
             ptx::cp_async_wait<0>();
         }
         __syncthreads();
-        const float *vb = v_s + (size_t)b * KC * VC + 4 * lane;
-        const float *pb = p_s + (size_t)b * KC * kPromptQH + warp * kHeads;
+        const float *vb = v_s + (size_t)b * KC * VC + 4 * cq;
+        const float *pb = p_s + (size_t)b * KC * kPromptQH + q * kHeads;
 #pragma unroll 4
         for (int k = 0; k < KC; k++) {  // key order
             const float4 v = *reinterpret_cast<const float4 *>(vb + (size_t)k * VC);
@@ -1142,11 +1178,11 @@ __global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) 
         if (more) store_p(b ^ 1);
         b ^= 1;
     }
-    if (warp < blk.nq) {
-        const DecodeTask &tk = p.tasks[blk.t0 + warp];
+    if (q < blk.nq) {
+        const DecodeTask &tk = p.tasks[blk.t0 + q];
 #pragma unroll
         for (int h = 0; h < kHeads; h++)
-            *reinterpret_cast<float4 *>(tk.out + (size_t)h * HD + col0 + 4 * lane) =
+            *reinterpret_cast<float4 *>(tk.out + (size_t)h * HD + col0 + 4 * cq) =
                 make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
     }
 }
@@ -1303,14 +1339,15 @@ cudaError_t launch_prompt_hd(const DecodeParams &p, int n_tasks, int cl, int n_b
     constexpr int KS = HD + 4;
     const size_t sc_smem = ((size_t)(kPromptQH + 2 * kPromptKeys) * KS + kPromptQH * kPromptKeys * kPromptRed) *
                            sizeof(float);
-    const size_t pv_smem = (size_t)2 * kPromptPvKeys * (kPvCols + kPromptQH) * sizeof(float);
+    const size_t pv_smem = (size_t)2 * kPromptPvKeys * (kPromptPvCols + kPromptQH) * sizeof(float);
     cudaFuncSetAttribute(prompt_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem);
-    cudaFuncSetAttribute(prompt_pv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pv_smem);
-    cudaError_t e = launch_k(pdl, prompt_scores_kernel<HD>, dim3(n_blocks, splits), dim3(256), sc_smem, s, p, cl);
+    cudaError_t e = launch_k(pdl, prompt_q_kernel<HD>, dim3(n_tasks), dim3(32 * kHeads), 0, s, p);
+    if (e == cudaSuccess)
+        e = launch_k(pdl, prompt_scores_kernel<HD>, dim3(n_blocks, splits), dim3(256), sc_smem, s, p, cl);
     if (e == cudaSuccess)
         e = launch_k(pdl, prompt_softmax_kernel, dim3(n_tasks), dim3(256), 0, s, p, n_tasks * kHeads);
     if (e == cudaSuccess)
-        e = launch_k(pdl, prompt_pv_kernel<HD>, dim3(n_blocks, HD / kPvCols), dim3(256), pv_smem, s, p, cl);
+        e = launch_k(pdl, prompt_pv_kernel<HD>, dim3(n_blocks, HD / kPromptPvCols), dim3(128), pv_smem, s, p, cl);
     return e;
 }
 

@@ -66,18 +66,30 @@ inline double u2d(uint64_t u) { double x; std::memcpy(&x, &u, 8); return x; }
 #endif
 
 // asuint64(2^(i/32)) - (i << 47): 2^(i/32) rounded to double, its exponent
-// contribution removed so that k can be added back as an integer.
+// contribution removed so that k can be added back as an integer. A table at
+// file scope (device code reads it through the read-only cache): as a local
+// array indexed at run time it would be rebuilt in local memory on every call.
+#define G4A_EXP2_32_TABLE \
+        0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull, \
+        0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull, \
+        0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull, \
+        0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull, \
+        0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull, \
+        0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull, \
+        0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull, \
+        0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull
+#ifdef __CUDACC__
+static __device__ const unsigned long long kExp2TabDev[32] = {G4A_EXP2_32_TABLE};
+#endif
+static const uint64_t kExp2TabHost[32] = {G4A_EXP2_32_TABLE};
+#undef G4A_EXP2_32_TABLE
+
 __host__ __device__ __forceinline__ uint64_t exp2_32_entry(int i) {
-    constexpr uint64_t kTab[32] = {
-        0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
-        0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
-        0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
-        0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
-        0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
-        0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
-        0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
-        0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
-    return kTab[i];
+#ifdef __CUDA_ARCH__
+    return (uint64_t)__ldg(&kExp2TabDev[i]);
+#else
+    return kExp2TabHost[i];
+#endif
 }
 
 __host__ __device__ __forceinline__ float expf(float x) {
