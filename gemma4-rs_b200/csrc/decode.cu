@@ -895,7 +895,7 @@ __global__ void __launch_bounds__(64) append_kernel(AppendParams p) {
 constexpr int kPromptQ = 8;                  // queries per block
 constexpr int kPromptQH = kPromptQ * kHeads;  // 64 (query, head) rows
 constexpr int kPromptKeys = 8;               // keys per staged chunk (scores)
-constexpr int kPromptRed = 20;               // floats per (row, key) of the lane table: 16 + pad
+constexpr int kPromptRed = 16;               // floats per (row, key) of the lane table
 constexpr int kPromptPvKeys = 32;            // keys per staged chunk (pv)
 
 struct PromptBlock {
@@ -938,10 +938,14 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
     ptx::pdl_wait();
     constexpr int KS = HD + 4;
     extern __shared__ float4 dyn4[];
-    float *q_s = reinterpret_cast<float *>(dyn4);  // [64][KS]
-    float *k_s = q_s + kPromptQH * KS;            // [2][kPromptKeys][KS]
+    // q rows unpadded (their reads are broadcasts), key rows padded so that
+    // the two half-warps' rows fall in different banks: two CTAs per SM at
+    // width 256
+    float *q_s = reinterpret_cast<float *>(dyn4);  // [64][HD]
+    float *k_s = q_s + kPromptQH * HD;            // [2][kPromptKeys][KS]
     float *red = k_s + 2 * kPromptKeys * KS;      // [64 * kPromptKeys][kPromptRed]
-    const PromptBlock blk = prompt_block(blockIdx.x, cl);
+    // blocks in reverse: the longest key ranges (latest positions) start first
+    const PromptBlock blk = prompt_block(gridDim.x - 1 - blockIdx.x, cl);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const DecodeTask &first = p.tasks[blk.t0];
     const int klo = first.lo, khi = p.tasks[blk.t0 + blk.nq - 1].hi;
@@ -954,7 +958,7 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (q < blk.nq)
             v = *reinterpret_cast<const float4 *>(p.tasks[blk.t0 + q].q_raw + (size_t)(r - q * kHeads) * HD + 4 * q4);
-        *reinterpret_cast<float4 *>(q_s + (size_t)r * KS + 4 * q4) = v;
+        *reinterpret_cast<float4 *>(q_s + (size_t)r * HD + 4 * q4) = v;
     }
     auto stage = [&](int c, int b) {
         const int r0 = klo + c * kPromptKeys, nr = min(kPromptKeys, khi - r0);
@@ -970,7 +974,7 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
         ptx::cp_async_commit();
     };
     const int kg = lane >> 4, l = lane & 15;
-    const float *qb = q_s + (size_t)(warp * kHeads) * KS + l;
+    const float *qb = q_s + (size_t)(warp * kHeads) * HD + l;
     int b = 0;
     stage(blockIdx.y, 0);
     for (int c = blockIdx.y; c < n_chunks; c += gridDim.y) {
@@ -991,7 +995,7 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
         for (int m = 0; m < HD / 16; m++) {
             float qv[kHeads], kv[4];
 #pragma unroll
-            for (int j = 0; j < kHeads; j++) qv[j] = qb[j * KS + 16 * m];
+            for (int j = 0; j < kHeads; j++) qv[j] = qb[j * HD + 16 * m];
 #pragma unroll
             for (int i = 0; i < 4; i++) kv[i] = kb[i * KS + 16 * m];
 #pragma unroll
@@ -1093,7 +1097,7 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
     extern __shared__ float4 dyn4[];
     float *v_s = reinterpret_cast<float *>(dyn4);  // [2][KC][VC]
     float *p_s = v_s + 2 * KC * VC;                // [2][KC][64]
-    const PromptBlock blk = prompt_block(blockIdx.x, cl);
+    const PromptBlock blk = prompt_block(gridDim.x - 1 - blockIdx.x, cl);  // longest ranges first
     const int col0 = blockIdx.y * VC;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = warp * 2 + (lane >> 4), cq = lane & 15;
@@ -1337,7 +1341,7 @@ template <int HD>
 cudaError_t launch_prompt_hd(const DecodeParams &p, int n_tasks, int cl, int n_blocks, int splits, cudaStream_t s,
                              bool pdl) {
     constexpr int KS = HD + 4;
-    const size_t sc_smem = ((size_t)(kPromptQH + 2 * kPromptKeys) * KS + kPromptQH * kPromptKeys * kPromptRed) *
+    const size_t sc_smem = ((size_t)kPromptQH * HD + 2 * kPromptKeys * KS + kPromptQH * kPromptKeys * kPromptRed) *
                            sizeof(float);
     const size_t pv_smem = (size_t)2 * kPromptPvKeys * (kPromptPvCols + kPromptQH) * sizeof(float);
     cudaFuncSetAttribute(prompt_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem);
