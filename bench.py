@@ -674,18 +674,19 @@ def run_case(torch, g4a, spec: str, reps: int, warmup: int):
     for configuration 1 alone (35 layer-equivalents in one call), or
     "decode-batch1" for configuration 0's latency, "q8-head[:rows]" for
     the Q8_0 output-head mat-vec (262,144 rows unless given), or
-    "decoder-prompt[:batch[:length]]" for g4a_model_prefill alone,
+    "decoder-prompt[:batch[:length[:vocab]]]" for g4a_model_prefill alone,
     "decoder[:b1,b2,...[:new_tokens]]" for configuration 4's decoder at
     those batch sizes (a short run when new_tokens is given), or
     "q8-gemm:rows:cols:n_vec[:geglu]" for the batched Q8_0 kernel alone."""
     ctx = g4a.Context(0, max_positions=MAX_CTX + 128)
     if spec.startswith("decoder-prompt"):
-        # decoder-prompt[:batch[:length]] -- g4a_model_prefill alone
+        # decoder-prompt[:batch[:length[:vocab]]] -- g4a_model_prefill alone (a
+        # smaller vocabulary keeps a profiling run's device memory small)
         import g4attn.model as gm
         parts = spec.split(":")
         batch = int(parts[1]) if len(parts) > 1 else 1
         length = int(parts[2]) if len(parts) > 2 else 628
-        w = gm.synthetic_weights(ctx, seed=4)
+        w = gm.synthetic_weights(ctx, seed=4, **({"vocab": int(parts[3])} if len(parts) > 3 else {}))
         res = measure_prompt(torch, gm, ctx, w, batch=batch, length=length, token_by_token=False)
         del w
         ctx.close()

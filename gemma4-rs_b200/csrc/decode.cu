@@ -973,6 +973,25 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
         }
         ptx::cp_async_commit();
     };
+    // the two (query, head) rows whose sums this thread writes: pair tid and
+    // tid + 256 of each chunk's table, i.e. rows tid / 8 and tid / 8 + 32
+    int s_lo[2], s_hi[2];
+    float s_scale[2], *s_row[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const int qh = tid / kPromptKeys + 32 * u, q = qh / kHeads;
+        s_lo[u] = 0;
+        s_hi[u] = 0;
+        s_scale[u] = 1.0f;
+        s_row[u] = p.scores;
+        if (q < blk.nq) {
+            const DecodeTask &tk = p.tasks[blk.t0 + q];
+            s_lo[u] = tk.lo;
+            s_hi[u] = tk.hi;
+            s_scale[u] = tk.scale;
+            s_row[u] = p.scores + ((size_t)(blk.t0 + q) * kHeads + (qh - q * kHeads)) * p.max_rows;
+        }
+    }
     const int kg = lane >> 4, l = lane & 15;
     const float *qb = q_s + (size_t)(warp * kHeads) * HD + l;
     int b = 0;
@@ -1009,24 +1028,23 @@ __global__ void __launch_bounds__(256) prompt_scores_kernel(DecodeParams p, int 
             for (int i = 0; i < 4; i++)
                 red[((warp * kHeads + j) * kPromptKeys + kg * 4 + i) * kPromptRed + l] = acc[j][i];
         __syncthreads();
-        // lanes added in order, one (row, key) pair at a time per thread
-        const int r0 = klo + c * kPromptKeys;
-        for (int pr = tid; pr < kPromptQH * kPromptKeys; pr += 256) {
-            const int qh = pr / kPromptKeys, q = qh / kHeads, h = qh - q * kHeads, k = r0 + (pr - qh * kPromptKeys);
-            if (q >= blk.nq) continue;
-            const DecodeTask &tk = p.tasks[blk.t0 + q];
-            if (k < tk.lo || k >= tk.hi) continue;
-            const float4 *rp = reinterpret_cast<const float4 *>(red + (size_t)pr * kPromptRed);
-            float s = -0.0f;
+        // lanes added in order; thread tid takes the pairs tid and tid + 256
+        // of the table (its two rows and key fixed, set up before the loop)
+        const int k = klo + c * kPromptKeys + (tid & (kPromptKeys - 1));
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float4 v = rp[u];
-                s = __fadd_rn(s, v.x);
-                s = __fadd_rn(s, v.y);
-                s = __fadd_rn(s, v.z);
-                s = __fadd_rn(s, v.w);
+        for (int u = 0; u < 2; u++) {
+            if (k < s_lo[u] || k >= s_hi[u]) continue;  // also rows past the block (empty range)
+            const float4 *rp = reinterpret_cast<const float4 *>(red + (size_t)(tid + 256 * u) * kPromptRed);
+            float sum = -0.0f;
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                const float4 v = rp[w];
+                sum = __fadd_rn(sum, v.x);
+                sum = __fadd_rn(sum, v.y);
+                sum = __fadd_rn(sum, v.z);
+                sum = __fadd_rn(sum, v.w);
             }
-            p.scores[((size_t)(blk.t0 + q) * kHeads + h) * p.max_rows + (k - tk.lo)] = __fmul_rn(s, tk.scale);
+            s_row[u][k - s_lo[u]] = __fmul_rn(sum, s_scale[u]);
         }
         __syncthreads();  // the lane table and this chunk's buffer are rewritten next
         b ^= 1;
@@ -1083,14 +1101,14 @@ __global__ void __launch_bounds__(256) prompt_softmax_kernel(DecodeParams p, int
     for (int r = lane; r < rows; r += 32) s[r] = __fdiv_rn(s[r], total);
 }
 
-// grid (blocks, HD / 64), 128 threads: warp w accumulates queries 2w and
-// 2w + 1 (a half-warp each) over 64 columns, lane & 15 = a quad of columns,
-// all eight heads; V rows and the probabilities of the block's 64 rows are
-// staged per chunk of kPromptPvKeys keys.
+// grid (blocks, HD / 64), 256 threads: warp w accumulates query w over 64
+// columns, lane = a pair of columns, all eight heads (each key's eight
+// probabilities one broadcast per warp); V rows and the probabilities of the
+// block's 64 rows are staged per chunk of kPromptPvKeys keys.
 constexpr int kPromptPvCols = 64;
 
 template <int HD>
-__global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) {
+__global__ void __launch_bounds__(256) prompt_pv_kernel(DecodeParams p, int cl) {
     ptx::pdl_trigger();
     ptx::pdl_wait();
     constexpr int VC = kPromptPvCols, KC = kPromptPvKeys;
@@ -1100,13 +1118,12 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
     const PromptBlock blk = prompt_block(gridDim.x - 1 - blockIdx.x, cl);  // longest ranges first
     const int col0 = blockIdx.y * VC;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int q = warp * 2 + (lane >> 4), cq = lane & 15;
     const DecodeTask &first = p.tasks[blk.t0];
     const int klo = first.lo, khi = p.tasks[blk.t0 + blk.nq - 1].hi;
     const int n_chunks = (khi - klo + KC - 1) / KC;
     const int32_t *bt = p.block_table ? p.block_table + (size_t)first.seq * p.max_pages : nullptr;
-    // probability gather: thread = (row gq, keys gk .. gk + 15 of the chunk)
-    const int gq = tid & (kPromptQH - 1), gk = (tid / kPromptQH) * 16;
+    // probability gather: thread = (row gq, keys gk .. gk + 7 of the chunk)
+    const int gq = tid & (kPromptQH - 1), gk = (tid / kPromptQH) * 8;
     const int gq_q = gq / kHeads;
     int g_lo = 0, g_hi = 0;
     const float *g_row = p.scores;
@@ -1116,11 +1133,11 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
         g_hi = gt.hi;
         g_row = p.scores + ((size_t)(blk.t0 + gq_q) * kHeads + (gq - gq_q * kHeads)) * p.max_rows;
     }
-    float pf[16];
+    float pf[8];
     auto load_p = [&](int c) {
         const int k0 = klo + c * KC + gk;
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < 8; j++) {
             const int k = k0 + j;
             pf[j] = (k >= g_lo && k < g_hi) ? g_row[k - g_lo] : 0.0f;
         }
@@ -1128,12 +1145,12 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
     auto store_p = [&](int b) {
         float *d = p_s + (size_t)b * KC * kPromptQH;
 #pragma unroll
-        for (int j = 0; j < 16; j++) d[(gk + j) * kPromptQH + gq] = pf[j];
+        for (int j = 0; j < 8; j++) d[(gk + j) * kPromptQH + gq] = pf[j];
     };
     auto stage_v = [&](int c, int b) {
         const int r0 = klo + c * KC, nr = min(KC, khi - r0);
         float *dst = v_s + (size_t)b * KC * VC;
-        for (int e = tid; e < KC * (VC / 4); e += 128) {
+        for (int e = tid; e < KC * (VC / 4); e += 256) {
             const int r = e / (VC / 4), q4 = e - r * (VC / 4);
             float *d = dst + (size_t)r * VC + 4 * q4;
             if (r < nr)
@@ -1143,11 +1160,9 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
         }
         ptx::cp_async_commit();
     };
-    float acc[kHeads][4];
+    float acc[kHeads][2];
 #pragma unroll
-    for (int h = 0; h < kHeads; h++)
-#pragma unroll
-        for (int u = 0; u < 4; u++) acc[h][u] = 0.0f;
+    for (int h = 0; h < kHeads; h++) acc[h][0] = acc[h][1] = 0.0f;
     load_p(0);
     store_p(0);
     stage_v(0, 0);
@@ -1162,11 +1177,11 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
             ptx::cp_async_wait<0>();
         }
         __syncthreads();
-        const float *vb = v_s + (size_t)b * KC * VC + 4 * cq;
-        const float *pb = p_s + (size_t)b * KC * kPromptQH + q * kHeads;
-#pragma unroll 4
+        const float *vb = v_s + (size_t)b * KC * VC + 2 * lane;
+        const float *pb = p_s + (size_t)b * KC * kPromptQH + warp * kHeads;
+#pragma unroll 8
         for (int k = 0; k < KC; k++) {  // key order
-            const float4 v = *reinterpret_cast<const float4 *>(vb + (size_t)k * VC);
+            const float2 v = *reinterpret_cast<const float2 *>(vb + (size_t)k * VC);
             const float4 p0 = *reinterpret_cast<const float4 *>(pb + (size_t)k * kPromptQH);
             const float4 p1 = *reinterpret_cast<const float4 *>(pb + (size_t)k * kPromptQH + 4);
             const float pp[kHeads] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
@@ -1174,20 +1189,17 @@ __global__ void __launch_bounds__(128) prompt_pv_kernel(DecodeParams p, int cl) 
             for (int h = 0; h < kHeads; h++) {
                 acc[h][0] = __fadd_rn(acc[h][0], __fmul_rn(pp[h], v.x));
                 acc[h][1] = __fadd_rn(acc[h][1], __fmul_rn(pp[h], v.y));
-                acc[h][2] = __fadd_rn(acc[h][2], __fmul_rn(pp[h], v.z));
-                acc[h][3] = __fadd_rn(acc[h][3], __fmul_rn(pp[h], v.w));
             }
         }
         __syncthreads();  // both buffers of this chunk are free
         if (more) store_p(b ^ 1);
         b ^= 1;
     }
-    if (q < blk.nq) {
-        const DecodeTask &tk = p.tasks[blk.t0 + q];
+    if (warp < blk.nq) {
+        const DecodeTask &tk = p.tasks[blk.t0 + warp];
 #pragma unroll
         for (int h = 0; h < kHeads; h++)
-            *reinterpret_cast<float4 *>(tk.out + (size_t)h * HD + col0 + 4 * cq) =
-                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+            *reinterpret_cast<float2 *>(tk.out + (size_t)h * HD + col0 + 2 * lane) = make_float2(acc[h][0], acc[h][1]);
     }
 }
 
@@ -1351,7 +1363,7 @@ cudaError_t launch_prompt_hd(const DecodeParams &p, int n_tasks, int cl, int n_b
     if (e == cudaSuccess)
         e = launch_k(pdl, prompt_softmax_kernel, dim3(n_tasks), dim3(256), 0, s, p, n_tasks * kHeads);
     if (e == cudaSuccess)
-        e = launch_k(pdl, prompt_pv_kernel<HD>, dim3(n_blocks, HD / kPromptPvCols), dim3(128), pv_smem, s, p, cl);
+        e = launch_k(pdl, prompt_pv_kernel<HD>, dim3(n_blocks, HD / kPromptPvCols), dim3(256), pv_smem, s, p, cl);
     return e;
 }
 
