@@ -14,56 +14,9 @@
 #include "g4attn_host.cpp"
 
 #include <cstdio>
-#include <cstdlib>
-#include <cstring>
 #include <random>
 
-extern "C" {
-cudaError_t cudaDeviceGetAttribute(int *v, cudaDeviceAttr, int) {
-    *v = 148;
-    return cudaSuccess;
-}
-cudaError_t cudaEventCreate(cudaEvent_t *e) {
-    *e = reinterpret_cast<cudaEvent_t>(std::malloc(8));
-    return cudaSuccess;
-}
-cudaError_t cudaEventCreateWithFlags(cudaEvent_t *e, unsigned) { return cudaEventCreate(e); }
-cudaError_t cudaEventDestroy(cudaEvent_t e) {
-    std::free(e);
-    return cudaSuccess;
-}
-cudaError_t cudaEventElapsedTime(float *ms, cudaEvent_t, cudaEvent_t) {
-    *ms = 0.0f;
-    return cudaSuccess;
-}
-cudaError_t cudaEventRecord(cudaEvent_t, cudaStream_t) { return cudaSuccess; }
-cudaError_t cudaEventSynchronize(cudaEvent_t) { return cudaSuccess; }
-cudaError_t cudaFree(void *p) {
-    std::free(p);
-    return cudaSuccess;
-}
-cudaError_t cudaFreeHost(void *p) { return cudaFree(p); }
-const char *cudaGetErrorString(cudaError_t) { return "host stand-in"; }
-cudaError_t cudaMalloc(void **p, size_t n) {
-    *p = std::aligned_alloc(256, (n + 255) / 256 * 256);
-    return *p ? cudaSuccess : cudaErrorMemoryAllocation;
-}
-cudaError_t cudaHostAlloc(void **p, size_t n, unsigned) { return cudaMalloc(p, n); }
-cudaError_t cudaMemcpy(void *d, const void *s, size_t n, cudaMemcpyKind) {
-    std::memcpy(d, s, n);
-    return cudaSuccess;
-}
-cudaError_t cudaMemcpyAsync(void *d, const void *s, size_t n, cudaMemcpyKind k, cudaStream_t) {
-    return cudaMemcpy(d, s, n, k);
-}
-cudaError_t cudaMemset(void *d, int v, size_t n) {
-    std::memset(d, v, n);
-    return cudaSuccess;
-}
-cudaError_t cudaMemsetAsync(void *d, int v, size_t n, cudaStream_t) { return cudaMemset(d, v, n); }
-cudaError_t cudaSetDevice(int) { return cudaSuccess; }
-cudaError_t cudaStreamSynchronize(cudaStream_t) { return cudaSuccess; }
-}
+#include "cuda_host_stubs.h"
 
 namespace g4a {
 cudaError_t launch_view(const ViewParams &, int, cudaStream_t) { return cudaSuccess; }
