@@ -597,7 +597,7 @@ struct Plan {
     std::vector<int32_t> cta_start;    // f16 kernel: per-CTA item ranges (items[0] holds all items)
     // assign_ctas scratch
     std::vector<DecodeItem> all;
-    std::vector<uint64_t> keys, heap;
+    std::vector<uint64_t> keys, keys_tmp, heap;
     std::vector<int32_t> cta_of, fill;
     void clear() {
         tasks.clear();
@@ -804,22 +804,50 @@ void assign_ctas(Plan &plan, int n_sm) {
     // (~cost, position) packed: an ascending sort is longest first, stable
     std::vector<uint64_t> &keys = plan.keys;
     keys.resize(n);
+    uint64_t max_cost = 0;
     for (size_t i = 0; i < n; i++) {
         const DecodeItem &it = all[i];
         const DecodeTask &t = plan.tasks[it.task];
         const uint64_t cost = (uint64_t)((int64_t)(it.row_hi - it.row_lo) * (t.hd / 256) + 64 + (t.n_splits > 1 ? 32 : 0));
         keys[i] = ((~cost & 0xFFFFFFFFFFull) << 24) | (uint64_t)i;
+        max_cost = std::max(max_cost, cost);
     }
-    std::sort(keys.begin(), keys.end());
+    if (max_cost < (1u << 16)) {
+        // the same order by a stable radix sort of 65535 - cost (two 8-bit
+        // passes), the keys being in position order to begin with
+        std::vector<uint64_t> &tmp = plan.keys_tmp;
+        tmp.resize(n);
+        for (int pass = 0; pass < 2; pass++) {
+            auto digit = [pass](uint64_t key) {
+                const uint32_t cost = (uint32_t)(~(key >> 24) & 0xFFFFFFFFFFull);
+                return ((65535u - cost) >> (8 * pass)) & 255u;
+            };
+            uint32_t start[257] = {};
+            for (const uint64_t key : keys) start[digit(key) + 1]++;
+            for (int d = 0; d < 256; d++) start[d + 1] += start[d];
+            for (const uint64_t key : keys) tmp[start[digit(key)]++] = key;
+            keys.swap(tmp);
+        }
+    } else {
+        std::sort(keys.begin(), keys.end());
+    }
     const int n_ctas = std::max(1, std::min<int>(n_sm, (int)n));
-    // min-heap of (load, cta) packed
+    // min-heap of (load, cta) packed. The first n_ctas items meet empty CTAs
+    // (every cost is positive), so item j goes to CTA j; the heap starts after.
     std::vector<uint64_t> &heap = plan.heap;
     heap.resize(n_ctas);
-    for (int b = 0; b < n_ctas; b++) heap[b] = (uint64_t)b;
     std::vector<int32_t> &cta_of = plan.cta_of;
     cta_of.resize(n);
     plan.cta_start.assign(n_ctas + 1, 0);
-    for (size_t j = 0; j < n; j++) {
+    const size_t head = std::min<size_t>(n, (size_t)n_ctas);
+    for (size_t j = 0; j < head; j++) {
+        const uint64_t cost = ~(keys[j] >> 24) & 0xFFFFFFFFFFull;
+        heap[j] = (cost << 24) | (uint64_t)j;
+        cta_of[j] = (int32_t)j;
+        plan.cta_start[j + 1]++;
+    }
+    std::make_heap(heap.begin(), heap.end(), std::greater<uint64_t>());
+    for (size_t j = head; j < n; j++) {
         const uint64_t cost = ~(keys[j] >> 24) & 0xFFFFFFFFFFull;
         std::pop_heap(heap.begin(), heap.end(), std::greater<uint64_t>());
         const int b = (int)(heap.back() & 0xFFFFFFull);
