@@ -118,7 +118,8 @@ cudaError_t launch_task_append(const DecodeParams &p, int hd, int n_tasks, cudaS
 // The exact attention of a prompt chunk: tasks s*cl .. s*cl + cl - 1 are cl
 // consecutive positions of one sequence (rows stored beforehand, new_row -1),
 // each task's output the exact kernels' bit for bit. Scores, softmax and
-// probabilities in p.scores ([tasks][heads][max_rows]).
+// probabilities in p.scores ([tasks][heads][max_rows]). The tasks' q rows are
+// normalized and rotated in place (q_raw is overwritten unless q_ready).
 cudaError_t launch_prompt_exact(const DecodeParams &p, int hd, int n_tasks, int cl, cudaStream_t s, bool pdl = false);
 // f16 paged caches (decode_f16_sm100.cu): persistent, TMA + tensor cores.
 constexpr int kF16MaxSplits = 96;  // merge weights fit the kernel's shared buffer
