@@ -7,7 +7,7 @@
 // chunking.
 //
 // A step is one fixed sequence of launches on the model's own stream (about
-// 16 per layer): the attention plan, embedding, per-layer inputs, then per
+// 10 per layer at small batches): the attention plan, embedding, per-layer inputs, then per
 // layer the fused residual/norm/quantize kernels, the Q8_0 mat-vecs and the
 // fused decode attention, then the soft-capped head and the argmax. Every
 // kernel rounds as the reference does (integer Q8_0 dots summed in block
