@@ -24,6 +24,10 @@ queries and outputs stay where they are.
 The collective and merge schedule is written against three small callables so
 that it can be checked on CPU ranks (gloo) with a numpy stand-in for the
 attention arithmetic; the product path passes the CUDA library's functions.
+
+The second schedule below (cp_prefill_kv_shards) keeps the keys and values
+where they are and merges the ranks' partial outputs by log-sum-exp across
+ranks (an all-reduce of the maxima, a reduce-scatter of the weighted sums).
 """
 from __future__ import annotations
 
@@ -153,3 +157,125 @@ def g4a_merge(ctx, torch, head_dim: int):
             parts = [(o, l)] + parts
         return parts[0][0]
     return merge
+
+
+# ---------------------------------------------------------------------------
+# Key/value shards with a cross-rank log-sum-exp merge
+# ---------------------------------------------------------------------------
+#
+# The other partition of the same problem: each rank keeps only its own key/
+# value chunks (the zigzag pair above, so that causal work stays balanced)
+# and attends every query that sees them. Per rank and query row that gives a
+# normalized partial output O_r and its log-sum-exp l_r (rows that see none of
+# the rank's keys: O_r = 0, l_r = -inf). Then
+#
+#   M   = max over ranks of l_r          (all-reduce, MAX, [T, heads])
+#   w_r = exp(l_r - M)                   (0 where l_r = -inf)
+#   O   = sum_r w_r O_r / sum_r w_r       (reduce-scatter, SUM, of w_r O_r and
+#                                         w_r: each rank receives the rows of
+#                                         its own two query chunks)
+#
+# No key/value row leaves its rank; the queries are all-gathered first and
+# the partial outputs (f32, all rows) cross the links once, so this moves
+# about 2 x T x heads x hd x 4 bytes per rank against the all-gather
+# schedule's 2 x T x hd x 2 in all.
+
+
+def kv_shard_problems(seq_len: int, world: int, rank: int) -> list[tuple[int, int, int, int]]:
+    """(q0, q1, k0, k1) for each of this rank's two key chunks: every query at
+    or after the chunk's first position sees it (causal)."""
+    return [(k0, seq_len, k0, k1) for k0, k1 in zigzag_chunks(seq_len, world, rank)]
+
+
+def rank_rows(seq_len: int, world: int) -> list[tuple[int, int]]:
+    """Row ranges in the order a reduce-scatter hands them out: rank 0's two
+    query chunks, then rank 1's, ..."""
+    return [c for r in range(world) for c in zigzag_chunks(seq_len, world, r)]
+
+
+def cp_prefill_kv_shards(q_all, k_chunks: Sequence, v_chunks: Sequence, seq_len: int, world: int, rank: int, be):
+    """Runs the key/value-shard schedule on one rank.
+
+    q_all: [T, heads, hd] queries (every rank's, as gathered); k_chunks /
+    v_chunks: this rank's two key/value chunks [c, hd].
+    be: the arithmetic and collectives, with
+      attend(problems, q_all, k_chunks, v_chunks) -> [(out [n, heads, hd], lse [n, heads])]
+          (problem i uses key chunk i);
+      partial(seq_len, problems, results) -> (O [T, heads, hd], lse [T, heads]):
+          this rank's two results on all rows, merged where both apply;
+      allreduce_max(lse) -> M;  weights(lse, M) -> exp(lse - M), 0 at -inf;
+      scale(O, w) -> w O;  to_rank_order(x, rows) -> x's row ranges `rows`
+          concatenated;  reduce_scatter_sum(x) -> this rank's 2c rows of the
+          sum over ranks;  finish(X, w) -> X / w.
+    Returns this rank's two output chunks [c, heads, hd] (chunks r and
+    2W-1-r)."""
+    problems = kv_shard_problems(seq_len, world, rank)
+    results = be.attend(problems, q_all, k_chunks, v_chunks)
+    o_r, lse_r = be.partial(seq_len, problems, results)
+    m = be.allreduce_max(lse_r)
+    w = be.weights(lse_r, m)
+    rows = rank_rows(seq_len, world)
+    x = be.reduce_scatter_sum(be.to_rank_order(be.scale(o_r, w), rows))
+    ws = be.reduce_scatter_sum(be.to_rank_order(w, rows))
+    out = be.finish(x, ws)
+    c = seq_len // (2 * world)
+    return [out[:c], out[c:]]
+
+
+class TorchKvShardBackend:
+    """The key/value-shard schedule on the GPU: g4a_prefill for the partial
+    attention (with position offsets and the log-sum-exp), g4a_lse_merge for
+    the rank's own two partials, NCCL through torch.distributed for the
+    all-reduce and the reduce-scatter, elementwise weights in torch."""
+
+    def __init__(self, ctx, torch, dist, head_dim: int, heads: int = 8):
+        self.ctx, self.torch, self.dist, self.hd, self.heads = ctx, torch, dist, head_dim, heads
+
+    def attend(self, problems, q_all, k_chunks, v_chunks):
+        torch, specs, outs = self.torch, [], []
+        for i, (q0, q1, k0, k1) in enumerate(problems):
+            out = torch.empty(q1 - q0, self.heads, self.hd, device=q_all.device)
+            lse = torch.empty(q1 - q0, self.heads, device=q_all.device)
+            specs.append(dict(head_dim=self.hd, window=0, n_q=q1 - q0, q_pos0=q0, n_kv=k1 - k0, kv_pos0=k0,
+                              q=q_all[q0:q1], k=k_chunks[i], v=v_chunks[i], out=out, lse=lse))
+            outs.append((out, lse))
+        self.ctx.prefill(specs)
+        return outs
+
+    def partial(self, seq_len, problems, results):
+        torch = self.torch
+        (a0, _, _, _), (b0, _, _, _) = problems
+        (oa, la), (ob, lb) = results
+        o = torch.zeros(seq_len, self.heads, self.hd, device=oa.device)
+        lse = torch.full((seq_len, self.heads), float("-inf"), device=oa.device)
+        o[a0:b0] = oa[:b0 - a0]
+        lse[a0:b0] = la[:b0 - a0]
+        n = seq_len - b0  # rows that see both chunks
+        o_both, l_both = o[b0:], lse[b0:]
+        self.ctx.lse_merge([oa[b0 - a0:].contiguous(), ob], [la[b0 - a0:].contiguous(), lb], n, self.heads, self.hd,
+                           o_both, l_both)
+        return o, lse
+
+    def allreduce_max(self, lse):
+        m = lse.clone()
+        self.dist.all_reduce(m, op=self.dist.ReduceOp.MAX)
+        return m
+
+    def weights(self, lse, m):
+        torch = self.torch
+        return torch.where(torch.isfinite(lse), torch.exp(lse - m), torch.zeros_like(lse))
+
+    def scale(self, o, w):
+        return o * w[..., None]
+
+    def to_rank_order(self, x, rows):
+        return self.torch.cat([x[a:b] for a, b in rows]).contiguous()
+
+    def reduce_scatter_sum(self, x):
+        world = self.dist.get_world_size()
+        out = self.torch.empty((x.shape[0] // world,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        self.dist.reduce_scatter_tensor(out, x, op=self.dist.ReduceOp.SUM)
+        return out
+
+    def finish(self, x, w):
+        return x / w[..., None]

@@ -1,7 +1,10 @@
-"""Context-parallel prefill schedule on CPU ranks (gloo, world size 2 and 4):
-zigzag chunking, the key/value all-gather, which (query, key) chunk pairs each
-rank computes, and the log-sum-exp merge, with a float64 numpy stand-in for
-the attention arithmetic. The result must equal plain causal attention."""
+"""Context-parallel prefill schedules on CPU ranks (gloo, world size 2 and 4),
+with a float64 numpy stand-in for the attention arithmetic; the result must
+equal plain causal attention:
+* the all-gather schedule: zigzag chunking, the key/value all-gather, which
+  (query, key) chunk pairs each rank computes, the local log-sum-exp merge;
+* the key/value-shard schedule: each rank's partials over all rows, the
+  all-reduce of the maxima and the reduce-scatter of the weighted sums."""
 import os
 import sys
 from pathlib import Path
@@ -117,3 +120,112 @@ def test_zigzag_chunks_cover_the_sequence():
         assert all(cov[i][1] == cov[i + 1][0] for i in range(len(cov) - 1))
     with pytest.raises(ValueError):
         cp.zigzag_chunks(100, 8, 0)
+
+
+class _NpKvShards:
+    """The key/value-shard schedule's arithmetic in float64 numpy, its
+    collectives over gloo (the reduce-scatter as an all-reduce and this
+    rank's slice)."""
+
+    def __init__(self, dist, torch, world, rank):
+        self.dist, self.torch, self.world, self.rank = dist, torch, world, rank
+
+    def attend(self, problems, q_all, k_chunks, v_chunks):
+        from g4attn import cp
+        probs = [cp.Problem(0, q0, q1, k0, k1, i) for i, (q0, q1, k0, k1) in enumerate(problems)]
+        out = []
+        for p in probs:
+            out += _np_attend([p], [q_all[p.q0:p.q1]], lambda p: k_chunks[p.own], lambda p: v_chunks[p.own])
+        return out
+
+    def partial(self, seq_len, problems, results):
+        (a0, _, _, _), (b0, _, _, _) = problems
+        (oa, la), (ob, lb) = results
+        hd = oa.shape[-1]
+        o = np.zeros((seq_len, 8, hd))
+        lse = np.full((seq_len, 8), -np.inf)
+        o[a0:b0], lse[a0:b0] = oa[:b0 - a0], la[:b0 - a0]
+        both = [(oa[b0 - a0:], la[b0 - a0:]), (ob, lb)]
+        o[b0:] = _np_merge(both)
+        m = np.maximum(both[0][1], both[1][1])
+        lse[b0:] = m + np.log(np.exp(both[0][1] - m) + np.exp(both[1][1] - m))
+        return o, lse
+
+    def allreduce_max(self, lse):
+        t = self.torch.from_numpy(lse.copy())
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t.numpy()
+
+    def weights(self, lse, m):
+        return np.where(np.isfinite(lse), np.exp(np.where(np.isfinite(lse), lse - m, 0.0)), 0.0)
+
+    def scale(self, o, w):
+        return o * w[..., None]
+
+    def to_rank_order(self, x, rows):
+        return np.concatenate([x[a:b] for a, b in rows])
+
+    def reduce_scatter_sum(self, x):
+        t = self.torch.from_numpy(np.ascontiguousarray(x))
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        n = x.shape[0] // self.world
+        return t.numpy()[self.rank * n:(self.rank + 1) * n]
+
+    def finish(self, x, w):
+        return x / w[..., None]
+
+
+def _kv_shard_rank_main(rank, world, port, T, hd, result_dir):
+    sys.path.insert(0, str(ROOT / "gemma4-rs_b200"))
+    import torch
+    import torch.distributed as dist
+    from g4attn import cp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    r = np.random.default_rng(9)
+    q = r.standard_normal((T, 8, hd)) / np.sqrt(hd)
+    k = r.standard_normal((T, hd))
+    v = r.standard_normal((T, hd))
+    chunks = cp.zigzag_chunks(T, world, rank)
+    outs = cp.cp_prefill_kv_shards(q, [k[a:b] for a, b in chunks], [v[a:b] for a, b in chunks], T, world, rank,
+                                   _NpKvShards(dist, torch, world, rank))
+    err = 0.0
+    for (a, b), o in zip(chunks, outs):
+        s = np.einsum("thd,kd->thk", q[a:b], k)
+        s = np.where(np.arange(T)[None, None, :] <= np.arange(a, b)[:, None, None], s, -np.inf)
+        s -= s.max(-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(-1, keepdims=True)
+        err = max(err, float(np.max(np.abs(p @ v - o))))
+    Path(result_dir, f"kv{rank}.txt").write_text(f"{err}")
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_kv_shard_schedule_matches_causal_attention(tmp_path, world):
+    """Key/value shards and the cross-rank log-sum-exp merge (all-reduce of
+    the maxima, reduce-scatter of the weighted partials): every rank's output
+    chunks equal plain causal attention."""
+    import torch.multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    T, hd = 64, 16
+    mp.start_processes(_kv_shard_rank_main, args=(world, port, T, hd, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for rank in range(world):
+        assert float(Path(tmp_path, f"kv{rank}.txt").read_text()) < 1e-12, rank
+
+
+def test_kv_shard_rows_cover_the_sequence():
+    sys.path.insert(0, str(ROOT / "gemma4-rs_b200"))
+    from g4attn import cp
+    for world in (1, 2, 4, 8):
+        rows = cp.rank_rows(1024, world)
+        assert sorted(rows) == [(i * 1024 // (2 * world), (i + 1) * 1024 // (2 * world)) for i in range(2 * world)]
+        for rank in range(world):
+            probs = cp.kv_shard_problems(1024, world, rank)
+            assert [p[2:] for p in probs] == cp.zigzag_chunks(1024, world, rank)
+            assert all(p[0] == p[2] and p[1] == 1024 for p in probs)

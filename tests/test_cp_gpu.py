@@ -62,3 +62,37 @@ def test_cp_prefill_matches_oracle(oracle, ctx, torch_cuda, world, T):
             got[a:b] = o.cpu().numpy()
     want = oracle.prefill_attend(q, k, v, 8, 0)
     assert max_abs_diff(got, want) <= TOL
+
+
+@pytest.mark.parametrize("world,T", [(2, 512), (4, 1024)])
+def test_kv_shard_merge_matches_oracle(oracle, ctx, torch_cuda, world, T):
+    """The key/value-shard partition's arithmetic on one GPU: each emulated
+    rank's partial outputs and log-sum-exps over all rows (g4a_prefill on its
+    two key chunks, g4a_lse_merge of the two), then the cross-rank maximum,
+    weights and sums that the all-reduce and reduce-scatter carry, done here
+    in one process; every rank's rows match the oracle's causal prefill."""
+    from g4attn import cp
+    torch = torch_cuda
+    hd = 512
+    r = rng(5000 + world)
+    q = oracle.round_bf16(unit_rms_rows(r.standard_normal((T, 8, hd)).astype(np.float32)))
+    k = oracle.round_bf16(unit_rms_rows(r.standard_normal((T, hd)).astype(np.float32)))
+    v = oracle.round_bf16(r.standard_normal((T, hd)).astype(np.float32))
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda().to(torch.bfloat16)
+    be = cp.TorchKvShardBackend(ctx, torch, None, hd)
+    q_all = dev(q)
+    rows = cp.rank_rows(T, world)
+    parts = []
+    for rank in range(world):
+        chunks = cp.zigzag_chunks(T, world, rank)
+        probs = cp.kv_shard_problems(T, world, rank)
+        res = be.attend(probs, q_all, [dev(k[a:b]) for a, b in chunks], [dev(v[a:b]) for a, b in chunks])
+        parts.append(be.partial(T, probs, res))
+    m = torch.stack([p[1] for p in parts]).amax(0)
+    x = sum(be.to_rank_order(be.scale(o, be.weights(l, m)), rows) for o, l in parts)
+    w = sum(be.to_rank_order(be.weights(l, m), rows) for o, l in parts)
+    got = be.finish(x, w)
+    ctx.sync()
+    ref = oracle.prefill_attend(q, k, v, 8, 0)
+    want = np.concatenate([ref[a:b] for a, b in rows])
+    assert max_abs_diff(got.cpu().numpy(), want) <= TOL
