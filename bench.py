@@ -211,14 +211,123 @@ def cpu_decode_rate(ctx_lens, budget_s: float, threads: int = 0, max_seqs: int =
     return done / el, cores, desc
 
 
+def _unit_rows_bf16(oracle, r, *shape):
+    x = r.standard_normal(shape).astype(np.float32)
+    x = x / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)).astype(np.float32)
+    return oracle.round_bf16(x)
+
+
+def cpu_batch1_latency(budget_s: float = 2.0):
+    """Configuration 0 on the host cores: the reference's attention block
+    (model.rs:393-410 without the projections: norms, RoPE, append, view,
+    window, the concat copy and the head-parallel attend) at position 627 on
+    layers 13 and 14 over f32 caches of 627 rows, repeated (the repeats append
+    past the attended range, so each does the same work). Microseconds per
+    layer, median of the repeats."""
+    import oracle
+    cores = oracle.pool_init(0)
+    hp = oracle.hparams_e2b()
+    ff = oracle.proportional_rope_freq_factors(HD_G, hp.global_p)
+    r = np.random.default_rng(628)
+    res = {}
+    for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
+        kv = oracle.KvCache()
+        kv.append_rows(layer, r.standard_normal((627, hd)).astype(np.float32),
+                       r.standard_normal((627, hd)).astype(np.float32))
+        q, k, v = (r.standard_normal(n).astype(np.float32) for n in (HEADS * hd, hd, hd))
+        w = np.ones(hd, np.float32)
+        ts = []
+        t_end = time.perf_counter() + budget_s / 2
+        while time.perf_counter() < t_end or len(ts) < 5:
+            t0 = time.perf_counter()
+            kv.attention_block(hp, layer, 627, q, k, v, w, w, ff)
+            ts.append(time.perf_counter() - t0)
+        res["local" if hd == HD_L else "global"] = round(statistics.median(ts) * 1e6, 1)
+    return {"value": round(res["local"] + res["global"], 1), "unit": "us per step (local + global layer)",
+            "us_local": res["local"], "us_global": res["global"], "cores": cores, "kind": "port",
+            "sample": "the full workload: one decode step at position 627, layers 13 and 14, f32 caches; "
+                      "median of repeats"}
+
+
+def cpu_prefill_cfg1(budget_s: float = 6.0):
+    """Configuration 1 on the host cores: the reference's prompt loop (one
+    attend per position, generate.rs:37-41 -> model.rs:345-366, heads on the
+    pool) restated in the oracle, over one sliding layer (628 tokens, window
+    512, 256-wide) and one global layer (628 tokens, 512-wide) on bf16-rounded
+    unit-RMS inputs; the 35-layer time is 28 x the sliding and 7 x the global
+    layer's median."""
+    import oracle
+    cores = oracle.pool_init(0)
+    r = np.random.default_rng(1628)
+    T = 628
+    times = {}
+    for hd, window in ((HD_L, 512), (HD_G, 0)):
+        q = _unit_rows_bf16(oracle, r, T, HEADS, hd)
+        k = _unit_rows_bf16(oracle, r, T, hd)
+        v = oracle.round_bf16(r.standard_normal((T, hd)).astype(np.float32))
+        ts = []
+        t_end = time.perf_counter() + budget_s / 2
+        while time.perf_counter() < t_end or len(ts) < 2:
+            t0 = time.perf_counter()
+            oracle.prefill_attend(q, k, v, HEADS, window)
+            ts.append(time.perf_counter() - t0)
+        times[hd] = statistics.median(ts)
+    total_s = 28 * times[HD_L] + 7 * times[HD_G]
+    flops = 28 * 4 * HEADS * HD_L * prefill_pairs(T, 512) + 7 * 4 * HEADS * HD_G * prefill_pairs(T, 0)
+    return {"value": round(flops / total_s / 1e12, 5), "unit": "TFLOP/s", "ms_35_layers": round(total_s * 1e3, 1),
+            "cores": cores, "kind": "port",
+            "sample": f"one sliding and one global 628-token layer through the token loop "
+                      f"({times[HD_L] * 1e3:.1f} / {times[HD_G] * 1e3:.1f} ms), scaled to 28 + 7 layers"}
+
+
+def cpu_prefill_cfg3(budget_s: float = 8.0, T: int = 32768):
+    """Configuration 3 on the host cores: query rows of the 32,768-token
+    global layer through the reference's attend (each row against its causal
+    keys [0, t]), at evenly spaced positions (the sample's mean pair count is
+    the layer's), as many as the time budget allows; TFLOP/s over the sampled
+    rows and the full layer's time at that rate."""
+    import oracle
+    cores = oracle.pool_init(0)
+    r = np.random.default_rng(3276)
+    k = _unit_rows_bf16(oracle, r, T, HD_G)
+    v = oracle.round_bf16(r.standard_normal((T, HD_G)).astype(np.float32))
+    flops = done = 0
+    n_rows = 0
+    t0 = time.perf_counter()
+    # positions in a van der Corput order over [0, T): any prefix is spread out
+    for i in range(1, T + 1):
+        f, b, x = 0.0, 0.5, i
+        while x:
+            f += b * (x & 1)
+            x >>= 1
+            b *= 0.5
+        t = int(f * T)
+        q = _unit_rows_bf16(oracle, r, HEADS * HD_G)
+        oracle.attend(q, k[: t + 1], v[: t + 1], HEADS, 1, 1.0)
+        flops += 4 * HEADS * HD_G * (t + 1)
+        n_rows += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    rate = flops / dt
+    full = 4 * HEADS * HD_G * (T * (T + 1) // 2)
+    return {"value": round(rate / 1e12, 5), "unit": "TFLOP/s", "s_full_layer": round(full / rate, 1),
+            "cores": cores, "kind": "port",
+            "sample": f"{n_rows} query rows of the 32,768-token layer at spread positions, {dt:.1f} s"}
+
+
 # --------------------------------------------------------------------------
 # GPU measurements
 # --------------------------------------------------------------------------
 
-def build_decode(torch, g4a, ctx, ctx_lens, extra_rows, seed):
+def build_decode(torch, g4a, ctx, ctx_lens, extra_rows, seed, keep=()):
     """Cache filled with each sequence's history (positions 0..c-2), inputs
-    for one decode step at position c-1 on layers 13 and 14."""
+    for one decode step at position c-1 on layers 13 and 14. For the
+    sequences listed in `keep`, the raw history rows (before norm and RoPE)
+    are also returned as host arrays, {(seq, layer): (k, v)}, for a parity
+    check of this exact workload."""
     n = len(ctx_lens)
+    kept = {}
     kv = g4a.KvCache(ctx, n, MAX_CTX + extra_rows, dtype=g4a.KV_F16, layers=[LOCAL_LAYER, GLOBAL_LAYER])
     gen = torch.Generator(device="cuda")
     gen.manual_seed(seed)
@@ -233,6 +342,8 @@ def build_decode(torch, g4a, ctx, ctx_lens, extra_rows, seed):
                 k = torch.randn(hist, hd, device="cuda", generator=gen)
                 v = torch.randn(hist, hd, device="cuda", generator=gen)
                 kv.append_tokens(s, layer, k, v, weights[layer][1])
+                if s in keep:
+                    kept[(s, layer)] = (k.cpu().numpy(), v.cpu().numpy())
     args = {}
     for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
         args[layer] = dict(layer=layer, q_raw=torch.randn(n, HEADS * hd, device="cuda", generator=gen),
@@ -241,6 +352,8 @@ def build_decode(torch, g4a, ctx, ctx_lens, extra_rows, seed):
                            q_norm_w=weights[layer][0], k_norm_w=weights[layer][1],
                            out=torch.empty(n, HEADS * hd, device="cuda"))
     ctx.sync()
+    if keep:
+        return kv, args, weights, kept
     return kv, args
 
 
@@ -333,7 +446,7 @@ def measure_batch1(torch, g4a, ctx, stream, reps=200):
     kv = g4a.KvCache(ctx, 1, 1024, dtype=g4a.KV_F32, layers=[LOCAL_LAYER, GLOBAL_LAYER])
     gen = torch.Generator(device="cuda")
     gen.manual_seed(628)
-    out = {}
+    out, args = {}, {}
     for layer, hd in ((LOCAL_LAYER, HD_L), (GLOBAL_LAYER, HD_G)):
         w = torch.ones(hd, device="cuda")
         kv.append_tokens(0, layer, torch.randn(627, hd, device="cuda", generator=gen),
@@ -358,6 +471,33 @@ def measure_batch1(torch, g4a, ctx, stream, reps=200):
         out["local" if hd == HD_L else "global"] = {"us_median": round(us, 2), "bytes": nbytes,
                                                     "GB_s": round(nbytes / us / 1e3, 1)}
         plan.close()
+        args[layer] = a
+    # e2e: both layers in one g4a_decode_host call per step from pinned host
+    # buffers (the inputs copied in, the outputs copied back, the call
+    # returning when they are there); each call appends, so the context grows
+    # from 628 by one row per call
+    pin = {}
+    for layer in (LOCAL_LAYER, GLOBAL_LAYER):
+        a = args[layer]
+        pin[layer] = {k: a[k].cpu().pin_memory() for k in ("q_raw", "k_raw", "v_raw")}
+        pin[layer]["out"] = torch.empty_like(a["out"], device="cpu").pin_memory()
+    host_args = g4a.DecodeHostArgs([dict(layer=layer, q_raw=pin[layer]["q_raw"], k_raw=pin[layer]["k_raw"],
+                                         v_raw=pin[layer]["v_raw"], q_norm_w=args[layer]["q_norm_w"],
+                                         k_norm_w=args[layer]["k_norm_w"], out=pin[layer]["out"])
+                                    for layer in (LOCAL_LAYER, GLOBAL_LAYER)])
+    e2e_reps = 60
+    ts = []
+    with torch.cuda.stream(stream):
+        for k in range(e2e_reps):
+            t0 = time.perf_counter()
+            ctx.decode_host(kv, host_args, [0], [628 + k])
+            ts.append(time.perf_counter() - t0)
+    h2d = sum(t.numel() * 4 for layer in pin for key, t in pin[layer].items() if key != "out")
+    d2h = sum(pin[layer]["out"].numel() * 4 for layer in pin)
+    out["e2e"] = {"value": round(statistics.median(ts[10:]) * 1e6, 2), "unit": "us per step (local + global layer)",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                  "api": "g4a_decode_host, both layers in one call, pinned host buffers; wall clock, median of "
+                         f"{e2e_reps - 10} calls after 10 (context 629..{628 + e2e_reps})"}
     kv.close()
     return out
 
@@ -380,20 +520,25 @@ def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2, include_long=
         return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
 
     def timed(problems):
-        problems = ctx.prefill_args(problems)  # packed once, as a caller's prompt loop would
-        for _ in range(warmup):
-            ctx.prefill(problems)
-        ts = []
-        for _ in range(reps):
-            flush_l2(torch, flush)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            ctx.prefill(problems)
-            e1.record(stream)
+        # Packed once, as a caller's prompt loop would. The repetitions are
+        # queued back to back on the library's stream, each after an L2 flush
+        # on the same stream, so that the events time the device work and not
+        # the host's launch of the first kernel after an idle GPU.
+        problems = ctx.prefill_args(problems)
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                ctx.prefill(problems)
+            evs = []
+            for _ in range(reps):
+                flush_l2(torch, flush)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                ctx.prefill(problems)
+                e1.record(stream)
+                evs.append((e0, e1))
             torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
         ctx.sync()
-        return statistics.median(ts)
+        return statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
 
     # configuration 1: 628 tokens, 35 layers, layers 15-34 reuse 13/14's K/V
     T = 628
@@ -899,6 +1044,11 @@ def main():
     if rank == 0 and not a.no_extras:
         extras["decode_batch1"] = measure_batch1(torch, g4a, ctx, stream)
         extras["prefill"] = measure_prefill(torch, g4a, ctx, stream, pk)
+        if dist is None:
+            # the reference's CPU path beside each configuration (rank 0 at N=1 only)
+            extras["decode_batch1"]["cpu_baseline"] = cpu_batch1_latency()
+            extras["prefill"]["cfg1_628x35"]["cpu_baseline"] = cpu_prefill_cfg1()
+            extras["prefill"]["cfg3_32768_global_1gpu"]["cpu_baseline"] = cpu_prefill_cfg3()
         extras["q8_0_matvec_head"] = measure_q8_head(torch, g4a, ctx, stream, pk)
         if dist is None:
             extras["e2e_decoder"] = measure_decoder(torch, g4a, ctx)

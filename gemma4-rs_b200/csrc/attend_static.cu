@@ -11,15 +11,19 @@
 // kScratchBytes (about 1 MiB): every GPU that loads this library holds it
 // until the process exits.
 //
-// Set-up: the first call on a device, with that device current, looks up the
-// array's device address (cudaGetSymbolAddress) and keeps it; make that first
-// call before any stream capture. Later calls reuse the address.
+// Set-up: the device is the one cuda_stream belongs to (the current device
+// for the legacy default stream). The first call on a device makes it current
+// for the moment of the call, looks up the array's device address there
+// (cudaGetSymbolAddress) and keeps it; make that first call before any stream
+// capture. Later calls reuse the address. The address is not looked up again
+// after cudaDeviceReset, so do not call this after resetting a device.
 //
 // Sharing: all calls on a device use the same array, which keeps the last
 // call's contents. The arrival counter that must start at zero is cleared by
-// each call (an async memset on the caller's stream). Calls that overlap on
-// the GPU (different streams, or a second call before the first finished on
-// another stream) race on the array; serialise them on one stream.
+// each call (an async memset on the caller's stream, the only reset: the
+// kernel never clears it). Calls that overlap on the GPU (different streams,
+// or a second call before the first finished on another stream) race on the
+// array; serialise them on one stream.
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -180,29 +184,40 @@ __global__ void __launch_bounds__(kThreadsS) attend_static_kernel(const float *_
 #pragma unroll
         for (int u = 0; u < CPT; u++) out[h * HD + threadIdx.x + kThreadsS * u] = o[u] / L;
     }
-    if (threadIdx.x == 0) *ticket = 0u;
 }
 
 std::mutex g_setup_mu;
 unsigned char *g_scratch[kMaxDevices] = {};
 
-// Device address of g4a_attend_scratch on the current device, looked up on
-// the first call for that device.
-cudaError_t scratch_for_current_device(unsigned char **out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
+// Device address of g4a_attend_scratch on device `dev`, looked up (with dev
+// current) on the first call for that device.
+cudaError_t scratch_for_device(int dev, unsigned char **out) {
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_setup_mu);
     if (!g_scratch[dev]) {
         void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g4a_attend_scratch);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g4a_attend_scratch);
         if (e != cudaSuccess) return e;
         g_scratch[dev] = static_cast<unsigned char *>(p);
     }
     *out = g_scratch[dev];
     return cudaSuccess;
 }
+
+// Makes the stream's device current for the life of the object and restores
+// the caller's device afterwards.
+struct DeviceOfStream {
+    int prev = -1, dev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceOfStream(cudaStream_t st) {
+        if ((err = cudaGetDevice(&prev)) != cudaSuccess) return;
+        if ((err = cudaStreamGetDevice(st, &dev)) != cudaSuccess) return;
+        if (dev != prev) err = cudaSetDevice(dev);
+    }
+    ~DeviceOfStream() {
+        if (prev >= 0 && dev >= 0 && dev != prev) cudaSetDevice(prev);
+    }
+};
 
 }  // namespace
 
@@ -214,17 +229,25 @@ extern "C" int g4a_attend_static(void *cuda_stream, const float *q_dev, const fl
     if (len < 0 || !q_dev || !out_dev) return G4A_COMPUTE;
     if (len == 0) return G4A_NONFINITE;  // empty softmax, as the reference's attend
     if (!keys_dev || !values_dev) return G4A_COMPUTE;
-    unsigned char *scratch = nullptr;
-    if (scratch_for_current_device(&scratch) != cudaSuccess) return G4A_CUDA;
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const DeviceOfStream on(st);
+    if (on.err != cudaSuccess) return G4A_CUDA;
+    unsigned char *scratch = nullptr;
+    if (scratch_for_device(on.dev, &scratch) != cudaSuccess) return G4A_CUDA;
     const int n_splits = (int)std::min<int64_t>(kMaxSplits, std::max<int64_t>(1, (len + 31) / 32));
     unsigned *ticket = reinterpret_cast<unsigned *>(scratch + (kPartOFloats + kPartMLFloats) * sizeof(float));
     if (cudaMemsetAsync(ticket, 0, sizeof(unsigned), st) != cudaSuccess) return G4A_CUDA;
-    if (head_dim == 256)
-        attend_static_kernel<256><<<n_splits, kThreadsS, 0, st>>>(q_dev, keys_dev, values_dev, len, n_splits, scale,
-                                                                  out_dev, scratch);
-    else
-        attend_static_kernel<512><<<n_splits, kThreadsS, 0, st>>>(q_dev, keys_dev, values_dev, len, n_splits, scale,
-                                                                  out_dev, scratch);
-    return cudaGetLastError() == cudaSuccess ? G4A_OK : G4A_CUDA;
+    // cudaLaunchKernelEx reports this launch's own error (not one left over
+    // from an earlier call in the process)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_splits);
+    cfg.blockDim = dim3(kThreadsS);
+    cfg.stream = st;
+    const cudaError_t e =
+        head_dim == 256
+            ? cudaLaunchKernelEx(&cfg, attend_static_kernel<256>, q_dev, keys_dev, values_dev, len, n_splits, scale,
+                                 out_dev, scratch)
+            : cudaLaunchKernelEx(&cfg, attend_static_kernel<512>, q_dev, keys_dev, values_dev, len, n_splits, scale,
+                                 out_dev, scratch);
+    return e == cudaSuccess ? G4A_OK : G4A_CUDA;
 }

@@ -12,6 +12,18 @@
 // exact arithmetic) and a cubic in r, all in double, rounded once to float.
 // glibc selects a build of it with fused multiply-adds on CPUs that have
 // them; the evaluation below follows that build (fma in the polynomial).
+// The method and its reduction and polynomial constants come from:
+//   Arm Optimized Routines, math/expf.c
+//   Copyright (c) 2017-2018, Arm Limited.
+//   SPDX-License-Identifier: MIT OR Apache-2.0 WITH LLVM-exception
+// under whose MIT terms: "The above copyright notice and this permission
+// notice shall be included in all copies or substantial portions of the
+// Software." (Permission is hereby granted, free of charge, to any person
+// obtaining a copy of this software and associated documentation files, to
+// deal in the Software without restriction, including without limitation the
+// rights to use, copy, modify, merge, publish, distribute, sublicense, and/or
+// sell copies of the Software. THE SOFTWARE IS PROVIDED "AS IS", WITHOUT
+// WARRANTY OF ANY KIND, EXPRESS OR IMPLIED.)
 //
 // tanhf: the single-precision port of Sun's fdlibm tanh/expm1, which glibc
 // uses for tanhf:

@@ -133,11 +133,13 @@ int g4a_attend(g4a_ctx *ctx, const float *q_dev, const float *keys_dev, const fl
  * its device memory to its own pools at start-up). It allocates nothing: its
  * scratch is a file-scope device array of about 1 MiB (64 row ranges x 8
  * heads x 512 columns of f32 plus their max/sum), held by every GPU that
- * loads the library until exit. Other shapes return G4A_COMPUTE. The first
- * call on a device (that device current) looks the array up; make it before
- * any stream capture. Calls share the array, so calls that overlap on the
- * GPU race; queue them on one stream. Queued on cuda_stream; no context is
- * used, and a non-finite softmax shows as NaN in out_dev. */
+ * loads the library until exit. Other shapes return G4A_COMPUTE. The work
+ * runs on the device cuda_stream belongs to; the first call on a device looks
+ * the array up there (making that device current for the call); make it
+ * before any stream capture. Each call clears the array's arrival counter
+ * with an async memset on cuda_stream before its kernel. Calls share the
+ * array, so calls that overlap on the GPU race; queue them on one stream. No
+ * context is used, and a non-finite softmax shows as NaN in out_dev. */
 int g4a_attend_static(void *cuda_stream, const float *q_dev, const float *keys_dev,
                       const float *values_dev, int64_t len, int32_t n_heads, int32_t n_kv_heads,
                       int32_t head_dim, float scale, float *out_dev);

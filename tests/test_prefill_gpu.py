@@ -213,3 +213,55 @@ def test_prefill_repeated_list_reads_current_values(oracle, ctx, torch_cuda):
     ctx.prefill([dict(head_dim=hd, window=64, n_q=T, n_kv=T, q=qd, k=kd, v=vd, out=out2)])
     ctx.sync()
     assert max_abs_diff(out2.cpu().numpy(), oracle.prefill_attend(q, k, v2, 8, 64)) <= TOL
+
+
+def sampled_rows(T, n, seed):
+    """n query positions spread over [0, T): the first and last rows, rows on
+    either side of 32-token row-tile and 128-key tile edges, and random rows."""
+    edges = {0, 1, T - 1, T - 2}
+    for e in (32, 128, 4096, T // 2):
+        for m in (e, 2 * e, 3 * e, T - e):
+            edges.update({m - 1, m})
+    edges = sorted(x for x in edges if 0 <= x < T)
+    r = rng(seed)
+    rest = r.choice(np.setdiff1d(np.arange(T), edges), size=max(0, n - len(edges)), replace=False)
+    return np.sort(np.concatenate([edges, rest]).astype(np.int64))
+
+
+def test_prefill_config3_32768_sampled_rows(oracle, ctx, torch_cuda):
+    """Configuration 3 at its benchmarked size: one 32,768-token global layer
+    (512-wide heads, full causal) in one call, unit-RMS bf16 Q/K and N(0,1) V
+    generated on the device. 256 query rows spread over the sequence (first,
+    last, both sides of row-tile and key-tile edges, random) are checked
+    against the oracle's attend over each row's causal keys [0, t] -- the
+    reference's prompt loop at position t (model.rs:326-366 over
+    eng/mod.rs:33-35's global range). This reaches what shorter cases do not:
+    256 key tiles per item, TMA rows past 2^15, and the lazy rescale over 32k
+    keys."""
+    torch = torch_cuda
+    T, hd = 32768, 512
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(32768)
+
+    def unit(shape):
+        x = torch.randn(*shape, device="cuda", generator=gen)
+        return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
+
+    q, k = unit((T, 8, hd)), unit((T, hd))
+    v = torch.randn(T, hd, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.full((T, 8, hd), float("nan"), device="cuda")
+    ctx.prefill([dict(head_dim=hd, window=0, n_q=T, n_kv=T, q=q, k=k, v=v, out=out)])
+    ctx.sync()
+    rows = sampled_rows(T, 256, 3)
+    assert len(rows) == 256
+    idx = torch.from_numpy(rows).cuda()
+    got = out.index_select(0, idx).cpu().numpy()
+    q_h = q.index_select(0, idx).float().cpu().numpy()
+    k_h, v_h = k.float().cpu().numpy(), v.float().cpu().numpy()
+    del out
+    oracle.pool_init(0)
+    worst = 0.0
+    for i, t in enumerate(rows):
+        want = oracle.attend(q_h[i].reshape(-1), k_h[: t + 1], v_h[: t + 1], 8, 1, 1.0)
+        worst = max(worst, max_abs_diff(got[i].reshape(-1), want))
+    assert worst <= TOL, worst

@@ -1,9 +1,9 @@
 """g4a_attend_static, the entry point for callers that cannot allocate device
 memory when they attend (for example a server whose device memory is already
 handed to its own pools). It keeps its scratch in a file-scope device array,
-so it must give what g4a_attend gives, call after call, while sharing that
-array. Collected last so that a failure here stops a -x run only after every
-other test has run.
+so it must give what the oracle (the reference's attend) and g4a_attend give,
+call after call, while sharing that array. Collected last so that a failure
+here stops a -x run only after every other test has run.
 """
 import ctypes
 
@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-4  # the decode tolerance used by the other attention tests
 
 
-def test_static_scratch_attend_matches_attend():
+def test_static_scratch_attend_matches_attend(oracle):
     import torch
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
@@ -28,12 +28,15 @@ def test_static_scratch_attend_matches_attend():
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     r = np.random.default_rng(2468)
-    # consecutive calls on one stream share the array; the third repeats the
-    # first shape after a different one has overwritten the scratch
-    for hd, length in ((512, 628), (256, 1000), (512, 628), (256, 7)):
-        q = torch.from_numpy(r.standard_normal(8 * hd).astype(np.float32) / np.float32(np.sqrt(hd))).cuda()
-        k = torch.from_numpy(r.standard_normal((length, hd)).astype(np.float32)).cuda()
-        v = torch.from_numpy(r.standard_normal((length, hd)).astype(np.float32)).cuda()
+    # Consecutive calls on one stream share the array; the third repeats the
+    # first shape after a different one has overwritten the scratch. Lengths
+    # past 2016 rows use all 64 row ranges (more than 32 rows each), 5000 and
+    # 4097 with a last 64-row block that is cut short.
+    for hd, length in ((512, 628), (256, 1000), (512, 628), (256, 7), (512, 5000), (256, 4097), (512, 5000)):
+        q_h = r.standard_normal(8 * hd).astype(np.float32) / np.float32(np.sqrt(hd))
+        k_h = r.standard_normal((length, hd)).astype(np.float32)
+        v_h = r.standard_normal((length, hd)).astype(np.float32)
+        q, k, v = (torch.from_numpy(a).cuda() for a in (q_h, k_h, v_h))
         want = torch.empty(8 * hd, device="cuda")
         got = torch.full((8 * hd,), float("nan"), device="cuda")
         torch.cuda.synchronize()
@@ -42,7 +45,10 @@ def test_static_scratch_attend_matches_attend():
         assert rc == g4attn.OK
         stream.synchronize()
         ctx.sync()
-        assert float((got - want).abs().max()) <= TOL, (hd, length)
+        got_h = got.cpu().numpy()
+        ref = oracle.attend(q_h, k_h, v_h, 8, 1, 1.0)
+        assert float(np.max(np.abs(got_h - ref))) <= TOL, (hd, length, "vs oracle")
+        assert float((got - want).abs().max()) <= TOL, (hd, length, "vs g4a_attend")
     x = torch.zeros(8 * 1024, device="cuda")
     rc = fn(stream.cuda_stream, x.data_ptr(), x.data_ptr(), x.data_ptr(), 4, 8, 1, 1024, 1.0, x.data_ptr())
     assert rc == g4attn.COMPUTE  # beyond the static scratch's 512 columns per head
