@@ -572,14 +572,42 @@ def measure_prefill(torch, g4a, ctx, stream, pk, reps=5, warmup=2, include_long=
     return res
 
 
-def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, warmup=3):
-    """Configuration 3 across ranks: the 32,768-token global layer split in
-    zigzag chunks (context parallel: NCCL all-gather of K/V overlapped with
-    the diagonal blocks, then the off-diagonal blocks and a log-sum-exp
-    merge). CUDA events on the library's stream, barrier and synchronize
-    around each repetition, max over ranks."""
-    from g4attn import cp
-    T = 32768
+def cp_sample_rows(T: int, n: int = 48) -> np.ndarray:
+    """Query rows whose outputs are checked against the oracle after a
+    multi-GPU run: the first and last rows, both sides of chunk edges, and
+    rows spread over the sequence."""
+    rows = {0, T - 1, T // 2 - 1, T // 2}
+    for w in (2, 4, 8, 16):
+        rows.update({T // w, T // w - 1})
+    rows.update(int(x) for x in np.linspace(0, T - 1, n - len(rows)))
+    return np.array(sorted(rows)[:n], np.int64)
+
+
+def torch_nccl_comm(torch, dist):
+    """The ncclComm_t of torch's default NCCL process group (the caller's
+    communicator, handed to g4a_cp_prefill), or None when this torch does not
+    expose it."""
+    try:
+        pg = dist.distributed_c10d._get_default_group()
+        return int(pg._get_backend(torch.device("cuda"))._comm_ptr()) or None
+    except Exception:
+        return None
+
+
+def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, warmup=3, T=32768):
+    """Configuration 3 across ranks through the C entry g4a_cp_prefill: the
+    32,768-token global layer in zigzag chunks (rank r: chunks r and
+    2W-1-r), both schedules on the caller's NCCL communicator (torch's):
+      kv_shards -- keys/values stay put, queries gathered, partial results
+                   merged across ranks (all-reduce MAX, reduce-scatter SUM);
+      gather_kv -- key/value chunks gathered during the diagonal blocks.
+    Each repetition: barrier, synchronize, CUDA events on the library's
+    stream around the call, synchronize; median over repetitions, max over
+    ranks. A second, profiled pass gives the per-phase device times (rank
+    max). Then sampled rows of every rank's output are gathered to rank 0 and
+    compared with the oracle's attend over each row's causal keys."""
+    import oracle
+    hd = HD_G
     gen = torch.Generator(device="cuda")
     gen.manual_seed(77 + rank)
 
@@ -587,38 +615,96 @@ def measure_cp_prefill(torch, g4a, ctx, stream, dist, world, rank, pk, reps=5, w
         x = torch.randn(*shape, device="cuda", generator=gen)
         return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
 
-    chunks = cp.zigzag_chunks(T, world, rank)
-    c = chunks[0][1] - chunks[0][0]
-    qc = [unit((c, HEADS, HD_G)) for _ in chunks]
-    kc = [unit((c, HD_G)) for _ in chunks]
-    vc = [torch.randn(c, HD_G, device="cuda", generator=gen).to(torch.bfloat16) for _ in chunks]
-    side = torch.cuda.Stream()
-    gather = cp.torch_gather_kv(dist, torch, side)
-    attend = cp.g4a_attend(ctx, torch, HD_G)
-    merge = cp.g4a_merge(ctx, torch, HD_G)
-    ts = []
-    with torch.cuda.stream(stream):
-        for i in range(warmup + reps):
-            dist.barrier()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            outs = cp.cp_prefill(qc, kc, vc, T, world, rank, gather, attend, merge)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            if i >= warmup:
-                ts.append(e0.elapsed_time(e1))
-    ctx.sync()
-    del outs
-    t = torch.tensor([statistics.median(ts)], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0])
-    flops = 4 * HEADS * HD_G * (T * (T + 1) // 2)
-    tf = flops / ms / 1e9
-    return {"ms": round(ms, 3), "tflop": round(flops / 1e12, 3), "TFLOP_s_job": round(tf, 1),
-            "frac_of_peak_per_gpu": round(tf / world / pk["bf16"], 4), "ranks": world,
-            "schedule": "zigzag 2W chunks, NCCL all-gather of K/V on a side stream, LSE merge",
-            "timing": "CUDA events per repetition, median over reps, max over ranks"}
+    c = T // (2 * world)
+    q, k = unit((2 * c, HEADS, hd)), unit((2 * c, hd))
+    v = torch.randn(2 * c, hd, device="cuda", generator=gen).to(torch.bfloat16)
+    comm = torch_nccl_comm(torch, dist)
+    own = None
+    if comm is None:
+        uid = [g4a.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        own = g4a.NcclComm(world, rank, uid[0], torch.cuda.current_device())
+        comm = own.ptr
+    flops = 4 * HEADS * hd * (T * (T + 1) // 2)
+    sample = cp_sample_rows(T)
+    chunk_of = lambda t: t // c
+    owner = lambda ch: ch if ch < world else 2 * world - 1 - ch
+    res = {"T": T, "ranks": world, "communicator": "torch ProcessGroupNCCL (_comm_ptr)" if own is None
+           else "library-made (g4a_nccl_comm_init)", "timing": "CUDA events around g4a_cp_prefill per repetition "
+           "(barrier + synchronize around each), median over reps, max over ranks; phases from a profiled pass"}
+    worst_all = 0.0
+    for name, sched in (("kv_shards", g4a.CP_KV_SHARDS), ("gather_kv", g4a.CP_GATHER_KV)):
+        out = torch.empty(2 * c, HEADS, hd, device="cuda")
+        ts = []
+        with torch.cuda.stream(stream):
+            for i in range(warmup + reps):
+                dist.barrier()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                ctx.cp_prefill(comm, sched, hd, T, q, k, v, out)
+                e1.record(stream)
+                ctx.cp_wait(comm, 60000)
+                if i >= warmup:
+                    ts.append(e0.elapsed_time(e1))
+            # profiled pass: device time of each phase (events between phases)
+            ctx.profile(True)
+            for i in range(reps):
+                dist.barrier()
+                torch.cuda.synchronize()
+                ctx.cp_prefill(comm, sched, hd, T, q, k, v, out)
+                ctx.cp_wait(comm, 60000)
+            ph = [ctx.profile_read(kid)[0] / reps for kid in (g4a.K_CP_EXCHANGE, g4a.K_CP_ATTEND_LOCAL,
+                                                                 g4a.K_CP_ATTEND_REMOTE, g4a.K_CP_MERGE)]
+            ctx.profile(False)
+        t = torch.tensor([statistics.median(ts)] + ph, device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        tf = flops / ms / 1e9
+        # parity: sampled rows of every rank to rank 0 (each row owned by one rank)
+        got = torch.zeros(len(sample), HEADS, hd, device="cuda")
+        qs = torch.zeros(len(sample), HEADS, hd, device="cuda")
+        for i, tpos in enumerate(sample):
+            ch = chunk_of(int(tpos))
+            if owner(ch) == rank:
+                local = (0 if ch == rank else c) + int(tpos) % c
+                got[i] = out[local]
+                qs[i] = q[local].float()
+        dist.all_reduce(got)
+        dist.all_reduce(qs)
+        kv_all = [torch.empty_like(k) for _ in range(world)]
+        dist.all_gather(kv_all, k)
+        k_full = torch.empty(T, hd, dtype=k.dtype, device="cuda")
+        for j, kj in enumerate(kv_all):
+            k_full[j * c:(j + 1) * c] = kj[:c]
+            k_full[(2 * world - 1 - j) * c:(2 * world - j) * c] = kj[c:]
+        dist.all_gather(kv_all, v)
+        v_full = torch.empty(T, hd, dtype=v.dtype, device="cuda")
+        for j, vj in enumerate(kv_all):
+            v_full[j * c:(j + 1) * c] = vj[:c]
+            v_full[(2 * world - 1 - j) * c:(2 * world - j) * c] = vj[c:]
+        worst = 0.0
+        if rank == 0:
+            oracle.pool_init(0)
+            k_h, v_h = k_full.float().cpu().numpy(), v_full.float().cpu().numpy()
+            got_h, q_h = got.cpu().numpy(), qs.cpu().numpy()
+            for i, tpos in enumerate(sample):
+                want = oracle.attend(q_h[i].reshape(-1), k_h[: tpos + 1], v_h[: tpos + 1], HEADS, 1, 1.0)
+                worst = max(worst, float(np.max(np.abs(got_h[i].reshape(-1).astype(np.float64) - want))))
+        worst_all = max(worst_all, worst)
+        del kv_all, k_full, v_full, out
+        res[name] = {"ms": round(ms, 3), "TFLOP_s_job": round(tf, 1),
+                     "frac_of_peak_per_gpu": round(tf / world / pk["bf16"], 4),
+                     "phases_ms_rank_max": {"exchange": round(float(t[1]), 3), "attend_local": round(float(t[2]), 3),
+                                            "attend_remote": round(float(t[3]), 3), "merge": round(float(t[4]), 3)},
+                     "parity_max_abs_diff": round(worst, 6)}
+    dist.barrier()
+    if own is not None:
+        own.close()
+    res["tflop"] = round(flops / 1e12, 3)
+    res["parity"] = {"rows_checked": int(len(sample)), "max_abs_diff": round(worst_all, 6), "tolerance": 2e-3,
+                     "against": "oracle attend over each row's causal keys (rank 0, gathered rows)"}
+    return res
 
 
 def q8_head_weights(torch, rows: int, cols: int, seed: int = 1):
@@ -1119,6 +1205,10 @@ def main():
                                 "sample": desc}
     line.update(extras)
     print(json.dumps(line), flush=True)
+    cp = extras.get("prefill_cp")
+    if cp and cp["parity"]["max_abs_diff"] > cp["parity"]["tolerance"]:
+        print(f"context-parallel parity failed: max |diff| {cp['parity']['max_abs_diff']}", file=sys.stderr)
+        sys.exit(1)
 
 
 if __name__ == "__main__":

@@ -295,6 +295,7 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
         if (sl.ev) cudaEventDestroy(sl.ev);
     }
     prefill_scratch_free(ctx->prefill);
+    if (ctx->cp_free) ctx->cp_free(ctx->cp);
     delete ctx;
 }
 

@@ -68,6 +68,9 @@ struct g4a_ctx {
     float *d_io = nullptr;
     size_t io_cap = 0;  // floats
     int *h_flag = nullptr;
+    // context-parallel prefill state (cp_host.cpp), freed by cp_free
+    void *cp = nullptr;
+    void (*cp_free)(void *) = nullptr;
 };
 
 namespace g4a {

@@ -217,4 +217,22 @@ void prefill_scratch_free(PrefillScratch *s);
 int prefill_run(PrefillScratch *s, int *d_err, int32_t n, const struct g4a_prefill_problem *problems,
                 cudaStream_t st, const char **msg);
 
+// Key/value-shard context-parallel merge (cp_kernels.cu): partial results of
+// one rank as row segments [t0, t1) of the sequence, o [t1-t0][8][hd] and
+// lse [t1-t0][8] (natural log).
+constexpr int kCpMaxSegs = 8;
+struct CpSeg {
+    int32_t t0, t1;
+    const float *o;
+    const float *lse;
+};
+struct CpSegs {
+    CpSeg s[kCpMaxSegs];
+    int32_t n;
+};
+cudaError_t launch_cp_rowmax(const CpSegs &segs, int32_t T, float *m, cudaStream_t st);
+cudaError_t launch_cp_pack(const CpSegs &segs, const float *m, int32_t W, int32_t c, int32_t hd, float *packed,
+                           cudaStream_t st);
+cudaError_t launch_cp_finish(const float *recv, int32_t rows, int32_t hd, float *out, cudaStream_t st);
+
 }  // namespace g4a

@@ -664,14 +664,28 @@ static bool encode_out_f32(CUtensorMap *map, const float *base, uint64_t cols, u
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// One prepared problem list: what a launch of it needs on the device (the
+// problem table, the work list, the fp16 copies of its V arrays) and the
+// V-conversion launches. Everything launched from here reads only buffers this
+// struct owns or the caller's pointers in the list, so an equal list means an
+// equal launch.
+struct Prepared {
+    std::vector<g4a_prefill_problem> key;
+    ProblemDev *d_problems = nullptr;
+    WorkItem *d_items = nullptr;
+    __half *v16 = nullptr;
+    struct ConvLaunch {
+        ConvSegs segs;
+        unsigned bx;
+        int cnt;
+    };
+    std::vector<ConvLaunch> conv;
+    size_t n_work[2] = {0, 0};
+    uint64_t used = 0;  // call counter at the last use
+};
+
 // Host-side state the prefill keeps in the context between calls.
 struct PrefillScratch {
-    __half *v16 = nullptr;
-    size_t v16_cap = 0;  // elements
-    ProblemDev *d_problems = nullptr;
-    size_t problems_cap = 0;
-    WorkItem *d_items = nullptr;
-    size_t items_cap = 0;
     bool attr_set = false;
     // Tensor maps by (kind, base, columns, rows): the encoder is a driver call
     // per map, and repeated calls (a model's layers, every prompt of a batch)
@@ -690,36 +704,36 @@ struct PrefillScratch {
         }
     };
     std::unordered_map<MapKey, CUtensorMap, MapHash> maps;
-    // The last problem list and what it needs at launch: a call that repeats
-    // it exactly (a model's prompt loop, a benchmark) skips validation, map
-    // encoding, work-list construction and uploads. Everything launched from
-    // here reads only buffers this struct owns or the caller's pointers in the
-    // list, so equal lists mean equal launches.
-    struct ConvLaunch {
-        ConvSegs segs;
-        unsigned bx;
-        int cnt;
-    };
-    std::vector<g4a_prefill_problem> last;
-    bool last_valid = false;
-    std::vector<ConvLaunch> conv;
-    size_t n_work[2] = {0, 0};
+    // The last few problem lists, prepared: a call that repeats one exactly (a
+    // model's prompt loop, a benchmark, the alternating lists of a
+    // context-parallel schedule) skips validation, map encoding, work-list
+    // construction and uploads.
+    static constexpr int kCached = 8;
+    Prepared cache[kCached];
+    uint64_t calls = 0;
 };
 
-static cudaError_t launch_prepared(PrefillScratch *S, int *d_err, cudaStream_t st) {
-    for (const auto &c : S->conv) bf16_to_f16_kernel<<<dim3(c.bx, c.cnt), 256, 0, st>>>(c.segs);
+static void free_prepared(Prepared &p) {
+    cudaFree(p.d_problems);
+    cudaFree(p.d_items);
+    cudaFree(p.v16);
+    p = Prepared();
+}
+
+static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_err, cudaStream_t st) {
+    for (const auto &c : P.conv) bf16_to_f16_kernel<<<dim3(c.bx, c.cnt), 256, 0, st>>>(c.segs);
     if (!S->attr_set) {
         cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
         cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
         S->attr_set = true;
     }
     // two CTAs (one cluster) per work item
-    if (S->n_work[0])
-        prefill_kernel<256><<<2 * (unsigned)S->n_work[0], kThreads, Cfg<256>::kSmemBytes, st>>>(S->d_problems,
-                                                                                             S->d_items, d_err);
-    if (S->n_work[1])
-        prefill_kernel<512><<<2 * (unsigned)S->n_work[1], kThreads, Cfg<512>::kSmemBytes, st>>>(
-            S->d_problems, S->d_items + S->n_work[0], d_err);
+    if (P.n_work[0])
+        prefill_kernel<256><<<2 * (unsigned)P.n_work[0], kThreads, Cfg<256>::kSmemBytes, st>>>(P.d_problems,
+                                                                                            P.d_items, d_err);
+    if (P.n_work[1])
+        prefill_kernel<512><<<2 * (unsigned)P.n_work[1], kThreads, Cfg<512>::kSmemBytes, st>>>(
+            P.d_problems, P.d_items + P.n_work[0], d_err);
     return cudaGetLastError();
 }
 
@@ -743,25 +757,8 @@ static bool cached_map(PrefillScratch *S, int kind, const void *base, uint64_t c
 PrefillScratch *prefill_scratch_new() { return new PrefillScratch(); }
 void prefill_scratch_free(PrefillScratch *s) {
     if (!s) return;
-    cudaFree(s->v16);
-    cudaFree(s->d_problems);
-    cudaFree(s->d_items);
+    for (auto &p : s->cache) free_prepared(p);
     delete s;
-}
-
-template <typename T>
-static cudaError_t grow_buf(T **p, size_t *cap, size_t need, cudaStream_t st) {
-    if (need <= *cap) return cudaSuccess;
-    if (*p) {
-        cudaStreamSynchronize(st);
-        cudaFree(*p);
-        *p = nullptr;
-        *cap = 0;
-    }
-    const size_t n = std::max(need, *cap * 2);
-    cudaError_t e = cudaMalloc(p, n * sizeof(T));
-    if (e == cudaSuccess) *cap = n;
-    return e;
 }
 
 // Validates, converts V to fp16, builds tensor maps and the work list, and
@@ -774,17 +771,29 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         *msg = "invalid prefill problem list";
         return G4A_COMPUTE;
     }
-    if (S->last_valid && (size_t)n == S->last.size() &&
-        (n == 0 || std::memcmp(pr, S->last.data(), (size_t)n * sizeof(g4a_prefill_problem)) == 0)) {
-        const cudaError_t e = launch_prepared(S, d_err, st);
-        if (e != cudaSuccess) {
-            *msg = cudaGetErrorString(e);
-            return G4A_CUDA;
+    S->calls++;
+    for (auto &P : S->cache) {
+        if (P.used && P.key.size() == (size_t)n &&
+            (n == 0 || std::memcmp(pr, P.key.data(), (size_t)n * sizeof(g4a_prefill_problem)) == 0)) {
+            P.used = S->calls;
+            const cudaError_t e = launch_prepared(S, P, d_err, st);
+            if (e != cudaSuccess) {
+                *msg = cudaGetErrorString(e);
+                return G4A_CUDA;
+            }
+            return G4A_OK;
         }
-        return G4A_OK;
     }
-    S->last_valid = false;
-    S->conv.clear();
+    // a new list: prepared into the least recently used slot (its buffers may
+    // still be read by queued launches, so the stream drains first)
+    Prepared *slot = &S->cache[0];
+    for (auto &P : S->cache)
+        if (P.used < slot->used) slot = &P;
+    if (slot->used) {
+        cudaStreamSynchronize(st);
+        free_prepared(*slot);
+    }
+    Prepared &P = *slot;
     // distinct V arrays -> fp16 copies, each sized for the most rows any problem reads
     std::vector<const void *> v_src;
     std::vector<size_t> v_len;
@@ -827,8 +836,9 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         v_off[k] = v_total;
         v_total += v_len[k];  // multiples of 256 elements: every copy stays 16-byte aligned
     }
-    cudaError_t e = grow_buf(&S->v16, &S->v16_cap, std::max<size_t>(v_total, 1), st);
+    cudaError_t e = cudaMalloc(&P.v16, std::max<size_t>(v_total, 1) * sizeof(__half));
     if (e != cudaSuccess) {
+        free_prepared(P);
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
@@ -838,12 +848,12 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         uint64_t most = 0;
         for (int q = 0; q < cnt; q++) {
             segs.src[q] = reinterpret_cast<const __nv_bfloat16 *>(v_src[k0 + q]);
-            segs.dst[q] = S->v16 + v_off[k0 + q];
+            segs.dst[q] = P.v16 + v_off[k0 + q];
             segs.n8[q] = v_len[k0 + q] / 8;
             most = std::max(most, segs.n8[q]);
         }
         const unsigned bx = (unsigned)std::min<uint64_t>((most + 255) / 256, 1024);
-        S->conv.push_back({segs, bx, cnt});
+        P.conv.push_back({segs, bx, cnt});
     }
     std::vector<ProblemDev> hp(std::max(n, 1));
     std::vector<WorkItem> work[2];
@@ -862,17 +872,20 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         if (p.n_q == 0) continue;
         if (!cached_map(S, 0, p.q_dev, p.head_dim, (uint64_t)p.n_q * 8, &d.tq)) {
             *msg = "cuTensorMapEncodeTiled failed for Q";
+            free_prepared(P);
             return G4A_CUDA;
         }
         if (!cached_map(S, 3, p.out_dev, p.head_dim, (uint64_t)p.n_q * 8, &d.to)) {
             *msg = "cuTensorMapEncodeTiled failed for the output";
+            free_prepared(P);
             return G4A_CUDA;
         }
         if (p.n_kv > 0) {
             size_t k = std::find(v_src.begin(), v_src.end(), p.v_dev) - v_src.begin();
             if (!cached_map(S, 1, p.k_dev, p.head_dim, p.n_kv, &d.tk) ||
-                !cached_map(S, 2, S->v16 + v_off[k], p.head_dim, p.n_kv, &d.tv)) {
+                !cached_map(S, 2, P.v16 + v_off[k], p.head_dim, p.n_kv, &d.tv)) {
                 *msg = "cuTensorMapEncodeTiled failed for K/V";
+                free_prepared(P);
                 return G4A_CUDA;
             }
         }
@@ -904,28 +917,32 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         std::stable_sort(w.begin(), w.end(),
                          [](const WorkItem &a, const WorkItem &b) { return a.n_kv_tiles > b.n_kv_tiles; });
     const size_t n_items = work[0].size() + work[1].size();
-    if ((e = grow_buf(&S->d_problems, &S->problems_cap, hp.size(), st)) != cudaSuccess ||
-        (e = grow_buf(&S->d_items, &S->items_cap, std::max<size_t>(n_items, 1), st)) != cudaSuccess) {
+    if ((e = cudaMalloc(&P.d_problems, hp.size() * sizeof(ProblemDev))) != cudaSuccess ||
+        (e = cudaMalloc(&P.d_items, std::max<size_t>(n_items, 1) * sizeof(WorkItem))) != cudaSuccess) {
+        free_prepared(P);
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
     std::vector<WorkItem> all(work[0]);
     all.insert(all.end(), work[1].begin(), work[1].end());
-    if ((e = cudaMemcpyAsync(S->d_problems, hp.data(), hp.size() * sizeof(ProblemDev), cudaMemcpyHostToDevice, st)) !=
+    // stream-ordered uploads from pageable memory (staged by the driver before
+    // the call returns)
+    if ((e = cudaMemcpyAsync(P.d_problems, hp.data(), hp.size() * sizeof(ProblemDev), cudaMemcpyHostToDevice, st)) !=
             cudaSuccess ||
-        (n_items && (e = cudaMemcpyAsync(S->d_items, all.data(), n_items * sizeof(WorkItem), cudaMemcpyHostToDevice,
+        (n_items && (e = cudaMemcpyAsync(P.d_items, all.data(), n_items * sizeof(WorkItem), cudaMemcpyHostToDevice,
                                          st)) != cudaSuccess)) {
+        free_prepared(P);
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
-    S->n_work[0] = work[0].size();
-    S->n_work[1] = work[1].size();
-    if ((e = launch_prepared(S, d_err, st)) != cudaSuccess) {
+    P.n_work[0] = work[0].size();
+    P.n_work[1] = work[1].size();
+    P.key.assign(pr, pr + n);
+    P.used = S->calls;
+    if ((e = launch_prepared(S, P, d_err, st)) != cudaSuccess) {
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
-    S->last.assign(pr, pr + n);
-    S->last_valid = true;
     return G4A_OK;
 }
 

@@ -28,7 +28,9 @@ HEADER = HERE.parent.parent / "include" / "g4attn.h"
 OK, CONTEXT_TOO_LONG, MISSING_LAYER, MISSING_WEIGHT, COMPUTE, NONFINITE, BAD_LAYER, CUDA, NCCL, TIMEOUT, \
     OUT_OF_PAGES = range(11)
 KV_F32, KV_F16 = 0, 1
-K_DECODE_PREP, K_DECODE_MAIN, K_DECODE_COMBINE, K_DECODE_SPLITKV, K_PREFILL, K_MATVEC_Q8 = range(6)
+K_DECODE_PREP, K_DECODE_MAIN, K_DECODE_COMBINE, K_DECODE_SPLITKV, K_PREFILL, K_MATVEC_Q8, K_CP_EXCHANGE, \
+    K_CP_ATTEND_LOCAL, K_CP_ATTEND_REMOTE, K_CP_MERGE = range(10)
+CP_KV_SHARDS, CP_GATHER_KV = 0, 1
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -59,6 +61,11 @@ class PrefillProblem(ctypes.Structure):
     _fields_ = [("head_dim", ctypes.c_int32), ("window", ctypes.c_int32), ("n_q", ctypes.c_int32),
                 ("q_pos0", ctypes.c_int32), ("n_kv", ctypes.c_int32), ("kv_pos0", ctypes.c_int32),
                 ("q_dev", _vp), ("k_dev", _vp), ("v_dev", _vp), ("out_dev", _vp), ("lse_dev", _vp)]
+
+
+class CpProblem(ctypes.Structure):
+    _fields_ = [("head_dim", ctypes.c_int32), ("seq_len", ctypes.c_int32), ("q_dev", _vp), ("k_dev", _vp),
+                ("v_dev", _vp), ("out_dev", _vp)]
 
 
 class EngError(RuntimeError):
@@ -137,6 +144,12 @@ def _load():
     L.g4a_model_set_eos.argtypes = [_vp, _i32p, ctypes.c_int32]
     L.g4a_model_generate.argtypes = [_vp, ctypes.c_int32, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                      _i32p]
+    L.g4a_cp_prefill.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(CpProblem)]
+    L.g4a_cp_wait.argtypes = [_vp, _vp, ctypes.c_int32]
+    L.g4a_nccl_unique_id.argtypes = [_vp]
+    L.g4a_nccl_comm_init.argtypes = [ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_int, ctypes.POINTER(_vp)]
+    L.g4a_nccl_comm_destroy.argtypes = [_vp]
+    L.g4a_nccl_comm_destroy.restype = None
     return L
 
 
@@ -352,6 +365,50 @@ class Context:
         po = (_vp * n)(*[_ptr(t) for t in outs])
         pl = (_vp * n)(*[_ptr(t) for t in lses])
         self.check(lib.g4a_lse_merge(self.h, n, po, pl, rows, n_heads, hd, _ptr(out), _ptr(lse)))
+
+
+    # ---- context-parallel prefill over an NCCL communicator ----
+    def cp_prefill(self, comm: int, schedule: int, head_dim: int, seq_len: int, q, k, v, out):
+        """g4a_cp_prefill: this rank's two zigzag chunks (q [2c, 8, hd], k/v
+        [2c, hd] bf16, out [2c, 8, hd] f32) of a seq_len-token global layer;
+        `comm` is an ncclComm_t as an integer (a torch ProcessGroupNCCL's
+        _comm_ptr(), or NcclComm.ptr)."""
+        pr = CpProblem(head_dim, seq_len, _ptr(q), _ptr(k), _ptr(v), _ptr(out))
+        self.check(lib.g4a_cp_prefill(self.h, _vp(comm), schedule, ctypes.byref(pr)))
+
+    def cp_wait(self, comm: int, timeout_ms: int):
+        self.check(lib.g4a_cp_wait(self.h, _vp(comm), timeout_ms))
+
+
+def nccl_unique_id() -> bytes:
+    buf = (ctypes.c_uint8 * 128)()
+    rc = lib.g4a_nccl_unique_id(buf)
+    if rc != OK:
+        raise EngError(rc, "nccl: no unique id (libnccl.so.2 missing?)")
+    return bytes(buf)
+
+
+class NcclComm:
+    """A communicator made by the library (g4a_nccl_comm_init) for callers
+    without one."""
+
+    def __init__(self, n_ranks: int, rank: int, uid: bytes, device: int):
+        buf = (ctypes.c_uint8 * 128)(*uid)
+        h = _vp()
+        rc = lib.g4a_nccl_comm_init(n_ranks, rank, buf, device, ctypes.byref(h))
+        if rc != OK:
+            raise EngError(rc, "nccl: communicator initialisation failed")
+        self.h = h
+        self.ptr = h.value
+        _live.add(self)
+
+    def close(self):
+        if getattr(self, "h", None) and not _exiting:
+            lib.g4a_nccl_comm_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 class PrefillArgs:

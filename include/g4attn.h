@@ -112,7 +112,11 @@ typedef enum g4a_kernel {
     G4A_K_DECODE_SPLITKV = 3,  /* f32 caches and g4a_attend */
     G4A_K_PREFILL = 4,         /* tcgen05 prefill (with its V conversion) */
     G4A_K_MATVEC_Q8 = 5,       /* Q8_0 mat-vec family (with its activation quantization) */
-    G4A_K_COUNT = 6
+    G4A_K_CP_EXCHANGE = 6,     /* g4a_cp_prefill: NCCL collectives (gathers, all-reduce, reduce-scatter) */
+    G4A_K_CP_ATTEND_LOCAL = 7, /* g4a_cp_prefill: attention over this rank's own data */
+    G4A_K_CP_ATTEND_REMOTE = 8,/* g4a_cp_prefill: attention over exchanged data */
+    G4A_K_CP_MERGE = 9,        /* g4a_cp_prefill: log-sum-exp merges, weights, packing */
+    G4A_K_COUNT = 10
 } g4a_kernel;
 int g4a_profile_enable(g4a_ctx *ctx, int enable);
 int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches);
@@ -269,6 +273,63 @@ int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *problems_hos
 int g4a_lse_merge(g4a_ctx *ctx, int32_t n_parts, const float *const *parts_out_host,
                   const float *const *parts_lse_host, int64_t rows, int32_t n_heads,
                   int32_t head_dim, float *out_dev, float *lse_dev);
+
+/* ---- context-parallel prefill of one long global layer over NCCL -------
+ * Replaces the reference's prompt loop on a global layer
+ * (crates/llm-gemma4/src/impl_/generate.rs:37-41, each position through
+ * model.rs:326-366 over all earlier keys, eng/mod.rs:33-35) for a sequence
+ * split over the W ranks of an NCCL communicator. The sequence of T tokens is
+ * cut into 2W equal chunks of c = T / (2W) tokens; rank r holds chunks r and
+ * 2W-1-r ("zigzag", equal causal work per rank) of the queries, keys and
+ * values, already normalised and rotated, and receives the attention output
+ * of those two chunks. Every rank calls with the same schedule, head_dim and
+ * seq_len.
+ *
+ *  G4A_CP_KV_SHARDS: keys and values stay on their rank. The queries are
+ *    gathered (all-gather and point-to-point), each rank attends every query
+ *    row that sees its two key chunks (rows of its own queries first, while
+ *    the gather runs), and the partial results are merged across ranks by
+ *    log-sum-exp: an all-reduce (MAX) of the per-row maxima, then a
+ *    reduce-scatter (SUM) of the weighted outputs and weights, which hands
+ *    each rank the rows of its own chunks.
+ *  G4A_CP_GATHER_KV: the key/value chunks are gathered (all-gather and
+ *    point-to-point, on a second stream) while each rank attends its two
+ *    diagonal blocks; then its query chunks against all earlier keys; the
+ *    two partials of each chunk are merged by log-sum-exp on the device.
+ *
+ * nccl_comm is the caller's ncclComm_t (for example the communicator of a
+ * torch ProcessGroupNCCL) of the libnccl.so.2 already loaded in the process
+ * (loaded on first use if none is). The call queues everything on the
+ * context's stream (and a stream of its own that it joins back) and returns;
+ * g4a_cp_wait or g4a_sync waits. q_dev [2][c][n_heads][hd], k_dev / v_dev
+ * [2][c][hd] bf16 (chunk r first); out_dev [2][c][n_heads][hd] f32. The
+ * context keeps the exchange buffers between calls. */
+typedef enum g4a_cp_schedule { G4A_CP_KV_SHARDS = 0, G4A_CP_GATHER_KV = 1 } g4a_cp_schedule;
+typedef struct g4a_cp_problem {
+    int32_t head_dim; /* 256 or 512 */
+    int32_t seq_len;  /* T, a multiple of 2 x ranks */
+    const void *q_dev;
+    const void *k_dev;
+    const void *v_dev;
+    float *out_dev;
+} g4a_cp_problem;
+int g4a_cp_prefill(g4a_ctx *ctx, void *nccl_comm, int32_t schedule, const g4a_cp_problem *problem);
+
+/* Waits for the context's stream from the host, polling the communicator's
+ * asynchronous error state (ncclCommGetAsyncError) as it waits. A
+ * communicator error, or timeout_ms passing first, aborts the communicator
+ * (ncclCommAbort: its pending collectives end, it is unusable afterwards)
+ * and returns G4A_NCCL or G4A_TIMEOUT; otherwise the device flags are
+ * checked as g4a_sync does. The reference reports failures as EngError
+ * results (crates/llm-eng/src/error.rs:3-15); there is no collective there. */
+int g4a_cp_wait(g4a_ctx *ctx, void *nccl_comm, int32_t timeout_ms);
+
+/* A communicator for callers that have none (no reference counterpart):
+ * one rank calls g4a_nccl_unique_id and hands the 128 bytes to the others,
+ * then every rank calls g4a_nccl_comm_init with its device. */
+int g4a_nccl_unique_id(uint8_t *id_host_128);
+int g4a_nccl_comm_init(int32_t n_ranks, int32_t rank, const uint8_t *id_host_128, int device, void **comm_out);
+void g4a_nccl_comm_destroy(void *comm);
 
 /* ---- Q8_0 mat-vec: the projections either side of attention ------------
  * crates/llm-backend-cpu/src/matvec.rs with the model's default numerics

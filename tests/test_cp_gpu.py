@@ -96,3 +96,57 @@ def test_kv_shard_merge_matches_oracle(oracle, ctx, torch_cuda, world, T):
     ref = oracle.prefill_attend(q, k, v, 8, 0)
     want = np.concatenate([ref[a:b] for a, b in rows])
     assert max_abs_diff(got.cpu().numpy(), want) <= TOL
+
+
+@pytest.fixture(scope="module")
+def comm1(torch_cuda):
+    """A one-rank NCCL communicator made by the library (g4a_nccl_*)."""
+    import g4attn
+    c = g4attn.NcclComm(1, 0, g4attn.nccl_unique_id(), 0)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("schedule", ["kv_shards", "gather_kv"])
+@pytest.mark.parametrize("hd,T", [(512, 1024), (256, 640)])
+def test_cp_prefill_c_entry_one_rank(oracle, ctx, comm1, torch_cuda, schedule, hd, T):
+    """g4a_cp_prefill through the C ABI on a one-rank communicator: both
+    schedules run their whole path (NCCL gathers, all-reduce and
+    reduce-scatter over one rank, the local and exchanged phases, the merges)
+    and give the causal prefill of the whole sequence, against the oracle;
+    per-phase device times are recorded; g4a_cp_wait returns OK."""
+    import g4attn
+    torch = torch_cuda
+    sched = g4attn.CP_KV_SHARDS if schedule == "kv_shards" else g4attn.CP_GATHER_KV
+    r = rng(6000 + hd + T)
+    q = oracle.round_bf16(unit_rms_rows(r.standard_normal((T, 8, hd)).astype(np.float32)))
+    k = oracle.round_bf16(unit_rms_rows(r.standard_normal((T, hd)).astype(np.float32)))
+    v = oracle.round_bf16(r.standard_normal((T, hd)).astype(np.float32))
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda().to(torch.bfloat16)
+    out = torch.full((T, 8, hd), float("nan"), device="cuda")
+    ctx.profile(True)
+    for _ in range(2):  # the second call reuses the context's exchange buffers and prepared lists
+        ctx.cp_prefill(comm1.ptr, sched, hd, T, dev(q), dev(k), dev(v), out)
+    ctx.cp_wait(comm1.ptr, 60000)
+    phases = {name: ctx.profile_read(kid) for name, kid in
+              (("exchange", g4attn.K_CP_EXCHANGE), ("local", g4attn.K_CP_ATTEND_LOCAL),
+               ("remote", g4attn.K_CP_ATTEND_REMOTE), ("merge", g4attn.K_CP_MERGE))}
+    ctx.profile(False)
+    assert all(n > 0 for _, n in phases.values()), phases
+    want = oracle.prefill_attend(q, k, v, 8, 0)
+    assert max_abs_diff(out.cpu().numpy(), want) <= TOL
+
+
+def test_cp_prefill_rejects_bad_calls(ctx, comm1, torch_cuda):
+    import g4attn
+    torch = torch_cuda
+    x = torch.zeros(64, 8, 512, device="cuda", dtype=torch.bfloat16)
+    kv = torch.zeros(64, 512, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(64, 8, 512, device="cuda")
+    for args in ((g4attn.CP_KV_SHARDS, 512, 63), (g4attn.CP_GATHER_KV, 128, 64), (7, 512, 64)):
+        with pytest.raises(g4attn.EngError) as e:
+            ctx.cp_prefill(comm1.ptr, args[0], args[1], args[2], x, kv, kv, out)
+        assert e.value.code == g4attn.COMPUTE
+    with pytest.raises(g4attn.EngError) as e:
+        ctx.cp_prefill(0, g4attn.CP_KV_SHARDS, 512, 64, x, kv, kv, out)
+    assert e.value.code == g4attn.COMPUTE
