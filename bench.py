@@ -146,7 +146,7 @@ class ClockSampler:
     def _run(self):
         while not self._stop.is_set():
             self._sample()
-            time.sleep(0.002)
+            time.sleep(0.005)
 
     def start(self):
         if self.nv:
@@ -362,12 +362,23 @@ def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, devic
     seqs = list(range(n))
     positions = [int(c) - 1 for c in ctx_lens]
     e2e_steps = min(steps, 50)
-    kv, args = build_decode(torch, g4a, ctx, ctx_lens, e2e_steps + 8, 1234 + device)
+    kv, args = build_decode(torch, g4a, ctx, ctx_lens, e2e_steps + 24, 1234 + device)
     # one staged step covering both layers (g4a_decode_plan: validation, page
     # allocation and metadata upload happen here, outside the timed region)
     plan = ctx.decode_plan(kv, [args[LOCAL_LAYER], args[GLOBAL_LAYER]], seqs, positions)
     for _ in range(warmup):
         plan.run()
+    # The step's three launches captured once into a CUDA graph (the plan
+    # launches kernels only, with programmatic dependent launch between them):
+    # a timed step is one graph launch, so that a rank's host thread keeps
+    # ahead of its GPU however many ranks share the host.
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+        plan.run()
+    with torch.cuda.stream(stream):
+        for _ in range(max(warmup, 3)):
+            graph.replay()
     clocks = ClockSampler(device)
     torch.cuda.synchronize()
     if dist is not None:
@@ -375,15 +386,19 @@ def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, devic
     clocks.start()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for k in range(steps):
-        plan.run()
-    t_end.record(stream)
+    with torch.cuda.stream(stream):
+        h0 = time.perf_counter()
+        t_start.record(stream)
+        for k in range(steps):
+            graph.replay()
+        t_end.record(stream)
+        enqueue_s = time.perf_counter() - h0
     torch.cuda.synchronize()
     clocks.stop()
     if dist is not None:
         dist.barrier()
     total_ms = t_start.elapsed_time(t_end)
+    del graph
     # Per-kernel durations: the same steps again with the library's CUDA events
     # around each launch (kept out of the headline region: events between the
     # launches stop the dependent-launch overlap).
@@ -431,10 +446,28 @@ def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, devic
         e_end.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_end)
+    # the same calls with the library's per-phase device timing: where a
+    # host-buffer step spends its time (copies in and out on the context's
+    # copy streams, the kernels of each layer on its stream)
+    pos_np = pos_np + e2e_steps
+    prof_steps = 8
+    ctx.profile(True)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for k in range(prof_steps):
+            ctx.decode_host(kv, host_args, seqs, pos_np + 1 + k)
+    wall = (time.perf_counter() - t0) / prof_steps
+    phases = {name: ctx.profile_read(kid) for name, kid in
+              (("copy_in", g4a.K_COPY_IN), ("prep", g4a.K_DECODE_PREP), ("main", g4a.K_DECODE_MAIN),
+               ("combine", g4a.K_DECODE_COMBINE), ("copy_out", g4a.K_COPY_OUT))}
+    ctx.profile(False)
+    e2e_phases = {k: round(ms / prof_steps * 1e3, 1) for k, (ms, n) in phases.items()}
+    e2e_phases["wall_per_call_profiled"] = round(wall * 1e6, 1)
     ctx.sync()
     kv.close()
     return {"total_ms": total_ms, "kernels": {k: (ms / max(n, 1), n) for k, (ms, n) in kern.items()},
-            "clocks": clocks.summary(), "e2e_ms": e2e_ms, "e2e_steps": e2e_steps, "h2d": h2d, "d2h": d2h}
+            "clocks": clocks.summary(), "e2e_ms": e2e_ms, "e2e_steps": e2e_steps, "h2d": h2d, "d2h": d2h,
+            "e2e_phases_us": e2e_phases, "enqueue_ms": enqueue_s * 1e3}
 
 
 def measure_batch1(torch, g4a, ctx, stream, reps=200):
@@ -1098,6 +1131,13 @@ def main():
         dist = dist_mod
     device = local_rank
     torch.cuda.set_device(device)
+    if world > 1:
+        # each rank's threads on its own share of the host's cores, so that
+        # the ranks' launch paths and clock samplers do not contend
+        cpus = sorted(os.sched_getaffinity(0))
+        share = max(1, len(cpus) // world)
+        mine = cpus[local_rank * share:(local_rank + 1) * share] or cpus
+        os.sched_setaffinity(0, mine)
     my_lens = shard(lengths, n_gpus, rank)
     ctx = g4a.Context(device, max_positions=MAX_CTX + 128)
     stream = torch.cuda.Stream()
@@ -1116,9 +1156,15 @@ def main():
         job_bytes = float(byt[0])
         clocks_all = [None] * world
         dist.all_gather_object(clocks_all, d["clocks"])
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {"rank": rank, "timed_ms": round(d["total_ms"], 4),
+                                          "host_enqueue_ms": round(d["enqueue_ms"], 4),
+                                          "main_kernel_us": round(d["kernels"]["main"][0] * 1e3, 2),
+                                          "bytes_per_step": int(sb["total"]), "cpus": sorted(os.sched_getaffinity(0))})
     else:
         job_bytes = float(sb["total"])
         clocks_all = [d["clocks"]]
+        per_rank = None
     tokens = SEQS_PER_GPU * n_gpus
     value = tokens * a.steps / total_s
     e2e_value = tokens * d["e2e_steps"] / e2e_s
@@ -1167,6 +1213,7 @@ def main():
         "dtype": "f16 KV / f32 compute",
         "data": "synthetic",
         "config": {
+            "timed_step": "one CUDA-graph replay of the step's three launches (prep, main, combine)",
             "workload": "cfg2: paged batched decode, 64 sequences per GPU, context U[1,4096] (seeded), "
                         "E2B layers 13 (sliding, 256-d) and 14 (global, 512-d), 8 q heads / 1 KV head, "
                         "f16 KV in 64-token pages, f32 q",
@@ -1195,14 +1242,19 @@ def main():
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": d["h2d"],
                 "d2h_bytes_per_step": d["d2h"], "steps": d["e2e_steps"],
-                "api": "g4a_decode_host (C ABI): pinned host q/k/v copied in, output copied back, one call per step"},
-        "gpu_launches": sum(v[1] for v in d["kernels"].values()),  # the timed pass launches the same kernels
+                "api": "g4a_decode_host (C ABI): pinned host q/k/v copied in, output copied back, one call per step; "
+                       "each layer's kernels start when its inputs are in, its output copied out during the next "
+                       "layer's kernels",
+                "phases_us_per_step": d["e2e_phases_us"]},
+        "gpu_launches": sum(v[1] for v in d["kernels"].values()),  # the timed graph replays the same kernels
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
                    "sm_max_mhz": clocks_all[0]["sm_max_mhz"] if clocks_all[0] else None, "reasons": reasons},
     }
     if cpu_rate is not None:
         line["cpu_baseline"] = {"value": round(cpu_rate, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
                                 "sample": desc}
+    if per_rank is not None:
+        line["per_rank"] = per_rank
     line.update(extras)
     print(json.dumps(line), flush=True)
     cp = extras.get("prefill_cp")

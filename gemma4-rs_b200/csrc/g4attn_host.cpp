@@ -290,6 +290,9 @@ extern "C" void g4a_ctx_destroy(g4a_ctx *ctx) {
     cudaFree(ctx->d_q8s);
     cudaFree(ctx->d_io);
     if (ctx->h_flag) cudaFreeHost(ctx->h_flag);
+    if (ctx->copy_in) cudaStreamSynchronize(ctx->copy_in), cudaStreamDestroy(ctx->copy_in);
+    if (ctx->copy_out) cudaStreamSynchronize(ctx->copy_out), cudaStreamDestroy(ctx->copy_out);
+    for (auto e : ctx->io_events) cudaEventDestroy(e);
     for (auto &sl : ctx->pin) {
         if (sl.p) cudaFreeHost(sl.p);
         if (sl.ev) cudaEventDestroy(sl.ev);
@@ -905,10 +908,16 @@ extern "C" int g4a_attend(g4a_ctx *ctx, const float *q, const float *keys, const
 
 namespace {
 
-// Validates one decode step, allocates the pages its appends need, advances
-// the cache lengths and fills `plan` (model.rs:393-410 per sequence and layer).
-int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
-                 const int32_t *seq_ids, const int32_t *positions, Plan &plan) {
+// Per-layer facts of a decode step, found by check_decode.
+struct DecodeLayers {
+    std::vector<int32_t> src, hd;
+    std::vector<char> owner, global;
+};
+
+// Validates one decode step (model.rs:389-399, context_memory.rs:53-69) and
+// allocates the pages its appends need; changes no cache length.
+int check_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
+                 const int32_t *seq_ids, const int32_t *positions, DecodeLayers &info) {
     if (!ctx || !kv || kv->ctx != ctx) return fail(ctx, G4A_COMPUTE, "compute: cache belongs to another context");
     cudaSetDevice(ctx->device);
     const g4a_hparams &hp = ctx->hp;
@@ -917,8 +926,12 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
     if (hp.n_heads != kHeads || hp.n_kv_heads != 1)
         return fail(ctx, G4A_COMPUTE, "compute: fused decode serves %d query heads over 1 KV head", kHeads);
     // ---- validate layers (model.rs:389-399) ----
-    std::vector<int32_t> src(n_layers), hd(n_layers);
-    std::vector<char> owner(n_layers), global(n_layers);
+    info.src.assign(n_layers, 0);
+    info.hd.assign(n_layers, 0);
+    info.owner.assign(n_layers, 0);
+    info.global.assign(n_layers, 0);
+    std::vector<int32_t> &src = info.src, &hd = info.hd;
+    std::vector<char> &owner = info.owner, &global = info.global;
     for (int32_t i = 0; i < n_layers; i++) {
         const g4a_decode_layer &a = layers[i];
         int32_t detail = 0;
@@ -974,10 +987,18 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
                 int rc = ensure_rows(kv, seq_ids[j], kv_len(kv, seq_ids[j], layers[i].layer) + 1);
                 if (rc) return rc;
             }
-    int rc = upload_bt(kv);
-    if (rc) return rc;
+    return upload_bt(kv);
+}
+
+// Fills `plan` with the tasks of layers [first, first + count) of a checked
+// step: one task per (sequence, layer), its rows cut into work items.
+void plan_decode(g4a_ctx *ctx, g4a_kv *kv, const g4a_decode_layer *layers, int32_t n_seqs, const int32_t *seq_ids,
+                 const int32_t *positions, const DecodeLayers &info, int32_t first, int32_t count, Plan &plan) {
+    const g4a_hparams &hp = ctx->hp;
+    const std::vector<int32_t> &src = info.src, &hd = info.hd;
+    const std::vector<char> &owner = info.owner, &global = info.global;
     int64_t weighted = 0;
-    for (int32_t i = 0; i < n_layers; i++)
+    for (int32_t i = first; i < first + count; i++)
         for (int32_t j = 0; j < n_seqs; j++) {
             int64_t lo, hi;
             if (global[i]) lo = 0, hi = (int64_t)positions[j] + 1;
@@ -988,7 +1009,7 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
     // f16 kernel: about three items per SM over the whole call, by K/V bytes
     const int64_t weighted_all = weighted;
     const int64_t item_weight = std::max<int64_t>(64, (weighted_all + 3 * ctx->n_sm - 1) / (3 * ctx->n_sm));
-    for (int32_t i = 0; i < n_layers; i++) {
+    for (int32_t i = first; i < first + count; i++) {
         const g4a_decode_layer &a = layers[i];
         const auto &L = kv->layers[src[i]];
         const int which = hd[i] == 512;
@@ -1028,9 +1049,25 @@ int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_la
         }
     }
     if (plan.f16_fast) assign_ctas(plan, ctx->n_sm);
+}
+
+// The appended rows of a planned step count as stored (context_memory.rs:44-51).
+void commit_decode(g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
+                   const int32_t *seq_ids, const DecodeLayers &info) {
     for (int32_t i = 0; i < n_layers; i++)
-        if (owner[i])
+        if (info.owner[i])
             for (int32_t j = 0; j < n_seqs; j++) kv_len(kv, seq_ids[j], layers[i].layer) += 1;
+}
+
+// Validates one decode step, allocates the pages its appends need, advances
+// the cache lengths and fills `plan` (model.rs:393-410 per sequence and layer).
+int build_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer *layers, int32_t n_seqs,
+                 const int32_t *seq_ids, const int32_t *positions, Plan &plan) {
+    DecodeLayers info;
+    const int rc = check_decode(ctx, kv, n_layers, layers, n_seqs, seq_ids, positions, info);
+    if (rc) return rc;
+    plan_decode(ctx, kv, layers, n_seqs, seq_ids, positions, info, 0, n_layers, plan);
+    commit_decode(kv, n_layers, layers, n_seqs, seq_ids, info);
     return G4A_OK;
 }
 
@@ -1044,6 +1081,22 @@ extern "C" int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_
     return run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16);
 }
 
+namespace {
+
+// Event from the context's spare list (profiling records).
+cudaEvent_t spare_event(g4a_ctx *ctx) {
+    cudaEvent_t e = nullptr;
+    if (!ctx->spare.empty()) {
+        e = ctx->spare.back();
+        ctx->spare.pop_back();
+    } else {
+        cudaEventCreate(&e);
+    }
+    return e;
+}
+
+}  // namespace
+
 extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer_host *layers,
                                int32_t n_seqs, const int32_t *seq_ids, const int32_t *positions) {
     if (!ctx || !kv) return G4A_COMPUTE;
@@ -1055,7 +1108,7 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
     std::vector<int32_t> width(n_layers);
     size_t total = 0;
     for (int32_t i = 0; i < n_layers; i++) {
-        width[i] = g4a_head_dim(&ctx->hp, layers[i].layer);  // the layer itself is checked by build_decode
+        width[i] = g4a_head_dim(&ctx->hp, layers[i].layer);  // the layer itself is checked by check_decode
         off[i] = total;
         total += (size_t)n_seqs * width[i] * (2 * kHeads + 2);
     }
@@ -1063,6 +1116,15 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
     if (rc) return rc;
     if (!ctx->h_flag) G4A_CUDA_TRY(ctx, cudaHostAlloc(reinterpret_cast<void **>(&ctx->h_flag), sizeof(int),
                                                       cudaHostAllocDefault));
+    if (!ctx->copy_in) G4A_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking));
+    if (!ctx->copy_out) G4A_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking));
+    // events: [0] call start, then per layer (inputs in, kernels done)
+    while (ctx->io_events.size() < 1 + 2 * (size_t)n_layers) {
+        cudaEvent_t e = nullptr;
+        G4A_CUDA_TRY(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        ctx->io_events.push_back(e);
+    }
+    cudaEvent_t *ev = ctx->io_events.data();
     std::vector<g4a_decode_layer> dev(n_layers);
     for (int32_t i = 0; i < n_layers; i++) {
         const size_t qn = (size_t)n_seqs * kHeads * width[i], kn = (size_t)n_seqs * width[i];
@@ -1072,36 +1134,67 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
                                   h.k_raw_host ? base + qn : nullptr, h.v_raw_host ? base + qn + kn : nullptr,
                                   h.q_norm_w_dev,  h.k_norm_w_dev, h.out_host ? base + qn + 2 * kn : nullptr};
     }
-    // The inputs go first, into the context's own slots, so that the copies
-    // overlap the host-side validation and planning; on a rejected call the
-    // stream is drained before returning (no copy still reads the caller's
-    // buffers) and neither the cache nor out_host has been touched.
+    // The inputs go first, layer by layer on the copy-in stream (after the
+    // work already queued on the context's stream), into the context's own
+    // slots, so that the copies overlap the host-side validation and planning
+    // and a later layer's copy overlaps an earlier layer's kernels. On a
+    // rejected call the copy stream is drained before returning (no copy
+    // still reads the caller's buffers) and neither the cache nor out_host has
+    // been touched.
+    G4A_CUDA_TRY(ctx, cudaEventRecord(ev[0], ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->copy_in, ev[0], 0));
     for (int32_t i = 0; i < n_layers; i++) {
         const size_t qb = (size_t)n_seqs * kHeads * width[i] * sizeof(float), kb = (size_t)n_seqs * width[i] * sizeof(float);
         const g4a_decode_layer_host &h = layers[i];
         int32_t src = -1;
         const bool owner = g4a_kv_source_layer(&ctx->hp, h.layer, &src, nullptr) == G4A_OK && src == h.layer;
+        cudaEvent_t a = ctx->profiling ? spare_event(ctx) : nullptr;
+        if (a) cudaEventRecord(a, ctx->copy_in);
         if (h.q_raw_host && qb)
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].q_raw_dev), h.q_raw_host, qb,
-                                              cudaMemcpyHostToDevice, ctx->stream));
+                                              cudaMemcpyHostToDevice, ctx->copy_in));
         if (owner && h.k_raw_host && h.v_raw_host && kb) {
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].k_raw_dev), h.k_raw_host, kb,
-                                              cudaMemcpyHostToDevice, ctx->stream));
+                                              cudaMemcpyHostToDevice, ctx->copy_in));
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].v_raw_dev), h.v_raw_host, kb,
-                                              cudaMemcpyHostToDevice, ctx->stream));
+                                              cudaMemcpyHostToDevice, ctx->copy_in));
         }
+        if (a) {
+            cudaEvent_t b = spare_event(ctx);
+            cudaEventRecord(b, ctx->copy_in);
+            ctx->recs.push_back({G4A_K_COPY_IN, a, b});
+        }
+        G4A_CUDA_TRY(ctx, cudaEventRecord(ev[1 + 2 * i], ctx->copy_in));
     }
-    Plan &plan = scratch_plan();
-    if ((rc = build_decode(ctx, kv, n_layers, dev.data(), n_seqs, seq_ids, positions, plan))) {
-        cudaStreamSynchronize(ctx->stream);
+    DecodeLayers info;
+    if ((rc = check_decode(ctx, kv, n_layers, dev.data(), n_seqs, seq_ids, positions, info))) {
+        cudaStreamSynchronize(ctx->copy_in);
         return rc;
     }
-    if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16))) return rc;
-    for (int32_t i = 0; i < n_layers; i++)
+    // Each layer's kernels once its inputs are in; its output copied out on
+    // the copy-out stream while the next layer's kernels run.
+    for (int32_t i = 0; i < n_layers; i++) {
+        G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->stream, ev[1 + 2 * i], 0));
+        Plan &plan = scratch_plan();
+        plan_decode(ctx, kv, dev.data(), n_seqs, seq_ids, positions, info, i, 1, plan);
+        if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16))) return rc;
+        G4A_CUDA_TRY(ctx, cudaEventRecord(ev[2 + 2 * i], ctx->stream));
+        if (!layers[i].out_host) continue;
+        G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->copy_out, ev[2 + 2 * i], 0));
+        cudaEvent_t a = ctx->profiling ? spare_event(ctx) : nullptr;
+        if (a) cudaEventRecord(a, ctx->copy_out);
         G4A_CUDA_TRY(ctx, cudaMemcpyAsync(layers[i].out_host, dev[i].out_dev,
                                           (size_t)n_seqs * kHeads * width[i] * sizeof(float), cudaMemcpyDeviceToHost,
-                                          ctx->stream));
+                                          ctx->copy_out));
+        if (a) {
+            cudaEvent_t b = spare_event(ctx);
+            cudaEventRecord(b, ctx->copy_out);
+            ctx->recs.push_back({G4A_K_COPY_OUT, a, b});
+        }
+    }
+    commit_decode(kv, n_layers, dev.data(), n_seqs, seq_ids, info);
     G4A_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->h_flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->copy_out));
     G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     const int flag = *ctx->h_flag;
     if (flag) {

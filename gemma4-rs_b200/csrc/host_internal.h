@@ -68,6 +68,10 @@ struct g4a_ctx {
     float *d_io = nullptr;
     size_t io_cap = 0;  // floats
     int *h_flag = nullptr;
+    // g4a_decode_host's copy streams (host-to-device inputs, device-to-host
+    // outputs) and its events: per layer, inputs copied and kernels done
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    std::vector<cudaEvent_t> io_events;
     // context-parallel prefill state (cp_host.cpp), freed by cp_free
     void *cp = nullptr;
     void (*cp_free)(void *) = nullptr;

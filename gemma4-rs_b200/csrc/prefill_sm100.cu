@@ -149,9 +149,9 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     return false;
 }
 
+// One work item on one CTA pair (both CTAs call this with the same item).
 template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
+__device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ problems, const WorkItem it, int *err) {
     using C = Cfg<HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,7 +161,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     volatile int *abort = &bars->abort;
 
     const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader
-    const WorkItem it = items[blockIdx.x >> 1];
     const ProblemDev &pb = problems[it.problem];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = it.n_kv_tiles;
@@ -573,6 +572,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+template <int HD>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
+    prefill_item<HD>(problems, items[blockIdx.x >> 1], err);
+}
+
+// Items of both head widths in one grid (a prompt's sliding and global layers
+// together), taken longest first: the width is the item's problem's.
+constexpr int kSmemMixed = Cfg<256>::kSmemBytes > Cfg<512>::kSmemBytes ? Cfg<256>::kSmemBytes : Cfg<512>::kSmemBytes;
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    prefill_kernel_mixed(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
+    const WorkItem it = items[blockIdx.x >> 1];
+    if (problems[it.problem].hd == 256) prefill_item<256>(problems, it, err);
+    else prefill_item<512>(problems, it, err);
+}
+
 // bf16 -> fp16 copies of up to kMaxSegs V arrays in one launch (blockIdx.y =
 // segment); 8 elements per thread and step. Every count is a multiple of 8
 // (a head width) and every address 16-byte aligned (checked on the host).
@@ -681,7 +696,8 @@ struct Prepared {
     };
     std::vector<ConvLaunch> conv;
     size_t n_work[2] = {0, 0};
-    uint64_t used = 0;  // call counter at the last use
+    bool mixed = false;  // both widths in one launch (the items in one cost order)
+    uint64_t used = 0;   // call counter at the last use
 };
 
 // Host-side state the prefill keeps in the context between calls.
@@ -725,9 +741,15 @@ static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_
     if (!S->attr_set) {
         cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
         cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_kernel_mixed, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMixed);
         S->attr_set = true;
     }
     // two CTAs (one cluster) per work item
+    if (P.mixed) {
+        prefill_kernel_mixed<<<2 * (unsigned)(P.n_work[0] + P.n_work[1]), kThreads, kSmemMixed, st>>>(
+            P.d_problems, P.d_items, d_err);
+        return cudaGetLastError();
+    }
     if (P.n_work[0])
         prefill_kernel<256><<<2 * (unsigned)P.n_work[0], kThreads, Cfg<256>::kSmemBytes, st>>>(P.d_problems,
                                                                                             P.d_items, d_err);
@@ -913,10 +935,14 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         }
     }
     // Largest work first: the block scheduler then fills SMs longest-first.
+    // With both widths, one launch takes every item in one order, an item's
+    // cost being its key tiles times 2 (width 256: S and PV of 256 columns)
+    // or 3 (a 256-column half of width 512 recomputes the 512-wide S).
     for (auto &w : work)
         std::stable_sort(w.begin(), w.end(),
                          [](const WorkItem &a, const WorkItem &b) { return a.n_kv_tiles > b.n_kv_tiles; });
     const size_t n_items = work[0].size() + work[1].size();
+    P.mixed = !work[0].empty() && !work[1].empty();
     if ((e = cudaMalloc(&P.d_problems, hp.size() * sizeof(ProblemDev))) != cudaSuccess ||
         (e = cudaMalloc(&P.d_items, std::max<size_t>(n_items, 1) * sizeof(WorkItem))) != cudaSuccess) {
         free_prepared(P);
@@ -925,6 +951,10 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
     }
     std::vector<WorkItem> all(work[0]);
     all.insert(all.end(), work[1].begin(), work[1].end());
+    if (P.mixed) {
+        auto cost = [&](const WorkItem &w) { return w.n_kv_tiles * (hp[w.problem].hd == 512 ? 3 : 2); };
+        std::stable_sort(all.begin(), all.end(), [&](const WorkItem &a, const WorkItem &b) { return cost(a) > cost(b); });
+    }
     // stream-ordered uploads from pageable memory (staged by the driver before
     // the call returns)
     if ((e = cudaMemcpyAsync(P.d_problems, hp.data(), hp.size() * sizeof(ProblemDev), cudaMemcpyHostToDevice, st)) !=

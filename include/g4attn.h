@@ -116,7 +116,9 @@ typedef enum g4a_kernel {
     G4A_K_CP_ATTEND_LOCAL = 7, /* g4a_cp_prefill: attention over this rank's own data */
     G4A_K_CP_ATTEND_REMOTE = 8,/* g4a_cp_prefill: attention over exchanged data */
     G4A_K_CP_MERGE = 9,        /* g4a_cp_prefill: log-sum-exp merges, weights, packing */
-    G4A_K_COUNT = 10
+    G4A_K_COPY_IN = 10,        /* g4a_decode_host: host-to-device copies of the inputs */
+    G4A_K_COPY_OUT = 11,       /* g4a_decode_host: device-to-host copies of the outputs */
+    G4A_K_COUNT = 12
 } g4a_kernel;
 int g4a_profile_enable(g4a_ctx *ctx, int enable);
 int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches);
@@ -210,13 +212,16 @@ int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_laye
 /* g4a_decode for a caller whose vectors live in host memory, as the
  * reference's attend (model.rs:345-366) takes host slices: q_raw_host
  * [n][n_heads*hd], k_raw_host/v_raw_host [n][hd] (owner layers; may be NULL
- * on KV-shared layers) are copied in on the context's stream, the step runs,
+ * on KV-shared layers) are copied in, the step runs on the context's stream,
  * out_host [n][n_heads*hd] is copied back, and the call returns when it is
  * there, with the device's softmax/timeout flags checked (G4A_NONFINITE,
  * G4A_TIMEOUT). Page-locked host buffers copy asynchronously by DMA;
  * pageable ones are staged by the driver. The norm weights stay device
- * pointers (model weights are resident). Validation happens before any
- * copy, so a rejected call leaves the cache and the outputs untouched. */
+ * pointers (model weights are resident). A rejected call leaves the cache and
+ * the outputs untouched. The layers run one after another, each as soon as
+ * its inputs are on the device: a later layer's inputs are copied in while an
+ * earlier layer's kernels run, and an earlier layer's output is copied out
+ * while a later layer's kernels run (two copy streams of the context). */
 typedef struct g4a_decode_layer_host {
     int32_t layer;
     const float *q_raw_host;
