@@ -555,6 +555,13 @@ __global__ void __launch_bounds__(kThreadsF16, 1) decode_f16_kernel(DecodeParams
     }
     __syncthreads();
     release_dependents();  // the combine kernel may be scheduled; it waits for our end
+    if (p.stall) {
+        // g4a_debug_stall: a bounded wait on a bit of the error word that
+        // nothing sets, before any load; the time-out is recorded as a
+        // stalled ring wait would record it, and the CTA does no work
+        if (threadIdx.x == 0 && !ptx::stall_wait(p.err_flag, 1 << 30, 2000000ull)) atomicOr(p.err_flag, 4);
+        return;
+    }
     const int i0 = p.cta_start[blockIdx.x], i1 = p.cta_start[blockIdx.x + 1];
     uint32_t st = 0;  // stage counter over this CTA's items
     if (warp == kWarpsC) {

@@ -310,6 +310,14 @@ extern "C" int g4a_ctx_set_stream(g4a_ctx *ctx, void *stream) {
     return G4A_OK;
 }
 
+extern "C" int g4a_debug_stall(g4a_ctx *ctx, int32_t kernel) {
+    if (!ctx) return G4A_COMPUTE;
+    if (kernel != G4A_K_DECODE_MAIN && kernel != G4A_K_PREFILL)
+        return fail(ctx, G4A_COMPUTE, "compute: no stall test for kernel %d", kernel);
+    ctx->stall_mask |= 1u << kernel;
+    return G4A_OK;
+}
+
 extern "C" int g4a_sync(g4a_ctx *ctx) {
     if (!ctx) return G4A_COMPUTE;
     cudaSetDevice(ctx->device);
@@ -750,6 +758,10 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
 
 int launch_staged(g4a_ctx *ctx, const Staged &st) {
     DecodeParams p = st.params;
+    if (st.f16_fast && (ctx->stall_mask & (1u << G4A_K_DECODE_MAIN))) {
+        p.stall = 1;
+        ctx->stall_mask &= ~(1u << G4A_K_DECODE_MAIN);
+    }
     const DecodeItem *items = reinterpret_cast<const DecodeItem *>(st.meta + st.items_offset);
     if (st.f16_fast) {  // both head widths in one launch
         p.items = items;
@@ -1263,8 +1275,10 @@ extern "C" int g4a_prefill(g4a_ctx *ctx, int32_t n, const g4a_prefill_problem *p
         return fail(ctx, G4A_COMPUTE, "compute: prefill serves %d query heads over 1 KV head", kHeads);
     const char *msg = "";
     int rc = G4A_OK;
+    const bool stall = (ctx->stall_mask & (1u << G4A_K_PREFILL)) != 0;
+    ctx->stall_mask &= ~(1u << G4A_K_PREFILL);
     const cudaError_t e = timed(ctx, G4A_K_PREFILL, [&] {
-        rc = prefill_run(ctx->prefill, ctx->d_err, n, problems, ctx->stream, &msg);
+        rc = prefill_run(ctx->prefill, ctx->d_err, n, problems, ctx->stream, &msg, stall);
         return cudaSuccess;
     });
     (void)e;

@@ -72,6 +72,9 @@ struct g4a_ctx {
     // outputs) and its events: per layer, inputs copied and kernels done
     cudaStream_t copy_in = nullptr, copy_out = nullptr;
     std::vector<cudaEvent_t> io_events;
+    // g4a_debug_stall: kernels (bit per g4a_kernel id) whose next launch runs
+    // the bounded test wait instead of its work
+    uint32_t stall_mask = 0;
     // context-parallel prefill state (cp_host.cpp), freed by cp_free
     void *cp = nullptr;
     void (*cp_free)(void *) = nullptr;

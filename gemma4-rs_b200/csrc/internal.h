@@ -83,6 +83,7 @@ struct DecodeParams {
     const int32_t *split_tasks;  // f16 kernel: tasks whose items are merged by the combine kernel
     int32_t max_rows;            // exact kernels: the most rows a task attends
     float *scores;               // exact kernels: [tasks][kHeads][max_rows]
+    int32_t stall;               // f16 main kernel: the g4a_debug_stall test wait, then no work
 };
 
 // Bulk append of already processed rows, or norm+RoPE of raw rows.
@@ -214,8 +215,9 @@ cudaError_t e2b_gather_rows(const int8_t *xq, const float *xs, int cols, const i
 struct PrefillScratch;
 PrefillScratch *prefill_scratch_new();
 void prefill_scratch_free(PrefillScratch *s);
+// stall: the g4a_debug_stall test wait in every CTA pair instead of the work
 int prefill_run(PrefillScratch *s, int *d_err, int32_t n, const struct g4a_prefill_problem *problems,
-                cudaStream_t st, const char **msg);
+                cudaStream_t st, const char **msg, bool stall = false);
 
 // Key/value-shard context-parallel merge (cp_kernels.cu): partial results of
 // one rank as row segments [t0, t1) of the sequence, o [t1-t0][8][hd] and

@@ -150,6 +150,14 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
 }
 
 // One work item on one CTA pair (both CTAs call this with the same item).
+// g4a_debug_stall: both CTAs of every pair skip the item after the leader's
+// bounded wait on a bit of the error word that nothing sets (no barrier,
+// TMEM or load touched yet), recording the time-out as a stalled wait would.
+__device__ __forceinline__ void stall_item(int *err) {
+    if (threadIdx.x == 0 && ptx::cluster_ctarank() == 0 && !ptx::stall_wait(err, 1 << 30, 2000000ull))
+        atomicOr(err, 2);
+}
+
 template <int HD>
 __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ problems, const WorkItem it, int *err) {
     using C = Cfg<HD>;
@@ -574,7 +582,8 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
 
 template <int HD>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
+    prefill_kernel(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err, int stall) {
+    if (stall) return stall_item(err);
     prefill_item<HD>(problems, items[blockIdx.x >> 1], err);
 }
 
@@ -582,7 +591,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // together), taken longest first: the width is the item's problem's.
 constexpr int kSmemMixed = Cfg<256>::kSmemBytes > Cfg<512>::kSmemBytes ? Cfg<256>::kSmemBytes : Cfg<512>::kSmemBytes;
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    prefill_kernel_mixed(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err) {
+    prefill_kernel_mixed(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items, int *err,
+                         int stall) {
+    if (stall) return stall_item(err);
     const WorkItem it = items[blockIdx.x >> 1];
     if (problems[it.problem].hd == 256) prefill_item<256>(problems, it, err);
     else prefill_item<512>(problems, it, err);
@@ -736,7 +747,8 @@ static void free_prepared(Prepared &p) {
     p = Prepared();
 }
 
-static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_err, cudaStream_t st) {
+static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_err, cudaStream_t st,
+                                   bool stall) {
     for (const auto &c : P.conv) bf16_to_f16_kernel<<<dim3(c.bx, c.cnt), 256, 0, st>>>(c.segs);
     if (!S->attr_set) {
         cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
@@ -747,15 +759,15 @@ static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_
     // two CTAs (one cluster) per work item
     if (P.mixed) {
         prefill_kernel_mixed<<<2 * (unsigned)(P.n_work[0] + P.n_work[1]), kThreads, kSmemMixed, st>>>(
-            P.d_problems, P.d_items, d_err);
+            P.d_problems, P.d_items, d_err, (int)stall);
         return cudaGetLastError();
     }
     if (P.n_work[0])
-        prefill_kernel<256><<<2 * (unsigned)P.n_work[0], kThreads, Cfg<256>::kSmemBytes, st>>>(P.d_problems,
-                                                                                            P.d_items, d_err);
+        prefill_kernel<256><<<2 * (unsigned)P.n_work[0], kThreads, Cfg<256>::kSmemBytes, st>>>(
+            P.d_problems, P.d_items, d_err, (int)stall);
     if (P.n_work[1])
         prefill_kernel<512><<<2 * (unsigned)P.n_work[1], kThreads, Cfg<512>::kSmemBytes, st>>>(
-            P.d_problems, P.d_items + P.n_work[0], d_err);
+            P.d_problems, P.d_items + P.n_work[0], d_err, (int)stall);
     return cudaGetLastError();
 }
 
@@ -787,7 +799,7 @@ void prefill_scratch_free(PrefillScratch *s) {
 // launches one kernel per head width. Returns a g4a_status; *msg names the
 // failure.
 int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_problem *pr, cudaStream_t st,
-                const char **msg) {
+                const char **msg, bool stall) {
     *msg = "";
     if (n < 0 || (n > 0 && !pr)) {
         *msg = "invalid prefill problem list";
@@ -798,7 +810,7 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         if (P.used && P.key.size() == (size_t)n &&
             (n == 0 || std::memcmp(pr, P.key.data(), (size_t)n * sizeof(g4a_prefill_problem)) == 0)) {
             P.used = S->calls;
-            const cudaError_t e = launch_prepared(S, P, d_err, st);
+            const cudaError_t e = launch_prepared(S, P, d_err, st, stall);
             if (e != cudaSuccess) {
                 *msg = cudaGetErrorString(e);
                 return G4A_CUDA;
@@ -969,7 +981,7 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
     P.n_work[1] = work[1].size();
     P.key.assign(pr, pr + n);
     P.used = S->calls;
-    if ((e = launch_prepared(S, P, d_err, st)) != cudaSuccess) {
+    if ((e = launch_prepared(S, P, d_err, st, stall)) != cudaSuccess) {
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }

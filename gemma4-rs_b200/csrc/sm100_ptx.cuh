@@ -135,6 +135,23 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// The wait behind g4a_debug_stall (tests of failure handling): polls a
+// device word for a bit that nothing sets, for at most limit_ns of the
+// global timer; returns false when the wait ran out, as it always does.
+__device__ __forceinline__ bool stall_wait(const int *word, int bit, uint64_t limit_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < limit_ns) {
+        if (*reinterpret_cast<const volatile int *>(word) & bit) return true;
+        __nanosleep(1000);
+    }
+    return false;
+}
+
 // L2 prefetch of one tile of a tensor map (no shared memory, no barrier).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const void *tmap, int32_t x, int32_t y) {
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)

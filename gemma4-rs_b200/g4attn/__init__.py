@@ -144,6 +144,7 @@ def _load():
     L.g4a_model_set_eos.argtypes = [_vp, _i32p, ctypes.c_int32]
     L.g4a_model_generate.argtypes = [_vp, ctypes.c_int32, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                      _i32p]
+    L.g4a_debug_stall.argtypes = [_vp, ctypes.c_int32]
     L.g4a_cp_prefill.argtypes = [_vp, _vp, ctypes.c_int32, ctypes.POINTER(CpProblem)]
     L.g4a_cp_wait.argtypes = [_vp, _vp, ctypes.c_int32]
     L.g4a_nccl_unique_id.argtypes = [_vp]
@@ -264,7 +265,7 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None) and not _exiting:
-            for o in [o for o in _live if not isinstance(o, Context) and o.ctx is self]:
+            for o in [o for o in _live if not isinstance(o, Context) and getattr(o, "ctx", None) is self]:
                 o.close()
             lib.g4a_ctx_destroy(self.h)
         self.h = None
@@ -284,6 +285,10 @@ class Context:
 
     def profile(self, enable: bool):
         self.check(lib.g4a_profile_enable(self.h, int(enable)))
+
+    def debug_stall(self, kernel: int):
+        """g4a_debug_stall: the next launch of `kernel` times out (tests)."""
+        self.check(lib.g4a_debug_stall(self.h, kernel))
 
     def profile_read(self, kernel: int):
         """(total device ms, launches) of one kernel since profiling was enabled."""

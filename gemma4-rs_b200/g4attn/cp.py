@@ -46,6 +46,24 @@ def zigzag_chunks(seq_len: int, world: int, rank: int) -> list[tuple[int, int]]:
     return [(a * c, (a + 1) * c), (b * c, (b + 1) * c)]
 
 
+def check_agreement(dist, torch, **meta: int) -> None:
+    """Raises ValueError on every rank unless all ranks pass the same values
+    (sequence length, head width, schedule ...): a rank with other shard
+    metadata would make the collectives of the schedule exchange mismatched
+    buffers. One small all-gather on the process group."""
+    names = sorted(meta)
+    mine = torch.tensor([int(meta[n]) for n in names], dtype=torch.int64)
+    if dist.get_backend() == "nccl":
+        mine = mine.cuda()
+    every = [torch.empty_like(mine) for _ in range(dist.get_world_size())]
+    dist.all_gather(every, mine)
+    table = torch.stack(every).cpu()
+    for i, n in enumerate(names):
+        vals = table[:, i].tolist()
+        if len(set(vals)) != 1:
+            raise ValueError(f"ranks disagree on {n}: {vals}")
+
+
 @dataclass
 class Problem:
     """Queries [q0, q1) against keys [k0, k1) (absolute positions). own >= 0:

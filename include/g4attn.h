@@ -123,6 +123,17 @@ typedef enum g4a_kernel {
 int g4a_profile_enable(g4a_ctx *ctx, int enable);
 int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches);
 
+/* For tests of failure handling (no reference counterpart; the reference's
+ * failures are EngError results, crates/llm-eng/src/error.rs:3-15): the next
+ * launch of `kernel` (G4A_K_DECODE_MAIN: the f16 paged decode, or
+ * G4A_K_PREFILL) on this context waits, before it loads anything, on a bit of
+ * the context's device error word that nothing sets; the wait gives up after
+ * about 2 ms as any bounded wait of the kernel gives up, records the
+ * time-out and skips the kernel's work. The call's g4a_sync (or
+ * g4a_decode_host itself) then returns G4A_TIMEOUT and the context stays
+ * usable. Other kernels return G4A_COMPUTE. */
+int g4a_debug_stall(g4a_ctx *ctx, int32_t kernel);
+
 /* ---- attention primitive ---------------------------------------------- */
 
 /* model.rs:348-366 attend: grouped-query attention for one query position.

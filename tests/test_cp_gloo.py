@@ -229,3 +229,95 @@ def test_kv_shard_rows_cover_the_sequence():
             probs = cp.kv_shard_problems(1024, world, rank)
             assert [p[2:] for p in probs] == cp.zigzag_chunks(1024, world, rank)
             assert all(p[0] == p[2] and p[1] == 1024 for p in probs)
+
+
+# ---------------------------------------------------------------------------
+# failures, made on the host: a rank that leaves, a rank that comes late, and
+# ranks that disagree on the shard metadata
+# ---------------------------------------------------------------------------
+
+def _failure_rank_main(rank, world, port, mode, result_dir):
+    sys.path.insert(0, str(ROOT / "gemma4-rs_b200"))
+    import time
+    from datetime import timedelta
+    import torch
+    import torch.distributed as dist
+    from g4attn import cp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    T, hd = 32, 8
+    if mode == "disagree":
+        T = 32 if rank == 0 else 48
+    r = np.random.default_rng(3)
+    q = r.standard_normal((T, 8, hd)) / np.sqrt(hd)
+    k = r.standard_normal((T, hd))
+    v = r.standard_normal((T, hd))
+    t0 = time.monotonic()
+    if mode == "dropped" and rank == world - 1:
+        # this rank leaves between steps: it never enters the schedule
+        Path(result_dir, f"f{rank}.txt").write_text("left")
+        os._exit(0)
+    if mode == "late" and rank == world - 1:
+        time.sleep(1.0)  # well inside the group's 5 s timeout
+    try:
+        cp.check_agreement(dist, torch, seq_len=T, head_dim=hd)
+        chunks = cp.zigzag_chunks(T, world, rank)
+        outs = cp.cp_prefill_kv_shards(q, [k[a:b] for a, b in chunks], [v[a:b] for a, b in chunks], T, world,
+                                       rank, _NpKvShards(dist, torch, world, rank))
+        err = 0.0
+        for (a, b), o in zip(chunks, outs):
+            s = np.einsum("thd,kd->thk", q[a:b], k)
+            s = np.where(np.arange(T)[None, None, :] <= np.arange(a, b)[:, None, None], s, -np.inf)
+            s -= s.max(-1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(-1, keepdims=True)
+            err = max(err, float(np.max(np.abs(p @ v - o))))
+        res = f"ok {err}"
+    except ValueError as e:
+        res = f"metadata {e}"
+    except Exception as e:  # the collective failed: the peer is gone or timed out
+        res = f"error {type(e).__name__}"
+    Path(result_dir, f"f{rank}.txt").write_text(f"{res}|{time.monotonic() - t0:.2f}")
+    os._exit(0)
+
+
+def _run_failure(tmp_path, mode, world=2):
+    import torch.multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.start_processes(_failure_rank_main, args=(world, port, mode, str(tmp_path)), nprocs=world, join=False,
+                             start_method="spawn")
+    while not ctx.join(timeout=60):
+        pass
+    return [Path(tmp_path, f"f{r}.txt").read_text() for r in range(world)]
+
+
+def test_cp_dropped_rank_raises_on_the_others(tmp_path):
+    """A rank that leaves between steps: the remaining rank's first collective
+    of the schedule fails with an error (no hang), within the group's
+    timeout."""
+    res = _run_failure(tmp_path, "dropped")
+    assert res[1] == "left"
+    what, secs = res[0].split("|")
+    assert what.startswith("error"), res[0]
+    assert float(secs) < 30.0
+
+
+def test_cp_late_rank_still_agrees(tmp_path):
+    """A rank that arrives a second late (inside the timeout): the schedule
+    waits for it and every rank's result is still exact."""
+    for r in _run_failure(tmp_path, "late"):
+        what, _ = r.split("|")
+        assert what.startswith("ok"), r
+        assert float(what.split()[1]) < 1e-12
+
+
+def test_cp_disagreeing_shard_metadata_is_rejected(tmp_path):
+    """Ranks with different sequence lengths: every rank gets the metadata
+    error before any data collective."""
+    for r in _run_failure(tmp_path, "disagree"):
+        what, _ = r.split("|")
+        assert what.startswith("metadata ranks disagree on seq_len"), r
