@@ -50,6 +50,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <unordered_map>
 #include <vector>
@@ -132,6 +133,7 @@ struct Barriers {
     uint64_t ring_empty[8];  // both: stage consumed (pair commit)
     uint32_t tmem_base;
     int abort;
+    int k_seen;              // leader: tiles whose K stages the S issuer has seen land
 };
 
 static_assert(sizeof(Barriers) <= 5120, "barrier region");
@@ -156,6 +158,24 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
 __device__ __forceinline__ void stall_item(int *err) {
     if (threadIdx.x == 0 && ptx::cluster_ctarank() == 0 && !ptx::stall_wait(err, 1 << 30, 2000000ull))
         atomicOr(err, 2);
+}
+
+// Bounded wait until a progress counter of another issuing thread of this
+// CTA reaches `target` (false on abort or time-out, as wait_bar).
+__device__ __forceinline__ bool wait_count(const int *counter, int target, volatile int *abort, int *err) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        if (*reinterpret_cast<const volatile int *>(counter) >= target) {
+            __threadfence_block();
+            return true;
+        }
+        if ((i & 1023) == 1023 && *abort) return false;
+    }
+    *abort = 1;
+    atomicOr(err, 2);
+    return false;
+}
+__device__ __forceinline__ void set_count(int *counter, int v) {
+    *reinterpret_cast<volatile int *>(counter) = v;
 }
 
 template <int HD>
@@ -186,6 +206,7 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
             ptx::mbar_init(&bars->ring_empty[i], 1);
         }
         bars->abort = 0;
+        bars->k_seen = 0;
         ptx::fence_mbar_init();
     }
     for (int i = threadIdx.x; i < 2 * 2 * kRows; i += blockDim.x)
@@ -324,6 +345,7 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
                         }
                         ptx::mma2_commit_pair(&bars->ring_empty[slot], kBothCtas);
                     }
+                    set_count(&bars->k_seen, j + 1);
                     if (ok) ptx::mma2_commit_pair(&bars->s_full[j & 1], kBothCtas);
                 }
             } else {
@@ -331,6 +353,14 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
                 constexpr uint32_t kIdescPV = ptx::idesc_f16(0, 0, 1, 2 * kRows, kDV);
                 for (int j = 0; j < n_tiles && ok; j++) {
                     if (!wait_bar<true>(&bars->p_full[j & 1], (uint32_t)(j >> 1) & 1u, abort, err)) {
+                        ok = false;
+                        break;
+                    }
+                    // Width 512 (5-stage ring, 4 K stages per tile): V(j)'s second
+                    // slot last held K(j+1)'s first stage. A parity wait on that
+                    // slot is exact only once that earlier fill has landed, which
+                    // the S issuer has seen when it has waited for K(j+1).
+                    if (HD == 512 && j + 1 < n_tiles && !wait_count(&bars->k_seen, j + 2, abort, err)) {
                         ok = false;
                         break;
                     }
@@ -599,6 +629,530 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     else prefill_item<512>(problems, it, err);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent form: one CTA pair per two SMs runs a host-assigned list of work
+// items (longest-processing-time first), its pipeline running on from item to
+// item. Roles as above, plus four epilogue warps (11-14, one thread per TMEM
+// lane) that read an item's O from TMEM, divide by the row sums and store it
+// straight to global memory while the next item's Q loads, its first S tiles
+// are computed and its first softmax runs; only the next item's first PV
+// waits for them (barrier o_free). The row sums and maxima pass from the
+// softmax warps to the epilogue warps through shared memory (stats, two
+// buffers by item parity). Tile-indexed barriers and buffers use a tile
+// counter that runs over all items of the pair, ring positions a stage
+// counter over all items; items without a visible key load nothing and only
+// write zeros (and lse -inf).
+// ---------------------------------------------------------------------------
+
+constexpr int kThreadsP = 480;
+constexpr int kEpiWarp0 = 11;
+
+struct PBars {
+    Mailbox box[2][2][128];   // [exchange parity][column half][row]
+    float2 stats[2][128];     // (running max in log2 units, row sum) per row, by item parity
+    uint64_t q_full;          // leader: both CTAs' Q bytes of an item
+    uint64_t q_empty;         // both: the item's last S MMA done (pair commit): Q smem free
+    uint64_t s_full[2];
+    uint64_t p_full[2];
+    uint64_t o_done[2];
+    uint64_t o_free;          // leader: 2 x 128 epilogue arrivals: an item's O read out of TMEM
+    uint64_t stats_full[2];   // both: 128 softmax arrivals (stats of an item written)
+    uint64_t stats_free[2];   // both: 128 epilogue arrivals (stats of an item read)
+    uint64_t mma_done;
+    uint64_t ring_full[8];
+    uint64_t ring_empty[8];
+    uint32_t tmem_base;
+    int abort;
+    int k_seen;               // leader: tiles whose K stages the S issuer has seen land
+    int v_seen;               // leader: tiles whose V stages the PV issuer has seen land
+};
+static_assert(sizeof(PBars) <= 8192, "persistent barrier region");
+
+template <int HD>
+struct CfgP {
+    static constexpr int kSmemBytes = Cfg<HD>::kSmemQ + Cfg<HD>::kSmemRing + 8192 + 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+template <int HD>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
+    prefill_persistent(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items,
+                       const int32_t *__restrict__ pair_start, int *err, int stall) {
+    if (stall) return stall_item(err);
+    using C = Cfg<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *q_smem = smem;
+    uint8_t *ring = smem + C::kSmemQ;
+    PBars *bars = reinterpret_cast<PBars *>(ring + C::kSmemRing);
+    volatile int *abort = &bars->abort;
+
+    const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pair = blockIdx.x >> 1;
+    const int i0 = pair_start[pair], i1 = pair_start[pair + 1];
+
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bars->q_full, 1);
+        ptx::mbar_init(&bars->q_empty, 1);
+        for (int i = 0; i < 2; i++) {
+            ptx::mbar_init(&bars->s_full[i], 1);
+            ptx::mbar_init(&bars->p_full[i], 2 * 256);
+            ptx::mbar_init(&bars->o_done[i], 1);
+            ptx::mbar_init(&bars->stats_full[i], kRows);
+            ptx::mbar_init(&bars->stats_free[i], kRows);
+        }
+        ptx::mbar_init(&bars->o_free, 2 * kRows);
+        ptx::mbar_init(&bars->mma_done, 2);
+        for (int i = 0; i < C::kRing; i++) {
+            ptx::mbar_init(&bars->ring_full[i], 1);
+            ptx::mbar_init(&bars->ring_empty[i], 1);
+        }
+        bars->abort = 0;
+        bars->k_seen = 0;
+        bars->v_seen = 0;
+        ptx::fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < 2 * 2 * kRows; i += blockDim.x)
+        bars->box[i / (2 * kRows)][(i / kRows) & 1][i % kRows] = Mailbox{-1, 0.0f};
+    if (warp == 1) {
+        ptx::tmem_alloc2(&bars->tmem_base, kTmemCols);
+        ptx::tmem_relinquish2();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();  // barrier inits of both CTAs visible before any remote signal
+    ptx::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    auto slot_of = [](int pos) { return pos % C::kRing; };
+    auto phase_of = [](int pos) { return (uint32_t)(pos / C::kRing) & 1u; };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        if (lane == 0) {
+            int slot = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;  // bit s: slot s received at least one load
+            uint32_t qk = 0;      // items with keys so far (Q loads issued)
+            bool ok = true;
+            for (int i = i0; i < i1 && ok; i++) {
+                const WorkItem it = items[i];
+                const int n_tiles = it.n_kv_tiles;
+                if (n_tiles == 0) continue;
+                const ProblemDev &pb = problems[it.problem];
+                ptx::prefetch_tmap(&pb.tq);
+                ptx::prefetch_tmap(&pb.tk);
+                ptx::prefetch_tmap(&pb.tv);
+                // Q of this item once the previous item's last S MMA has read the old Q
+                if (qk > 0 && !wait_bar(&bars->q_empty, (qk - 1) & 1u, abort, err)) {
+                    ok = false;
+                    break;
+                }
+                if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * C::kSmemQ);
+                const uint32_t q_full_l = ptx::mapa(&bars->q_full, 0);
+                for (int c = 0; c < C::kQBoxes; c++)
+                    ptx::tma_load_2d_pair(q_smem + c * kQBoxBytes, &pb.tq, q_full_l, 64 * c,
+                                          it.q_tile * 2 * kRows + (int)rank * kRows);
+                qk++;
+                auto push = [&](const CUtensorMap *m, const int *xs, const int *ys) {
+                    if (!ok) return;
+                    if (!wait_bar(&bars->ring_empty[slot], phase ^ 1u, abort, err)) {
+                        ok = false;
+                        return;
+                    }
+                    if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * C::kStageBytes);
+                    const uint32_t bar_l = ptx::mapa(&bars->ring_full[slot], 0);
+                    for (int b = 0; b < C::kStageBoxes; b++)
+                        ptx::tma_load_2d_pair(ring + slot * C::kStageBytes + b * kBoxBytes, m, bar_l, xs[b], ys[b]);
+                    issued |= 1u << slot;
+                    if (++slot == C::kRing) {
+                        slot = 0;
+                        phase ^= 1u;
+                    }
+                };
+                auto push_k = [&](int j) {
+                    const int y = (it.kv_tile_lo + j) * kKeysPerTile + 64 * (int)rank;
+                    for (int st = 0; st < C::kKStages; st++) {
+                        int xs[C::kStageBoxes], ys[C::kStageBoxes];
+                        for (int b = 0; b < C::kStageBoxes; b++) {
+                            xs[b] = 64 * (st * C::kStageBoxes + b);
+                            ys[b] = y;
+                        }
+                        push(&pb.tk, xs, ys);
+                    }
+                };
+                auto push_v = [&](int j) {
+                    const int x = it.dv_half * kDV + 128 * (int)rank;
+                    const int y = (it.kv_tile_lo + j) * kKeysPerTile;
+                    for (int st = 0; st < C::kVStages; st++) {
+                        int xs[C::kStageBoxes], ys[C::kStageBoxes];
+                        for (int b = 0; b < C::kStageBoxes; b++) {
+                            const int q = st * C::kStageBoxes + b;
+                            xs[b] = x + 64 * (q & 1);
+                            ys[b] = y + 64 * (q >> 1);
+                        }
+                        push(&pb.tv, xs, ys);
+                    }
+                };
+                push_k(0);
+                for (int j = 0; j < n_tiles && ok; j++) {
+                    if (j + 1 < n_tiles) push_k(j + 1);
+                    push_v(j);
+                }
+            }
+            // Drain (leader): every load of both CTAs signals the leader's
+            // barriers; no TMA write may land after the pair exits. Normally
+            // the MMA threads already waited for every load; after an abort,
+            // wait here (bounded) for the last Q and each slot's latest load.
+            if (rank == 0 && qk > 0) {
+                for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->q_full, (qk - 1) & 1u); i++) {
+                }
+                if (!ok || *abort) {
+                    for (int s = 0; s < C::kRing; s++) {
+                        if (!(issued >> s & 1u)) continue;
+                        const uint32_t ph = s < slot ? phase : phase ^ 1u;
+                        for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->ring_full[s], ph); i++) {
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == 1 || warp == kPvWarp) {
+        // ------------------------------------------------------------ MMA issuers (leader)
+        const uint64_t q_desc = ptx::smem_desc(ptx::smem_u32(q_smem), 16, 1024);
+        const uint64_t k_desc = ptx::smem_desc(ptx::smem_u32(ring), 16, 1024);
+        const uint64_t v_desc = ptx::smem_desc(ptx::smem_u32(ring), kBoxBytes, 1024);
+        if (lane == 0 && rank == 0) {
+            bool ok = true;
+            uint32_t g = 0;    // tile counter over the pair's items
+            uint32_t qk = 0;   // items with keys so far
+            int pos_base = 0;  // push-sequence position of the item's first stage
+            for (int i = i0; i < i1 && ok; i++) {
+                const int n_tiles = items[i].n_kv_tiles;
+                if (n_tiles == 0) continue;
+                if (warp == 1) {
+                    // S(g) = Q K^T into S buffer g&1, once PV(g-2) has read P(g-2) from it
+                    constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, 2 * kRows, kKeysPerTile);
+                    if (!wait_bar(&bars->q_full, qk & 1u, abort, err)) {
+                        ok = false;
+                        break;
+                    }
+                    for (int j = 0; j < n_tiles && ok; j++, g++) {
+                        if (g >= 2 && !wait_bar(&bars->o_done[g & 1], ((g - 2) >> 1) & 1u, abort, err)) {
+                            ok = false;
+                            break;
+                        }
+                        // Width 512: K(0)'s last stage takes the slot of the previous
+                        // item's last V stage; its parity wait is exact once the PV
+                        // issuer has seen that V stage land.
+                        if (HD == 512 && j == 0 && g >= 1 && !wait_count(&bars->v_seen, (int)g, abort, err)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        const uint32_t d = tmem + ((g & 1) ? kColS1 : kColS0);
+                        const int pos = pos_base + C::k_pos(j);
+                        for (int st = 0; st < C::kKStages && ok; st++) {
+                            const int slot = slot_of(pos + st);
+                            if (!wait_bar(&bars->ring_full[slot], phase_of(pos + st), abort, err)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+#pragma unroll
+                            for (int b = 0; b < C::kStageBoxes; b++) {
+                                const uint64_t kd = k_desc + (uint64_t)((slot * C::kStageBytes + b * kBoxBytes) >> 4);
+                                const uint64_t qd = q_desc + (uint64_t)((C::kStageBoxes * st + b) * (kQBoxBytes >> 4));
+                                ptx::mma2_ss(d, qd, kd, kIdescS, (st | b) != 0);
+#pragma unroll
+                                for (int kk = 1; kk < 4; kk++) ptx::mma2_ss(d, qd + 2 * kk, kd + 2 * kk, kIdescS, 1);
+                            }
+                            ptx::mma2_commit_pair(&bars->ring_empty[slot], kBothCtas);
+                        }
+                        set_count(&bars->k_seen, (int)g + 1);
+                        if (ok) ptx::mma2_commit_pair(&bars->s_full[g & 1], kBothCtas);
+                    }
+                    // the item's Q is free once its last S MMA completes
+                    if (ok) ptx::mma2_commit_pair(&bars->q_empty, kBothCtas);
+                } else {
+                    // O += P(g) V(g) once the softmax of both CTAs published P(g);
+                    // the item's first PV also waits for the previous item's O to
+                    // be read out by the epilogue warps of both CTAs
+                    constexpr uint32_t kIdescPV = ptx::idesc_f16(0, 0, 1, 2 * kRows, kDV);
+                    for (int j = 0; j < n_tiles && ok; j++, g++) {
+                        if (!wait_bar<true>(&bars->p_full[g & 1], (g >> 1) & 1u, abort, err)) {
+                            ok = false;
+                            break;
+                        }
+                        if (j == 0 && qk > 0 && !wait_bar(&bars->o_free, (qk - 1) & 1u, abort, err)) {
+                            ok = false;
+                            break;
+                        }
+                        // width 512: V(j)'s second slot last held K(j+1)'s first stage
+                        // (see the per-item kernel)
+                        if (HD == 512 && j + 1 < n_tiles && !wait_count(&bars->k_seen, (int)g + 2, abort, err)) {
+                            ok = false;
+                            break;
+                        }
+                        const int pos = pos_base + C::v_pos(j, n_tiles);
+                        for (int c = 0; c < C::kVStages && ok; c++)
+                            ok = wait_bar(&bars->ring_full[slot_of(pos + c)], phase_of(pos + c), abort, err);
+                        if (!ok) break;
+                        set_count(&bars->v_seen, (int)g + 1);
+                        ptx::tc_fence_after();
+                        const uint32_t p_tmem = tmem + ((g & 1) ? kColS1 : kColS0);
+                        const uint64_t vd0 = v_desc + (uint64_t)((slot_of(pos) * C::kStageBytes) >> 4);
+                        const uint64_t vd1 =
+                            v_desc + (uint64_t)((slot_of(pos + 2 / C::kStageBoxes) * C::kStageBytes +
+                                                 (2 % C::kStageBoxes) * kBoxBytes) >> 4);
+                        ptx::mma2_ts(tmem + kColO, p_tmem, vd0, kIdescPV, j > 0);
+#pragma unroll
+                        for (int ks = 1; ks < kKeysPerTile / 16; ks++)
+                            ptx::mma2_ts(tmem + kColO, p_tmem + 8 * ks, (ks < 4 ? vd0 : vd1) + (2048 >> 4) * (ks & 3),
+                                         kIdescPV, 1);
+                        for (int c = 0; c < C::kVStages; c++)
+                            ptx::mma2_commit_pair(&bars->ring_empty[slot_of(pos + c)], kBothCtas);
+                        ptx::mma2_commit_pair(&bars->o_done[g & 1], kBothCtas);
+                    }
+                }
+                qk++;
+                pos_base += n_tiles * (C::kKStages + C::kVStages);
+            }
+            // Every MMA this thread issued completes before either CTA
+            // releases TMEM or exits (mma_done expects one commit per issuer).
+            ptx::mma2_commit_pair(&bars->mma_done, kBothCtas);
+            for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->mma_done, 0); i++) {
+            }
+        } else if (warp == 1 && lane == 0) {
+            // non-leader: wait (bounded) for the leader's final commits
+            for (uint32_t i = 0; i < kWaitLimit && !ptx::mbar_try_wait(&bars->mma_done, 0); i++) {
+                if ((i & 1023) == 1023 && *abort) break;
+            }
+        }
+    } else if (warp < kEpiWarp0) {
+        // ------------------------------------------------------------ softmax (warps 2-9)
+        const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const float kLog2e = 1.4426950408889634f;
+        const uint32_t p_full_l0 = ptx::mapa(&bars->p_full[0], 0), p_full_l1 = ptx::mapa(&bars->p_full[1], 0);
+        Mailbox *my_box = &bars->box[0][half][row];
+        Mailbox *other_box = &bars->box[0][half ^ 1][row];
+        uint32_t e = 0;  // exchanges with the partner thread so far (both halves make the same sequence)
+        // Post (e, v) and read the partner's value for the same exchange.
+        auto swap = [&](float v, float *out) -> bool {
+            const int seq = (int)e;
+            const int par = seq & 1;
+            e++;
+            const uint32_t mine = ptx::smem_u32(my_box + par * 2 * kRows);
+            const uint32_t theirs = ptx::smem_u32(other_box + par * 2 * kRows);
+            const uint64_t word = (uint64_t)(uint32_t)seq | ((uint64_t)__float_as_uint(v) << 32);
+            asm volatile("st.volatile.shared.b64 [%0], %1;" ::"r"(mine), "l"(word) : "memory");
+            for (uint32_t i = 0; i < kWaitLimit; i++) {
+                uint64_t t;
+                asm volatile("ld.volatile.shared.b64 %0, [%1];" : "=l"(t) : "r"(theirs) : "memory");
+                if ((int)(uint32_t)t == seq) {
+                    *out = __uint_as_float((uint32_t)(t >> 32));
+                    return true;
+                }
+                if ((i & 255) == 255 && *abort) return false;
+            }
+            *abort = 1;
+            atomicOr(err, 2);
+            return false;
+        };
+        bool ok = true;
+        uint32_t g = 0, qk = 0;
+        for (int i = i0; i < i1 && ok; i++) {
+            const WorkItem it = items[i];
+            const int n_tiles = it.n_kv_tiles;
+            if (n_tiles == 0) continue;
+            const ProblemDev &pb = problems[it.problem];
+            const int tok0 = it.q_tile * kTokensPerPair + (int)rank * kTokensPerCta;
+            const int qpos = pb.q_pos0 + tok0 + row / 8;
+            const int vis_hi = min(qpos - pb.kv_pos0, pb.n_kv - 1);
+            const int vis_lo = pb.window > 0 ? qpos - pb.window + 1 - pb.kv_pos0 : INT_MIN / 2;
+            const int q_first = pb.q_pos0 + tok0;
+            const int q_last = q_first + kTokensPerCta - 1;
+            float m_used = -CUDART_INF_F;
+            float l = 0.0f;
+            for (int j = 0; j < n_tiles && ok; j++, g++) {
+                if (!__all_sync(0xffffffffu, wait_bar(&bars->s_full[g & 1], (g >> 1) & 1u, abort, err))) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t s_addr = tmem + lane_addr + ((g & 1) ? kColS1 : kColS0);
+                uint32_t r0[32], r1[32];
+                ptx::tmem_ld32(s_addr + 64 * half, r0);
+                ptx::tmem_ld32(s_addr + 64 * half + 32, r1);
+                ptx::tmem_wait_ld();
+                ptx::tmem_ld_fence(r0);
+                ptx::tmem_ld_fence(r1);
+                float s[64];
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    s[c] = __uint_as_float(r0[c]);
+                    s[32 + c] = __uint_as_float(r1[c]);
+                }
+                const int k0 = (it.kv_tile_lo + j) * kKeysPerTile;
+                const int kp0 = pb.kv_pos0 + k0;
+                const bool edge = k0 + kKeysPerTile > pb.n_kv || kp0 + kKeysPerTile - 1 > q_first ||
+                                  (pb.window > 0 && q_last - kp0 >= pb.window);
+                if (edge) {
+                    const int kb = k0 + 64 * half;
+                    const int lo = vis_lo - kb, hi = vis_hi - kb;
+#pragma unroll
+                    for (int c = 0; c < 64; c++) s[c] = (c >= lo && c <= hi) ? s[c] : -CUDART_INF_F;
+                }
+                float mx = s[0];
+#pragma unroll
+                for (int c = 1; c < 64; c++) mx = fmaxf(mx, s[c]);
+                float mo;
+                if (!__all_sync(0xffffffffu, swap(mx, &mo))) {
+                    ok = false;
+                    break;
+                }
+                mx = fmaxf(mx, mo) * kLog2e;
+                // lazy rescale with a 2^15 margin (P <= 2^15 fits fp16)
+                const bool grow = mx > m_used + 15.0f;
+                const bool o_live = grow && m_used != -CUDART_INF_F;
+                const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
+                if (grow) m_used = mx;
+                const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
+                uint32_t pk[32];
+                float rs0 = 0.0f, rs1 = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    const float p0 = ptx::ex2(fmaf(s[2 * c], kLog2e, neg_m));
+                    const float p1 = ptx::ex2(fmaf(s[2 * c + 1], kLog2e, neg_m));
+                    rs0 += p0;
+                    rs1 += p1;
+                    pk[c] = ptx::pack_half2(p0, p1);
+                }
+                l = l * f + (rs0 + rs1);
+                ptx::tmem_st32(s_addr + 32 * half, pk);
+                if (__any_sync(0xffffffffu, o_live)) {
+                    // O holds this item's earlier tiles (j >= 1): wait for PV(g-1)
+                    if (!__all_sync(0xffffffffu, wait_bar(&bars->o_done[(g - 1) & 1], ((g - 1) >> 1) & 1u, abort, err))) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < kDV / 128; c++) {
+                        uint32_t o0[32], o1[32];
+                        const uint32_t o_addr = tmem + lane_addr + kColO + 128 * half + 64 * c;
+                        ptx::tmem_ld32(o_addr, o0);
+                        ptx::tmem_ld32(o_addr + 32, o1);
+                        ptx::tmem_wait_ld();
+                        ptx::tmem_ld_fence(o0);
+                        ptx::tmem_ld_fence(o1);
+#pragma unroll
+                        for (int k = 0; k < 32; k++) {
+                            o0[k] = __float_as_uint(__uint_as_float(o0[k]) * f);
+                            o1[k] = __float_as_uint(__uint_as_float(o1[k]) * f);
+                        }
+                        ptx::tmem_st32(o_addr, o0);
+                        ptx::tmem_st32(o_addr + 32, o1);
+                    }
+                }
+                ptx::tmem_wait_st();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive_cl((g & 1) ? p_full_l1 : p_full_l0);
+            }
+            if (!ok) break;
+            // the item's row sums meet; its stats go to the epilogue warps
+            float lo_ = 0.0f;
+            if (!__all_sync(0xffffffffu, swap(l, &lo_))) {
+                ok = false;
+                break;
+            }
+            l += lo_;
+            if (qk >= 2 && !__all_sync(0xffffffffu, wait_bar(&bars->stats_free[qk & 1], ((qk - 2) >> 1) & 1u, abort, err))) {
+                ok = false;
+                break;
+            }
+            if (half == 0) {
+                bars->stats[qk & 1][row] = make_float2(m_used, l);
+                ptx::mbar_arrive(&bars->stats_full[qk & 1]);
+            }
+            qk++;
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 11-14)
+        // One thread per TMEM lane (row) of this CTA: warp w reaches lanes
+        // 32 * (w % 4).. of the TMEM; the row's 256 output columns are read
+        // 32 at a time, divided by the row sum and stored 128 bytes at a time.
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const uint32_t o_free_l = ptx::mapa(&bars->o_free, 0);
+        bool ok = true;
+        uint32_t g = 0, qk = 0;
+        for (int i = i0; i < i1 && ok; i++) {
+            const WorkItem it = items[i];
+            const int n_tiles = it.n_kv_tiles;
+            const ProblemDev &pb = problems[it.problem];
+            const int tok = it.q_tile * kTokensPerPair + (int)rank * kTokensPerCta + row / 8;
+            const int head = row % 8;
+            const bool row_valid = tok < pb.n_q;
+            float *dst = pb.out + ((size_t)tok * 8 + head) * HD + it.dv_half * kDV;
+            if (n_tiles == 0) {  // no visible key: zeros, lse -inf
+                if (row_valid) {
+                    for (int c = 0; c < kDV / 4; c++) reinterpret_cast<float4 *>(dst)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (pb.lse && it.dv_half == 0) pb.lse[(size_t)tok * 8 + head] = -CUDART_INF_F;
+                }
+                continue;
+            }
+            const uint32_t g_last = g + (uint32_t)n_tiles - 1;
+            g += (uint32_t)n_tiles;
+            if (!__all_sync(0xffffffffu, wait_bar(&bars->stats_full[qk & 1], (qk >> 1) & 1u, abort, err))) {
+                ok = false;
+                break;
+            }
+            const float2 st = bars->stats[qk & 1][row];
+            ptx::mbar_arrive(&bars->stats_free[qk & 1]);
+            if (!__all_sync(0xffffffffu, wait_bar(&bars->o_done[g_last & 1], (g_last >> 1) & 1u, abort, err))) {
+                ok = false;
+                break;
+            }
+            ptx::tc_fence_after();
+            const float inv = st.y > 0.0f ? 1.0f / st.y : 0.0f;
+#pragma unroll 1
+            for (int c = 0; c < kDV / 32; c++) {
+                uint32_t r[32];
+                ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
+                ptx::tmem_wait_ld();
+                ptx::tmem_ld_fence(r);
+                if (row_valid) {
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        reinterpret_cast<float4 *>(dst + 32 * c)[k] =
+                            make_float4(__uint_as_float(r[4 * k]) * inv, __uint_as_float(r[4 * k + 1]) * inv,
+                                        __uint_as_float(r[4 * k + 2]) * inv, __uint_as_float(r[4 * k + 3]) * inv);
+                }
+            }
+            // O of this item is out of TMEM: the next item's first PV may overwrite it
+            ptx::tc_fence_before();
+            ptx::mbar_arrive_cl(o_free_l);
+            if (row_valid && pb.lse && it.dv_half == 0)
+                pb.lse[(size_t)tok * 8 + head] = st.y > 0.0f ? (st.x + log2f(st.y)) * 0.6931471805599453f : -CUDART_INF_F;
+            qk++;
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();  // no MMA or load of the pair still touches either CTA
+    if (warp == 1) {
+        __syncwarp();
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc2(tmem, kTmemCols);
+    }
+}
+
 // bf16 -> fp16 copies of up to kMaxSegs V arrays in one launch (blockIdx.y =
 // segment); 8 elements per thread and step. Every count is a multiple of 8
 // (a head width) and every address 16-byte aligned (checked on the host).
@@ -708,12 +1262,19 @@ struct Prepared {
     std::vector<ConvLaunch> conv;
     size_t n_work[2] = {0, 0};
     bool mixed = false;  // both widths in one launch (the items in one cost order)
+    // persistent launches: per width, n_pairs CTA pairs, pair p running the
+    // items [pair_start[p], pair_start[p + 1]) of that width's list
+    bool persistent = false;
+    int32_t *d_pair_start = nullptr;  // width 256's table, then width 512's
+    int n_pairs[2] = {0, 0};
     uint64_t used = 0;   // call counter at the last use
 };
 
 // Host-side state the prefill keeps in the context between calls.
 struct PrefillScratch {
     bool attr_set = false;
+    int n_sm = 0;          // of the device, read on the first call
+    int persistent = -1;   // 1: persistent CTA pairs, 0: a CTA pair per item (G4A_PREFILL_KERNEL)
     // Tensor maps by (kind, base, columns, rows): the encoder is a driver call
     // per map, and repeated calls (a model's layers, every prompt of a batch)
     // name the same buffers.
@@ -744,6 +1305,7 @@ static void free_prepared(Prepared &p) {
     cudaFree(p.d_problems);
     cudaFree(p.d_items);
     cudaFree(p.v16);
+    cudaFree(p.d_pair_start);
     p = Prepared();
 }
 
@@ -754,7 +1316,20 @@ static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_
         cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
         cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
         cudaFuncSetAttribute(prefill_kernel_mixed, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMixed);
+        cudaFuncSetAttribute(prefill_persistent<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             CfgP<256>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_persistent<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             CfgP<512>::kSmemBytes);
         S->attr_set = true;
+    }
+    if (P.persistent) {
+        if (P.n_pairs[0])
+            prefill_persistent<256><<<2 * (unsigned)P.n_pairs[0], kThreadsP, CfgP<256>::kSmemBytes, st>>>(
+                P.d_problems, P.d_items, P.d_pair_start, d_err, (int)stall);
+        if (P.n_pairs[1])
+            prefill_persistent<512><<<2 * (unsigned)P.n_pairs[1], kThreadsP, CfgP<512>::kSmemBytes, st>>>(
+                P.d_problems, P.d_items + P.n_work[0], P.d_pair_start + P.n_pairs[0] + 1, d_err, (int)stall);
+        return cudaGetLastError();
     }
     // two CTAs (one cluster) per work item
     if (P.mixed) {
@@ -954,7 +1529,56 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         std::stable_sort(w.begin(), w.end(),
                          [](const WorkItem &a, const WorkItem &b) { return a.n_kv_tiles > b.n_kv_tiles; });
     const size_t n_items = work[0].size() + work[1].size();
-    P.mixed = !work[0].empty() && !work[1].empty();
+    if (S->persistent < 0) {
+        const char *mode = getenv("G4A_PREFILL_KERNEL");  // measurement switch: "item" or "persistent"
+        S->persistent = !(mode && std::strcmp(mode, "item") == 0);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&S->n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || S->n_sm < 2)
+            S->n_sm = 148;
+    }
+    P.persistent = S->persistent == 1;
+    P.mixed = !P.persistent && !work[0].empty() && !work[1].empty();
+    std::vector<int32_t> pair_start;
+    if (P.persistent) {
+        // Longest-processing-time assignment per width: an item costs its key
+        // tiles times 2 (width 256) or 3 (a half of width 512, which
+        // recomputes the 512-wide S), plus 2 for its Q load and epilogue;
+        // items go longest first to the least loaded pair, and each pair's
+        // list is stored in assignment order.
+        for (int w = 0; w < 2; w++) {
+            std::vector<WorkItem> &list = work[w];
+            const int n_pairs = (int)std::min<size_t>(list.size(), (size_t)(S->n_sm / 2));
+            P.n_pairs[w] = n_pairs;
+            const int base = (int)pair_start.size();
+            pair_start.resize(base + n_pairs + 1, 0);
+            if (n_pairs == 0) continue;
+            auto cost = [&](const WorkItem &it) { return (int64_t)it.n_kv_tiles * (w ? 3 : 2) + 2; };
+            std::vector<int64_t> load(n_pairs, 0);
+            std::vector<int> owner(list.size());
+            std::vector<int> count(n_pairs, 0);
+            for (size_t k = 0; k < list.size(); k++) {  // list is longest first
+                int best = 0;
+                for (int q = 1; q < n_pairs; q++)
+                    if (load[q] < load[best]) best = q;
+                owner[k] = best;
+                load[best] += cost(list[k]);
+                count[best]++;
+            }
+            for (int q = 0; q < n_pairs; q++) pair_start[base + q + 1] = pair_start[base + q] + count[q];
+            std::vector<int> fill(pair_start.begin() + base, pair_start.begin() + base + n_pairs);
+            std::vector<WorkItem> ordered(list.size());
+            for (size_t k = 0; k < list.size(); k++) ordered[fill[owner[k]]++] = list[k];
+            list.swap(ordered);
+        }
+        if ((e = cudaMalloc(&P.d_pair_start, pair_start.size() * sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMemcpyAsync(P.d_pair_start, pair_start.data(), pair_start.size() * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, st)) != cudaSuccess) {
+            free_prepared(P);
+            *msg = cudaGetErrorString(e);
+            return G4A_CUDA;
+        }
+    }
     if ((e = cudaMalloc(&P.d_problems, hp.size() * sizeof(ProblemDev))) != cudaSuccess ||
         (e = cudaMalloc(&P.d_items, std::max<size_t>(n_items, 1) * sizeof(WorkItem))) != cudaSuccess) {
         free_prepared(P);
