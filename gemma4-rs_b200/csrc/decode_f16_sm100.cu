@@ -50,7 +50,6 @@ constexpr int kStageBytes = 65536;              // K + V of one stage
 constexpr int kQRegion = 16384;
 constexpr int kRegionBytes = 32768;
 constexpr uint32_t kPollLimit = 1u << 22;
-constexpr int kPrefetch = 4;  // stages fetched into L2 ahead of the one being loaded
 
 template <int HD>
 struct F16Cfg {
@@ -297,25 +296,10 @@ __device__ __forceinline__ bool produce_item(const DecodeParams &p, const Decode
         return true;
     };
     const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
-    // The stages kPrefetch ahead of the one being loaded are fetched into L2
-    // meanwhile, so that more of the item's rows are in flight from HBM than
-    // the shared-memory ring holds (a stage never spans two pages).
-    auto prefetch = [&](int r0) {
-        if (r0 >= it.row_hi) return;
-        const int page = __ldg(bt + r0 / p.page_tokens);
-        const int y = page * p.page_tokens + (r0 % p.page_tokens);
-#pragma unroll
-        for (int c = 0; c < C::kBoxes; c++) {
-            ptx::tma_prefetch_l2_2d(tk.tmap_k, 64 * c, y);
-            ptx::tma_prefetch_l2_2d(tk.tmap_v, 64 * c, y);
-        }
-    };
     const int first = it.row_lo / C::S * C::S;
-    for (int k = 1; k <= kPrefetch; k++) prefetch(first + k * C::S);
     int issued = 0;
     for (int r0 = first; r0 < it.row_hi; r0 += C::S, st++, issued++) {
         const int slot = st % kSlots;
-        if (issued > 0) prefetch(r0 + kPrefetch * C::S);
         if (!q_issued && issued == kSlots - 1 && !issue_q()) return false;
         if (!prereq_done && tk.new_row >= r0 && tk.new_row < r0 + C::S) {
             wait_prerequisite();
