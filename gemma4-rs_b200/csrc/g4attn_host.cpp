@@ -1109,12 +1109,74 @@ cudaEvent_t spare_event(g4a_ctx *ctx) {
 
 }  // namespace
 
+namespace {
+
+// The device-side address of page-locked host memory the device can reach
+// (cudaHostAlloc'd or registered memory under unified addressing), or false
+// for pageable memory.
+bool mapped_host(const void *p, void **dev) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (a.type != cudaMemoryTypeHost || !a.devicePointer) return false;
+    *dev = a.devicePointer;
+    return true;
+}
+
+// The end of a host-buffer step: the step's device flags read back with the
+// stream drained, mapped to the reference's errors.
+int finish_host_step(g4a_ctx *ctx) {
+    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->h_flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    const int flag = *ctx->h_flag;
+    if (flag) {
+        G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+        if (flag & 6) return fail(ctx, G4A_TIMEOUT, "compute: a device wait ran out (flag %d)", flag);
+        return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
+    }
+    return G4A_OK;
+}
+
+}  // namespace
+
 extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_layer_host *layers,
                                int32_t n_seqs, const int32_t *seq_ids, const int32_t *positions) {
     if (!ctx || !kv) return G4A_COMPUTE;
     cudaSetDevice(ctx->device);
     if (n_layers < 0 || n_seqs < 0 || (n_layers > 0 && !layers))
         return fail(ctx, G4A_COMPUTE, "compute: invalid decode arguments");
+    if (!ctx->h_flag) G4A_CUDA_TRY(ctx, cudaHostAlloc(reinterpret_cast<void **>(&ctx->h_flag), sizeof(int),
+                                                      cudaHostAllocDefault));
+    // Page-locked buffers the device can address: the step's kernels read
+    // q/k/v and write the outputs in place over the bus (the prep kernel
+    // reads each input once, the main and combine kernels write each output
+    // once), one launch for all layers and no staging copies; the transfers
+    // overlap the attention of other tasks. Other buffers go through the
+    // context's device slots below.
+    {
+        bool mapped = n_layers > 0;
+        std::vector<g4a_decode_layer> zc(n_layers);
+        for (int32_t i = 0; i < n_layers && mapped; i++) {
+            const g4a_decode_layer_host &h = layers[i];
+            void *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+            mapped = (!h.q_raw_host || mapped_host(h.q_raw_host, &q)) &&
+                     (!h.k_raw_host || mapped_host(h.k_raw_host, &k)) &&
+                     (!h.v_raw_host || mapped_host(h.v_raw_host, &v)) && (!h.out_host || mapped_host(h.out_host, &o));
+            zc[i] = g4a_decode_layer{h.layer, static_cast<const float *>(q), static_cast<const float *>(k),
+                                     static_cast<const float *>(v), h.q_norm_w_dev, h.k_norm_w_dev,
+                                     static_cast<float *>(o)};
+        }
+        if (mapped) {
+            Plan &plan = scratch_plan();
+            int rc = build_decode(ctx, kv, n_layers, zc.data(), n_seqs, seq_ids, positions, plan);
+            if (rc) return rc;
+            if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16)))
+                return rc;
+            return finish_host_step(ctx);
+        }
+    }
     // device slots: per layer q [n][8 hd], k and v [n][hd], out [n][8 hd]
     std::vector<size_t> off(n_layers);
     std::vector<int32_t> width(n_layers);
@@ -1126,8 +1188,6 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
     }
     int rc = grow(ctx, &ctx->d_io, &ctx->io_cap, std::max<size_t>(total, 1), false);
     if (rc) return rc;
-    if (!ctx->h_flag) G4A_CUDA_TRY(ctx, cudaHostAlloc(reinterpret_cast<void **>(&ctx->h_flag), sizeof(int),
-                                                      cudaHostAllocDefault));
     if (!ctx->copy_in) G4A_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking));
     if (!ctx->copy_out) G4A_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking));
     // events: [0] call start, then per layer (inputs in, kernels done)
@@ -1205,16 +1265,8 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
         }
     }
     commit_decode(kv, n_layers, dev.data(), n_seqs, seq_ids, info);
-    G4A_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->h_flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->copy_out));
-    G4A_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    const int flag = *ctx->h_flag;
-    if (flag) {
-        G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
-        if (flag & 6) return fail(ctx, G4A_TIMEOUT, "compute: a device wait ran out (flag %d)", flag);
-        return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
-    }
-    return G4A_OK;
+    return finish_host_step(ctx);
 }
 
 struct g4a_plan {

@@ -226,13 +226,17 @@ int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_laye
  * on KV-shared layers) are copied in, the step runs on the context's stream,
  * out_host [n][n_heads*hd] is copied back, and the call returns when it is
  * there, with the device's softmax/timeout flags checked (G4A_NONFINITE,
- * G4A_TIMEOUT). Page-locked host buffers copy asynchronously by DMA;
- * pageable ones are staged by the driver. The norm weights stay device
- * pointers (model weights are resident). A rejected call leaves the cache and
- * the outputs untouched. The layers run one after another, each as soon as
- * its inputs are on the device: a later layer's inputs are copied in while an
+ * G4A_TIMEOUT). When every buffer is page-locked memory the device can
+ * address (cudaHostAlloc'd or registered, under unified addressing), the
+ * step's kernels read the inputs and write the outputs in place over the bus,
+ * all layers in one launch, with no staging copies. Otherwise the buffers go
+ * through device slots of the context, layer by layer, each layer running as
+ * soon as its inputs are in: a later layer's inputs are copied in while an
  * earlier layer's kernels run, and an earlier layer's output is copied out
- * while a later layer's kernels run (two copy streams of the context). */
+ * while a later layer's kernels run (two copy streams of the context;
+ * pageable memory is staged by the driver). The norm weights stay device
+ * pointers (model weights are resident). A rejected call leaves the cache and
+ * the outputs untouched. */
 typedef struct g4a_decode_layer_host {
     int32_t layer;
     const float *q_raw_host;

@@ -63,6 +63,13 @@ cudaError_t cudaStreamDestroy(cudaStream_t s) {
     return cudaSuccess;
 }
 cudaError_t cudaStreamWaitEvent(cudaStream_t, cudaEvent_t, unsigned) { return cudaSuccess; }
+// every host pointer is pageable to the stand-ins (the copy path of g4a_decode_host)
+cudaError_t cudaPointerGetAttributes(cudaPointerAttributes *a, const void *) {
+    *a = cudaPointerAttributes{};
+    a->type = cudaMemoryTypeUnregistered;
+    return cudaSuccess;
+}
+cudaError_t cudaGetLastError() { return cudaSuccess; }
 cudaError_t cudaStreamBeginCapture(cudaStream_t, cudaStreamCaptureMode) { return cudaSuccess; }
 cudaError_t cudaStreamEndCapture(cudaStream_t, cudaGraph_t *g) {
     *g = reinterpret_cast<cudaGraph_t>(std::malloc(8));
