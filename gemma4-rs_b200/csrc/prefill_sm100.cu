@@ -72,6 +72,7 @@ constexpr int kBoxBytes = 64 * 128;   // 64 columns x 64 rows (bf16 / fp16)
 constexpr int kOutBoxBytes = 128 * 128;  // 32 f32 columns x 128 rows
 constexpr int kThreads = 352;
 constexpr int kPvWarp = 10;
+constexpr int kSoftmaxWarps = 8;     // warps 2-9
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS0 = 256, kColS1 = 384;
 constexpr uint32_t kWaitLimit = 1u << 22;  // polls; far above any legitimate wait
@@ -123,7 +124,7 @@ struct Barriers {
     Mailbox box[2][2][128];  // [seq parity][column half][row]
     uint64_t q_full;         // leader: both CTAs' Q bytes
     uint64_t s_full[2];      // both: S buffer ready (pair commit)
-    uint64_t p_full[2];      // leader: 256 arrivals from each CTA
+    uint64_t p_full[2];      // leader: one arrival per softmax warp of each CTA
     uint64_t o_done[2];      // both: PV of the tile in this S buffer done (pair commit): O
                              // updated, P buffer free. A wait by phase parity is exact
                              // only while its barrier is at most one phase behind the
@@ -197,7 +198,7 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
         ptx::mbar_init(&bars->q_full, 1);
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&bars->s_full[i], 1);
-            ptx::mbar_init(&bars->p_full[i], 2 * 256);
+            ptx::mbar_init(&bars->p_full[i], 2 * kSoftmaxWarps);
             ptx::mbar_init(&bars->o_done[i], 1);
         }
         ptx::mbar_init(&bars->mma_done, 2);
@@ -546,7 +547,10 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
             }
             ptx::tmem_wait_st();
             ptx::tc_fence_before();
-            ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);  // the leader's barrier (release, cluster scope)
+            // one arrival per warp on the leader's barrier (release, cluster scope)
+            // once every lane's P is in TMEM
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);
         }
         // ---- epilogue: O / l, staged in shared memory, written by TMA ----
         float lo_ = 0.0f;
@@ -655,7 +659,7 @@ struct PBars {
     uint64_t s_full[2];
     uint64_t p_full[2];
     uint64_t o_done[2];
-    uint64_t o_free;          // leader: 2 x 128 epilogue arrivals: an item's O read out of TMEM
+    uint64_t o_free;          // leader: one arrival per epilogue warp of each CTA: an item's O read out of TMEM
     uint64_t stats_full[2];   // both: 128 softmax arrivals (stats of an item written)
     uint64_t stats_free[2];   // both: 128 epilogue arrivals (stats of an item read)
     uint64_t mma_done;
@@ -668,9 +672,15 @@ struct PBars {
 };
 static_assert(sizeof(PBars) <= 8192, "persistent barrier region");
 
+// Epilogue staging: per epilogue warp 32 rows x 16 f32 columns, the 16-byte
+// chunks of row r at chunk index k ^ ((r >> 1) & 3) (conflict-free writes of
+// one row per lane and reads of 8 rows per instruction)
+constexpr int kEpiWarps = 4;
+constexpr int kEpiStageBytes = kEpiWarps * 32 * 16 * 4;
+
 template <int HD>
 struct CfgP {
-    static constexpr int kSmemBytes = Cfg<HD>::kSmemQ + Cfg<HD>::kSmemRing + 8192 + 1024;
+    static constexpr int kSmemBytes = Cfg<HD>::kSmemQ + Cfg<HD>::kSmemRing + 8192 + kEpiStageBytes + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -697,12 +707,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
         ptx::mbar_init(&bars->q_empty, 1);
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&bars->s_full[i], 1);
-            ptx::mbar_init(&bars->p_full[i], 2 * 256);
+            ptx::mbar_init(&bars->p_full[i], 2 * kSoftmaxWarps);
             ptx::mbar_init(&bars->o_done[i], 1);
             ptx::mbar_init(&bars->stats_full[i], kRows);
             ptx::mbar_init(&bars->stats_free[i], kRows);
         }
-        ptx::mbar_init(&bars->o_free, 2 * kRows);
+        ptx::mbar_init(&bars->o_free, 2 * kEpiWarps);
         ptx::mbar_init(&bars->mma_done, 2);
         for (int i = 0; i < C::kRing; i++) {
             ptx::mbar_init(&bars->ring_full[i], 1);
@@ -1061,7 +1071,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 }
                 ptx::tmem_wait_st();
                 ptx::tc_fence_before();
-                ptx::mbar_arrive_cl((g & 1) ? p_full_l1 : p_full_l0);
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive_cl((g & 1) ? p_full_l1 : p_full_l0);
             }
             if (!ok) break;
             // the item's row sums meet; its stats go to the epilogue warps
@@ -1084,26 +1095,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
     } else {
         // ------------------------------------------------------------ epilogue (warps 11-14)
         // One thread per TMEM lane (row) of this CTA: warp w reaches lanes
-        // 32 * (w % 4).. of the TMEM; the row's 256 output columns are read
-        // 32 at a time, divided by the row sum and stored 128 bytes at a time.
+        // 32 * (w % 4).. of the TMEM. The row's 256 output columns are read 32
+        // at a time and divided by the row sum; each 16-column half goes
+        // through the warp's staging buffer, from which 4 lanes per row store
+        // 64 contiguous bytes (8 rows per instruction). O is free for the next
+        // item once the last columns are in registers.
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const uint32_t o_free_l = ptx::mapa(&bars->o_free, 0);
+        float *stage = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 8192) + (warp - kEpiWarp0) * 32 * 16;
         bool ok = true;
         uint32_t g = 0, qk = 0;
         for (int i = i0; i < i1 && ok; i++) {
             const WorkItem it = items[i];
             const int n_tiles = it.n_kv_tiles;
             const ProblemDev &pb = problems[it.problem];
-            const int tok = it.q_tile * kTokensPerPair + (int)rank * kTokensPerCta + row / 8;
-            const int head = row % 8;
-            const bool row_valid = tok < pb.n_q;
-            float *dst = pb.out + ((size_t)tok * 8 + head) * HD + it.dv_half * kDV;
+            const int tok0 = it.q_tile * kTokensPerPair + (int)rank * kTokensPerCta;  // this CTA's first token
+            // rows [tok0 * 8, tok0 * 8 + 128) of the [n_q * 8][HD] output; this warp's rows quad * 32 ..
+            float *out_rows = pb.out + (size_t)tok0 * 8 * HD + it.dv_half * kDV;
+            const int valid_rows = min(kRows, (pb.n_q - tok0) * 8);  // rows of tokens below n_q
             if (n_tiles == 0) {  // no visible key: zeros, lse -inf
-                if (row_valid) {
+                if (row < valid_rows) {
+                    float *dst = out_rows + (size_t)row * HD;
                     for (int c = 0; c < kDV / 4; c++) reinterpret_cast<float4 *>(dst)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (pb.lse && it.dv_half == 0) pb.lse[(size_t)tok * 8 + head] = -CUDART_INF_F;
+                    if (pb.lse && it.dv_half == 0) pb.lse[(size_t)tok0 * 8 + row] = -CUDART_INF_F;
                 }
                 continue;
             }
@@ -1127,19 +1143,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
                 ptx::tmem_wait_ld();
                 ptx::tmem_ld_fence(r);
-                if (row_valid) {
+                if (c == kDV / 32 - 1) {
+                    // every column of O is in registers: the next item's first PV may overwrite it
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive_cl(o_free_l);
+                }
 #pragma unroll
-                    for (int k = 0; k < 8; k++)
-                        reinterpret_cast<float4 *>(dst + 32 * c)[k] =
-                            make_float4(__uint_as_float(r[4 * k]) * inv, __uint_as_float(r[4 * k + 1]) * inv,
-                                        __uint_as_float(r[4 * k + 2]) * inv, __uint_as_float(r[4 * k + 3]) * inv);
+                for (int h = 0; h < 2; h++) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int ck = k ^ ((lane >> 1) & 3);
+                        reinterpret_cast<float4 *>(stage + lane * 16)[ck] =
+                            make_float4(__uint_as_float(r[16 * h + 4 * k]) * inv, __uint_as_float(r[16 * h + 4 * k + 1]) * inv,
+                                        __uint_as_float(r[16 * h + 4 * k + 2]) * inv,
+                                        __uint_as_float(r[16 * h + 4 * k + 3]) * inv);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int rr = 8 * q + (lane >> 2), k = lane & 3;
+                        const float4 v = reinterpret_cast<const float4 *>(stage + rr * 16)[k ^ ((rr >> 1) & 3)];
+                        const int orow = quad * 32 + rr;
+                        if (orow < valid_rows)
+                            reinterpret_cast<float4 *>(out_rows + (size_t)orow * HD + 32 * c + 16 * h)[k] = v;
+                    }
+                    __syncwarp();
                 }
             }
-            // O of this item is out of TMEM: the next item's first PV may overwrite it
-            ptx::tc_fence_before();
-            ptx::mbar_arrive_cl(o_free_l);
-            if (row_valid && pb.lse && it.dv_half == 0)
-                pb.lse[(size_t)tok * 8 + head] = st.y > 0.0f ? (st.x + log2f(st.y)) * 0.6931471805599453f : -CUDART_INF_F;
+            if (row < valid_rows && pb.lse && it.dv_half == 0)
+                pb.lse[(size_t)tok0 * 8 + row] = st.y > 0.0f ? (st.x + log2f(st.y)) * 0.6931471805599453f : -CUDART_INF_F;
             qk++;
         }
     }
