@@ -480,9 +480,15 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
 #pragma unroll
                 for (int i = 0; i < 64; i++) s[i] = (i >= lo && i <= hi) ? s[i] : -CUDART_INF_F;
             }
-            float mx = s[0];
+            // row max as a tree (depth 6, not a chain of 63)
+            float mt[32];
 #pragma unroll
-            for (int i = 1; i < 64; i++) mx = fmaxf(mx, s[i]);
+            for (int c = 0; c < 32; c++) mt[c] = fmaxf(s[c], s[c + 32]);
+#pragma unroll
+            for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+                for (int c = 0; c < w; c++) mt[c] = fmaxf(mt[c], mt[c + w]);
+            float mx = mt[0];
             float mo;
             if (!__all_sync(0xffffffffu, swap(j, mx, &mo))) {
                 ok = false;
@@ -502,16 +508,19 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
             // with no visible key so far keeps m = -inf; subtract 0 then.
             const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
             uint32_t pk[32];
-            float rs0 = 0.0f, rs1 = 0.0f;
+            // row sum in 8 partial sums, then a tree
+            float rs[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) rs[k] = 0.0f;
 #pragma unroll
             for (int i = 0; i < 32; i++) {
                 const float p0 = ptx::ex2(fmaf(s[2 * i], kLog2e, neg_m));
                 const float p1 = ptx::ex2(fmaf(s[2 * i + 1], kLog2e, neg_m));
-                rs0 += p0;
-                rs1 += p1;
+                rs[(2 * i) & 7] += p0;
+                rs[(2 * i + 1) & 7] += p1;
                 pk[i] = ptx::pack_half2(p0, p1);
             }
-            l = l * f + (rs0 + rs1);
+            l = l * f + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
             // P (fp16 pairs) goes over the first 64 columns of this S buffer;
             // half 1's columns 32-63 were read by half 0 before it posted its
             // max, which half 1 has seen.
@@ -1017,9 +1026,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
 #pragma unroll
                     for (int c = 0; c < 64; c++) s[c] = (c >= lo && c <= hi) ? s[c] : -CUDART_INF_F;
                 }
-                float mx = s[0];
+                // row max as a tree (depth 6, not a chain of 63)
+                float mt[32];
 #pragma unroll
-                for (int c = 1; c < 64; c++) mx = fmaxf(mx, s[c]);
+                for (int c = 0; c < 32; c++) mt[c] = fmaxf(s[c], s[c + 32]);
+#pragma unroll
+                for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+                    for (int c = 0; c < w; c++) mt[c] = fmaxf(mt[c], mt[c + w]);
+                float mx = mt[0];
                 float mo;
                 if (!__all_sync(0xffffffffu, swap(mx, &mo))) {
                     ok = false;
@@ -1033,16 +1048,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 if (grow) m_used = mx;
                 const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
                 uint32_t pk[32];
-                float rs0 = 0.0f, rs1 = 0.0f;
+                // row sum in 8 partial sums, then a tree
+                float rs[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) rs[k] = 0.0f;
 #pragma unroll
                 for (int c = 0; c < 32; c++) {
                     const float p0 = ptx::ex2(fmaf(s[2 * c], kLog2e, neg_m));
                     const float p1 = ptx::ex2(fmaf(s[2 * c + 1], kLog2e, neg_m));
-                    rs0 += p0;
-                    rs1 += p1;
+                    rs[(2 * c) & 7] += p0;
+                    rs[(2 * c + 1) & 7] += p1;
                     pk[c] = ptx::pack_half2(p0, p1);
                 }
-                l = l * f + (rs0 + rs1);
+                l = l * f + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
                 ptx::tmem_st32(s_addr + 32 * half, pk);
                 if (__any_sync(0xffffffffu, o_live)) {
                     // O holds this item's earlier tiles (j >= 1): wait for PV(g-1)
