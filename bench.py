@@ -459,7 +459,8 @@ def measure_decode(torch, g4a, ctx, stream, ctx_lens, steps, warmup, dist, devic
     wall = (time.perf_counter() - t0) / prof_steps
     phases = {name: ctx.profile_read(kid) for name, kid in
               (("copy_in", g4a.K_COPY_IN), ("prep", g4a.K_DECODE_PREP), ("main", g4a.K_DECODE_MAIN),
-               ("combine", g4a.K_DECODE_COMBINE), ("copy_out", g4a.K_COPY_OUT))}
+               ("combine", g4a.K_DECODE_COMBINE), ("copy_out", g4a.K_COPY_OUT),
+               ("host_issue", g4a.K_HOST_ISSUE), ("host_wait", g4a.K_HOST_WAIT))}
     ctx.profile(False)
     e2e_phases = {k: round(ms / prof_steps * 1e3, 1) for k, (ms, n) in phases.items()}
     e2e_phases["wall_per_call_profiled"] = round(wall * 1e6, 1)

@@ -29,7 +29,7 @@ OK, CONTEXT_TOO_LONG, MISSING_LAYER, MISSING_WEIGHT, COMPUTE, NONFINITE, BAD_LAY
     OUT_OF_PAGES = range(11)
 KV_F32, KV_F16 = 0, 1
 K_DECODE_PREP, K_DECODE_MAIN, K_DECODE_COMBINE, K_DECODE_SPLITKV, K_PREFILL, K_MATVEC_Q8, K_CP_EXCHANGE, \
-    K_CP_ATTEND_LOCAL, K_CP_ATTEND_REMOTE, K_CP_MERGE, K_COPY_IN, K_COPY_OUT = range(12)
+    K_CP_ATTEND_LOCAL, K_CP_ATTEND_REMOTE, K_CP_MERGE, K_COPY_IN, K_COPY_OUT, K_HOST_ISSUE, K_HOST_WAIT = range(14)
 CP_KV_SHARDS, CP_GATHER_KV = 0, 1
 
 _i32p = ctypes.POINTER(ctypes.c_int32)

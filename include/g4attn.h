@@ -118,7 +118,9 @@ typedef enum g4a_kernel {
     G4A_K_CP_MERGE = 9,        /* g4a_cp_prefill: log-sum-exp merges, weights, packing */
     G4A_K_COPY_IN = 10,        /* g4a_decode_host: host-to-device copies of the inputs */
     G4A_K_COPY_OUT = 11,       /* g4a_decode_host: device-to-host copies of the outputs */
-    G4A_K_COUNT = 12
+    G4A_K_HOST_ISSUE = 12,     /* g4a_decode_host: host time from entry until everything is queued */
+    G4A_K_HOST_WAIT = 13,      /* g4a_decode_host: host time blocked in the final synchronisation */
+    G4A_K_COUNT = 14
 } g4a_kernel;
 int g4a_profile_enable(g4a_ctx *ctx, int enable);
 int g4a_profile_read(g4a_ctx *ctx, int32_t kernel, double *total_ms, int64_t *launches);
@@ -226,10 +228,11 @@ int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_laye
  * on KV-shared layers) are copied in, the step runs on the context's stream,
  * out_host [n][n_heads*hd] is copied back, and the call returns when it is
  * there, with the device's softmax/timeout flags checked (G4A_NONFINITE,
- * G4A_TIMEOUT). When every buffer is page-locked memory the device can
- * address (cudaHostAlloc'd or registered, under unified addressing), the
- * step's kernels read the inputs and write the outputs in place over the bus,
- * all layers in one launch, with no staging copies. Otherwise the buffers go
+ * G4A_TIMEOUT). For a small step (up to 256 KB of q/k/v/out, e.g. one
+ * sequence) whose buffers are all page-locked memory the device can address
+ * (cudaHostAlloc'd or registered, under unified addressing), the step's
+ * kernels read the inputs and write the outputs in place over the bus, all
+ * layers in one launch, with no staging copies. Otherwise the buffers go
  * through device slots of the context, layer by layer, each layer running as
  * soon as its inputs are in: a later layer's inputs are copied in while an
  * earlier layer's kernels run, and an earlier layer's output is copied out

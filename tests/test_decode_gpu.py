@@ -480,3 +480,49 @@ def test_decode_both_widths_long_contexts(g4a, oracle, ctx, torch_cuda):
                                               w[layer][1], ff, kv_store=1)
                 assert max_abs_diff(got[s], ref) <= TOL, (step, layer, lengths[s])
     kv.close()
+
+
+def test_decode_host_in_place_small_step(g4a, oracle, ctx, torch_cuda):
+    """A small host-buffer step (one sequence, both layers: 55 KB) with every
+    buffer page-locked runs in place (the kernels read q/k/v and write the
+    output over the bus): bit for bit g4a_decode's on a twin cache, and the
+    oracle's within the decode bar; a second step in a row as well."""
+    torch = torch_cuda
+    hp = oracle.hparams_e2b()
+    ff = oracle.proportional_rope_freq_factors(512, 0.25)
+    r = rng(555)
+    L = 300
+    caches = []
+    for _ in range(2):
+        rr = rng(556)
+        kv = g4a.KvCache(ctx, 1, 512, dtype=1, layers=[13, 14])
+        okv = oracle.KvCache()
+        w = {l: (norm_weight(rr, oracle.head_dim(hp, l)), norm_weight(rr, oracle.head_dim(hp, l))) for l in (13, 14)}
+        for layer in (13, 14):
+            _fill_history(g4a, oracle, torch, kv, okv, hp, 0, layer, L, rr, w[layer][1], ff)
+        caches.append((kv, okv))
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    for step in range(2):
+        dev_args, host_args, raws = [], [], {}
+        for layer in (13, 14):
+            hd = oracle.head_dim(hp, layer)
+            q_raw, k_raw, v_raw = normal(r, 1, 8 * hd), normal(r, 1, hd), normal(r, 1, hd)
+            raws[layer] = (q_raw, k_raw, v_raw)
+            wq, wk = dev(torch, w[layer][0]), dev(torch, w[layer][1])
+            dev_args.append(dict(layer=layer, q_raw=dev(torch, q_raw), k_raw=dev(torch, k_raw),
+                                 v_raw=dev(torch, v_raw), q_norm_w=wq, k_norm_w=wk,
+                                 out=torch.empty(1, 8 * hd, device="cuda")))
+            host_args.append(dict(layer=layer, q_raw=pin(q_raw), k_raw=pin(k_raw), v_raw=pin(v_raw), q_norm_w=wq,
+                                  k_norm_w=wk, out=torch.full((1, 8 * hd), float("nan")).pin_memory()))
+        ctx.decode(caches[0][0], dev_args, [0], [L + step])
+        ctx.sync()
+        ctx.decode_host(caches[1][0], host_args, [0], [L + step])
+        for a, h in zip(dev_args, host_args):
+            layer = a["layer"]
+            got = h["out"].numpy()
+            assert np.array_equal(got, host(a["out"])), (step, layer)
+            ref = caches[1][1].attention_block(hp, layer, L + step, *raws[layer], w[layer][0], w[layer][1], ff,
+                                               kv_store=1)
+            assert max_abs_diff(got[0], ref) <= TOL, (step, layer)
+    for kv_, _ in caches:
+        kv_.close()
