@@ -161,6 +161,23 @@ __device__ __forceinline__ void stall_item(int *err) {
         atomicOr(err, 2);
 }
 
+// 2^x on the FMA pipe, for part of the softmax's exponentials (the MUFU pipe
+// takes 16 per clock per SM, the FMA pipe 128 operations): x = n + f with n
+// rounded to the nearest integer by the 1.5 * 2^23 addition trick and f in
+// [-0.5, 0.5]; 2^f by a cubic whose coefficients were fitted for this kernel
+// (minimax of the relative error, 7.5e-5, below the fp16 rounding of P);
+// 2^n added to the exponent bits. Below -125 the result is 0, as the
+// hardware's flushed ex2 gives for masked (-inf) scores.
+__device__ __forceinline__ float ex2_fma(float x) {
+    const float xc = fmaxf(x, -125.0f);
+    const float t = xc + 12582912.0f;
+    const int n = __float_as_int(t) - 0x4B400000;
+    const float f = xc - (t - 12582912.0f);
+    const float p = fmaf(fmaf(fmaf(0.05517149f, f, 0.24261093f), f, 0.69326097f), f, 0.99992806f);
+    const float r = __int_as_float(__float_as_int(p) + (n << 23));
+    return x < -125.0f ? 0.0f : r;
+}
+
 // Bounded wait until a progress counter of another issuing thread of this
 // CTA reaches `target` (false on abort or time-out, as wait_bar).
 __device__ __forceinline__ bool wait_count(const int *counter, int target, volatile int *abort, int *err) {
@@ -514,8 +531,10 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
             for (int k = 0; k < 8; k++) rs[k] = 0.0f;
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-                const float p0 = ptx::ex2(fmaf(s[2 * i], kLog2e, neg_m));
-                const float p1 = ptx::ex2(fmaf(s[2 * i + 1], kLog2e, neg_m));
+                // half of the exponentials on the MUFU pipe, half on the FMA pipe
+                const float x0 = fmaf(s[2 * i], kLog2e, neg_m), x1 = fmaf(s[2 * i + 1], kLog2e, neg_m);
+                const float p0 = (i & 1) ? ex2_fma(x0) : ptx::ex2(x0);
+                const float p1 = (i & 1) ? ex2_fma(x1) : ptx::ex2(x1);
                 rs[(2 * i) & 7] += p0;
                 rs[(2 * i + 1) & 7] += p1;
                 pk[i] = ptx::pack_half2(p0, p1);
@@ -559,7 +578,10 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
             // one arrival per warp on the leader's barrier (release, cluster scope)
             // once every lane's P is in TMEM
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);
+            if (lane == 0) {  // the leader's own warps arrive locally (CTA-scope release)
+                if (rank == 0) ptx::mbar_arrive(&bars->p_full[j & 1]);
+                else ptx::mbar_arrive_cl((j & 1) ? p_full_l1 : p_full_l0);
+            }
         }
         // ---- epilogue: O / l, staged in shared memory, written by TMA ----
         float lo_ = 0.0f;
@@ -1054,8 +1076,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 for (int k = 0; k < 8; k++) rs[k] = 0.0f;
 #pragma unroll
                 for (int c = 0; c < 32; c++) {
-                    const float p0 = ptx::ex2(fmaf(s[2 * c], kLog2e, neg_m));
-                    const float p1 = ptx::ex2(fmaf(s[2 * c + 1], kLog2e, neg_m));
+                    // half of the exponentials on the MUFU pipe, half on the FMA pipe
+                    const float x0 = fmaf(s[2 * c], kLog2e, neg_m), x1 = fmaf(s[2 * c + 1], kLog2e, neg_m);
+                    const float p0 = (c & 1) ? ex2_fma(x0) : ptx::ex2(x0);
+                    const float p1 = (c & 1) ? ex2_fma(x1) : ptx::ex2(x1);
                     rs[(2 * c) & 7] += p0;
                     rs[(2 * c + 1) & 7] += p1;
                     pk[c] = ptx::pack_half2(p0, p1);
@@ -1090,7 +1114,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 ptx::tmem_wait_st();
                 ptx::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) ptx::mbar_arrive_cl((g & 1) ? p_full_l1 : p_full_l0);
+                if (lane == 0) {  // the leader's own warps arrive locally (CTA-scope release)
+                    if (rank == 0) ptx::mbar_arrive(&bars->p_full[g & 1]);
+                    else ptx::mbar_arrive_cl((g & 1) ? p_full_l1 : p_full_l0);
+                }
             }
             if (!ok) break;
             // the item's row sums meet; its stats go to the epilogue warps
@@ -1165,7 +1192,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                     // every column of O is in registers: the next item's first PV may overwrite it
                     ptx::tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive_cl(o_free_l);
+                    if (lane == 0) {
+                        if (rank == 0) ptx::mbar_arrive(&bars->o_free);
+                        else ptx::mbar_arrive_cl(o_free_l);
+                    }
                 }
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
