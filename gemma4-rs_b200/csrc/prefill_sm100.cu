@@ -81,6 +81,7 @@ constexpr uint16_t kBothCtas = 0x3;
 struct alignas(64) ProblemDev {
     CUtensorMap tq, tk, tv;  // Q [n_q*8, hd] bf16 (128-row boxes), K [n_kv, hd] bf16, V [n_kv, hd] fp16 (64-row boxes)
     CUtensorMap to;          // out [n_q*8, hd] f32, 32-column x 128-row boxes, 128-byte swizzle
+    CUtensorMap tk32;        // K with 32-row boxes (the persistent kernel's 64-key tiles at width 512)
     int32_t hd, window, n_q, q_pos0, n_kv, kv_pos0;
     float *out;
     float *lse;
@@ -176,6 +177,43 @@ __device__ __forceinline__ float ex2_fma(float x) {
     const float p = fmaf(fmaf(fmaf(0.05517149f, f, 0.24261093f), f, 0.69326097f), f, 0.99992806f);
     const float r = __int_as_float(__float_as_int(p) + (n << 23));
     return x < -125.0f ? 0.0f : r;
+}
+
+// ex2_fma on a pair, with packed fp32 arithmetic: the same operations in the
+// same order (each lane rounds as the scalar form), except that x below -125
+// is clamped there, giving 2^-125 * p(f) instead of 0. That value rounds to 0
+// in fp16 P, and its share of a row sum (which is at least 1 once a key is
+// visible) is below 1e-36; a row that sees no key keeps its -inf maximum, so
+// its output stays 0 and its lse -inf.
+__device__ __forceinline__ float2 ex2_fma2(float2 x) {
+    const float2 xc = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    const float2 t = ptx::add2(xc, magic);
+    const float2 f = ptx::sub2(xc, ptx::sub2(t, magic));
+    float2 p = ptx::fma2(make_float2(0.05517149f, 0.05517149f), f, make_float2(0.24261093f, 0.24261093f));
+    p = ptx::fma2(p, f, make_float2(0.69326097f, 0.69326097f));
+    p = ptx::fma2(p, f, make_float2(0.99992806f, 0.99992806f));
+    // t's low mantissa bits hold n + 2^22 and 0x4B400000 << 23 wraps to 0, so
+    // (t bits << 23) adds n to p's exponent
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+// Maximum of N values by three-input max instructions (depth log3 N).
+template <int N> __device__ __forceinline__ float max_tree(const float (&v)[N]) {
+    if constexpr (N == 1) {
+        return v[0];
+    } else if constexpr (N == 2) {
+        return fmaxf(v[0], v[1]);
+    } else {
+        constexpr int M = N / 3, R = N - 3 * M;
+        float t[M + R];
+#pragma unroll
+        for (int c = 0; c < M; c++) t[c] = ptx::max3(v[3 * c], v[3 * c + 1], v[3 * c + 2]);
+#pragma unroll
+        for (int c = 0; c < R; c++) t[M + c] = v[3 * M + c];
+        return max_tree<M + R>(t);
+    }
 }
 
 // Bounded wait until a progress counter of another issuing thread of this
@@ -709,18 +747,47 @@ static_assert(sizeof(PBars) <= 8192, "persistent barrier region");
 constexpr int kEpiWarps = 4;
 constexpr int kEpiStageBytes = kEpiWarps * 32 * 16 * 4;
 
-template <int HD>
+// Persistent-kernel tiling: KEYS keys per tile (the N of S). Width 256 takes
+// 128-key tiles (its ring holds two tiles). Width 512 takes 64 or 128: with 64
+// each CTA stages 32 KB of K (32 keys x 512 columns, boxes of 32 rows) and
+// 16 KB of V (64 keys x its 128 output columns) per tile, so that the 5-slot
+// ring holds K(j+1), V(j) and K(j+2) together; with 128 a tile's 96 KB exceed
+// the 80 KB ring, but each tile carries twice the tensor work per softmax
+// round trip.
+template <int HD, int KEYS>
 struct CfgP {
-    static constexpr int kSmemBytes = Cfg<HD>::kSmemQ + Cfg<HD>::kSmemRing + 8192 + kEpiStageBytes + 1024;
+    static constexpr int kKeys = KEYS;                  // N of S for the pair
+    static constexpr int kKeysCta = kKeys / 2;         // K rows each CTA loads
+    static constexpr int kKBoxBytes = kKeysCta * 128;  // one 64-column box of those rows
+    static constexpr int kQBoxes = Cfg<HD>::kQBoxes;
+    static constexpr int kRing = Cfg<HD>::kRing;
+    static constexpr int kStageBytes = Cfg<HD>::kStageBytes;
+    static constexpr int kKBoxesPerStage = kStageBytes / kKBoxBytes;
+    static constexpr int kKStages = HD / 64 / kKBoxesPerStage;
+    static constexpr int kVBoxesPerStage = kStageBytes / kBoxBytes;       // V boxes: 64 keys x 64 columns
+    static constexpr int kVStages = 2 * (kKeys / 64) / kVBoxesPerStage;   // 2 column atoms per 64 keys
+    static constexpr int kScores = kKeys / 2;                             // scores per softmax thread
+    static constexpr int kSmemQ = Cfg<HD>::kSmemQ;
+    static constexpr int kSmemRing = kRing * kStageBytes;
+    static constexpr int kSmemBytes = kSmemQ + kSmemRing + 8192 + kEpiStageBytes + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kKStages * kKBoxesPerStage * 64 == HD && kVStages >= 1, "stage layout");
+    // A tile's stages exceed the ring (width 512, 128 keys): a slot is refilled
+    // before every consumer has waited on its previous fill, and two progress
+    // counters keep each parity wait exact.
+    static constexpr bool kSeen = kKStages + kVStages > kRing;
+    __device__ static int k_pos(int j) { return j == 0 ? 0 : kKStages + (j - 1) * (kKStages + kVStages); }
+    __device__ static int v_pos(int j, int n) {
+        return kKStages + j * (kKStages + kVStages) + (j + 1 < n ? kKStages : 0);
+    }
 };
 
-template <int HD>
+template <int HD, int KEYS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
     prefill_persistent(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items,
                        const int32_t *__restrict__ pair_start, int *err, int stall) {
     if (stall) return stall_item(err);
-    using C = Cfg<HD>;
+    using C = CfgP<HD, KEYS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *q_smem = smem;
@@ -783,7 +850,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 if (n_tiles == 0) continue;
                 const ProblemDev &pb = problems[it.problem];
                 ptx::prefetch_tmap(&pb.tq);
-                ptx::prefetch_tmap(&pb.tk);
+                ptx::prefetch_tmap(C::kKeysCta == 32 ? &pb.tk32 : &pb.tk);
                 ptx::prefetch_tmap(&pb.tv);
                 // Q of this item once the previous item's last S MMA has read the old Q
                 if (qk > 0 && !wait_bar(&bars->q_empty, (qk - 1) & 1u, abort, err)) {
@@ -795,8 +862,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 for (int c = 0; c < C::kQBoxes; c++)
                     ptx::tma_load_2d_pair(q_smem + c * kQBoxBytes, &pb.tq, q_full_l, 64 * c,
                                           it.q_tile * 2 * kRows + (int)rank * kRows);
+                // the next item's Q into L2 meanwhile (its load waits for this
+                // item's last S, then reads L2 instead of HBM)
+                for (int n = i + 1; n < i1; n++) {
+                    const WorkItem nx = items[n];
+                    if (nx.n_kv_tiles == 0) continue;
+                    const CUtensorMap *ntq = &problems[nx.problem].tq;
+                    for (int c = 0; c < C::kQBoxes; c++)
+                        ptx::tma_prefetch_l2_2d(ntq, 64 * c, nx.q_tile * 2 * kRows + (int)rank * kRows);
+                    break;
+                }
                 qk++;
-                auto push = [&](const CUtensorMap *m, const int *xs, const int *ys) {
+                // one stage of n boxes of box_bytes each, box b at (xs[b], ys[b])
+                auto push = [&](const CUtensorMap *m, const int *xs, const int *ys, int n, int box_bytes) {
                     if (!ok) return;
                     if (!wait_bar(&bars->ring_empty[slot], phase ^ 1u, abort, err)) {
                         ok = false;
@@ -804,36 +882,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                     }
                     if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->ring_full[slot], 2 * C::kStageBytes);
                     const uint32_t bar_l = ptx::mapa(&bars->ring_full[slot], 0);
-                    for (int b = 0; b < C::kStageBoxes; b++)
-                        ptx::tma_load_2d_pair(ring + slot * C::kStageBytes + b * kBoxBytes, m, bar_l, xs[b], ys[b]);
+                    for (int b = 0; b < n; b++)
+                        ptx::tma_load_2d_pair(ring + slot * C::kStageBytes + b * box_bytes, m, bar_l, xs[b], ys[b]);
                     issued |= 1u << slot;
                     if (++slot == C::kRing) {
                         slot = 0;
                         phase ^= 1u;
                     }
                 };
+                // K: this CTA's kKeysCta keys of the tile, all HD columns (width 512:
+                // the map with 32-row boxes)
+                const CUtensorMap *tk = C::kKeysCta == 32 ? &pb.tk32 : &pb.tk;
                 auto push_k = [&](int j) {
-                    const int y = (it.kv_tile_lo + j) * kKeysPerTile + 64 * (int)rank;
+                    const int y = (it.kv_tile_lo + j) * C::kKeys + C::kKeysCta * (int)rank;
                     for (int st = 0; st < C::kKStages; st++) {
-                        int xs[C::kStageBoxes], ys[C::kStageBoxes];
-                        for (int b = 0; b < C::kStageBoxes; b++) {
-                            xs[b] = 64 * (st * C::kStageBoxes + b);
+                        int xs[C::kKBoxesPerStage], ys[C::kKBoxesPerStage];
+                        for (int b = 0; b < C::kKBoxesPerStage; b++) {
+                            xs[b] = 64 * (st * C::kKBoxesPerStage + b);
                             ys[b] = y;
                         }
-                        push(&pb.tk, xs, ys);
+                        push(tk, xs, ys, C::kKBoxesPerStage, C::kKBoxBytes);
                     }
                 };
+                // V: this CTA's 128 output columns (two 64-column atoms) of the
+                // tile's 64-key halves; box q = 2 * key half + atom
                 auto push_v = [&](int j) {
                     const int x = it.dv_half * kDV + 128 * (int)rank;
-                    const int y = (it.kv_tile_lo + j) * kKeysPerTile;
+                    const int y = (it.kv_tile_lo + j) * C::kKeys;
                     for (int st = 0; st < C::kVStages; st++) {
-                        int xs[C::kStageBoxes], ys[C::kStageBoxes];
-                        for (int b = 0; b < C::kStageBoxes; b++) {
-                            const int q = st * C::kStageBoxes + b;
+                        int xs[C::kVBoxesPerStage], ys[C::kVBoxesPerStage];
+                        for (int b = 0; b < C::kVBoxesPerStage; b++) {
+                            const int q = st * C::kVBoxesPerStage + b;
                             xs[b] = x + 64 * (q & 1);
                             ys[b] = y + 64 * (q >> 1);
                         }
-                        push(&pb.tv, xs, ys);
+                        push(&pb.tv, xs, ys, C::kVBoxesPerStage, kBoxBytes);
                     }
                 };
                 push_k(0);
@@ -874,7 +957,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 if (n_tiles == 0) continue;
                 if (warp == 1) {
                     // S(g) = Q K^T into S buffer g&1, once PV(g-2) has read P(g-2) from it
-                    constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, 2 * kRows, kKeysPerTile);
+                    constexpr uint32_t kIdescS = ptx::idesc_f16(1, 1, 0, 2 * kRows, C::kKeys);
                     if (!wait_bar(&bars->q_full, qk & 1u, abort, err)) {
                         ok = false;
                         break;
@@ -884,10 +967,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                             ok = false;
                             break;
                         }
-                        // Width 512: K(0)'s last stage takes the slot of the previous
-                        // item's last V stage; its parity wait is exact once the PV
-                        // issuer has seen that V stage land.
-                        if (HD == 512 && j == 0 && g >= 1 && !wait_count(&bars->v_seen, (int)g, abort, err)) {
+                        // K(0)'s last stage takes the slot of the previous item's last
+                        // V stage; its parity wait is exact once the PV issuer has
+                        // seen that V stage land
+                        if (C::kSeen && j == 0 && g >= 1 && !wait_count(&bars->v_seen, (int)g, abort, err)) {
                             ok = false;
                             break;
                         }
@@ -902,16 +985,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                             }
                             ptx::tc_fence_after();
 #pragma unroll
-                            for (int b = 0; b < C::kStageBoxes; b++) {
-                                const uint64_t kd = k_desc + (uint64_t)((slot * C::kStageBytes + b * kBoxBytes) >> 4);
-                                const uint64_t qd = q_desc + (uint64_t)((C::kStageBoxes * st + b) * (kQBoxBytes >> 4));
+                            for (int b = 0; b < C::kKBoxesPerStage; b++) {
+                                const uint64_t kd =
+                                    k_desc + (uint64_t)((slot * C::kStageBytes + b * C::kKBoxBytes) >> 4);
+                                const uint64_t qd =
+                                    q_desc + (uint64_t)((C::kKBoxesPerStage * st + b) * (kQBoxBytes >> 4));
                                 ptx::mma2_ss(d, qd, kd, kIdescS, (st | b) != 0);
 #pragma unroll
                                 for (int kk = 1; kk < 4; kk++) ptx::mma2_ss(d, qd + 2 * kk, kd + 2 * kk, kIdescS, 1);
                             }
                             ptx::mma2_commit_pair(&bars->ring_empty[slot], kBothCtas);
                         }
-                        set_count(&bars->k_seen, (int)g + 1);
+                        if (C::kSeen) set_count(&bars->k_seen, (int)g + 1);
                         if (ok) ptx::mma2_commit_pair(&bars->s_full[g & 1], kBothCtas);
                     }
                     // the item's Q is free once its last S MMA completes
@@ -930,9 +1015,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                             ok = false;
                             break;
                         }
-                        // width 512: V(j)'s second slot last held K(j+1)'s first stage
-                        // (see the per-item kernel)
-                        if (HD == 512 && j + 1 < n_tiles && !wait_count(&bars->k_seen, (int)g + 2, abort, err)) {
+                        // V(j)'s second slot last held K(j+1)'s first stage when a tile
+                        // exceeds the ring; otherwise every slot's previous fill has
+                        // landed before its next parity wait (both checked by a
+                        // randomized model of the protocol)
+                        if (C::kSeen && j + 1 < n_tiles && !wait_count(&bars->k_seen, (int)g + 2, abort, err)) {
                             ok = false;
                             break;
                         }
@@ -940,18 +1027,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                         for (int c = 0; c < C::kVStages && ok; c++)
                             ok = wait_bar(&bars->ring_full[slot_of(pos + c)], phase_of(pos + c), abort, err);
                         if (!ok) break;
-                        set_count(&bars->v_seen, (int)g + 1);
+                        if (C::kSeen) set_count(&bars->v_seen, (int)g + 1);
                         ptx::tc_fence_after();
                         const uint32_t p_tmem = tmem + ((g & 1) ? kColS1 : kColS0);
-                        const uint64_t vd0 = v_desc + (uint64_t)((slot_of(pos) * C::kStageBytes) >> 4);
-                        const uint64_t vd1 =
-                            v_desc + (uint64_t)((slot_of(pos + 2 / C::kStageBoxes) * C::kStageBytes +
-                                                 (2 % C::kStageBoxes) * kBoxBytes) >> 4);
-                        ptx::mma2_ts(tmem + kColO, p_tmem, vd0, kIdescPV, j > 0);
+                        // keys 16 ks.. are in V box vb = 2 * (ks / 4) (its 64-key half,
+                        // first column atom; the next box holds the second atom), 16
+                        // rows of 128 bytes per k-step
 #pragma unroll
-                        for (int ks = 1; ks < kKeysPerTile / 16; ks++)
-                            ptx::mma2_ts(tmem + kColO, p_tmem + 8 * ks, (ks < 4 ? vd0 : vd1) + (2048 >> 4) * (ks & 3),
-                                         kIdescPV, 1);
+                        for (int ks = 0; ks < C::kKeys / 16; ks++) {
+                            const int vb = 2 * (ks / 4);
+                            const uint64_t vd =
+                                v_desc + (uint64_t)((slot_of(pos + vb / C::kVBoxesPerStage) * C::kStageBytes +
+                                                     (vb % C::kVBoxesPerStage) * kBoxBytes) >> 4) +
+                                (uint64_t)((2048 >> 4) * (ks & 3));
+                            ptx::mma2_ts(tmem + kColO, p_tmem + 8 * ks, vd, kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+                        }
                         for (int c = 0; c < C::kVStages; c++)
                             ptx::mma2_commit_pair(&bars->ring_empty[slot_of(pos + c)], kBothCtas);
                         ptx::mma2_commit_pair(&bars->o_done[g & 1], kBothCtas);
@@ -1026,37 +1116,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 }
                 ptx::tc_fence_after();
                 const uint32_t s_addr = tmem + lane_addr + ((g & 1) ? kColS1 : kColS0);
-                uint32_t r0[32], r1[32];
-                ptx::tmem_ld32(s_addr + 64 * half, r0);
-                ptx::tmem_ld32(s_addr + 64 * half + 32, r1);
-                ptx::tmem_wait_ld();
-                ptx::tmem_ld_fence(r0);
-                ptx::tmem_ld_fence(r1);
-                float s[64];
+                // this thread's kSc scores: columns [kSc * half, kSc * half + kSc) of S
+                constexpr int kSc = C::kScores;
+                float s[kSc];
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    s[c] = __uint_as_float(r0[c]);
-                    s[32 + c] = __uint_as_float(r1[c]);
+                for (int q = 0; q < kSc / 32; q++) {
+                    uint32_t r0[32];
+                    ptx::tmem_ld32(s_addr + kSc * half + 32 * q, r0);
+                    ptx::tmem_wait_ld();
+                    ptx::tmem_ld_fence(r0);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) s[32 * q + c] = __uint_as_float(r0[c]);
                 }
-                const int k0 = (it.kv_tile_lo + j) * kKeysPerTile;
+                const int k0 = (it.kv_tile_lo + j) * C::kKeys;
                 const int kp0 = pb.kv_pos0 + k0;
-                const bool edge = k0 + kKeysPerTile > pb.n_kv || kp0 + kKeysPerTile - 1 > q_first ||
+                const bool edge = k0 + C::kKeys > pb.n_kv || kp0 + C::kKeys - 1 > q_first ||
                                   (pb.window > 0 && q_last - kp0 >= pb.window);
                 if (edge) {
-                    const int kb = k0 + 64 * half;
-                    const int lo = vis_lo - kb, hi = vis_hi - kb;
+                    const int kb = k0 + kSc * half;
+                    const int lo = vis_lo - kb, hi = vis_hi - kb;  // visible columns: lo <= c <= hi
+                    // a warp's 32 rows are 4 tokens: the sides that cut into the
+                    // tile agree across it, and a one-sided mask takes 2 instructions
+                    const bool cut_lo = __any_sync(0xffffffffu, lo > 0);
+                    const bool cut_hi = __any_sync(0xffffffffu, hi < kSc - 1);
+                    if (cut_lo && cut_hi) {
 #pragma unroll
-                    for (int c = 0; c < 64; c++) s[c] = (c >= lo && c <= hi) ? s[c] : -CUDART_INF_F;
+                        for (int c = 0; c < kSc; c++) s[c] = (c >= lo && c <= hi) ? s[c] : -CUDART_INF_F;
+                    } else if (cut_hi) {
+#pragma unroll
+                        for (int c = 0; c < kSc; c++) s[c] = c <= hi ? s[c] : -CUDART_INF_F;
+                    } else if (cut_lo) {
+#pragma unroll
+                        for (int c = 0; c < kSc; c++) s[c] = c >= lo ? s[c] : -CUDART_INF_F;
+                    }
                 }
-                // row max as a tree (depth 6, not a chain of 63)
-                float mt[32];
-#pragma unroll
-                for (int c = 0; c < 32; c++) mt[c] = fmaxf(s[c], s[c + 32]);
-#pragma unroll
-                for (int w = 16; w >= 1; w >>= 1)
-#pragma unroll
-                    for (int c = 0; c < w; c++) mt[c] = fmaxf(mt[c], mt[c + w]);
-                float mx = mt[0];
+                float mx = max_tree<kSc>(s);
                 float mo;
                 if (!__all_sync(0xffffffffu, swap(mx, &mo))) {
                     ok = false;
@@ -1069,23 +1163,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
                 if (grow) m_used = mx;
                 const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
-                uint32_t pk[32];
-                // row sum in 8 partial sums, then a tree
-                float rs[8];
+                uint32_t pk[kSc / 2];
+                // pairs of scores in packed fp32: x = s log2e - m, P = 2^x (5 of
+                // every 8 pairs on the MUFU pipe, the rest on the FMA pipe), the
+                // row sum in 4 packed partial sums
+                const float2 scale = make_float2(kLog2e, kLog2e), shift = make_float2(neg_m, neg_m);
+                float2 rs[4];
 #pragma unroll
-                for (int k = 0; k < 8; k++) rs[k] = 0.0f;
+                for (int k = 0; k < 4; k++) rs[k] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    // half of the exponentials on the MUFU pipe, half on the FMA pipe
-                    const float x0 = fmaf(s[2 * c], kLog2e, neg_m), x1 = fmaf(s[2 * c + 1], kLog2e, neg_m);
-                    const float p0 = (c & 1) ? ex2_fma(x0) : ptx::ex2(x0);
-                    const float p1 = (c & 1) ? ex2_fma(x1) : ptx::ex2(x1);
-                    rs[(2 * c) & 7] += p0;
-                    rs[(2 * c + 1) & 7] += p1;
-                    pk[c] = ptx::pack_half2(p0, p1);
+                for (int c = 0; c < kSc / 2; c++) {
+                    const float2 x = ptx::fma2(make_float2(s[2 * c], s[2 * c + 1]), scale, shift);
+                    const float2 pr = (c & 7) < 5 ? make_float2(ptx::ex2(x.x), ptx::ex2(x.y)) : ex2_fma2(x);
+                    rs[c & 3] = ptx::add2(rs[c & 3], pr);
+                    pk[c] = ptx::pack_half2(pr.x, pr.y);
                 }
-                l = l * f + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
-                ptx::tmem_st32(s_addr + 32 * half, pk);
+                const float2 rsum = ptx::add2(ptx::add2(rs[0], rs[1]), ptx::add2(rs[2], rs[3]));
+                l = l * f + (rsum.x + rsum.y);
+                // P (fp16 pairs) over the first kSc columns of this S buffer; the
+                // columns half 1 writes were read by half 0 before it posted its max
+                if constexpr (kSc == 64) ptx::tmem_st32(s_addr + 32 * half, pk);
+                else ptx::tmem_st16(s_addr + 16 * half, pk);
                 if (__any_sync(0xffffffffu, o_live)) {
                     // O holds this item's earlier tiles (j >= 1): wait for PV(g-1)
                     if (!__all_sync(0xffffffffu, wait_bar(&bars->o_done[(g - 1) & 1], ((g - 1) >> 1) & 1u, abort, err))) {
@@ -1102,10 +1200,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                         ptx::tmem_wait_ld();
                         ptx::tmem_ld_fence(o0);
                         ptx::tmem_ld_fence(o1);
+                        const float2 f2 = make_float2(f, f);
 #pragma unroll
-                        for (int k = 0; k < 32; k++) {
-                            o0[k] = __float_as_uint(__uint_as_float(o0[k]) * f);
-                            o1[k] = __float_as_uint(__uint_as_float(o1[k]) * f);
+                        for (int k = 0; k < 32; k += 2) {
+                            float2 a0 = ptx::mul2(make_float2(__uint_as_float(o0[k]), __uint_as_float(o0[k + 1])), f2);
+                            float2 a1 = ptx::mul2(make_float2(__uint_as_float(o1[k]), __uint_as_float(o1[k + 1])), f2);
+                            o0[k] = __float_as_uint(a0.x);
+                            o0[k + 1] = __float_as_uint(a0.y);
+                            o1[k] = __float_as_uint(a1.x);
+                            o1[k + 1] = __float_as_uint(a1.y);
                         }
                         ptx::tmem_st32(o_addr, o0);
                         ptx::tmem_st32(o_addr + 32, o1);
@@ -1127,7 +1230,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 break;
             }
             l += lo_;
-            if (qk >= 2 && !__all_sync(0xffffffffu, wait_bar(&bars->stats_free[qk & 1], ((qk - 2) >> 1) & 1u, abort, err))) {
+            // Only half 0 writes the stats, so only it waits for their slot: the
+            // epilogue may release the slot's next use (this item's stats) as soon
+            // as half 0 posts them, and a parity wait of half 1 would then find
+            // the barrier two phases on.
+            if (half == 0 && qk >= 2 &&
+                !__all_sync(0xffffffffu, wait_bar(&bars->stats_free[qk & 1], ((qk - 2) >> 1) & 1u, abort, err))) {
                 ok = false;
                 break;
             }
@@ -1182,21 +1290,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             }
             ptx::tc_fence_after();
             const float inv = st.y > 0.0f ? 1.0f / st.y : 0.0f;
-#pragma unroll 1
-            for (int c = 0; c < kDV / 32; c++) {
-                uint32_t r[32];
-                ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * c, r);
-                ptx::tmem_wait_ld();
-                ptx::tmem_ld_fence(r);
-                if (c == kDV / 32 - 1) {
-                    // every column of O is in registers: the next item's first PV may overwrite it
-                    ptx::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (rank == 0) ptx::mbar_arrive(&bars->o_free);
-                        else ptx::mbar_arrive_cl(o_free_l);
-                    }
-                }
+            // chunk c's 32 columns of this row, divided by the row sum: each
+            // 16-column half through the warp's staging buffer, then 4 lanes per
+            // row store 64 contiguous bytes (8 rows per instruction)
+            auto emit = [&](const uint32_t(&r)[32], int c) {
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
 #pragma unroll
@@ -1217,6 +1314,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                             reinterpret_cast<float4 *>(out_rows + (size_t)orow * HD + 32 * c + 16 * h)[k] = v;
                     }
                     __syncwarp();
+                }
+            };
+            // Two register sets: the TMEM load of the next chunk is in flight
+            // while the current one is stored. O is free for the next item once
+            // the last chunk is in registers.
+            uint32_t ra[32], rb[32];
+            ptx::tmem_ld32(tmem + lane_addr + kColO, ra);
+            ptx::tmem_wait_ld();
+            ptx::tmem_ld_fence(ra);
+#pragma unroll 1
+            for (int c = 0; c < kDV / 32; c += 2) {
+                ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * (c + 1), rb);
+                emit(ra, c);
+                ptx::tmem_wait_ld();
+                ptx::tmem_ld_fence(rb);
+                const bool more = c + 2 < kDV / 32;
+                if (more) {
+                    ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * (c + 2), ra);
+                } else {
+                    // every column of O is in registers: the next item's first PV may overwrite it
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (rank == 0) ptx::mbar_arrive(&bars->o_free);
+                        else ptx::mbar_arrive_cl(o_free_l);
+                    }
+                }
+                emit(rb, c + 1);
+                if (more) {
+                    ptx::tmem_wait_ld();
+                    ptx::tmem_ld_fence(ra);
                 }
             }
             if (row < valid_rows && pb.lse && it.dv_half == 0)
@@ -1346,6 +1474,7 @@ struct Prepared {
     // persistent launches: per width, n_pairs CTA pairs, pair p running the
     // items [pair_start[p], pair_start[p + 1]) of that width's list
     bool persistent = false;
+    int keys512 = 128;  // key tile of the width-512 persistent launch
     int32_t *d_pair_start = nullptr;  // width 256's table, then width 512's
     int n_pairs[2] = {0, 0};
     uint64_t used = 0;   // call counter at the last use
@@ -1356,6 +1485,7 @@ struct PrefillScratch {
     bool attr_set = false;
     int n_sm = 0;          // of the device, read on the first call
     int persistent = -1;   // 1: persistent CTA pairs, 0: a CTA pair per item (G4A_PREFILL_KERNEL)
+    int keys512 = 128;     // key tile of the persistent width-512 kernel (G4A_PREFILL_KEYS512: 64 or 128)
     // Tensor maps by (kind, base, columns, rows): the encoder is a driver call
     // per map, and repeated calls (a model's layers, every prompt of a batch)
     // name the same buffers.
@@ -1397,18 +1527,23 @@ static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_
         cudaFuncSetAttribute(prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::kSmemBytes);
         cudaFuncSetAttribute(prefill_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<512>::kSmemBytes);
         cudaFuncSetAttribute(prefill_kernel_mixed, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMixed);
-        cudaFuncSetAttribute(prefill_persistent<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             CfgP<256>::kSmemBytes);
-        cudaFuncSetAttribute(prefill_persistent<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             CfgP<512>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_persistent<256, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             CfgP<256, 128>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_persistent<512, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             CfgP<512, 64>::kSmemBytes);
+        cudaFuncSetAttribute(prefill_persistent<512, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             CfgP<512, 128>::kSmemBytes);
         S->attr_set = true;
     }
     if (P.persistent) {
         if (P.n_pairs[0])
-            prefill_persistent<256><<<2 * (unsigned)P.n_pairs[0], kThreadsP, CfgP<256>::kSmemBytes, st>>>(
+            prefill_persistent<256, 128><<<2 * (unsigned)P.n_pairs[0], kThreadsP, CfgP<256, 128>::kSmemBytes, st>>>(
                 P.d_problems, P.d_items, P.d_pair_start, d_err, (int)stall);
-        if (P.n_pairs[1])
-            prefill_persistent<512><<<2 * (unsigned)P.n_pairs[1], kThreadsP, CfgP<512>::kSmemBytes, st>>>(
+        if (P.n_pairs[1] && P.keys512 == 64)
+            prefill_persistent<512, 64><<<2 * (unsigned)P.n_pairs[1], kThreadsP, CfgP<512, 64>::kSmemBytes, st>>>(
+                P.d_problems, P.d_items + P.n_work[0], P.d_pair_start + P.n_pairs[0] + 1, d_err, (int)stall);
+        else if (P.n_pairs[1])
+            prefill_persistent<512, 128><<<2 * (unsigned)P.n_pairs[1], kThreadsP, CfgP<512, 128>::kSmemBytes, st>>>(
                 P.d_problems, P.d_items + P.n_work[0], P.d_pair_start + P.n_pairs[0] + 1, d_err, (int)stall);
         return cudaGetLastError();
     }
@@ -1437,7 +1572,7 @@ static bool cached_map(PrefillScratch *S, int kind, const void *base, uint64_t c
     }
     bool ok;
     if (kind == 3) ok = encode_out_f32(out, static_cast<const float *>(base), cols, rows);
-    else ok = encode_tmap_2d(out, kind == 2 ? 1 : 0, base, cols, rows, kind == 0 ? kRows : 64);
+    else ok = encode_tmap_2d(out, kind == 2 ? 1 : 0, base, cols, rows, kind == 0 ? kRows : kind == 4 ? 32 : 64);
     if (!ok) return false;
     if (S->maps.size() > 4096) S->maps.clear();
     S->maps.emplace(key, *out);
@@ -1545,12 +1680,23 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         const unsigned bx = (unsigned)std::min<uint64_t>((most + 255) / 256, 1024);
         P.conv.push_back({segs, bx, cnt});
     }
+    if (S->persistent < 0) {
+        const char *mode = getenv("G4A_PREFILL_KERNEL");  // measurement switch: "item" or "persistent"
+        S->persistent = !(mode && std::strcmp(mode, "item") == 0);
+        const char *keys = getenv("G4A_PREFILL_KEYS512");  // measurement switch: "64" or "128"
+        S->keys512 = keys && std::strcmp(keys, "64") == 0 ? 64 : 128;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&S->n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || S->n_sm < 2)
+            S->n_sm = 148;
+    }
     std::vector<ProblemDev> hp(std::max(n, 1));
     std::vector<WorkItem> work[2];
     for (int32_t i = 0; i < n; i++) {
         const g4a_prefill_problem &p = pr[i];
         ProblemDev &d = hp[i];
         std::memset(&d, 0, sizeof d);
+        const bool wide_tiles = S->persistent == 1 && p.head_dim == 512 && S->keys512 == 64;
         d.hd = p.head_dim;
         d.window = p.window;
         d.n_q = p.n_q;
@@ -1573,13 +1719,17 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         if (p.n_kv > 0) {
             size_t k = std::find(v_src.begin(), v_src.end(), p.v_dev) - v_src.begin();
             if (!cached_map(S, 1, p.k_dev, p.head_dim, p.n_kv, &d.tk) ||
-                !cached_map(S, 2, P.v16 + v_off[k], p.head_dim, p.n_kv, &d.tv)) {
+                !cached_map(S, 2, P.v16 + v_off[k], p.head_dim, p.n_kv, &d.tv) ||
+                (wide_tiles && !cached_map(S, 4, p.k_dev, p.head_dim, p.n_kv, &d.tk32))) {
                 *msg = "cuTensorMapEncodeTiled failed for K/V";
                 free_prepared(P);
                 return G4A_CUDA;
             }
         }
         const int n_qt = (p.n_q + kTokensPerPair - 1) / kTokensPerPair;
+        // key tile of this problem's items: 64 keys for width 512 in the
+        // persistent kernel when it runs 64-key tiles, else 128
+        const int tile_keys = wide_tiles ? 64 : kKeysPerTile;
         for (int t = 0; t < n_qt; t++) {
             const int64_t q_lo = (int64_t)p.q_pos0 + (int64_t)t * kTokensPerPair;
             const int64_t q_hi = (int64_t)p.q_pos0 + std::min<int64_t>((int64_t)(t + 1) * kTokensPerPair, p.n_q) - 1;
@@ -1593,8 +1743,8 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
                 w.kv_tile_lo = 0;
                 w.n_kv_tiles = 0;
             } else {
-                w.kv_tile_lo = (int32_t)(klo / kKeysPerTile);
-                w.n_kv_tiles = (int32_t)(khi / kKeysPerTile) - w.kv_tile_lo + 1;
+                w.kv_tile_lo = (int32_t)(klo / tile_keys);
+                w.n_kv_tiles = (int32_t)(khi / tile_keys) - w.kv_tile_lo + 1;
             }
             for (int h = 0; h < p.head_dim / kDV; h++) {
                 w.dv_half = h;
@@ -1610,21 +1760,15 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         std::stable_sort(w.begin(), w.end(),
                          [](const WorkItem &a, const WorkItem &b) { return a.n_kv_tiles > b.n_kv_tiles; });
     const size_t n_items = work[0].size() + work[1].size();
-    if (S->persistent < 0) {
-        const char *mode = getenv("G4A_PREFILL_KERNEL");  // measurement switch: "item" or "persistent"
-        S->persistent = !(mode && std::strcmp(mode, "item") == 0);
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&S->n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || S->n_sm < 2)
-            S->n_sm = 148;
-    }
     P.persistent = S->persistent == 1;
+    P.keys512 = S->keys512;
     P.mixed = !P.persistent && !work[0].empty() && !work[1].empty();
     std::vector<int32_t> pair_start;
     if (P.persistent) {
         // Longest-processing-time assignment per width: an item costs its key
-        // tiles times 2 (width 256) or 3 (a half of width 512, which
-        // recomputes the 512-wide S), plus 2 for its Q load and epilogue;
+        // tiles times 4 (width 256: S and PV over 128 keys) or 3 per 64 keys
+        // (a half of width 512, which recomputes the 512-wide S), plus 4 for
+        // its Q load and epilogue;
         // items go longest first to the least loaded pair, and each pair's
         // list is stored in assignment order.
         for (int w = 0; w < 2; w++) {
@@ -1634,7 +1778,8 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
             const int base = (int)pair_start.size();
             pair_start.resize(base + n_pairs + 1, 0);
             if (n_pairs == 0) continue;
-            auto cost = [&](const WorkItem &it) { return (int64_t)it.n_kv_tiles * (w ? 3 : 2) + 2; };
+            const int tile_cost = w == 0 ? 4 : S->keys512 == 64 ? 3 : 6;
+            auto cost = [&](const WorkItem &it) { return (int64_t)it.n_kv_tiles * tile_cost + 4; };
             std::vector<int64_t> load(n_pairs, 0);
             std::vector<int> owner(list.size());
             std::vector<int> count(n_pairs, 0);
