@@ -219,8 +219,11 @@ template <int N> __device__ __forceinline__ float max_tree(const float (&v)[N]) 
 // Bounded wait until a progress counter of another issuing thread of this
 // CTA reaches `target` (false on abort or time-out, as wait_bar).
 __device__ __forceinline__ bool wait_count(const int *counter, int target, volatile int *abort, int *err) {
+    const uint32_t a = ptx::smem_u32(counter);
     for (uint32_t i = 0; i < kWaitLimit; i++) {
-        if (*reinterpret_cast<const volatile int *>(counter) >= target) {
+        int v;
+        asm volatile("ld.volatile.shared.b32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+        if (v >= target) {
             __threadfence_block();
             return true;
         }
@@ -231,7 +234,7 @@ __device__ __forceinline__ bool wait_count(const int *counter, int target, volat
     return false;
 }
 __device__ __forceinline__ void set_count(int *counter, int v) {
-    *reinterpret_cast<volatile int *>(counter) = v;
+    asm volatile("st.volatile.shared.b32 [%0], %1;" ::"r"(ptx::smem_u32(counter)), "r"(v) : "memory");
 }
 
 template <int HD>
@@ -786,7 +789,14 @@ template <int HD, int KEYS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
     prefill_persistent(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items,
                        const int32_t *__restrict__ pair_start, int *err, int stall) {
-    if (stall) return stall_item(err);
+    // A launch that follows this one in the stream (the other head width of
+    // the same call) may take SMs as this launch's pairs exit.
+    ptx::pdl_trigger();
+    if (stall) {
+        stall_item(err);
+        ptx::pdl_wait();
+        return;
+    }
     using C = CfgP<HD, KEYS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1100,11 +1110,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             const WorkItem it = items[i];
             const int n_tiles = it.n_kv_tiles;
             if (n_tiles == 0) continue;
+            // the problem's fields in registers for the item (the inline asm's
+            // memory clobbers would otherwise reload them from global memory)
             const ProblemDev &pb = problems[it.problem];
+            const int kv_pos0 = pb.kv_pos0, n_kv = pb.n_kv, window = pb.window;
             const int tok0 = it.q_tile * kTokensPerPair + (int)rank * kTokensPerCta;
             const int qpos = pb.q_pos0 + tok0 + row / 8;
-            const int vis_hi = min(qpos - pb.kv_pos0, pb.n_kv - 1);
-            const int vis_lo = pb.window > 0 ? qpos - pb.window + 1 - pb.kv_pos0 : INT_MIN / 2;
+            const int vis_hi = min(qpos - kv_pos0, n_kv - 1);
+            const int vis_lo = window > 0 ? qpos - window + 1 - kv_pos0 : INT_MIN / 2;
             const int q_first = pb.q_pos0 + tok0;
             const int q_last = q_first + kTokensPerCta - 1;
             float m_used = -CUDART_INF_F;
@@ -1129,9 +1142,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                     for (int c = 0; c < 32; c++) s[32 * q + c] = __uint_as_float(r0[c]);
                 }
                 const int k0 = (it.kv_tile_lo + j) * C::kKeys;
-                const int kp0 = pb.kv_pos0 + k0;
-                const bool edge = k0 + C::kKeys > pb.n_kv || kp0 + C::kKeys - 1 > q_first ||
-                                  (pb.window > 0 && q_last - kp0 >= pb.window);
+                const int kp0 = kv_pos0 + k0;
+                const bool edge = k0 + C::kKeys > n_kv || kp0 + C::kKeys - 1 > q_first ||
+                                  (window > 0 && q_last - kp0 >= window);
                 if (edge) {
                     const int kb = k0 + kSc * half;
                     const int lo = vis_lo - kb, hi = vis_hi - kb;  // visible columns: lo <= c <= hi
@@ -1247,17 +1260,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (warps 11-14)
-        // One thread per TMEM lane (row) of this CTA: warp w reaches lanes
-        // 32 * (w % 4).. of the TMEM. The row's 256 output columns are read 32
-        // at a time and divided by the row sum; each 16-column half goes
-        // through the warp's staging buffer, from which 4 lanes per row store
-        // 64 contiguous bytes (8 rows per instruction). O is free for the next
-        // item once the last columns are in registers.
+        // Warp w reaches TMEM lanes 32 * (w % 4).. (the rows of this CTA it
+        // writes); thread t reads its own row's statistics, and the 256 output
+        // columns are read 32 at a time and divided by the row sums.
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const uint32_t o_free_l = ptx::mapa(&bars->o_free, 0);
-        float *stage = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 8192) + (warp - kEpiWarp0) * 32 * 16;
         bool ok = true;
         uint32_t g = 0, qk = 0;
         for (int i = i0; i < i1 && ok; i++) {
@@ -1290,48 +1299,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             }
             ptx::tc_fence_after();
             const float inv = st.y > 0.0f ? 1.0f / st.y : 0.0f;
-            // chunk c's 32 columns of this row, divided by the row sum: each
-            // 16-column half through the warp's staging buffer, then 4 lanes per
-            // row store 64 contiguous bytes (8 rows per instruction)
-            auto emit = [&](const uint32_t(&r)[32], int c) {
+            // Stores straight from registers: with the 16x256b TMEM shape, lanes
+            // 4 g .. 4 g + 3 hold 8 consecutive columns (32 bytes) of one row, so
+            // each 8-byte store completes a sector with its 3 neighbours, and no
+            // staging in shared memory competes with the tensor core's operand
+            // reads. Lane t writes rows 8 k + t / 4 (k = 0..3) of the warp's 32.
+            const int tr = lane >> 2, tc = 2 * (lane & 3);
+            float rinv[4];
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
+            for (int k = 0; k < 4; k++) rinv[k] = __shfl_sync(0xffffffffu, inv, 8 * k + tr);
+            // chunk c (32 columns): lo holds rows 0-15 of the warp's 32, hi rows 16-31
+            auto load = [&](int c, uint32_t(&lo)[16], uint32_t(&hi)[16]) {
+                ptx::tmem_ld16x256_x4(tmem + lane_addr + kColO + 32 * c, lo);
+                ptx::tmem_ld16x256_x4(tmem + lane_addr + (16u << 16) + kColO + 32 * c, hi);
+            };
+            auto emit = [&](const uint32_t(&lo)[16], const uint32_t(&hi)[16], int c) {
+#pragma unroll
+                for (int sh = 0; sh < 2; sh++) {
+                    const uint32_t(&r)[16] = sh ? hi : lo;
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        const int ck = k ^ ((lane >> 1) & 3);
-                        reinterpret_cast<float4 *>(stage + lane * 16)[ck] =
-                            make_float4(__uint_as_float(r[16 * h + 4 * k]) * inv, __uint_as_float(r[16 * h + 4 * k + 1]) * inv,
-                                        __uint_as_float(r[16 * h + 4 * k + 2]) * inv,
-                                        __uint_as_float(r[16 * h + 4 * k + 3]) * inv);
-                    }
-                    __syncwarp();
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const int rr = 8 * q + (lane >> 2), k = lane & 3;
-                        const float4 v = reinterpret_cast<const float4 *>(stage + rr * 16)[k ^ ((rr >> 1) & 3)];
-                        const int orow = quad * 32 + rr;
-                        if (orow < valid_rows)
-                            reinterpret_cast<float4 *>(out_rows + (size_t)orow * HD + 32 * c + 16 * h)[k] = v;
+                        for (int e = 0; e < 2; e++) {  // e = 1: the row 8 below
+                            const int orow = quad * 32 + 16 * sh + 8 * e + tr;
+                            const float w = rinv[2 * sh + e];
+                            if (orow < valid_rows)
+                                *reinterpret_cast<float2 *>(out_rows + (size_t)orow * HD + 32 * c + 8 * k + tc) =
+                                    make_float2(__uint_as_float(r[4 * k + 2 * e]) * w,
+                                                __uint_as_float(r[4 * k + 2 * e + 1]) * w);
+                        }
                     }
-                    __syncwarp();
                 }
             };
-            // Two register sets: the TMEM load of the next chunk is in flight
+            // Two register sets: the TMEM loads of the next chunk are in flight
             // while the current one is stored. O is free for the next item once
             // the last chunk is in registers.
-            uint32_t ra[32], rb[32];
-            ptx::tmem_ld32(tmem + lane_addr + kColO, ra);
+            uint32_t a0[16], a1[16], b0[16], b1[16];
+            load(0, a0, a1);
             ptx::tmem_wait_ld();
-            ptx::tmem_ld_fence(ra);
+            ptx::tmem_ld_fence16(a0);
+            ptx::tmem_ld_fence16(a1);
 #pragma unroll 1
             for (int c = 0; c < kDV / 32; c += 2) {
-                ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * (c + 1), rb);
-                emit(ra, c);
+                load(c + 1, b0, b1);
+                emit(a0, a1, c);
                 ptx::tmem_wait_ld();
-                ptx::tmem_ld_fence(rb);
+                ptx::tmem_ld_fence16(b0);
+                ptx::tmem_ld_fence16(b1);
                 const bool more = c + 2 < kDV / 32;
                 if (more) {
-                    ptx::tmem_ld32(tmem + lane_addr + kColO + 32 * (c + 2), ra);
+                    load(c + 2, a0, a1);
                 } else {
                     // every column of O is in registers: the next item's first PV may overwrite it
                     ptx::tc_fence_before();
@@ -1341,10 +1358,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                         else ptx::mbar_arrive_cl(o_free_l);
                     }
                 }
-                emit(rb, c + 1);
+                emit(b0, b1, c + 1);
                 if (more) {
                     ptx::tmem_wait_ld();
-                    ptx::tmem_ld_fence(ra);
+                    ptx::tmem_ld_fence16(a0);
+                    ptx::tmem_ld_fence16(a1);
                 }
             }
             if (row < valid_rows && pb.lse && it.dv_half == 0)
@@ -1360,6 +1378,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
         ptx::tc_fence_after();
         ptx::tmem_dealloc2(tmem, kTmemCols);
     }
+    // Launched behind the other width: finish only after it (later work in the
+    // stream then follows both launches); a no-op for a plain launch.
+    ptx::pdl_wait();
 }
 
 // bf16 -> fp16 copies of up to kMaxSegs V arrays in one launch (blockIdx.y =
@@ -1539,13 +1560,34 @@ static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_
         if (P.n_pairs[0])
             prefill_persistent<256, 128><<<2 * (unsigned)P.n_pairs[0], kThreadsP, CfgP<256, 128>::kSmemBytes, st>>>(
                 P.d_problems, P.d_items, P.d_pair_start, d_err, (int)stall);
-        if (P.n_pairs[1] && P.keys512 == 64)
-            prefill_persistent<512, 64><<<2 * (unsigned)P.n_pairs[1], kThreadsP, CfgP<512, 64>::kSmemBytes, st>>>(
-                P.d_problems, P.d_items + P.n_work[0], P.d_pair_start + P.n_pairs[0] + 1, d_err, (int)stall);
-        else if (P.n_pairs[1])
-            prefill_persistent<512, 128><<<2 * (unsigned)P.n_pairs[1], kThreadsP, CfgP<512, 128>::kSmemBytes, st>>>(
-                P.d_problems, P.d_items + P.n_work[0], P.d_pair_start + P.n_pairs[0] + 1, d_err, (int)stall);
-        return cudaGetLastError();
+        if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return e;
+        if (P.n_pairs[1]) {
+            // Width 512 behind width 256 with programmatic stream serialization:
+            // its pairs start on SMs freed by the first launch's finished pairs
+            // (the two share no data; the kernel waits for its predecessor only
+            // before it exits).
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute pdl[1];
+            pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            pdl[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = pdl;
+            cfg.numAttrs = P.n_pairs[0] ? 1 : 0;
+            cfg.stream = st;
+            cfg.gridDim = dim3(2 * (unsigned)P.n_pairs[1]);
+            cfg.blockDim = dim3(kThreadsP);
+            const WorkItem *items = P.d_items + P.n_work[0];
+            const int32_t *starts = P.d_pair_start + P.n_pairs[0] + 1;
+            const int st_flag = (int)stall;
+            if (P.keys512 == 64) {
+                cfg.dynamicSmemBytes = CfgP<512, 64>::kSmemBytes;
+                return cudaLaunchKernelEx(&cfg, prefill_persistent<512, 64>, (const ProblemDev *)P.d_problems, items,
+                                          starts, d_err, st_flag);
+            }
+            cfg.dynamicSmemBytes = CfgP<512, 128>::kSmemBytes;
+            return cudaLaunchKernelEx(&cfg, prefill_persistent<512, 128>, (const ProblemDev *)P.d_problems, items, starts,
+                                      d_err, st_flag);
+        }
+        return cudaSuccess;
     }
     // two CTAs (one cluster) per work item
     if (P.mixed) {
