@@ -17,7 +17,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -235,10 +237,23 @@ struct Region {
     }
 };
 
-int run_prefill(g4a_ctx *ctx, const std::vector<g4a_prefill_problem> &probs) {
+// SMs the local attention leaves to the exchange running beside it: NCCL's
+// kernels need SMs of their own, and a persistent prefill holding all of them
+// would delay the exchange until it ends (G4A_CP_RESERVE_SMS overrides, for
+// measurement).
+int exchange_sms() {
+    static const int n = [] {
+        const char *e = getenv("G4A_CP_RESERVE_SMS");
+        return e ? std::max(0, atoi(e)) : 8;
+    }();
+    return n;
+}
+
+int run_prefill(g4a_ctx *ctx, const std::vector<g4a_prefill_problem> &probs, int reserve_sms = 0) {
     if (probs.empty()) return G4A_OK;
     const char *msg = "";
-    const int rc = prefill_run(ctx->prefill, ctx->d_err, (int32_t)probs.size(), probs.data(), ctx->stream, &msg);
+    const int rc = prefill_run(ctx->prefill, ctx->d_err, (int32_t)probs.size(), probs.data(), ctx->stream, &msg,
+                               false, reserve_sms);
     if (rc != G4A_OK) return fail(ctx, rc, "compute: %s", msg);
     return G4A_OK;
 }
@@ -318,8 +333,10 @@ int schedule_gather_kv(g4a_ctx *ctx, NcclApi &api, ncclComm_t comm, CpState *s, 
     G4A_CUDA_TRY(ctx, cudaEventRecord(s->ev_gathered, s->side));
     {
         Region reg(ctx, G4A_K_CP_ATTEND_LOCAL, ctx->stream);
-        if ((rc = run_prefill(ctx, {problem(hd, qA, c, a0, kA, vA, c, a0, o[0], l[0]),
-                                    problem(hd, qB, c, b0, kB, vB, c, b0, o[1], l[1])})))
+        if ((rc = run_prefill(ctx,
+                              {problem(hd, qA, c, a0, kA, vA, c, a0, o[0], l[0]),
+                               problem(hd, qB, c, b0, kB, vB, c, b0, o[1], l[1])},
+                              W > 1 ? exchange_sms() : 0)))
             return rc;
         reg.end();
     }
@@ -412,7 +429,7 @@ int schedule_kv_shards(g4a_ctx *ctx, NcclApi &api, ncclComm_t comm, CpState *s, 
     G4A_CUDA_TRY(ctx, cudaEventRecord(s->ev_gathered, s->side));
     {
         Region reg(ctx, G4A_K_CP_ATTEND_LOCAL, ctx->stream);
-        if ((rc = run_prefill(ctx, local))) return rc;
+        if ((rc = run_prefill(ctx, local, W > 1 ? exchange_sms() : 0))) return rc;
         reg.end();
     }
     G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->stream, s->ev_gathered, 0));

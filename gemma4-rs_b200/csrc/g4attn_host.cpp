@@ -326,6 +326,7 @@ extern "C" int g4a_sync(g4a_ctx *ctx) {
     int flag = 0;
     G4A_CUDA_TRY(ctx, cudaMemcpy(&flag, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (flag) {
+        ctx->err_epoch++;
         G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
         if (flag & 6)  // bit 1: a prefill wait ran out, bit 2: a decode wait ran out
             return fail(ctx, G4A_TIMEOUT, "compute: a device wait ran out (flag %d)", flag);
@@ -676,6 +677,8 @@ struct Staged {
     int32_t n_tasks = 0;
     int32_t n_split_tasks = 0;
     uint8_t *q_blocks = nullptr;  // f16 kernel scratch
+    bool own = false;             // buffers of this plan alone
+    uint32_t ticket_epoch = 0;    // the context's error count when the tickets were last clear
 };
 
 // Copies a plan's metadata to the device. With own_buffers the buffers are
@@ -705,11 +708,17 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
         G4A_CUDA_TRY(ctx, cudaMalloc(&st->part_ml, n_ml * sizeof(float)));
         G4A_CUDA_TRY(ctx, cudaMalloc(&st->tickets, n_tk * sizeof(unsigned)));
         G4A_CUDA_TRY(ctx, cudaMemsetAsync(st->tickets, 0, n_tk * sizeof(unsigned), ctx->stream));
+        st->own = true;
+        st->ticket_epoch = ctx->err_epoch;
     } else {
         if ((rc = grow(ctx, &ctx->d_meta, &ctx->meta_cap, bytes, false))) return rc;
         if ((rc = grow(ctx, &ctx->d_part_o, &ctx->part_o_cap, n_po, false))) return rc;
         if ((rc = grow(ctx, &ctx->d_part_ml, &ctx->part_ml_cap, n_ml, false))) return rc;
         if ((rc = grow(ctx, &ctx->d_tickets, &ctx->tickets_cap, n_tk, true))) return rc;
+        if (ctx->tickets_epoch != ctx->err_epoch) {  // an aborted step may have left counts
+            G4A_CUDA_TRY(ctx, cudaMemsetAsync(ctx->d_tickets, 0, ctx->tickets_cap * sizeof(unsigned), ctx->stream));
+            ctx->tickets_epoch = ctx->err_epoch;
+        }
         if (n_qb && (rc = grow(ctx, &ctx->d_qblocks, &ctx->qblocks_cap, n_qb, false))) return rc;
         st->q_blocks = ctx->d_qblocks;
         st->meta = ctx->d_meta;
@@ -757,7 +766,11 @@ int stage_plan(g4a_ctx *ctx, const Plan &plan, const int32_t *d_bt, int32_t max_
     return G4A_OK;
 }
 
-int launch_staged(g4a_ctx *ctx, const Staged &st) {
+int launch_staged(g4a_ctx *ctx, Staged &st) {
+    if (st.own && st.ticket_epoch != ctx->err_epoch) {  // an aborted step may have left counts
+        G4A_CUDA_TRY(ctx, cudaMemsetAsync(st.tickets, 0, std::max<size_t>(st.n_tasks, 1) * sizeof(unsigned), ctx->stream));
+        st.ticket_epoch = ctx->err_epoch;
+    }
     DecodeParams p = st.params;
     if (st.f16_fast && (ctx->stall_mask & (1u << G4A_K_DECODE_MAIN))) {
         p.stall = 1;
@@ -1147,6 +1160,7 @@ int finish_host_step(g4a_ctx *ctx, std::chrono::steady_clock::time_point t0, cud
     }
     const int flag = *ctx->h_flag;
     if (flag) {
+        ctx->err_epoch++;
         G4A_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
         if (flag & 6) return fail(ctx, G4A_TIMEOUT, "compute: a device wait ran out (flag %d)", flag);
         return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");

@@ -28,6 +28,10 @@ struct g4a_ctx {
     size_t part_ml_cap = 0;
     unsigned *d_tickets = nullptr;
     size_t tickets_cap = 0;
+    // Device errors reported so far, and the count when d_tickets was last
+    // cleared: a step that aborted may leave split-task tickets counted.
+    uint32_t err_epoch = 0;
+    uint32_t tickets_epoch = 0;
     uint8_t *d_meta = nullptr;
     size_t meta_cap = 0;
     std::vector<uint8_t> h_meta;

@@ -215,9 +215,11 @@ cudaError_t e2b_gather_rows(const int8_t *xq, const float *xs, int cols, const i
 struct PrefillScratch;
 PrefillScratch *prefill_scratch_new();
 void prefill_scratch_free(PrefillScratch *s);
-// stall: the g4a_debug_stall test wait in every CTA pair instead of the work
+// stall: the g4a_debug_stall test wait in every CTA pair instead of the work;
+// reserve_sms: SMs the persistent kernel leaves free (for a collective that
+// runs beside it on another stream)
 int prefill_run(PrefillScratch *s, int *d_err, int32_t n, const struct g4a_prefill_problem *problems,
-                cudaStream_t st, const char **msg, bool stall = false);
+                cudaStream_t st, const char **msg, bool stall = false, int reserve_sms = 0);
 
 // Key/value-shard context-parallel merge (cp_kernels.cu): partial results of
 // one rank as row segments [t0, t1) of the sequence, o [t1-t0][8][hd] and

@@ -507,6 +507,9 @@ int submit(g4a_model *m, int32_t n, int32_t n_out, bool chunk, int32_t cl = 1) {
     const int32_t flags = *m->h_err;
     if (flags) {
         cudaMemset(ctx->d_err, 0, sizeof(int));
+        // an aborted step may leave split-task tickets counted
+        cudaMemset(m->tickets, 0, (size_t)m->R * sizeof(unsigned));
+        ctx->err_epoch++;
         if (flags & 1) return fail(ctx, G4A_NONFINITE, "compute: softmax input is not finite");
         return fail(ctx, G4A_TIMEOUT, "compute: a device wait timed out (flags %d)", flags);
     }

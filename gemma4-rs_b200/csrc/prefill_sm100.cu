@@ -1496,6 +1496,7 @@ struct Prepared {
     // items [pair_start[p], pair_start[p + 1]) of that width's list
     bool persistent = false;
     int keys512 = 128;  // key tile of the width-512 persistent launch
+    int reserve = 0;    // SMs left free (part of the cache key)
     int32_t *d_pair_start = nullptr;  // width 256's table, then width 512's
     int n_pairs[2] = {0, 0};
     uint64_t used = 0;   // call counter at the last use
@@ -1632,7 +1633,7 @@ void prefill_scratch_free(PrefillScratch *s) {
 // launches one kernel per head width. Returns a g4a_status; *msg names the
 // failure.
 int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_problem *pr, cudaStream_t st,
-                const char **msg, bool stall) {
+                const char **msg, bool stall, int reserve_sms) {
     *msg = "";
     if (n < 0 || (n > 0 && !pr)) {
         *msg = "invalid prefill problem list";
@@ -1640,7 +1641,7 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
     }
     S->calls++;
     for (auto &P : S->cache) {
-        if (P.used && P.key.size() == (size_t)n &&
+        if (P.used && P.key.size() == (size_t)n && P.reserve == reserve_sms &&
             (n == 0 || std::memcmp(pr, P.key.data(), (size_t)n * sizeof(g4a_prefill_problem)) == 0)) {
             P.used = S->calls;
             const cudaError_t e = launch_prepared(S, P, d_err, st, stall);
@@ -1815,7 +1816,8 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         // list is stored in assignment order.
         for (int w = 0; w < 2; w++) {
             std::vector<WorkItem> &list = work[w];
-            const int n_pairs = (int)std::min<size_t>(list.size(), (size_t)(S->n_sm / 2));
+            const int n_pairs =
+                (int)std::min<size_t>(list.size(), (size_t)std::max(1, (S->n_sm - std::max(0, reserve_sms)) / 2));
             P.n_pairs[w] = n_pairs;
             const int base = (int)pair_start.size();
             pair_start.resize(base + n_pairs + 1, 0);
@@ -1872,6 +1874,7 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
     P.n_work[0] = work[0].size();
     P.n_work[1] = work[1].size();
     P.key.assign(pr, pr + n);
+    P.reserve = reserve_sms;
     P.used = S->calls;
     if ((e = launch_prepared(S, P, d_err, st, stall)) != cudaSuccess) {
         *msg = cudaGetErrorString(e);

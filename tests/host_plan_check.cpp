@@ -20,7 +20,7 @@
 
 namespace g4a {
 cudaError_t launch_view(const ViewParams &, int, cudaStream_t) { return cudaSuccess; }
-int prefill_run(PrefillScratch *, int *, int32_t, const g4a_prefill_problem *, cudaStream_t, const char **, bool) { return 0; }
+int prefill_run(PrefillScratch *, int *, int32_t, const g4a_prefill_problem *, cudaStream_t, const char **, bool, int) { return 0; }
 cudaError_t launch_append(const AppendParams &, int, cudaStream_t) { return cudaSuccess; }
 cudaError_t launch_decode(const DecodeParams &, int, int, bool, cudaStream_t) { return cudaSuccess; }
 bool encode_tmap_2d(void *, int, const void *, uint64_t, uint64_t, uint32_t) { return true; }
