@@ -1226,38 +1226,45 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
     if (rc) return rc;
     if (!ctx->copy_in) G4A_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking));
     if (!ctx->copy_out) G4A_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking));
-    // events: [0] call start, then per layer (inputs in, kernels done)
-    while (ctx->io_events.size() < 1 + 2 * (size_t)n_layers) {
+    // events: [0] call start, [1] inputs in, [2] kernels done
+    while (ctx->io_events.size() < 3) {
         cudaEvent_t e = nullptr;
         G4A_CUDA_TRY(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         ctx->io_events.push_back(e);
     }
     cudaEvent_t *ev = ctx->io_events.data();
     std::vector<g4a_decode_layer> dev(n_layers);
+    // Outputs in page-locked memory the device can address are written in
+    // place by the kernels (posted writes over the bus while the step runs);
+    // other outputs go through the device slots and a copy after the kernels.
+    std::vector<char> out_in_place(n_layers, 0);
     for (int32_t i = 0; i < n_layers; i++) {
         const size_t qn = (size_t)n_seqs * kHeads * width[i], kn = (size_t)n_seqs * width[i];
         float *base = ctx->d_io + off[i];
         const g4a_decode_layer_host &h = layers[i];
+        void *o_mapped = nullptr;
+        out_in_place[i] = h.out_host && mapped_host(h.out_host, &o_mapped);
+        float *out_dev = out_in_place[i] ? static_cast<float *>(o_mapped) : h.out_host ? base + qn + 2 * kn : nullptr;
         dev[i] = g4a_decode_layer{h.layer,          h.q_raw_host ? base : nullptr,
                                   h.k_raw_host ? base + qn : nullptr, h.v_raw_host ? base + qn + kn : nullptr,
-                                  h.q_norm_w_dev,  h.k_norm_w_dev, h.out_host ? base + qn + 2 * kn : nullptr};
+                                  h.q_norm_w_dev,  h.k_norm_w_dev, out_dev};
     }
-    // The inputs go first, layer by layer on the copy-in stream (after the
-    // work already queued on the context's stream), into the context's own
-    // slots, so that the copies overlap the host-side validation and planning
-    // and a later layer's copy overlaps an earlier layer's kernels. On a
-    // rejected call the copy stream is drained before returning (no copy
-    // still reads the caller's buffers) and neither the cache nor out_host has
-    // been touched.
+    // The inputs go first on the copy-in stream (after the work already
+    // queued on the context's stream), into the context's own slots, so that
+    // the copies overlap the host-side validation and planning (measured: a
+    // second copy stream does not shorten them; the host link's rate bounds
+    // them). On a rejected call the copy stream is drained before returning
+    // (no copy still reads the caller's buffers) and neither the cache nor
+    // out_host has been touched.
     G4A_CUDA_TRY(ctx, cudaEventRecord(ev[0], ctx->stream));
     G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->copy_in, ev[0], 0));
+    cudaEvent_t prof_a = ctx->profiling ? spare_event(ctx) : nullptr;
+    if (prof_a) cudaEventRecord(prof_a, ctx->copy_in);
     for (int32_t i = 0; i < n_layers; i++) {
         const size_t qb = (size_t)n_seqs * kHeads * width[i] * sizeof(float), kb = (size_t)n_seqs * width[i] * sizeof(float);
         const g4a_decode_layer_host &h = layers[i];
         int32_t src = -1;
         const bool owner = g4a_kv_source_layer(&ctx->hp, h.layer, &src, nullptr) == G4A_OK && src == h.layer;
-        cudaEvent_t a = ctx->profiling ? spare_event(ctx) : nullptr;
-        if (a) cudaEventRecord(a, ctx->copy_in);
         if (h.q_raw_host && qb)
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].q_raw_dev), h.q_raw_host, qb,
                                               cudaMemcpyHostToDevice, ctx->copy_in));
@@ -1267,33 +1274,38 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].v_raw_dev), h.v_raw_host, kb,
                                               cudaMemcpyHostToDevice, ctx->copy_in));
         }
-        if (a) {
-            cudaEvent_t b = spare_event(ctx);
-            cudaEventRecord(b, ctx->copy_in);
-            ctx->recs.push_back({G4A_K_COPY_IN, a, b});
-        }
-        G4A_CUDA_TRY(ctx, cudaEventRecord(ev[1 + 2 * i], ctx->copy_in));
+    }
+    G4A_CUDA_TRY(ctx, cudaEventRecord(ev[1], ctx->copy_in));
+    if (prof_a) {
+        cudaEvent_t b = spare_event(ctx);
+        cudaEventRecord(b, ctx->copy_in);
+        ctx->recs.push_back({G4A_K_COPY_IN, prof_a, b});
     }
     DecodeLayers info;
     if ((rc = check_decode(ctx, kv, n_layers, dev.data(), n_seqs, seq_ids, positions, info))) {
         cudaStreamSynchronize(ctx->copy_in);
         return rc;
     }
-    // Each layer's kernels once its inputs are in; its output copied out on
-    // the copy-out stream while the next layer's kernels run.
-    for (int32_t i = 0; i < n_layers; i++) {
-        G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->stream, ev[1 + 2 * i], 0));
+    // One launch set for all layers once every input is in (per-layer
+    // launches each pay a persistent kernel's ramp and tail, which cost more
+    // than the copy overlap they buy), then every output copied out.
+    G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->stream, ev[1], 0));
+    {
         Plan &plan = scratch_plan();
-        plan_decode(ctx, kv, dev.data(), n_seqs, seq_ids, positions, info, i, 1, plan);
+        plan_decode(ctx, kv, dev.data(), n_seqs, seq_ids, positions, info, 0, n_layers, plan);
         if ((rc = run_plan(ctx, plan, kv->d_bt, kv->max_pages, kv->page_tokens, kv->dtype == G4A_KV_F16))) return rc;
-        G4A_CUDA_TRY(ctx, cudaEventRecord(ev[2 + 2 * i], ctx->stream));
-        if (!layers[i].out_host) continue;
-        G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->copy_out, ev[2 + 2 * i], 0));
+    }
+    G4A_CUDA_TRY(ctx, cudaEventRecord(ev[2], ctx->stream));
+    G4A_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->copy_out, ev[2], 0));
+    {
         cudaEvent_t a = ctx->profiling ? spare_event(ctx) : nullptr;
         if (a) cudaEventRecord(a, ctx->copy_out);
-        G4A_CUDA_TRY(ctx, cudaMemcpyAsync(layers[i].out_host, dev[i].out_dev,
-                                          (size_t)n_seqs * kHeads * width[i] * sizeof(float), cudaMemcpyDeviceToHost,
-                                          ctx->copy_out));
+        for (int32_t i = 0; i < n_layers; i++) {
+            if (!layers[i].out_host || out_in_place[i]) continue;
+            G4A_CUDA_TRY(ctx, cudaMemcpyAsync(layers[i].out_host, dev[i].out_dev,
+                                              (size_t)n_seqs * kHeads * width[i] * sizeof(float),
+                                              cudaMemcpyDeviceToHost, ctx->copy_out));
+        }
         if (a) {
             cudaEvent_t b = spare_event(ctx);
             cudaEventRecord(b, ctx->copy_out);
