@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -1034,6 +1035,7 @@ void plan_decode(g4a_ctx *ctx, g4a_kv *kv, const g4a_decode_layer *layers, int32
     plan.f16_fast = kv->dtype == G4A_KV_F16 && kv->d_tmaps != nullptr;
     // f16 kernel: about three items per SM over the whole call, by K/V bytes
     const int64_t weighted_all = weighted;
+    // (measured on configuration 2: 2, 4, 6 and 8 items per SM were 1-15 % slower)
     const int64_t item_weight = std::max<int64_t>(64, (weighted_all + 3 * ctx->n_sm - 1) / (3 * ctx->n_sm));
     for (int32_t i = first; i < first + count; i++) {
         const g4a_decode_layer &a = layers[i];
