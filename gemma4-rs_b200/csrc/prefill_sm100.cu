@@ -365,6 +365,15 @@ __device__ __forceinline__ void prefill_item(const ProblemDev *__restrict__ prob
                     }
                 }
             }
+            // Non-leader after an abort: its loads signal the leader's barriers,
+            // which the leader may not have armed for a stage it never reached,
+            // so their completion cannot be observed from here; the CTA lets
+            // 200 us of the global timer pass (far above any load's latency)
+            // before it may exit.
+            if (rank != 0 && (!ok || *abort)) {
+                const uint64_t t0 = ptx::globaltimer_ns();
+                while (ptx::globaltimer_ns() - t0 < 200000ull) __nanosleep(2000);
+            }
         }
     } else if (warp == 1 || warp == kPvWarp) {
         // ------------------------------------------------------------ MMA issuers (leader)
@@ -950,6 +959,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                         }
                     }
                 }
+            }
+            // Non-leader after an abort: its loads signal the leader's barriers,
+            // which the leader may not have armed for a stage it never reached,
+            // so their completion cannot be observed from here; the CTA lets
+            // 200 us of the global timer pass (far above any load's latency)
+            // before it may exit.
+            if (rank != 0 && (!ok || *abort)) {
+                const uint64_t t0 = ptx::globaltimer_ns();
+                while (ptx::globaltimer_ns() - t0 < 200000ull) __nanosleep(2000);
             }
         }
     } else if (warp == 1 || warp == kPvWarp) {
