@@ -797,7 +797,7 @@ struct CfgP {
 template <int HD, int KEYS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
     prefill_persistent(const ProblemDev *__restrict__ problems, const WorkItem *__restrict__ items,
-                       const int32_t *__restrict__ pair_start, int *err, int stall) {
+                       const int32_t *__restrict__ pair_start, int *err, int stall, int wait_v) {
     // A launch that follows this one in the stream (the other head width of
     // the same call) may take SMs as this launch's pairs exit.
     ptx::pdl_trigger();
@@ -926,6 +926,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 // V: this CTA's 128 output columns (two 64-column atoms) of the
                 // tile's 64-key halves; box q = 2 * key half + atom
                 auto push_v = [&](int j) {
+                    if (wait_v) {  // V comes from the conversion this launch may overlap
+                        ptx::pdl_wait();
+                        wait_v = 0;
+                    }
                     const int x = it.dv_half * kDV + 128 * (int)rank;
                     const int y = (it.kv_tile_lo + j) * C::kKeys;
                     for (int st = 0; st < C::kVStages; st++) {
@@ -1412,6 +1416,7 @@ struct ConvSegs {
 };
 
 __global__ void bf16_to_f16_kernel(ConvSegs segs) {
+    ptx::pdl_trigger();  // a prefill launched behind it may start; it waits before reading V
     const int sg = blockIdx.y;
     const uint4 *src = reinterpret_cast<const uint4 *>(segs.src[sg]);
     uint4 *dst = reinterpret_cast<uint4 *>(segs.dst[sg]);
@@ -1507,7 +1512,8 @@ struct Prepared {
         unsigned bx;
         int cnt;
     };
-    std::vector<ConvLaunch> conv;
+    std::vector<ConvLaunch> conv;  // the width-512 sources' launches first, then width 256's
+    size_t n_conv_wide = 0;
     size_t n_work[2] = {0, 0};
     bool mixed = false;  // both widths in one launch (the items in one cost order)
     // persistent launches: per width, n_pairs CTA pairs, pair p running the
@@ -1576,35 +1582,44 @@ static cudaError_t launch_prepared(PrefillScratch *S, const Prepared &P, int *d_
         S->attr_set = true;
     }
     if (P.persistent) {
-        if (P.n_pairs[0])
-            prefill_persistent<256, 128><<<2 * (unsigned)P.n_pairs[0], kThreadsP, CfgP<256, 128>::kSmemBytes, st>>>(
-                P.d_problems, P.d_items, P.d_pair_start, d_err, (int)stall);
-        if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return e;
+        // Programmatic stream serialization: the width-256 launch starts while
+        // the width-256 V conversion (the last conversion launch) runs and waits
+        // for it before its first V load; width 512 follows width 256, taking
+        // SMs as its pairs finish (its V, converted first, is complete by then).
+        // Alone, width 512 follows the conversions the same way width 256 does.
+        const bool narrow_conv = P.conv.size() > P.n_conv_wide;
+        const int st_flag = (int)stall;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute pdl[1];
+        pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pdl[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = pdl;
+        cfg.stream = st;
+        cfg.blockDim = dim3(kThreadsP);
+        if (P.n_pairs[0]) {
+            cfg.numAttrs = narrow_conv ? 1 : 0;
+            cfg.gridDim = dim3(2 * (unsigned)P.n_pairs[0]);
+            cfg.dynamicSmemBytes = CfgP<256, 128>::kSmemBytes;
+            const cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_persistent<256, 128>, (const ProblemDev *)P.d_problems,
+                                                     (const WorkItem *)P.d_items, (const int32_t *)P.d_pair_start, d_err,
+                                                     st_flag, narrow_conv ? 1 : 0);
+            if (e != cudaSuccess) return e;
+        }
         if (P.n_pairs[1]) {
-            // Width 512 behind width 256 with programmatic stream serialization:
-            // its pairs start on SMs freed by the first launch's finished pairs
-            // (the two share no data; the kernel waits for its predecessor only
-            // before it exits).
-            cudaLaunchConfig_t cfg = {};
-            cudaLaunchAttribute pdl[1];
-            pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            pdl[0].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = pdl;
-            cfg.numAttrs = P.n_pairs[0] ? 1 : 0;
-            cfg.stream = st;
+            const bool first = P.n_pairs[0] == 0;
+            const int wait_v = first && !P.conv.empty() ? 1 : 0;
+            cfg.numAttrs = !first || wait_v ? 1 : 0;
             cfg.gridDim = dim3(2 * (unsigned)P.n_pairs[1]);
-            cfg.blockDim = dim3(kThreadsP);
             const WorkItem *items = P.d_items + P.n_work[0];
             const int32_t *starts = P.d_pair_start + P.n_pairs[0] + 1;
-            const int st_flag = (int)stall;
             if (P.keys512 == 64) {
                 cfg.dynamicSmemBytes = CfgP<512, 64>::kSmemBytes;
                 return cudaLaunchKernelEx(&cfg, prefill_persistent<512, 64>, (const ProblemDev *)P.d_problems, items,
-                                          starts, d_err, st_flag);
+                                          starts, d_err, st_flag, wait_v);
             }
             cfg.dynamicSmemBytes = CfgP<512, 128>::kSmemBytes;
             return cudaLaunchKernelEx(&cfg, prefill_persistent<512, 128>, (const ProblemDev *)P.d_problems, items, starts,
-                                      d_err, st_flag);
+                                      d_err, st_flag, wait_v);
         }
         return cudaSuccess;
     }
@@ -1683,6 +1698,7 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
     // distinct V arrays -> fp16 copies, each sized for the most rows any problem reads
     std::vector<const void *> v_src;
     std::vector<size_t> v_len;
+    std::vector<char> v_wide;  // read by a width-512 problem
     for (int32_t i = 0; i < n; i++) {
         const g4a_prefill_problem &p = pr[i];
         if (p.head_dim != 256 && p.head_dim != 512) {
@@ -1712,8 +1728,10 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
             if (k == v_src.size()) {
                 v_src.push_back(p.v_dev);
                 v_len.push_back(0);
+                v_wide.push_back(0);
             }
             v_len[k] = std::max(v_len[k], (size_t)p.n_kv * p.head_dim);
+            v_wide[k] |= p.head_dim == 512;
         }
     }
     std::vector<size_t> v_off(v_src.size(), 0);
@@ -1728,18 +1746,27 @@ int prefill_run(PrefillScratch *S, int *d_err, int32_t n, const g4a_prefill_prob
         *msg = cudaGetErrorString(e);
         return G4A_CUDA;
     }
-    for (size_t k0 = 0; k0 < v_src.size(); k0 += kMaxSegs) {
-        ConvSegs segs{};
-        const int cnt = (int)std::min<size_t>(kMaxSegs, v_src.size() - k0);
-        uint64_t most = 0;
-        for (int q = 0; q < cnt; q++) {
-            segs.src[q] = reinterpret_cast<const __nv_bfloat16 *>(v_src[k0 + q]);
-            segs.dst[q] = P.v16 + v_off[k0 + q];
-            segs.n8[q] = v_len[k0 + q] / 8;
-            most = std::max(most, segs.n8[q]);
+    // conversion launches by width group: the sources any width-512 problem
+    // reads first, so that a launch never mixes the groups
+    for (int wide = 1; wide >= 0; wide--) {
+        std::vector<size_t> grp;
+        for (size_t k = 0; k < v_src.size(); k++)
+            if ((v_wide[k] != 0) == (wide != 0)) grp.push_back(k);
+        for (size_t k0 = 0; k0 < grp.size(); k0 += kMaxSegs) {
+            ConvSegs segs{};
+            const int cnt = (int)std::min<size_t>(kMaxSegs, grp.size() - k0);
+            uint64_t most = 0;
+            for (int q = 0; q < cnt; q++) {
+                const size_t k = grp[k0 + q];
+                segs.src[q] = reinterpret_cast<const __nv_bfloat16 *>(v_src[k]);
+                segs.dst[q] = P.v16 + v_off[k];
+                segs.n8[q] = v_len[k] / 8;
+                most = std::max(most, segs.n8[q]);
+            }
+            const unsigned bx = (unsigned)std::min<uint64_t>((most + 255) / 256, 1024);
+            P.conv.push_back({segs, bx, cnt});
         }
-        const unsigned bx = (unsigned)std::min<uint64_t>((most + 255) / 256, 1024);
-        P.conv.push_back({segs, bx, cnt});
+        if (wide) P.n_conv_wide = P.conv.size();
     }
     if (S->persistent < 0) {
         const char *mode = getenv("G4A_PREFILL_KERNEL");  // measurement switch: "item" or "persistent"
