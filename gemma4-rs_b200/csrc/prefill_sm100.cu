@@ -1198,27 +1198,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                 const float f = o_live ? ptx::ex2(m_used - mx) : 1.0f;
                 if (grow) m_used = mx;
                 const float neg_m = m_used == -CUDART_INF_F ? 0.0f : -m_used;
-                uint32_t pk[kSc / 2];
                 // pairs of scores in packed fp32: x = s log2e - m, P = 2^x (5 of
                 // every 8 pairs on the MUFU pipe, the rest on the FMA pipe), the
-                // row sum in 4 packed partial sums
+                // row sum in 4 packed partial sums. P (fp16 pairs) goes over the
+                // first kSc / 2 columns of this half's part of the S buffer, 16
+                // columns at a time, each store issued as soon as its pairs are
+                // packed (the next pairs' exponentials overlap its latency); the
+                // columns half 1 writes were read by half 0 before it posted its max.
                 const float2 scale = make_float2(kLog2e, kLog2e), shift = make_float2(neg_m, neg_m);
                 float2 rs[4];
 #pragma unroll
                 for (int k = 0; k < 4; k++) rs[k] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int c = 0; c < kSc / 2; c++) {
-                    const float2 x = ptx::fma2(make_float2(s[2 * c], s[2 * c + 1]), scale, shift);
-                    const float2 pr = (c & 7) < 5 ? make_float2(ptx::ex2(x.x), ptx::ex2(x.y)) : ex2_fma2(x);
-                    rs[c & 3] = ptx::add2(rs[c & 3], pr);
-                    pk[c] = ptx::pack_half2(pr.x, pr.y);
+                for (int q = 0; q < kSc / 32; q++) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int cc = 0; cc < 16; cc++) {
+                        const int c = 16 * q + cc;
+                        const float2 x = ptx::fma2(make_float2(s[2 * c], s[2 * c + 1]), scale, shift);
+                        const float2 pr = (c & 7) < 5 ? make_float2(ptx::ex2(x.x), ptx::ex2(x.y)) : ex2_fma2(x);
+                        rs[c & 3] = ptx::add2(rs[c & 3], pr);
+                        pk[cc] = ptx::pack_half2(pr.x, pr.y);
+                    }
+                    ptx::tmem_st16(s_addr + (kSc / 2) * half + 16 * q, pk);
                 }
                 const float2 rsum = ptx::add2(ptx::add2(rs[0], rs[1]), ptx::add2(rs[2], rs[3]));
                 l = l * f + (rsum.x + rsum.y);
-                // P (fp16 pairs) over the first kSc columns of this S buffer; the
-                // columns half 1 writes were read by half 0 before it posted its max
-                if constexpr (kSc == 64) ptx::tmem_st32(s_addr + 32 * half, pk);
-                else ptx::tmem_st16(s_addr + 16 * half, pk);
                 if (__any_sync(0xffffffffu, o_live)) {
                     // O holds this item's earlier tiles (j >= 1): wait for PV(g-1)
                     if (!__all_sync(0xffffffffu, wait_bar(&bars->o_done[(g - 1) & 1], ((g - 1) >> 1) & 1u, abort, err))) {
