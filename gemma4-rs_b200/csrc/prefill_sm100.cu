@@ -748,7 +748,7 @@ struct PBars {
     uint64_t ring_empty[8];
     uint32_t tmem_base;
     int abort;
-    int k_seen;               // leader: tiles whose K stages the S issuer has seen land
+    int k_seen;               // leader: K stages the S issuer has seen land (over the pair's tiles)
     int v_seen;               // leader: tiles whose V stages the PV issuer has seen land
 };
 static_assert(sizeof(PBars) <= 8192, "persistent barrier region");
@@ -1015,6 +1015,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                                 ok = false;
                                 break;
                             }
+                            if (C::kSeen) set_count(&bars->k_seen, (int)(g * C::kKStages) + st + 1);
                             ptx::tc_fence_after();
 #pragma unroll
                             for (int b = 0; b < C::kKBoxesPerStage; b++) {
@@ -1028,7 +1029,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                             }
                             ptx::mma2_commit_pair(&bars->ring_empty[slot], kBothCtas);
                         }
-                        if (C::kSeen) set_count(&bars->k_seen, (int)g + 1);
                         if (ok) ptx::mma2_commit_pair(&bars->s_full[g & 1], kBothCtas);
                     }
                     // the item's Q is free once its last S MMA completes
@@ -1048,10 +1048,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                             break;
                         }
                         // V(j)'s second slot last held K(j+1)'s first stage when a tile
-                        // exceeds the ring; otherwise every slot's previous fill has
-                        // landed before its next parity wait (both checked by a
-                        // randomized model of the protocol)
-                        if (C::kSeen && j + 1 < n_tiles && !wait_count(&bars->k_seen, (int)g + 2, abort, err)) {
+                        // exceeds the ring: the wait needs only that stage seen (PV(j)
+                        // then runs between S(j+1)'s stages); otherwise every slot's
+                        // previous fill has landed before its next parity wait (both
+                        // checked by a randomized model of the protocol)
+                        if (C::kSeen && j + 1 < n_tiles &&
+                            !wait_count(&bars->k_seen, (int)((g + 1) * C::kKStages) + 1, abort, err)) {
                             ok = false;
                             break;
                         }

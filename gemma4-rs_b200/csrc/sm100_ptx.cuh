@@ -65,9 +65,14 @@ __device__ __forceinline__ uint32_t mapa(const void *p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
 }
-// Arrive (release at cluster scope) on a barrier that may live in the other CTA.
+// Arrive on a barrier that may live in the other CTA, with the default
+// (CTA-scope release) semantics. The callers order only tensor-memory work
+// across it (their tcgen05 loads or stores completed by tcgen05.wait and
+// fenced with tcgen05.fence::before_thread_sync), which needs no cluster-scope
+// release of generic memory; a release at cluster scope held each arriving
+// thread for about 1,300 cycles in the prefill kernels' softmax warps.
 __device__ __forceinline__ void mbar_arrive_cl(uint32_t bar_cl) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cl) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cl) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
