@@ -212,7 +212,7 @@ __device__ __forceinline__ void prep_task(const DecodeParams &p, const DecodeTas
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float2 *rope = (tk.global ? p.rope_global : p.rope_local) + (size_t)tk.position * (HD / 2);
     uint8_t *qblk = reinterpret_cast<uint8_t *>(p.q_blocks) + (size_t)task * kQBlockBytes;
-    {  // q of head `warp` (model.rs:395-396)
+    if (warp < kHeads) {  // q of head `warp` (model.rs:395-396)
         const int h = warp;
         float x[HD / 32];
 #pragma unroll
@@ -228,25 +228,29 @@ __device__ __forceinline__ void prep_task(const DecodeParams &p, const DecodeTas
             *reinterpret_cast<__half *>(qblk + q_off<HD>(h + 8, col)) = lo;
         }
     }
-    if (tk.new_row >= 0 && warp < 2) {  // the appended token (model.rs:400-405)
+    // the appended token (model.rs:400-405): k on warp 8, v on warp 9, beside
+    // the q heads rather than after two of them
+    if (tk.new_row >= 0 && warp >= kHeads) {
+        const bool is_k = warp == kHeads;
         float x[HD / 32];
-        const float *src = warp == 0 ? tk.k_raw : tk.v_raw;
+        const float *src = is_k ? tk.k_raw : tk.v_raw;
 #pragma unroll
         for (int k = 0; k < HD / 32; k++) x[k] = __ldg(src + lane + 32 * k);
-        if (warp == 0)
+        if (is_k)
             norm_rope_pre<HD>(x, tk.k_w, rope, p.eps, lane);
         else
             norm_rope_pre<HD>(x, nullptr, nullptr, p.eps, lane);
         const int32_t *bt = p.block_table + (size_t)tk.seq * p.max_pages;
         const int page = bt[tk.new_row / p.page_tokens];
-        __half *dst = const_cast<__half *>(reinterpret_cast<const __half *>(warp == 0 ? tk.k_base : tk.v_base)) +
+        __half *dst = const_cast<__half *>(reinterpret_cast<const __half *>(is_k ? tk.k_base : tk.v_base)) +
                       ((size_t)page * p.page_tokens + (tk.new_row % p.page_tokens)) * HD;
 #pragma unroll
         for (int k = 0; k < HD / 32; k++) dst[lane + 32 * k] = __float2half_rn(x[k]);
     }
 }
 
-__global__ void __launch_bounds__(256) decode_f16_prep(DecodeParams p) {
+constexpr int kPrepThreads = 32 * (kHeads + 2);  // a warp per q head, one for k, one for v
+__global__ void __launch_bounds__(kPrepThreads) decode_f16_prep(DecodeParams p) {
     release_dependents();  // the main kernel may be scheduled now; it waits for our writes
     const DecodeTask &tk = p.tasks[blockIdx.x];
     if (tk.hd == 256) prep_task<256>(p, tk, blockIdx.x);
@@ -585,18 +589,54 @@ __global__ void __launch_bounds__(kThreadsF16, 1) decode_f16_kernel(DecodeParams
 // combine: out = sum_i w_i O_i / sum_i w_i l_i, w_i = exp(m_i - max_j m_j)
 // ---------------------------------------------------------------------------
 
-// max values of the partials are in base-2 units (scores times log2 e)
+// max values of the partials are in base-2 units (scores times log2 e).
+// One block per (task, head). Warp w takes the 128-column chunk w % C (C = hd
+// / 128; lane = 4 columns) and the splits s = w / C, w / C + G, ... (G = 8 /
+// C); it loads them as float4 in rounds of kCombineRound, the next round in
+// flight while the current one is summed, and the G warp sums of a chunk meet
+// in shared memory. The first round is loaded before the weights are known.
+constexpr int kCombineChunk = 128;  // columns per warp
+constexpr int kCombineRound = 6;    // float4 loads in flight per thread and round
 __global__ void __launch_bounds__(256) decode_f16_combine(DecodeParams p) {
     wait_prerequisite();  // every partial of the main kernel is written
     const int task = p.split_tasks[blockIdx.x >> 3];
     const int h = blockIdx.x & 7;
     const DecodeTask &tk = p.tasks[task];
     const int ns = tk.n_splits, hd = tk.hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nc = hd / kCombineChunk, chunk = warp % nc, sg = warp / nc, G = 8 / nc;
     __shared__ float wsm[kF16MaxSplits + 1];
+    __shared__ float4 red[8][32];
     const float *pml = p.part_ml + (size_t)tk.partial_base * 2 * kHeads;
-    const float *pall = p.part_o + (size_t)tk.partial_base * kHeads * 512 + (size_t)h * hd;
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
+    const float *pcol =
+        p.part_o + (size_t)tk.partial_base * kHeads * 512 + (size_t)h * hd + chunk * kCombineChunk + 4 * lane;
+    const int mine = ns > sg ? (ns - sg + G - 1) / G : 0;  // splits of this warp
+    const int rounds = (mine + kCombineRound - 1) / kCombineRound;
+    auto load = [&](float4 (&v)[kCombineRound], int r) {
+#pragma unroll
+        for (int k = 0; k < kCombineRound; k++) {
+            const int i = r * kCombineRound + k;
+            v[k] = i < mine ? __ldcg(reinterpret_cast<const float4 *>(pcol + (size_t)(sg + G * i) * kHeads * 512))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto accumulate = [&](const float4 (&v)[kCombineRound], int r) {
+#pragma unroll
+        for (int k = 0; k < kCombineRound; k++) {
+            const int i = r * kCombineRound + k;
+            if (i < mine) {
+                const float w = wsm[sg + G * i];
+                o.x = fmaf(v[k].x, w, o.x);
+                o.y = fmaf(v[k].y, w, o.y);
+                o.z = fmaf(v[k].z, w, o.z);
+                o.w = fmaf(v[k].w, w, o.w);
+            }
+        }
+    };
+    float4 a[kCombineRound], b[kCombineRound];
+    if (rounds > 0) load(a, 0);
+    if (warp == 0) {
         float mv[3], lv[3];
         float M = -CUDART_INF_F;
 #pragma unroll
@@ -607,7 +647,7 @@ __global__ void __launch_bounds__(256) decode_f16_combine(DecodeParams p) {
             M = fmaxf(M, mv[k]);
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.0f;
 #pragma unroll
         for (int k = 0; k < 3; k++) {
@@ -617,24 +657,41 @@ __global__ void __launch_bounds__(256) decode_f16_combine(DecodeParams p) {
             L = fmaf(lv[k], w, L);
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
         if (lane == 0) {
             wsm[ns] = 1.0f / L;
             if (!(L > 0.0f) || !(L < CUDART_INF_F)) atomicOr(p.err_flag, 1);
         }
     }
     __syncthreads();
-    for (int c = threadIdx.x; c < hd; c += 256) {
-        float o = 0.0f;
-        for (int s0 = 0; s0 < ns; s0 += 8) {
-            float v[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) v[k] = s0 + k < ns ? pall[(size_t)(s0 + k) * kHeads * 512 + c] : 0.0f;
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-                if (s0 + k < ns) o = fmaf(v[k], wsm[s0 + k], o);
+    for (int r = 0; r < rounds; r += 2) {
+        if (r + 1 < rounds) load(b, r + 1);
+        accumulate(a, r);
+        if (r + 2 < rounds) load(a, r + 2);
+        if (r + 1 < rounds) accumulate(b, r + 1);
+    }
+    red[warp][lane] = o;
+    __syncthreads();
+    if (sg == 0) {
+        float4 t = o;
+        for (int g = 1; g < G; g++) {
+            const float4 u = red[chunk + nc * g][lane];
+            t.x += u.x;
+            t.y += u.y;
+            t.z += u.z;
+            t.w += u.w;
         }
-        tk.out[h * hd + c] = o * wsm[ns];
+        const float inv = wsm[ns];
+        float *dst = tk.out + (size_t)h * hd + chunk * kCombineChunk + 4 * lane;
+        const float4 r = make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+        if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            *reinterpret_cast<float4 *>(dst) = r;
+        } else {
+            dst[0] = r.x;
+            dst[1] = r.y;
+            dst[2] = r.z;
+            dst[3] = r.w;
+        }
     }
 }
 
@@ -648,7 +705,7 @@ cudaError_t launch_decode_f16(const DecodeParams &p, int stage, int n, cudaStrea
         attr = true;
     }
     if (stage == 0) {
-        decode_f16_prep<<<n, 256, 0, s>>>(p);
+        decode_f16_prep<<<n, kPrepThreads, 0, s>>>(p);
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg = {};
