@@ -1239,17 +1239,26 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
     // Outputs in page-locked memory the device can address are written in
     // place by the kernels (posted writes over the bus while the step runs);
     // other outputs go through the device slots and a copy after the kernels.
-    std::vector<char> out_in_place(n_layers, 0);
+    // The appended k and v rows (one row per sequence, a fifth of the input
+    // bytes but two of every layer's three copies) are read in place by the
+    // prep kernel when they sit in page-locked memory the device can address:
+    // each prep block reads its two rows over the bus in parallel with the
+    // others, which costs less than two more copies with their fixed cost.
+    std::vector<char> out_in_place(n_layers, 0), kv_in_place(n_layers, 0);
     for (int32_t i = 0; i < n_layers; i++) {
         const size_t qn = (size_t)n_seqs * kHeads * width[i], kn = (size_t)n_seqs * width[i];
         float *base = ctx->d_io + off[i];
         const g4a_decode_layer_host &h = layers[i];
-        void *o_mapped = nullptr;
+        void *o_mapped = nullptr, *k_mapped = nullptr, *v_mapped = nullptr;
         out_in_place[i] = h.out_host && mapped_host(h.out_host, &o_mapped);
+        kv_in_place[i] = h.k_raw_host && h.v_raw_host && mapped_host(h.k_raw_host, &k_mapped) &&
+                         mapped_host(h.v_raw_host, &v_mapped);
         float *out_dev = out_in_place[i] ? static_cast<float *>(o_mapped) : h.out_host ? base + qn + 2 * kn : nullptr;
-        dev[i] = g4a_decode_layer{h.layer,          h.q_raw_host ? base : nullptr,
-                                  h.k_raw_host ? base + qn : nullptr, h.v_raw_host ? base + qn + kn : nullptr,
-                                  h.q_norm_w_dev,  h.k_norm_w_dev, out_dev};
+        const float *k_dev = kv_in_place[i] ? static_cast<const float *>(k_mapped) : h.k_raw_host ? base + qn : nullptr;
+        const float *v_dev =
+            kv_in_place[i] ? static_cast<const float *>(v_mapped) : h.v_raw_host ? base + qn + kn : nullptr;
+        dev[i] = g4a_decode_layer{h.layer, h.q_raw_host ? base : nullptr, k_dev, v_dev, h.q_norm_w_dev,
+                                  h.k_norm_w_dev, out_dev};
     }
     // The inputs go first on the copy-in stream (after the work already
     // queued on the context's stream), into the context's own slots, so that
@@ -1270,7 +1279,7 @@ extern "C" int g4a_decode_host(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const
         if (h.q_raw_host && qb)
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].q_raw_dev), h.q_raw_host, qb,
                                               cudaMemcpyHostToDevice, ctx->copy_in));
-        if (owner && h.k_raw_host && h.v_raw_host && kb) {
+        if (owner && h.k_raw_host && h.v_raw_host && kb && !kv_in_place[i]) {
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].k_raw_dev), h.k_raw_host, kb,
                                               cudaMemcpyHostToDevice, ctx->copy_in));
             G4A_CUDA_TRY(ctx, cudaMemcpyAsync(const_cast<float *>(dev[i].v_raw_dev), h.v_raw_host, kb,

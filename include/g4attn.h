@@ -232,12 +232,13 @@ int g4a_decode(g4a_ctx *ctx, g4a_kv *kv, int32_t n_layers, const g4a_decode_laye
  * sequence) whose buffers are all page-locked memory the device can address
  * (cudaHostAlloc'd or registered, under unified addressing), the step's
  * kernels read the inputs and write the outputs in place over the bus, all
- * layers in one launch, with no staging copies. Otherwise the inputs are
- * copied into device slots of the context (a copy stream of the context;
- * pageable memory is staged by the driver) and all layers run in one launch
- * set once they are in; outputs in page-locked memory the device can address
- * are written in place by the kernels, other outputs are copied back after
- * them. The norm weights stay device
+ * layers in one launch, with no staging copies. Otherwise q is copied into
+ * device slots of the context (a copy stream of the context; pageable memory
+ * is staged by the driver), as are k and v unless both are page-locked memory
+ * the device can address, which the prep kernel then reads in place; all
+ * layers run in one launch set once the copies are in; outputs in page-locked
+ * memory the device can address are written in place by the kernels, other
+ * outputs are copied back after them. The norm weights stay device
  * pointers (model weights are resident). A rejected call leaves the cache and
  * the outputs untouched. */
 typedef struct g4a_decode_layer_host {
